@@ -1,0 +1,507 @@
+// attention.cu — paged attention over quantized KV pages (decode and chunked prefill).
+//
+// Replaces the reference's attention paths: mx.fast.scaled_dot_product_attention and the
+// Metal `fused_sdpa` shader (squish/hardware/fused_kernels.py:87-133, CPU restatement
+// :218-224) and the split-KV decode kernel `flash_decode_split_f32`
+// (squish_quant_rs/src/lib.rs:3056), which returns (out, lse, max) per split for a later
+// merge. Here the cache is paged (page tables read in-kernel, no gather) and quantized;
+// each 16-token tile is dequantized into shared memory (kv_format.cuh) and multiplied on
+// the tensor cores with mma.sync m16n8k16 (GQA query heads of one KV head form the
+// 16-row M side in decode; query tokens in prefill). Decode is HBM-bound: the roofline
+// is the quantized KV bytes per step, not MMA rate.
+//
+// Softmax runs in the log2 domain (scores pre-multiplied by scale*log2(e), exp2f).
+#include "kernels.h"
+#include "kv_format.cuh"
+
+namespace sq {
+
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Fill `rows` token rows of a [rows][D+8] bf16 smem tile from the paged cache.
+// Work items are (token, 8-dim chunk); invalid tokens (>= kv_len) are zero-filled.
+template <int D, int FMT>
+__device__ __forceinline__ void load_tile(__nv_bfloat16* tile, const uint8_t* codes, const __half* scales,
+                                          const int* bt, int h, int Hkv, int PS, int G, int tok0, int rows,
+                                          int kv_len, int item0, int item_stride) {
+  constexpr int LD = D + 8;
+  constexpr int CB = kv_code_bytes(FMT, D);
+  const int NS = kv_nscale(FMT, D, G);
+  for (int it = item0; it < rows * (D / 8); it += item_stride) {
+    const int r = it / (D / 8), c = it % (D / 8);
+    const int tok = tok0 + r;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (tok < kv_len) {
+      const int page = bt[tok / PS];
+      const size_t rowid = ((size_t)page * Hkv + h) * PS + (tok % PS);
+      v = kv_dequant8<FMT>(codes + rowid * CB, scales + rowid * NS, c * 8, G);
+    }
+    *reinterpret_cast<uint4*>(tile + r * LD + c * 8) = v;
+  }
+}
+
+// ------------------------------------------------------------------------------- decode
+// grid (B, Hkv, splits), 4 warps; warp w handles 16-token tiles t0+w, t0+w+4, ...
+// M side of each MMA = the G_q query heads of this KV head (padded to 16).
+template <int D, int FK, int FV>
+__global__ void __launch_bounds__(128) decode_kernel(const AttnParams p) {
+  constexpr int LD = D + 8;
+  constexpr int NWARP = 4;
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int Gq = p.Hq / p.Hkv;
+  const int kv_len = p.seq_lens[b];
+  const int n_tiles = (kv_len + 15) / 16;
+  const int t0 = split * p.tiles_per_split;
+  const int t1 = min(n_tiles, t0 + p.tiles_per_split);
+  const int* bt = p.block_tables + (size_t)b * p.bt_stride;
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(sm) + warp * 2 * 16 * LD;
+  __nv_bfloat16* Vs = Ks + 16 * LD;
+  const float scale = p.sm_scale * kLog2e;
+
+  // Q fragments (A operand, rows = heads g and g+8).
+  uint32_t qa[D / 16][4];
+  {
+    const __nv_bfloat16* qb = p.q + (size_t)b * p.ld_q + (size_t)h * Gq * D;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const int c0 = ks * 16 + 2 * t4;
+      auto ld2 = [&](int row, int col) -> uint32_t {
+        if (row >= Gq) return 0u;
+        return *reinterpret_cast<const uint32_t*>(qb + (size_t)row * D + col);
+      };
+      qa[ks][0] = ld2(g, c0);
+      qa[ks][1] = ld2(g + 8, c0);
+      qa[ks][2] = ld2(g, c0 + 8);
+      qa[ks][3] = ld2(g + 8, c0 + 8);
+    }
+  }
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+  for (int tile = t0 + warp; tile < t1; tile += NWARP) {
+    const int tok0 = tile * 16;
+    load_tile<D, FK>(Ks, p.k_codes, p.k_scales, bt, h, p.Hkv, p.page_size, p.group, tok0, 16, kv_len, lane, 32);
+    load_tile<D, FV>(Vs, p.v_codes, p.v_scales, bt, h, p.Hkv, p.page_size, p.group, tok0, 16, kv_len, lane, 32);
+    __syncwarp();
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+    const uint32_t kbase = smem_addr(Ks);
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const int tok = (lane & 7) + ((lane >> 4) << 3);
+      const int col = ks * 16 + ((lane >> 3) & 1) * 8;
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(kbase + (tok * LD + col) * 2, b0, b1, b2, b3);
+      mma16816(s[0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
+      mma16816(s[1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
+    }
+    // scale + mask + online softmax (rows g, g+8; columns = tokens)
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tok = tok0 + nt * 8 + 2 * t4 + (e & 1);
+        float v = s[nt][e] * scale;
+        if (tok >= kv_len) v = -INFINITY;
+        s[nt][e] = v;
+      }
+      mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float a0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - mn0);
+    const float a1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - mn1);
+    const float base0 = (mn0 == -INFINITY) ? 0.f : mn0, base1 = (mn1 == -INFINITY) ? 0.f : mn1;
+    m0 = mn0;
+    m1 = mn1;
+    float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      s[nt][0] = exp2f(s[nt][0] - base0);
+      s[nt][1] = exp2f(s[nt][1] - base0);
+      s[nt][2] = exp2f(s[nt][2] - base1);
+      s[nt][3] = exp2f(s[nt][3] - base1);
+      rs0 += s[nt][0] + s[nt][1];
+      rs1 += s[nt][2] + s[nt][3];
+    }
+    l0 = l0 * a0 + rs0;
+    l1 = l1 * a1 + rs1;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= a0;
+      o[i][1] *= a0;
+      o[i][2] *= a1;
+      o[i][3] *= a1;
+    }
+    const uint32_t pa0 = pack_bf2(s[0][0], s[0][1]), pa1 = pack_bf2(s[0][2], s[0][3]);
+    const uint32_t pa2 = pack_bf2(s[1][0], s[1][1]), pa3 = pack_bf2(s[1][2], s[1][3]);
+    const uint32_t vbase = smem_addr(Vs);
+#pragma unroll
+    for (int dt = 0; dt < D / 16; ++dt) {
+      const int tok = (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int col = dt * 16 + (lane >> 4) * 8;
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vbase + (tok * LD + col) * 2, b0, b1, b2, b3);
+      mma16816(o[2 * dt], pa0, pa1, pa2, pa3, b0, b1);
+      mma16816(o[2 * dt + 1], pa0, pa1, pa2, pa3, b2, b3);
+    }
+    __syncwarp();
+  }
+  // quad-reduce l
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  // cross-warp merge through shared memory: [warp][16 rows] m, l and [warp][16][D] o
+  __syncthreads();
+  float* mw = reinterpret_cast<float*>(sm);
+  float* lw = mw + NWARP * 16;
+  float* ow = lw + NWARP * 16;
+  if (t4 == 0) {
+    mw[warp * 16 + g] = m0;
+    mw[warp * 16 + g + 8] = m1;
+    lw[warp * 16 + g] = l0;
+    lw[warp * 16 + g + 8] = l1;
+  }
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) {
+    const int col = i * 8 + 2 * t4;
+    ow[(warp * 16 + g) * D + col] = o[i][0];
+    ow[(warp * 16 + g) * D + col + 1] = o[i][1];
+    ow[(warp * 16 + g + 8) * D + col] = o[i][2];
+    ow[(warp * 16 + g + 8) * D + col + 1] = o[i][3];
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < Gq * D; idx += blockDim.x) {
+    const int row = idx / D, d = idx % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) M = fmaxf(M, mw[w * 16 + row]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < NWARP; ++w) {
+        const float f = (mw[w * 16 + row] == -INFINITY) ? 0.f : exp2f(mw[w * 16 + row] - M);
+        L += lw[w * 16 + row] * f;
+        O += ow[(w * 16 + row) * D + d] * f;
+      }
+    }
+    const int hq = h * Gq + row;
+    if (p.splits == 1) {
+      p.out[(size_t)b * p.ld_out + (size_t)hq * D + d] = __float2bfloat16(L > 0.f ? O / L : 0.f);
+    } else {
+      const size_t base = ((size_t)b * p.Hq + hq) * p.splits + split;
+      p.o_part[base * D + d] = (L > 0.f) ? O / L : 0.f;
+      if (d == 0) p.lse_part[base] = (L > 0.f) ? M + log2f(L) : -INFINITY;
+    }
+  }
+}
+
+// grid (B, Hq), D threads: combine split partials (log2-domain LSE weights).
+__global__ void decode_merge_kernel(const AttnParams p) {
+  const int b = blockIdx.x, hq = blockIdx.y, d = threadIdx.x;
+  const int D = p.D, S = p.splits;
+  const size_t base = ((size_t)b * p.Hq + hq) * S;
+  float M = -INFINITY;
+  for (int s = 0; s < S; ++s) M = fmaxf(M, p.lse_part[base + s]);
+  float L = 0.f, O = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < S; ++s) {
+      const float lse = p.lse_part[base + s];
+      if (lse == -INFINITY) continue;
+      const float f = exp2f(lse - M);
+      L += f;
+      O += p.o_part[(base + s) * D + d] * f;
+    }
+  }
+  if (d < D) p.out[(size_t)b * p.ld_out + (size_t)hq * D + d] = __float2bfloat16(L > 0.f ? O / L : 0.f);
+}
+
+// ------------------------------------------------------------------------------- prefill
+// grid (n_tiles, Hkv * head_blocks); warps = query heads of this KV head (<= 8 per block).
+// Each warp owns 32 query rows (2 m16 tiles) of one head; K/V tiles of 32 tokens are
+// dequantized once per block into shared memory and shared by all its warps.
+constexpr int PQ = 32;  // query rows per block
+constexpr int PK = 32;  // kv tokens per tile
+
+template <int D, int FK, int FV>
+__global__ void __launch_bounds__(256) prefill_kernel(const AttnParams p) {
+  constexpr int LD = D + 8;
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int tile = blockIdx.x;
+  const int Gq = p.Hq / p.Hkv;
+  const int hblocks = (Gq + 7) / 8;
+  const int h = blockIdx.y / hblocks;
+  const int hq0 = h * Gq + (blockIdx.y % hblocks) * 8;
+  const int nheads = min(8, h * Gq + Gq - hq0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int b = p.tile_seq[tile];
+  const int q0 = p.tile_q0[tile];
+  const int qlen = p.q_len[b];
+  const int ctx = p.ctx_len[b];
+  const int qn = min(PQ, qlen - q0);
+  const int pos0 = ctx - qlen + q0;  // absolute position of query row 0
+  const int kv_end = pos0 + qn;      // exclusive
+  const int* bt = p.block_tables + (size_t)b * p.bt_stride;
+  const float scale = p.sm_scale * kLog2e;
+
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(sm);
+  __nv_bfloat16* Vs = Ks + PK * LD;
+  __nv_bfloat16* Qs = Vs + PK * LD + warp * PQ * LD;
+  const int hq = hq0 + warp;
+  const bool active = warp < nheads;
+
+  // stage Q rows of this warp's head
+  if (active) {
+    for (int it = lane; it < PQ * (D / 8); it += 32) {
+      const int r = it / (D / 8), c = it % (D / 8);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r < qn)
+        v = *reinterpret_cast<const uint4*>(p.q + (size_t)(p.q_start[b] + q0 + r) * p.ld_q + (size_t)hq * D + c * 8);
+      *reinterpret_cast<uint4*>(Qs + r * LD + c * 8) = v;
+    }
+  }
+  float o[2][D / 8][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) o[mt][i][0] = o[mt][i][1] = o[mt][i][2] = o[mt][i][3] = 0.f;
+  float mrow[2][2] = {{-INFINITY, -INFINITY}, {-INFINITY, -INFINITY}};
+  float lrow[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+
+  const int n_kv_tiles = (kv_end + PK - 1) / PK;
+  for (int kt = 0; kt < n_kv_tiles; ++kt) {
+    const int tok0 = kt * PK;
+    __syncthreads();  // previous tile fully consumed
+    load_tile<D, FK>(Ks, p.k_codes, p.k_scales, bt, h, p.Hkv, p.page_size, p.group, tok0, PK, kv_end,
+                     threadIdx.x, blockDim.x);
+    load_tile<D, FV>(Vs, p.v_codes, p.v_scales, bt, h, p.Hkv, p.page_size, p.group, tok0, PK, kv_end,
+                     threadIdx.x, blockDim.x);
+    __syncthreads();
+    if (!active) continue;
+    float s[2][PK / 8][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < PK / 8; ++nt) s[mt][nt][0] = s[mt][nt][1] = s[mt][nt][2] = s[mt][nt][3] = 0.f;
+    const uint32_t qbase = smem_addr(Qs), kbase = smem_addr(Ks), vbase = smem_addr(Vs);
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      uint32_t a[2][4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const int row = mt * 16 + (lane & 15);
+        const int col = ks * 16 + (lane >> 4) * 8;
+        ldsm_x4(qbase + (row * LD + col) * 2, a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
+      }
+#pragma unroll
+      for (int np = 0; np < PK / 16; ++np) {
+        const int tok = np * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int col = ks * 16 + ((lane >> 3) & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kbase + (tok * LD + col) * 2, b0, b1, b2, b3);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          mma16816(s[mt][2 * np], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b0, b1);
+          mma16816(s[mt][2 * np + 1], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b2, b3);
+        }
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int nt = 0; nt < PK / 8; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int qrow = mt * 16 + g + ((e >> 1) << 3);
+          const int key = tok0 + nt * 8 + 2 * t4 + (e & 1);
+          float v = s[mt][nt][e] * scale;
+          if (key > pos0 + qrow || qrow >= qn) v = -INFINITY;
+          s[mt][nt][e] = v;
+          mx[e >> 1] = fmaxf(mx[e >> 1], v);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+        const float mn = fmaxf(mrow[mt][r], mx[r]);
+        const float alpha = (mrow[mt][r] == -INFINITY) ? 0.f : exp2f(mrow[mt][r] - mn);
+        mrow[mt][r] = mn;
+        mx[r] = alpha;  // reuse as the rescale factor
+      }
+      const float base0 = (mrow[mt][0] == -INFINITY) ? 0.f : mrow[mt][0];
+      const float base1 = (mrow[mt][1] == -INFINITY) ? 0.f : mrow[mt][1];
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < PK / 8; ++nt) {
+        s[mt][nt][0] = exp2f(s[mt][nt][0] - base0);
+        s[mt][nt][1] = exp2f(s[mt][nt][1] - base0);
+        s[mt][nt][2] = exp2f(s[mt][nt][2] - base1);
+        s[mt][nt][3] = exp2f(s[mt][nt][3] - base1);
+        rs0 += s[mt][nt][0] + s[mt][nt][1];
+        rs1 += s[mt][nt][2] + s[mt][nt][3];
+      }
+      lrow[mt][0] = lrow[mt][0] * mx[0] + rs0;
+      lrow[mt][1] = lrow[mt][1] * mx[1] + rs1;
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        o[mt][i][0] *= mx[0];
+        o[mt][i][1] *= mx[0];
+        o[mt][i][2] *= mx[1];
+        o[mt][i][3] *= mx[1];
+      }
+    }
+#pragma unroll
+    for (int kk = 0; kk < PK / 16; ++kk) {
+      uint32_t pa[2][4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        pa[mt][0] = pack_bf2(s[mt][2 * kk][0], s[mt][2 * kk][1]);
+        pa[mt][1] = pack_bf2(s[mt][2 * kk][2], s[mt][2 * kk][3]);
+        pa[mt][2] = pack_bf2(s[mt][2 * kk + 1][0], s[mt][2 * kk + 1][1]);
+        pa[mt][3] = pack_bf2(s[mt][2 * kk + 1][2], s[mt][2 * kk + 1][3]);
+      }
+#pragma unroll
+      for (int dt = 0; dt < D / 16; ++dt) {
+        const int tok = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int col = dt * 16 + (lane >> 4) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vbase + (tok * LD + col) * 2, b0, b1, b2, b3);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          mma16816(o[mt][2 * dt], pa[mt][0], pa[mt][1], pa[mt][2], pa[mt][3], b0, b1);
+          mma16816(o[mt][2 * dt + 1], pa[mt][0], pa[mt][1], pa[mt][2], pa[mt][3], b2, b3);
+        }
+      }
+    }
+  }
+  if (!active) return;
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float l = lrow[mt][r];
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      lrow[mt][r] = (l > 0.f) ? 1.f / l : 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int qrow = mt * 16 + g + r * 8;
+      if (qrow >= qn) continue;
+      __nv_bfloat16* dst = p.out + (size_t)(p.q_start[b] + q0 + qrow) * p.ld_out + (size_t)hq * D;
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        const int col = i * 8 + 2 * t4;
+        *reinterpret_cast<uint32_t*>(dst + col) =
+            pack_bf2(o[mt][i][2 * r] * lrow[mt][r], o[mt][i][2 * r + 1] * lrow[mt][r]);
+      }
+    }
+  }
+}
+
+template <int D, int FK, int FV>
+cudaError_t launch_decode(const AttnParams& p, cudaStream_t s) {
+  constexpr int LD = D + 8;
+  const size_t kv_bytes = (size_t)4 * 2 * 16 * LD * 2;
+  const size_t merge_bytes = (size_t)4 * 16 * 2 * 4 + (size_t)4 * 16 * D * 4;
+  const size_t smem = kv_bytes > merge_bytes ? kv_bytes : merge_bytes;
+  auto k = decode_kernel<D, FK, FV>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  k<<<dim3(p.B, p.Hkv, p.splits), 128, smem, s>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || p.splits == 1) return e;
+  decode_merge_kernel<<<dim3(p.B, p.Hq), D, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+template <int D, int FK, int FV>
+cudaError_t launch_prefill(const AttnParams& p, cudaStream_t s) {
+  constexpr int LD = D + 8;
+  const size_t smem = (size_t)(2 * PK + 8 * PQ) * LD * 2;
+  auto k = prefill_kernel<D, FK, FV>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int Gq = p.Hq / p.Hkv;
+  const int hblocks = (Gq + 7) / 8;
+  const int warps = Gq < 8 ? Gq : 8;
+  k<<<dim3(p.n_tiles, p.Hkv * hblocks), warps * 32, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+#define SQ_ATTN_DISPATCH(FN)                                                   \
+  template <int D>                                                             \
+  cudaError_t FN##_fmt(const AttnParams& p, cudaStream_t s) {                  \
+    if (p.fmt_k == KV_BF16 && p.fmt_v == KV_BF16) return FN<D, KV_BF16, KV_BF16>(p, s); \
+    if (p.fmt_k == KV_INT8 && p.fmt_v == KV_INT8) return FN<D, KV_INT8, KV_INT8>(p, s); \
+    if (p.fmt_k == KV_INT4 && p.fmt_v == KV_INT4) return FN<D, KV_INT4, KV_INT4>(p, s); \
+    if (p.fmt_k == KV_INT2 && p.fmt_v == KV_INT2) return FN<D, KV_INT2, KV_INT2>(p, s); \
+    if (p.fmt_k == KV_K8 && p.fmt_v == KV_V4) return FN<D, KV_K8, KV_V4>(p, s);         \
+    return cudaErrorInvalidValue;                                              \
+  }
+
+SQ_ATTN_DISPATCH(launch_decode)
+SQ_ATTN_DISPATCH(launch_prefill)
+
+}  // namespace
+
+cudaError_t paged_decode_attn_launch(const AttnParams& p, cudaStream_t s) {
+  if (p.B == 0) return cudaSuccess;
+  if (p.D == 128) return launch_decode_fmt<128>(p, s);
+  if (p.D == 64) return launch_decode_fmt<64>(p, s);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t paged_prefill_attn_launch(const AttnParams& p, cudaStream_t s) {
+  if (p.n_tiles == 0) return cudaSuccess;
+  if (p.D == 128) return launch_prefill_fmt<128>(p, s);
+  if (p.D == 64) return launch_prefill_fmt<64>(p, s);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace sq

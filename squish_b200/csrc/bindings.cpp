@@ -1,0 +1,325 @@
+// bindings.cpp — Python bindings of the CUDA kernels and the C++ CPU reference library.
+//
+// Every CUDA entry point launches on the current torch stream, allocates nothing, and
+// takes its workspaces from the caller, so the calls can be captured in CUDA graphs.
+// Tensors are checked for device, dtype and contiguity; a failed launch raises.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "kernels.h"
+#include "w4a16_gemm.h"
+#include "cpu_ref.h"
+
+namespace {
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+#define CHECK_DT(x, dt) TORCH_CHECK((x).scalar_type() == (dt), #x " has wrong dtype")
+#define CUDA_OK(expr)                                                                       \
+  do {                                                                                      \
+    cudaError_t _e = (expr);                                                                \
+    TORCH_CHECK(_e == cudaSuccess, "squish_b200 kernel launch failed: ", cudaGetErrorString(_e)); \
+  } while (0)
+
+template <typename T>
+T* ptr(const torch::Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+template <typename T>
+T* optr(const c10::optional<torch::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    CUDA_OK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 row-major [rows, cols] (row stride ld elements), box [box_rows, 64], 128B swizzle.
+CUtensorMap make_bf16_map(const void* base, int rows, int cols, int ld, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", (int)r, ")");
+  return m;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+// ------------------------------------------------------------------ INT4 GEMM
+std::vector<torch::Tensor> repack_int4(torch::Tensor packed, torch::Tensor scales, torch::Tensor zeros, int64_t K,
+                                       int64_t group) {
+  CHECK_CUDA(packed);
+  CHECK_CONTIG(packed);
+  CHECK_CONTIG(scales);
+  CHECK_CONTIG(zeros);
+  CHECK_DT(packed, torch::kUInt8);
+  CHECK_DT(scales, torch::kFloat32);
+  CHECK_DT(zeros, torch::kFloat32);
+  TORCH_CHECK(group == 16 || group == 32 || group % 64 == 0, "INT4 group size must be 16, 32 or a multiple of 64");
+  TORCH_CHECK(K % 2 == 0 && packed.size(1) * 2 == K, "packed width must be K/2");
+  const c10::cuda::CUDAGuard g(packed.device());
+  const int64_t N = packed.size(0);
+  const int64_t kb = (K + 63) / 64;
+  const int64_t npad = (N + 255) / 256 * 256;
+  const int64_t gpk = group >= 64 ? 1 : 64 / group;
+  auto opts = packed.options().dtype(torch::kInt32);
+  torch::Tensor wq = torch::empty({npad / 128, kb, 1024}, opts);
+  torch::Tensor sz = torch::empty({npad / 128, kb, gpk * 128}, opts);
+  CUDA_OK(sq::repack_int4_launch(ptr<uint8_t>(packed), ptr<float>(scales), ptr<float>(zeros), ptr<uint32_t>(wq),
+                                 ptr<uint32_t>(sz), (int)N, (int)K, (int)group, cur_stream()));
+  return {wq, sz};
+}
+
+// Tile choice shared by the GEMM launch and the workspace sizing in Python.
+std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
+  int bn, nt = 1;
+  if (M <= 16) bn = 16;
+  else if (M <= 32) bn = 32;
+  else if (M <= 64) bn = 64;
+  else if (M <= 128) bn = 128;
+  else {
+    bn = 256;
+    nt = (N % 256 == 0 && N >= 2048) ? 2 : 1;
+  }
+  const int64_t kb = (K + 63) / 64;
+  const int64_t tiles = ((N + 128 * nt - 1) / (128 * nt)) * ((M + bn - 1) / bn);
+  int64_t splits = 1;
+  const int64_t sms = num_sms();
+  if (tiles * 2 <= sms) {
+    splits = std::min<int64_t>(sms / tiles, std::max<int64_t>(1, kb / 4));
+    splits = std::max<int64_t>(splits, 1);
+  }
+  int64_t kps = (kb + splits - 1) / splits;
+  splits = (kb + kps - 1) / kps;
+  return {bn, nt, splits, kps, tiles};
+}
+
+void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, int64_t K, int64_t group,
+                torch::Tensor y, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual,
+                int64_t epilogue, torch::Tensor ws, torch::Tensor counters, torch::Tensor status) {
+  CHECK_CUDA(x);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(y, torch::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be [M, K] with unit column stride");
+  TORCH_CHECK(x.size(1) == K, "x.size(1) != K");
+  TORCH_CHECK(y.stride(1) == 1, "y must have unit column stride");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16) == 0,
+              "x rows must be 16-byte aligned");
+  const int64_t M = x.size(0);
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard g(x.device());
+  auto plan = gemm_plan(M, N, K);
+  const int bn = (int)plan[0], nt = (int)plan[1];
+  sq::W4A16Params p{};
+  p.wq = ptr<uint32_t>(wq);
+  p.sz = ptr<uint32_t>(sz);
+  p.bias = optr<__nv_bfloat16>(bias);
+  p.residual = optr<__nv_bfloat16>(residual);
+  p.y = ptr<__nv_bfloat16>(y);
+  p.ws = ptr<float>(ws);
+  p.counters = ptr<int>(counters);
+  p.status = ptr<int>(status);
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.ldy = (int)y.stride(0);
+  p.ldr = residual.has_value() ? (int)residual->stride(0) : 0;
+  p.kb_total = (int)((K + 63) / 64);
+  p.splits = (int)plan[2];
+  p.kb_per_split = (int)plan[3];
+  p.gpk = group >= 64 ? 1 : (int)(64 / group);
+  p.epilogue = (int)epilogue;
+  if (p.splits > 1) {
+    TORCH_CHECK(ws.numel() >= (int64_t)p.splits * M * N, "split-K workspace too small");
+    TORCH_CHECK(counters.numel() >= plan[4], "split-K counter buffer too small");
+  }
+  const CUtensorMap xmap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), bn);
+  CUDA_OK(sq::w4a16_gemm_launch(xmap, p, bn, nt, cur_stream()));
+}
+
+// ------------------------------------------------------------------ norm / rope / attention
+void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> row_idx, double eps) {
+  CHECK_CUDA(x);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(w, torch::kBFloat16);
+  const int64_t H = x.size(-1);
+  TORCH_CHECK(H % 8 == 0, "hidden size must be a multiple of 8");
+  const int64_t rows = row_idx.has_value() ? row_idx->numel() : x.size(0);
+  const c10::cuda::CUDAGuard g(x.device());
+  CUDA_OK(sq::rmsnorm_launch(ptr<__nv_bfloat16>(x), ptr<__nv_bfloat16>(w), ptr<__nv_bfloat16>(y),
+                             optr<int>(row_idx), (int)rows, (int)H, (int)x.stride(0), (int)y.stride(0), (float)eps,
+                             cur_stream()));
+}
+
+void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin, torch::Tensor q_out,
+                   torch::Tensor slot_mapping, torch::Tensor k_codes, torch::Tensor k_scales, torch::Tensor v_codes,
+                   torch::Tensor v_scales, int64_t Hq, int64_t Hkv, int64_t D, int64_t page_size, int64_t group,
+                   int64_t fmt_k, int64_t fmt_v) {
+  CHECK_CUDA(qkv);
+  CHECK_DT(qkv, torch::kBFloat16);
+  CHECK_DT(positions, torch::kInt32);
+  CHECK_DT(slot_mapping, torch::kInt32);
+  TORCH_CHECK(group >= 32 && D % group == 0, "KV group must be >= 32 and divide head_dim");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  sq::RopeKvParams p{};
+  p.qkv = ptr<__nv_bfloat16>(qkv);
+  p.ld_qkv = (int)qkv.stride(0);
+  p.positions = ptr<int>(positions);
+  p.cos_sin = ptr<float>(cos_sin);
+  p.q_out = ptr<__nv_bfloat16>(q_out);
+  p.slot_mapping = ptr<int>(slot_mapping);
+  p.k_codes = ptr<uint8_t>(k_codes);
+  p.k_scales = reinterpret_cast<__half*>(k_scales.data_ptr());
+  p.v_codes = ptr<uint8_t>(v_codes);
+  p.v_scales = reinterpret_cast<__half*>(v_scales.data_ptr());
+  p.Hq = (int)Hq;
+  p.Hkv = (int)Hkv;
+  p.D = (int)D;
+  p.page_size = (int)page_size;
+  p.group = (int)group;
+  p.fmt_k = (int)fmt_k;
+  p.fmt_v = (int)fmt_v;
+  CUDA_OK(sq::rope_kv_write_launch(p, (int)qkv.size(0), cur_stream()));
+}
+
+sq::AttnParams attn_common(torch::Tensor q, torch::Tensor k_codes, torch::Tensor k_scales, torch::Tensor v_codes,
+                           torch::Tensor v_scales, torch::Tensor block_tables, torch::Tensor out, int64_t Hq,
+                           int64_t Hkv, int64_t D, int64_t page_size, int64_t group, int64_t fmt_k, int64_t fmt_v,
+                           double sm_scale) {
+  CHECK_CUDA(q);
+  CHECK_DT(q, torch::kBFloat16);
+  CHECK_DT(out, torch::kBFloat16);
+  CHECK_DT(block_tables, torch::kInt32);
+  TORCH_CHECK(page_size % 16 == 0, "page size must be a multiple of 16");
+  TORCH_CHECK(Hq % Hkv == 0 && Hq / Hkv <= 16, "GQA group must be <= 16");
+  sq::AttnParams p{};
+  p.q = ptr<__nv_bfloat16>(q);
+  p.ld_q = (int)q.stride(0);
+  p.k_codes = ptr<uint8_t>(k_codes);
+  p.k_scales = reinterpret_cast<const __half*>(k_scales.data_ptr());
+  p.v_codes = ptr<uint8_t>(v_codes);
+  p.v_scales = reinterpret_cast<const __half*>(v_scales.data_ptr());
+  p.block_tables = ptr<int>(block_tables);
+  p.bt_stride = (int)block_tables.stride(0);
+  p.out = ptr<__nv_bfloat16>(out);
+  p.ld_out = (int)out.stride(0);
+  p.Hq = (int)Hq;
+  p.Hkv = (int)Hkv;
+  p.D = (int)D;
+  p.page_size = (int)page_size;
+  p.group = (int)group;
+  p.fmt_k = (int)fmt_k;
+  p.fmt_v = (int)fmt_v;
+  p.sm_scale = (float)sm_scale;
+  return p;
+}
+
+void paged_decode_attention(torch::Tensor q, torch::Tensor k_codes, torch::Tensor k_scales, torch::Tensor v_codes,
+                            torch::Tensor v_scales, torch::Tensor block_tables, torch::Tensor seq_lens,
+                            torch::Tensor out, torch::Tensor o_part, torch::Tensor lse_part, int64_t Hq, int64_t Hkv,
+                            int64_t D, int64_t page_size, int64_t group, int64_t fmt_k, int64_t fmt_v,
+                            double sm_scale, int64_t splits, int64_t tiles_per_split) {
+  const c10::cuda::CUDAGuard g(q.device());
+  auto p = attn_common(q, k_codes, k_scales, v_codes, v_scales, block_tables, out, Hq, Hkv, D, page_size, group,
+                       fmt_k, fmt_v, sm_scale);
+  CHECK_DT(seq_lens, torch::kInt32);
+  p.seq_lens = ptr<int>(seq_lens);
+  p.B = (int)seq_lens.size(0);
+  p.splits = (int)splits;
+  p.tiles_per_split = (int)tiles_per_split;
+  if (splits > 1) {
+    TORCH_CHECK(o_part.numel() >= p.B * Hq * splits * D && lse_part.numel() >= p.B * Hq * splits,
+                "decode split workspace too small");
+  }
+  p.o_part = ptr<float>(o_part);
+  p.lse_part = ptr<float>(lse_part);
+  CUDA_OK(sq::paged_decode_attn_launch(p, cur_stream()));
+}
+
+void paged_prefill_attention(torch::Tensor q, torch::Tensor k_codes, torch::Tensor k_scales, torch::Tensor v_codes,
+                             torch::Tensor v_scales, torch::Tensor block_tables, torch::Tensor tile_seq,
+                             torch::Tensor tile_q0, torch::Tensor q_start, torch::Tensor q_len, torch::Tensor ctx_len,
+                             int64_t n_tiles, torch::Tensor out, int64_t Hq, int64_t Hkv, int64_t D,
+                             int64_t page_size, int64_t group, int64_t fmt_k, int64_t fmt_v, double sm_scale) {
+  const c10::cuda::CUDAGuard g(q.device());
+  auto p = attn_common(q, k_codes, k_scales, v_codes, v_scales, block_tables, out, Hq, Hkv, D, page_size, group,
+                       fmt_k, fmt_v, sm_scale);
+  p.tile_seq = ptr<int>(tile_seq);
+  p.tile_q0 = ptr<int>(tile_q0);
+  p.q_start = ptr<int>(q_start);
+  p.q_len = ptr<int>(q_len);
+  p.ctx_len = ptr<int>(ctx_len);
+  p.n_tiles = (int)n_tiles;
+  CUDA_OK(sq::paged_prefill_attn_launch(p, cur_stream()));
+}
+
+void sample(torch::Tensor logits, c10::optional<torch::Tensor> temperature, c10::optional<torch::Tensor> top_p,
+            c10::optional<torch::Tensor> top_k, c10::optional<torch::Tensor> min_p,
+            c10::optional<torch::Tensor> rep_penalty, c10::optional<torch::Tensor> hist,
+            c10::optional<torch::Tensor> allow_mask, int64_t seed, c10::optional<torch::Tensor> step,
+            torch::Tensor out_tokens, c10::optional<torch::Tensor> out_logprob, torch::Tensor work) {
+  CHECK_CUDA(logits);
+  CHECK_DT(logits, torch::kBFloat16);
+  CHECK_DT(work, torch::kFloat32);
+  const c10::cuda::CUDAGuard g(logits.device());
+  sq::SamplerParams p{};
+  p.logits = ptr<__nv_bfloat16>(logits);
+  p.ld = (int)logits.stride(0);
+  p.V = (int)logits.size(1);
+  p.B = (int)logits.size(0);
+  TORCH_CHECK(work.numel() >= (int64_t)p.B * p.V, "sampler workspace too small");
+  p.temperature = optr<float>(temperature);
+  p.top_p = optr<float>(top_p);
+  p.top_k = optr<int>(top_k);
+  p.min_p = optr<float>(min_p);
+  p.rep_penalty = optr<float>(rep_penalty);
+  p.hist = optr<int>(hist);
+  p.hist_stride = hist.has_value() ? (int)hist->size(1) : 0;
+  p.allow_mask = optr<uint32_t>(allow_mask);
+  p.seed = (uint64_t)seed;
+  p.step = optr<int>(step);
+  p.out_tokens = ptr<int>(out_tokens);
+  p.out_logprob = optr<float>(out_logprob);
+  CUDA_OK(sq::sampler_launch(p, ptr<float>(work), cur_stream()));
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "squish_b200 native kernels (sm_100a CUDA + C++ CPU reference)";
+  m.def("repack_int4", &repack_int4);
+  m.def("gemm_plan", &gemm_plan);
+  m.def("w4a16_gemm", &w4a16_gemm);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("rope_kv_write", &rope_kv_write);
+  m.def("paged_decode_attention", &paged_decode_attention);
+  m.def("paged_prefill_attention", &paged_prefill_attention);
+  m.def("sample", &sample);
+  sqcpu::register_cpu(m);
+}

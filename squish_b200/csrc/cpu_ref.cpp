@@ -1,0 +1,515 @@
+// cpu_ref.cpp — C++ CPU library restating the reference's native quantization kernels
+// (squish_quant_rs/src/lib.rs, Rust + Rayon) with ATen's parallel_for. These serve three roles:
+// the convert-time quantizers of `squish compress` on hosts without a GPU, the CPU
+// oracle for the CUDA kernels' numerics tests, and the timed CPU baseline.
+//
+// Semantics follow the Rust source line by line where the format is defined by it:
+//   quantize_int8_f32 (lib.rs:56), quantize_int8_grouped (121), quantize_int4_grouped (259),
+//   quantize_int4_asymmetric_grouped (402) / dequantize (490), NF4 (742-890),
+//   pack_int3_grouped_f32 (1125) / unpack_int3_grouped (1200), quantize_int2_grouped_f32 (1440)
+//   / dequantize (1510), quantized_matmul_int4 (5511).
+// Rust's f32::round rounds half away from zero; std::round does the same.
+#include <torch/extension.h>
+#include <ATen/Parallel.h>
+#include <cmath>
+#include <cstdint>
+#include <vector>
+
+#include "cpu_ref.h"
+
+namespace sqcpu {
+
+namespace {
+
+void check_cpu_f32_2d(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(!t.is_cuda(), name, " must be a CPU tensor");
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.scalar_type() == torch::kFloat32, name, " must be float32");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+template <class F>
+void prange(int64_t n, F&& f) {
+  at::parallel_for(0, n, 1, [&](int64_t b, int64_t e) {
+    for (int64_t i = b; i < e; ++i) f(i);
+  });
+}
+
+inline float clampf(float v, float lo, float hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+const float kNF4[16] = {-1.0f,
+                        -0.6961928009986877f,
+                        -0.5250730514526367f,
+                        -0.39491748809814453f,
+                        -0.28444138169288635f,
+                        -0.18477343022823334f,
+                        -0.09105003625154495f,
+                        0.0f,
+                        0.07958029955625534f,
+                        0.16093020141124725f,
+                        0.24611230194568634f,
+                        0.33791524171829224f,
+                        0.44070982933044434f,
+                        0.5626170039176941f,
+                        0.7229568362236023f,
+                        1.0f};
+
+// ---------------------------------------------------------------- INT8 symmetric
+std::vector<torch::Tensor> quantize_int8(torch::Tensor x, int64_t group) {
+  check_cpu_f32_2d(x, "x");
+  const int64_t N = x.size(0), D = x.size(1);
+  const int64_t g = group <= 0 ? D : group;
+  TORCH_CHECK(D % g == 0, "group must divide columns");
+  const int64_t G = D / g;
+  auto q = torch::empty({N, D}, torch::kInt8);
+  auto s = torch::empty({N, G}, torch::kFloat32);
+  const float* xp = x.data_ptr<float>();
+  int8_t* qp = q.data_ptr<int8_t>();
+  float* sp = s.data_ptr<float>();
+  prange(N, [&](int64_t r) {
+    for (int64_t j = 0; j < G; ++j) {
+      const float* row = xp + r * D + j * g;
+      float am = 0.f;
+      for (int64_t i = 0; i < g; ++i) am = std::max(am, std::fabs(row[i]));
+      const float sc = am == 0.f ? 1.f : am / 127.f;
+      sp[r * G + j] = sc;
+      const float inv = 1.f / sc;
+      for (int64_t i = 0; i < g; ++i) qp[r * D + j * g + i] = (int8_t)clampf(std::round(row[i] * inv), -127.f, 127.f);
+    }
+  });
+  return {q, s};
+}
+
+torch::Tensor dequantize_int8(torch::Tensor q, torch::Tensor s) {
+  const int64_t N = q.size(0), D = q.size(1), G = s.size(1), g = D / G;
+  auto out = torch::empty({N, D}, torch::kFloat32);
+  const int8_t* qp = q.contiguous().data_ptr<int8_t>();
+  const float* sp = s.contiguous().data_ptr<float>();
+  float* op = out.data_ptr<float>();
+  prange(N, [&](int64_t r) {for (int64_t c = 0; c < D; ++c) op[r * D + c] = (float)qp[r * D + c] * sp[r * G + c / g];});
+  return out;
+}
+
+// ---------------------------------------------------------------- INT4 asymmetric (primary weight format)
+std::vector<torch::Tensor> quantize_int4_asym(torch::Tensor x, int64_t group) {
+  check_cpu_f32_2d(x, "x");
+  const int64_t N = x.size(0), D = x.size(1);
+  TORCH_CHECK(D % group == 0 && D % 2 == 0, "columns must be even and divisible by group");
+  const int64_t G = D / group;
+  auto packed = torch::empty({N, D / 2}, torch::kUInt8);
+  auto scales = torch::empty({N, G}, torch::kFloat32);
+  auto offsets = torch::empty({N, G}, torch::kFloat32);
+  const float* xp = x.data_ptr<float>();
+  uint8_t* pp = packed.data_ptr<uint8_t>();
+  float* sp = scales.data_ptr<float>();
+  float* op = offsets.data_ptr<float>();
+  prange(N, [&](int64_t r) {
+    const float* row = xp + r * D;
+    for (int64_t g = 0; g < G; ++g) {
+      float mn = INFINITY, mx = -INFINITY;
+      for (int64_t i = g * group; i < (g + 1) * group; ++i) {
+        mn = std::min(mn, row[i]);
+        mx = std::max(mx, row[i]);
+      }
+      sp[r * G + g] = (mx == mn) ? 1.f : (mx - mn) / 15.f;
+      op[r * G + g] = mn;
+    }
+    for (int64_t i = 0; i < D / 2; ++i) {
+      const int64_t j0 = 2 * i, j1 = j0 + 1;
+      const int64_t g0 = j0 / group, g1 = j1 / group;
+      const uint8_t q0 = (uint8_t)clampf(std::round((row[j0] - op[r * G + g0]) / sp[r * G + g0]), 0.f, 15.f);
+      const uint8_t q1 = (uint8_t)clampf(std::round((row[j1] - op[r * G + g1]) / sp[r * G + g1]), 0.f, 15.f);
+      pp[r * (D / 2) + i] = (uint8_t)((q0 & 0xF) | ((q1 & 0xF) << 4));
+    }
+  });
+  return {packed, scales, offsets};
+}
+
+// Per-group MSE clip search (8 candidates beta in [0, 0.1]) then the plain quantizer,
+// as squish/quant/quantizer.py:500-605 does in numpy ahead of the Rust call.
+std::vector<torch::Tensor> quantize_int4_asym_mse(torch::Tensor x, int64_t group, int64_t n_clip) {
+  check_cpu_f32_2d(x, "x");
+  const int64_t N = x.size(0), D = x.size(1);
+  TORCH_CHECK(D % group == 0, "group must divide columns");
+  if (N == 1) return quantize_int4_asym(x, group);
+  auto clipped = x.clone();
+  float* cp = clipped.data_ptr<float>();
+  const int64_t G = N * (D / group);
+  std::vector<float> betas(n_clip);
+  for (int64_t i = 0; i < n_clip; ++i) betas[i] = n_clip == 1 ? 0.f : 0.10f * (float)i / (float)(n_clip - 1);
+  prange(G, [&](int64_t gi) {
+    float* grp = cp + gi * group;
+    float mn = INFINITY, mx = -INFINITY;
+    for (int64_t i = 0; i < group; ++i) {
+      mn = std::min(mn, grp[i]);
+      mx = std::max(mx, grp[i]);
+    }
+    const float rng = mx - mn;
+    float best = INFINITY, blo = mn, bhi = mx;
+    for (float beta : betas) {
+      const float lo = mn + beta * rng, hi = mx - beta * rng;
+      if (lo >= hi) continue;
+      const float sc = (hi - lo) > 0 ? (hi - lo) / 15.f : 1.f;
+      double mse = 0.0;
+      for (int64_t i = 0; i < group; ++i) {
+        const float v = clampf(grp[i], lo, hi);
+        const float q = clampf(std::nearbyint((v - lo) / sc), 0.f, 15.f);
+        const float d = grp[i] - (lo + q * sc);
+        mse += (double)d * d;
+      }
+      mse /= (double)group;
+      if (mse < best) {
+        best = (float)mse;
+        blo = lo;
+        bhi = hi;
+      }
+    }
+    for (int64_t i = 0; i < group; ++i) grp[i] = clampf(grp[i], blo, bhi);
+  });
+  return quantize_int4_asym(clipped, group);
+}
+
+torch::Tensor dequantize_int4_asym(torch::Tensor packed, torch::Tensor scales, torch::Tensor offsets, int64_t group) {
+  const int64_t N = packed.size(0), D = packed.size(1) * 2, G = scales.size(1);
+  auto out = torch::empty({N, D}, torch::kFloat32);
+  const uint8_t* pp = packed.contiguous().data_ptr<uint8_t>();
+  const float* sp = scales.contiguous().data_ptr<float>();
+  const float* op = offsets.contiguous().data_ptr<float>();
+  float* o = out.data_ptr<float>();
+  prange(N, [&](int64_t r) {for (int64_t c = 0; c < D; ++c) {
+      const uint8_t b = pp[r * (D / 2) + c / 2];
+      const float q = (float)((c & 1) ? (b >> 4) : (b & 0xF));
+      const int64_t g = c / group;
+      o[r * D + c] = op[r * G + g] + q * sp[r * G + g];
+    }});
+  return out;
+}
+
+// out[b, i] = sum_j x[b, j] * (offset[i, g(j)] + q[i, j] * scale[i, g(j)])  (fp32 accumulation)
+torch::Tensor quantized_matmul_int4(torch::Tensor packed, torch::Tensor scales, torch::Tensor offsets, torch::Tensor x,
+                                    int64_t group) {
+  check_cpu_f32_2d(x, "x");
+  const int64_t O = packed.size(0), K = packed.size(1) * 2, B = x.size(0), G = scales.size(1);
+  TORCH_CHECK(x.size(1) == K, "x.size(1) must equal packed.size(1)*2");
+  auto out = torch::empty({B, O}, torch::kFloat32);
+  const uint8_t* pp = packed.contiguous().data_ptr<uint8_t>();
+  const float* sp = scales.contiguous().data_ptr<float>();
+  const float* op = offsets.contiguous().data_ptr<float>();
+  const float* xp = x.data_ptr<float>();
+  float* o = out.data_ptr<float>();
+  at::parallel_for(0, O, 1, [&](int64_t i0, int64_t i1) {
+    std::vector<float> wrow(K);
+    for (int64_t i = i0; i < i1; ++i) {
+      for (int64_t c = 0; c < K; ++c) {
+        const uint8_t b = pp[i * (K / 2) + c / 2];
+        const float q = (float)((c & 1) ? (b >> 4) : (b & 0xF));
+        wrow[c] = op[i * G + c / group] + q * sp[i * G + c / group];
+      }
+      for (int64_t bb = 0; bb < B; ++bb) {
+        const float* xr = xp + bb * K;
+        float acc = 0.f;
+        for (int64_t c = 0; c < K; ++c) acc += xr[c] * wrow[c];
+        o[bb * O + i] = acc;
+      }
+    }
+  });
+  return out;
+}
+
+// ---------------------------------------------------------------- INT4 symmetric legacy (__q4/__s4)
+std::vector<torch::Tensor> quantize_int4_sym(torch::Tensor x, int64_t group) {
+  check_cpu_f32_2d(x, "x");
+  const int64_t N = x.size(0), D = x.size(1), G = D / group;
+  auto packed = torch::empty({N, D / 2}, torch::kUInt8);
+  auto scales = torch::empty({N, G}, torch::kFloat32);
+  const float* xp = x.data_ptr<float>();
+  uint8_t* pp = packed.data_ptr<uint8_t>();
+  float* sp = scales.data_ptr<float>();
+  prange(N, [&](int64_t r) {
+    for (int64_t g = 0; g < G; ++g) {
+      float am = 0.f;
+      for (int64_t i = g * group; i < (g + 1) * group; ++i) am = std::max(am, std::fabs(xp[r * D + i]));
+      sp[r * G + g] = am == 0.f ? 1.f : am / 7.f;
+    }
+    for (int64_t i = 0; i < D / 2; ++i) {
+      uint8_t qq[2];
+      for (int k = 0; k < 2; ++k) {
+        const int64_t j = 2 * i + k;
+        const float q = clampf(std::round(xp[r * D + j] / sp[r * G + j / group]), -7.f, 7.f);
+        qq[k] = (uint8_t)((int)q + 7);
+      }
+      pp[r * (D / 2) + i] = (uint8_t)((qq[0] & 0xF) | ((qq[1] & 0xF) << 4));
+    }
+  });
+  return {packed, scales};
+}
+
+torch::Tensor dequantize_int4_sym(torch::Tensor packed, torch::Tensor scales, int64_t group) {
+  const int64_t N = packed.size(0), D = packed.size(1) * 2, G = scales.size(1);
+  auto out = torch::empty({N, D}, torch::kFloat32);
+  const uint8_t* pp = packed.contiguous().data_ptr<uint8_t>();
+  const float* sp = scales.contiguous().data_ptr<float>();
+  float* o = out.data_ptr<float>();
+  prange(N, [&](int64_t r) {for (int64_t c = 0; c < D; ++c) {
+      const uint8_t b = pp[r * (D / 2) + c / 2];
+      const int q = (int)((c & 1) ? (b >> 4) : (b & 0xF)) - 7;
+      o[r * D + c] = (float)q * sp[r * G + c / group];
+    }});
+  return out;
+}
+
+// ---------------------------------------------------------------- NF4
+std::vector<torch::Tensor> quantize_nf4(torch::Tensor x, int64_t group) {
+  check_cpu_f32_2d(x, "x");
+  const int64_t N = x.size(0), D = x.size(1), G = D / group;
+  auto packed = torch::empty({N, D / 2}, torch::kUInt8);
+  auto scales = torch::empty({N, G}, torch::kFloat32);
+  const float* xp = x.data_ptr<float>();
+  uint8_t* pp = packed.data_ptr<uint8_t>();
+  float* sp = scales.data_ptr<float>();
+  prange(N, [&](int64_t r) {
+    for (int64_t g = 0; g < G; ++g) {
+      float am = 0.f;
+      for (int64_t i = g * group; i < (g + 1) * group; ++i) am = std::max(am, std::fabs(xp[r * D + i]));
+      sp[r * G + g] = am == 0.f ? 1.f : am;
+    }
+    for (int64_t i = 0; i < D / 2; ++i) {
+      uint8_t qq[2];
+      for (int k = 0; k < 2; ++k) {
+        const int64_t j = 2 * i + k;
+        const float v = xp[r * D + j] / sp[r * G + j / group];
+        int best = 0;
+        float bd = INFINITY;
+        for (int l = 0; l < 16; ++l) {
+          const float d = std::fabs(v - kNF4[l]);
+          if (d < bd) {
+            bd = d;
+            best = l;
+          }
+        }
+        qq[k] = (uint8_t)best;
+      }
+      pp[r * (D / 2) + i] = (uint8_t)(qq[0] | (qq[1] << 4));
+    }
+  });
+  return {packed, scales};
+}
+
+torch::Tensor dequantize_nf4(torch::Tensor packed, torch::Tensor scales, int64_t group) {
+  const int64_t N = packed.size(0), D = packed.size(1) * 2, G = scales.size(1);
+  auto out = torch::empty({N, D}, torch::kFloat32);
+  const uint8_t* pp = packed.contiguous().data_ptr<uint8_t>();
+  const float* sp = scales.contiguous().data_ptr<float>();
+  float* o = out.data_ptr<float>();
+  prange(N, [&](int64_t r) {for (int64_t c = 0; c < D; ++c) {
+      const uint8_t b = pp[r * (D / 2) + c / 2];
+      o[r * D + c] = kNF4[(c & 1) ? (b >> 4) : (b & 0xF)] * sp[r * G + c / group];
+    }});
+  return out;
+}
+
+// ---------------------------------------------------------------- INT3 symmetric, 8 values per 3 bytes
+std::vector<torch::Tensor> pack_int3(torch::Tensor x, int64_t group) {
+  check_cpu_f32_2d(x, "x");
+  const int64_t N = x.size(0), D = x.size(1), G = D / group;
+  TORCH_CHECK(D % group == 0, "group must divide columns");
+  const int64_t padded = (D + 7) / 8 * 8, NP = padded * 3 / 8;
+  auto packed = torch::zeros({N, NP}, torch::kUInt8);
+  auto scales = torch::empty({N, G}, torch::kFloat32);
+  const float* xp = x.data_ptr<float>();
+  uint8_t* pp = packed.data_ptr<uint8_t>();
+  float* sp = scales.data_ptr<float>();
+  prange(N, [&](int64_t r) {
+    for (int64_t g = 0; g < G; ++g) {
+      float am = 0.f;
+      for (int64_t i = g * group; i < (g + 1) * group; ++i) am = std::max(am, std::fabs(xp[r * D + i]));
+      sp[r * G + g] = am == 0.f ? 1.f : am / 3.f;
+    }
+    for (int64_t ch = 0; ch < (D + 7) / 8; ++ch) {
+      uint32_t bits = 0;
+      for (int b = 0; b < 8; ++b) {
+        const int64_t j = ch * 8 + b;
+        uint32_t v = 0;
+        if (j < D) v = (uint32_t)((int)clampf(std::round(xp[r * D + j] / sp[r * G + j / group]), -3.f, 3.f) & 7);
+        bits |= v << (3 * b);
+      }
+      for (int k = 0; k < 3; ++k) pp[r * NP + ch * 3 + k] = (uint8_t)((bits >> (8 * k)) & 0xFF);
+    }
+  });
+  return {packed, scales};
+}
+
+torch::Tensor unpack_int3(torch::Tensor packed, torch::Tensor scales, int64_t group, int64_t n_cols) {
+  const int64_t N = packed.size(0), NP = packed.size(1), G = scales.size(1);
+  auto out = torch::empty({N, n_cols}, torch::kFloat32);
+  const uint8_t* pp = packed.contiguous().data_ptr<uint8_t>();
+  const float* sp = scales.contiguous().data_ptr<float>();
+  float* o = out.data_ptr<float>();
+  prange(N, [&](int64_t r) {for (int64_t j = 0; j < n_cols; ++j) {
+      const int64_t ch = j / 8, b = j % 8;
+      uint32_t bits = 0;
+      for (int k = 0; k < 3; ++k) {
+        const int64_t idx = ch * 3 + k;
+        bits |= (uint32_t)(idx < NP ? pp[r * NP + idx] : 0) << (8 * k);
+      }
+      int v = (int)((bits >> (3 * b)) & 7);
+      if (v & 4) v -= 8;  // sign-extend 3-bit two's complement
+      o[r * n_cols + j] = (float)v * sp[r * G + j / group];
+    }});
+  (void)G;
+  return out;
+}
+
+// ---------------------------------------------------------------- INT2 asymmetric, 4 per byte
+std::vector<torch::Tensor> quantize_int2(torch::Tensor x, int64_t group) {
+  check_cpu_f32_2d(x, "x");
+  const int64_t N = x.size(0), D = x.size(1), G = D / group;
+  TORCH_CHECK(D % group == 0 && D % 4 == 0, "columns must be divisible by group and 4");
+  auto packed = torch::empty({N, D / 4}, torch::kUInt8);
+  auto scales = torch::empty({N, G}, torch::kFloat32);
+  auto offsets = torch::empty({N, G}, torch::kFloat32);
+  const float* xp = x.data_ptr<float>();
+  uint8_t* pp = packed.data_ptr<uint8_t>();
+  float* sp = scales.data_ptr<float>();
+  float* op = offsets.data_ptr<float>();
+  prange(N, [&](int64_t r) {
+    for (int64_t g = 0; g < G; ++g) {
+      float mn = INFINITY, mx = -INFINITY;
+      for (int64_t i = g * group; i < (g + 1) * group; ++i) {
+        mn = std::min(mn, xp[r * D + i]);
+        mx = std::max(mx, xp[r * D + i]);
+      }
+      sp[r * G + g] = mx == mn ? 1.f : (mx - mn) / 3.f;
+      op[r * G + g] = mn;
+    }
+    for (int64_t i = 0; i < D / 4; ++i) {
+      uint8_t byte = 0;
+      for (int b = 0; b < 4; ++b) {
+        const int64_t j = i * 4 + b, g = j / group;
+        const uint8_t q = (uint8_t)clampf(std::round((xp[r * D + j] - op[r * G + g]) / sp[r * G + g]), 0.f, 3.f);
+        byte |= (uint8_t)((q & 3) << (2 * b));
+      }
+      pp[r * (D / 4) + i] = byte;
+    }
+  });
+  return {packed, scales, offsets};
+}
+
+torch::Tensor dequantize_int2(torch::Tensor packed, torch::Tensor scales, torch::Tensor offsets, int64_t group) {
+  const int64_t N = packed.size(0), D = packed.size(1) * 4, G = scales.size(1);
+  auto out = torch::empty({N, D}, torch::kFloat32);
+  const uint8_t* pp = packed.contiguous().data_ptr<uint8_t>();
+  const float* sp = scales.contiguous().data_ptr<float>();
+  const float* op = offsets.contiguous().data_ptr<float>();
+  float* o = out.data_ptr<float>();
+  prange(N, [&](int64_t r) {for (int64_t c = 0; c < D; ++c) {
+      const uint8_t q = (pp[r * (D / 4) + c / 4] >> (2 * (c % 4))) & 3;
+      o[r * D + c] = op[r * G + c / group] + (float)q * sp[r * G + c / group];
+    }});
+  return out;
+}
+
+// ---------------------------------------------------------------- KV page codecs (oracle for kv_write.cu)
+// x: [rows, D] -> codes [rows, D*bits/8] u8, scales [rows, nscale] f32 (fp16-rounded like the kernel)
+std::vector<torch::Tensor> kv_quantize(torch::Tensor x, int64_t fmt, int64_t group) {
+  check_cpu_f32_2d(x, "x");
+  const int64_t R = x.size(0), D = x.size(1), NG = D / group;
+  const bool asym = (fmt == 4 || fmt == 5);
+  const int bits = fmt == 1 || fmt == 4 ? 8 : fmt == 2 || fmt == 5 ? 4 : 2;
+  const float qmax = fmt == 1 ? 127.f : fmt == 2 ? 7.5f : fmt == 3 ? 1.5f : fmt == 4 ? 255.f : 15.f;
+  auto codes = torch::zeros({R, D * bits / 8}, torch::kUInt8);
+  auto scales = torch::zeros({R, NG * (asym ? 2 : 1)}, torch::kFloat32);
+  const float* xp = x.data_ptr<float>();
+  uint8_t* cp = codes.data_ptr<uint8_t>();
+  float* sp = scales.data_ptr<float>();
+  const int64_t CB = D * bits / 8, NS = NG * (asym ? 2 : 1);
+  auto h16 = [](float v) { return c10::Half(v).operator float(); };
+  prange(R, [&](int64_t r) {
+    for (int64_t g = 0; g < NG; ++g) {
+      const float* v = xp + r * D + g * group;
+      float lo = INFINITY, hi = -INFINITY, am = 0.f;
+      for (int64_t i = 0; i < group; ++i) {
+        lo = std::min(lo, v[i]);
+        hi = std::max(hi, v[i]);
+        am = std::max(am, std::fabs(v[i]));
+      }
+      float s, z = 0.f;
+      if (asym) {
+        s = (hi - lo) / qmax;
+        if (s == 0.f) s = 1.f;
+        s = h16(s);
+        z = h16(lo);
+        sp[r * NS + 2 * g] = s;
+        sp[r * NS + 2 * g + 1] = z;
+      } else {
+        s = h16(std::max(am, 1e-8f) / qmax);
+        if (s == 0.f) s = 6e-8f;
+        sp[r * NS + g] = s;
+      }
+      for (int64_t i = 0; i < group; ++i) {
+        float t;
+        if (asym) t = std::nearbyint((v[i] - z) / s);
+        else if (fmt == 1) t = std::nearbyint(v[i] / s);
+        else t = std::nearbyint(v[i] / s + qmax);
+        int q;
+        if (fmt == 1) q = (int)clampf(t, -128.f, 127.f);
+        else if (fmt == 4) q = (int)clampf(t, 0.f, 255.f);
+        else if (bits == 4) q = (int)clampf(t, 0.f, 15.f);
+        else q = (int)clampf(t, 0.f, 3.f);
+        const int64_t d = g * group + i;
+        if (bits == 8) cp[r * CB + d] = (uint8_t)(q & 0xFF);
+        else if (bits == 4) cp[r * CB + d / 2] |= (uint8_t)((q & 0xF) << (4 * (d & 1)));
+        else cp[r * CB + d / 4] |= (uint8_t)((q & 3) << (2 * (d & 3)));
+      }
+    }
+  });
+  return {codes, scales};
+}
+
+torch::Tensor kv_dequantize(torch::Tensor codes, torch::Tensor scales, int64_t fmt, int64_t group, int64_t D) {
+  const int64_t R = codes.size(0), CB = codes.size(1), NS = scales.size(1);
+  const bool asym = (fmt == 4 || fmt == 5);
+  const int bits = fmt == 1 || fmt == 4 ? 8 : fmt == 2 || fmt == 5 ? 4 : 2;
+  auto out = torch::empty({R, D}, torch::kFloat32);
+  const uint8_t* cp = codes.contiguous().data_ptr<uint8_t>();
+  const float* sp = scales.contiguous().data_ptr<float>();
+  float* o = out.data_ptr<float>();
+  prange(R, [&](int64_t r) {for (int64_t d = 0; d < D; ++d) {
+      const int64_t g = d / group;
+      int q;
+      if (bits == 8) q = (fmt == 1) ? (int)(int8_t)cp[r * CB + d] : (int)cp[r * CB + d];
+      else if (bits == 4) q = (cp[r * CB + d / 2] >> (4 * (d & 1))) & 0xF;
+      else q = (cp[r * CB + d / 4] >> (2 * (d & 3))) & 3;
+      float v;
+      if (asym) v = (float)q * sp[r * NS + 2 * g] + sp[r * NS + 2 * g + 1];
+      else if (fmt == 1) v = (float)q * sp[r * NS + g];
+      else if (fmt == 2) v = ((float)q - 7.5f) * sp[r * NS + g];
+      else v = ((float)q - 1.5f) * sp[r * NS + g];
+      o[r * D + d] = v;
+    }});
+  return out;
+}
+
+}  // namespace
+
+void register_cpu(pybind11::module& m) {
+  auto c = m.def_submodule("cpu", "C++ CPU reference kernels (restating squish_quant_rs)");
+  c.def("quantize_int8", &quantize_int8);
+  c.def("dequantize_int8", &dequantize_int8);
+  c.def("quantize_int4_asym", &quantize_int4_asym);
+  c.def("quantize_int4_asym_mse", &quantize_int4_asym_mse);
+  c.def("dequantize_int4_asym", &dequantize_int4_asym);
+  c.def("quantized_matmul_int4", &quantized_matmul_int4);
+  c.def("quantize_int4_sym", &quantize_int4_sym);
+  c.def("dequantize_int4_sym", &dequantize_int4_sym);
+  c.def("quantize_nf4", &quantize_nf4);
+  c.def("dequantize_nf4", &dequantize_nf4);
+  c.def("pack_int3", &pack_int3);
+  c.def("unpack_int3", &unpack_int3);
+  c.def("quantize_int2", &quantize_int2);
+  c.def("dequantize_int2", &dequantize_int2);
+  c.def("kv_quantize", &kv_quantize);
+  c.def("kv_dequantize", &kv_dequantize);
+}
+
+}  // namespace sqcpu

@@ -1,0 +1,76 @@
+// kernels.h — launch interfaces of the non-GEMM CUDA kernels.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace sq {
+
+struct RopeKvParams {
+  const __nv_bfloat16* qkv;  // [T, ld_qkv]: Hq*D q | Hkv*D k | Hkv*D v
+  int ld_qkv;
+  const int* positions;      // [T]
+  const float* cos_sin;      // [max_pos, D]: cos(D/2) | sin(D/2)
+  __nv_bfloat16* q_out;      // [T, Hq, D]
+  const int* slot_mapping;   // [T] page*page_size + offset, -1 = do not store
+  uint8_t* k_codes;
+  __half* k_scales;
+  uint8_t* v_codes;
+  __half* v_scales;
+  int Hq, Hkv, D, page_size, group, fmt_k, fmt_v;
+};
+
+struct AttnParams {
+  const __nv_bfloat16* q;  // [rows, ld_q] (Hq*D per row)
+  int ld_q;
+  const uint8_t* k_codes;
+  const __half* k_scales;
+  const uint8_t* v_codes;
+  const __half* v_scales;
+  const int* block_tables;  // [B, bt_stride]
+  int bt_stride;
+  __nv_bfloat16* out;       // [rows, ld_out]
+  int ld_out;
+  int Hq, Hkv, D, page_size, group, fmt_k, fmt_v;
+  float sm_scale;
+  // decode: one query row per sequence b (row b of q/out)
+  const int* seq_lens;      // [B] kv length including the current token
+  int B;
+  int splits, tiles_per_split;
+  float* o_part;            // [B, Hq, splits, D]
+  float* lse_part;          // [B, Hq, splits]
+  // prefill (varlen, causal over the paged context)
+  const int* tile_seq;      // [n_tiles] sequence index of the work tile
+  const int* tile_q0;       // [n_tiles] first query (within the chunk) of the tile
+  const int* q_start;       // [B] first row of the sequence's chunk in q/out
+  const int* q_len;         // [B]
+  const int* ctx_len;       // [B] kv length after this chunk
+  int n_tiles;
+};
+
+cudaError_t rope_kv_write_launch(const RopeKvParams& p, int T, cudaStream_t s);
+cudaError_t rmsnorm_launch(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, const int* row_idx,
+                           int rows, int H, int ldx, int ldy, float eps, cudaStream_t s);
+cudaError_t paged_decode_attn_launch(const AttnParams& p, cudaStream_t s);
+cudaError_t paged_prefill_attn_launch(const AttnParams& p, cudaStream_t s);
+
+struct SamplerParams {
+  const __nv_bfloat16* logits;  // [B, ld]
+  int ld, V, B;
+  const float* temperature;     // [B] (<= 0 -> greedy)
+  const float* top_p;           // [B] (>= 1 -> off)
+  const int* top_k;             // [B] (<= 0 -> off)
+  const float* min_p;           // [B] (<= 0 -> off)
+  const float* rep_penalty;     // [B] (== 1 -> off)
+  const int* hist;              // [B, hist_stride] recent token ids for the repetition penalty, -1 padded
+  int hist_stride;
+  const uint32_t* allow_mask;   // [B, ceil(V/32)] grammar bitmask (bit set = allowed) or nullptr
+  uint64_t seed;
+  const int* step;              // [B] per-row counter mixed into the RNG stream
+  int* out_tokens;              // [B]
+  float* out_logprob;           // [B] log-probability of the chosen token (after processing) or nullptr
+};
+cudaError_t sampler_launch(const SamplerParams& p, float* work, cudaStream_t s);
+
+}  // namespace sq

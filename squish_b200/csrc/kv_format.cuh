@@ -1,0 +1,118 @@
+// kv_format.cuh — quantized KV page formats shared by the KV-write and attention kernels.
+//
+// A layer's KV cache is two code pools and two scale pools:
+//   codes  [num_pages][Hkv][page_size][code_bytes]     uint8
+//   scales [num_pages][Hkv][page_size][n_scale]        fp16
+// one row per (page, kv head, token slot). Formats follow the reference codecs:
+//   KV_INT4 : symmetric 16 levels, x = (idx - 7.5) * absmax/7.5 per (token, head, group)
+//             (squish/kv/kv_cache.py:297-375, generalised from whole-head to group G)
+//   KV_INT2 : symmetric 4 levels {-1.5,-0.5,0.5,1.5} * absmax/1.5 (kv_cache.py:159-240)
+//   KV_INT8 : symmetric, x = q * absmax/127 (kv_cache.py:78-119)
+//   KV_K8 / KV_V4 : the k8v4 codec, asymmetric affine per group, keys 8-bit (255 levels),
+//             values 4-bit (15 levels), scale = (hi-lo)/qmax, zero = lo (squish/kv/k8v4_codec.py:64-137)
+//   KV_BF16 : unquantized bf16.
+// Nibble order: low nibble = even dim (as in the reference packers); 2-bit: dim 4i+j at bits 2j.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace sq {
+
+enum KvFmt : int { KV_BF16 = 0, KV_INT8 = 1, KV_INT4 = 2, KV_INT2 = 3, KV_K8 = 4, KV_V4 = 5 };
+
+__host__ __device__ constexpr int kv_bits(int f) {
+  return f == KV_BF16 ? 16 : (f == KV_INT8 || f == KV_K8) ? 8 : (f == KV_INT4 || f == KV_V4) ? 4 : 2;
+}
+__host__ __device__ constexpr bool kv_asym(int f) { return f == KV_K8 || f == KV_V4; }
+__host__ __device__ constexpr int kv_code_bytes(int f, int D) { return D * kv_bits(f) / 8; }
+__host__ __device__ constexpr int kv_nscale(int f, int D, int G) {
+  return f == KV_BF16 ? 0 : (D / G) * (kv_asym(f) ? 2 : 1);
+}
+__host__ __device__ constexpr float kv_qmax(int f) {
+  return f == KV_INT8 ? 127.f : f == KV_INT4 ? 7.5f : f == KV_INT2 ? 1.5f : f == KV_K8 ? 255.f : 15.f;
+}
+
+struct KvLayer {
+  const uint8_t* codes;
+  const __half* scales;
+};
+
+__device__ __forceinline__ uint32_t bf2u(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+
+// Dequantize 8 consecutive dims [d8, d8+8) of one (page, head, token) row into 8 bf16.
+template <int FMT>
+__device__ __forceinline__ uint4 kv_dequant8(const uint8_t* __restrict__ row_codes,
+                                             const __half* __restrict__ row_scales, int d8, int G) {
+  if constexpr (FMT == KV_BF16) {
+    return *reinterpret_cast<const uint4*>(row_codes + d8 * 2);
+  } else if constexpr (FMT == KV_INT4 || FMT == KV_V4) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(row_codes + d8 / 2);
+    const int g = d8 / G;
+    float s, z;
+    if constexpr (FMT == KV_INT4) {
+      s = __half2float(row_scales[g]);
+      z = -7.5f * s;
+    } else {
+      s = __half2float(row_scales[2 * g]);
+      z = __half2float(row_scales[2 * g + 1]);
+    }
+    const __nv_bfloat162 s2 = __floats2bfloat162_rn(s, s), z2 = __floats2bfloat162_rn(z, z);
+    const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.f, 128.f);
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t b = (w >> (8 * i)) & 0xFFu;
+      uint32_t t = (b & 0xFu) | ((b >> 4) << 16) | 0x43004300u;
+      __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&t);
+      v = __hfma2(__hsub2(v, k128), s2, z2);
+      o[i] = bf2u(v);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+  } else if constexpr (FMT == KV_INT2) {
+    const uint32_t w = *reinterpret_cast<const uint16_t*>(row_codes + d8 / 4);
+    const float s = __half2float(row_scales[d8 / G]);
+    const __nv_bfloat162 s2 = __floats2bfloat162_rn(s, s), z2 = __floats2bfloat162_rn(-1.5f * s, -1.5f * s);
+    const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.f, 128.f);
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t lo = (w >> (4 * i)) & 0x3u, hi = (w >> (4 * i + 2)) & 0x3u;
+      uint32_t t = lo | (hi << 16) | 0x43004300u;
+      __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&t);
+      v = __hfma2(__hsub2(v, k128), s2, z2);
+      o[i] = bf2u(v);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+  } else {  // KV_INT8 (signed) or KV_K8 (unsigned, asymmetric)
+    const uint2 w = *reinterpret_cast<const uint2*>(row_codes + d8);
+    const int g = d8 / G;
+    float s, z;
+    if constexpr (FMT == KV_INT8) {
+      s = __half2float(row_scales[g]);
+      z = 0.f;
+    } else {
+      s = __half2float(row_scales[2 * g]);
+      z = __half2float(row_scales[2 * g + 1]);
+    }
+    const uint32_t ww[2] = {w.x, w.y};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t word = ww[i >> 1];
+      const int sh = (i & 1) * 16;
+      float a, b;
+      if constexpr (FMT == KV_INT8) {
+        a = (float)(int8_t)((word >> sh) & 0xFF);
+        b = (float)(int8_t)((word >> (sh + 8)) & 0xFF);
+      } else {
+        a = (float)((word >> sh) & 0xFF);
+        b = (float)((word >> (sh + 8)) & 0xFF);
+      }
+      o[i] = bf2u(__floats2bfloat162_rn(fmaf(a, s, z), fmaf(b, s, z)));
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+}  // namespace sq

@@ -1,0 +1,463 @@
+// w4a16_gemm.cu — weight-only INT4 (asymmetric, group-scaled) GEMM for sm_100a.
+//
+//   Y[M, N] = X[M, K] (bf16) . dequant(W)[N, K]^T  (+ bias) (+ residual)
+//   or, for a fused gate/up projection, Y[M, N/2] = silu(gate) * up.
+//
+// The math this replaces is the reference's fused INT4 matmul
+// (squish_quant_rs/src/lib.rs:5511 `quantized_matmul_int4`, numpy oracle
+// squish/quant/quantizer.py:632 `_quantized_matmul_int4_numpy`): W_hat = offset + q*scale
+// per (row, group), q the unsigned nibble. Here it runs on the 5th-generation tensor cores:
+//
+//  * swap-AB: weight rows are the MMA M side (128 per tile = one TMEM lane each), tokens
+//    the MMA N side (16..256), so a decode batch of 1-64 tokens still fills the M side;
+//  * packed weights and their (scale, zero) pairs are stored tile-major on the device (one
+//    contiguous 4 KiB + gpk*512 B block per 128 rows x 64 columns) and streamed with 1-D
+//    bulk copies into a deep shared-memory ring (L2 evict-first: read once per launch);
+//  * activations arrive by TMA (2-D tensor map, 128-byte swizzle, zero fill past M and K);
+//  * dequant warps turn nibbles into bf16 with the 0x4300 exponent trick plus one bf16x2
+//    subtract and one bf16x2 FMA per pair, and write the canonical SWIZZLE_128B K-major
+//    operand layout the MMA reads;
+//  * one thread issues tcgen05.mma (kind::f16, fp32 accumulators in TMEM) and retires ring
+//    slots with tcgen05.commit;
+//  * epilogue warps read TMEM with tcgen05.ld. With split-K, every split writes an fp32
+//    partial into a workspace and the last CTA to arrive on an output tile sums the
+//    partials in split order (deterministic) and applies the epilogue.
+//
+// Every wait is bounded (sm100.cuh); on timeout *status is set and the kernel still
+// releases its TMEM before exiting.
+#include "sm100.cuh"
+#include "w4a16_gemm.h"
+
+namespace sq {
+
+namespace {
+
+constexpr int BM = 128;                    // weight rows per MMA tile
+constexpr int BK = 64;                     // K per stage = one 128-byte bf16 swizzle row
+constexpr int W_TILE_BYTES = BM * BK / 2;  // 4096
+constexpr int A_TILE_BYTES = BM * BK * 2;  // 16384
+
+template <int BN_, int NT_, int DQ_SPLIT_>
+struct Cfg {
+  static constexpr int BN = BN_;
+  static constexpr int NT = NT_;                // 128-row weight tiles per CTA
+  static constexpr int kDq = 128 * DQ_SPLIT_;   // dequant threads
+  static constexpr int kChunks = 2 / DQ_SPLIT_; // 32-column chunks per dequant thread per tile
+  static constexpr int kThreads = 128 + kDq;    // warps 0-3 control, 4.. dequant (4-7 also epilogue)
+  static constexpr int kXBytes = BN * 128;
+  static constexpr int kTmemCols = (NT * BN <= 32)    ? 32
+                                   : (NT * BN <= 64)  ? 64
+                                   : (NT * BN <= 128) ? 128
+                                   : (NT * BN <= 256) ? 256
+                                                      : 512;
+};
+
+struct Layout {
+  uint32_t x_off, w_off, w_stage, bar_off, total;
+};
+
+__host__ __device__ inline Layout make_layout(int bn, int nt, int gpk, int rw, int rx, int ra) {
+  Layout L;
+  L.x_off = (uint32_t)(ra * nt * A_TILE_BYTES);
+  L.w_off = L.x_off + (uint32_t)(rx * bn * 128);
+  L.w_stage = (uint32_t)(nt * (W_TILE_BYTES + gpk * BM * 4));
+  L.bar_off = L.w_off + (uint32_t)rw * L.w_stage;
+  L.bar_off = (L.bar_off + 15u) & ~15u;
+  L.total = L.bar_off + (uint32_t)(2 * rw + 2 * rx + 2 * ra + 1) * 8u + 16u;
+  return L;
+}
+
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+
+// 8 nibbles of one 32-bit word (interleaved so that (w >> 4e) & 0x000F000F holds columns
+// 2e and 2e+1) -> 8 bf16 = one 16-byte operand chunk.
+__device__ __forceinline__ uint4 dq_word(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 z2) {
+  const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.f, 128.f);
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    uint32_t t = ((w >> (4 * e)) & 0x000F000Fu) | 0x43004300u;  // bf16(128 + q)
+    __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&t);
+    v = __hsub2(v, k128);   // exact q
+    v = __hfma2(v, s2, z2); // q*scale + zero, one rounding
+    o[e] = bf2_bits(v);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.f + __expf(-g)); }
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <class C>
+__global__ void __launch_bounds__(C::kThreads, 1)
+    w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const W4A16Params p) {
+  constexpr int BN = C::BN;
+  constexpr int NT = C::NT;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int gpk = p.gpk;
+  const int ring_w = p.ring_w, ring_x = p.ring_x, ring_a = p.ring_a;
+  const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a);
+  uint8_t* a_ring = smem;
+  uint8_t* x_ring = smem + L.x_off;
+  uint8_t* w_ring = smem + L.w_off;
+  uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+  uint64_t* w_empty = w_full + ring_w;
+  uint64_t* x_full = w_empty + ring_w;
+  uint64_t* x_empty = x_full + ring_x;
+  uint64_t* a_full = x_empty + ring_x;
+  uint64_t* a_empty = a_full + ring_a;
+  uint64_t* acc_full = a_empty + ring_a;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  int* flag_slot = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nblk = blockIdx.x;
+  const int mblk = blockIdx.y;
+  const int split = blockIdx.z;
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+  const int nkb = max(0, kb1 - kb0);
+  int* status = p.status;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ring_w; ++i) {
+      mbar_init(&w_full[i], 1);
+      mbar_init(&w_empty[i], C::kDq);
+    }
+    for (int i = 0; i < ring_x; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 1);
+    }
+    for (int i = 0; i < ring_a; ++i) {
+      mbar_init(&a_full[i], C::kDq);
+      mbar_init(&a_empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_mbar_init();
+    prefetch_tmap(&xmap);
+  }
+  if (warp == 3) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ weight producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      const size_t tile_words = W_TILE_BYTES / 4;
+      const size_t sz_words = (size_t)gpk * BM;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % ring_w;
+        if (!mbar_wait(&w_empty[s], ((i / ring_w) & 1) ^ 1, status, SQ_ERR_TIMEOUT_W)) break;
+        uint8_t* dst = w_ring + s * L.w_stage;
+        mbar_expect_tx(&w_full[s], L.w_stage);
+        const int kb = kb0 + i;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const size_t rb = (size_t)nblk * NT + t;
+          bulk_g2s_hint(dst + t * W_TILE_BYTES, p.wq + (rb * p.kb_total + kb) * tile_words, W_TILE_BYTES,
+                        &w_full[s], pol);
+          bulk_g2s_hint(dst + NT * W_TILE_BYTES + t * sz_words * 4, p.sz + (rb * p.kb_total + kb) * sz_words,
+                        (uint32_t)(sz_words * 4), &w_full[s], pol);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ activation producer (TMA)
+    if (lane == 0) {
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % ring_x;
+        if (!mbar_wait(&x_empty[s], ((i / ring_x) & 1) ^ 1, status, SQ_ERR_TIMEOUT_X)) break;
+        mbar_expect_tx(&x_full[s], C::kXBytes);
+        tma_load_2d(x_ring + s * C::kXBytes, &xmap, (kb0 + i) * BK, mblk * BN, &x_full[s]);
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      for (int i = 0; i < nkb; ++i) {
+        const int sx = i % ring_x, sa = i % ring_a;
+        if (!mbar_wait(&x_full[sx], (i / ring_x) & 1, status, SQ_ERR_TIMEOUT_X)) break;
+        if (!mbar_wait(&a_full[sa], (i / ring_a) & 1, status, SQ_ERR_TIMEOUT_A)) break;
+        tc_fence_after();
+        const uint32_t xa = smem_u32(x_ring + sx * C::kXBytes);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const uint32_t aa = smem_u32(a_ring + (sa * NT + t) * A_TILE_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16_ss(tmem + t * BN, sdesc_sw128(aa + k * 32), sdesc_sw128(xa + k * 32), idesc,
+                        (i > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(&x_empty[sx]);
+        mma_commit(&a_empty[sa]);
+      }
+      mma_commit(acc_full);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------ dequant warps
+    const int d = threadIdx.x - 128;
+    const int r = d & (BM - 1);
+    const int part = d >> 7;
+    const int sw_row = r & 7;
+    const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + sw_row * 128);
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % ring_w, sa = i % ring_a;
+      if (!mbar_wait(&w_full[s], (i / ring_w) & 1, status, SQ_ERR_TIMEOUT_W)) break;
+      const uint8_t* wst = w_ring + s * L.w_stage;
+      const uint32_t* szst = reinterpret_cast<const uint32_t*>(wst + NT * W_TILE_BYTES);
+      uint4 wv[NT][C::kChunks];
+      uint32_t szv[NT][C::kChunks][4];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+#pragma unroll
+        for (int cc = 0; cc < C::kChunks; ++cc) {
+          const int c = part * C::kChunks + cc;
+          wv[t][cc] = *reinterpret_cast<const uint4*>(wst + t * W_TILE_BYTES + (c * BM + r) * 16);
+#pragma unroll
+          for (int w = 0; w < 4; ++w) szv[t][cc][w] = szst[(t * gpk + (((c * 4 + w) * gpk) >> 3)) * BM + r];
+        }
+      }
+      mbar_arrive(&w_empty[s]);
+      if (!mbar_wait(&a_empty[sa], ((i / ring_a) & 1) ^ 1, status, SQ_ERR_TIMEOUT_A)) break;
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        uint8_t* adst = a_ring + (sa * NT + t) * A_TILE_BYTES + row_off;
+#pragma unroll
+        for (int cc = 0; cc < C::kChunks; ++cc) {
+          const int c = part * C::kChunks + cc;
+          const uint32_t ww[4] = {wv[t][cc].x, wv[t][cc].y, wv[t][cc].z, wv[t][cc].w};
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const uint32_t szw = szv[t][cc][w];
+            const __nv_bfloat16 sc = __ushort_as_bfloat16((unsigned short)(szw & 0xFFFFu));
+            const __nv_bfloat16 ze = __ushort_as_bfloat16((unsigned short)(szw >> 16));
+            const uint4 o = dq_word(ww[w], __bfloat162bfloat162(sc), __bfloat162bfloat162(ze));
+            *reinterpret_cast<uint4*>(adst + (((c * 4 + w) ^ sw_row) << 4)) = o;
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&a_full[sa]);
+    }
+  }
+
+  // ------------------------------------------------ epilogue: warps 4..7 = TMEM lane quarters
+  if (warp >= 4 && warp < 8) {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;  // row within a 128-row weight tile
+    const int m0 = mblk * BN;
+    const bool single = (p.splits == 1);
+    const bool silu_mode = (p.epilogue == EPI_SILU_MUL);
+    float* xch = reinterpret_cast<float*>(a_ring);  // operand buffers are dead once acc_full fires
+
+    // Emit 16 consecutive token columns of tile t for this thread's row.
+    auto emit16 = [&](int t, int c0, const float(&val)[16]) {
+      if (silu_mode) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) xch[j * 128 + row] = val[j];
+        epi_bar();
+        if (row < 64) {
+          const int nn = (nblk * NT + t) * 64 + row;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c0 + j;
+            const float u = xch[j * 128 + row + 64];
+            if (m < p.M && nn < (p.N >> 1)) p.y[(size_t)m * p.ldy + nn] = __float2bfloat16(silu(val[j]) * u);
+          }
+        }
+        epi_bar();
+      } else {
+        const int n = (nblk * NT + t) * BM + row;
+        if (n < p.N) {
+          const float b = p.bias ? __bfloat162float(p.bias[n]) : 0.f;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c0 + j;
+            if (m < p.M) {
+              float acc = val[j] + b;
+              if (p.residual) acc += __bfloat162float(p.residual[(size_t)m * p.ldr + n]);
+              p.y[(size_t)m * p.ldy + n] = __float2bfloat16(acc);
+            }
+          }
+        }
+      }
+    };
+
+    const bool have_acc = (nkb > 0) && mbar_wait(acc_full, 0, status, SQ_ERR_TIMEOUT_ACC);
+    tc_fence_after();
+#pragma unroll 1
+    for (int t = 0; t < NT; ++t) {
+      const int n = (nblk * NT + t) * BM + row;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t v[16];
+        if (have_acc) {
+          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(t * BN + c0), v);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0u;
+        }
+        if (single) {
+          float val[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) val[j] = __uint_as_float(v[j]);
+          emit16(t, c0, val);
+        } else if (n < p.N) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c0 + j;
+            if (m < p.M) p.ws[((size_t)split * p.M + m) * p.N + n] = __uint_as_float(v[j]);
+          }
+        }
+      }
+    }
+    if (!single) {
+      __threadfence();
+      epi_bar();
+      const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+      if (threadIdx.x == 128) {
+        const int prev = atomicAdd(&p.counters[tile], 1);
+        *flag_slot = (prev == p.splits - 1) ? 1 : 0;
+      }
+      epi_bar();
+      if (*flag_slot) {
+        __threadfence();
+#pragma unroll 1
+        for (int t = 0; t < NT; ++t) {
+          const int n = (nblk * NT + t) * BM + row;
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float val[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = m0 + c0 + j;
+              float acc = 0.f;
+              if (m < p.M && n < p.N)
+                for (int s = 0; s < p.splits; ++s) acc += __ldcg(&p.ws[((size_t)s * p.M + m) * p.N + n]);
+              val[j] = acc;
+            }
+            emit16(t, c0, val);
+          }
+        }
+        if (threadIdx.x == 128) p.counters[tile] = 0;  // self-reset for the next launch
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 3) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+template <class C>
+cudaError_t launch_cfg(const CUtensorMap& xmap, W4A16Params p, int rw, int rx, int ra, cudaStream_t stream) {
+  p.ring_w = rw;
+  p.ring_x = rx;
+  p.ring_a = ra;
+  const Layout L = make_layout(C::BN, C::NT, p.gpk, rw, rx, ra);
+  const size_t smem = (size_t)L.total + 1024;  // + alignment slack
+  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
+  auto kern = w4a16_gemm_kernel<C>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((p.N + BM * C::NT - 1) / (BM * C::NT), (p.M + C::BN - 1) / C::BN, p.splits);
+  kern<<<grid, C::kThreads, smem, stream>>>(xmap, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// Ring depths: W stage = nt*(4 KiB + gpk*512 B), X stage = bn*128 B, A stage = nt*16 KiB.
+// Decode shapes (small bn) are HBM-bound: a deep weight ring keeps ~70 KiB in flight per SM.
+cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s) {
+  const int wr = p.gpk >= 4 ? 10 : 14;
+  if (nt == 1) {
+    switch (bn) {
+      case 16: return launch_cfg<Cfg<16, 1, 2>>(xmap, p, wr, 4, 4, s);
+      case 32: return launch_cfg<Cfg<32, 1, 2>>(xmap, p, wr, 4, 4, s);
+      case 64: return launch_cfg<Cfg<64, 1, 2>>(xmap, p, 12, 4, 3, s);
+      case 128: return launch_cfg<Cfg<128, 1, 2>>(xmap, p, 8, 4, 3, s);
+      case 256: return launch_cfg<Cfg<256, 1, 2>>(xmap, p, 6, 3, 2, s);
+      default: return cudaErrorInvalidValue;
+    }
+  } else if (nt == 2) {
+    switch (bn) {
+      case 128: return launch_cfg<Cfg<128, 2, 2>>(xmap, p, 6, 4, 2, s);
+      case 256: return launch_cfg<Cfg<256, 2, 2>>(xmap, p, 4, 3, 2, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  return cudaErrorInvalidValue;
+}
+
+// ---------------------------------------------------------------------------------
+// Repack the canonical npy-dir INT4 asymmetric layout into the tile-major device layout.
+//   src: packed (N, K/2) u8 with lo nibble = even column; scales/zeros (N, G) fp32.
+//   dst: wq [Np/128][KB][2][128][4] u32, sz [Np/128][KB][gpk][128] u32 (bf16 scale | bf16 zero << 16)
+//   Np = N rounded up to 256, KB = ceil(K/64); padding rows/columns dequantize to 0.
+__global__ void repack_int4_kernel(const uint8_t* __restrict__ packed, const float* __restrict__ scales,
+                                   const float* __restrict__ zeros, uint32_t* __restrict__ wq,
+                                   uint32_t* __restrict__ sz, int N, int K, int group, int kb_total, int n_pad,
+                                   int gpk) {
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)n_pad * kb_total) return;
+  const int n = (int)(idx % n_pad);
+  const int kb = (int)(idx / n_pad);
+  const int rb = n / 128, r = n % 128;
+  const int G = (K + group - 1) / group;
+  const int pos[8] = {0, 16, 4, 20, 8, 24, 12, 28};
+  uint32_t* wt = wq + ((size_t)rb * kb_total + kb) * 1024;
+  for (int c = 0; c < 2; ++c) {
+    for (int w = 0; w < 4; ++w) {
+      uint32_t word = 0;
+      for (int e = 0; e < 8; ++e) {
+        const int col = kb * 64 + c * 32 + w * 8 + e;
+        uint32_t qv = 0;
+        if (n < N && col < K) {
+          const uint8_t b = packed[(size_t)n * (K / 2) + col / 2];
+          qv = (col & 1) ? (b >> 4) : (b & 0xF);
+        }
+        word |= qv << pos[e];
+      }
+      wt[(c * 128 + r) * 4 + w] = word;
+    }
+  }
+  uint32_t* st = sz + ((size_t)rb * kb_total + kb) * gpk * 128;
+  for (int j = 0; j < gpk; ++j) {
+    const int col = kb * 64 + j * (64 / gpk);
+    const int g = col / group;
+    float sc = 0.f, ze = 0.f;
+    if (n < N && col < K && g < G) {
+      sc = scales[(size_t)n * G + g];
+      ze = zeros[(size_t)n * G + g];
+    }
+    const uint32_t sb = __bfloat16_as_ushort(__float2bfloat16(sc));
+    const uint32_t zb = __bfloat16_as_ushort(__float2bfloat16(ze));
+    st[j * 128 + r] = sb | (zb << 16);
+  }
+}
+
+cudaError_t repack_int4_launch(const uint8_t* packed, const float* scales, const float* zeros, uint32_t* wq,
+                               uint32_t* sz, int N, int K, int group, cudaStream_t s) {
+  const int kb_total = (K + 63) / 64;
+  const int n_pad = (N + 255) / 256 * 256;
+  const int gpk = group >= 64 ? 1 : 64 / group;
+  const long total = (long)n_pad * kb_total;
+  repack_int4_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(packed, scales, zeros, wq, sz, N, K, group,
+                                                                     kb_total, n_pad, gpk);
+  return cudaGetLastError();
+}
+
+}  // namespace sq

@@ -1,0 +1,33 @@
+// w4a16_gemm.h — host/device interface of the INT4 weight-only tcgen05 GEMM.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace sq {
+
+enum : int { EPI_PLAIN = 0, EPI_SILU_MUL = 1 };
+
+struct W4A16Params {
+  const uint32_t* wq;             // tile-major packed nibbles  [N/128][KB][2][128][4]
+  const uint32_t* sz;             // tile-major (scale | zero<<16) bf16 pairs [N/128][KB][gpk][128]
+  const __nv_bfloat16* bias;      // [N] or nullptr
+  const __nv_bfloat16* residual;  // [M, ldr] added in the epilogue, or nullptr (may alias y)
+  __nv_bfloat16* y;               // [M, ldy]
+  float* ws;                      // split-K partials [splits][M][N] (splits > 1)
+  int* counters;                  // per output tile arrival counters, zero on entry, reset on exit
+  int* status;                    // device status word (0 = ok)
+  int M, N, K;
+  int ldy, ldr;
+  int kb_total, kb_per_split, splits;
+  int gpk;                        // (scale, zero) groups per 64-column k-block: 1, 2 or 4
+  int epilogue;                   // EPI_PLAIN | EPI_SILU_MUL
+  int ring_w, ring_x, ring_a;     // set by the launcher
+};
+
+cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s);
+cudaError_t repack_int4_launch(const uint8_t* packed, const float* scales, const float* zeros, uint32_t* wq,
+                               uint32_t* sz, int N, int K, int group, cudaStream_t s);
+
+}  // namespace sq

@@ -1,0 +1,178 @@
+"""Python wrappers of the native kernels.
+
+Every wrapper launches on the current CUDA stream and allocates nothing when the
+caller provides the output: scratch memory (split-K partials, tile counters, the
+decode split partials, the sampler's fp32 row buffer) lives in a per-device
+:class:`Workspace`, so whole decode steps can be captured in CUDA graphs.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .._ext import native
+
+# KV page formats understood by the attention kernels (csrc/kv_format.cuh)
+KV_FORMATS = {"bf16": (0, 0), "int8": (1, 1), "int4": (2, 2), "int2": (3, 3), "k8v4": (4, 5)}
+KV_BITS = {0: 16, 1: 8, 2: 4, 3: 2, 4: 8, 5: 4}
+KV_ASYM = {4, 5}
+
+
+class Workspace:
+    """Per-device scratch buffers shared by all kernels of one stream."""
+
+    GEMM_WS_FLOATS = 12 * 1024 * 1024
+    GEMM_COUNTERS = 1 << 16
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.gemm_ws = torch.empty(self.GEMM_WS_FLOATS, dtype=torch.float32, device=device)
+        self.gemm_counters = torch.zeros(self.GEMM_COUNTERS, dtype=torch.int32, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self._attn_o = torch.empty(0, dtype=torch.float32, device=device)
+        self._attn_lse = torch.empty(0, dtype=torch.float32, device=device)
+        self._sampler = torch.empty(0, dtype=torch.float32, device=device)
+
+    def attn_buffers(self, b: int, hq: int, splits: int, d: int):
+        need = b * hq * splits * d
+        if self._attn_o.numel() < need:
+            self._attn_o = torch.empty(max(need, 1 << 20), dtype=torch.float32, device=self.device)
+            self._attn_lse = torch.empty(max(need // d, 1 << 16), dtype=torch.float32, device=self.device)
+        return self._attn_o, self._attn_lse
+
+    def reserve_attn(self, b: int, hq: int, splits: int, d: int):
+        self.attn_buffers(b, hq, splits, d)
+
+    def sampler_buffer(self, rows: int, vocab: int):
+        need = rows * vocab
+        if self._sampler.numel() < need:
+            self._sampler = torch.empty(need, dtype=torch.float32, device=self.device)
+        return self._sampler
+
+    def check(self) -> None:
+        """Raise if any kernel recorded an error (a bounded wait that timed out)."""
+        code = int(self.status.item())
+        if code != 0:
+            self.status.zero_()
+            raise RuntimeError(f"squish_b200 kernel reported status {code} (bounded wait timed out)")
+
+
+_WORKSPACES: dict[int, Workspace] = {}
+
+
+def workspace(device: torch.device | None = None) -> Workspace:
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _WORKSPACES.get(idx)
+    if ws is None:
+        ws = Workspace(torch.device("cuda", idx))
+        _WORKSPACES[idx] = ws
+    return ws
+
+
+@dataclass
+class Int4Weight:
+    """An INT4 asymmetric group-quantized weight in the tile-major device layout."""
+
+    wq: torch.Tensor  # int32 [Np/128, KB, 1024]
+    sz: torch.Tensor  # int32 [Np/128, KB, gpk*128]
+    n: int
+    k: int
+    group: int
+    bias: torch.Tensor | None = None
+
+    @property
+    def nbytes(self) -> int:
+        return self.wq.numel() * 4 + self.sz.numel() * 4
+
+
+def prepare_int4_weight(packed: torch.Tensor, scales: torch.Tensor, offsets: torch.Tensor, k: int, group: int,
+                        device, bias: torch.Tensor | None = None) -> Int4Weight:
+    """Upload an npy-dir INT4 asymmetric weight (``__q4a/__s4a/__z4a``) and repack it on the GPU."""
+    dev = torch.device(device)
+    p = packed.to(dev, torch.uint8).contiguous()
+    s = scales.to(dev, torch.float32).contiguous()
+    z = offsets.to(dev, torch.float32).contiguous()
+    wq, sz = native().repack_int4(p, s, z, int(k), int(group))
+    b = None if bias is None else bias.to(dev, torch.bfloat16).contiguous()
+    return Int4Weight(wq=wq, sz=sz, n=int(packed.shape[0]), k=int(k), group=int(group), bias=b)
+
+
+def gemm_plan(m: int, n: int, k: int):
+    bn, nt, splits, kps, tiles = native().gemm_plan(m, n, k)
+    return {"bn": bn, "nt": nt, "splits": splits, "kb_per_split": kps, "tiles": tiles}
+
+
+EPI_PLAIN, EPI_SILU_MUL = 0, 1
+
+
+def w4a16_linear(x: torch.Tensor, w: Int4Weight, out: torch.Tensor | None = None,
+                 residual: torch.Tensor | None = None, silu_mul: bool = False,
+                 ws: Workspace | None = None) -> torch.Tensor:
+    """y = x @ dequant(w)^T (+bias) (+residual); with ``silu_mul`` the weight rows are
+    interleaved gate/up blocks of 64 and y = silu(gate) * up has N/2 columns."""
+    ws = ws or workspace(x.device)
+    m = x.shape[0]
+    ncols = w.n // 2 if silu_mul else w.n
+    if out is None:
+        out = torch.empty((m, ncols), dtype=torch.bfloat16, device=x.device)
+    native().w4a16_gemm(x, w.wq, w.sz, w.n, w.k, w.group, out, w.bias, residual,
+                        EPI_SILU_MUL if silu_mul else EPI_PLAIN, ws.gemm_ws, ws.gemm_counters, ws.status)
+    return out
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None,
+            row_idx: torch.Tensor | None = None) -> torch.Tensor:
+    rows = x.shape[0] if row_idx is None else row_idx.numel()
+    if out is None:
+        out = torch.empty((rows, x.shape[1]), dtype=torch.bfloat16, device=x.device)
+    native().rmsnorm(x, weight, out, row_idx, float(eps))
+    return out
+
+
+def rope_kv_write(qkv, positions, cos_sin, q_out, slot_mapping, k_codes, k_scales, v_codes, v_scales,
+                  hq: int, hkv: int, d: int, page_size: int, group: int, fmt_k: int, fmt_v: int) -> None:
+    native().rope_kv_write(qkv, positions, cos_sin, q_out, slot_mapping, k_codes, k_scales, v_codes, v_scales,
+                           hq, hkv, d, page_size, group, fmt_k, fmt_v)
+
+
+def decode_splits(batch: int, hkv: int, max_ctx: int, num_sms: int = 148) -> tuple[int, int]:
+    """Split count for flash-decoding: aim for ~4 CTAs per SM, >= 4 tiles per split."""
+    tiles = max(1, math.ceil(max_ctx / 16))
+    base = max(1, batch * hkv)
+    want = max(1, (4 * num_sms + base - 1) // base)
+    splits = max(1, min(want, tiles // 4 if tiles >= 8 else 1))
+    tps = math.ceil(tiles / splits)
+    splits = math.ceil(tiles / tps)
+    return splits, tps
+
+
+def paged_decode_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables, seq_lens, out, hq, hkv, d,
+                           page_size, group, fmt_k, fmt_v, sm_scale, max_ctx: int, ws: Workspace | None = None,
+                           splits: tuple[int, int] | None = None):
+    ws = ws or workspace(q.device)
+    b = seq_lens.shape[0]
+    s, tps = splits or decode_splits(b, hkv, max_ctx)
+    o_part, lse = ws.attn_buffers(b, hq, s, d)
+    native().paged_decode_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables, seq_lens, out, o_part,
+                                    lse, hq, hkv, d, page_size, group, fmt_k, fmt_v, float(sm_scale), s, tps)
+    return out
+
+
+def paged_prefill_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables, tile_seq, tile_q0, q_start,
+                            q_len, ctx_len, n_tiles, out, hq, hkv, d, page_size, group, fmt_k, fmt_v, sm_scale):
+    native().paged_prefill_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables, tile_seq, tile_q0,
+                                     q_start, q_len, ctx_len, int(n_tiles), out, hq, hkv, d, page_size, group,
+                                     fmt_k, fmt_v, float(sm_scale))
+    return out
+
+
+def sample(logits, out_tokens, temperature=None, top_p=None, top_k=None, min_p=None, rep_penalty=None, hist=None,
+           allow_mask=None, seed: int = 0, step=None, out_logprob=None, ws: Workspace | None = None):
+    ws = ws or workspace(logits.device)
+    work = ws.sampler_buffer(logits.shape[0], logits.shape[1])
+    native().sample(logits, temperature, top_p, top_k, min_p, rep_penalty, hist, allow_mask, int(seed), step,
+                    out_tokens, out_logprob, work)
+    return out_tokens
