@@ -180,7 +180,8 @@ void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<to
 void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin, torch::Tensor q_out,
                    torch::Tensor slot_mapping, torch::Tensor k_codes, torch::Tensor k_scales, torch::Tensor v_codes,
                    torch::Tensor v_scales, int64_t Hq, int64_t Hkv, int64_t D, int64_t page_size, int64_t group,
-                   int64_t fmt_k, int64_t fmt_v) {
+                   int64_t fmt_k, int64_t fmt_v, c10::optional<torch::Tensor> q_norm,
+                   c10::optional<torch::Tensor> k_norm, double norm_eps) {
   CHECK_CUDA(qkv);
   CHECK_DT(qkv, torch::kBFloat16);
   CHECK_DT(positions, torch::kInt32);
@@ -205,6 +206,9 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos
   p.group = (int)group;
   p.fmt_k = (int)fmt_k;
   p.fmt_v = (int)fmt_v;
+  p.q_norm = optr<__nv_bfloat16>(q_norm);
+  p.k_norm = optr<__nv_bfloat16>(k_norm);
+  p.norm_eps = (float)norm_eps;
   CUDA_OK(sq::rope_kv_write_launch(p, (int)qkv.size(0), cur_stream()));
 }
 
@@ -309,6 +313,23 @@ void sample(torch::Tensor logits, c10::optional<torch::Tensor> temperature, c10:
   CUDA_OK(sq::sampler_launch(p, ptr<float>(work), cur_stream()));
 }
 
+std::vector<torch::Tensor> quantize_int4_asym_cuda(torch::Tensor x, int64_t group, int64_t n_clip) {
+  CHECK_CUDA(x);
+  CHECK_CONTIG(x);
+  TORCH_CHECK(x.dim() == 2, "x must be 2-D");
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 || x.scalar_type() == torch::kBFloat16, "x must be f32 or bf16");
+  const int64_t rows = x.size(0), cols = x.size(1);
+  TORCH_CHECK(cols % group == 0 && group % 2 == 0, "group must divide columns and be even");
+  const c10::cuda::CUDAGuard g(x.device());
+  auto packed = torch::empty({rows, cols / 2}, x.options().dtype(torch::kUInt8));
+  auto scales = torch::empty({rows, cols / group}, x.options().dtype(torch::kFloat32));
+  auto offsets = torch::empty({rows, cols / group}, x.options().dtype(torch::kFloat32));
+  CUDA_OK(sq::quantize_int4_asym_launch(x.data_ptr(), x.scalar_type() == torch::kBFloat16, ptr<uint8_t>(packed),
+                                        ptr<float>(scales), ptr<float>(offsets), (int)rows, (int)cols, (int)group,
+                                        (int)n_clip, cur_stream()));
+  return {packed, scales, offsets};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -321,5 +342,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_decode_attention", &paged_decode_attention);
   m.def("paged_prefill_attention", &paged_prefill_attention);
   m.def("sample", &sample);
+  m.def("quantize_int4_asym", &quantize_int4_asym_cuda);
   sqcpu::register_cpu(m);
 }

@@ -19,6 +19,9 @@ struct RopeKvParams {
   uint8_t* v_codes;
   __half* v_scales;
   int Hq, Hkv, D, page_size, group, fmt_k, fmt_v;
+  const __nv_bfloat16* q_norm;  // [D] per-head RMSNorm weight applied before RoPE (Qwen3), or nullptr
+  const __nv_bfloat16* k_norm;
+  float norm_eps;
 };
 
 struct AttnParams {
@@ -72,5 +75,8 @@ struct SamplerParams {
   float* out_logprob;           // [B] log-probability of the chosen token (after processing) or nullptr
 };
 cudaError_t sampler_launch(const SamplerParams& p, float* work, cudaStream_t s);
+
+cudaError_t quantize_int4_asym_launch(const void* x, bool bf16, uint8_t* packed, float* scales, float* offsets,
+                                      int rows, int cols, int group, int n_clip, cudaStream_t s);
 
 }  // namespace sq

@@ -124,7 +124,17 @@ __global__ void rope_kv_write_kernel(RopeKvParams p) {
     const __nv_bfloat16* src = row + (size_t)j * D;
 #pragma unroll
     for (int jj = 0; jj < J; ++jj) v[jj] = __bfloat162float(src[lane + 32 * jj]);
-    if (j < p.Hq + p.Hkv) {  // rotate q and k
+    if (j < p.Hq + p.Hkv) {  // (optional per-head RMSNorm, Qwen3) then rotate q and k
+      const __nv_bfloat16* nw = (j < p.Hq) ? p.q_norm : p.k_norm;
+      if (nw != nullptr) {
+        float ss = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < J; ++jj) ss += v[jj] * v[jj];
+        ss = warp_sum(ss);
+        const float inv = rsqrtf(ss / (float)D + p.norm_eps);
+#pragma unroll
+        for (int jj = 0; jj < J; ++jj) v[jj] = v[jj] * inv * __bfloat162float(nw[lane + 32 * jj]);
+      }
       float r[J];
 #pragma unroll
       for (int jj = 0; jj < J / 2; ++jj) {

@@ -1,0 +1,265 @@
+"""LLMEngine: the public inference API (continuous batching over a paged, quantized KV cache).
+
+    eng = LLMEngine.from_preset("qwen2.5-7b", device="cuda")
+    rid = eng.add_request(prompt_token_ids, SamplingParams(max_tokens=64))
+    while eng.has_unfinished():
+        for out in eng.step(): ...
+
+Each ``step()`` schedules one batch (scheduler.py), builds the flat step inputs, runs the
+model runner (one H2D copy of the packed metadata, one D2H copy of the sampled token
+ids), then appends tokens, applies stop conditions and publishes full KV blocks for
+prefix reuse.
+"""
+from __future__ import annotations
+
+import itertools
+import time
+import zlib
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from ..kv.paged import BlockManager, bytes_per_page
+from ..models.config import ModelConfig, QuantConfig, get_preset
+from ..models.decoder import StepInputs, prefill_tiles
+from ..models.weights import Checkpoint, random_checkpoint
+from .request import Request, RequestOutput, Status
+from .sampling import SamplingParams
+from .scheduler import Schedule, Scheduler
+
+
+@dataclass
+class EngineConfig:
+    max_num_seqs: int = 64
+    max_num_batched_tokens: int = 2048
+    max_model_len: int = 4096
+    gpu_memory_utilization: float = 0.85
+    num_pages: int | None = None
+    enable_prefix_caching: bool = True
+    cuda_graphs: bool = True
+    chunk_align: int = 0
+    hist_window: int = 64
+    seed: int = 0
+
+
+@dataclass
+class EngineStats:
+    steps: int = 0
+    prompt_tokens: int = 0
+    generated_tokens: int = 0
+    prefix_hit_tokens: int = 0
+    preemptions: int = 0
+    ttfts: list = field(default_factory=list)
+    h2d_bytes: int = 0
+    d2h_bytes: int = 0
+
+
+class LLMEngine:
+    def __init__(self, runner, cfg: ModelConfig, qcfg: QuantConfig, ecfg: EngineConfig, num_pages: int):
+        self.runner = runner
+        self.cfg, self.qcfg, self.ecfg = cfg, qcfg, ecfg
+        self.blocks = BlockManager(num_pages, qcfg.page_size, ecfg.enable_prefix_caching, model_key=cfg.name)
+        self.scheduler = Scheduler(self.blocks, ecfg.max_num_seqs, ecfg.max_num_batched_tokens, ecfg.max_model_len,
+                                   ecfg.chunk_align)
+        self.requests: dict[str, Request] = {}
+        self._ids = itertools.count()
+        self.stats = EngineStats()
+        self.max_pages = (ecfg.max_model_len + qcfg.page_size - 1) // qcfg.page_size
+        self.graphs = None
+
+    # ------------------------------------------------------------------ construction
+    @staticmethod
+    def plan_pages(cfg: ModelConfig, qcfg: QuantConfig, ecfg: EngineConfig, device) -> int:
+        if ecfg.num_pages:
+            return ecfg.num_pages
+        dev = torch.device(device)
+        if dev.type != "cuda":
+            return max(64, ecfg.max_num_seqs * ((ecfg.max_model_len + qcfg.page_size - 1) // qcfg.page_size))
+        free, total = torch.cuda.mem_get_info(dev)
+        budget = free - (1.0 - ecfg.gpu_memory_utilization) * total
+        per = bytes_per_page(cfg, qcfg)
+        return max(16, int(budget // per))
+
+    @classmethod
+    def from_checkpoint(cls, ck: Checkpoint, device="cuda", ecfg: EngineConfig | None = None, **kw) -> "LLMEngine":
+        ecfg = ecfg or EngineConfig(**kw)
+        dev = torch.device(device)
+        if dev.type == "cuda":
+            from ..models.decoder import CudaRunner
+
+            # weights first, then size the page pool from what is left
+            runner = CudaRunner(ck, dev, num_pages=1, max_num_tokens=ecfg.max_num_batched_tokens,
+                                max_num_seqs=ecfg.max_num_seqs, max_model_len=ecfg.max_model_len,
+                                free_checkpoint=True)
+            del runner.pools
+            torch.cuda.empty_cache()
+            num_pages = cls.plan_pages(ck.config, ck.quant, ecfg, dev)
+            from ..kv.paged import KVPools
+
+            runner.pools = KVPools(ck.config, ck.quant, num_pages, dev)
+        else:
+            from ..models.decoder import TorchPagedRunner
+
+            num_pages = cls.plan_pages(ck.config, ck.quant, ecfg, dev)
+            runner = TorchPagedRunner(ck, num_pages, ecfg.max_model_len)
+        eng = cls(runner, ck.config, ck.quant, ecfg, num_pages)
+        if dev.type == "cuda" and ecfg.cuda_graphs:
+            from .cuda_graph import DecodeGraphs
+
+            eng.graphs = DecodeGraphs(eng)
+        return eng
+
+    @classmethod
+    def from_preset(cls, name: str, device="cuda", seed: int = 0, ecfg: EngineConfig | None = None,
+                    **kw) -> "LLMEngine":
+        cfg, q = get_preset(name)
+        dev = torch.device(device)
+        ck = random_checkpoint(cfg, q, seed=seed, device=dev)
+        return cls.from_checkpoint(ck, dev, ecfg, **kw)
+
+    # ------------------------------------------------------------------ requests
+    def add_request(self, prompt: list[int], params: SamplingParams | None = None, rid: str | None = None) -> str:
+        params = (params or SamplingParams()).validate()
+        rid = rid or f"req-{next(self._ids)}"
+        req = Request(rid, list(map(int, prompt)), params)
+        self.scheduler.add(req)
+        self.requests[rid] = req
+        return rid
+
+    def abort(self, rid: str) -> None:
+        req = self.requests.get(rid)
+        if req is None or req.status is Status.FINISHED:
+            return
+        if req in self.scheduler.waiting:
+            self.scheduler.waiting.remove(req)
+            req.status = Status.FINISHED
+            req.finish_reason = "abort"
+        else:
+            self.scheduler.finish(req, "abort")
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_work()
+
+    # ------------------------------------------------------------------ step
+    def build_inputs(self, sched: Schedule) -> StepInputs:
+        ps = self.qcfg.page_size
+        entries = sched.decode + sched.prefill
+        T = sum(e.n for e in entries)
+        ids = np.empty(T, dtype=np.int32)
+        pos = np.empty(T, dtype=np.int32)
+        slots = np.empty(T, dtype=np.int32)
+        nb = len(entries)
+        maxp = max((len(e.req.pages) for e in entries), default=1)
+        if self.graphs is not None:
+            maxp = self.max_pages
+        bt = np.zeros((nb, max(maxp, 1)), dtype=np.int32)
+        rows, samp = [], []
+        off = 0
+        for i, e in enumerate(entries):
+            r = e.req
+            toks = r.tokens
+            ids[off:off + e.n] = toks[e.start:e.start + e.n]
+            p = np.arange(e.start, e.start + e.n, dtype=np.int32)
+            pos[off:off + e.n] = p
+            pg = np.asarray(r.pages, dtype=np.int32)
+            slots[off:off + e.n] = pg[p // ps] * ps + p % ps
+            bt[i, :len(r.pages)] = pg
+            if e.sample:
+                rows.append(off + e.n - 1)
+                samp.append(r)
+            off += e.n
+        nd = len(sched.decode)
+        dl = np.asarray([e.start + 1 for e in sched.decode], dtype=np.int32)
+        ql = np.asarray([e.n for e in sched.prefill], dtype=np.int32)
+        ctx = np.asarray([e.start + e.n for e in sched.prefill], dtype=np.int32)
+        qs = np.zeros(len(ql), dtype=np.int32)
+        if len(ql):
+            qs[1:] = np.cumsum(ql)[:-1]
+        tseq, tq0 = prefill_tiles(ql)
+        B = len(samp)
+        temp = np.asarray([r.params.temperature for r in samp], dtype=np.float32)
+        topp = np.asarray([r.params.top_p for r in samp], dtype=np.float32)
+        topk = np.asarray([r.params.top_k for r in samp], dtype=np.int32)
+        minp = np.asarray([r.params.min_p for r in samp], dtype=np.float32)
+        rep = np.asarray([r.params.repetition_penalty for r in samp], dtype=np.float32)
+        step = np.asarray([r.rng_step + (zlib.crc32(r.rid.encode()) & 0xFFFF) * 65536 for r in samp],
+                          dtype=np.int64)
+        step = (step & 0x7FFFFFFF).astype(np.int32)
+        hist = None
+        if B and (rep != 1.0).any():
+            hw = self.ecfg.hist_window
+            hist = np.full((B, hw), -1, dtype=np.int32)
+            for i, r in enumerate(samp):
+                t = r.tokens[-hw:]
+                hist[i, :len(t)] = t
+        return StepInputs(ids, pos, slots, nd, dl, qs, ql, ctx, tseq, tq0, bt, np.asarray(rows, dtype=np.int32), temp,
+                          topp, topk, minp, rep, step, hist, self.ecfg.seed,
+                          int(dl.max()) if nd else 0), samp
+
+    def step(self) -> list[RequestOutput]:
+        sched = self.scheduler.schedule()
+        self.stats.preemptions += len(sched.preempted)
+        if sched.empty:
+            return []
+        st, samp = self.build_inputs(sched)
+        if self.graphs is not None and not sched.prefill and self.graphs.can_run(st):
+            toks = self.graphs.run(st)
+        else:
+            toks = self.runner.execute(st)
+        self.stats.steps += 1
+        self.stats.h2d_bytes += st.h2d_bytes()
+        self.stats.d2h_bytes += 4 * len(samp)
+        now = time.perf_counter()
+        outs: list[RequestOutput] = []
+        # advance computed counters, publish full blocks
+        for e in sched.decode + sched.prefill:
+            r = e.req
+            r.num_computed = e.start + e.n
+            if not e.sample:
+                self.stats.prompt_tokens += e.n
+        for r, t in zip(samp, toks.tolist()):
+            if r.first_token_time is None:
+                r.first_token_time = now
+                self.stats.ttfts.append(now - r.arrival)
+                self.stats.prefix_hit_tokens += r.prefix_hit_tokens
+            r.output.append(int(t))
+            r.rng_step += 1
+            self.stats.generated_tokens += 1
+            self._publish_blocks(r)
+            reason = self._stop_reason(r, int(t))
+            if reason:
+                self.scheduler.finish(r, reason)
+                r.finish_time = now
+            outs.append(RequestOutput(r.rid, [int(t)], reason is not None, reason, len(r.prompt), len(r.output)))
+        return outs
+
+    def _publish_blocks(self, r: Request) -> None:
+        full = r.num_computed // self.qcfg.page_size
+        if full > r.registered_blocks:
+            r.chain_hash = self.blocks.register_blocks(r.tokens, r.pages, r.registered_blocks,
+                                                       full - r.registered_blocks, r.chain_hash)
+            r.registered_blocks = full
+
+    def _stop_reason(self, r: Request, tok: int) -> str | None:
+        p = r.params
+        n = len(r.output)
+        if n >= p.min_tokens:
+            if not p.ignore_eos and tok == self.cfg.eos_token_id:
+                return "stop"
+            if tok in p.stop_token_ids:
+                return "stop"
+        if n >= p.max_tokens:
+            return "length"
+        if r.total_len >= self.ecfg.max_model_len:
+            return "length"
+        return None
+
+    # ------------------------------------------------------------------ convenience
+    def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None
+                 ) -> list[list[int]]:
+        ps = params if isinstance(params, list) else [params] * len(prompts)
+        rids = [self.add_request(p, sp) for p, sp in zip(prompts, ps)]
+        while self.has_unfinished():
+            self.step()
+        return [self.requests[r].output for r in rids]

@@ -1,0 +1,445 @@
+"""Decoder forward over the paged KV cache.
+
+:class:`StepInputs` is one engine iteration, flattened: decode sequences first (one
+token each), then prefill chunks. :class:`CudaRunner` runs it with the sm_100a kernels:
+
+  embed -> [RMSNorm -> W4A16 qkv(+bias) -> RoPE+KV-quant write -> paged attention
+  (decode split-K kernel | prefill causal kernel) -> W4A16 o_proj (+residual in the
+  epilogue) -> RMSNorm -> W4A16 gate_up with the SiLU*up epilogue -> W4A16 down_proj
+  (+residual)] x L -> RMSNorm of the logit rows -> W4A16 lm_head -> fused sampler.
+
+Activation buffers are allocated once for the step token budget, so decode steps
+can be captured in CUDA graphs (engine/cuda_graph.py). :class:`TorchPagedRunner` is the
+same step in plain PyTorch on the CPU (dequantized weights, the C++ KV codec), used as
+the oracle of the engine path in CPU tests.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from .. import ops
+from .._ext import native
+from ..kv.paged import KVPools
+from ..ops.kernels import KV_FORMATS, Int4Weight
+from .config import ModelConfig, QuantConfig
+from .reference import rope_table
+from .weights import Checkpoint, QTensor
+
+
+@dataclass
+class StepInputs:
+    input_ids: np.ndarray          # int32 [T]
+    positions: np.ndarray          # int32 [T]
+    slot_mapping: np.ndarray       # int32 [T]
+    num_decode: int
+    decode_seq_lens: np.ndarray    # int32 [Bd]
+    prefill_q_start: np.ndarray    # int32 [Bp] (relative to the first prefill row)
+    prefill_q_len: np.ndarray      # int32 [Bp]
+    prefill_ctx_len: np.ndarray    # int32 [Bp]
+    tile_seq: np.ndarray           # int32 [n_tiles]
+    tile_q0: np.ndarray            # int32 [n_tiles]
+    block_tables: np.ndarray       # int32 [Bd + Bp, max_pages]
+    logits_rows: np.ndarray        # int32 [B]
+    temperature: np.ndarray        # f32 [B]
+    top_p: np.ndarray              # f32 [B]
+    top_k: np.ndarray              # int32 [B]
+    min_p: np.ndarray              # f32 [B]
+    rep_penalty: np.ndarray        # f32 [B]
+    rng_step: np.ndarray           # int32 [B]
+    hist: np.ndarray | None = None  # int32 [B, H] recent tokens for the repetition penalty
+    seed: int = 0
+    max_decode_ctx: int = 0
+    all_logits: bool = False       # also return the logits of every logit row (spec verify)
+
+    @property
+    def num_tokens(self) -> int:
+        return int(self.input_ids.shape[0])
+
+    @property
+    def num_prefill(self) -> int:
+        return int(self.prefill_q_len.shape[0])
+
+    def h2d_bytes(self) -> int:
+        n = 0
+        for v in self.__dict__.values():
+            if isinstance(v, np.ndarray):
+                n += v.nbytes
+        return n
+
+
+def prefill_tiles(q_len: np.ndarray, tile: int = 32) -> tuple[np.ndarray, np.ndarray]:
+    seq, q0 = [], []
+    for i, ql in enumerate(q_len.tolist()):
+        for s in range(0, ql, tile):
+            seq.append(i)
+            q0.append(s)
+    return np.asarray(seq, dtype=np.int32), np.asarray(q0, dtype=np.int32)
+
+
+# ----------------------------------------------------------------------------- device weights
+@dataclass
+class LayerWeights:
+    ln1: torch.Tensor
+    ln2: torch.Tensor
+    qkv: Int4Weight
+    o: Int4Weight
+    gate_up: Int4Weight | None
+    down: Int4Weight | None
+    q_norm: torch.Tensor | None = None
+    k_norm: torch.Tensor | None = None
+    moe: object | None = None
+
+
+def _cat_q4a(parts: list[QTensor]) -> QTensor:
+    return QTensor("q4a", (sum(p.shape[0] for p in parts), parts[0].shape[1]),
+                   packed=torch.cat([p.packed for p in parts]), scales=torch.cat([p.scales for p in parts]),
+                   offsets=torch.cat([p.offsets for p in parts]), group=parts[0].group)
+
+
+def _interleave_gate_up(gate: QTensor, up: QTensor) -> QTensor:
+    """Rows [g0:64, u0:64, g64:128, u64:128, ...] (F padded to a multiple of 64 with zero
+    rows), the layout the SiLU*up GEMM epilogue expects."""
+    f = gate.shape[0]
+    fp = (f + 63) // 64 * 64
+
+    def pad(t, fill=0):
+        if t.shape[0] == fp:
+            return t
+        z = torch.full((fp - f,) + tuple(t.shape[1:]), fill, dtype=t.dtype, device=t.device)
+        return torch.cat([t, z])
+
+    def inter(a, b):
+        a, b = pad(a), pad(b)
+        return torch.stack([a.view(fp // 64, 64, -1), b.view(fp // 64, 64, -1)], 1).reshape(2 * fp, -1)
+
+    return QTensor("q4a", (2 * fp, gate.shape[1]), packed=inter(gate.packed, up.packed),
+                   scales=inter(gate.scales, up.scales), offsets=inter(gate.offsets, up.offsets), group=gate.group)
+
+
+def _to_int4(t: QTensor, device, bias: torch.Tensor | None = None) -> Int4Weight:
+    if t.kind != "q4a":
+        raise ValueError("CUDA path expects INT4 (q4a) linear weights")
+    return ops.prepare_int4_weight(t.packed, t.scales, t.offsets, t.shape[1], t.group, device, bias=bias)
+
+
+def _dense(t: QTensor, device, dtype=torch.bfloat16) -> torch.Tensor:
+    return t.data.to(device=device, dtype=dtype).contiguous()
+
+
+class CudaRunner:
+    """Runs engine steps on one GPU with the sm_100a kernels."""
+
+    def __init__(self, ck: Checkpoint, device, num_pages: int, max_num_tokens: int = 4096, max_num_seqs: int = 256,
+                 max_model_len: int = 4096, pools: KVPools | None = None, free_checkpoint: bool = False):
+        self.cfg: ModelConfig = ck.config
+        self.qcfg: QuantConfig = ck.quant
+        self.device = torch.device(device)
+        cfg, dev = self.cfg, self.device
+        self.max_num_tokens = max_num_tokens
+        self.max_num_seqs = max_num_seqs
+        self.max_model_len = max_model_len
+        self.ws = ops.workspace(dev)
+        self.fk, self.fv = KV_FORMATS[self.qcfg.kv_dtype]
+        self.F = cfg.intermediate_size
+        self.F_pad = (self.F + 63) // 64 * 64
+        t = ck.tensors
+        self.embed = _dense(t["model.embed_tokens.weight"], dev)
+        self.layers: list[LayerWeights] = []
+        for i in range(cfg.num_layers):
+            p = f"model.layers.{i}."
+            qkv = _cat_q4a([t[p + "self_attn.q_proj.weight"], t[p + "self_attn.k_proj.weight"],
+                            t[p + "self_attn.v_proj.weight"]])
+            bias = None
+            if cfg.qkv_bias:
+                bias = torch.cat([t[p + f"self_attn.{n}.bias"].data.float() for n in ("q_proj", "k_proj", "v_proj")])
+            lw = LayerWeights(ln1=_dense(t[p + "input_layernorm.weight"], dev),
+                              ln2=_dense(t[p + "post_attention_layernorm.weight"], dev),
+                              qkv=_to_int4(qkv, dev, bias), o=_to_int4(t[p + "self_attn.o_proj.weight"], dev),
+                              gate_up=None, down=None)
+            if cfg.qk_norm:
+                lw.q_norm = _dense(t[p + "self_attn.q_norm.weight"], dev)
+                lw.k_norm = _dense(t[p + "self_attn.k_norm.weight"], dev)
+            if cfg.is_moe:
+                from .moe import MoELayer
+
+                lw.moe = MoELayer.from_checkpoint(ck, i, dev)
+            else:
+                lw.gate_up = _to_int4(_interleave_gate_up(t[p + "mlp.gate_proj.weight"], t[p + "mlp.up_proj.weight"]),
+                                      dev)
+                lw.down = _to_int4(t[p + "mlp.down_proj.weight"], dev)
+            self.layers.append(lw)
+            if free_checkpoint:
+                for k in list(t):
+                    if k.startswith(p):
+                        del t[k]
+        self.norm = _dense(t["model.norm.weight"], dev)
+        lm = t["lm_head.weight"]
+        self.lm_head_q = _to_int4(lm, dev) if lm.kind == "q4a" else None
+        self.lm_head_dense = _dense(lm, dev) if lm.kind == "dense" else None
+        self.cos_sin = rope_table(cfg, max(max_model_len, 16) + 1).to(dev)
+        self.pools = pools or KVPools(cfg, self.qcfg, num_pages, dev)
+        self.sm_scale = 1.0 / math.sqrt(cfg.head_dim)
+        self._alloc_buffers()
+
+    # ------------------------------------------------------------------ buffers
+    def _alloc_buffers(self):
+        cfg, dev, T = self.cfg, self.device, self.max_num_tokens
+        bf = torch.bfloat16
+        self.h = torch.empty(T, cfg.hidden_size, dtype=bf, device=dev)
+        self.x = torch.empty(T, cfg.hidden_size, dtype=bf, device=dev)
+        self.qkv = torch.empty(T, cfg.q_size + 2 * cfg.kv_size, dtype=bf, device=dev)
+        self.q = torch.empty(T, cfg.q_size, dtype=bf, device=dev)
+        self.attn = torch.empty(T, cfg.q_size, dtype=bf, device=dev)
+        f_act = self.F_pad if not cfg.is_moe else 0
+        self.act = torch.empty(T, max(f_act, 8), dtype=bf, device=dev)
+        B = self.max_num_seqs
+        self.xs = torch.empty(B, cfg.hidden_size, dtype=bf, device=dev)
+        self.logits = torch.empty(B, cfg.vocab_size, dtype=bf, device=dev)
+        self.tokens = torch.empty(B, dtype=torch.int32, device=dev)
+        self.tokens_host = torch.empty(B, dtype=torch.int32, pin_memory=True)
+        self.max_pages = (self.max_model_len + self.qcfg.page_size - 1) // self.qcfg.page_size
+        # one packed int32 staging area for all per-step metadata
+        self.meta_cap = 8 * T + 16 * B + B * self.max_pages + B * 64 + 1024
+        self.meta_host = torch.empty(self.meta_cap, dtype=torch.int32, pin_memory=True)
+        self.meta_dev = torch.empty(self.meta_cap, dtype=torch.int32, device=dev)
+        self.ws.reserve_attn(B, cfg.num_heads, 64, cfg.head_dim)
+        self.ws.sampler_buffer(B, cfg.vocab_size)
+
+    # ------------------------------------------------------------------ metadata upload
+    def upload(self, st: StepInputs) -> dict:
+        """Pack all per-step arrays into one pinned buffer, one H2D copy; return device views."""
+        arrays = {
+            "ids": st.input_ids, "pos": st.positions, "slots": st.slot_mapping, "dlens": st.decode_seq_lens,
+            "qs": st.prefill_q_start, "ql": st.prefill_q_len, "ctx": st.prefill_ctx_len, "tseq": st.tile_seq,
+            "tq0": st.tile_q0, "rows": st.logits_rows, "temp": st.temperature.view(np.int32),
+            "topp": st.top_p.view(np.int32), "topk": st.top_k, "minp": st.min_p.view(np.int32),
+            "rep": st.rep_penalty.view(np.int32), "step": st.rng_step,
+        }
+        bt = st.block_tables
+        if st.hist is not None:
+            arrays["hist"] = st.hist.reshape(-1)
+        host = self.meta_host.numpy()
+        off = 0
+        offs = {}
+        for k, a in arrays.items():
+            n = a.size
+            host[off:off + n] = a.reshape(-1)
+            offs[k] = (off, n)
+            off += n
+        nb = bt.size
+        host[off:off + nb] = bt.reshape(-1)
+        offs["bt"] = (off, nb)
+        off += nb
+        if off > self.meta_cap:
+            raise ValueError("step metadata exceeds the staging buffer")
+        self.meta_dev[:off].copy_(self.meta_host[:off], non_blocking=True)
+        d = {k: self.meta_dev[o:o + n] for k, (o, n) in offs.items()}
+        for k in ("temp", "topp", "minp", "rep"):
+            d[k] = d[k].view(torch.float32)
+        d["bt"] = d["bt"].view(bt.shape[0], bt.shape[1]) if bt.size else d["bt"].view(0, max(bt.shape[1], 1))
+        if "hist" in d:
+            d["hist"] = d["hist"].view(st.hist.shape[0], st.hist.shape[1])
+        return d
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, st: StepInputs, m: dict) -> torch.Tensor:
+        cfg = self.cfg
+        T, Bd = st.num_tokens, st.num_decode
+        Bp = st.num_prefill
+        ws = self.ws
+        h, x = self.h[:T], self.x[:T]
+        torch.index_select(self.embed, 0, m["ids"], out=h)
+        hq, hkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        ps, grp = self.qcfg.page_size, self.qcfg.kv_group
+        dsplit = ops.kernels.decode_splits(max(Bd, 1), hkv, max(st.max_decode_ctx, 1)) if Bd else (1, 1)
+        bt = m["bt"]
+        for li, lw in enumerate(self.layers):
+            ops.rmsnorm(h, lw.ln1, cfg.rms_eps, out=x)
+            qkv = ops.w4a16_linear(x, lw.qkv, out=self.qkv[:T], ws=ws)
+            kc, ks, vc, vs = self.pools.layers[li]
+            q = self.q[:T]
+            ops.rope_kv_write(qkv, m["pos"], self.cos_sin, q, m["slots"], kc, ks, vc, vs, hq, hkv, d, ps, grp,
+                              self.fk, self.fv, lw.q_norm, lw.k_norm, cfg.rms_eps)
+            attn = self.attn[:T]
+            if Bd:
+                ops.paged_decode_attention(q[:Bd], kc, ks, vc, vs, bt[:Bd], m["dlens"], attn[:Bd], hq, hkv, d, ps, grp,
+                                           self.fk, self.fv, self.sm_scale, st.max_decode_ctx, ws=ws, splits=dsplit)
+            if Bp:
+                ops.paged_prefill_attention(q[Bd:], kc, ks, vc, vs, bt[Bd:], m["tseq"], m["tq0"], m["qs"], m["ql"],
+                                            m["ctx"], st.tile_seq.shape[0], attn[Bd:], hq, hkv, d, ps, grp, self.fk,
+                                            self.fv, self.sm_scale)
+            ops.w4a16_linear(attn, lw.o, out=h, residual=h, ws=ws)
+            ops.rmsnorm(h, lw.ln2, cfg.rms_eps, out=x)
+            if lw.moe is not None:
+                lw.moe.forward(x, h, ws)
+            else:
+                act = ops.w4a16_linear(x, lw.gate_up, out=self.act[:T], silu_mul=True, ws=ws)
+                ops.w4a16_linear(act[:, : self.F], lw.down, out=h, residual=h, ws=ws)
+        B = st.logits_rows.shape[0]
+        xs = ops.rmsnorm(h, self.norm, cfg.rms_eps, out=self.xs[:B], row_idx=m["rows"])
+        if self.lm_head_q is not None:
+            return ops.w4a16_linear(xs, self.lm_head_q, out=self.logits[:B], ws=ws)
+        return torch.matmul(xs, self.lm_head_dense.T, out=self.logits[:B])
+
+    def sample(self, st: StepInputs, m: dict, logits: torch.Tensor) -> torch.Tensor:
+        B = logits.shape[0]
+        greedy = bool((st.temperature <= 0).all()) and st.hist is None
+        out = self.tokens[:B]
+        if greedy and not (st.rep_penalty != 1).any():
+            ops.sample(logits, out, ws=self.ws)
+        else:
+            ops.sample(logits, out, temperature=m["temp"], top_p=m["topp"], top_k=m["topk"], min_p=m["minp"],
+                       rep_penalty=m["rep"], hist=m.get("hist"), seed=st.seed, step=m["step"], ws=self.ws)
+        return out
+
+    def sample_full(self, st: StepInputs, m: dict, logits: torch.Tensor) -> torch.Tensor:
+        """The sampler with every per-row parameter bound (no host-side branching: graph-safe)."""
+        out = self.tokens[: logits.shape[0]]
+        ops.sample(logits, out, temperature=m["temp"], top_p=m["topp"], top_k=m["topk"], min_p=m["minp"],
+                   rep_penalty=m["rep"], hist=m.get("hist"), seed=st.seed, step=m["step"], ws=self.ws)
+        return out
+
+    # ------------------------------------------------------------------ device-side step timing
+    timing = False
+    _events: list = []
+
+    def timer_start(self) -> None:
+        if self.timing:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self._events.append([e, None])
+
+    def timer_stop(self) -> None:
+        if self.timing:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self._events[-1][1] = e
+
+    def device_time_ms(self, reset: bool = True) -> float:
+        """Sum of the device intervals (H2D metadata copy .. sampled-token D2H) of timed steps."""
+        torch.cuda.synchronize(self.device)
+        t = sum(a.elapsed_time(b) for a, b in self._events if b is not None)
+        if reset:
+            self._events = []
+        return t
+
+    @torch.inference_mode()
+    def execute(self, st: StepInputs) -> np.ndarray:
+        self.timer_start()
+        m = self.upload(st)
+        logits = self.forward(st, m)
+        toks = self.sample(st, m, logits)
+        B = toks.shape[0]
+        self.tokens_host[:B].copy_(toks, non_blocking=True)
+        self.timer_stop()
+        torch.cuda.current_stream(self.device).synchronize()
+        self.last_logits = logits if st.all_logits else None
+        return self.tokens_host[:B].numpy().copy()
+
+
+# ----------------------------------------------------------------------------- CPU oracle of the step
+class TorchPagedRunner:
+    """The same step semantics as CudaRunner in plain PyTorch on the CPU (fp32)."""
+
+    def __init__(self, ck: Checkpoint, num_pages: int, max_model_len: int = 2048):
+        from .reference import ReferenceModel
+
+        self.ref = ReferenceModel(ck)
+        self.cfg, self.qcfg = ck.config, ck.quant
+        cfg, q = self.cfg, self.qcfg
+        self.ps = q.page_size
+        # dense (dequantized) page pools [P, Hkv, PS, D]
+        self.k = torch.zeros(cfg.num_layers, num_pages, cfg.num_kv_heads, self.ps, cfg.head_dim)
+        self.v = torch.zeros_like(self.k)
+        self.cos_sin = rope_table(cfg, max_model_len + 1)
+        self.last_logits = None
+
+    @torch.no_grad()
+    def execute(self, st: StepInputs) -> np.ndarray:
+        from .reference import _rms, _rope
+
+        cfg, w = self.cfg, self.ref.w
+        T = st.num_tokens
+        ids = torch.from_numpy(st.input_ids.astype(np.int64))
+        pos = torch.from_numpy(st.positions.astype(np.int64))
+        slots = torch.from_numpy(st.slot_mapping.astype(np.int64))
+        cs = self.cos_sin[pos]
+        h = w["model.embed_tokens.weight"][ids]
+        hq, hkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        Bd = st.num_decode
+        # per-row (sequence index, visible context length) for attention
+        seq_rows = []
+        for i in range(Bd):
+            seq_rows.append((i, int(st.decode_seq_lens[i]), i, 1))
+        for j in range(st.num_prefill):
+            seq_rows.append((Bd + j, int(st.prefill_ctx_len[j]), Bd + int(st.prefill_q_start[j]),
+                             int(st.prefill_q_len[j])))
+        for li in range(cfg.num_layers):
+            p = f"model.layers.{li}."
+            x = _rms(h, w[p + "input_layernorm.weight"], cfg.rms_eps)
+            qv = x @ w[p + "self_attn.q_proj.weight"].T
+            kv = x @ w[p + "self_attn.k_proj.weight"].T
+            vv = x @ w[p + "self_attn.v_proj.weight"].T
+            if cfg.qkv_bias:
+                qv = qv + w[p + "self_attn.q_proj.bias"]
+                kv = kv + w[p + "self_attn.k_proj.bias"]
+                vv = vv + w[p + "self_attn.v_proj.bias"]
+            qv, kv, vv = qv.view(T, hq, d), kv.view(T, hkv, d), vv.view(T, hkv, d)
+            if cfg.qk_norm:
+                qv = _rms(qv, w[p + "self_attn.q_norm.weight"], cfg.rms_eps)
+                kv = _rms(kv, w[p + "self_attn.k_norm.weight"], cfg.rms_eps)
+            qv, kv = _rope(qv, cs), _rope(kv, cs)
+            kq = self.ref._kv_roundtrip(kv, self.ref.fk)
+            vq = self.ref._kv_roundtrip(vv, self.ref.fv)
+            valid = slots >= 0
+            pg, off = slots[valid] // self.ps, slots[valid] % self.ps
+            self.k[li, pg, :, off] = kq[valid]
+            self.v[li, pg, :, off] = vq[valid]
+            attn = torch.zeros(T, hq * d)
+            for (bt_row, ctx, r0, n) in seq_rows:
+                npg = (ctx + self.ps - 1) // self.ps
+                pages = torch.from_numpy(st.block_tables[bt_row, :npg].astype(np.int64))
+                K = self.k[li, pages].permute(0, 2, 1, 3).reshape(-1, hkv, d)[:ctx]
+                V = self.v[li, pages].permute(0, 2, 1, 3).reshape(-1, hkv, d)[:ctx]
+                K = K.repeat_interleave(hq // hkv, dim=1)
+                V = V.repeat_interleave(hq // hkv, dim=1)
+                qq = qv[r0:r0 + n]
+                s = torch.einsum("qhd,khd->hqk", qq, K) / math.sqrt(d)
+                qpos = torch.arange(ctx - n, ctx)
+                s = s.masked_fill(torch.arange(ctx)[None, None, :] > qpos[None, :, None], float("-inf"))
+                attn[r0:r0 + n] = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), V).reshape(n, hq * d)
+            h = h + attn @ w[p + "self_attn.o_proj.weight"].T
+            x = _rms(h, w[p + "post_attention_layernorm.weight"], cfg.rms_eps)
+            h = h + self.ref._mlp(p, x)
+        rows = torch.from_numpy(st.logits_rows.astype(np.int64))
+        xs = _rms(h[rows], w["model.norm.weight"], cfg.rms_eps)
+        logits = xs @ w["lm_head.weight"].T
+        self.last_logits = logits
+        out = np.empty(len(rows), dtype=np.int32)
+        for i in range(len(rows)):
+            lg = logits[i].clone()
+            if st.hist is not None and st.rep_penalty[i] != 1.0:
+                ids_ = [t for t in st.hist[i].tolist() if t >= 0]
+                for t in set(ids_):
+                    lg[t] = lg[t] / st.rep_penalty[i] if lg[t] > 0 else lg[t] * st.rep_penalty[i]
+            if st.temperature[i] <= 0:
+                out[i] = int(lg.argmax())
+            else:
+                g = torch.Generator().manual_seed(int(st.seed) * 1000003 + int(st.rng_step[i]))
+                pr = torch.softmax(lg / float(st.temperature[i]), -1)
+                if st.top_k[i] > 0:
+                    kth = pr.topk(int(st.top_k[i])).values[-1]
+                    pr = torch.where(pr >= kth, pr, torch.zeros_like(pr))
+                if st.top_p[i] < 1.0:
+                    sp, si = pr.sort(descending=True)
+                    cum = sp.cumsum(0)
+                    cut = int((cum < st.top_p[i]).sum()) + 1
+                    keep = torch.zeros_like(pr)
+                    keep[si[:cut]] = pr[si[:cut]]
+                    pr = keep
+                out[i] = int(torch.multinomial(pr / pr.sum(), 1, generator=g))
+        return out

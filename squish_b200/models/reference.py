@@ -1,0 +1,146 @@
+"""Pure-PyTorch fp32 decoder: the end-to-end oracle for the CUDA model.
+
+It runs the same architecture with the dequantized weights (offset + q * scale in
+fp32) and stores K/V through the same quantize -> dequantize codec as the device's
+paged cache (the C++ CPU restatement of csrc/kv_write.cu), so CUDA logits can be
+compared against it step by step. It has no batching and no paging: one sequence,
+dense per-layer caches. The reference framework has no model code of its own (the
+forward pass lives in mlx_lm / HF transformers, squish/backend.py:222-390).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .._ext import native
+from ..ops.kernels import KV_FORMATS
+from .config import ModelConfig, QuantConfig
+from .weights import Checkpoint
+
+
+def rope_table(cfg: ModelConfig, max_pos: int | None = None) -> torch.Tensor:
+    """[max_pos, head_dim] fp32 table: cos (D/2) | sin (D/2), computed in float64."""
+    d = cfg.head_dim
+    n = max_pos or cfg.max_position
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, dtype=torch.float64) / d))
+    sc = cfg.rope_scaling or {}
+    if sc.get("rope_type", sc.get("type")) == "llama3":
+        # Llama-3 frequency smoothing (wavelength-dependent scaling)
+        factor = sc.get("factor", 8.0)
+        lo, hi = sc.get("low_freq_factor", 1.0), sc.get("high_freq_factor", 4.0)
+        old = sc.get("original_max_position_embeddings", 8192)
+        wl = 2 * math.pi / inv
+        smooth = (old / wl - lo) / (hi - lo)
+        scaled = torch.where(wl > old / lo, inv / factor, inv)
+        mid = (wl <= old / lo) & (wl >= old / hi)
+        inv = torch.where(mid, (1 - smooth) * inv / factor + smooth * inv, scaled)
+    t = torch.arange(n, dtype=torch.float64)
+    f = torch.outer(t, inv)
+    return torch.cat([f.cos(), f.sin()], dim=1).float()
+
+
+def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+
+
+def _rope(x: torch.Tensor, cs: torch.Tensor) -> torch.Tensor:
+    d = x.shape[-1]
+    c, s = cs[:, None, : d // 2], cs[:, None, d // 2:]
+    x1, x2 = x[..., : d // 2], x[..., d // 2:]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+class ReferenceModel:
+    def __init__(self, ck: Checkpoint):
+        self.cfg: ModelConfig = ck.config
+        self.q: QuantConfig = ck.quant
+        cfg = self.cfg
+        self.w = {k: v.dequantize().float().cpu() for k, v in ck.tensors.items()}
+        self.cos_sin = rope_table(cfg, min(cfg.max_position, 8192))
+        self.fk, self.fv = KV_FORMATS[self.q.kv_dtype]
+
+    def _kv_roundtrip(self, x: torch.Tensor, fmt: int) -> torch.Tensor:
+        """[T, Hkv, D] -> through the KV page codec and back."""
+        if fmt == 0:
+            return x.to(torch.bfloat16).float()
+        t, h, d = x.shape
+        codes, scales = native().cpu.kv_quantize(x.reshape(t * h, d).contiguous(), fmt, self.q.kv_group)
+        return native().cpu.kv_dequantize(codes, scales, fmt, self.q.kv_group, d).reshape(t, h, d)
+
+    def new_cache(self):
+        return [{"k": torch.zeros(0, self.cfg.num_kv_heads, self.cfg.head_dim),
+                 "v": torch.zeros(0, self.cfg.num_kv_heads, self.cfg.head_dim)} for _ in range(self.cfg.num_layers)]
+
+    def _mlp(self, p: str, x: torch.Tensor) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        if not cfg.is_moe:
+            g = x @ w[p + "mlp.gate_proj.weight"].T
+            u = x @ w[p + "mlp.up_proj.weight"].T
+            return (torch.nn.functional.silu(g) * u) @ w[p + "mlp.down_proj.weight"].T
+        logits = x @ w[p + "mlp.gate.weight"].T
+        probs = torch.softmax(logits, dim=-1)
+        topv, topi = probs.topk(cfg.num_experts_per_tok, dim=-1)
+        if cfg.norm_topk_prob:
+            topv = topv / topv.sum(-1, keepdim=True)
+        out = torch.zeros_like(x)
+        for t in range(x.shape[0]):
+            for j in range(topi.shape[1]):
+                e = int(topi[t, j])
+                q = p + f"mlp.experts.{e}."
+                g = x[t] @ w[q + "gate_proj.weight"].T
+                u = x[t] @ w[q + "up_proj.weight"].T
+                out[t] += topv[t, j] * ((torch.nn.functional.silu(g) * u) @ w[q + "down_proj.weight"].T)
+        return out
+
+    @torch.no_grad()
+    def forward(self, tokens: list[int], cache, start_pos: int) -> torch.Tensor:
+        """Run ``tokens`` at positions start_pos.. (appending to ``cache``); return logits [T, V]."""
+        cfg, w = self.cfg, self.w
+        t = len(tokens)
+        pos = torch.arange(start_pos, start_pos + t)
+        cs = self.cos_sin[pos]
+        h = w["model.embed_tokens.weight"][torch.tensor(tokens)]
+        d, hq, hkv = cfg.head_dim, cfg.num_heads, cfg.num_kv_heads
+        for i in range(cfg.num_layers):
+            p = f"model.layers.{i}."
+            x = _rms(h, w[p + "input_layernorm.weight"], cfg.rms_eps)
+            q = x @ w[p + "self_attn.q_proj.weight"].T
+            k = x @ w[p + "self_attn.k_proj.weight"].T
+            v = x @ w[p + "self_attn.v_proj.weight"].T
+            if cfg.qkv_bias:
+                q = q + w[p + "self_attn.q_proj.bias"]
+                k = k + w[p + "self_attn.k_proj.bias"]
+                v = v + w[p + "self_attn.v_proj.bias"]
+            q, k, v = q.view(t, hq, d), k.view(t, hkv, d), v.view(t, hkv, d)
+            if cfg.qk_norm:
+                q = _rms(q, w[p + "self_attn.q_norm.weight"], cfg.rms_eps)
+                k = _rms(k, w[p + "self_attn.k_norm.weight"], cfg.rms_eps)
+            q, k = _rope(q, cs), _rope(k, cs)
+            c = cache[i]
+            c["k"] = torch.cat([c["k"], self._kv_roundtrip(k, self.fk)])
+            c["v"] = torch.cat([c["v"], self._kv_roundtrip(v, self.fv)])
+            kk = c["k"].repeat_interleave(hq // hkv, dim=1)
+            vv = c["v"].repeat_interleave(hq // hkv, dim=1)
+            s = torch.einsum("qhd,khd->hqk", q, kk) / math.sqrt(d)
+            kpos = torch.arange(kk.shape[0])
+            s = s.masked_fill(kpos[None, None, :] > pos[None, :, None], float("-inf"))
+            a = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vv).reshape(t, hq * d)
+            h = h + a @ w[p + "self_attn.o_proj.weight"].T
+            x = _rms(h, w[p + "post_attention_layernorm.weight"], cfg.rms_eps)
+            h = h + self._mlp(p, x)
+        x = _rms(h, w["model.norm.weight"], cfg.rms_eps)
+        return x @ w["lm_head.weight"].T
+
+    def greedy(self, prompt: list[int], max_new: int) -> tuple[list[int], list[torch.Tensor]]:
+        cache = self.new_cache()
+        logits = self.forward(prompt, cache, 0)[-1]
+        out, all_logits = [], []
+        pos = len(prompt)
+        for _ in range(max_new):
+            all_logits.append(logits)
+            tok = int(logits.argmax())
+            out.append(tok)
+            logits = self.forward([tok], cache, pos)[-1]
+            pos += 1
+        return out, all_logits

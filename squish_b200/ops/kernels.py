@@ -61,6 +61,14 @@ class Workspace:
 
 _WORKSPACES: dict[int, Workspace] = {}
 
+# Number of this package's kernels launched from Python (a CUDA-graph replay adds the
+# count recorded while it was captured). Read by the benchmark as its launch count.
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
 
 def workspace(device: torch.device | None = None) -> Workspace:
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -120,6 +128,7 @@ def w4a16_linear(x: torch.Tensor, w: Int4Weight, out: torch.Tensor | None = None
         out = torch.empty((m, ncols), dtype=torch.bfloat16, device=x.device)
     native().w4a16_gemm(x, w.wq, w.sz, w.n, w.k, w.group, out, w.bias, residual,
                         EPI_SILU_MUL if silu_mul else EPI_PLAIN, ws.gemm_ws, ws.gemm_counters, ws.status)
+    _count()
     return out
 
 
@@ -129,13 +138,19 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor
     if out is None:
         out = torch.empty((rows, x.shape[1]), dtype=torch.bfloat16, device=x.device)
     native().rmsnorm(x, weight, out, row_idx, float(eps))
+    _count()
     return out
 
 
 def rope_kv_write(qkv, positions, cos_sin, q_out, slot_mapping, k_codes, k_scales, v_codes, v_scales,
-                  hq: int, hkv: int, d: int, page_size: int, group: int, fmt_k: int, fmt_v: int) -> None:
+                  hq: int, hkv: int, d: int, page_size: int, group: int, fmt_k: int, fmt_v: int,
+                  q_norm=None, k_norm=None, norm_eps: float = 1e-6) -> None:
     native().rope_kv_write(qkv, positions, cos_sin, q_out, slot_mapping, k_codes, k_scales, v_codes, v_scales,
-                           hq, hkv, d, page_size, group, fmt_k, fmt_v)
+                           hq, hkv, d, page_size, group, fmt_k, fmt_v, q_norm, k_norm, float(norm_eps))
+    _count()
+
+
+MAX_DECODE_SPLITS = 64
 
 
 def decode_splits(batch: int, hkv: int, max_ctx: int, num_sms: int = 148) -> tuple[int, int]:
@@ -143,7 +158,7 @@ def decode_splits(batch: int, hkv: int, max_ctx: int, num_sms: int = 148) -> tup
     tiles = max(1, math.ceil(max_ctx / 16))
     base = max(1, batch * hkv)
     want = max(1, (4 * num_sms + base - 1) // base)
-    splits = max(1, min(want, tiles // 4 if tiles >= 8 else 1))
+    splits = max(1, min(want, tiles // 4 if tiles >= 8 else 1, MAX_DECODE_SPLITS))
     tps = math.ceil(tiles / splits)
     splits = math.ceil(tiles / tps)
     return splits, tps
@@ -158,6 +173,7 @@ def paged_decode_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables
     o_part, lse = ws.attn_buffers(b, hq, s, d)
     native().paged_decode_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables, seq_lens, out, o_part,
                                     lse, hq, hkv, d, page_size, group, fmt_k, fmt_v, float(sm_scale), s, tps)
+    _count(2 if s > 1 else 1)
     return out
 
 
@@ -166,6 +182,7 @@ def paged_prefill_attention(q, k_codes, k_scales, v_codes, v_scales, block_table
     native().paged_prefill_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables, tile_seq, tile_q0,
                                      q_start, q_len, ctx_len, int(n_tiles), out, hq, hkv, d, page_size, group,
                                      fmt_k, fmt_v, float(sm_scale))
+    _count()
     return out
 
 
@@ -175,4 +192,5 @@ def sample(logits, out_tokens, temperature=None, top_p=None, top_k=None, min_p=N
     work = ws.sampler_buffer(logits.shape[0], logits.shape[1])
     native().sample(logits, temperature, top_p, top_k, min_p, rep_penalty, hist, allow_mask, int(seed), step,
                     out_tokens, out_logprob, work)
+    _count()
     return out_tokens

@@ -1,0 +1,92 @@
+"""End-to-end CUDA engine against the CPU fp32 oracle, and CUDA graphs against eager."""
+import dataclasses
+
+import numpy as np
+import pytest
+import torch
+
+from squish_b200.engine.engine import EngineConfig, LLMEngine
+from squish_b200.engine.sampling import SamplingParams
+from squish_b200.models.config import ModelConfig, QuantConfig, get_preset
+from squish_b200.models.reference import ReferenceModel
+from squish_b200.models.weights import random_checkpoint
+
+pytestmark = pytest.mark.gpu
+
+
+def _prompt(seed, n, vocab):
+    return np.random.default_rng(seed).integers(0, vocab, n).tolist()
+
+
+def _configs():
+    tiny, tq = get_preset("tiny-llama")
+    qwen2 = ModelConfig("tiny-qwen2", "qwen2", 1000, 896, 2, 14, 2, 64, 1024, 1e-6, 1e6, qkv_bias=True,
+                        max_position=4096)
+    qwen3 = ModelConfig("tiny-qwen3", "qwen3", 1000, 512, 2, 8, 2, 128, 768, 1e-6, 1e6, qk_norm=True,
+                        max_position=4096)
+    return [(tiny, tq), (qwen2, QuantConfig(4, 64, True, "int4", 32, 16)),
+            (qwen3, QuantConfig(4, 64, True, "k8v4", 64, 16)), (tiny, dataclasses.replace(tq, kv_dtype="bf16"))]
+
+
+@pytest.mark.parametrize("idx", range(4))
+def test_cuda_engine_matches_cpu_oracle(cuda, idx):
+    cfg, q = _configs()[idx]
+    ck_cpu = random_checkpoint(cfg, q, seed=0, device="cpu")
+    ref = ReferenceModel(ck_cpu)
+    prompts = [_prompt(1, 32, cfg.vocab_size), _prompt(2, 77, cfg.vocab_size)]
+    cache = ref.new_cache()
+    ref_logits = ref.forward(prompts[0], cache, 0)[-1]
+    eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
+                                    EngineConfig(max_num_seqs=4, max_num_batched_tokens=64, max_model_len=512,
+                                                 num_pages=128, cuda_graphs=False))
+    rid = eng.add_request(prompts[0], SamplingParams(max_tokens=1, ignore_eos=True))
+    eng.step()
+    eng.step()
+    gpu_logits = eng.runner.logits[0].float().cpu()
+    cos = torch.nn.functional.cosine_similarity(gpu_logits, ref_logits, dim=0)
+    assert cos > 0.99, f"cosine {cos}"
+    assert eng.requests[rid].output[0] == int(ref_logits.argmax())
+    # greedy continuation: the first tokens agree (bf16 vs fp32 may drift later)
+    want = ref.greedy(prompts[1], 8)[0]
+    got = eng.generate([prompts[1]], SamplingParams(max_tokens=8, ignore_eos=True))[0]
+    agree = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), len(want))
+    assert agree >= 3, (got, want)
+    eng.runner.ws.check()
+
+
+def test_tiny_config_64_tokens_oracle(cuda):
+    """The tiny Llama oracle workload: 32-token prompt (seed 1), greedy 64 tokens."""
+    cfg, q = get_preset("tiny-llama")
+    ck = random_checkpoint(cfg, q, seed=0, device="cpu")
+    prompt = torch.randint(0, 32000, (32,), generator=torch.Generator().manual_seed(1)).tolist()
+    want, _ = ReferenceModel(ck).greedy(prompt, 64)
+    eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
+                                    EngineConfig(max_num_seqs=1, max_model_len=256, num_pages=32))
+    got = eng.generate([prompt], SamplingParams(max_tokens=64, ignore_eos=True))[0]
+    agree = sum(a == b for a, b in zip(got, want)) / 64
+    assert agree >= 0.75, (agree, got, want)
+
+
+def test_graphs_match_eager(cuda):
+    cfg, q = get_preset("tiny-llama")
+    prompts = [_prompt(10 + i, 20 + 9 * i, cfg.vocab_size) for i in range(5)]
+    outs = []
+    for graphs in (False, True):
+        eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
+                                        EngineConfig(max_num_seqs=8, max_model_len=512, num_pages=128,
+                                                     cuda_graphs=graphs))
+        outs.append(eng.generate(prompts, SamplingParams(max_tokens=24, ignore_eos=True)))
+        if graphs:
+            assert eng.graphs.graphs, "decode steps should have run through CUDA graphs"
+    assert outs[0] == outs[1]
+
+
+def test_sampled_decoding_runs_in_graphs(cuda):
+    cfg, q = get_preset("tiny-llama")
+    eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
+                                    EngineConfig(max_num_seqs=4, max_model_len=256, num_pages=64))
+    out = eng.generate([_prompt(40, 12, cfg.vocab_size)] * 3,
+                       [SamplingParams(max_tokens=16, temperature=0.8, top_p=0.9, top_k=50, repetition_penalty=1.1,
+                                       ignore_eos=True)] * 3)
+    assert all(len(o) == 16 for o in out)
+    assert all(0 <= t < cfg.vocab_size for o in out for t in o)

@@ -248,7 +248,8 @@ def test_paged_prefill_attention(cuda, kvfmt, hq, hkv, d):
         qs = int(q_start[i])
         qpos = torch.arange(c - ql, c)
         ref = attention(q[qs:qs + ql].float().view(ql, hq, d), k, v, qpos, sm_scale(d))
-        torch.testing.assert_close(out[qs:qs + ql].float().cpu().view(ql, hq, d), ref, rtol=2e-2, atol=2e-2)
+        # P is rounded to bf16 before the PV product (as in any bf16 flash kernel)
+        torch.testing.assert_close(out[qs:qs + ql].float().cpu().view(ql, hq, d), ref, rtol=2e-2, atol=3e-2)
 
 
 def test_sampler_greedy_and_filters(cuda):
