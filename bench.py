@@ -225,6 +225,7 @@ def run_ours(args, world, rank, local):
     h2d0, d2h0 = eng.stats.h2d_bytes, eng.stats.d2h_bytes
     steps0 = eng.stats.steps
     launches0 = LAUNCHES[0]
+    g0, mx0, sched0 = eng.stats.graph_steps, eng.stats.mixed_steps, eng.stats.scheduled_tokens
     clocks = ClockSampler(local, args.clocks != "0")
     barrier(world)
     clocks.start()
@@ -276,6 +277,8 @@ def run_ours(args, world, rank, local):
         "gpu_launches": int(tot_launch),
         "clocks": clk,
         "load_s": round(load_s, 1),
+        "steps_detail": {"graph_decode": eng.stats.graph_steps - g0, "with_prefill": eng.stats.mixed_steps - mx0,
+                         "tokens_per_step": (eng.stats.scheduled_tokens - sched0) / args.steps},
         "impl": "ours",
     }
     return res

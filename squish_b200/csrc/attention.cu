@@ -494,6 +494,7 @@ cudaError_t paged_decode_attn_launch(const AttnParams& p, cudaStream_t s) {
   if (p.B == 0) return cudaSuccess;
   if (p.D == 128) return launch_decode_fmt<128>(p, s);
   if (p.D == 64) return launch_decode_fmt<64>(p, s);
+  if (p.D == 32) return launch_decode_fmt<32>(p, s);
   return cudaErrorInvalidValue;
 }
 
@@ -501,6 +502,7 @@ cudaError_t paged_prefill_attn_launch(const AttnParams& p, cudaStream_t s) {
   if (p.n_tiles == 0) return cudaSuccess;
   if (p.D == 128) return launch_prefill_fmt<128>(p, s);
   if (p.D == 64) return launch_prefill_fmt<64>(p, s);
+  if (p.D == 32) return launch_prefill_fmt<32>(p, s);
   return cudaErrorInvalidValue;
 }
 

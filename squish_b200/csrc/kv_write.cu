@@ -135,16 +135,24 @@ __global__ void rope_kv_write_kernel(RopeKvParams p) {
 #pragma unroll
         for (int jj = 0; jj < J; ++jj) v[jj] = v[jj] * inv * __bfloat162float(nw[lane + 32 * jj]);
       }
-      float r[J];
-#pragma unroll
-      for (int jj = 0; jj < J / 2; ++jj) {
-        const int i = lane + 32 * jj;
+      if constexpr (J == 1) {
+        // D = 32: dims i and i+16 sit in lanes i and i+16
+        const float other = __shfl_xor_sync(0xffffffffu, v[0], 16);
+        const int i = lane & 15;
         const float c = cs[i], s = cs[D / 2 + i];
-        r[jj] = v[jj] * c - v[jj + J / 2] * s;
-        r[jj + J / 2] = v[jj + J / 2] * c + v[jj] * s;
-      }
+        v[0] = (lane < 16) ? v[0] * c - other * s : v[0] * c + other * s;
+      } else {
+        float r[J];
 #pragma unroll
-      for (int jj = 0; jj < J; ++jj) v[jj] = r[jj];
+        for (int jj = 0; jj < J / 2; ++jj) {
+          const int i = lane + 32 * jj;
+          const float c = cs[i], s = cs[D / 2 + i];
+          r[jj] = v[jj] * c - v[jj + J / 2] * s;
+          r[jj + J / 2] = v[jj + J / 2] * c + v[jj] * s;
+        }
+#pragma unroll
+        for (int jj = 0; jj < J; ++jj) v[jj] = r[jj];
+      }
     }
     if (j < p.Hq) {
       __nv_bfloat16* dst = p.q_out + ((size_t)t * p.Hq + j) * D;
@@ -210,6 +218,7 @@ cudaError_t rope_kv_write_launch(const RopeKvParams& p, int T, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   const int threads = 256;
   switch (p.D) {
+    case 32: rope_kv_write_kernel<32><<<T, threads, 0, s>>>(p); break;
     case 64: rope_kv_write_kernel<64><<<T, threads, 0, s>>>(p); break;
     case 128: rope_kv_write_kernel<128><<<T, threads, 0, s>>>(p); break;
     case 256: rope_kv_write_kernel<256><<<T, threads, 0, s>>>(p); break;

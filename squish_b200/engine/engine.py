@@ -53,6 +53,9 @@ class EngineStats:
     ttfts: list = field(default_factory=list)
     h2d_bytes: int = 0
     d2h_bytes: int = 0
+    graph_steps: int = 0
+    mixed_steps: int = 0
+    scheduled_tokens: int = 0
 
 
 class LLMEngine:
@@ -205,8 +208,11 @@ class LLMEngine:
         st, samp = self.build_inputs(sched)
         if self.graphs is not None and not sched.prefill and self.graphs.can_run(st):
             toks = self.graphs.run(st)
+            self.stats.graph_steps += 1
         else:
             toks = self.runner.execute(st)
+            self.stats.mixed_steps += 1 if sched.prefill else 0
+        self.stats.scheduled_tokens += st.num_tokens
         self.stats.steps += 1
         self.stats.h2d_bytes += st.h2d_bytes()
         self.stats.d2h_bytes += 4 * len(samp)
