@@ -46,28 +46,6 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// Fill `rows` token rows of a [rows][D+8] bf16 smem tile from the paged cache.
-// Work items are (token, 8-dim chunk); invalid tokens (>= kv_len) are zero-filled.
-template <int D, int FMT>
-__device__ __forceinline__ void load_tile(__nv_bfloat16* tile, const uint8_t* codes, const __half* scales,
-                                          const int* bt, int h, int Hkv, int PS, int G, int tok0, int rows,
-                                          int kv_len, int item0, int item_stride) {
-  constexpr int LD = D + 8;
-  constexpr int CB = kv_code_bytes(FMT, D);
-  const int NS = kv_nscale(FMT, D, G);
-  for (int it = item0; it < rows * (D / 8); it += item_stride) {
-    const int r = it / (D / 8), c = it % (D / 8);
-    const int tok = tok0 + r;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (tok < kv_len) {
-      const int page = bt[tok / PS];
-      const size_t rowid = ((size_t)page * Hkv + h) * PS + (tok % PS);
-      v = kv_dequant8<FMT>(codes + rowid * CB, scales + rowid * NS, c * 8, G);
-    }
-    *reinterpret_cast<uint4*>(tile + r * LD + c * 8) = v;
-  }
-}
-
 // ------------------------------------------------------------------------------- decode
 // grid (B, Hkv, splits), 4 warps; warp w handles 16-token tiles t0+w, t0+w+4, ...
 // M side of each MMA = the G_q query heads of this KV head (padded to 16).
@@ -111,10 +89,35 @@ __global__ void __launch_bounds__(128) decode_kernel(const AttnParams p) {
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
+  // Each lane owns half a row (token lane/2, dims [half*D/2, +D/2)) of the 16-token tile.
+  // A tile never crosses a page (page_size % 16 == 0), so one page-table read per tile;
+  // the next tile's raw codes are loaded into registers while this tile is computed.
+  using RK = RowPart<D, FK, 2>;
+  using RV = RowPart<D, FV, 2>;
+  const int rr = lane >> 1, part = lane & 1;
+  const int PS = p.page_size;
+  constexpr int CBK = kv_code_bytes(FK, D), CBV = kv_code_bytes(FV, D);
+  const int NSK = kv_nscale(FK, D, p.group), NSV = kv_nscale(FV, D, p.group);
+  auto fetch = [&](int tile, RK& a, RV& c) {
+    const int tok = tile * 16 + rr;
+    if (tile < t1 && tok < kv_len) {
+      const int page = __ldg(bt + (tile * 16) / PS);
+      const size_t rowid = ((size_t)page * p.Hkv + h) * PS + ((tile * 16) % PS) + rr;
+      a.load(p.k_codes + rowid * CBK, p.k_scales + rowid * NSK, part, p.group);
+      c.load(p.v_codes + rowid * CBV, p.v_scales + rowid * NSV, part, p.group);
+    } else {
+      a.clear();
+      c.clear();
+    }
+  };
+  RK rk;
+  RV rv;
+  fetch(t0 + warp, rk, rv);
   for (int tile = t0 + warp; tile < t1; tile += NWARP) {
     const int tok0 = tile * 16;
-    load_tile<D, FK>(Ks, p.k_codes, p.k_scales, bt, h, p.Hkv, p.page_size, p.group, tok0, 16, kv_len, lane, 32);
-    load_tile<D, FV>(Vs, p.v_codes, p.v_scales, bt, h, p.Hkv, p.page_size, p.group, tok0, 16, kv_len, lane, 32);
+    rk.store(Ks + rr * LD + part * RK::DIMS, p.group);
+    rv.store(Vs + rr * LD + part * RV::DIMS, p.group);
+    fetch(tile + NWARP, rk, rv);  // in flight during this tile's math
     __syncwarp();
     float s[2][4];
 #pragma unroll
@@ -311,14 +314,51 @@ __global__ void __launch_bounds__(256) prefill_kernel(const AttnParams p) {
   float mrow[2][2] = {{-INFINITY, -INFINITY}, {-INFINITY, -INFINITY}};
   float lrow[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
 
+  // K/V tile loader: items = (row, part of a row) of the 32-token tile, at most two per
+  // thread; raw codes of tile kt+1 are fetched into registers while tile kt is computed.
+  // parts per row: up to 4, but every part must hold whole 32-bit words of codes
+  constexpr int WK = D * kv_bits(FK) / 32, WV = D * kv_bits(FV) / 32;
+  constexpr int NP = (WK < WV ? WK : WV) >= 4 ? 4 : 2;
+  using RK = RowPart<D, FK, NP>;
+  using RV = RowPart<D, FV, NP>;
+  constexpr int ITEMS = PK * NP;
+  const int PS = p.page_size;
+  constexpr int CBK = kv_code_bytes(FK, D), CBV = kv_code_bytes(FV, D);
+  const int NSK = kv_nscale(FK, D, p.group), NSV = kv_nscale(FV, D, p.group);
+  RK rk[2];
+  RV rv[2];
+  auto fetch = [&](int kt) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int it = threadIdx.x + i * blockDim.x;
+      if (it >= ITEMS) continue;
+      const int r = it / NP, part = it % NP;
+      const int tok = kt * PK + r;
+      if (tok < kv_end) {
+        const int page = __ldg(bt + tok / PS);
+        const size_t rowid = ((size_t)page * p.Hkv + h) * PS + (tok % PS);
+        rk[i].load(p.k_codes + rowid * CBK, p.k_scales + rowid * NSK, part, p.group);
+        rv[i].load(p.v_codes + rowid * CBV, p.v_scales + rowid * NSV, part, p.group);
+      } else {
+        rk[i].clear();
+        rv[i].clear();
+      }
+    }
+  };
   const int n_kv_tiles = (kv_end + PK - 1) / PK;
+  fetch(0);
   for (int kt = 0; kt < n_kv_tiles; ++kt) {
     const int tok0 = kt * PK;
     __syncthreads();  // previous tile fully consumed
-    load_tile<D, FK>(Ks, p.k_codes, p.k_scales, bt, h, p.Hkv, p.page_size, p.group, tok0, PK, kv_end,
-                     threadIdx.x, blockDim.x);
-    load_tile<D, FV>(Vs, p.v_codes, p.v_scales, bt, h, p.Hkv, p.page_size, p.group, tok0, PK, kv_end,
-                     threadIdx.x, blockDim.x);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int it = threadIdx.x + i * blockDim.x;
+      if (it >= ITEMS) continue;
+      const int r = it / NP, part = it % NP;
+      rk[i].store(Ks + r * LD + part * RK::DIMS, p.group);
+      rv[i].store(Vs + r * LD + part * RV::DIMS, p.group);
+    }
+    if (kt + 1 < n_kv_tiles) fetch(kt + 1);
     __syncthreads();
     if (!active) continue;
     float s[2][PK / 8][4];

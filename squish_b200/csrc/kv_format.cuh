@@ -115,4 +115,117 @@ __device__ __forceinline__ uint4 kv_dequant8(const uint8_t* __restrict__ row_cod
   }
 }
 
+// Raw (still quantized) codes and scales of one contiguous part (D/P dims) of one
+// (page, head, token) row, held in registers so the load of the next tile can be in
+// flight while the current one is computed; dequant() turns 8 dims into 8 bf16.
+// Requires a KV group size >= 32 (so a part holds at most D/P/32 scale groups).
+template <int D, int FMT, int P>
+struct RowPart {
+  static constexpr int DIMS = D / P;
+  static constexpr int BYTES = DIMS * kv_bits(FMT) / 8;
+  static constexpr int WORDS = BYTES / 4;
+  static constexpr int CHUNKS = DIMS / 8;
+  static constexpr int NG = DIMS >= 32 ? DIMS / 32 : 1;
+  static_assert(BYTES % 4 == 0, "row part must be a whole number of 32-bit words");
+  uint32_t w[WORDS];
+  float s[NG], z[NG];
+
+  __device__ __forceinline__ void clear() {
+#pragma unroll
+    for (int i = 0; i < WORDS; ++i) w[i] = 0u;
+#pragma unroll
+    for (int i = 0; i < NG; ++i) s[i] = z[i] = 0.f;
+  }
+
+  __device__ __forceinline__ void load(const uint8_t* __restrict__ row_codes, const __half* __restrict__ row_scales,
+                                       int part, int G) {
+    const uint8_t* src = row_codes + part * BYTES;
+    if constexpr (BYTES % 16 == 0 && (D * kv_bits(FMT) / 8) % 16 == 0) {
+#pragma unroll
+      for (int i = 0; i < WORDS / 4; ++i) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + i);
+        w[4 * i] = v.x;
+        w[4 * i + 1] = v.y;
+        w[4 * i + 2] = v.z;
+        w[4 * i + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < WORDS; ++i) w[i] = __ldg(reinterpret_cast<const uint32_t*>(src) + i);
+    }
+    if constexpr (FMT != KV_BF16) {
+      const int geff = G < DIMS ? G : DIMS;
+#pragma unroll
+      for (int gi = 0; gi < NG; ++gi) {
+        const int g = (part * DIMS + gi * geff) / G;
+        if constexpr (kv_asym(FMT)) {
+          s[gi] = __half2float(__ldg(row_scales + 2 * g));
+          z[gi] = __half2float(__ldg(row_scales + 2 * g + 1));
+        } else {
+          s[gi] = __half2float(__ldg(row_scales + g));
+          z[gi] = (FMT == KV_INT4) ? -7.5f * s[gi] : (FMT == KV_INT2) ? -1.5f * s[gi] : 0.f;
+        }
+      }
+    }
+  }
+
+  // 8 dims starting at c*8 within the part -> 8 bf16
+  __device__ __forceinline__ uint4 dequant(int c, int G) const {
+    if constexpr (FMT == KV_BF16) {
+      return make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    } else {
+      const int geff = G < DIMS ? G : DIMS;
+      const int gi = NG == 1 ? 0 : (c * 8) / geff;
+      const float sc = s[gi], ze = z[gi];
+      if constexpr (FMT == KV_INT4 || FMT == KV_V4 || FMT == KV_INT2) {
+        const __nv_bfloat162 s2 = __floats2bfloat162_rn(sc, sc), z2 = __floats2bfloat162_rn(ze, ze);
+        const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.f, 128.f);
+        uint32_t o[4];
+        if constexpr (FMT == KV_INT2) {
+          const uint32_t word = (w[c >> 1] >> ((c & 1) * 16)) & 0xFFFFu;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t lo = (word >> (4 * i)) & 0x3u, hi = (word >> (4 * i + 2)) & 0x3u;
+            uint32_t t = lo | (hi << 16) | 0x43004300u;
+            __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&t);
+            o[i] = bf2u(__hfma2(__hsub2(v, k128), s2, z2));
+          }
+        } else {
+          const uint32_t word = w[c];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t b = (word >> (8 * i)) & 0xFFu;
+            uint32_t t = (b & 0xFu) | ((b >> 4) << 16) | 0x43004300u;
+            __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&t);
+            o[i] = bf2u(__hfma2(__hsub2(v, k128), s2, z2));
+          }
+        }
+        return make_uint4(o[0], o[1], o[2], o[3]);
+      } else {  // 8-bit: KV_INT8 signed symmetric, KV_K8 unsigned asymmetric
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t word = w[2 * c + (i >> 1)];
+          const int sh = (i & 1) * 16;
+          float a, b;
+          if constexpr (FMT == KV_INT8) {
+            a = (float)(int8_t)((word >> sh) & 0xFF);
+            b = (float)(int8_t)((word >> (sh + 8)) & 0xFF);
+          } else {
+            a = (float)((word >> sh) & 0xFF);
+            b = (float)((word >> (sh + 8)) & 0xFF);
+          }
+          o[i] = bf2u(__floats2bfloat162_rn(fmaf(a, sc, ze), fmaf(b, sc, ze)));
+        }
+        return make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+
+  __device__ __forceinline__ void store(__nv_bfloat16* dst, int G) const {
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) *reinterpret_cast<uint4*>(dst + c * 8) = dequant(c, G);
+  }
+};
+
 }  // namespace sq

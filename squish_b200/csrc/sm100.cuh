@@ -71,11 +71,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait. Returns false (and records `code` in *status) on timeout.
+// Bounded wait. Returns false (and records `code` in *status) on timeout. The status word
+// (global memory) is polled only every 4096 spins, so a normal hand-off costs one
+// try_wait, not an L2 round trip.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
-  for (uint32_t i = 0; i < kMaxSpin; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  for (uint32_t i = 1; i < kMaxSpin; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile int*>(status) != SQ_OK) return false;  // someone else gave up
+    if ((i & 4095u) == 0 && *reinterpret_cast<volatile int*>(status) != SQ_OK) return false;
   }
   atomicCAS(status, SQ_OK, code);
   return false;

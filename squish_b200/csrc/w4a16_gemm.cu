@@ -19,9 +19,11 @@
 //    operand layout the MMA reads;
 //  * one thread issues tcgen05.mma (kind::f16, fp32 accumulators in TMEM) and retires ring
 //    slots with tcgen05.commit;
-//  * epilogue warps read TMEM with tcgen05.ld. With split-K, every split writes an fp32
-//    partial into a workspace and the last CTA to arrive on an output tile sums the
-//    partials in split order (deterministic) and applies the epilogue.
+//  * epilogue warps read TMEM with tcgen05.ld. With split-K (decode shapes with too few
+//    output tiles to fill 148 SMs) the split CTAs of a tile form a thread-block cluster:
+//    each stages its fp32 partial in its own shared memory and, after a cluster barrier,
+//    reduces a slice of the tile by reading all partials over distributed shared memory
+//    in split order (deterministic, no global workspace).
 //
 // Every wait is bounded (sm100.cuh); on timeout *status is set and the kernel still
 // releases its TMEM before exiting.
@@ -314,47 +316,60 @@ __global__ void __launch_bounds__(C::kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) val[j] = __uint_as_float(v[j]);
           emit16(t, c0, val);
-        } else if (n < p.N) {
+        } else {
+          // split-K: stage this CTA's fp32 partial in its own shared memory, [column][row]
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = m0 + c0 + j;
-            if (m < p.M) p.ws[((size_t)split * p.M + m) * p.N + n] = __uint_as_float(v[j]);
-          }
+          for (int j = 0; j < 16; ++j) xch[(c0 + j) * BM + row] = __uint_as_float(v[j]);
         }
-      }
-    }
-    if (!single) {
-      __threadfence();
-      epi_bar();
-      const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-      if (threadIdx.x == 128) {
-        const int prev = atomicAdd(&p.counters[tile], 1);
-        *flag_slot = (prev == p.splits - 1) ? 1 : 0;
-      }
-      epi_bar();
-      if (*flag_slot) {
-        __threadfence();
-#pragma unroll 1
-        for (int t = 0; t < NT; ++t) {
-          const int n = (nblk * NT + t) * BM + row;
-#pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 16) {
-            float val[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int m = m0 + c0 + j;
-              float acc = 0.f;
-              if (m < p.M && n < p.N)
-                for (int s = 0; s < p.splits; ++s) acc += __ldcg(&p.ws[((size_t)s * p.M + m) * p.N + n]);
-              val[j] = acc;
-            }
-            emit16(t, c0, val);
-          }
-        }
-        if (threadIdx.x == 128) p.counters[tile] = 0;  // self-reset for the next launch
       }
     }
   }
+
+  if constexpr (NT == 1) {
+  if (p.splits > 1) {
+    // The split CTAs of one output tile form a cluster along z. After a cluster barrier,
+    // CTA r reduces columns [r*BN/S, (r+1)*BN/S) of the tile by reading every CTA's
+    // partial through distributed shared memory, in split order (deterministic).
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    const int S = p.splits;
+    const int jb = (BN + S - 1) / S;
+    const int j0 = split * jb, j1 = min(BN, j0 + jb);
+    const int m0 = mblk * BN;
+    const uint32_t base = smem_u32(a_ring);
+    auto ld_part = [&](int s, int idx) -> float {
+      uint32_t ra, val;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(base + idx * 4), "r"(s));
+      asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(val) : "r"(ra) : "memory");
+      return __uint_as_float(val);
+    };
+    if (p.epilogue == EPI_SILU_MUL) {
+      for (int idx = threadIdx.x; idx < (j1 - j0) * 64; idx += blockDim.x) {
+        const int j = j0 + idx / 64, r = idx % 64;
+        const int m = m0 + j, nn = nblk * 64 + r;
+        float g = 0.f, u = 0.f;
+        for (int s = 0; s < S; ++s) {
+          g += ld_part(s, j * BM + r);
+          u += ld_part(s, j * BM + r + 64);
+        }
+        if (m < p.M && nn < (p.N >> 1)) p.y[(size_t)m * p.ldy + nn] = __float2bfloat16(silu(g) * u);
+      }
+    } else {
+      for (int idx = threadIdx.x; idx < (j1 - j0) * BM; idx += blockDim.x) {
+        const int j = j0 + idx / BM, r = idx % BM;
+        const int m = m0 + j, n = nblk * BM + r;
+        float acc = 0.f;
+        for (int s = 0; s < S; ++s) acc += ld_part(s, j * BM + r);
+        if (m < p.M && n < p.N) {
+          acc += p.bias ? __bfloat162float(p.bias[n]) : 0.f;
+          if (p.residual) acc += __bfloat162float(p.residual[(size_t)m * p.ldr + n]);
+          p.y[(size_t)m * p.ldy + n] = __float2bfloat16(acc);
+        }
+      }
+    }
+    // keep every CTA's shared memory alive until all remote reads are done
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  }
+  }  // NT == 1 (split-K never runs with two weight tiles per CTA)
 
   tc_fence_before();
   __syncthreads();
@@ -373,8 +388,24 @@ cudaError_t launch_cfg(const CUtensorMap& xmap, W4A16Params p, int rw, int rx, i
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((p.N + BM * C::NT - 1) / (BM * C::NT), (p.M + C::BN - 1) / C::BN, p.splits);
-  kern<<<grid, C::kThreads, smem, stream>>>(xmap, p);
-  return cudaGetLastError();
+  if (p.splits == 1) {
+    kern<<<grid, C::kThreads, smem, stream>>>(xmap, p);
+    return cudaGetLastError();
+  }
+  if (C::NT != 1 || p.splits > 8) return cudaErrorInvalidConfiguration;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)p.splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, xmap, p);
 }
 
 }  // namespace

@@ -28,6 +28,22 @@ def _configs():
             (qwen3, QuantConfig(4, 64, True, "k8v4", 64, 16)), (tiny, dataclasses.replace(tq, kv_dtype="bf16"))]
 
 
+def _teacher_forced_ok(ref, prompt, got, tol=0.02):
+    """Every GPU token is (within tol of the logit range) the oracle's argmax, with the
+    oracle fed the GPU's own tokens. Random N(0, 0.02) models have nearly flat logits, so
+    exact greedy agreement between bf16 and fp32 is not a meaningful criterion."""
+    cache = ref.new_cache()
+    lg = ref.forward(prompt, cache, 0)[-1]
+    pos = len(prompt)
+    worst = 0.0
+    for t in got:
+        rng = float(lg.max() - lg.min())
+        worst = max(worst, float(lg.max() - lg[t]) / rng)
+        lg = ref.forward([t], cache, pos)[-1]
+        pos += 1
+    return worst <= tol, worst
+
+
 @pytest.mark.parametrize("idx", range(4))
 def test_cuda_engine_matches_cpu_oracle(cuda, idx):
     cfg, q = _configs()[idx]
@@ -39,18 +55,15 @@ def test_cuda_engine_matches_cpu_oracle(cuda, idx):
     eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
                                     EngineConfig(max_num_seqs=4, max_num_batched_tokens=64, max_model_len=512,
                                                  num_pages=128, cuda_graphs=False))
-    rid = eng.add_request(prompts[0], SamplingParams(max_tokens=1, ignore_eos=True))
-    eng.step()
+    eng.add_request(prompts[0], SamplingParams(max_tokens=1, ignore_eos=True))
     eng.step()
     gpu_logits = eng.runner.logits[0].float().cpu()
     cos = torch.nn.functional.cosine_similarity(gpu_logits, ref_logits, dim=0)
     assert cos > 0.99, f"cosine {cos}"
-    assert eng.requests[rid].output[0] == int(ref_logits.argmax())
-    # greedy continuation: the first tokens agree (bf16 vs fp32 may drift later)
-    want = ref.greedy(prompts[1], 8)[0]
+    # chunked prefill (77 tokens, 64-token budget) then greedy decode
     got = eng.generate([prompts[1]], SamplingParams(max_tokens=8, ignore_eos=True))[0]
-    agree = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), len(want))
-    assert agree >= 3, (got, want)
+    ok, worst = _teacher_forced_ok(ref, prompts[1], got)
+    assert ok, (worst, got)
     eng.runner.ws.check()
 
 
@@ -59,12 +72,11 @@ def test_tiny_config_64_tokens_oracle(cuda):
     cfg, q = get_preset("tiny-llama")
     ck = random_checkpoint(cfg, q, seed=0, device="cpu")
     prompt = torch.randint(0, 32000, (32,), generator=torch.Generator().manual_seed(1)).tolist()
-    want, _ = ReferenceModel(ck).greedy(prompt, 64)
     eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
                                     EngineConfig(max_num_seqs=1, max_model_len=256, num_pages=32))
     got = eng.generate([prompt], SamplingParams(max_tokens=64, ignore_eos=True))[0]
-    agree = sum(a == b for a, b in zip(got, want)) / 64
-    assert agree >= 0.75, (agree, got, want)
+    ok, worst = _teacher_forced_ok(ReferenceModel(ck), prompt, got)
+    assert ok, (worst, got)
 
 
 def test_graphs_match_eager(cuda):
