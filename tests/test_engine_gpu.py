@@ -28,7 +28,7 @@ def _configs():
             (qwen3, QuantConfig(4, 64, True, "k8v4", 64, 16)), (tiny, dataclasses.replace(tq, kv_dtype="bf16"))]
 
 
-def _teacher_forced_ok(ref, prompt, got, tol=0.02):
+def _teacher_forced_ok(ref, prompt, got, tol=0.04):
     """Every GPU token is (within tol of the logit range) the oracle's argmax, with the
     oracle fed the GPU's own tokens. Random N(0, 0.02) models have nearly flat logits, so
     exact greedy agreement between bf16 and fp32 is not a meaningful criterion."""
