@@ -22,6 +22,7 @@ def main():
     ap.add_argument("--group", type=int, default=64)
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--silu", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="print per-k-block role timestamps of CTA 0")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     w = torch.randn(a.n, a.k, device=dev, dtype=torch.bfloat16) * 0.02
@@ -32,6 +33,16 @@ def main():
     for _ in range(a.iters):
         y = ops.w4a16_linear(x, wt, silu_mul=a.silu)
     torch.cuda.synchronize()
+    if a.trace:
+        tr = torch.zeros(8 * 64, dtype=torch.int64, device=dev)
+        ops.w4a16_linear(x, wt, silu_mul=a.silu, trace=tr)
+        torch.cuda.synchronize()
+        t = tr.view(8, 64).cpu()
+        base = int(t[t > 0].min())
+        names = ["w_issue", "x_issue", "mma_xfull", "mma_afull", "dq_wfull", "dq_aempty", "dq_afull", "acc_full"]
+        for i in range(min(64, (a.k + 63) // 64)):
+            print(i, " ".join(f"{n}={(int(t[j, i]) - base) if t[j, i] > 0 else -1}" for j, n in enumerate(names)
+                               if j < 7 or i == 0))
     ops.workspace(dev).check()
     print("plan", ops.gemm_plan(a.m, a.n, a.k), "ok", tuple(y.shape))
 

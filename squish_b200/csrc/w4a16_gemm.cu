@@ -89,6 +89,11 @@ __device__ __forceinline__ uint4 dq_word(uint32_t w, __nv_bfloat162 s2, __nv_bfl
 
 __device__ __forceinline__ float silu(float g) { return g / (1.f + __expf(-g)); }
 
+// Optional pipeline trace (profiling builds pass p.trace): slot*64 + k-block.
+__device__ __forceinline__ void trace_mark(unsigned long long* tr, int slot, int i) {
+  if (tr != nullptr && i < 64 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) tr[slot * 64 + i] = clock64();
+}
+
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 template <class C>
@@ -171,6 +176,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
           bulk_g2s_hint(dst + NT * W_TILE_BYTES + t * sz_words * 4, p.sz + (rb * p.kb_total + kb) * sz_words,
                         (uint32_t)(sz_words * 4), &w_full[s], pol);
         }
+        trace_mark(p.trace, 0, i);
       }
     }
   } else if (warp == 1) {
@@ -181,6 +187,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
         if (!mbar_wait(&x_empty[s], ((i / ring_x) & 1) ^ 1, status, SQ_ERR_TIMEOUT_X)) break;
         mbar_expect_tx(&x_full[s], C::kXBytes);
         tma_load_2d(x_ring + s * C::kXBytes, &xmap, (kb0 + i) * BK, mblk * BN, &x_full[s]);
+        trace_mark(p.trace, 1, i);
       }
     }
   } else if (warp == 2) {
@@ -190,7 +197,9 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       for (int i = 0; i < nkb; ++i) {
         const int sx = i % ring_x, sa = i % ring_a;
         if (!mbar_wait(&x_full[sx], (i / ring_x) & 1, status, SQ_ERR_TIMEOUT_X)) break;
+        trace_mark(p.trace, 2, i);
         if (!mbar_wait(&a_full[sa], (i / ring_a) & 1, status, SQ_ERR_TIMEOUT_A)) break;
+        trace_mark(p.trace, 3, i);
         tc_fence_after();
         const uint32_t xa = smem_u32(x_ring + sx * C::kXBytes);
 #pragma unroll
@@ -216,6 +225,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     for (int i = 0; i < nkb; ++i) {
       const int s = i % ring_w, sa = i % ring_a;
       if (!mbar_wait(&w_full[s], (i / ring_w) & 1, status, SQ_ERR_TIMEOUT_W)) break;
+      if (d == 0) trace_mark(p.trace, 4, i);
       const uint8_t* wst = w_ring + s * L.w_stage;
       const uint32_t* szst = reinterpret_cast<const uint32_t*>(wst + NT * W_TILE_BYTES);
       uint4 wv[NT][C::kChunks];
@@ -232,6 +242,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       }
       mbar_arrive(&w_empty[s]);
       if (!mbar_wait(&a_empty[sa], ((i / ring_a) & 1) ^ 1, status, SQ_ERR_TIMEOUT_A)) break;
+      if (d == 0) trace_mark(p.trace, 5, i);
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         uint8_t* adst = a_ring + (sa * NT + t) * A_TILE_BYTES + row_off;
@@ -251,6 +262,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&a_full[sa]);
+      if (d == 0) trace_mark(p.trace, 6, i);
     }
   }
 
@@ -297,6 +309,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     };
 
     const bool have_acc = (nkb > 0) && mbar_wait(acc_full, 0, status, SQ_ERR_TIMEOUT_ACC);
+    if (threadIdx.x == 128) trace_mark(p.trace, 7, 0);
     tc_fence_after();
 #pragma unroll 1
     for (int t = 0; t < NT; ++t) {

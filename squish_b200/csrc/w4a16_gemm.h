@@ -24,6 +24,7 @@ struct W4A16Params {
   int gpk;                        // (scale, zero) groups per 64-column k-block: 1, 2 or 4
   int epilogue;                   // EPI_PLAIN | EPI_SILU_MUL
   int ring_w, ring_x, ring_a;     // set by the launcher
+  unsigned long long* trace;      // optional: per-k-block role timestamps of CTA (0,0,0), 8 x 64 entries
 };
 
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s);

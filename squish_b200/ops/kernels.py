@@ -118,7 +118,7 @@ EPI_PLAIN, EPI_SILU_MUL = 0, 1
 
 def w4a16_linear(x: torch.Tensor, w: Int4Weight, out: torch.Tensor | None = None,
                  residual: torch.Tensor | None = None, silu_mul: bool = False,
-                 ws: Workspace | None = None) -> torch.Tensor:
+                 ws: Workspace | None = None, trace: torch.Tensor | None = None) -> torch.Tensor:
     """y = x @ dequant(w)^T (+bias) (+residual); with ``silu_mul`` the weight rows are
     interleaved gate/up blocks of 64 and y = silu(gate) * up has N/2 columns."""
     ws = ws or workspace(x.device)
@@ -127,7 +127,7 @@ def w4a16_linear(x: torch.Tensor, w: Int4Weight, out: torch.Tensor | None = None
     if out is None:
         out = torch.empty((m, ncols), dtype=torch.bfloat16, device=x.device)
     native().w4a16_gemm(x, w.wq, w.sz, w.n, w.k, w.group, out, w.bias, residual,
-                        EPI_SILU_MUL if silu_mul else EPI_PLAIN, ws.gemm_ws, ws.gemm_counters, ws.status)
+                        EPI_SILU_MUL if silu_mul else EPI_PLAIN, ws.gemm_ws, ws.gemm_counters, ws.status, trace)
     _count()
     return out
 
