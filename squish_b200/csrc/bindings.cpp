@@ -89,11 +89,10 @@ std::vector<torch::Tensor> repack_int4(torch::Tensor packed, torch::Tensor scale
   const int64_t npad = (N + 255) / 256 * 256;
   const int64_t gpk = group >= 64 ? 1 : 64 / group;
   auto opts = packed.options().dtype(torch::kInt32);
-  torch::Tensor wq = torch::empty({npad / 128, kb, 1024}, opts);
-  torch::Tensor sz = torch::empty({npad / 128, kb, gpk * 128}, opts);
-  CUDA_OK(sq::repack_int4_launch(ptr<uint8_t>(packed), ptr<float>(scales), ptr<float>(zeros), ptr<uint32_t>(wq),
-                                 ptr<uint32_t>(sz), (int)N, (int)K, (int)group, cur_stream()));
-  return {wq, sz};
+  torch::Tensor wt = torch::empty({npad / 128, kb, 1024 + gpk * 128}, opts);
+  CUDA_OK(sq::repack_int4_launch(ptr<uint8_t>(packed), ptr<float>(scales), ptr<float>(zeros), ptr<uint32_t>(wt),
+                                 (int)N, (int)K, (int)group, cur_stream()));
+  return {wt, torch::empty({0}, opts)};
 }
 
 // Tile choice shared by the GEMM launch and the workspace sizing in Python.
@@ -117,9 +116,10 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
     tiles = tiles_of(bn, nt);
   }
   int64_t splits = 1;
-  if (tiles * 2 <= sms) {
+  const int64_t slots = (bn <= 64) ? 2 * sms : sms;  // decode shapes run two CTAs per SM
+  if (tiles * 2 <= slots) {
     // split-K over a thread-block cluster (<= 8 CTAs, portable cluster size)
-    splits = std::min<int64_t>({sms / tiles, std::max<int64_t>(1, kb / 4), 8});
+    splits = std::min<int64_t>({slots / tiles, std::max<int64_t>(1, kb / 4), 8});
     splits = std::max<int64_t>(splits, 1);
   }
   int64_t kps = (kb + splits - 1) / splits;

@@ -10,23 +10,24 @@
 //
 //  * swap-AB: weight rows are the MMA M side (128 per tile = one TMEM lane each), tokens
 //    the MMA N side (16..256), so a decode batch of 1-64 tokens still fills the M side;
-//  * packed weights and their (scale, zero) pairs are stored tile-major on the device (one
-//    contiguous 4 KiB + gpk*512 B block per 128 rows x 64 columns) and streamed with 1-D
-//    bulk copies into a deep shared-memory ring (L2 evict-first: read once per launch);
+//  * each (128 rows x 64 columns) weight tile is one contiguous block on the device —
+//    4 KiB of interleaved nibbles followed by its (scale, zero) bf16 pairs — streamed with
+//    one 1-D bulk copy per stage into a shared-memory ring (L2 evict-first);
 //  * activations arrive by TMA (2-D tensor map, 128-byte swizzle, zero fill past M and K);
 //  * dequant warps turn nibbles into bf16 with the 0x4300 exponent trick plus one bf16x2
 //    subtract and one bf16x2 FMA per pair, and write the canonical SWIZZLE_128B K-major
-//    operand layout the MMA reads;
+//    operand layout; they signal per warp (one mbarrier arrive per warp, not per thread);
 //  * one thread issues tcgen05.mma (kind::f16, fp32 accumulators in TMEM) and retires ring
 //    slots with tcgen05.commit;
 //  * epilogue warps read TMEM with tcgen05.ld. With split-K (decode shapes with too few
-//    output tiles to fill 148 SMs) the split CTAs of a tile form a thread-block cluster:
+//    output tiles to fill the SMs) the split CTAs of a tile form a thread-block cluster:
 //    each stages its fp32 partial in its own shared memory and, after a cluster barrier,
 //    reduces a slice of the tile by reading all partials over distributed shared memory
 //    in split order (deterministic, no global workspace).
 //
-// Every wait is bounded (sm100.cuh); on timeout *status is set and the kernel still
-// releases its TMEM before exiting.
+// Decode shapes (BN <= 64) run two CTAs per SM (small rings), so two independent
+// pipelines hide each other's hand-off latency. Every wait is bounded (sm100.cuh); on
+// timeout *status is set and the kernel still releases its TMEM before exiting.
 #include "sm100.cuh"
 #include "w4a16_gemm.h"
 
@@ -36,16 +37,16 @@ namespace {
 
 constexpr int BM = 128;                    // weight rows per MMA tile
 constexpr int BK = 64;                     // K per stage = one 128-byte bf16 swizzle row
-constexpr int W_TILE_BYTES = BM * BK / 2;  // 4096
+constexpr int W_TILE_BYTES = BM * BK / 2;  // 4096 nibble bytes per tile
 constexpr int A_TILE_BYTES = BM * BK * 2;  // 16384
 
-template <int BN_, int NT_, int DQ_SPLIT_>
+template <int BN_, int NT_, int MINB_>
 struct Cfg {
   static constexpr int BN = BN_;
-  static constexpr int NT = NT_;                // 128-row weight tiles per CTA
-  static constexpr int kDq = 128 * DQ_SPLIT_;   // dequant threads
-  static constexpr int kChunks = 2 / DQ_SPLIT_; // 32-column chunks per dequant thread per tile
-  static constexpr int kThreads = 128 + kDq;    // warps 0-3 control, 4.. dequant (4-7 also epilogue)
+  static constexpr int NT = NT_;          // 128-row weight tiles per CTA
+  static constexpr int kMinBlocks = MINB_;
+  static constexpr int kDqWarps = 8;      // dequant warps 4..11; thread -> (row, half of the 64 columns)
+  static constexpr int kThreads = 128 + 32 * kDqWarps;
   static constexpr int kXBytes = BN * 128;
   static constexpr int kTmemCols = (NT * BN <= 32)    ? 32
                                    : (NT * BN <= 64)  ? 64
@@ -54,18 +55,22 @@ struct Cfg {
                                                       : 512;
 };
 
+__host__ __device__ constexpr int tile_bytes(int gpk) { return W_TILE_BYTES + gpk * BM * 4; }
+
 struct Layout {
-  uint32_t x_off, w_off, w_stage, bar_off, total;
+  uint32_t x_off, w_off, w_stage, bar_off, trace_off, total;
 };
 
-__host__ __device__ inline Layout make_layout(int bn, int nt, int gpk, int rw, int rx, int ra) {
+__host__ __device__ inline Layout make_layout(int bn, int nt, int gpk, int rw, int rx, int ra, bool trace) {
   Layout L;
   L.x_off = (uint32_t)(ra * nt * A_TILE_BYTES);
   L.w_off = L.x_off + (uint32_t)(rx * bn * 128);
-  L.w_stage = (uint32_t)(nt * (W_TILE_BYTES + gpk * BM * 4));
+  L.w_stage = (uint32_t)(nt * tile_bytes(gpk));
   L.bar_off = L.w_off + (uint32_t)rw * L.w_stage;
   L.bar_off = (L.bar_off + 15u) & ~15u;
-  L.total = L.bar_off + (uint32_t)(2 * rw + 2 * rx + 2 * ra + 1) * 8u + 16u;
+  L.trace_off = L.bar_off + (uint32_t)(2 * rw + 2 * rx + 2 * ra + 1) * 8u + 16u;
+  L.trace_off = (L.trace_off + 7u) & ~7u;
+  L.total = L.trace_off + (trace ? 16u * 64u * 8u : 0u);
   return L;
 }
 
@@ -89,15 +94,34 @@ __device__ __forceinline__ uint4 dq_word(uint32_t w, __nv_bfloat162 s2, __nv_bfl
 
 __device__ __forceinline__ float silu(float g) { return g / (1.f + __expf(-g)); }
 
-// Optional pipeline trace (profiling builds pass p.trace): slot*64 + k-block.
-__device__ __forceinline__ void trace_mark(unsigned long long* tr, int slot, int i) {
-  if (tr != nullptr && i < 64 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) tr[slot * 64 + i] = clock64();
+// Optional pipeline trace (p.trace != nullptr): CTA (0,0,0) stamps clock64() per role and
+// k-block into shared memory (no global traffic inside the pipeline) and copies the
+// 16 x 64 table to p.trace at exit.
+__device__ __forceinline__ void trace_mark(unsigned long long* smem_tr, int slot, int i) {
+  if (smem_tr != nullptr && i < 64) smem_tr[slot * 64 + i] = clock64();
 }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// ring position: stage index and phase parity, advanced without division
+struct Ring {
+  int s = 0;
+  uint32_t ph = 0;
+  int n;
+  __device__ explicit Ring(int n_) : n(n_) {}
+  __device__ __forceinline__ void next() {
+    if (++s == n) {
+      s = 0;
+      ph ^= 1u;
+    }
+  }
+};
 
 template <class C>
-__global__ void __launch_bounds__(C::kThreads, 1)
+__global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const W4A16Params p) {
   constexpr int BN = C::BN;
   constexpr int NT = C::NT;
@@ -106,7 +130,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
 
   const int gpk = p.gpk;
   const int ring_w = p.ring_w, ring_x = p.ring_x, ring_a = p.ring_a;
-  const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a);
+  const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a, p.trace != nullptr);
   uint8_t* a_ring = smem;
   uint8_t* x_ring = smem + L.x_off;
   uint8_t* w_ring = smem + L.w_off;
@@ -118,7 +142,9 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   uint64_t* a_empty = a_full + ring_a;
   uint64_t* acc_full = a_empty + ring_a;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
-  int* flag_slot = reinterpret_cast<int*>(tmem_slot + 1);
+  unsigned long long* str = nullptr;
+  if (p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+    str = reinterpret_cast<unsigned long long*>(smem + L.trace_off);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -133,14 +159,14 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < ring_w; ++i) {
       mbar_init(&w_full[i], 1);
-      mbar_init(&w_empty[i], C::kDq);
+      mbar_init(&w_empty[i], C::kDqWarps);
     }
     for (int i = 0; i < ring_x; ++i) {
       mbar_init(&x_full[i], 1);
       mbar_init(&x_empty[i], 1);
     }
     for (int i = 0; i < ring_a; ++i) {
-      mbar_init(&a_full[i], C::kDq);
+      mbar_init(&a_full[i], C::kDqWarps);
       mbar_init(&a_empty[i], 1);
     }
     mbar_init(acc_full, 1);
@@ -155,63 +181,65 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int tbytes = tile_bytes(gpk);
 
   if (warp == 0) {
-    // ------------------------------------------------ weight producer
+    // ------------------------------------------------ weight producer: one bulk copy per tile
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
-      const size_t tile_words = W_TILE_BYTES / 4;
-      const size_t sz_words = (size_t)gpk * BM;
+      Ring r(ring_w);
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % ring_w;
-        if (!mbar_wait(&w_empty[s], ((i / ring_w) & 1) ^ 1, status, SQ_ERR_TIMEOUT_W)) break;
-        uint8_t* dst = w_ring + s * L.w_stage;
-        mbar_expect_tx(&w_full[s], L.w_stage);
+        if (!mbar_wait(&w_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_W)) break;
+        uint8_t* dst = w_ring + r.s * L.w_stage;
+        mbar_expect_tx(&w_full[r.s], L.w_stage);
         const int kb = kb0 + i;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-          const size_t rb = (size_t)nblk * NT + t;
-          bulk_g2s_hint(dst + t * W_TILE_BYTES, p.wq + (rb * p.kb_total + kb) * tile_words, W_TILE_BYTES,
-                        &w_full[s], pol);
-          bulk_g2s_hint(dst + NT * W_TILE_BYTES + t * sz_words * 4, p.sz + (rb * p.kb_total + kb) * sz_words,
-                        (uint32_t)(sz_words * 4), &w_full[s], pol);
+          const size_t tile = ((size_t)nblk * NT + t) * p.kb_total + kb;
+          bulk_g2s_hint(dst + t * tbytes, reinterpret_cast<const uint8_t*>(p.wq) + tile * tbytes, (uint32_t)tbytes,
+                        &w_full[r.s], pol);
         }
-        trace_mark(p.trace, 0, i);
+        trace_mark(str, 0, i);
+        r.next();
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------ activation producer (TMA)
     if (lane == 0) {
+      Ring r(ring_x);
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % ring_x;
-        if (!mbar_wait(&x_empty[s], ((i / ring_x) & 1) ^ 1, status, SQ_ERR_TIMEOUT_X)) break;
-        mbar_expect_tx(&x_full[s], C::kXBytes);
-        tma_load_2d(x_ring + s * C::kXBytes, &xmap, (kb0 + i) * BK, mblk * BN, &x_full[s]);
-        trace_mark(p.trace, 1, i);
+        if (!mbar_wait(&x_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_X)) break;
+        mbar_expect_tx(&x_full[r.s], C::kXBytes);
+        tma_load_2d(x_ring + r.s * C::kXBytes, &xmap, (kb0 + i) * BK, mblk * BN, &x_full[r.s]);
+        trace_mark(str, 1, i);
+        r.next();
       }
     }
   } else if (warp == 2) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      Ring rx(ring_x), ra(ring_a);
       for (int i = 0; i < nkb; ++i) {
-        const int sx = i % ring_x, sa = i % ring_a;
-        if (!mbar_wait(&x_full[sx], (i / ring_x) & 1, status, SQ_ERR_TIMEOUT_X)) break;
-        trace_mark(p.trace, 2, i);
-        if (!mbar_wait(&a_full[sa], (i / ring_a) & 1, status, SQ_ERR_TIMEOUT_A)) break;
-        trace_mark(p.trace, 3, i);
+        if (!mbar_wait(&x_full[rx.s], rx.ph, status, SQ_ERR_TIMEOUT_X)) break;
+        trace_mark(str, 2, i);
+        if (!mbar_wait(&a_full[ra.s], ra.ph, status, SQ_ERR_TIMEOUT_A)) break;
+        trace_mark(str, 3, i);
         tc_fence_after();
-        const uint32_t xa = smem_u32(x_ring + sx * C::kXBytes);
+        const uint32_t xa = smem_u32(x_ring + rx.s * C::kXBytes);
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-          const uint32_t aa = smem_u32(a_ring + (sa * NT + t) * A_TILE_BYTES);
+          const uint32_t aa = smem_u32(a_ring + (ra.s * NT + t) * A_TILE_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             mma_bf16_ss(tmem + t * BN, sdesc_sw128(aa + k * 32), sdesc_sw128(xa + k * 32), idesc,
                         (i > 0 || k > 0) ? 1u : 0u);
         }
-        mma_commit(&x_empty[sx]);
-        mma_commit(&a_empty[sa]);
+        mma_commit(&x_empty[rx.s]);
+        mma_commit(&a_empty[ra.s]);
+        trace_mark(str, 12, i);
+        rx.next();
+        ra.next();
       }
       mma_commit(acc_full);
     }
@@ -219,50 +247,45 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     // ------------------------------------------------ dequant warps
     const int d = threadIdx.x - 128;
     const int r = d & (BM - 1);
-    const int part = d >> 7;
+    const int c = d >> 7;  // which 32-column half of the 64-column tile
     const int sw_row = r & 7;
     const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + sw_row * 128);
+    Ring rw(ring_w), ra(ring_a);
     for (int i = 0; i < nkb; ++i) {
-      const int s = i % ring_w, sa = i % ring_a;
-      if (!mbar_wait(&w_full[s], (i / ring_w) & 1, status, SQ_ERR_TIMEOUT_W)) break;
-      if (d == 0) trace_mark(p.trace, 4, i);
-      const uint8_t* wst = w_ring + s * L.w_stage;
-      const uint32_t* szst = reinterpret_cast<const uint32_t*>(wst + NT * W_TILE_BYTES);
-      uint4 wv[NT][C::kChunks];
-      uint32_t szv[NT][C::kChunks][4];
+      if (!mbar_wait(&w_full[rw.s], rw.ph, status, SQ_ERR_TIMEOUT_W)) break;
+      if (d == 0) trace_mark(str, 4, i);
+      const uint8_t* wst = w_ring + rw.s * L.w_stage;
+      uint4 o[NT][4];
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
+        const uint8_t* tb = wst + t * tbytes;
+        const uint4 wv = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 16);
+        const uint32_t* szt = reinterpret_cast<const uint32_t*>(tb + W_TILE_BYTES);
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-        for (int cc = 0; cc < C::kChunks; ++cc) {
-          const int c = part * C::kChunks + cc;
-          wv[t][cc] = *reinterpret_cast<const uint4*>(wst + t * W_TILE_BYTES + (c * BM + r) * 16);
-#pragma unroll
-          for (int w = 0; w < 4; ++w) szv[t][cc][w] = szst[(t * gpk + (((c * 4 + w) * gpk) >> 3)) * BM + r];
+        for (int w = 0; w < 4; ++w) {
+          const uint32_t szw = szt[(((c * 4 + w) * gpk) >> 3) * BM + r];
+          const __nv_bfloat16 sc = __ushort_as_bfloat16((unsigned short)(szw & 0xFFFFu));
+          const __nv_bfloat16 ze = __ushort_as_bfloat16((unsigned short)(szw >> 16));
+          o[t][w] = dq_word(ww[w], __bfloat162bfloat162(sc), __bfloat162bfloat162(ze));
         }
       }
-      mbar_arrive(&w_empty[s]);
-      if (!mbar_wait(&a_empty[sa], ((i / ring_a) & 1) ^ 1, status, SQ_ERR_TIMEOUT_A)) break;
-      if (d == 0) trace_mark(p.trace, 5, i);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&w_empty[rw.s]);  // raw tile consumed (one arrive per warp)
+      if (!mbar_wait(&a_empty[ra.s], ra.ph ^ 1u, status, SQ_ERR_TIMEOUT_A)) break;
+      if (d == 0) trace_mark(str, 5, i);
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
-        uint8_t* adst = a_ring + (sa * NT + t) * A_TILE_BYTES + row_off;
+        uint8_t* adst = a_ring + (ra.s * NT + t) * A_TILE_BYTES + row_off;
 #pragma unroll
-        for (int cc = 0; cc < C::kChunks; ++cc) {
-          const int c = part * C::kChunks + cc;
-          const uint32_t ww[4] = {wv[t][cc].x, wv[t][cc].y, wv[t][cc].z, wv[t][cc].w};
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const uint32_t szw = szv[t][cc][w];
-            const __nv_bfloat16 sc = __ushort_as_bfloat16((unsigned short)(szw & 0xFFFFu));
-            const __nv_bfloat16 ze = __ushort_as_bfloat16((unsigned short)(szw >> 16));
-            const uint4 o = dq_word(ww[w], __bfloat162bfloat162(sc), __bfloat162bfloat162(ze));
-            *reinterpret_cast<uint4*>(adst + (((c * 4 + w) ^ sw_row) << 4)) = o;
-          }
-        }
+        for (int w = 0; w < 4; ++w) *reinterpret_cast<uint4*>(adst + (((c * 4 + w) ^ sw_row) << 4)) = o[t][w];
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&a_full[sa]);
-      if (d == 0) trace_mark(p.trace, 6, i);
+      fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core (async proxy)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[ra.s]);
+      if (d == 0) trace_mark(str, 6, i);
+      rw.next();
+      ra.next();
     }
   }
 
@@ -309,11 +332,10 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     };
 
     const bool have_acc = (nkb > 0) && mbar_wait(acc_full, 0, status, SQ_ERR_TIMEOUT_ACC);
-    if (threadIdx.x == 128) trace_mark(p.trace, 7, 0);
+    if (threadIdx.x == 128) trace_mark(str, 7, 0);
     tc_fence_after();
 #pragma unroll 1
     for (int t = 0; t < NT; ++t) {
-      const int n = (nblk * NT + t) * BM + row;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t v[16];
@@ -339,53 +361,54 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   }
 
   if constexpr (NT == 1) {
-  if (p.splits > 1) {
-    // The split CTAs of one output tile form a cluster along z. After a cluster barrier,
-    // CTA r reduces columns [r*BN/S, (r+1)*BN/S) of the tile by reading every CTA's
-    // partial through distributed shared memory, in split order (deterministic).
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-    const int S = p.splits;
-    const int jb = (BN + S - 1) / S;
-    const int j0 = split * jb, j1 = min(BN, j0 + jb);
-    const int m0 = mblk * BN;
-    const uint32_t base = smem_u32(a_ring);
-    auto ld_part = [&](int s, int idx) -> float {
-      uint32_t ra, val;
-      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(base + idx * 4), "r"(s));
-      asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(val) : "r"(ra) : "memory");
-      return __uint_as_float(val);
-    };
-    if (p.epilogue == EPI_SILU_MUL) {
-      for (int idx = threadIdx.x; idx < (j1 - j0) * 64; idx += blockDim.x) {
-        const int j = j0 + idx / 64, r = idx % 64;
-        const int m = m0 + j, nn = nblk * 64 + r;
-        float g = 0.f, u = 0.f;
-        for (int s = 0; s < S; ++s) {
-          g += ld_part(s, j * BM + r);
-          u += ld_part(s, j * BM + r + 64);
+    if (p.splits > 1) {
+      // The split CTAs of one output tile form a cluster along z. After a cluster barrier,
+      // CTA r reduces columns [r*BN/S, (r+1)*BN/S) of the tile by reading every CTA's
+      // partial through distributed shared memory, in split order (deterministic).
+      cluster_sync();
+      const int S = p.splits;
+      const int jb = (BN + S - 1) / S;
+      const int j0 = split * jb, j1 = min(BN, j0 + jb);
+      const int m0 = mblk * BN;
+      const uint32_t base = smem_u32(a_ring);
+      auto ld_part = [&](int s, int idx) -> float {
+        uint32_t ra, val;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(base + idx * 4), "r"(s));
+        asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(val) : "r"(ra) : "memory");
+        return __uint_as_float(val);
+      };
+      if (p.epilogue == EPI_SILU_MUL) {
+        for (int idx = threadIdx.x; idx < (j1 - j0) * 64; idx += blockDim.x) {
+          const int j = j0 + idx / 64, r = idx % 64;
+          const int m = m0 + j, nn = nblk * 64 + r;
+          float g = 0.f, u = 0.f;
+          for (int s = 0; s < S; ++s) {
+            g += ld_part(s, j * BM + r);
+            u += ld_part(s, j * BM + r + 64);
+          }
+          if (m < p.M && nn < (p.N >> 1)) p.y[(size_t)m * p.ldy + nn] = __float2bfloat16(silu(g) * u);
         }
-        if (m < p.M && nn < (p.N >> 1)) p.y[(size_t)m * p.ldy + nn] = __float2bfloat16(silu(g) * u);
-      }
-    } else {
-      for (int idx = threadIdx.x; idx < (j1 - j0) * BM; idx += blockDim.x) {
-        const int j = j0 + idx / BM, r = idx % BM;
-        const int m = m0 + j, n = nblk * BM + r;
-        float acc = 0.f;
-        for (int s = 0; s < S; ++s) acc += ld_part(s, j * BM + r);
-        if (m < p.M && n < p.N) {
-          acc += p.bias ? __bfloat162float(p.bias[n]) : 0.f;
-          if (p.residual) acc += __bfloat162float(p.residual[(size_t)m * p.ldr + n]);
-          p.y[(size_t)m * p.ldy + n] = __float2bfloat16(acc);
+      } else {
+        for (int idx = threadIdx.x; idx < (j1 - j0) * BM; idx += blockDim.x) {
+          const int j = j0 + idx / BM, r = idx % BM;
+          const int m = m0 + j, n = nblk * BM + r;
+          float acc = 0.f;
+          for (int s = 0; s < S; ++s) acc += ld_part(s, j * BM + r);
+          if (m < p.M && n < p.N) {
+            acc += p.bias ? __bfloat162float(p.bias[n]) : 0.f;
+            if (p.residual) acc += __bfloat162float(p.residual[(size_t)m * p.ldr + n]);
+            p.y[(size_t)m * p.ldy + n] = __float2bfloat16(acc);
+          }
         }
       }
+      cluster_sync();  // keep every CTA's shared memory alive until all remote reads are done
     }
-    // keep every CTA's shared memory alive until all remote reads are done
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
   }
-  }  // NT == 1 (split-K never runs with two weight tiles per CTA)
 
   tc_fence_before();
   __syncthreads();
+  if (str != nullptr)
+    for (int i = threadIdx.x; i < 16 * 64; i += blockDim.x) p.trace[i] = str[i];
   if (warp == 3) tmem_dealloc(tmem, C::kTmemCols);
 }
 
@@ -394,7 +417,7 @@ cudaError_t launch_cfg(const CUtensorMap& xmap, W4A16Params p, int rw, int rx, i
   p.ring_w = rw;
   p.ring_x = rx;
   p.ring_a = ra;
-  const Layout L = make_layout(C::BN, C::NT, p.gpk, rw, rx, ra);
+  const Layout L = make_layout(C::BN, C::NT, p.gpk, rw, rx, ra, p.trace != nullptr);
   const size_t smem = (size_t)L.total + 1024;  // + alignment slack
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
   auto kern = w4a16_gemm_kernel<C>;
@@ -423,23 +446,22 @@ cudaError_t launch_cfg(const CUtensorMap& xmap, W4A16Params p, int rw, int rx, i
 
 }  // namespace
 
-// Ring depths: W stage = nt*(4 KiB + gpk*512 B), X stage = bn*128 B, A stage = nt*16 KiB.
-// Decode shapes (small bn) are HBM-bound: a deep weight ring keeps ~70 KiB in flight per SM.
+// Ring depths (stages): W = nt*(4 KiB + gpk*512 B), X = bn*128 B, A = nt*16 KiB.
+// BN <= 64 (decode): ~95-105 KiB per CTA so two CTAs share an SM.
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s) {
-  const int wr = p.gpk >= 4 ? 10 : 14;
   if (nt == 1) {
     switch (bn) {
-      case 16: return launch_cfg<Cfg<16, 1, 2>>(xmap, p, wr, 4, 4, s);
-      case 32: return launch_cfg<Cfg<32, 1, 2>>(xmap, p, wr, 4, 4, s);
-      case 64: return launch_cfg<Cfg<64, 1, 2>>(xmap, p, 12, 4, 3, s);
-      case 128: return launch_cfg<Cfg<128, 1, 2>>(xmap, p, 8, 4, 3, s);
-      case 256: return launch_cfg<Cfg<256, 1, 2>>(xmap, p, 6, 3, 2, s);
+      case 16: return launch_cfg<Cfg<16, 1, 2>>(xmap, p, 8, 4, 2, s);
+      case 32: return launch_cfg<Cfg<32, 1, 2>>(xmap, p, 8, 4, 2, s);
+      case 64: return launch_cfg<Cfg<64, 1, 2>>(xmap, p, p.gpk >= 4 ? 6 : 8, 3, 2, s);
+      case 128: return launch_cfg<Cfg<128, 1, 1>>(xmap, p, 8, 4, 3, s);
+      case 256: return launch_cfg<Cfg<256, 1, 1>>(xmap, p, 6, 3, 2, s);
       default: return cudaErrorInvalidValue;
     }
   } else if (nt == 2) {
     switch (bn) {
-      case 128: return launch_cfg<Cfg<128, 2, 2>>(xmap, p, 6, 4, 2, s);
-      case 256: return launch_cfg<Cfg<256, 2, 2>>(xmap, p, 4, 3, 2, s);
+      case 128: return launch_cfg<Cfg<128, 2, 1>>(xmap, p, 6, 4, 2, s);
+      case 256: return launch_cfg<Cfg<256, 2, 1>>(xmap, p, 4, 3, 2, s);
       default: return cudaErrorInvalidValue;
     }
   }
@@ -449,12 +471,13 @@ cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int
 // ---------------------------------------------------------------------------------
 // Repack the canonical npy-dir INT4 asymmetric layout into the tile-major device layout.
 //   src: packed (N, K/2) u8 with lo nibble = even column; scales/zeros (N, G) fp32.
-//   dst: wq [Np/128][KB][2][128][4] u32, sz [Np/128][KB][gpk][128] u32 (bf16 scale | bf16 zero << 16)
+//   dst: per (128-row block rb, 64-column block kb) one contiguous tile of
+//        1024 words of nibbles [2 halves][128 rows][4 words] followed by gpk*128 words of
+//        (bf16 scale | bf16 zero << 16) [gpk][128 rows].
 //   Np = N rounded up to 256, KB = ceil(K/64); padding rows/columns dequantize to 0.
 __global__ void repack_int4_kernel(const uint8_t* __restrict__ packed, const float* __restrict__ scales,
-                                   const float* __restrict__ zeros, uint32_t* __restrict__ wq,
-                                   uint32_t* __restrict__ sz, int N, int K, int group, int kb_total, int n_pad,
-                                   int gpk) {
+                                   const float* __restrict__ zeros, uint32_t* __restrict__ wt, int N, int K,
+                                   int group, int kb_total, int n_pad, int gpk) {
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long)n_pad * kb_total) return;
   const int n = (int)(idx % n_pad);
@@ -462,7 +485,7 @@ __global__ void repack_int4_kernel(const uint8_t* __restrict__ packed, const flo
   const int rb = n / 128, r = n % 128;
   const int G = (K + group - 1) / group;
   const int pos[8] = {0, 16, 4, 20, 8, 24, 12, 28};
-  uint32_t* wt = wq + ((size_t)rb * kb_total + kb) * 1024;
+  uint32_t* tile = wt + ((size_t)rb * kb_total + kb) * (1024 + gpk * 128);
   for (int c = 0; c < 2; ++c) {
     for (int w = 0; w < 4; ++w) {
       uint32_t word = 0;
@@ -475,10 +498,10 @@ __global__ void repack_int4_kernel(const uint8_t* __restrict__ packed, const flo
         }
         word |= qv << pos[e];
       }
-      wt[(c * 128 + r) * 4 + w] = word;
+      tile[(c * 128 + r) * 4 + w] = word;
     }
   }
-  uint32_t* st = sz + ((size_t)rb * kb_total + kb) * gpk * 128;
+  uint32_t* st = tile + 1024;
   for (int j = 0; j < gpk; ++j) {
     const int col = kb * 64 + j * (64 / gpk);
     const int g = col / group;
@@ -493,13 +516,13 @@ __global__ void repack_int4_kernel(const uint8_t* __restrict__ packed, const flo
   }
 }
 
-cudaError_t repack_int4_launch(const uint8_t* packed, const float* scales, const float* zeros, uint32_t* wq,
-                               uint32_t* sz, int N, int K, int group, cudaStream_t s) {
+cudaError_t repack_int4_launch(const uint8_t* packed, const float* scales, const float* zeros, uint32_t* wt, int N,
+                               int K, int group, cudaStream_t s) {
   const int kb_total = (K + 63) / 64;
   const int n_pad = (N + 255) / 256 * 256;
   const int gpk = group >= 64 ? 1 : 64 / group;
   const long total = (long)n_pad * kb_total;
-  repack_int4_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(packed, scales, zeros, wq, sz, N, K, group,
+  repack_int4_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(packed, scales, zeros, wt, N, K, group,
                                                                      kb_total, n_pad, gpk);
   return cudaGetLastError();
 }

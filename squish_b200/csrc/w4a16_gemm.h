@@ -10,8 +10,9 @@ namespace sq {
 enum : int { EPI_PLAIN = 0, EPI_SILU_MUL = 1 };
 
 struct W4A16Params {
-  const uint32_t* wq;             // tile-major packed nibbles  [N/128][KB][2][128][4]
-  const uint32_t* sz;             // tile-major (scale | zero<<16) bf16 pairs [N/128][KB][gpk][128]
+  const uint32_t* wq;             // tile-major weight tiles [N/128][KB][1024 + gpk*128] words (nibbles, then
+                                  // (scale | zero<<16) bf16 pairs)
+  const uint32_t* sz;             // unused (kept for layout compatibility)
   const __nv_bfloat16* bias;      // [N] or nullptr
   const __nv_bfloat16* residual;  // [M, ldr] added in the epilogue, or nullptr (may alias y)
   __nv_bfloat16* y;               // [M, ldy]
@@ -24,11 +25,11 @@ struct W4A16Params {
   int gpk;                        // (scale, zero) groups per 64-column k-block: 1, 2 or 4
   int epilogue;                   // EPI_PLAIN | EPI_SILU_MUL
   int ring_w, ring_x, ring_a;     // set by the launcher
-  unsigned long long* trace;      // optional: per-k-block role timestamps of CTA (0,0,0), 8 x 64 entries
+  unsigned long long* trace;      // optional: per-k-block role timestamps of CTA (0,0,0), 16 x 64 entries
 };
 
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s);
-cudaError_t repack_int4_launch(const uint8_t* packed, const float* scales, const float* zeros, uint32_t* wq,
-                               uint32_t* sz, int N, int K, int group, cudaStream_t s);
+cudaError_t repack_int4_launch(const uint8_t* packed, const float* scales, const float* zeros, uint32_t* wt, int N,
+                               int K, int group, cudaStream_t s);
 
 }  // namespace sq

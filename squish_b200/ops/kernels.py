@@ -84,8 +84,8 @@ def workspace(device: torch.device | None = None) -> Workspace:
 class Int4Weight:
     """An INT4 asymmetric group-quantized weight in the tile-major device layout."""
 
-    wq: torch.Tensor  # int32 [Np/128, KB, 1024]
-    sz: torch.Tensor  # int32 [Np/128, KB, gpk*128]
+    wq: torch.Tensor  # int32 [Np/128, KB, 1024 + gpk*128]: nibbles then (scale, zero) pairs per tile
+    sz: torch.Tensor  # unused (empty)
     n: int
     k: int
     group: int
