@@ -113,13 +113,15 @@ __global__ void rope_kv_write_kernel(RopeKvParams p) {
   constexpr int J = D / 32;
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
   const int pos = p.positions[t];
   const int slot = p.slot_mapping ? p.slot_mapping[t] : -1;
   const __nv_bfloat16* row = p.qkv + (size_t)t * p.ld_qkv;
   const float* cs = p.cos_sin + (size_t)pos * D;  // [cos(D/2) | sin(D/2)]
   const int jobs = p.Hq + 2 * p.Hkv;
-  for (int j = warp; j < jobs; j += nwarps) {
+  {
+    // one warp per (token, head): grid (T, ceil(jobs / warps per block))
+    const int j = blockIdx.y * (blockDim.x >> 5) + warp;
+    if (j >= jobs) return;
     float v[J];
     const __nv_bfloat16* src = row + (size_t)j * D;
 #pragma unroll
@@ -171,44 +173,58 @@ __global__ void rope_kv_write_kernel(RopeKvParams p) {
   }
 }
 
-// One warp per row; H % 8 == 0. y[i] = x[row_idx[i]] * rsqrt(mean(x^2) + eps) * w
-__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
-                               __nv_bfloat16* __restrict__ y, const int* __restrict__ row_idx, int rows, int H,
-                               int ldx, int ldy, float eps) {
-  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (r >= rows) return;
+// One CTA (128 threads) per row, the row held in registers (H % 8 == 0, H <= 8192):
+// y[i] = x[row_idx[i]] * rsqrt(mean(x^2) + eps) * w.
+template <int MAXV>
+__global__ void __launch_bounds__(128) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                      const __nv_bfloat16* __restrict__ w,
+                                                      __nv_bfloat16* __restrict__ y, const int* __restrict__ row_idx,
+                                                      int rows, int H, int ldx, int ldy, float eps) {
+  __shared__ float red[4];
+  const int r = blockIdx.x;
   const int src = row_idx ? row_idx[r] : r;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)src * ldx);
   const uint4* wr = reinterpret_cast<const uint4*>(w);
   uint4* yr = reinterpret_cast<uint4*>(y + (size_t)r * ldy);
   const int nv = H / 8;
+  uint4 v[MAXV];
   float ss = 0.f;
-  for (int i = lane; i < nv; i += 32) {
-    const uint4 u = xr[i];
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float2 f = __bfloat1622float2(h[k]);
-      ss += f.x * f.x + f.y * f.y;
+  for (int i = 0; i < MAXV; ++i) {
+    const int idx = threadIdx.x + i * 128;
+    if (idx < nv) {
+      v[i] = xr[idx];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(h[k]);
+        ss += f.x * f.x + f.y * f.y;
+      }
     }
   }
   ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  ss = red[0] + red[1] + red[2] + red[3];
   const float inv = rsqrtf(ss / (float)H + eps);
-  for (int i = lane; i < nv; i += 32) {
-    const uint4 u = xr[i], wu = wr[i];
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-    const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(&wu);
-    uint4 o;
-    uint32_t* oo = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float2 f = __bfloat1622float2(h[k]);
-      const float2 gw = __bfloat1622float2(g[k]);
-      __nv_bfloat162 r2 = __floats2bfloat162_rn(f.x * inv * gw.x, f.y * inv * gw.y);
-      oo[k] = *reinterpret_cast<uint32_t*>(&r2);
+  for (int i = 0; i < MAXV; ++i) {
+    const int idx = threadIdx.x + i * 128;
+    if (idx < nv) {
+      const uint4 wu = wr[idx];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[i]);
+      const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(&wu);
+      uint4 o;
+      uint32_t* oo = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(h[k]);
+        const float2 gw = __bfloat1622float2(g[k]);
+        __nv_bfloat162 r2 = __floats2bfloat162_rn(f.x * inv * gw.x, f.y * inv * gw.y);
+        oo[k] = *reinterpret_cast<uint32_t*>(&r2);
+      }
+      yr[idx] = o;
     }
-    yr[i] = o;
   }
 }
 
@@ -216,12 +232,13 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_b
 
 cudaError_t rope_kv_write_launch(const RopeKvParams& p, int T, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  const int threads = 256;
+  const int threads = 128;
+  const dim3 grid(T, (p.Hq + 2 * p.Hkv + 3) / 4);
   switch (p.D) {
-    case 32: rope_kv_write_kernel<32><<<T, threads, 0, s>>>(p); break;
-    case 64: rope_kv_write_kernel<64><<<T, threads, 0, s>>>(p); break;
-    case 128: rope_kv_write_kernel<128><<<T, threads, 0, s>>>(p); break;
-    case 256: rope_kv_write_kernel<256><<<T, threads, 0, s>>>(p); break;
+    case 32: rope_kv_write_kernel<32><<<grid, threads, 0, s>>>(p); break;
+    case 64: rope_kv_write_kernel<64><<<grid, threads, 0, s>>>(p); break;
+    case 128: rope_kv_write_kernel<128><<<grid, threads, 0, s>>>(p); break;
+    case 256: rope_kv_write_kernel<256><<<grid, threads, 0, s>>>(p); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -230,8 +247,12 @@ cudaError_t rope_kv_write_launch(const RopeKvParams& p, int T, cudaStream_t s) {
 cudaError_t rmsnorm_launch(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, const int* row_idx,
                            int rows, int H, int ldx, int ldy, float eps, cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
-  const int warps = 8;
-  rmsnorm_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, s>>>(x, w, y, row_idx, rows, H, ldx, ldy, eps);
+  const int nv = H / 8;
+  if (nv <= 128) rmsnorm_kernel<1><<<rows, 128, 0, s>>>(x, w, y, row_idx, rows, H, ldx, ldy, eps);
+  else if (nv <= 256) rmsnorm_kernel<2><<<rows, 128, 0, s>>>(x, w, y, row_idx, rows, H, ldx, ldy, eps);
+  else if (nv <= 512) rmsnorm_kernel<4><<<rows, 128, 0, s>>>(x, w, y, row_idx, rows, H, ldx, ldy, eps);
+  else if (nv <= 1024) rmsnorm_kernel<8><<<rows, 128, 0, s>>>(x, w, y, row_idx, rows, H, ldx, ldy, eps);
+  else return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
 

@@ -183,13 +183,15 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
   const uint32_t tmem = *tmem_slot;
   const int tbytes = tile_bytes(gpk);
 
+  // Warps 0-2 run converged: every lane waits, one elected lane issues (tensor-core and
+  // bulk-copy instructions are issued by one thread of a converged warp).
   if (warp == 0) {
     // ------------------------------------------------ weight producer: one bulk copy per tile
-    if (lane == 0) {
-      const uint64_t pol = policy_evict_first();
-      Ring r(ring_w);
-      for (int i = 0; i < nkb; ++i) {
-        if (!mbar_wait(&w_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_W)) break;
+    const uint64_t pol = policy_evict_first();
+    Ring r(ring_w);
+    for (int i = 0; i < nkb; ++i) {
+      if (!mbar_wait(&w_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_W)) break;
+      if (elect_one()) {
         uint8_t* dst = w_ring + r.s * L.w_stage;
         mbar_expect_tx(&w_full[r.s], L.w_stage);
         const int kb = kb0 + i;
@@ -200,32 +202,34 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
                         &w_full[r.s], pol);
         }
         trace_mark(str, 0, i);
-        r.next();
       }
+      __syncwarp();
+      r.next();
     }
   } else if (warp == 1) {
     // ------------------------------------------------ activation producer (TMA)
-    if (lane == 0) {
-      Ring r(ring_x);
-      for (int i = 0; i < nkb; ++i) {
-        if (!mbar_wait(&x_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_X)) break;
+    Ring r(ring_x);
+    for (int i = 0; i < nkb; ++i) {
+      if (!mbar_wait(&x_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_X)) break;
+      if (elect_one()) {
         mbar_expect_tx(&x_full[r.s], C::kXBytes);
         tma_load_2d(x_ring + r.s * C::kXBytes, &xmap, (kb0 + i) * BK, mblk * BN, &x_full[r.s]);
         trace_mark(str, 1, i);
-        r.next();
       }
+      __syncwarp();
+      r.next();
     }
   } else if (warp == 2) {
     // ------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
-      Ring rx(ring_x), ra(ring_a);
-      for (int i = 0; i < nkb; ++i) {
-        if (!mbar_wait(&x_full[rx.s], rx.ph, status, SQ_ERR_TIMEOUT_X)) break;
-        trace_mark(str, 2, i);
-        if (!mbar_wait(&a_full[ra.s], ra.ph, status, SQ_ERR_TIMEOUT_A)) break;
-        trace_mark(str, 3, i);
-        tc_fence_after();
+    constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+    Ring rx(ring_x), ra(ring_a);
+    for (int i = 0; i < nkb; ++i) {
+      if (!mbar_wait(&x_full[rx.s], rx.ph, status, SQ_ERR_TIMEOUT_X)) break;
+      if (lane == 0) trace_mark(str, 2, i);
+      if (!mbar_wait(&a_full[ra.s], ra.ph, status, SQ_ERR_TIMEOUT_A)) break;
+      if (lane == 0) trace_mark(str, 3, i);
+      tc_fence_after();
+      if (elect_one()) {
         const uint32_t xa = smem_u32(x_ring + rx.s * C::kXBytes);
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
@@ -238,11 +242,13 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         mma_commit(&x_empty[rx.s]);
         mma_commit(&a_empty[ra.s]);
         trace_mark(str, 12, i);
-        rx.next();
-        ra.next();
       }
-      mma_commit(acc_full);
+      __syncwarp();
+      rx.next();
+      ra.next();
     }
+    if (elect_one()) mma_commit(acc_full);
+    __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------ dequant warps
     const int d = threadIdx.x - 128;
@@ -451,9 +457,9 @@ cudaError_t launch_cfg(const CUtensorMap& xmap, W4A16Params p, int rw, int rx, i
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s) {
   if (nt == 1) {
     switch (bn) {
-      case 16: return launch_cfg<Cfg<16, 1, 2>>(xmap, p, 8, 4, 2, s);
-      case 32: return launch_cfg<Cfg<32, 1, 2>>(xmap, p, 8, 4, 2, s);
-      case 64: return launch_cfg<Cfg<64, 1, 2>>(xmap, p, p.gpk >= 4 ? 6 : 8, 3, 2, s);
+      case 16: return launch_cfg<Cfg<16, 1, 2>>(xmap, p, 8, 4, 3, s);
+      case 32: return launch_cfg<Cfg<32, 1, 2>>(xmap, p, 8, 4, 3, s);
+      case 64: return launch_cfg<Cfg<64, 1, 2>>(xmap, p, p.gpk >= 2 ? 6 : 8, 3, 3, s);
       case 128: return launch_cfg<Cfg<128, 1, 1>>(xmap, p, 8, 4, 3, s);
       case 256: return launch_cfg<Cfg<256, 1, 1>>(xmap, p, 6, 3, 2, s);
       default: return cudaErrorInvalidValue;
