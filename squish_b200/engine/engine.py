@@ -70,6 +70,7 @@ class LLMEngine:
         self.stats = EngineStats()
         self.max_pages = (ecfg.max_model_len + qcfg.page_size - 1) // qcfg.page_size
         self.graphs = None
+        self.hidden_states: dict[str, np.ndarray] = {}  # rid -> final hidden of the last prompt token
 
     # ------------------------------------------------------------------ construction
     @staticmethod
@@ -196,9 +197,17 @@ class LLMEngine:
             for i, r in enumerate(samp):
                 t = r.tokens[-hw:]
                 hist[i, :len(t)] = t
-        return StepInputs(ids, pos, slots, nd, dl, qs, ql, ctx, tseq, tq0, bt, np.asarray(rows, dtype=np.int32), temp,
-                          topp, topk, minp, rep, step, hist, self.ecfg.seed,
-                          int(dl.max()) if nd else 0), samp
+        mask = None
+        if B and any(r.params.grammar is not None for r in samp):
+            words = (self.cfg.vocab_size + 31) // 32
+            mask = np.full((B, words), -1, dtype=np.int32)
+            for i, r in enumerate(samp):
+                if r.params.grammar is not None:
+                    mask[i] = np.asarray(r.params.grammar.allowed_mask(), dtype=np.uint32).view(np.int32)[:words]
+        st = StepInputs(ids, pos, slots, nd, dl, qs, ql, ctx, tseq, tq0, bt, np.asarray(rows, dtype=np.int32), temp,
+                        topp, topk, minp, rep, step, hist, self.ecfg.seed, int(dl.max()) if nd else 0)
+        st.allow_mask = mask
+        return st, samp
 
     def step(self) -> list[RequestOutput]:
         sched = self.scheduler.schedule()
@@ -206,7 +215,7 @@ class LLMEngine:
         if sched.empty:
             return []
         st, samp = self.build_inputs(sched)
-        if self.graphs is not None and not sched.prefill and self.graphs.can_run(st):
+        if self.graphs is not None and not sched.prefill and st.allow_mask is None and self.graphs.can_run(st):
             toks = self.graphs.run(st)
             self.stats.graph_steps += 1
         else:
@@ -224,7 +233,14 @@ class LLMEngine:
             r.num_computed = e.start + e.n
             if not e.sample:
                 self.stats.prompt_tokens += e.n
+        want_hidden = [i for i, r in enumerate(samp) if r.params.return_hidden]
+        if want_hidden:
+            hid = self.runner.last_hidden
+            for i in want_hidden:
+                self.hidden_states[samp[i].rid] = hid[i].float().cpu().numpy()
         for r, t in zip(samp, toks.tolist()):
+            if r.params.grammar is not None:
+                r.params.grammar.advance(int(t))
             if r.first_token_time is None:
                 r.first_token_time = now
                 self.stats.ttfts.append(now - r.arrival)
@@ -254,6 +270,8 @@ class LLMEngine:
             if not p.ignore_eos and tok == self.cfg.eos_token_id:
                 return "stop"
             if tok in p.stop_token_ids:
+                return "stop"
+            if p.grammar is not None and getattr(p.grammar, "is_terminated", lambda: False)():
                 return "stop"
         if n >= p.max_tokens:
             return "length"

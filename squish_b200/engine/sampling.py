@@ -17,8 +17,10 @@ class SamplingParams:
     ignore_eos: bool = False
     min_tokens: int = 0
     logprobs: bool = False
-    # grammar-constrained decoding: an object with allowed_mask(state)->np.uint32[V/32] and advance(tok)
+    # grammar-constrained decoding: an object with allowed_mask()->np.uint32[ceil(V/32)] and advance(tok)
     grammar: object | None = None
+    # keep the final-norm hidden state of the last prompt token (embeddings)
+    return_hidden: bool = False
 
     def validate(self) -> "SamplingParams":
         if self.max_tokens < 1:

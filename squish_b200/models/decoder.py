@@ -54,6 +54,7 @@ class StepInputs:
     seed: int = 0
     max_decode_ctx: int = 0
     all_logits: bool = False       # also return the logits of every logit row (spec verify)
+    allow_mask: np.ndarray | None = None  # int32 [B, ceil(V/32)] grammar bitmask (bit set = token allowed)
 
     @property
     def num_tokens(self) -> int:
@@ -203,7 +204,7 @@ class CudaRunner:
         self.tokens_host = torch.empty(B, dtype=torch.int32, pin_memory=True)
         self.max_pages = (self.max_model_len + self.qcfg.page_size - 1) // self.qcfg.page_size
         # one packed int32 staging area for all per-step metadata
-        self.meta_cap = 8 * T + 16 * B + B * self.max_pages + B * 64 + 1024
+        self.meta_cap = 8 * T + 16 * B + B * self.max_pages + B * 64 + B * ((cfg.vocab_size + 31) // 32) + 1024
         self.meta_host = torch.empty(self.meta_cap, dtype=torch.int32, pin_memory=True)
         self.meta_dev = torch.empty(self.meta_cap, dtype=torch.int32, device=dev)
         self.ws.reserve_attn(B, cfg.num_heads, 64, cfg.head_dim)
@@ -222,6 +223,8 @@ class CudaRunner:
         bt = st.block_tables
         if st.hist is not None:
             arrays["hist"] = st.hist.reshape(-1)
+        if st.allow_mask is not None:
+            arrays["mask"] = st.allow_mask.reshape(-1)
         host = self.meta_host.numpy()
         off = 0
         offs = {}
@@ -243,6 +246,8 @@ class CudaRunner:
         d["bt"] = d["bt"].view(bt.shape[0], bt.shape[1]) if bt.size else d["bt"].view(0, max(bt.shape[1], 1))
         if "hist" in d:
             d["hist"] = d["hist"].view(st.hist.shape[0], st.hist.shape[1])
+        if "mask" in d:
+            d["mask"] = d["mask"].view(st.allow_mask.shape[0], st.allow_mask.shape[1])
         return d
 
     # ------------------------------------------------------------------ forward
@@ -290,10 +295,11 @@ class CudaRunner:
         greedy = bool((st.temperature <= 0).all()) and st.hist is None
         out = self.tokens[:B]
         if greedy and not (st.rep_penalty != 1).any():
-            ops.sample(logits, out, ws=self.ws)
+            ops.sample(logits, out, allow_mask=m.get("mask"), ws=self.ws)
         else:
             ops.sample(logits, out, temperature=m["temp"], top_p=m["topp"], top_k=m["topk"], min_p=m["minp"],
-                       rep_penalty=m["rep"], hist=m.get("hist"), seed=st.seed, step=m["step"], ws=self.ws)
+                       rep_penalty=m["rep"], hist=m.get("hist"), allow_mask=m.get("mask"), seed=st.seed,
+                       step=m["step"], ws=self.ws)
         return out
 
     def sample_full(self, st: StepInputs, m: dict, logits: torch.Tensor) -> torch.Tensor:
@@ -338,6 +344,7 @@ class CudaRunner:
         self.timer_stop()
         torch.cuda.current_stream(self.device).synchronize()
         self.last_logits = logits if st.all_logits else None
+        self.last_hidden = self.xs[:B]
         return self.tokens_host[:B].numpy().copy()
 
 
@@ -419,9 +426,13 @@ class TorchPagedRunner:
         xs = _rms(h[rows], w["model.norm.weight"], cfg.rms_eps)
         logits = xs @ w["lm_head.weight"].T
         self.last_logits = logits
+        self.last_hidden = xs
         out = np.empty(len(rows), dtype=np.int32)
         for i in range(len(rows)):
             lg = logits[i].clone()
+            if st.allow_mask is not None:
+                bits = np.unpackbits(st.allow_mask[i].view(np.uint8), bitorder="little")[: lg.shape[0]]
+                lg[torch.from_numpy(bits == 0)] = float("-inf")
             if st.hist is not None and st.rep_penalty[i] != 1.0:
                 ids_ = [t for t in st.hist[i].tolist() if t >= 0]
                 for t in set(ids_):

@@ -1,0 +1,442 @@
+"""HTTP server: OpenAI-compatible ``/v1/*``, Ollama-compatible ``/api/*`` (ollama.py) and the
+LocalAI probes, over an :class:`AsyncEngine`.
+
+Route set and response shapes follow the reference server (squish/server.py:3374-4835):
+chat/completions (SSE streaming with ``stream_options.include_usage``, tools), completions
+(string, token list or batch), embeddings, models, tokenize, health, model/status,
+Prometheus metrics, trace, quality. Requests are batched by the engine (continuous
+batching), not serialised on one inference thread.
+"""
+from __future__ import annotations
+
+import asyncio
+import json
+import time
+import uuid
+
+import numpy as np
+from fastapi import FastAPI, HTTPException, Request
+from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+
+from ..engine.sampling import SamplingParams
+from ..utils import telemetry
+from .async_engine import AsyncEngine, QueueFullError
+from .chat_template import apply_chat_template
+from .tokenizer import IncrementalDetokenizer
+from .tool_calling import ToolCallStreamFilter, parse_tool_calls
+from .validation import parse_embedding_input, parse_int, parse_max_tokens, parse_temperature, parse_top_p
+
+VERSION = "0.1.0"
+
+
+class ServerState:
+    def __init__(self, aeng: AsyncEngine, model_name: str, api_key: str | None = None, arch: str = "qwen2",
+                 governor=None, load_time_s: float = 0.0):
+        self.aeng = aeng
+        self.model_name = model_name
+        self.api_key = api_key
+        self.arch = arch
+        self.governor = governor
+        self.load_time_s = load_time_s
+        self.loaded_at = time.time()
+        self.created = int(time.time())
+
+    @property
+    def tok(self):
+        return self.aeng.tokenizer
+
+
+def _check_auth(request: Request, st: ServerState) -> None:
+    if not st.api_key:
+        return
+    h = request.headers.get("authorization", "")
+    if not h.lower().startswith("bearer ") or h[7:].strip() != st.api_key:
+        raise HTTPException(status_code=401, detail="invalid or missing API key")
+
+
+async def _json(request: Request) -> dict:
+    try:
+        body = await request.json()
+    except (json.JSONDecodeError, ValueError, UnicodeDecodeError) as exc:
+        raise HTTPException(status_code=400, detail="request body must be valid JSON") from exc
+    if not isinstance(body, dict):
+        raise HTTPException(status_code=400, detail="request body must be a JSON object")
+    return body
+
+
+def sampling_from_openai(body: dict, default_max: int, eos_ids: list[int] | None = None) -> SamplingParams:
+    stop_ids = list(eos_ids or [])
+    return SamplingParams(
+        max_tokens=max(1, parse_max_tokens(body.get("max_tokens", body.get("max_completion_tokens")), default_max)),
+        temperature=parse_temperature(body.get("temperature")),
+        top_p=parse_top_p(body.get("top_p")),
+        top_k=parse_int(body.get("top_k"), "top_k", 0),
+        min_p=float(body.get("min_p", 0.0) or 0.0),
+        repetition_penalty=float(body.get("repetition_penalty", body.get("repeat_penalty", 1.0)) or 1.0),
+        seed=body.get("seed"),
+        stop_token_ids=stop_ids,
+        ignore_eos=bool(body.get("ignore_eos", False)),
+    )
+
+
+def _stop_strings(body: dict) -> list[str]:
+    s = body.get("stop")
+    if s is None:
+        return []
+    if isinstance(s, str):
+        return [s]
+    if isinstance(s, list):
+        return [x for x in s if isinstance(x, str) and x]
+    raise HTTPException(status_code=400, detail="'stop' must be a string or list of strings")
+
+
+def _truncate_at_stop(text: str, stops: list[str]) -> tuple[str, bool]:
+    cut = min((text.find(s) for s in stops if s in text), default=-1)
+    return (text[:cut], True) if cut >= 0 else (text, False)
+
+
+async def _run_one(st: ServerState, prompt_ids: list[int], params: SamplingParams, stops: list[str]):
+    """Collect one request; returns (text, token ids, finish_reason, prompt_tokens)."""
+    detok = IncrementalDetokenizer(st.tok)
+    text, ids, reason, ptoks = "", [], "stop", len(prompt_ids)
+    async for ev in st.aeng.stream(prompt_ids, params):
+        ids.extend(ev.token_ids)
+        text += detok.push(ev.token_ids)
+        if stops:
+            text, hit = _truncate_at_stop(text, stops)
+            if hit:
+                reason = "stop"
+                break
+        if ev.finished:
+            reason = "length" if ev.reason == "length" else ("stop" if ev.reason in ("stop", None) else ev.reason)
+            break
+    return text, ids, reason, ptoks
+
+
+def create_app(st: ServerState) -> FastAPI:
+    app = FastAPI(title="squish-b200", version=VERSION)
+    app.state.squish = st
+
+    @app.middleware("http")
+    async def shed_on_memory_pressure(request: Request, call_next):
+        gov = st.governor
+        if gov is not None and gov.critical and request.url.path not in ("/health", "/v1/metrics", "/model/status"):
+            return JSONResponse({"error": {"message": "server under memory pressure", "type": "overloaded"}},
+                                status_code=503, headers={"Retry-After": "2"})
+        return await call_next(request)
+
+    @app.exception_handler(QueueFullError)
+    async def _queue_full(request: Request, exc: QueueFullError):
+        return JSONResponse({"error": {"message": str(exc), "type": "rate_limit"}}, status_code=429,
+                            headers={"Retry-After": "1"})
+
+    def model_card() -> dict:
+        return {"id": st.model_name, "object": "model", "created": st.created, "owned_by": "squish"}
+
+    # ------------------------------------------------------------------ models / health
+    @app.get("/v1/models")
+    async def list_models(request: Request):
+        _check_auth(request, st)
+        return {"object": "list", "data": [model_card()]}
+
+    @app.get("/v1/models/{model_id:path}")
+    async def get_model(model_id: str, request: Request):
+        _check_auth(request, st)
+        if model_id != st.model_name:
+            raise HTTPException(status_code=404, detail=f"model {model_id!r} not found")
+        return model_card()
+
+    @app.get("/health")
+    async def health():
+        a = st.aeng
+        gov = st.governor
+        return {"status": "ok" if a.alive else "degraded", "model": st.model_name, "loaded": True,
+                "model_loaded": True, "load_mode": "eager", "load_error": a.last_error, "loader": "squish-b200",
+                "load_time_s": round(st.load_time_s, 2), "requests": a.requests_total, "tokens_gen": a.tokens_total,
+                "inflight": a.inflight, "avg_tps": round(a.avg_tps, 1), "avg_ttft_s": round(a.avg_ttft, 3),
+                "uptime_s": round(time.time() - st.loaded_at, 1),
+                "mem_available_gb": None if gov is None else round(gov.available_gb, 2),
+                "mem_pressure": None if gov is None else gov.level,
+                "engine_heartbeat_age_s": round(time.time() - a.heartbeat, 3)}
+
+    @app.get("/model/status")
+    async def model_status():
+        return {"load_mode": "eager", "model_loaded": True, "model": st.model_name,
+                "load_time_s": round(st.load_time_s, 2), "load_error": None}
+
+    @app.get("/v1/metrics")
+    async def metrics():
+        a, eng = st.aeng, st.aeng.engine
+        bm = eng.blocks
+        used = bm.num_pages - bm.num_free()
+        stats = eng.stats
+        lines = []
+
+        def m(name, typ, help_, val):
+            lines.extend([f"# HELP {name} {help_}", f"# TYPE {name} {typ}", f"{name} {val}"])
+
+        m("squish_requests_total", "counter", "Total inference requests served", a.requests_total)
+        m("squish_tokens_generated_total", "counter", "Total tokens generated", a.tokens_total)
+        m("squish_inflight_requests", "gauge", "Current in-flight requests", a.inflight)
+        m("squish_avg_tokens_per_second", "gauge", "Rolling average tokens/sec (last 20 requests)",
+          f"{a.avg_tps:.2f}")
+        m("squish_avg_ttft_seconds", "gauge", "Rolling average time-to-first-token (last 20 requests)",
+          f"{a.avg_ttft:.4f}")
+        m("squish_uptime_seconds", "counter", "Server uptime", round(time.time() - st.loaded_at, 1))
+        m("squish_model_load_seconds", "gauge", "Time taken to load the model", f"{st.load_time_s:.3f}")
+        m("squish_prefix_cache_hits_total", "counter", "Prefix page-cache hits", bm.hits)
+        m("squish_prefix_cache_hit_tokens_total", "counter", "Prompt tokens served from shared pages", bm.hit_tokens)
+        m("squish_paged_kv_free_blocks", "gauge", "Paged KV cache free pages", bm.num_free())
+        m("squish_paged_kv_used_blocks", "gauge", "Paged KV cache used pages", used)
+        m("squish_kv_cache_tokens", "gauge", "KV cache token capacity in use", used * bm.page_size)
+        m("squish_engine_steps_total", "counter", "Engine iterations", stats.steps)
+        m("squish_preemptions_total", "counter", "Requests preempted for KV capacity", stats.preemptions)
+        m("squish_errors_total", "counter", "Engine step failures", a.errors_total)
+        ttfts = sorted(stats.ttfts[-1000:])
+        if ttfts:
+            m("squish_ttft_p50_seconds", "gauge", "Median TTFT (last 1000)", f"{ttfts[len(ttfts) // 2]:.4f}")
+            m("squish_ttft_p99_seconds", "gauge", "p99 TTFT (last 1000)",
+              f"{ttfts[min(len(ttfts) - 1, int(0.99 * len(ttfts)))]:.4f}")
+        return PlainTextResponse("\n".join(lines) + "\n", media_type="text/plain; version=0.0.4")
+
+    @app.get("/v1/quality")
+    async def quality():
+        a = st.aeng
+        rec = list(a.recent)
+        tps = sorted(r[0] for r in rec)
+        ttft = sorted(r[1] for r in rec)
+
+        def pct(xs, q):
+            return xs[min(len(xs) - 1, int(q * len(xs)))] if xs else None
+
+        return {"model": st.model_name, "window": len(rec), "tps_p50": pct(tps, 0.5), "tps_p95": pct(tps, 0.95),
+                "ttft_p50_s": pct(ttft, 0.5), "ttft_p95_s": pct(ttft, 0.95)}
+
+    @app.get("/v1/trace")
+    async def get_trace():
+        return telemetry.tracer().to_chrome()
+
+    @app.delete("/v1/trace")
+    async def clear_trace():
+        telemetry.tracer().clear()
+        return {"cleared": True}
+
+    @app.post("/v1/tokenize")
+    async def tokenize(request: Request):
+        _check_auth(request, st)
+        body = await _json(request)
+        if "messages" in body:
+            text = apply_chat_template(body["messages"], st.tok, st.arch)
+        elif "text" in body:
+            text = body["text"]
+        else:
+            raise HTTPException(status_code=400, detail="Provide 'text' or 'messages' in request body")
+        ids = st.tok.encode(text)
+        return {"token_ids": ids, "token_count": len(ids), "model": st.model_name}
+
+    @app.post("/v1/detokenize")
+    async def detokenize(request: Request):
+        _check_auth(request, st)
+        body = await _json(request)
+        ids = body.get("token_ids") or body.get("tokens")
+        if not isinstance(ids, list):
+            raise HTTPException(status_code=400, detail="Provide 'token_ids'")
+        return {"text": st.tok.decode(ids), "model": st.model_name}
+
+    # ------------------------------------------------------------------ chat completions
+    @app.post("/v1/chat/completions")
+    async def chat_completions(request: Request):
+        _check_auth(request, st)
+        body = await _json(request)
+        messages = body.get("messages")
+        if not isinstance(messages, list) or not messages:
+            raise HTTPException(status_code=400, detail="'messages' must be a non-empty list")
+        tools = body.get("tools") or None
+        if body.get("tool_choice") == "none":
+            tools = None
+        with telemetry.span("chat_template"):
+            prompt = apply_chat_template(messages, st.tok, st.arch, tools=tools)
+            prompt_ids = st.tok.encode(prompt)
+        params = sampling_from_openai(body, 512, [st.tok.eos_token_id] if st.tok.eos_token_id is not None else [])
+        stops = _stop_strings(body)
+        n = max(1, parse_int(body.get("n"), "n", 1, lo=1))
+        rid = f"chatcmpl-{uuid.uuid4().hex[:24]}"
+        created = int(time.time())
+        include_usage = bool((body.get("stream_options") or {}).get("include_usage"))
+        if body.get("stream"):
+            if n != 1:
+                raise HTTPException(status_code=400, detail="streaming supports n = 1")
+            return StreamingResponse(_chat_stream(st, rid, created, prompt_ids, params, stops, tools, include_usage),
+                                     media_type="text/event-stream")
+        results = await asyncio.gather(*[_run_one(st, prompt_ids, params, stops) for _ in range(n)])
+        choices, completion_tokens = [], 0
+        for i, (text, ids, reason, _) in enumerate(results):
+            msg = {"role": "assistant", "content": text}
+            if tools:
+                content, calls = parse_tool_calls(text)
+                if calls:
+                    msg = {"role": "assistant", "content": content or None, "tool_calls": calls}
+                    reason = "tool_calls"
+            choices.append({"index": i, "message": msg, "finish_reason": reason, "logprobs": None})
+            completion_tokens += len(ids)
+        return {"id": rid, "object": "chat.completion", "created": created, "model": st.model_name,
+                "choices": choices,
+                "usage": {"prompt_tokens": len(prompt_ids), "completion_tokens": completion_tokens,
+                          "total_tokens": len(prompt_ids) + completion_tokens}}
+
+    # ------------------------------------------------------------------ completions
+    @app.post("/v1/completions")
+    async def completions(request: Request):
+        _check_auth(request, st)
+        body = await _json(request)
+        prompt = body.get("prompt")
+        if isinstance(prompt, str):
+            prompts = [st.tok.encode(prompt)]
+        elif isinstance(prompt, list) and prompt and all(isinstance(t, int) for t in prompt):
+            prompts = [prompt]
+        elif isinstance(prompt, list) and prompt and all(isinstance(p, str) for p in prompt):
+            prompts = [st.tok.encode(p) for p in prompt]
+        elif isinstance(prompt, list) and prompt and all(isinstance(p, list) for p in prompt):
+            prompts = [list(map(int, p)) for p in prompt]
+        else:
+            raise HTTPException(status_code=400, detail="'prompt' must be a string, token list, or a list of those")
+        params = sampling_from_openai(body, 256, [st.tok.eos_token_id] if st.tok.eos_token_id is not None else [])
+        stops = _stop_strings(body)
+        rid = f"cmpl-{uuid.uuid4().hex[:24]}"
+        created = int(time.time())
+        if body.get("stream"):
+            if len(prompts) != 1:
+                raise HTTPException(status_code=400, detail="streaming supports a single prompt")
+            return StreamingResponse(_completion_stream(st, rid, created, prompts[0], params, stops),
+                                     media_type="text/event-stream")
+        results = await asyncio.gather(*[_run_one(st, p, params, stops) for p in prompts])
+        echo = bool(body.get("echo"))
+        choices, ptoks, ctoks = [], 0, 0
+        for i, ((text, ids, reason, pt), p) in enumerate(zip(results, prompts)):
+            if echo:
+                text = st.tok.decode(p) + text
+            choices.append({"index": i, "text": text, "finish_reason": reason, "logprobs": None})
+            ptoks += pt
+            ctoks += len(ids)
+        return {"id": rid, "object": "text_completion", "created": created, "model": st.model_name,
+                "choices": choices, "usage": {"prompt_tokens": ptoks, "completion_tokens": ctoks,
+                                              "total_tokens": ptoks + ctoks}}
+
+    # ------------------------------------------------------------------ embeddings
+    @app.post("/v1/embeddings")
+    async def embeddings(request: Request):
+        _check_auth(request, st)
+        body = await _json(request)
+        inputs = parse_embedding_input(body.get("input"))
+        vecs, total = await embed_texts(st, inputs)
+        return {"object": "list", "model": st.model_name,
+                "data": [{"object": "embedding", "index": i, "embedding": v} for i, v in enumerate(vecs)],
+                "usage": {"prompt_tokens": total, "total_tokens": total}}
+
+    # ------------------------------------------------------------------ LocalAI probes
+    @app.get("/")
+    async def root():
+        return {"status": "ok", "name": "squish-b200", "version": VERSION}
+
+    @app.get("/v1/version")
+    async def version():
+        return {"version": VERSION}
+
+    @app.get("/readyz")
+    async def readyz():
+        return {"status": "ready" if st.aeng.alive else "starting"}
+
+    from .ollama import mount_ollama
+
+    mount_ollama(app, st)
+    return app
+
+
+async def embed_texts(st: ServerState, texts: list[str]) -> tuple[list[list[float]], int]:
+    """Last-token hidden state (after the final RMSNorm), L2-normalised, per input."""
+    out, total = [], 0
+    for t in texts:
+        ids = st.tok.encode(t) or [st.tok.eos_token_id or 0]
+        total += len(ids)
+        params = SamplingParams(max_tokens=1, temperature=0.0, ignore_eos=True, return_hidden=True)
+        rid, sink = st.aeng.submit(ids, params, asyncio.get_running_loop())
+        ev = None
+        while True:
+            ev = await sink.aq.get()
+            if ev.finished:
+                break
+        h = st.aeng.engine.hidden_states.pop(rid, None)
+        if h is None:
+            raise HTTPException(status_code=500, detail="embedding unavailable")
+        v = np.asarray(h, dtype=np.float32)
+        v = v / (np.linalg.norm(v) + 1e-12)
+        out.append(v.tolist())
+    return out, total
+
+
+def _sse(obj) -> bytes:
+    return f"data: {json.dumps(obj)}\n\n".encode()
+
+
+async def _chat_stream(st, rid, created, prompt_ids, params, stops, tools, include_usage):
+    base = {"id": rid, "object": "chat.completion.chunk", "created": created, "model": st.model_name}
+    yield _sse({**base, "choices": [{"index": 0, "delta": {"role": "assistant", "content": ""},
+                                     "finish_reason": None}]})
+    detok = IncrementalDetokenizer(st.tok)
+    filt = ToolCallStreamFilter() if tools else None
+    text_all, n_out, reason = "", 0, "stop"
+    async for ev in st.aeng.stream(prompt_ids, params):
+        n_out += len(ev.token_ids)
+        delta = detok.push(ev.token_ids)
+        text_all += delta
+        hit = False
+        if stops:
+            cut, hit = _truncate_at_stop(text_all, stops)
+            if hit:
+                delta = delta[: max(0, len(delta) - (len(text_all) - len(cut)))]
+                text_all = cut
+        if filt is not None:
+            delta = filt.push(delta)
+        if delta:
+            yield _sse({**base, "choices": [{"index": 0, "delta": {"content": delta}, "finish_reason": None}]})
+        if hit:
+            reason = "stop"
+            break
+        if ev.finished:
+            reason = "length" if ev.reason == "length" else "stop"
+            break
+    if tools:
+        _, calls = parse_tool_calls(text_all)
+        if calls:
+            reason = "tool_calls"
+            yield _sse({**base, "choices": [{"index": 0, "delta": {"tool_calls": [dict(c, index=i) for i, c in
+                                                                                  enumerate(calls)]},
+                                             "finish_reason": None}]})
+    yield _sse({**base, "choices": [{"index": 0, "delta": {}, "finish_reason": reason}]})
+    if include_usage:
+        yield _sse({**base, "choices": [], "usage": {"prompt_tokens": len(prompt_ids), "completion_tokens": n_out,
+                                                     "total_tokens": len(prompt_ids) + n_out}})
+    yield b"data: [DONE]\n\n"
+
+
+async def _completion_stream(st, rid, created, prompt_ids, params, stops):
+    base = {"id": rid, "object": "text_completion", "created": created, "model": st.model_name}
+    detok = IncrementalDetokenizer(st.tok)
+    text_all = ""
+    async for ev in st.aeng.stream(prompt_ids, params):
+        delta = detok.push(ev.token_ids)
+        text_all += delta
+        hit = False
+        if stops:
+            cut, hit = _truncate_at_stop(text_all, stops)
+            if hit:
+                delta = delta[: max(0, len(delta) - (len(text_all) - len(cut)))]
+        reason = None
+        if hit:
+            reason = "stop"
+        elif ev.finished:
+            reason = "length" if ev.reason == "length" else "stop"
+        yield _sse({**base, "choices": [{"index": 0, "text": delta, "finish_reason": reason, "logprobs": None}]})
+        if reason:
+            break
+    yield b"data: [DONE]\n\n"

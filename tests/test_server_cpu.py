@@ -1,0 +1,116 @@
+"""HTTP surface (OpenAI, Ollama, LocalAI, metrics) over the CPU oracle engine."""
+import json
+
+import pytest
+from fastapi.testclient import TestClient
+
+from squish_b200.engine.engine import EngineConfig, LLMEngine
+from squish_b200.models.config import get_preset
+from squish_b200.models.weights import random_checkpoint
+from squish_b200.serving.async_engine import AsyncEngine
+from squish_b200.serving.memory_governor import CRITICAL, MemoryGovernor
+from squish_b200.serving.server import ServerState, create_app
+from squish_b200.serving.tokenizer import ByteTokenizer
+from squish_b200.serving.tool_calling import parse_tool_calls
+
+
+@pytest.fixture(scope="module")
+def client():
+    cfg, q = get_preset("tiny-llama")
+    eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), "cpu",
+                                    EngineConfig(max_num_seqs=8, max_model_len=512, num_pages=256))
+    aeng = AsyncEngine(eng, ByteTokenizer(cfg.vocab_size, cfg.eos_token_id), model_name="tiny").start()
+    st = ServerState(aeng, "tiny", api_key=None, arch="llama")
+    with TestClient(create_app(st)) as c:
+        yield c
+    aeng.stop()
+
+
+def test_models_health_metrics(client):
+    assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
+    h = client.get("/health").json()
+    assert h["status"] == "ok" and h["model_loaded"]
+    m = client.get("/v1/metrics").text
+    assert "squish_requests_total" in m and "squish_paged_kv_free_blocks" in m
+    assert client.get("/readyz").json()["status"] == "ready"
+
+
+def test_chat_completion_nonstream(client):
+    r = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 5,
+                                                  "temperature": 0, "ignore_eos": True})
+    assert r.status_code == 200, r.text
+    d = r.json()
+    assert d["object"] == "chat.completion"
+    assert d["usage"]["completion_tokens"] == 5
+    assert d["choices"][0]["finish_reason"] == "length"
+
+
+def test_chat_completion_stream_with_usage(client):
+    with client.stream("POST", "/v1/chat/completions",
+                       json={"messages": [{"role": "user", "content": "hello"}], "max_tokens": 4, "stream": True,
+                             "temperature": 0, "ignore_eos": True, "stream_options": {"include_usage": True}}) as r:
+        lines = [l for l in r.iter_lines() if l.startswith("data: ")]
+    assert lines[-1] == "data: [DONE]"
+    chunks = [json.loads(l[6:]) for l in lines[:-1]]
+    assert chunks[0]["choices"][0]["delta"]["role"] == "assistant"
+    assert chunks[-1]["usage"]["completion_tokens"] == 4
+    assert any(c["choices"] and c["choices"][0]["finish_reason"] == "length" for c in chunks)
+
+
+def test_completions_tokens_and_batch(client):
+    r = client.post("/v1/completions", json={"prompt": ["a", "bb"], "max_tokens": 3, "temperature": 0,
+                                             "ignore_eos": True})
+    d = r.json()
+    assert len(d["choices"]) == 2 and d["usage"]["completion_tokens"] == 6
+    r = client.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 2, "temperature": 0,
+                                             "ignore_eos": True})
+    assert r.json()["usage"]["prompt_tokens"] == 3
+
+
+def test_validation_errors(client):
+    assert client.post("/v1/chat/completions", json={"messages": []}).status_code == 400
+    assert client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
+                                                      "temperature": 5}).status_code == 400
+    assert client.post("/v1/completions", content="not json").status_code == 400
+
+
+def test_tokenize_and_embeddings(client):
+    t = client.post("/v1/tokenize", json={"text": "abc"}).json()
+    assert t["token_count"] == 3
+    e = client.post("/v1/embeddings", json={"input": ["abc", "de"]}).json()
+    assert len(e["data"]) == 2 and len(e["data"][0]["embedding"]) == 256
+    v = e["data"][0]["embedding"]
+    assert abs(sum(x * x for x in v) - 1.0) < 1e-3
+
+
+def test_ollama_routes(client):
+    assert "version" in client.get("/api/version").json()
+    assert client.get("/api/tags").json()["models"][0]["name"] == "tiny"
+    r = client.post("/api/generate", json={"model": "tiny", "prompt": "hey", "stream": False,
+                                           "options": {"num_predict": 3, "temperature": 0}})
+    d = r.json()
+    assert d["done"] and d["eval_count"] >= 1
+    with client.stream("POST", "/api/chat", json={"model": "tiny", "messages": [{"role": "user", "content": "yo"}],
+                                                  "options": {"num_predict": 3, "temperature": 0}}) as r:
+        rows = [json.loads(l) for l in r.iter_lines() if l]
+    assert rows[-1]["done"] and rows[-1]["eval_count"] >= 1
+    assert client.post("/api/pull", json={"name": "x"}).status_code == 501
+    assert client.post("/api/show", json={"model": "tiny"}).json()["details"]["family"] == "llama"
+
+
+def test_tool_call_parsing():
+    content, calls = parse_tool_calls('ok <tool_call>{"name": "get_weather", "arguments": {"city": "Oslo"}}'
+                                      '</tool_call>')
+    assert content == "ok" and calls[0]["function"]["name"] == "get_weather"
+    assert json.loads(calls[0]["function"]["arguments"]) == {"city": "Oslo"}
+
+
+def test_memory_governor_levels():
+    state = {"free": 50.0}
+    gov = MemoryGovernor(mem_probe=lambda: (state["free"], 100.0), kv_usage=lambda: 0.1)
+    seen = []
+    gov.on_change(lambda a, b: seen.append(b))
+    assert gov.evaluate() == 0
+    state["free"] = 1.0
+    assert gov.evaluate() == CRITICAL and gov.critical
+    assert seen == [CRITICAL]
