@@ -1,0 +1,165 @@
+"""``squish compress``: HF safetensors (or random init) -> npy-dir, shard by shard, resumable.
+
+Per shard: load tensors (on the GPU when one is present, where the INT4 quantizer runs as a
+CUDA kernel), quantize every 2-D projection weight, pass embeddings, norms, biases and MoE
+routers through as fp16, write the tensor files, then commit ``manifest.json`` and
+``_compress_progress.json`` (completed shards) before moving on — the reference's
+streaming converter contract (squish/convert.py:610-935). Re-running after an interruption
+skips completed shards. ``delete_source`` removes a raw shard only after its output and
+progress are on disk.
+"""
+from __future__ import annotations
+
+import json
+import os
+import shutil
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from ..models.config import QuantConfig, from_hf_config, get_preset, to_hf_config
+from ..models.weights import QTensor, random_checkpoint
+from ..quant.codecs import quantize
+from .npy_dir import safe_key, tensor_files
+
+PASSTHROUGH_PATTERNS = ("embed_tokens", "norm", "mlp.gate.weight", ".bias")
+
+
+def should_quantize(name: str, shape: tuple, patterns=PASSTHROUGH_PATTERNS) -> bool:
+    if len(shape) != 2:
+        return False
+    if any(p in name for p in patterns) and not name.endswith("lm_head.weight"):
+        return False
+    return True
+
+
+def _write_tensor(td: Path, name: str, t: QTensor) -> int:
+    n = 0
+    for key, a in tensor_files(name, t).items():
+        p = td / f"{key}.npy"
+        np.save(str(p), a)
+        n += p.stat().st_size
+    return n
+
+
+def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size: int = 64, mse_clip: bool = False,
+             device: str | None = None, delete_source: bool = False, random_preset: str | None = None,
+             seed: int = 0, kv_dtype: str = "int4", log=print) -> dict:
+    out = Path(out_dir)
+    td = out / "tensors"
+    td.mkdir(parents=True, exist_ok=True)
+    dev = torch.device(device or ("cuda" if torch.cuda.is_available() else "cpu"))
+    progress_path = out / "_compress_progress.json"
+    man_path = out / "manifest.json"
+    manifest = json.loads(man_path.read_text()) if man_path.exists() else {}
+    done = json.loads(progress_path.read_text())["completed_shards"] if progress_path.exists() else []
+    stats = {"n_quantized": 0, "n_passthrough": 0, "bytes": 0, "shards": 0, "skipped_shards": len(done)}
+    t0 = time.time()
+
+    if random_preset:
+        cfg, q = get_preset(random_preset)
+        q.group_size, q.mse_clip, q.kv_dtype = group_size, mse_clip, kv_dtype
+        if "random-init" not in done:
+            ck = random_checkpoint(cfg, q, seed=seed, device=dev)
+            for name, t in ck.tensors.items():
+                if name == "lm_head.weight" and cfg.tie_embeddings:
+                    continue
+                if t.kind != "dense" and kind != "q4a":
+                    t = quantize(t.dequantize(), kind, group_size, mse_clip)
+                stats["bytes"] += _write_tensor(td, name, t)
+                stats["n_quantized" if t.kind != "dense" else "n_passthrough"] += 1
+                manifest[name] = safe_key(name)
+            done.append("random-init")
+        shards = []
+    else:
+        from safetensors import safe_open
+
+        src = Path(model_dir)
+        cfg = from_hf_config(str(src))
+        q = QuantConfig(weight_bits=16 if kind == "dense" else 4, group_size=group_size, mse_clip=mse_clip,
+                        kv_dtype=kv_dtype)
+        shards = sorted(p for p in src.glob("*.safetensors"))
+        if not shards:
+            raise FileNotFoundError(f"no *.safetensors in {src}")
+        for i, shard in enumerate(shards):
+            if shard.name in done:
+                continue
+            with safe_open(str(shard), "pt", device=str(dev) if dev.type == "cuda" else "cpu") as f:
+                for name in f.keys():
+                    w = f.get_tensor(name)
+                    if should_quantize(name, tuple(w.shape)):
+                        t = quantize(w if dev.type == "cuda" else w.float(), kind, group_size, mse_clip)
+                        stats["n_quantized"] += 1
+                    else:
+                        t = QTensor("dense", tuple(w.shape), data=w.float().cpu())
+                        stats["n_passthrough"] += 1
+                    stats["bytes"] += _write_tensor(td, name, t)
+                    manifest[name] = safe_key(name)
+                    del w
+            man_path.write_text(json.dumps(manifest, indent=2))
+            done.append(shard.name)
+            progress_path.write_text(json.dumps({"completed_shards": done, "total_shards": len(shards),
+                                                 "delete_source": delete_source}, indent=2))
+            stats["shards"] += 1
+            log(f"  shard {i + 1}/{len(shards)} {shard.name} done")
+            if delete_source:
+                shard.unlink()
+        for extra in ("tokenizer.json", "tokenizer_config.json", "tokenizer.model", "special_tokens_map.json",
+                      "generation_config.json", "vocab.json", "merges.txt"):
+            if (src / extra).exists():
+                shutil.copy2(src / extra, out / extra)
+    man_path.write_text(json.dumps(manifest, indent=2))
+    progress_path.write_text(json.dumps({"completed_shards": done, "total_shards": max(len(shards), 1),
+                                         "delete_source": delete_source}, indent=2))
+    (out / "config.json").write_text(json.dumps(to_hf_config(cfg), indent=2))
+    q.weight_bits = 16 if kind == "dense" else 4
+    (out / "squish_quant.json").write_text(json.dumps(dict(q.__dict__, weight_kind=kind), indent=2))
+    (td / ".manifest_ready").touch()
+    stats["seconds"] = round(time.time() - t0, 2)
+    return stats
+
+
+def load_checkpoint(path: str, device: str | None = None):
+    """Any supported checkpoint -> (Checkpoint, tokenizer directory or None)."""
+    from .npy_dir import detect_format, read_npy_dir, read_squish_4bit
+
+    fmt = detect_format(path)
+    p = Path(path)
+    if fmt == "gguf":
+        from .gguf import read_gguf
+
+        return read_gguf(path), None
+    if fmt == "squizd":
+        from .squizd import read_squizd
+
+        return read_squizd(path), None
+    cfg = from_hf_config(str(p))
+    qpath = p / "squish_quant.json"
+    q = QuantConfig()
+    if qpath.exists():
+        d = json.loads(qpath.read_text())
+        q = QuantConfig(**{k: v for k, v in d.items() if k in QuantConfig.__dataclass_fields__})
+    if fmt == "npy-dir":
+        return read_npy_dir(p, cfg, q), str(p)
+    if fmt == "squish_4bit":
+        return read_squish_4bit(p, cfg, q), str(p)
+    if fmt == "hf":
+        from safetensors.torch import load_file
+
+        from ..models.weights import Checkpoint
+
+        ck = Checkpoint(cfg, q)
+        for f in sorted(p.glob("*.safetensors")):
+            for name, w in load_file(str(f)).items():
+                if should_quantize(name, tuple(w.shape)):
+                    dev = device or ("cuda" if torch.cuda.is_available() else "cpu")
+                    ck.tensors[name] = quantize(w.to(dev), "q4a", q.group_size, q.mse_clip)
+                else:
+                    ck.tensors[name] = QTensor("dense", tuple(w.shape), data=w.float())
+        if "lm_head.weight" not in ck.tensors:
+            ck.tensors["lm_head.weight"] = quantize(ck.tensors["model.embed_tokens.weight"].data, "q4a",
+                                                    q.group_size)
+        return ck, str(p)
+    raise ValueError(fmt)

@@ -121,9 +121,18 @@ def _interleave_gate_up(gate: QTensor, up: QTensor) -> QTensor:
                    scales=inter(gate.scales, up.scales), offsets=inter(gate.offsets, up.offsets), group=gate.group)
 
 
-def _to_int4(t: QTensor, device, bias: torch.Tensor | None = None) -> Int4Weight:
-    if t.kind != "q4a":
-        raise ValueError("CUDA path expects INT4 (q4a) linear weights")
+def _as_q4a(t: QTensor, group: int) -> QTensor:
+    """The tcgen05 GEMM consumes INT4 asymmetric tiles; other stored kinds (INT8, NF4, INT3,
+    INT2, AQLM, dense) are decoded once at load and re-encoded as INT4 group ``group``."""
+    if t.kind == "q4a":
+        return t
+    from ..quant.codecs import quantize
+
+    return quantize(t.dequantize().float(), "q4a", group)
+
+
+def _to_int4(t: QTensor, device, bias: torch.Tensor | None = None, group: int = 64) -> Int4Weight:
+    t = _as_q4a(t, group)
     return ops.prepare_int4_weight(t.packed, t.scales, t.offsets, t.shape[1], t.group, device, bias=bias)
 
 
@@ -152,8 +161,8 @@ class CudaRunner:
         self.layers: list[LayerWeights] = []
         for i in range(cfg.num_layers):
             p = f"model.layers.{i}."
-            qkv = _cat_q4a([t[p + "self_attn.q_proj.weight"], t[p + "self_attn.k_proj.weight"],
-                            t[p + "self_attn.v_proj.weight"]])
+            g = self.qcfg.group_size
+            qkv = _cat_q4a([_as_q4a(t[p + f"self_attn.{n}_proj.weight"], g) for n in "qkv"])
             bias = None
             if cfg.qkv_bias:
                 bias = torch.cat([t[p + f"self_attn.{n}.bias"].data.float() for n in ("q_proj", "k_proj", "v_proj")])
@@ -169,8 +178,8 @@ class CudaRunner:
 
                 lw.moe = MoELayer.from_checkpoint(ck, i, dev)
             else:
-                lw.gate_up = _to_int4(_interleave_gate_up(t[p + "mlp.gate_proj.weight"], t[p + "mlp.up_proj.weight"]),
-                                      dev)
+                lw.gate_up = _to_int4(_interleave_gate_up(_as_q4a(t[p + "mlp.gate_proj.weight"], g),
+                                                          _as_q4a(t[p + "mlp.up_proj.weight"], g)), dev)
                 lw.down = _to_int4(t[p + "mlp.down_proj.weight"], dev)
             self.layers.append(lw)
             if free_checkpoint:
@@ -179,7 +188,7 @@ class CudaRunner:
                         del t[k]
         self.norm = _dense(t["model.norm.weight"], dev)
         lm = t["lm_head.weight"]
-        self.lm_head_q = _to_int4(lm, dev) if lm.kind == "q4a" else None
+        self.lm_head_q = _to_int4(lm, dev, group=self.qcfg.group_size) if lm.kind != "dense" else None
         self.lm_head_dense = _dense(lm, dev) if lm.kind == "dense" else None
         self.cos_sin = rope_table(cfg, max(max_model_len, 16) + 1).to(dev)
         self.pools = pools or KVPools(cfg, self.qcfg, num_pages, dev)

@@ -31,11 +31,17 @@ class QTensor:
     offsets: torch.Tensor | None = None
     group: int = 0
     data: torch.Tensor | None = None
+    extra: dict | None = None  # INT3 low-rank compensator (lra, lrb)
 
     def dequantize(self) -> torch.Tensor:
-        """fp32 reconstruction (offset + q * scale), on the tensor's device."""
+        """fp32 reconstruction on the CPU for the CPU-decoded kinds, on the tensor's device
+        for INT4 asymmetric."""
         if self.kind == "dense":
             return self.data.float()
+        if self.kind != "q4a":
+            from ..quant.codecs import dequantize_qtensor
+
+            return dequantize_qtensor(self)
         p = self.packed.to(torch.int64)
         q = torch.empty(p.shape[0], p.shape[1] * 2, dtype=torch.float32, device=p.device)
         q[:, 0::2] = (p & 0xF).float()

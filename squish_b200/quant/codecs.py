@@ -1,0 +1,70 @@
+"""Weight codecs of the npy-dir format (quantize / dequantize), on top of the C++ CPU kernels.
+
+Each codec restates a reference quantizer (squish_quant_rs/src/lib.rs, squish/quant/*):
+INT8 symmetric, INT4 asymmetric (+ MSE clip search), INT4 symmetric legacy, NF4, INT3
+(8 values per 3 bytes, with the optional low-rank compensator of MiLo), INT2 asymmetric,
+and AQLM additive codebooks (quant/aqlm.py).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from .._ext import native
+from ..models.weights import QTensor
+
+
+def dequantize_qtensor(t: QTensor) -> torch.Tensor:
+    C = native().cpu
+    k = t.kind
+    if k == "q4a":
+        return C.dequantize_int4_asym(t.packed.cpu(), t.scales.cpu().float(), t.offsets.cpu().float(), t.group)
+    if k == "nf4":
+        return C.dequantize_nf4(t.packed.cpu(), t.scales.cpu().float(), t.group)
+    if k == "q8":
+        return C.dequantize_int8(t.packed.cpu(), t.scales.cpu().float())
+    if k == "q2":
+        return C.dequantize_int2(t.packed.cpu(), t.scales.cpu().float(), t.offsets.cpu().float(), t.group)
+    if k == "q3":
+        w = C.unpack_int3(t.packed.cpu(), t.scales.cpu().float(), t.group, t.shape[-1])
+        if t.offsets is not None:
+            w = w + t.offsets.cpu().float().repeat_interleave(t.group, dim=1)[:, : w.shape[1]]
+        ex = t.extra or {}
+        if "lra" in ex:  # low-rank compensator: W += A @ B
+            w = w + ex["lra"].float() @ ex["lrb"].float()
+        return w
+    if k == "aqlm":
+        from .aqlm import aqlm_dequantize
+
+        return aqlm_dequantize(t)
+    raise ValueError(f"unknown tensor kind {k!r}")
+
+
+def quantize(w: torch.Tensor, kind: str, group: int, mse_clip: bool = False) -> QTensor:
+    """Quantize a 2-D weight to ``kind`` (q4a | q8 | nf4 | q2 | q3 | aqlm | dense)."""
+    from ..models.weights import pick_group, quantize_q4a
+
+    C = native().cpu
+    if kind == "q4a":
+        return quantize_q4a(w, group, mse_clip)
+    if kind == "dense":
+        return QTensor("dense", tuple(w.shape), data=w)
+    wf = w.detach().float().cpu().contiguous()
+    g = pick_group(wf.shape[1], group)
+    if kind == "q8":
+        q, s = C.quantize_int8(wf, g)
+        return QTensor("q8", tuple(wf.shape), packed=q, scales=s, group=g)
+    if kind == "nf4":
+        p, s = C.quantize_nf4(wf, g)
+        return QTensor("nf4", tuple(wf.shape), packed=p, scales=s, group=g)
+    if kind == "q2":
+        p, s, z = C.quantize_int2(wf, g)
+        return QTensor("q2", tuple(wf.shape), packed=p, scales=s, offsets=z, group=g)
+    if kind == "q3":
+        p, s = C.pack_int3(wf, g)
+        return QTensor("q3", tuple(wf.shape), packed=p, scales=s, group=g)
+    if kind == "aqlm":
+        from .aqlm import aqlm_quantize
+
+        return aqlm_quantize(wf)
+    raise ValueError(f"unknown quantization kind {kind!r}")
