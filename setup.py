@@ -7,7 +7,7 @@ produces squish_b200/_C*.so (CUDA kernels for sm_100a + the C++ CPU reference li
 import glob
 import os
 
-from setuptools import setup
+from setuptools import find_packages, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -28,7 +28,8 @@ if os.environ.get("SQ_PTXAS_VERBOSE"):
 setup(
     name="squish_b200",
     version="0.1.0",
-    packages=["squish_b200"],
+    packages=find_packages(include=["squish_b200", "squish_b200.*"]),
+    entry_points={"console_scripts": ["squish=squish_b200.cli:main"]},
     ext_modules=[
         CUDAExtension(
             name="squish_b200._C",

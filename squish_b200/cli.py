@@ -1,0 +1,357 @@
+"""``squish`` command line (the reference's verbs, squish/cli.py:6715-6975).
+
+    squish serve MODEL       OpenAI + Ollama + LocalAI HTTP server
+    squish run MODEL [TEXT]  one-shot generation when TEXT is given, else serve
+    squish compress SRC      HF safetensors (or --random-init PRESET) -> npy-dir
+    squish convert SRC DST   between npy-dir / squizd
+    squish models            local checkpoints and built-in presets
+    squish catalog           presets with their sizes
+    squish pull NAME         (offline) materialise a preset as a random-init checkpoint
+    squish bench MODEL       closed-loop serving load (tok/s, TTFT p50/p99)
+    squish doctor            GPU, extension and interconnect checks
+    squish config ...        get / set / show / reset / path of ~/.squish/config.json
+    squish daemon ...        start / stop / status / ping / reload the UDS daemon
+    squish version
+
+MODEL is a checkpoint path or a preset name (random-init weights of that architecture).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+from pathlib import Path
+
+from . import config as ucfg
+
+__version__ = "0.1.0"
+
+
+def _engine_args(p: argparse.ArgumentParser) -> None:
+    e = ucfg.load()["engine"]
+    p.add_argument("model", nargs="?", default=None, help="checkpoint path or preset name")
+    p.add_argument("--device", default=None)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--kv-dtype", "--kv-bits", dest="kv_dtype", default=None,
+                   choices=["bf16", "fp16", "int8", "int4", "int2", "k8v4"])
+    p.add_argument("--max-num-seqs", "--batch-size", dest="max_num_seqs", type=int, default=e["max_num_seqs"])
+    p.add_argument("--max-num-batched-tokens", "--chunk-prefill-size", dest="max_num_batched_tokens", type=int,
+                   default=e["max_num_batched_tokens"])
+    p.add_argument("--max-model-len", "--max-kv-size", dest="max_model_len", type=int, default=e["max_model_len"])
+    p.add_argument("--gpu-memory-utilization", type=float, default=e["gpu_memory_utilization"])
+    p.add_argument("--no-cuda-graphs", action="store_true")
+    p.add_argument("--no-prefix-caching", "--no-block-kv-cache", dest="no_prefix_caching", action="store_true")
+    p.add_argument("--chunk-align", type=int, default=0, help="grid-aligned prefill chunks (bit-exact prefix reuse)")
+
+
+def _ecfg(a):
+    from .engine.engine import EngineConfig
+
+    return EngineConfig(max_num_seqs=a.max_num_seqs, max_num_batched_tokens=a.max_num_batched_tokens,
+                        max_model_len=a.max_model_len, gpu_memory_utilization=a.gpu_memory_utilization,
+                        enable_prefix_caching=not a.no_prefix_caching, cuda_graphs=not a.no_cuda_graphs,
+                        chunk_align=a.chunk_align, seed=a.seed)
+
+
+def _kv(a):
+    return {"fp16": "bf16"}.get(a.kv_dtype, a.kv_dtype)
+
+
+def _model(a) -> str:
+    return a.model or ucfg.get("model.default")
+
+
+def cmd_serve(a) -> int:
+    import uvicorn
+
+    from .api import load_engine
+    from .serving.async_engine import AsyncEngine
+    from .serving.server import ServerState, create_app
+
+    c = ucfg.load()["server"]
+    loaded = load_engine(_model(a), a.device, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a))
+    aeng = AsyncEngine(loaded.engine, loaded.tokenizer, max_pending=c["max_pending"], model_name=loaded.name).start()
+    key = a.api_key if a.api_key is not None else os.environ.get("SQUISH_API_KEY", c["api_key"])
+    st = ServerState(aeng, loaded.name, api_key=key or None, arch=loaded.engine.cfg.arch, load_time_s=loaded.load_s)
+    print(f"squish: {loaded.name} loaded in {loaded.load_s:.1f}s; listening on http://{a.host or c['host']}:"
+          f"{a.port or c['port']}", file=sys.stderr)
+    try:
+        uvicorn.run(create_app(st), host=a.host or c["host"], port=a.port or c["port"], log_level="warning")
+    finally:
+        aeng.stop()
+    return 0
+
+
+def cmd_run(a) -> int:
+    if not a.text:
+        return cmd_serve(a)
+    from .api import LLM
+    from .engine.sampling import SamplingParams
+    from .serving.chat_template import apply_chat_template
+
+    llm = LLM(_model(a), a.device, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a))
+    prompt = apply_chat_template([{"role": "user", "content": " ".join(a.text)}], llm.tokenizer,
+                                 arch=llm.engine.cfg.arch)
+    p = SamplingParams(max_tokens=a.max_tokens, temperature=a.temperature, top_p=a.top_p,
+                       stop_token_ids=[llm.engine.cfg.eos_token_id])
+    out = llm.generate([prompt], p)[0]
+    print(out["text"])
+    return 0
+
+
+def cmd_compress(a) -> int:
+    from .io.convert import compress
+
+    kind = {"int4": "q4a", "int8": "q8", "nf4": "nf4", "int3": "q3", "int2": "q2", "aqlm": "aqlm",
+            "none": "dense"}[a.format]
+    out = a.output or (str(Path(a.source).with_name(Path(a.source).name + "-squished")) if a.source else
+                       str(ucfg.squish_home() / "models" / a.random_init))
+    st = compress(a.source, out, kind=kind, group_size=a.group_size, mse_clip=a.mse, device=a.device,
+                  delete_source=a.delete_source, random_preset=a.random_init, seed=a.seed, kv_dtype=a.kv_dtype)
+    print(json.dumps({"output": out, **st}))
+    return 0
+
+
+def cmd_convert(a) -> int:
+    from .io.convert import load_checkpoint
+    from .io.npy_dir import write_npy_dir
+    from .io.squizd import write_squizd
+
+    ck, _ = load_checkpoint(a.source, "cpu")
+    if a.to == "squizd":
+        write_squizd(a.dest, ck, group=a.group_size)
+    else:
+        write_npy_dir(a.dest, ck)
+    print(json.dumps({"output": a.dest, "format": a.to, "tensors": len(ck.tensors)}))
+    return 0
+
+
+def _local_models() -> list[dict]:
+    from .io.npy_dir import detect_format
+
+    dirs = [ucfg.squish_home() / "models"]
+    extra = ucfg.get("model.models_dir")
+    if extra:
+        dirs.append(Path(extra))
+    out = []
+    for d in dirs:
+        if not d.is_dir():
+            continue
+        for p in sorted(d.iterdir()):
+            try:
+                fmt = detect_format(p)
+            except (ValueError, OSError):
+                continue
+            size = sum(f.stat().st_size for f in p.rglob("*") if f.is_file()) if p.is_dir() else p.stat().st_size
+            out.append({"name": p.name, "path": str(p), "format": fmt, "bytes": size})
+    return out
+
+
+def _catalog() -> list[dict]:
+    from .models.config import PRESETS
+
+    rows = []
+    for name, (c, q) in sorted(PRESETS.items()):
+        rows.append({"name": name, "arch": c.arch, "layers": c.num_layers, "hidden": c.hidden_size,
+                     "params_b": round(c.num_params() / 1e9, 2) if hasattr(c, "num_params") else None,
+                     "weights": f"int{q.weight_bits} g{q.group_size}", "kv": q.kv_dtype})
+    return rows
+
+
+def cmd_models(a) -> int:
+    print(json.dumps({"local": _local_models(), "presets": [r["name"] for r in _catalog()]}, indent=2))
+    return 0
+
+
+def cmd_catalog(a) -> int:
+    print(json.dumps(_catalog(), indent=2))
+    return 0
+
+
+def cmd_pull(a) -> int:
+    from .models.config import PRESETS
+
+    if a.name.lower() not in PRESETS:
+        print(f"squish pull: no network access here; {a.name!r} is not a built-in preset "
+              f"({', '.join(sorted(PRESETS))}). Download the HF checkpoint elsewhere and run "
+              f"'squish compress <dir>'.", file=sys.stderr)
+        return 2
+    a.source, a.random_init, a.output = None, a.name.lower(), None
+    a.format, a.mse, a.delete_source, a.kv_dtype = "int4", False, False, "int4"
+    a.group_size = PRESETS[a.name.lower()][1].group_size
+    return cmd_compress(a)
+
+
+def cmd_bench(a) -> int:
+    import torch
+
+    from .api import load_engine
+    from .utils.loadgen import run_load
+
+    loaded = load_engine(_model(a), a.device, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a))
+    sync = torch.cuda.synchronize if torch.cuda.is_available() and loaded.engine.runner.__class__.__name__ == \
+        "CudaRunner" else None
+    rows = []
+    for c in a.concurrency:
+        rows.append(run_load(loaded.engine, num_requests=max(a.requests, c), concurrency=c, prompt_min=a.prompt_min,
+                             prompt_max=a.prompt_max, max_tokens=a.max_tokens, seed=a.seed, sync=sync))
+        print(json.dumps({"model": loaded.name, **rows[-1]}), flush=True)
+    return 0
+
+
+def doctor_report() -> dict:
+    import torch
+
+    rep: dict = {"python": sys.version.split()[0], "torch": torch.__version__, "cuda_available":
+                 torch.cuda.is_available(), "squish_home": str(ucfg.squish_home())}
+    try:
+        from ._ext import native
+
+        native()
+        rep["extension"] = "loaded"
+    except Exception as exc:  # noqa: BLE001 - report, do not raise
+        rep["extension"] = f"missing: {exc}"
+    if torch.cuda.is_available():
+        n = torch.cuda.device_count()
+        gpus = []
+        for i in range(n):
+            p = torch.cuda.get_device_properties(i)
+            gpus.append({"index": i, "name": p.name, "sm": f"{p.major}.{p.minor}", "sms": p.multi_processor_count,
+                         "memory_gb": round(p.total_memory / 2**30, 1), "sm_100a": (p.major, p.minor) == (10, 0)})
+        rep["gpus"] = gpus
+        if n > 1:
+            rep["peer_access"] = all(torch.cuda.can_device_access_peer(0, j) for j in range(1, n))
+        try:
+            rep["nccl"] = ".".join(map(str, torch.cuda.nccl.version()))
+        except (AttributeError, RuntimeError):
+            rep["nccl"] = None
+    return rep
+
+
+def cmd_doctor(a) -> int:
+    rep = doctor_report()
+    print(json.dumps(rep, indent=2))
+    return 0 if rep.get("extension") == "loaded" else 1
+
+
+def cmd_config(a) -> int:
+    if a.action == "show":
+        print(json.dumps(ucfg.load(), indent=2, sort_keys=True))
+    elif a.action == "path":
+        print(ucfg.config_path())
+    elif a.action == "get":
+        v = ucfg.get(a.key)
+        if v is None:
+            print(f"unknown key {a.key}", file=sys.stderr)
+            return 1
+        print(json.dumps(v))
+    elif a.action == "set":
+        ucfg.set_value(a.key, a.value)
+        print(json.dumps(ucfg.get(a.key)))
+    elif a.action == "reset":
+        ucfg.reset()
+    return 0
+
+
+def cmd_daemon(a) -> int:
+    from . import daemon as d
+
+    if a.action == "start":
+        if d.is_running():
+            print("squishd already running", file=sys.stderr)
+            return 1
+        print(f"squishd listening on {d.sock_path()}", file=sys.stderr)
+        d.Daemon(default_model=_model(a)).serve_forever()
+        return 0
+    if not d.is_running():
+        print("squishd is not running", file=sys.stderr)
+        return 1
+    cmd = {"status": "status", "ping": "ping", "stop": "stop", "reload": "reload"}[a.action]
+    req = {"_cmd": cmd}
+    if a.model:
+        req["model"] = a.model
+    print(json.dumps(d.request(req), indent=2))
+    return 0
+
+
+def build_parser() -> argparse.ArgumentParser:
+    ap = argparse.ArgumentParser(prog="squish", description="B200-native quantized LLM inference server")
+    ap.add_argument("--version", action="version", version=f"squish-b200 {__version__}")
+    sub = ap.add_subparsers(dest="cmd")
+
+    for name in ("serve", "run"):
+        p = sub.add_parser(name)
+        _engine_args(p)
+        p.add_argument("--host", default=None)
+        p.add_argument("--port", type=int, default=None)
+        p.add_argument("--api-key", default=None)
+        if name == "run":
+            p.add_argument("text", nargs="*")
+            p.add_argument("--max-tokens", type=int, default=256)
+            p.add_argument("--temperature", type=float, default=0.0)
+            p.add_argument("--top-p", type=float, default=1.0)
+        p.set_defaults(fn=cmd_serve if name == "serve" else cmd_run)
+
+    p = sub.add_parser("compress")
+    p.add_argument("source", nargs="?", default=None)
+    p.add_argument("-o", "--output", default=None)
+    p.add_argument("--format", default="int4", choices=["int4", "int8", "nf4", "int3", "int2", "aqlm", "none"])
+    p.add_argument("--group-size", type=int, default=64)
+    p.add_argument("--mse", action="store_true", help="MSE-optimal clipping search (INT4)")
+    p.add_argument("--random-init", default=None, metavar="PRESET")
+    p.add_argument("--delete-source", action="store_true")
+    p.add_argument("--device", default=None)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--kv-dtype", default="int4")
+    p.set_defaults(fn=cmd_compress)
+
+    p = sub.add_parser("convert")
+    p.add_argument("source")
+    p.add_argument("dest")
+    p.add_argument("--to", default="squizd", choices=["squizd", "npy-dir"])
+    p.add_argument("--group-size", type=int, default=64)
+    p.set_defaults(fn=cmd_convert)
+
+    sub.add_parser("models").set_defaults(fn=cmd_models)
+    sub.add_parser("catalog").set_defaults(fn=cmd_catalog)
+    p = sub.add_parser("pull")
+    p.add_argument("name")
+    p.add_argument("--device", default=None)
+    p.add_argument("--seed", type=int, default=0)
+    p.set_defaults(fn=cmd_pull)
+
+    p = sub.add_parser("bench")
+    _engine_args(p)
+    p.add_argument("--concurrency", type=int, nargs="+", default=[1, 8, 32, 64])
+    p.add_argument("--requests", type=int, default=64)
+    p.add_argument("--prompt-min", type=int, default=128)
+    p.add_argument("--prompt-max", type=int, default=2048)
+    p.add_argument("--max-tokens", type=int, default=256)
+    p.set_defaults(fn=cmd_bench)
+
+    sub.add_parser("doctor").set_defaults(fn=cmd_doctor)
+    p = sub.add_parser("config")
+    p.add_argument("action", choices=["show", "get", "set", "reset", "path"], nargs="?", default="show")
+    p.add_argument("key", nargs="?")
+    p.add_argument("value", nargs="?")
+    p.set_defaults(fn=cmd_config)
+    p = sub.add_parser("daemon")
+    p.add_argument("action", choices=["start", "stop", "status", "ping", "reload"], nargs="?", default="status")
+    p.add_argument("--model", default=None)
+    p.set_defaults(fn=cmd_daemon)
+    sub.add_parser("version").set_defaults(fn=lambda a: print(f"squish-b200 {__version__}") or 0)
+    return ap
+
+
+def main(argv: list[str] | None = None) -> int:
+    ap = build_parser()
+    a = ap.parse_args(argv)
+    if not getattr(a, "fn", None):
+        ap.print_help()
+        return 0
+    return int(a.fn(a) or 0)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
