@@ -168,6 +168,97 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, 
   CUDA_OK(sq::w4a16_gemm_launch(xmap, p, bn, nt, cur_stream()));
 }
 
+// Grouped (mixture-of-experts) INT4 GEMM over expert-sorted, tile-padded rows of x.
+void w4a16_grouped_gemm(torch::Tensor x, torch::Tensor wq, int64_t N, int64_t K, int64_t group, torch::Tensor y,
+                        int64_t epilogue, torch::Tensor tile_expert, torch::Tensor num_tiles, int64_t bn,
+                        torch::Tensor ws, torch::Tensor counters, torch::Tensor status) {
+  CHECK_CUDA(x);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(y, torch::kBFloat16);
+  CHECK_DT(tile_expert, torch::kInt32);
+  CHECK_DT(num_tiles, torch::kInt32);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(1) == K, "x must be [rows, K]");
+  TORCH_CHECK(wq.dim() == 2, "wq must be [experts, words per expert]");
+  TORCH_CHECK(bn == 16 || bn == 32 || bn == 64 || bn == 128, "bn must be 16/32/64/128");
+  const int64_t M = x.size(0);
+  TORCH_CHECK(M % bn == 0 && tile_expert.numel() >= M / bn, "rows must be a multiple of bn, one expert per tile");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16) == 0,
+              "x rows must be 16-byte aligned");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard g(x.device());
+  sq::W4A16Params p{};
+  p.wq = ptr<uint32_t>(wq);
+  p.sz = p.wq;
+  p.y = ptr<__nv_bfloat16>(y);
+  p.ws = ptr<float>(ws);
+  p.counters = ptr<int>(counters);
+  p.status = ptr<int>(status);
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.ldy = (int)y.stride(0);
+  p.kb_total = (int)((K + 63) / 64);
+  p.splits = 1;
+  p.kb_per_split = p.kb_total;
+  p.gpk = group >= 64 ? 1 : (int)(64 / group);
+  p.epilogue = (int)epilogue;
+  p.tile_expert = ptr<int>(tile_expert);
+  p.num_tiles = ptr<int>(num_tiles);
+  p.expert_stride = (long long)wq.stride(0) * wq.element_size();
+  TORCH_CHECK(p.expert_stride % 16 == 0, "expert stride must be 16-byte aligned");
+  const CUtensorMap xmap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), (int)bn);
+  CUDA_OK(sq::w4a16_gemm_launch(xmap, p, (int)bn, 1, cur_stream()));
+}
+
+void moe_route(torch::Tensor logits, int64_t K, bool renorm, torch::Tensor topk_ids, torch::Tensor topk_w) {
+  CHECK_CUDA(logits);
+  CHECK_DT(logits, torch::kBFloat16);
+  CHECK_DT(topk_ids, torch::kInt32);
+  CHECK_DT(topk_w, torch::kFloat32);
+  TORCH_CHECK(logits.stride(1) == 1, "logits must have unit column stride");
+  const c10::cuda::CUDAGuard g(logits.device());
+  CUDA_OK(sq::moe_route_launch(ptr<__nv_bfloat16>(logits), (int)logits.stride(0), (int)logits.size(0),
+                               (int)logits.size(1), (int)K, renorm, ptr<int>(topk_ids), ptr<float>(topk_w),
+                               cur_stream()));
+}
+
+void moe_align(torch::Tensor ids, int64_t E, int64_t bn, torch::Tensor sorted_slot, torch::Tensor slot_pos,
+               torch::Tensor tile_expert, torch::Tensor num_tiles, c10::optional<torch::Tensor> counts) {
+  CHECK_CUDA(ids);
+  CHECK_DT(ids, torch::kInt32);
+  CHECK_CONTIG(ids);
+  const int64_t TK = ids.numel();
+  TORCH_CHECK(sorted_slot.numel() >= TK + E * (bn - 1), "sorted_slot too small for the padded layout");
+  TORCH_CHECK(tile_expert.numel() * bn >= sorted_slot.numel(), "tile_expert too small");
+  const c10::cuda::CUDAGuard g(ids.device());
+  CUDA_OK(sq::moe_align_launch(ptr<int>(ids), (int)TK, (int)E, (int)bn, (int)tile_expert.numel(),
+                               ptr<int>(sorted_slot), ptr<int>(slot_pos), ptr<int>(tile_expert), ptr<int>(num_tiles),
+                               optr<int>(counts), cur_stream()));
+}
+
+void moe_gather(torch::Tensor x, torch::Tensor sorted_slot, torch::Tensor num_tiles, int64_t bn, int64_t K,
+                torch::Tensor xs) {
+  CHECK_CUDA(x);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(xs, torch::kBFloat16);
+  TORCH_CHECK(x.stride(1) == 1 && xs.stride(1) == 1 && x.size(1) == xs.size(1), "bad gather shapes");
+  const c10::cuda::CUDAGuard g(x.device());
+  CUDA_OK(sq::moe_gather_launch(ptr<__nv_bfloat16>(x), (int)x.stride(0), ptr<int>(sorted_slot), ptr<int>(num_tiles),
+                                (int)std::min<int64_t>(xs.size(0), sorted_slot.numel()), (int)bn, (int)K,
+                                (int)x.size(1), ptr<__nv_bfloat16>(xs), (int)xs.stride(0), cur_stream()));
+}
+
+void moe_combine(torch::Tensor ys, torch::Tensor slot_pos, torch::Tensor topk_w, int64_t K, torch::Tensor h) {
+  CHECK_CUDA(ys);
+  CHECK_DT(ys, torch::kBFloat16);
+  CHECK_DT(h, torch::kBFloat16);
+  TORCH_CHECK(ys.stride(1) == 1 && h.stride(1) == 1 && ys.size(1) == h.size(1), "bad combine shapes");
+  const c10::cuda::CUDAGuard g(h.device());
+  CUDA_OK(sq::moe_combine_launch(ptr<__nv_bfloat16>(ys), (int)ys.stride(0), ptr<int>(slot_pos), ptr<float>(topk_w),
+                                 (int)h.size(0), (int)K, (int)h.size(1), ptr<__nv_bfloat16>(h), (int)h.stride(0),
+                                 cur_stream()));
+}
+
 // ------------------------------------------------------------------ norm / rope / attention
 void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> row_idx, double eps) {
   CHECK_CUDA(x);
@@ -342,6 +433,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("repack_int4", &repack_int4);
   m.def("gemm_plan", &gemm_plan);
   m.def("w4a16_gemm", &w4a16_gemm);
+  m.def("w4a16_grouped_gemm", &w4a16_grouped_gemm);
+  m.def("moe_route", &moe_route);
+  m.def("moe_align", &moe_align);
+  m.def("moe_gather", &moe_gather);
+  m.def("moe_combine", &moe_combine);
   m.def("rmsnorm", &rmsnorm);
   m.def("rope_kv_write", &rope_kv_write);
   m.def("paged_decode_attention", &paged_decode_attention);

@@ -79,4 +79,13 @@ cudaError_t sampler_launch(const SamplerParams& p, float* work, cudaStream_t s);
 cudaError_t quantize_int4_asym_launch(const void* x, bool bf16, uint8_t* packed, float* scales, float* offsets,
                                       int rows, int cols, int group, int n_clip, cudaStream_t s);
 
+cudaError_t moe_route_launch(const __nv_bfloat16* logits, int ld, int T, int E, int K, bool renorm, int* topk_ids,
+                             float* topk_w, cudaStream_t s);
+cudaError_t moe_align_launch(const int* ids, int TK, int E, int bn, int max_tiles, int* sorted_slot, int* slot_pos,
+                             int* tile_expert, int* num_tiles, int* counts, cudaStream_t s);
+cudaError_t moe_gather_launch(const __nv_bfloat16* x, int ldx, const int* sorted_slot, const int* num_tiles,
+                              int max_rows, int bn, int K, int H, __nv_bfloat16* xs, int ldxs, cudaStream_t s);
+cudaError_t moe_combine_launch(const __nv_bfloat16* ys, int ldys, const int* slot_pos, const float* topk_w, int T,
+                               int K, int H, __nv_bfloat16* h, int ldh, cudaStream_t s);
+
 }  // namespace sq

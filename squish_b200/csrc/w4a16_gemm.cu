@@ -125,6 +125,11 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     w4a16_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const W4A16Params p) {
   constexpr int BN = C::BN;
   constexpr int NT = C::NT;
+  const uint8_t* wbase = reinterpret_cast<const uint8_t*>(p.wq);
+  if (p.tile_expert != nullptr) {  // grouped mode: whole CTA leaves before any setup
+    if ((int)blockIdx.y >= __ldg(p.num_tiles)) return;
+    wbase += (size_t)__ldg(p.tile_expert + blockIdx.y) * (size_t)p.expert_stride;
+  }
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -198,7 +203,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
           const size_t tile = ((size_t)nblk * NT + t) * p.kb_total + kb;
-          bulk_g2s_hint(dst + t * tbytes, reinterpret_cast<const uint8_t*>(p.wq) + tile * tbytes, (uint32_t)tbytes,
+          bulk_g2s_hint(dst + t * tbytes, wbase + tile * tbytes, (uint32_t)tbytes,
                         &w_full[r.s], pol);
         }
         trace_mark(str, 0, i);

@@ -26,6 +26,12 @@ struct W4A16Params {
   int epilogue;                   // EPI_PLAIN | EPI_SILU_MUL
   int ring_w, ring_x, ring_a;     // set by the launcher
   unsigned long long* trace;      // optional: per-k-block role timestamps of CTA (0,0,0), 16 x 64 entries
+  // Grouped (mixture-of-experts) mode, when tile_expert != nullptr: the rows of X are sorted
+  // by expert and padded so every BN-row token tile belongs to one expert; token tile y uses
+  // the weights at wq + tile_expert[y] * expert_stride bytes, and tiles y >= *num_tiles exit.
+  const int* tile_expert;
+  const int* num_tiles;
+  long long expert_stride;
 };
 
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s);

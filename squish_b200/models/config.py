@@ -95,6 +95,10 @@ def _register(cfg: ModelConfig, q: QuantConfig) -> None:
 _register(ModelConfig("tiny-llama", "llama", 32000, 256, 4, 8, 2, 32, 688, 1e-6, 10000.0, tie_embeddings=True,
                       max_position=2048),
           QuantConfig(4, 32, True, "int4", 32, 16))
+# Tiny Qwen3-MoE (tests): 16 experts, top-4, expert FFN 128.
+_register(ModelConfig("tiny-moe", "qwen3_moe", 1024, 256, 2, 8, 2, 64, 512, 1e-6, 1e6, qk_norm=True, num_experts=16,
+                      num_experts_per_tok=4, moe_intermediate_size=128, max_position=2048),
+          QuantConfig(4, 64, True, "int4", 32, 16))
 # Qwen2.5-7B shape: INT4 g64 weights (bf16 scales), INT4 KV in 16-token pages.
 _register(ModelConfig("qwen2.5-7b", "qwen2", 152064, 3584, 28, 28, 4, 128, 18944, 1e-6, 1e6, qkv_bias=True,
                       max_position=32768, bos_token_id=151643, eos_token_id=151645),

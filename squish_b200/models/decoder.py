@@ -174,9 +174,11 @@ class CudaRunner:
                 lw.q_norm = _dense(t[p + "self_attn.q_norm.weight"], dev)
                 lw.k_norm = _dense(t[p + "self_attn.k_norm.weight"], dev)
             if cfg.is_moe:
-                from .moe import MoELayer
+                from .moe import MoELayer, MoEScratch
 
-                lw.moe = MoELayer.from_checkpoint(ck, i, dev)
+                if i == 0:
+                    self.moe_scratch = MoEScratch(cfg, max_num_tokens, dev)
+                lw.moe = MoELayer.from_checkpoint(ck, i, dev, self.moe_scratch)
             else:
                 lw.gate_up = _to_int4(_interleave_gate_up(_as_q4a(t[p + "mlp.gate_proj.weight"], g),
                                                           _as_q4a(t[p + "mlp.up_proj.weight"], g)), dev)

@@ -194,3 +194,66 @@ def sample(logits, out_tokens, temperature=None, top_p=None, top_k=None, min_p=N
                     out_tokens, out_logprob, work)
     _count()
     return out_tokens
+
+
+# ----------------------------------------------------------------------------- mixture of experts
+def moe_tile(tokens: int, top_k: int, experts: int) -> int:
+    """Token tile of the grouped GEMM for ``tokens`` routed tokens: the smallest of 16/32/64/128
+    that covers the mean rows per expert (padding per expert is at most one tile)."""
+    avg = tokens * top_k / max(experts, 1)
+    for bn in (16, 32, 64):
+        if avg <= bn:
+            return bn
+    return 128
+
+
+def moe_padded_rows(tokens: int, top_k: int, experts: int, bn: int) -> int:
+    rows = tokens * top_k + experts * (bn - 1)
+    return (rows + bn - 1) // bn * bn
+
+
+def moe_route(logits: torch.Tensor, top_k: int, renorm: bool, ids: torch.Tensor, weights: torch.Tensor) -> None:
+    native().moe_route(logits, top_k, renorm, ids, weights)
+    _count()
+
+
+def moe_align(ids: torch.Tensor, experts: int, bn: int, sorted_slot: torch.Tensor, slot_pos: torch.Tensor,
+              tile_expert: torch.Tensor, num_tiles: torch.Tensor, counts: torch.Tensor | None = None) -> None:
+    native().moe_align(ids, experts, bn, sorted_slot, slot_pos, tile_expert, num_tiles, counts)
+    _count()
+
+
+def moe_gather(x: torch.Tensor, sorted_slot: torch.Tensor, num_tiles: torch.Tensor, bn: int, top_k: int,
+               xs: torch.Tensor) -> None:
+    native().moe_gather(x, sorted_slot, num_tiles, bn, top_k, xs)
+    _count()
+
+
+def moe_combine(ys: torch.Tensor, slot_pos: torch.Tensor, weights: torch.Tensor, top_k: int, h: torch.Tensor) -> None:
+    native().moe_combine(ys, slot_pos, weights, top_k, h)
+    _count()
+
+
+@dataclass
+class GroupedInt4Weight:
+    """Per-expert INT4 weights stacked in the tile-major layout: wq [E, words per expert]."""
+
+    wq: torch.Tensor
+    n: int
+    k: int
+    group: int
+
+
+def stack_int4_experts(ws: list[Int4Weight]) -> GroupedInt4Weight:
+    wq = torch.stack([w.wq.reshape(-1) for w in ws]).contiguous()
+    return GroupedInt4Weight(wq=wq, n=ws[0].n, k=ws[0].k, group=ws[0].group)
+
+
+def w4a16_grouped_linear(xs: torch.Tensor, w: GroupedInt4Weight, out: torch.Tensor, tile_expert: torch.Tensor,
+                         num_tiles: torch.Tensor, bn: int, silu_mul: bool = False,
+                         ws: Workspace | None = None) -> torch.Tensor:
+    ws = ws or workspace(xs.device)
+    native().w4a16_grouped_gemm(xs, w.wq, w.n, w.k, w.group, out, EPI_SILU_MUL if silu_mul else EPI_PLAIN,
+                                tile_expert, num_tiles, bn, ws.gemm_ws, ws.gemm_counters, ws.status)
+    _count()
+    return out
