@@ -295,6 +295,11 @@ __global__ void __launch_bounds__(256) prefill_kernel(const AttnParams p) {
   __nv_bfloat16* Qs = Vs + PK * LD + warp * PQ * LD;
   const int hq = hq0 + warp;
   const bool active = warp < nheads;
+  __shared__ int tmask[PQ];
+  const int cstart = ctx - qlen;  // absolute position of chunk token 0
+  if (threadIdx.x < PQ)
+    tmask[threadIdx.x] = (p.tree_mask != nullptr && (int)threadIdx.x < qn)
+                             ? p.tree_mask[p.q_start[b] + q0 + threadIdx.x] : 0;
 
   // stage Q rows of this warp's head
   if (active) {
@@ -400,6 +405,10 @@ __global__ void __launch_bounds__(256) prefill_kernel(const AttnParams p) {
           const int key = tok0 + nt * 8 + 2 * t4 + (e & 1);
           float v = s[mt][nt][e] * scale;
           if (key > pos0 + qrow || qrow >= qn) v = -INFINITY;
+          else if (key >= cstart) {
+            const int tm = tmask[qrow];
+            if (tm != 0 && !((tm >> (key - cstart)) & 1)) v = -INFINITY;
+          }
           s[mt][nt][e] = v;
           mx[e >> 1] = fmaxf(mx[e >> 1], v);
         }

@@ -259,6 +259,57 @@ void moe_combine(torch::Tensor ys, torch::Tensor slot_pos, torch::Tensor topk_w,
                                  cur_stream()));
 }
 
+// ------------------------------------------------------------------ speculative decoding
+void tree_verify(torch::Tensor logits, c10::optional<torch::Tensor> draft_logits, torch::Tensor meta,
+                 torch::Tensor temperature, torch::Tensor step, int64_t seed, torch::Tensor scratch, torch::Tensor out) {
+  CHECK_CUDA(logits);
+  CHECK_DT(logits, torch::kBFloat16);
+  CHECK_DT(meta, torch::kInt32);
+  CHECK_DT(out, torch::kInt32);
+  CHECK_DT(scratch, torch::kFloat32);
+  TORCH_CHECK(logits.stride(1) == 1, "logits must have unit column stride");
+  const int64_t G = meta.size(0);
+  TORCH_CHECK(meta.size(1) == sq::kTreeMetaInts && out.size(1) == 2 + sq::kMaxTreeNodes, "bad tree meta/out shape");
+  TORCH_CHECK(scratch.numel() >= G * logits.size(1), "scratch too small");
+  const c10::cuda::CUDAGuard g(logits.device());
+  sq::TreeVerifyParams p{};
+  p.logits = ptr<__nv_bfloat16>(logits);
+  p.ld = (int)logits.stride(0);
+  p.V = (int)logits.size(1);
+  if (draft_logits.has_value() && draft_logits->defined()) {
+    CHECK_DT((*draft_logits), torch::kBFloat16);
+    TORCH_CHECK(draft_logits->size(1) == logits.size(1), "draft vocabulary differs from the target's");
+    p.draft_logits = ptr<__nv_bfloat16>(*draft_logits);
+    p.ld_draft = (int)draft_logits->stride(0);
+  }
+  p.meta = ptr<int>(meta);
+  p.temperature = ptr<float>(temperature);
+  p.step = ptr<int>(step);
+  p.seed = (unsigned long long)seed;
+  p.scratch = ptr<float>(scratch);
+  p.out = ptr<int>(out);
+  CUDA_OK(sq::tree_verify_launch(p, (int)G, cur_stream()));
+}
+
+void kv_compact(torch::Tensor layer_ptrs, torch::Tensor src, torch::Tensor dst, int64_t Hkv, int64_t page_size,
+                int64_t kc_bytes, int64_t vc_bytes, int64_t ks_n, int64_t vs_n) {
+  CHECK_CUDA(layer_ptrs);
+  TORCH_CHECK(layer_ptrs.scalar_type() == torch::kInt64 && layer_ptrs.size(1) == 4, "layer_ptrs must be [L, 4] int64");
+  const c10::cuda::CUDAGuard g(layer_ptrs.device());
+  sq::KvCompactParams p{};
+  p.layers = reinterpret_cast<const sq::KvLayerPtrs*>(layer_ptrs.data_ptr());
+  p.src = ptr<int>(src);
+  p.dst = ptr<int>(dst);
+  p.n_pairs = (int)src.numel();
+  p.Hkv = (int)Hkv;
+  p.page_size = (int)page_size;
+  p.kc_bytes = (int)kc_bytes;
+  p.vc_bytes = (int)vc_bytes;
+  p.ks_n = (int)ks_n;
+  p.vs_n = (int)vs_n;
+  CUDA_OK(sq::kv_compact_launch(p, (int)layer_ptrs.size(0), cur_stream()));
+}
+
 // ------------------------------------------------------------------ norm / rope / attention
 void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> row_idx, double eps) {
   CHECK_CUDA(x);
@@ -366,10 +417,12 @@ void paged_prefill_attention(torch::Tensor q, torch::Tensor k_codes, torch::Tens
                              torch::Tensor v_scales, torch::Tensor block_tables, torch::Tensor tile_seq,
                              torch::Tensor tile_q0, torch::Tensor q_start, torch::Tensor q_len, torch::Tensor ctx_len,
                              int64_t n_tiles, torch::Tensor out, int64_t Hq, int64_t Hkv, int64_t D,
-                             int64_t page_size, int64_t group, int64_t fmt_k, int64_t fmt_v, double sm_scale) {
+                             int64_t page_size, int64_t group, int64_t fmt_k, int64_t fmt_v, double sm_scale,
+                             c10::optional<torch::Tensor> tree_mask) {
   const c10::cuda::CUDAGuard g(q.device());
   auto p = attn_common(q, k_codes, k_scales, v_codes, v_scales, block_tables, out, Hq, Hkv, D, page_size, group,
                        fmt_k, fmt_v, sm_scale);
+  p.tree_mask = optr<int>(tree_mask);
   p.tile_seq = ptr<int>(tile_seq);
   p.tile_q0 = ptr<int>(tile_q0);
   p.q_start = ptr<int>(q_start);
@@ -435,6 +488,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w4a16_gemm", &w4a16_gemm);
   m.def("w4a16_grouped_gemm", &w4a16_grouped_gemm);
   m.def("moe_route", &moe_route);
+  m.def("tree_verify", &tree_verify);
+  m.def("kv_compact", &kv_compact);
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);

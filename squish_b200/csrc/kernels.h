@@ -50,6 +50,9 @@ struct AttnParams {
   const int* q_len;         // [B]
   const int* ctx_len;       // [B] kv length after this chunk
   int n_tiles;
+  // optional token-tree masks (speculative verification), one per query row: bit j set =
+  // the row may attend chunk token j; 0 = plain causal. A tree chunk is at most 32 tokens.
+  const int* tree_mask;
 };
 
 cudaError_t rope_kv_write_launch(const RopeKvParams& p, int T, cudaStream_t s);
@@ -78,6 +81,38 @@ cudaError_t sampler_launch(const SamplerParams& p, float* work, cudaStream_t s);
 
 cudaError_t quantize_int4_asym_launch(const void* x, bool bf16, uint8_t* packed, float* scales, float* offsets,
                                       int rows, int cols, int group, int n_clip, cudaStream_t s);
+
+// ---------------------------------------------------------------- speculative decoding
+constexpr int kMaxTreeNodes = 32;
+constexpr int kTreeMetaInts = 2 + 3 * kMaxTreeNodes;  // row0, n, parent[], token[], qrow[]
+struct TreeVerifyParams {
+  const __nv_bfloat16* logits;        // [rows, ld] target logits, node i of group g at row meta.row0 + i
+  int ld, V;
+  const __nv_bfloat16* draft_logits;  // [rows_q, ld_draft] or nullptr (deterministic drafts only)
+  int ld_draft;
+  const int* meta;                    // [G, kTreeMetaInts]
+  const float* temperature;           // [G]
+  const int* step;                    // [G]
+  unsigned long long seed;
+  float* scratch;                     // [G, V] residual distribution
+  int* out;                           // [G, 2 + kMaxTreeNodes]: n_accepted, final token, accepted nodes
+};
+struct KvLayerPtrs {
+  uint8_t* kc;
+  __half* ks;
+  uint8_t* vc;
+  __half* vs;
+};
+struct KvCompactParams {
+  const KvLayerPtrs* layers;  // [L] device array
+  const int* src;             // [n] absolute cache slots (page * page_size + offset)
+  const int* dst;
+  int n_pairs;
+  int Hkv, page_size;
+  int kc_bytes, vc_bytes, ks_n, vs_n;  // per (token, head) row
+};
+cudaError_t tree_verify_launch(const TreeVerifyParams& p, int groups, cudaStream_t s);
+cudaError_t kv_compact_launch(const KvCompactParams& p, int layers, cudaStream_t s);
 
 cudaError_t moe_route_launch(const __nv_bfloat16* logits, int ld, int T, int E, int K, bool renorm, int* topk_ids,
                              float* topk_w, cudaStream_t s);

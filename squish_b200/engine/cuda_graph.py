@@ -12,6 +12,8 @@ this is the CUDA counterpart.
 """
 from __future__ import annotations
 
+import gc
+
 import numpy as np
 import torch
 
@@ -74,10 +76,19 @@ class DecodeGraphs:
         torch.cuda.current_stream(r.device).wait_stream(s)
         torch.cuda.synchronize(r.device)
         g = torch.cuda.CUDAGraph()
+        r.ws.frozen = True
         before = LAUNCHES[0]
-        with torch.cuda.graph(g, pool=self.pool):
-            logits = r.forward(st, m)
-            toks = r.sample_full(st, m, logits)
+        # A cyclic garbage collection during capture could destroy an unreachable engine's
+        # graphs (cudaGraphExecDestroy), which is not permitted while a stream captures and
+        # invalidates this capture: collect first, keep the collector off until capture ends.
+        gc.collect()
+        gc.disable()
+        try:
+            with torch.cuda.graph(g, pool=self.pool):
+                logits = r.forward(st, m)
+                toks = r.sample_full(st, m, logits)
+        finally:
+            gc.enable()
         n_kernels = LAUNCHES[0] - before
         if self.pool is None:
             self.pool = g.pool()

@@ -26,7 +26,8 @@ from ..models.decoder import StepInputs, prefill_tiles
 from ..models.weights import Checkpoint, random_checkpoint
 from .request import Request, RequestOutput, Status
 from .sampling import SamplingParams
-from .scheduler import Schedule, Scheduler
+from .scheduler import Schedule, ScheduledEntry, Scheduler
+from .speculative import TREE_META_INTS, _Guard, make_proposer, spec_eligible
 
 
 @dataclass
@@ -41,6 +42,7 @@ class EngineConfig:
     chunk_align: int = 0
     hist_window: int = 64
     seed: int = 0
+    spec: object | None = None  # speculative.SpecConfig: prompt lookup / draft model / Jacobi
 
 
 @dataclass
@@ -71,6 +73,9 @@ class LLMEngine:
         self.max_pages = (ecfg.max_model_len + qcfg.page_size - 1) // qcfg.page_size
         self.graphs = None
         self.hidden_states: dict[str, np.ndarray] = {}  # rid -> final hidden of the last prompt token
+        self.proposer = None
+        self.guard = None
+        self.spec_stats = {"verifies": 0, "drafted": 0, "accepted": 0, "emitted": 0}
 
     # ------------------------------------------------------------------ construction
     @staticmethod
@@ -93,9 +98,10 @@ class LLMEngine:
             from ..models.decoder import CudaRunner
 
             # weights first, then size the page pool from what is left
+            spec_rows = ecfg.max_num_seqs * ecfg.spec.max_nodes if ecfg.spec is not None else 0
             runner = CudaRunner(ck, dev, num_pages=1, max_num_tokens=ecfg.max_num_batched_tokens,
                                 max_num_seqs=ecfg.max_num_seqs, max_model_len=ecfg.max_model_len,
-                                free_checkpoint=True)
+                                free_checkpoint=True, spec_rows=spec_rows)
             del runner.pools
             torch.cuda.empty_cache()
             num_pages = cls.plan_pages(ck.config, ck.quant, ecfg, dev)
@@ -112,6 +118,9 @@ class LLMEngine:
             from .cuda_graph import DecodeGraphs
 
             eng.graphs = DecodeGraphs(eng)
+        if ecfg.spec is not None:
+            eng.proposer = make_proposer(ecfg.spec, eng)
+            eng.guard = _Guard(ecfg.spec.miss_limit, ecfg.spec.cooldown) if ecfg.spec.adaptive else None
         return eng
 
     @classmethod
@@ -159,16 +168,31 @@ class LLMEngine:
             maxp = self.max_pages
         bt = np.zeros((nb, max(maxp, 1)), dtype=np.int32)
         rows, samp = [], []
+        trees = [e for e in entries if e.tree is not None]
+        tmask = np.zeros(T, dtype=np.int32) if trees else None
+        vrows, vmeta, vreqs = [], [], []
         off = 0
         for i, e in enumerate(entries):
             r = e.req
+            pg = np.asarray(r.pages, dtype=np.int32)
+            bt[i, :len(r.pages)] = pg
+            if e.tree is not None:
+                tr = e.tree
+                ids[off:off + e.n] = tr.tokens
+                pos[off:off + e.n] = e.start + np.asarray(tr.depth, dtype=np.int32)
+                p = np.arange(e.start, e.start + e.n, dtype=np.int32)
+                slots[off:off + e.n] = pg[p // ps] * ps + p % ps
+                tmask[off:off + e.n] = tr.masks()
+                vmeta.append(tr.meta_row(len(vrows)))
+                vrows.extend(range(off, off + e.n))
+                vreqs.append(r)
+                off += e.n
+                continue
             toks = r.tokens
             ids[off:off + e.n] = toks[e.start:e.start + e.n]
             p = np.arange(e.start, e.start + e.n, dtype=np.int32)
             pos[off:off + e.n] = p
-            pg = np.asarray(r.pages, dtype=np.int32)
             slots[off:off + e.n] = pg[p // ps] * ps + p % ps
-            bt[i, :len(r.pages)] = pg
             if e.sample:
                 rows.append(off + e.n - 1)
                 samp.append(r)
@@ -187,9 +211,13 @@ class LLMEngine:
         topk = np.asarray([r.params.top_k for r in samp], dtype=np.int32)
         minp = np.asarray([r.params.min_p for r in samp], dtype=np.float32)
         rep = np.asarray([r.params.repetition_penalty for r in samp], dtype=np.float32)
-        step = np.asarray([r.rng_step + (zlib.crc32(r.rid.encode()) & 0xFFFF) * 65536 for r in samp],
-                          dtype=np.int64)
-        step = (step & 0x7FFFFFFF).astype(np.int32)
+
+        def rng_steps(reqs):
+            st_ = np.asarray([r.rng_step + (zlib.crc32(r.rid.encode()) & 0xFFFF) * 65536 for r in reqs],
+                             dtype=np.int64)
+            return (st_ & 0x7FFFFFFF).astype(np.int32)
+
+        step = rng_steps(samp)
         hist = None
         if B and (rep != 1.0).any():
             hw = self.ecfg.hist_window
@@ -204,18 +232,70 @@ class LLMEngine:
             for i, r in enumerate(samp):
                 if r.params.grammar is not None:
                     mask[i] = np.asarray(r.params.grammar.allowed_mask(), dtype=np.uint32).view(np.int32)[:words]
-        st = StepInputs(ids, pos, slots, nd, dl, qs, ql, ctx, tseq, tq0, bt, np.asarray(rows, dtype=np.int32), temp,
-                        topp, topk, minp, rep, step, hist, self.ecfg.seed, int(dl.max()) if nd else 0)
+        st = StepInputs(ids, pos, slots, nd, dl, qs, ql, ctx, tseq, tq0, bt,
+                        np.asarray(rows + vrows, dtype=np.int32), temp, topp, topk, minp, rep, step, hist,
+                        self.ecfg.seed, int(dl.max()) if nd else 0)
         st.allow_mask = mask
+        if trees:
+            st.tree_mask = tmask
+            st.verify_meta = np.stack(vmeta).astype(np.int32)
+            st.verify_temp = np.asarray([r.params.temperature for r in vreqs], dtype=np.float32)
+            st.verify_step = rng_steps(vreqs)
+            st.verify_preds = bool(getattr(self.proposer, "wants_preds", False))
+            st.draft_logits = getattr(self.proposer, "qbuf", None)
         return st, samp
+
+    def run_entries(self, decode: list[ScheduledEntry], prefill: list[ScheduledEntry]) -> np.ndarray:
+        """Run one forward over explicit entries (used by a draft model's proposer); returns the
+        sampled token of every sampling entry; logits stay in ``runner.logits``."""
+        st, _ = self.build_inputs(Schedule(decode, prefill, []))
+        if self.graphs is not None and not prefill and self.graphs.can_run(st):
+            return self.graphs.run(st)
+        return self.runner.execute(st)
+
+    def _attach_drafts(self, sched: Schedule) -> None:
+        """Turn decode entries with a draft tree into verification chunks (prefill group)."""
+        sc = self.ecfg.spec
+        cands = [e.req for e in sched.decode if spec_eligible(e.req.params) and
+                 (self.guard is None or self.guard.allow(e.req.rid))]
+        if not cands:
+            return
+        trees = self.proposer.propose(cands)
+        if not trees:
+            return
+        budget = min(self.ecfg.max_num_batched_tokens, getattr(self.runner, "max_num_tokens", 1 << 30))
+        used = sum(e.n for e in sched.decode + sched.prefill)
+        cap_rows = getattr(self.runner, "spec_rows", 1 << 30)
+        rows = 0
+        verify = []
+        for e in list(sched.decode):
+            t = trees.get(e.req.rid)
+            if t is None or t.size < 2:
+                continue
+            n = min(t.size, sc.max_nodes)
+            if used + n - 1 > budget or rows + n > cap_rows:
+                break
+            if not self.scheduler._ensure_pages(e.req, e.start + n):
+                continue
+            if n < t.size:  # parents precede children, so a prefix of the nodes is a tree
+                t = type(t)(t.tokens[:n], t.parent[:n], t.qrow[:n])
+            e.n, e.tree = n, t
+            sched.decode.remove(e)
+            verify.append(e)
+            used += n - 1
+            rows += n
+        sched.prefill[:0] = verify
 
     def step(self) -> list[RequestOutput]:
         sched = self.scheduler.schedule()
         self.stats.preemptions += len(sched.preempted)
         if sched.empty:
             return []
+        if self.proposer is not None and sched.decode:
+            self._attach_drafts(sched)
         st, samp = self.build_inputs(sched)
-        if self.graphs is not None and not sched.prefill and st.allow_mask is None and self.graphs.can_run(st):
+        if (self.graphs is not None and not sched.prefill and st.allow_mask is None and st.num_verify == 0
+                and self.graphs.can_run(st)):
             toks = self.graphs.run(st)
             self.stats.graph_steps += 1
         else:
@@ -224,21 +304,32 @@ class LLMEngine:
         self.stats.scheduled_tokens += st.num_tokens
         self.stats.steps += 1
         self.stats.h2d_bytes += st.h2d_bytes()
-        self.stats.d2h_bytes += 4 * len(samp)
+        self.stats.d2h_bytes += 4 * len(samp) + 4 * st.num_verify * (2 + 32)
         now = time.perf_counter()
         outs: list[RequestOutput] = []
         # advance computed counters, publish full blocks
         for e in sched.decode + sched.prefill:
             r = e.req
-            r.num_computed = e.start + e.n
-            if not e.sample:
-                self.stats.prompt_tokens += e.n
+            if e.tree is None:
+                r.num_computed = e.start + e.n
+                if not e.sample:
+                    self.stats.prompt_tokens += e.n
         want_hidden = [i for i, r in enumerate(samp) if r.params.return_hidden]
         if want_hidden:
             hid = self.runner.last_hidden
             for i in want_hidden:
                 self.hidden_states[samp[i].rid] = hid[i].float().cpu().numpy()
         for r, t in zip(samp, toks.tolist()):
+            outs.append(self._emit(r, [int(t)], now))
+        if st.num_verify:
+            outs.extend(self._apply_verify(sched, st, now))
+        return outs
+
+    def _emit(self, r: Request, new: list[int], now: float) -> RequestOutput:
+        """Append tokens to a request (stopping early at a stop condition)."""
+        got = []
+        reason = None
+        for t in new:
             if r.params.grammar is not None:
                 r.params.grammar.advance(int(t))
             if r.first_token_time is None:
@@ -248,12 +339,63 @@ class LLMEngine:
             r.output.append(int(t))
             r.rng_step += 1
             self.stats.generated_tokens += 1
-            self._publish_blocks(r)
+            got.append(int(t))
             reason = self._stop_reason(r, int(t))
             if reason:
-                self.scheduler.finish(r, reason)
-                r.finish_time = now
-            outs.append(RequestOutput(r.rid, [int(t)], reason is not None, reason, len(r.prompt), len(r.output)))
+                break
+        self._publish_blocks(r)
+        if reason:
+            self.scheduler.finish(r, reason)
+            r.finish_time = now
+            if self.proposer is not None:
+                self.proposer.forget(r.rid)
+                if self.guard is not None:
+                    self.guard.forget(r.rid)
+        return RequestOutput(r.rid, got, reason is not None, reason, len(r.prompt), len(r.output))
+
+    def _apply_verify(self, sched: Schedule, st: StepInputs, now: float) -> list[RequestOutput]:
+        res = self.runner.last_verify
+        preds = getattr(self.runner, "last_preds", None)
+        ps = self.qcfg.page_size
+        src, dst, outs = [], [], []
+        vrow = 0
+        g = 0
+        fa = self.ecfg.spec.force_accept
+        for e in sched.prefill:
+            if e.tree is None:
+                continue
+            r, tr = e.req, e.tree
+            nacc, final = int(res[g, 0]), int(res[g, 1])
+            path = [int(x) for x in res[g, 2:2 + nacc]]
+            if fa is not None:  # benchmark knob: pretend the first chain matched exactly fa drafts
+                chain, u = [], 0
+                while len(chain) < fa:
+                    kids = [c for c in range(1, tr.size) if tr.parent[c] == u]
+                    if not kids:
+                        break
+                    u = kids[0]
+                    chain.append(u)
+                path, nacc = chain, len(chain)
+            toks = [tr.tokens[c] for c in path] + [final]
+            for j, c in enumerate(path):
+                if c != j + 1:
+                    a, b = e.start + c, e.start + j + 1
+                    src.append(r.pages[a // ps] * ps + a % ps)
+                    dst.append(r.pages[b // ps] * ps + b % ps)
+            r.num_computed = e.start + nacc + 1
+            self.spec_stats["verifies"] += 1
+            self.spec_stats["drafted"] += tr.size - 1
+            self.spec_stats["accepted"] += nacc
+            self.spec_stats["emitted"] += nacc + 1
+            if self.guard is not None:
+                self.guard.record(r.rid, nacc)
+            p_ = None if preds is None else preds[vrow:vrow + tr.size]
+            self.proposer.after_verify(r, nacc, p_)
+            vrow += tr.size
+            g += 1
+            outs.append(self._emit(r, toks, now))
+        if src:
+            self.runner.kv_compact(src, dst)
         return outs
 
     def _publish_blocks(self, r: Request) -> None:

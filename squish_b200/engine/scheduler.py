@@ -34,6 +34,7 @@ class ScheduledEntry:
     start: int     # first position computed this step
     n: int         # tokens computed this step
     sample: bool   # this chunk reaches the end of the known tokens -> sample a token
+    tree: object = None  # speculative draft tree verified by this entry (n = tree size)
 
 
 @dataclass

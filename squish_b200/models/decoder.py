@@ -55,6 +55,13 @@ class StepInputs:
     max_decode_ctx: int = 0
     all_logits: bool = False       # also return the logits of every logit row (spec verify)
     allow_mask: np.ndarray | None = None  # int32 [B, ceil(V/32)] grammar bitmask (bit set = token allowed)
+    # speculative verification: logits_rows = the B sample rows, then every tree node's row
+    tree_mask: np.ndarray | None = None    # int32 [T] ancestor bits within the chunk (0 = causal)
+    verify_meta: np.ndarray | None = None  # int32 [G, TREE_META_INTS] (row0 relative to the first node row)
+    verify_temp: np.ndarray | None = None  # f32 [G]
+    verify_step: np.ndarray | None = None  # int32 [G]
+    verify_preds: bool = False             # also return the greedy token of every node row (Jacobi)
+    draft_logits: object = None            # device tensor of draft-model rows (q of the rejection test)
 
     @property
     def num_tokens(self) -> int:
@@ -63,6 +70,14 @@ class StepInputs:
     @property
     def num_prefill(self) -> int:
         return int(self.prefill_q_len.shape[0])
+
+    @property
+    def num_sample_rows(self) -> int:
+        return int(self.temperature.shape[0])
+
+    @property
+    def num_verify(self) -> int:
+        return 0 if self.verify_meta is None else int(self.verify_meta.shape[0])
 
     def h2d_bytes(self) -> int:
         n = 0
@@ -144,15 +159,17 @@ class CudaRunner:
     """Runs engine steps on one GPU with the sm_100a kernels."""
 
     def __init__(self, ck: Checkpoint, device, num_pages: int, max_num_tokens: int = 4096, max_num_seqs: int = 256,
-                 max_model_len: int = 4096, pools: KVPools | None = None, free_checkpoint: bool = False):
+                 max_model_len: int = 4096, pools: KVPools | None = None, free_checkpoint: bool = False,
+                 spec_rows: int = 0):
         self.cfg: ModelConfig = ck.config
         self.qcfg: QuantConfig = ck.quant
         self.device = torch.device(device)
         cfg, dev = self.cfg, self.device
         self.max_num_tokens = max_num_tokens
         self.max_num_seqs = max_num_seqs
+        self.spec_rows = spec_rows
         self.max_model_len = max_model_len
-        self.ws = ops.workspace(dev)
+        self.ws = ops.Workspace(dev)  # owned by this runner: its CUDA graphs capture these buffers
         self.fk, self.fv = KV_FORMATS[self.qcfg.kv_dtype]
         self.F = cfg.intermediate_size
         self.F_pad = (self.F + 63) // 64 * 64
@@ -209,17 +226,24 @@ class CudaRunner:
         f_act = self.F_pad if not cfg.is_moe else 0
         self.act = torch.empty(T, max(f_act, 8), dtype=bf, device=dev)
         B = self.max_num_seqs
-        self.xs = torch.empty(B, cfg.hidden_size, dtype=bf, device=dev)
-        self.logits = torch.empty(B, cfg.vocab_size, dtype=bf, device=dev)
-        self.tokens = torch.empty(B, dtype=torch.int32, device=dev)
-        self.tokens_host = torch.empty(B, dtype=torch.int32, pin_memory=True)
+        R = B + min(T, self.spec_rows)  # logit rows: samples + speculative tree nodes
+        self.xs = torch.empty(R, cfg.hidden_size, dtype=bf, device=dev)
+        self.logits = torch.empty(R, cfg.vocab_size, dtype=bf, device=dev)
+        self.tokens = torch.empty(B + T, dtype=torch.int32, device=dev)
+        self.tokens_host = torch.empty(B + T, dtype=torch.int32, pin_memory=True)
+        self.vout = torch.zeros(B, 2 + ops.kernels.MAX_TREE_NODES, dtype=torch.int32, device=dev)
+        self.vout_host = torch.zeros(B, 2 + ops.kernels.MAX_TREE_NODES, dtype=torch.int32, pin_memory=True)
+        self._layer_ptrs = None
+        self.last_verify = None
+        self.last_preds = None
         self.max_pages = (self.max_model_len + self.qcfg.page_size - 1) // self.qcfg.page_size
         # one packed int32 staging area for all per-step metadata
-        self.meta_cap = 8 * T + 16 * B + B * self.max_pages + B * 64 + B * ((cfg.vocab_size + 31) // 32) + 1024
+        self.meta_cap = (9 * T + 16 * B + B * self.max_pages + B * 64 + B * ((cfg.vocab_size + 31) // 32) + 1024 +
+                         B * (ops.kernels.TREE_META_INTS + 2))
         self.meta_host = torch.empty(self.meta_cap, dtype=torch.int32, pin_memory=True)
         self.meta_dev = torch.empty(self.meta_cap, dtype=torch.int32, device=dev)
         self.ws.reserve_attn(B, cfg.num_heads, 64, cfg.head_dim)
-        self.ws.sampler_buffer(B, cfg.vocab_size)
+        self.ws.sampler_buffer(R, cfg.vocab_size)
 
     # ------------------------------------------------------------------ metadata upload
     def upload(self, st: StepInputs) -> dict:
@@ -236,6 +260,12 @@ class CudaRunner:
             arrays["hist"] = st.hist.reshape(-1)
         if st.allow_mask is not None:
             arrays["mask"] = st.allow_mask.reshape(-1)
+        if st.tree_mask is not None:
+            arrays["tmask"] = st.tree_mask
+        if st.verify_meta is not None:
+            arrays["vmeta"] = st.verify_meta.reshape(-1)
+            arrays["vtemp"] = st.verify_temp.view(np.int32)
+            arrays["vstep"] = st.verify_step
         host = self.meta_host.numpy()
         off = 0
         offs = {}
@@ -259,6 +289,9 @@ class CudaRunner:
             d["hist"] = d["hist"].view(st.hist.shape[0], st.hist.shape[1])
         if "mask" in d:
             d["mask"] = d["mask"].view(st.allow_mask.shape[0], st.allow_mask.shape[1])
+        if "vmeta" in d:
+            d["vmeta"] = d["vmeta"].view(st.verify_meta.shape[0], st.verify_meta.shape[1])
+            d["vtemp"] = d["vtemp"].view(torch.float32)
         return d
 
     # ------------------------------------------------------------------ forward
@@ -285,9 +318,10 @@ class CudaRunner:
                 ops.paged_decode_attention(q[:Bd], kc, ks, vc, vs, bt[:Bd], m["dlens"], attn[:Bd], hq, hkv, d, ps, grp,
                                            self.fk, self.fv, self.sm_scale, st.max_decode_ctx, ws=ws, splits=dsplit)
             if Bp:
+                tm = m["tmask"][Bd:] if "tmask" in m else None
                 ops.paged_prefill_attention(q[Bd:], kc, ks, vc, vs, bt[Bd:], m["tseq"], m["tq0"], m["qs"], m["ql"],
                                             m["ctx"], st.tile_seq.shape[0], attn[Bd:], hq, hkv, d, ps, grp, self.fk,
-                                            self.fv, self.sm_scale)
+                                            self.fv, self.sm_scale, tree_mask=tm)
             ops.w4a16_linear(attn, lw.o, out=h, residual=h, ws=ws)
             ops.rmsnorm(h, lw.ln2, cfg.rms_eps, out=x)
             if lw.moe is not None:
@@ -349,14 +383,42 @@ class CudaRunner:
         self.timer_start()
         m = self.upload(st)
         logits = self.forward(st, m)
-        toks = self.sample(st, m, logits)
+        nS = st.num_sample_rows
+        toks = self.sample(st, m, logits[:nS]) if nS else self.tokens[:0]
         B = toks.shape[0]
         self.tokens_host[:B].copy_(toks, non_blocking=True)
+        G = st.num_verify
+        if G:
+            vl = logits[nS:]
+            ops.kernels.tree_verify(vl, m["vmeta"], m["vtemp"], m["vstep"], st.seed, self.vout[:G],
+                                    draft_logits=st.draft_logits, ws=self.ws)
+            self.vout_host[:G].copy_(self.vout[:G], non_blocking=True)
+            if st.verify_preds:
+                nv = vl.shape[0]
+                preds = self.tokens[B:B + nv]
+                ops.sample(vl, preds, ws=self.ws)
+                self.tokens_host[B:B + nv].copy_(preds, non_blocking=True)
         self.timer_stop()
         torch.cuda.current_stream(self.device).synchronize()
         self.last_logits = logits if st.all_logits else None
         self.last_hidden = self.xs[:B]
+        if G:
+            self.last_verify = self.vout_host[:G].numpy().copy()
+            nv = logits.shape[0] - nS
+            self.last_preds = self.tokens_host[B:B + nv].numpy().copy() if st.verify_preds else None
         return self.tokens_host[:B].numpy().copy()
+
+    def kv_compact(self, src: list[int], dst: list[int]) -> None:
+        """Move accepted tree nodes' KV rows (every layer) from ``src`` to ``dst`` cache slots."""
+        if not src:
+            return
+        if self._layer_ptrs is None:
+            rows = [[kc.data_ptr(), ks.data_ptr(), vc.data_ptr(), vs.data_ptr()] for kc, ks, vc, vs in self.pools.layers]
+            self._layer_ptrs = torch.tensor(rows, dtype=torch.int64, device=self.device)
+        kc, ks, vc, vs = self.pools.layers[0]
+        pair = torch.tensor([src, dst], dtype=torch.int32).to(self.device, non_blocking=False)
+        ops.kernels.kv_compact(self._layer_ptrs, pair[0], pair[1], self.cfg.num_kv_heads, self.qcfg.page_size,
+                               kc.shape[-1], vc.shape[-1], ks.shape[-1], vs.shape[-1])
 
 
 # ----------------------------------------------------------------------------- CPU oracle of the step
@@ -375,6 +437,13 @@ class TorchPagedRunner:
         self.v = torch.zeros_like(self.k)
         self.cos_sin = rope_table(cfg, max_model_len + 1)
         self.last_logits = None
+        self.logits = None
+        self.last_verify = self.last_preds = None
+
+    def kv_compact(self, src: list[int], dst: list[int]) -> None:
+        for a, b in zip(src, dst):
+            self.k[:, b // self.ps, :, b % self.ps] = self.k[:, a // self.ps, :, a % self.ps]
+            self.v[:, b // self.ps, :, b % self.ps] = self.v[:, a // self.ps, :, a % self.ps]
 
     @torch.no_grad()
     def execute(self, st: StepInputs) -> np.ndarray:
@@ -428,7 +497,15 @@ class TorchPagedRunner:
                 qq = qv[r0:r0 + n]
                 s = torch.einsum("qhd,khd->hqk", qq, K) / math.sqrt(d)
                 qpos = torch.arange(ctx - n, ctx)
-                s = s.masked_fill(torch.arange(ctx)[None, None, :] > qpos[None, :, None], float("-inf"))
+                bad = torch.arange(ctx)[None, :] > qpos[:, None]
+                if st.tree_mask is not None:
+                    for i in range(n):
+                        tm = int(st.tree_mask[r0 + i]) & 0xFFFFFFFF
+                        if tm:
+                            for j in range(n):
+                                if not (tm >> j) & 1:
+                                    bad[i, ctx - n + j] = True
+                s = s.masked_fill(bad[None], float("-inf"))
                 attn[r0:r0 + n] = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), V).reshape(n, hq * d)
             h = h + attn @ w[p + "self_attn.o_proj.weight"].T
             x = _rms(h, w[p + "post_attention_layernorm.weight"], cfg.rms_eps)
@@ -436,10 +513,31 @@ class TorchPagedRunner:
         rows = torch.from_numpy(st.logits_rows.astype(np.int64))
         xs = _rms(h[rows], w["model.norm.weight"], cfg.rms_eps)
         logits = xs @ w["lm_head.weight"].T
+        self.logits = logits.to(torch.bfloat16)
         self.last_logits = logits
         self.last_hidden = xs
-        out = np.empty(len(rows), dtype=np.int32)
-        for i in range(len(rows)):
+        nS = st.num_sample_rows
+        self.last_verify = self.last_preds = None
+        if st.num_verify:
+            from ..engine.speculative import MAX_TREE_NODES, DraftTree, tree_verify_ref
+
+            vl = logits[nS:]
+            res = np.zeros((st.num_verify, 2 + MAX_TREE_NODES), dtype=np.int32)
+            for g_, meta in enumerate(st.verify_meta):
+                r0_, n_ = int(meta[0]), int(meta[1])
+                par = meta[2:2 + n_].tolist()
+                tok = meta[2 + MAX_TREE_NODES:2 + MAX_TREE_NODES + n_].tolist()
+                qr = meta[2 + 2 * MAX_TREE_NODES:2 + 2 * MAX_TREE_NODES + n_].tolist()
+                tree = DraftTree(tok, par, qr)
+                path, fin = tree_verify_ref(vl[r0_:r0_ + n_], tree, float(st.verify_temp[g_]), int(st.seed),
+                                            int(st.verify_step[g_]), st.draft_logits)
+                res[g_, 0], res[g_, 1] = len(path), fin
+                res[g_, 2:2 + len(path)] = path
+            self.last_verify = res
+            if st.verify_preds:
+                self.last_preds = vl.argmax(-1).numpy().astype(np.int32)
+        out = np.empty(nS, dtype=np.int32)
+        for i in range(nS):
             lg = logits[i].clone()
             if st.allow_mask is not None:
                 bits = np.unpackbits(st.allow_mask[i].view(np.uint8), bitorder="little")[: lg.shape[0]]

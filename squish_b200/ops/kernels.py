@@ -34,10 +34,18 @@ class Workspace:
         self._attn_o = torch.empty(0, dtype=torch.float32, device=device)
         self._attn_lse = torch.empty(0, dtype=torch.float32, device=device)
         self._sampler = torch.empty(0, dtype=torch.float32, device=device)
+        # set once a CUDA graph has captured these buffers: growing one then would leave the
+        # graph writing to freed memory, so it becomes an error instead
+        self.frozen = False
+
+    def _grow_check(self, what: str) -> None:
+        if self.frozen:
+            raise RuntimeError(f"workspace {what} buffer would grow after CUDA-graph capture; reserve it up front")
 
     def attn_buffers(self, b: int, hq: int, splits: int, d: int):
         need = b * hq * splits * d
-        if self._attn_o.numel() < need:
+        if self._attn_o.numel() < need or self._attn_lse.numel() < need // d:
+            self._grow_check("attention")
             self._attn_o = torch.empty(max(need, 1 << 20), dtype=torch.float32, device=self.device)
             self._attn_lse = torch.empty(max(need // d, 1 << 16), dtype=torch.float32, device=self.device)
         return self._attn_o, self._attn_lse
@@ -48,6 +56,7 @@ class Workspace:
     def sampler_buffer(self, rows: int, vocab: int):
         need = rows * vocab
         if self._sampler.numel() < need:
+            self._grow_check("sampler")
             self._sampler = torch.empty(need, dtype=torch.float32, device=self.device)
         return self._sampler
 
@@ -178,10 +187,13 @@ def paged_decode_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables
 
 
 def paged_prefill_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables, tile_seq, tile_q0, q_start,
-                            q_len, ctx_len, n_tiles, out, hq, hkv, d, page_size, group, fmt_k, fmt_v, sm_scale):
+                            q_len, ctx_len, n_tiles, out, hq, hkv, d, page_size, group, fmt_k, fmt_v, sm_scale,
+                            tree_mask=None):
+    """Causal attention of prefill chunks over their paged context; ``tree_mask`` (int32 per
+    query row, bit j = may attend chunk token j, 0 = causal) turns a chunk into a token tree."""
     native().paged_prefill_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables, tile_seq, tile_q0,
                                      q_start, q_len, ctx_len, int(n_tiles), out, hq, hkv, d, page_size, group,
-                                     fmt_k, fmt_v, float(sm_scale))
+                                     fmt_k, fmt_v, float(sm_scale), tree_mask)
     _count()
     return out
 
@@ -257,3 +269,25 @@ def w4a16_grouped_linear(xs: torch.Tensor, w: GroupedInt4Weight, out: torch.Tens
                                 tile_expert, num_tiles, bn, ws.gemm_ws, ws.gemm_counters, ws.status)
     _count()
     return out
+
+
+# ----------------------------------------------------------------------------- speculative decoding
+MAX_TREE_NODES = 32
+TREE_META_INTS = 2 + 3 * MAX_TREE_NODES
+
+
+def tree_verify(logits: torch.Tensor, meta: torch.Tensor, temperature: torch.Tensor, step: torch.Tensor, seed: int,
+                out: torch.Tensor, draft_logits: torch.Tensor | None = None, ws: Workspace | None = None) -> torch.Tensor:
+    """Walk each group's draft tree against its target logits rows (greedy or rejection
+    sampling); out[g] = (n_accepted, final token, accepted node indices...)."""
+    ws = ws or workspace(logits.device)
+    scratch = ws.sampler_buffer(meta.shape[0], logits.shape[1])
+    native().tree_verify(logits, draft_logits, meta, temperature, step, int(seed), scratch, out)
+    _count()
+    return out
+
+
+def kv_compact(layer_ptrs: torch.Tensor, src: torch.Tensor, dst: torch.Tensor, hkv: int, page_size: int,
+               kc_bytes: int, vc_bytes: int, ks_n: int, vs_n: int) -> None:
+    native().kv_compact(layer_ptrs, src, dst, hkv, page_size, kc_bytes, vc_bytes, ks_n, vs_n)
+    _count()

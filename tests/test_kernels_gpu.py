@@ -185,6 +185,7 @@ def _gather(dense, bt_row, n_tok, ps):
                                             ("int8", 14, 2, 64), ("int2", 32, 4, 128)])
 @pytest.mark.parametrize("lens", [[1, 17, 300], [2048, 5, 64, 1000], [33]])
 def test_paged_decode_attention(cuda, kvfmt, hq, hkv, d, lens):
+    torch.manual_seed(sum(lens) + hq)
     ps, group = 16, 32 if kvfmt != "k8v4" else 64
     fk, fv = ops.KV_FORMATS[kvfmt]
     max_pages = max((l + ps - 1) // ps for l in lens)
@@ -207,11 +208,13 @@ def test_paged_decode_attention(cuda, kvfmt, hq, hkv, d, lens):
         k = _gather(kd, bt[i], l, ps).to(torch.bfloat16).float()
         v = _gather(vd, bt[i], l, ps).to(torch.bfloat16).float()
         ref = attention(q[i].float().view(1, hq, d), k, v, torch.tensor([l - 1]), sm_scale(d))
-        torch.testing.assert_close(out[i].float().cpu().view(1, hq, d), ref, rtol=2e-2, atol=2e-2)
+        # P is rounded to bf16 before the PV product; over 2k keys that is ~1e-2 absolute
+        torch.testing.assert_close(out[i].float().cpu().view(1, hq, d), ref, rtol=2e-2, atol=3e-2)
 
 
 @pytest.mark.parametrize("kvfmt,hq,hkv,d", [("int4", 28, 4, 128), ("k8v4", 16, 2, 128), ("bf16", 8, 2, 64)])
 def test_paged_prefill_attention(cuda, kvfmt, hq, hkv, d):
+    torch.manual_seed(hq + d)
     ps, group = 16, 32 if kvfmt != "k8v4" else 64
     fk, fv = ops.KV_FORMATS[kvfmt]
     # (chunk length, total context after the chunk): fresh prompts and chunked continuations

@@ -1,0 +1,152 @@
+"""Speculative decoding on the CPU oracle: draft trees, n-gram lookup, the verifier's host
+restatement (greedy exactness and the lossless sampling property), and the engine paths
+(prompt lookup with branching trees, Jacobi, draft model) against plain greedy decoding.
+
+Mirrors the reference's greedy-identity contract (tests/test_prompt_lookup_batched.py):
+speculation must not change greedy output.
+"""
+import numpy as np
+import pytest
+import torch
+
+from squish_b200.engine.engine import EngineConfig, LLMEngine
+from squish_b200.engine.sampling import SamplingParams
+from squish_b200.engine.speculative import (NGramIndex, SpecConfig, _uni, build_tree, tree_verify_ref)
+from squish_b200.models.config import get_preset
+from squish_b200.models.weights import random_checkpoint
+
+
+def test_build_tree_merges_prefixes_and_masks():
+    t = build_tree(7, [[1, 2, 3], [1, 2, 4], [5]], max_nodes=16)
+    assert t.tokens == [7, 1, 2, 3, 4, 5]
+    assert t.parent == [-1, 0, 1, 2, 2, 0]
+    assert t.depth == [0, 1, 2, 3, 3, 1]
+    m = t.masks()
+    assert m[3] == 0b001111 and m[4] == 0b010111 and m[5] == 0b100001
+    t2 = build_tree(7, [[1, 2, 3], [9, 9, 9]], max_nodes=5)
+    assert t2.size == 5 and t2.tokens == [7, 1, 2, 3, 9]
+
+
+def test_ngram_continuations():
+    idx = NGramIndex(1, 3)
+    toks = [1, 2, 3, 4, 9, 1, 2, 3, 5, 7, 1, 2, 3]
+    idx.update(toks)
+    c = idx.continuations(toks, 3, 2)
+    assert c == [[5, 7, 1], [4, 9, 1]]  # most recent match of (1,2,3) first
+    idx.update(toks + [8])
+    assert idx.continuations(toks + [8], 2, 1) == []
+
+
+def test_uniform_hash_is_in_range_and_deterministic():
+    u = _uni(1, 2, 3, np.arange(1000))
+    assert (u > 0).all() and (u < 1).all() and abs(float(u.mean()) - 0.5) < 0.05
+    assert np.array_equal(u, _uni(1, 2, 3, np.arange(1000)))
+
+
+def test_verify_ref_greedy_follows_argmax_chain():
+    V = 50
+    lg = torch.full((5, V), -5.0)
+    # root predicts 3; node(3) predicts 8; node(8) predicts 2
+    lg[0, 3] = lg[1, 8] = lg[2, 2] = 5.0
+    lg[3, 1] = lg[4, 1] = 5.0
+    t = build_tree(0, [[3, 8, 9], [4]], 16)  # nodes: 3,8,9 chain then 4
+    path, fin = tree_verify_ref(lg, t, 0.0, 0, 0)
+    assert path == [1, 2] and fin == 2  # 3 and 8 accepted, 9 rejected -> argmax at node(8) = 2
+
+
+def test_verify_ref_sampling_is_lossless():
+    """First emitted token ~ p whatever the (deterministic or model) draft: chi-square check."""
+    V = 6
+    g = torch.Generator().manual_seed(0)
+    lg = torch.randn(4, V, generator=g) * 1.5
+    p = torch.softmax(lg[0], -1).numpy()
+    ql = torch.randn(2, V, generator=g)
+    N = 4000
+    for kind in ("lookup", "draft"):
+        counts = np.zeros(V)
+        for s in range(N):
+            if kind == "lookup":
+                t = build_tree(0, [[2, 1], [4]], 16)
+                path, fin = tree_verify_ref(lg, t, 1.0, 123, s)
+            else:
+                q = torch.softmax(ql[0], -1).numpy()
+                d1 = int(np.searchsorted(np.cumsum(q), _uni(7, s, 1, 0)))  # draft sample from q
+                d1 = min(d1, V - 1)
+                t = build_tree(0, [[d1]], 16, [[0]])
+                path, fin = tree_verify_ref(lg[:2], t, 1.0, 123, s, draft_logits=ql)
+            first = t.tokens[path[0]] if path else fin
+            counts[first] += 1
+        exp = p * N
+        chi2 = float(((counts - exp) ** 2 / exp).sum())
+        assert chi2 < 25.0, (kind, chi2, counts, exp)  # 5 dof: p ~ 1e-4
+
+
+def _engine(spec=None, seed=0):
+    cfg, q = get_preset("tiny-llama")
+    ck = random_checkpoint(cfg, q, seed=seed, device="cpu")
+    return LLMEngine.from_checkpoint(ck, "cpu", EngineConfig(max_num_seqs=4, max_num_batched_tokens=256,
+                                                             max_model_len=512, num_pages=128, cuda_graphs=False,
+                                                             spec=spec))
+
+
+def _prompts():
+    rng = np.random.default_rng(3)
+    base = rng.integers(0, 32000, 12).tolist()
+    return [base * 3 + base[:5], rng.integers(0, 32000, 20).tolist() * 2]
+
+
+@pytest.mark.parametrize("spec", [SpecConfig("prompt_lookup", k=4, branches=3, max_nodes=12),
+                                  SpecConfig("jacobi", k=3), SpecConfig("draft", k=3, draft_model="tiny-llama")])
+def test_speculative_greedy_matches_plain_greedy(spec):
+    sp = SamplingParams(max_tokens=24, ignore_eos=True)
+    want = _engine().generate(_prompts(), sp)
+    eng = _engine(spec)
+    got = eng.generate(_prompts(), sp)
+    assert got == want
+    st = eng.spec_stats
+    assert st["verifies"] > 0 and st["emitted"] >= st["verifies"]
+    if spec.method == "draft":  # the draft is the target itself: every draft is accepted
+        assert st["accepted"] == st["drafted"]
+
+
+def test_force_accept_knob_emits_fixed_lengths():
+    sc = SpecConfig("jacobi", k=4, force_accept=2, adaptive=False)
+    eng = _engine(sc)
+    out = eng.generate([_prompts()[0]], SamplingParams(max_tokens=13, ignore_eos=True))[0]
+    assert len(out) == 13
+    assert eng.spec_stats["accepted"] == 2 * eng.spec_stats["verifies"]
+
+
+def test_second_branch_acceptance_compacts_kv():
+    """A tree whose first branch is wrong and second branch is the true continuation: the
+    accepted nodes are not the index-ordered chain, so their KV rows must be moved."""
+    prompt = _prompts()[1]
+    sp = SamplingParams(max_tokens=12, ignore_eos=True)
+    want = _engine().generate([prompt], sp)[0]
+    eng = _engine(SpecConfig("prompt_lookup", k=3, branches=2, max_nodes=16, adaptive=False))
+
+    class Oracle:
+        def propose(self, reqs):
+            out = {}
+            for r in reqs:
+                done = len(r.output)
+                true = want[done:done + 3]
+                wrong = [(t + 1) % 32000 for t in true]
+                if true:
+                    out[r.rid] = build_tree(r.tokens[-1], [wrong, true], 16)
+            return out
+
+        def after_verify(self, r, accepted, preds=None):
+            pass
+
+        def forget(self, rid):
+            pass
+
+    eng.proposer = Oracle()
+    calls = []
+    orig = eng.runner.kv_compact
+    eng.runner.kv_compact = lambda s, d: (calls.append((list(s), list(d))), orig(s, d))
+    got = eng.generate([prompt], sp)[0]
+    assert got == want
+    assert calls, "the second branch should have been compacted"
+    assert eng.spec_stats["accepted"] > 0
