@@ -22,7 +22,8 @@ Reported (rank 0, one JSON line):
   ttft_ms      p50 / p99 over requests whose first token came in the timed window.
 The reference arm runs the unmodified reference package from baseline/_ref through its
 public torch backend (squish.backend.BE.stream_generate: HF transformers generate with
-a KV cache, fp16 weights -- the reference's CUDA loader serves fp16).
+a KV cache, fp16 weights: the reference's INT4 torch loader dequantizes to fp16 before
+loading, so fp16 is what its CUDA path computes with).
 """
 from __future__ import annotations
 
@@ -37,7 +38,7 @@ import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 METRIC = "output tok/s + p50/p99 TTFT, Qwen2.5-7B-shape INT4 w/ INT4 KV, 1/2/4/8 B200"
-BASELINE_VALUE = None  # BASELINE.md publishes no B200 number for this metric
+PUBLISHED_VALUE = None  # the reference publishes no B200 number for this metric
 
 
 def parse():
@@ -395,6 +396,12 @@ def main():
                 dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(res), flush=True)
+    if args.impl == "reference":
+        # the reference's HF streamer leaves its generation thread running when a request is
+        # cut at the step budget; end the process without waiting for it
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
 
 
 if __name__ == "__main__":

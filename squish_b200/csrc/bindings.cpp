@@ -10,7 +10,10 @@
 #include <cudaTypedefs.h>
 
 #include "kernels.h"
+#include <cstring>
+
 #include "w4a16_gemm.h"
+#include "comm.h"
 #include "cpu_ref.h"
 
 namespace {
@@ -310,6 +313,141 @@ void kv_compact(torch::Tensor layer_ptrs, torch::Tensor src, torch::Tensor dst, 
   CUDA_OK(sq::kv_compact_launch(p, (int)layer_ptrs.size(0), cur_stream()));
 }
 
+// ------------------------------------------------------------------ tensor parallel (NVLink peer memory)
+// Device memory shared across processes with CUDA IPC: one cudaMalloc per buffer, its
+// handle exchanged through torch.distributed, opened by every peer.
+std::vector<torch::Tensor> ipc_alloc(int64_t bytes) {
+  void* p = nullptr;
+  CUDA_OK(cudaMalloc(&p, (size_t)bytes));
+  CUDA_OK(cudaMemset(p, 0, (size_t)bytes));
+  cudaIpcMemHandle_t h;
+  CUDA_OK(cudaIpcGetMemHandle(&h, p));
+  auto ht = torch::empty({(int64_t)sizeof(h)}, torch::kUInt8);
+  std::memcpy(ht.data_ptr(), &h, sizeof(h));
+  auto pt = torch::tensor({(int64_t)reinterpret_cast<uintptr_t>(p)}, torch::kInt64);
+  return {pt, ht};
+}
+
+int64_t ipc_open(torch::Tensor handle) {
+  TORCH_CHECK(handle.numel() == (int64_t)sizeof(cudaIpcMemHandle_t), "bad IPC handle");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.contiguous().data_ptr(), sizeof(h));
+  void* p = nullptr;
+  CUDA_OK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return (int64_t)reinterpret_cast<uintptr_t>(p);
+}
+
+void ipc_close(int64_t ptr) { CUDA_OK(cudaIpcCloseMemHandle(reinterpret_cast<void*>((uintptr_t)ptr))); }
+void ipc_free(int64_t ptr) { CUDA_OK(cudaFree(reinterpret_cast<void*>((uintptr_t)ptr))); }
+
+torch::Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> sizes, torch::ScalarType dtype, int64_t device) {
+  auto opts = torch::TensorOptions().dtype(dtype).device(torch::kCUDA, (int)device);
+  return torch::from_blob(reinterpret_cast<void*>((uintptr_t)ptr), sizes, opts);
+}
+
+// INT4 GEMM whose output tiles are pushed to every rank (fused all-reduce, producer side).
+// Returns the launch plan {bn, nt, splits, grid_x, grid_y} for the matching tp_reduce.
+std::vector<int64_t> w4a16_gemm_push(torch::Tensor x, torch::Tensor wq, int64_t N, int64_t K, int64_t group,
+                                     int64_t ldy, torch::Tensor push_dst, torch::Tensor push_flags,
+                                     int64_t push_stride, int64_t flag_stride, torch::Tensor seq, int64_t tp,
+                                     torch::Tensor ws, torch::Tensor counters, torch::Tensor status) {
+  CHECK_CUDA(x);
+  CHECK_DT(x, torch::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(1) == K, "x must be [M, K]");
+  TORCH_CHECK(push_dst.scalar_type() == torch::kInt64 && push_dst.numel() == tp, "push_dst: [tp] int64 pointers");
+  TORCH_CHECK(push_flags.scalar_type() == torch::kInt64 && push_flags.numel() == tp, "push_flags: [tp] pointers");
+  const int64_t M = x.size(0);
+  const c10::cuda::CUDAGuard g(x.device());
+  auto plan = gemm_plan(M, N, K);
+  const int bn = (int)plan[0], nt = (int)plan[1];
+  sq::W4A16Params p{};
+  p.wq = ptr<uint32_t>(wq);
+  p.sz = p.wq;
+  p.y = nullptr;
+  p.ws = ptr<float>(ws);
+  p.counters = ptr<int>(counters);
+  p.status = ptr<int>(status);
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.ldy = (int)ldy;
+  p.kb_total = (int)((K + 63) / 64);
+  p.splits = (int)plan[2];
+  p.kb_per_split = (int)plan[3];
+  p.gpk = group >= 64 ? 1 : (int)(64 / group);
+  p.epilogue = sq::EPI_PLAIN;
+  p.push_dst = reinterpret_cast<__nv_bfloat16* const*>(push_dst.data_ptr());
+  p.push_flags = reinterpret_cast<int* const*>(push_flags.data_ptr());
+  p.push_stride = push_stride;
+  p.flag_stride = (int)flag_stride;
+  p.seq = ptr<int>(seq);
+  p.tp = (int)tp;
+  const int64_t gx = (N + 128 * nt - 1) / (128 * nt), gy = (M + bn - 1) / bn;
+  if (M > 0) {
+    const CUtensorMap xmap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), bn);
+    CUDA_OK(sq::w4a16_gemm_launch(xmap, p, bn, nt, cur_stream()));
+  }
+  return {bn, nt, plan[2], gx, gy};
+}
+
+void tp_reduce(torch::Tensor recv, int64_t recv_stride, int64_t src_stride, int64_t ld, torch::Tensor flags,
+               int64_t flag_stride, int64_t flag_src_stride, int64_t expect, torch::Tensor out, bool residual,
+               int64_t M, int64_t N, int64_t tile_m, int64_t tile_n, int64_t grid_x, int64_t grid_y, int64_t tp,
+               torch::Tensor seq, torch::Tensor done, torch::Tensor status) {
+  CHECK_CUDA(out);
+  CHECK_DT(out, torch::kBFloat16);
+  const c10::cuda::CUDAGuard g(out.device());
+  sq::TpReduceParams p{};
+  p.recv = ptr<__nv_bfloat16>(recv);
+  p.recv_stride = recv_stride;
+  p.src_stride = src_stride;
+  p.ld = (int)ld;
+  p.flags = ptr<int>(flags);
+  p.flag_stride = (int)flag_stride;
+  p.flag_src_stride = (int)flag_src_stride;
+  p.expect = (int)expect;
+  p.out = ptr<__nv_bfloat16>(out);
+  p.ld_out = (int)out.stride(0);
+  p.residual_in_out = residual ? 1 : 0;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.tile_m = (int)tile_m;
+  p.tile_n = (int)tile_n;
+  p.tp = (int)tp;
+  p.seq = ptr<int>(seq);
+  p.done = ptr<int>(done);
+  p.status = ptr<int>(status);
+  if (M == 0) return;
+  CUDA_OK(sq::tp_reduce_launch(p, (int)grid_x, (int)grid_y, cur_stream()));
+}
+
+void tp_gather(torch::Tensor src, torch::Tensor dst_ptrs, int64_t ld_dst, int64_t row0, int64_t col0,
+               torch::Tensor flag_ptrs,
+               torch::Tensor local_flags, int64_t flag_stride, int64_t blocks, int64_t rank, int64_t tp,
+               torch::Tensor seq, torch::Tensor status) {
+  CHECK_CUDA(src);
+  CHECK_DT(src, torch::kBFloat16);
+  const c10::cuda::CUDAGuard g(src.device());
+  sq::TpGatherParams p{};
+  p.src = ptr<__nv_bfloat16>(src);
+  p.ld_src = (int)src.stride(0);
+  p.dst = reinterpret_cast<__nv_bfloat16* const*>(dst_ptrs.data_ptr());
+  p.ld_dst = (int)ld_dst;
+  p.row0 = (int)row0;
+  p.col0 = (int)col0;
+  p.rows = (int)src.size(0);
+  p.cols = (int)src.size(1);
+  p.flags = reinterpret_cast<int* const*>(flag_ptrs.data_ptr());
+  p.local_flags = ptr<int>(local_flags);
+  p.flag_stride = (int)flag_stride;
+  p.expect = (int)blocks;
+  p.rank = (int)rank;
+  p.tp = (int)tp;
+  p.seq = ptr<int>(seq);
+  p.status = ptr<int>(status);
+  CUDA_OK(sq::tp_gather_launch(p, cur_stream()));
+}
+
 // ------------------------------------------------------------------ norm / rope / attention
 void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> row_idx, double eps) {
   CHECK_CUDA(x);
@@ -489,6 +627,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w4a16_grouped_gemm", &w4a16_grouped_gemm);
   m.def("moe_route", &moe_route);
   m.def("tree_verify", &tree_verify);
+  m.def("ipc_alloc", &ipc_alloc);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("ipc_free", &ipc_free);
+  m.def("tensor_from_ptr", &tensor_from_ptr);
+  m.def("w4a16_gemm_push", &w4a16_gemm_push);
+  m.def("tp_reduce", &tp_reduce);
+  m.def("tp_gather", &tp_gather);
   m.def("kv_compact", &kv_compact);
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);

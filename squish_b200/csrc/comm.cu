@@ -1,0 +1,148 @@
+// comm.cu — tensor-parallel collectives over NVLink peer memory (no NCCL on the hot path).
+//
+// Fused GEMM -> all-reduce (row-parallel o_proj / down_proj): the INT4 GEMM runs in push
+// mode (w4a16_gemm.cu): each CTA stores its bf16 partial output tile straight into every
+// rank's receive buffer slot for this source rank (P2P stores over NVLink) and bumps that
+// tile's flag on every rank. tp_reduce (below) then runs on each rank: one CTA per GEMM
+// output tile waits until the tile's flag from every source rank reached its expected
+// count, sums the tp partials in rank order (the same order on every rank, so every rank
+// holds bit-identical results), adds the residual and writes the hidden state in place.
+// The transfer of early tiles overlaps the GEMM of later ones.
+//
+// Buffers alternate by parity (bit 0 of a device-side op counter) so a fast rank can push
+// op s+1 while a slow one still reads op s; a rank can only reach op s+2 after every peer
+// pushed op s+1, which each peer does only after finishing its read of op s. The consumer
+// clears its flags after reading; the last CTA to finish advances the counter. Every wait
+// is bounded: on timeout the status word gets SQ_ERR_TIMEOUT_PEER and the kernel goes on.
+//
+// tp_gather: each rank stores its column block (vocab shard of the logits) into every
+// rank's full-width output (P2P stores), then bumps a per-source flag on every rank; a
+// one-warp kernel waits for all sources. The output has no parity copy: between two
+// gathers every rank passes at least one tp_reduce, which needs every peer's next push,
+// which a peer issues only after it finished reading the previous gather's output.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "comm.h"
+#include "sm100.cuh"
+
+namespace sq {
+
+namespace {
+
+constexpr long long kPeerSpin = 1LL << 22;  // ~seconds of polling, then report and go on
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// wait until *f >= want (bounded); returns false on timeout
+__device__ bool wait_flag(const int* f, int want, int* status) {
+  for (long long i = 0; i < kPeerSpin; ++i) {
+    if (ld_acquire_sys(f) >= want) return true;
+    if ((i & 4095) == 4095 && *reinterpret_cast<volatile int*>(status) != 0) return false;
+  }
+  atomicCAS(status, 0, SQ_ERR_TIMEOUT_PEER);
+  return false;
+}
+
+__global__ void __launch_bounds__(256) tp_reduce_kernel(const TpReduceParams p) {
+  const int tile = blockIdx.x * gridDim.y + blockIdx.y;  // same numbering as the GEMM grid
+  const int par = *reinterpret_cast<volatile const int*>(p.seq) & 1;
+  const int tp = p.tp;
+  int* flags = p.flags + (size_t)par * p.flag_stride;
+  if ((int)threadIdx.x < tp) wait_flag(flags + (size_t)threadIdx.x * p.flag_src_stride + tile, p.expect, p.status);
+  __syncthreads();
+  __threadfence();
+  const int n0 = blockIdx.x * p.tile_n, m0 = blockIdx.y * p.tile_m;
+  const int n1 = min(p.N, n0 + p.tile_n), m1 = min(p.M, m0 + p.tile_m);
+  const __nv_bfloat16* recv = p.recv + (size_t)par * p.recv_stride;
+  const int w = n1 - n0;
+  // each thread handles pairs of columns
+  for (int idx = threadIdx.x * 2; idx < (m1 - m0) * w; idx += blockDim.x * 2) {
+    const int m = m0 + idx / w, n = n0 + idx % w;
+    const bool two = (idx % w) + 1 < w;
+    float a0 = 0.f, a1 = 0.f;
+    for (int r = 0; r < tp; ++r) {
+      const __nv_bfloat16* src = recv + (size_t)r * p.src_stride + (size_t)m * p.ld + n;
+      a0 += __bfloat162float(src[0]);
+      if (two) a1 += __bfloat162float(src[1]);
+    }
+    __nv_bfloat16* o = p.out + (size_t)m * p.ld_out + n;
+    if (p.residual_in_out) {
+      a0 += __bfloat162float(o[0]);
+      if (two) a1 += __bfloat162float(o[1]);
+    }
+    o[0] = __float2bfloat16(a0);
+    if (two) o[1] = __float2bfloat16(a1);
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < tp) flags[(size_t)threadIdx.x * p.flag_src_stride + tile] = 0;
+  // the last CTA advances the op counter
+  __shared__ int last;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = (atomicAdd(p.done, 1) == (int)(gridDim.x * gridDim.y) - 1);
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    *p.done = 0;
+    __threadfence();
+    atomicAdd(p.seq, 1);
+  }
+}
+
+// src [rows, cols] is written into every rank's dst at rows row0.., columns col0..
+__global__ void __launch_bounds__(256) tp_gather_push_kernel(const TpGatherParams p) {
+  const int par = __ldg(p.seq) & 1;
+  const int vec = p.cols / 8;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.rows * vec; i += gridDim.x * blockDim.x) {
+    const int r = i / vec, c = i % vec;
+    const uint4 v = reinterpret_cast<const uint4*>(p.src + (size_t)r * p.ld_src)[c];
+    for (int k = 0; k < p.tp; ++k)
+      reinterpret_cast<uint4*>(p.dst[k] + (size_t)(p.row0 + r) * p.ld_dst + p.col0)[c] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int k = 0; k < p.tp; ++k) {
+      int* f = p.flags[k] + (size_t)par * p.flag_stride + p.rank;
+      asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(f), "r"(1) : "memory");
+    }
+}
+
+__global__ void tp_gather_wait_kernel(const TpGatherParams p) {
+  const int par = __ldg(p.seq) & 1;
+  int* flags = p.local_flags + (size_t)par * p.flag_stride;
+  if ((int)threadIdx.x < p.tp) {
+    wait_flag(flags + threadIdx.x, p.expect, p.status);
+    flags[threadIdx.x] = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(p.seq, 1);
+  }
+}
+
+}  // namespace
+
+cudaError_t tp_reduce_launch(const TpReduceParams& p, int grid_x, int grid_y, cudaStream_t s) {
+  if (p.tp > 256) return cudaErrorInvalidValue;
+  tp_reduce_kernel<<<dim3(grid_x, grid_y), 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t tp_gather_launch(const TpGatherParams& p, cudaStream_t s) {
+  if (p.cols % 8 || p.ld_src % 8 || p.ld_dst % 8 || p.col0 % 8) return cudaErrorInvalidValue;
+  tp_gather_push_kernel<<<p.expect, 256, 0, s>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  tp_gather_wait_kernel<<<1, 32, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace sq

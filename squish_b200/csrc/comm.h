@@ -1,0 +1,43 @@
+// comm.h — tensor-parallel collectives over NVLink peer memory (see comm.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace sq {
+
+struct TpReduceParams {
+  const __nv_bfloat16* recv;  // local receive buffer [2 parity][tp src][rows][ld]
+  long long recv_stride;      // elements per parity
+  long long src_stride;       // elements per source rank
+  int ld;
+  int* flags;                 // local flags [2 parity][tp src][tiles]
+  int flag_stride, flag_src_stride;
+  int expect;                 // arrivals per (source, tile): the GEMM's split count
+  __nv_bfloat16* out;         // [M, ld_out]: out = residual (its old value) + sum
+  int ld_out;
+  int residual_in_out;
+  int M, N, tile_m, tile_n, tp;
+  int* seq;                   // device op counter (parity = seq & 1)
+  int* done;                  // CTA completion counter, zero between ops
+  int* status;
+};
+
+struct TpGatherParams {
+  const __nv_bfloat16* src;      // this rank's rows [rows, ld_src]
+  int ld_src;
+  __nv_bfloat16* const* dst;     // [tp] every rank's output base
+  int ld_dst;
+  int row0, col0, rows, cols;
+  int* const* flags;             // [tp] every rank's gather flags [2 parity][tp src]
+  int* local_flags;
+  int flag_stride;
+  int expect;                    // pushing CTAs per source
+  int rank, tp;
+  int* seq;
+  int* status;
+};
+
+cudaError_t tp_reduce_launch(const TpReduceParams& p, int grid_x, int grid_y, cudaStream_t s);
+cudaError_t tp_gather_launch(const TpGatherParams& p, cudaStream_t s);
+
+}  // namespace sq

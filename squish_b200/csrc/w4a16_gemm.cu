@@ -102,6 +102,26 @@ __device__ __forceinline__ void trace_mark(unsigned long long* smem_tr, int slot
 }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Store one output element locally, or (push mode) into every rank's receive buffer.
+__device__ __forceinline__ void store_out(const W4A16Params& p, int par, int m, int n, float v) {
+  const __nv_bfloat16 b = __float2bfloat16(v);
+  if (p.push_dst == nullptr) {
+    p.y[(size_t)m * p.ldy + n] = b;
+    return;
+  }
+  const size_t off = (size_t)par * p.push_stride + (size_t)m * p.ldy + n;
+  for (int r = 0; r < p.tp; ++r) p.push_dst[r][off] = b;
+}
+
+// After this CTA's stores of an output tile: make them visible system-wide, then bump the
+// tile's arrival flag on every rank (release at system scope).
+__device__ __forceinline__ void push_signal(const W4A16Params& p, int par, int tile) {
+  for (int r = 0; r < p.tp; ++r) {
+    int* f = p.push_flags[r] + (size_t)par * p.flag_stride + tile;
+    asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(f), "r"(1) : "memory");
+  }
+}
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -307,6 +327,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     const int m0 = mblk * BN;
     const bool single = (p.splits == 1);
     const bool silu_mode = (p.epilogue == EPI_SILU_MUL);
+    const int par = p.push_dst != nullptr ? (__ldg(p.seq) & 1) : 0;
     float* xch = reinterpret_cast<float*>(a_ring);  // operand buffers are dead once acc_full fires
 
     // Emit 16 consecutive token columns of tile t for this thread's row.
@@ -335,7 +356,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
             if (m < p.M) {
               float acc = val[j] + b;
               if (p.residual) acc += __bfloat162float(p.residual[(size_t)m * p.ldr + n]);
-              p.y[(size_t)m * p.ldy + n] = __float2bfloat16(acc);
+              store_out(p, par, m, n, acc);
             }
           }
         }
@@ -368,6 +389,11 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
           for (int j = 0; j < 16; ++j) xch[(c0 + j) * BM + row] = __uint_as_float(v[j]);
         }
       }
+    }
+    if (single && p.push_dst != nullptr) {
+      __threadfence_system();
+      epi_bar();
+      if (threadIdx.x == 128) push_signal(p, par, nblk * gridDim.y + mblk);
     }
   }
 
@@ -408,9 +434,14 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
           if (m < p.M && n < p.N) {
             acc += p.bias ? __bfloat162float(p.bias[n]) : 0.f;
             if (p.residual) acc += __bfloat162float(p.residual[(size_t)m * p.ldr + n]);
-            p.y[(size_t)m * p.ldy + n] = __float2bfloat16(acc);
+            store_out(p, p.push_dst != nullptr ? (__ldg(p.seq) & 1) : 0, m, n, acc);
           }
         }
+      }
+      if (p.push_dst != nullptr) {
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0) push_signal(p, __ldg(p.seq) & 1, nblk * gridDim.y + mblk);
       }
       cluster_sync();  // keep every CTA's shared memory alive until all remote reads are done
     }

@@ -32,6 +32,16 @@ struct W4A16Params {
   const int* tile_expert;
   const int* num_tiles;
   long long expert_stride;
+  // Tensor-parallel push mode (fused GEMM -> all-reduce), when push_dst != nullptr: the
+  // partial tile is stored into every rank's receive buffer (peer memory over NVLink) at
+  // push_dst[r] + parity * push_stride, then each CTA adds 1 to its tile's flag on every
+  // rank (push_flags[r] + parity * flag_stride + tile). parity = *seq & 1.
+  __nv_bfloat16* const* push_dst;
+  int* const* push_flags;
+  long long push_stride;
+  int flag_stride;
+  const int* seq;
+  int tp;
 };
 
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s);

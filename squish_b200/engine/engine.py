@@ -43,6 +43,8 @@ class EngineConfig:
     hist_window: int = 64
     seed: int = 0
     spec: object | None = None  # speculative.SpecConfig: prompt lookup / draft model / Jacobi
+    tp: int = 1                 # tensor-parallel ranks (one process per GPU, torch.distributed initialised)
+    tp_mode: str = "nvlink"     # "nvlink": fused GEMM+all-reduce over peer memory; "nccl": NCCL baseline
 
 
 @dataclass
@@ -94,6 +96,8 @@ class LLMEngine:
     def from_checkpoint(cls, ck: Checkpoint, device="cuda", ecfg: EngineConfig | None = None, **kw) -> "LLMEngine":
         ecfg = ecfg or EngineConfig(**kw)
         dev = torch.device(device)
+        if ecfg.tp > 1:
+            return cls._from_checkpoint_tp(ck, dev, ecfg)
         if dev.type == "cuda":
             from ..models.decoder import CudaRunner
 
@@ -114,6 +118,51 @@ class LLMEngine:
             num_pages = cls.plan_pages(ck.config, ck.quant, ecfg, dev)
             runner = TorchPagedRunner(ck, num_pages, ecfg.max_model_len)
         eng = cls(runner, ck.config, ck.quant, ecfg, num_pages)
+        if dev.type == "cuda" and ecfg.cuda_graphs:
+            from .cuda_graph import DecodeGraphs
+
+            eng.graphs = DecodeGraphs(eng)
+        if ecfg.spec is not None:
+            eng.proposer = make_proposer(ecfg.spec, eng)
+            eng.guard = _Guard(ecfg.spec.miss_limit, ecfg.spec.cooldown) if ecfg.spec.adaptive else None
+        return eng
+
+    @classmethod
+    def _from_checkpoint_tp(cls, ck: Checkpoint, dev: torch.device, ecfg: EngineConfig) -> "LLMEngine":
+        """Tensor-parallel engine: this process holds one shard; every rank runs the same
+        host logic (scheduling is deterministic and every rank samples the same tokens)."""
+        import torch.distributed as dist
+
+        from ..kv.paged import KVPools
+        from ..parallel.comm import TPComm
+
+        if not dist.is_initialized() or dist.get_world_size() != ecfg.tp:
+            raise RuntimeError(f"tp={ecfg.tp} needs torch.distributed initialised with {ecfg.tp} ranks")
+        cfg = ck.config
+        spec_rows = ecfg.max_num_seqs * ecfg.spec.max_nodes if ecfg.spec is not None else 0
+        rows = ecfg.max_num_seqs + min(ecfg.max_num_batched_tokens, spec_rows)
+        if dev.type == "cuda":
+            from ..parallel.tp_runner import TPCudaRunner
+
+            comm = TPComm(ecfg.tp_mode, ecfg.max_num_batched_tokens, cfg.hidden_size, rows, cfg.vocab_size,
+                          device=dev)
+            runner = TPCudaRunner(ck, dev, 1, comm, max_num_tokens=ecfg.max_num_batched_tokens,
+                                  max_num_seqs=ecfg.max_num_seqs, max_model_len=ecfg.max_model_len,
+                                  free_checkpoint=True, spec_rows=spec_rows)
+            del runner.pools
+            torch.cuda.empty_cache()
+            pages = torch.tensor([cls.plan_pages(runner.cfg, ck.quant, ecfg, dev)], device=dev)
+            dist.all_reduce(pages, op=dist.ReduceOp.MIN)  # identical pools -> identical scheduling
+            num_pages = int(pages.item())
+            runner.pools = KVPools(runner.cfg, ck.quant, num_pages, dev)
+        else:
+            from ..parallel.tp_runner import TorchTPRunner
+
+            comm = TPComm("cpu", ecfg.max_num_batched_tokens, cfg.hidden_size, rows, cfg.vocab_size)
+            num_pages = cls.plan_pages(cfg, ck.quant, ecfg, dev)
+            runner = TorchTPRunner(ck, num_pages, comm, ecfg.max_model_len)
+        eng = cls(runner, cfg, ck.quant, ecfg, num_pages)
+        eng.comm = comm
         if dev.type == "cuda" and ecfg.cuda_graphs:
             from .cuda_graph import DecodeGraphs
 

@@ -322,17 +322,25 @@ class CudaRunner:
                 ops.paged_prefill_attention(q[Bd:], kc, ks, vc, vs, bt[Bd:], m["tseq"], m["tq0"], m["qs"], m["ql"],
                                             m["ctx"], st.tile_seq.shape[0], attn[Bd:], hq, hkv, d, ps, grp, self.fk,
                                             self.fv, self.sm_scale, tree_mask=tm)
-            ops.w4a16_linear(attn, lw.o, out=h, residual=h, ws=ws)
+            self._row_parallel(attn, lw.o, h)
             ops.rmsnorm(h, lw.ln2, cfg.rms_eps, out=x)
             if lw.moe is not None:
                 lw.moe.forward(x, h, ws)
             else:
                 act = ops.w4a16_linear(x, lw.gate_up, out=self.act[:T], silu_mul=True, ws=ws)
-                ops.w4a16_linear(act[:, : self.F], lw.down, out=h, residual=h, ws=ws)
+                self._row_parallel(act[:, : self.F], lw.down, h)
         B = st.logits_rows.shape[0]
         xs = ops.rmsnorm(h, self.norm, cfg.rms_eps, out=self.xs[:B], row_idx=m["rows"])
+        return self._lm_head(xs, B)
+
+    # hooks overridden by the tensor-parallel runner
+    def _row_parallel(self, x: torch.Tensor, w: Int4Weight, h: torch.Tensor) -> None:
+        """h += x @ w^T (residual fused into the GEMM epilogue)."""
+        ops.w4a16_linear(x, w, out=h, residual=h, ws=self.ws)
+
+    def _lm_head(self, xs: torch.Tensor, B: int) -> torch.Tensor:
         if self.lm_head_q is not None:
-            return ops.w4a16_linear(xs, self.lm_head_q, out=self.logits[:B], ws=ws)
+            return ops.w4a16_linear(xs, self.lm_head_q, out=self.logits[:B], ws=self.ws)
         return torch.matmul(xs, self.lm_head_dense.T, out=self.logits[:B])
 
     def sample(self, st: StepInputs, m: dict, logits: torch.Tensor) -> torch.Tensor:
@@ -507,12 +515,12 @@ class TorchPagedRunner:
                                     bad[i, ctx - n + j] = True
                 s = s.masked_fill(bad[None], float("-inf"))
                 attn[r0:r0 + n] = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), V).reshape(n, hq * d)
-            h = h + attn @ w[p + "self_attn.o_proj.weight"].T
+            h = h + self.ref._rp(attn, w[p + "self_attn.o_proj.weight"])
             x = _rms(h, w[p + "post_attention_layernorm.weight"], cfg.rms_eps)
             h = h + self.ref._mlp(p, x)
         rows = torch.from_numpy(st.logits_rows.astype(np.int64))
         xs = _rms(h[rows], w["model.norm.weight"], cfg.rms_eps)
-        logits = xs @ w["lm_head.weight"].T
+        logits = self.ref._head(xs, w["lm_head.weight"])
         self.logits = logits.to(torch.bfloat16)
         self.last_logits = logits
         self.last_hidden = xs

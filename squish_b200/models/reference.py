@@ -72,12 +72,23 @@ class ReferenceModel:
         return [{"k": torch.zeros(0, self.cfg.num_kv_heads, self.cfg.head_dim),
                  "v": torch.zeros(0, self.cfg.num_kv_heads, self.cfg.head_dim)} for _ in range(self.cfg.num_layers)]
 
+    # tensor-parallel hooks (set by the CPU tensor-parallel runner): row-parallel matmul
+    # with an all-reduce, and the vocab-parallel LM head with a gather
+    rp_hook = None
+    head_hook = None
+
+    def _rp(self, x: torch.Tensor, wt: torch.Tensor) -> torch.Tensor:
+        return x @ wt.T if self.rp_hook is None else self.rp_hook(x, wt)
+
+    def _head(self, x: torch.Tensor, wt: torch.Tensor) -> torch.Tensor:
+        return x @ wt.T if self.head_hook is None else self.head_hook(x, wt)
+
     def _mlp(self, p: str, x: torch.Tensor) -> torch.Tensor:
         cfg, w = self.cfg, self.w
         if not cfg.is_moe:
             g = x @ w[p + "mlp.gate_proj.weight"].T
             u = x @ w[p + "mlp.up_proj.weight"].T
-            return (torch.nn.functional.silu(g) * u) @ w[p + "mlp.down_proj.weight"].T
+            return self._rp((torch.nn.functional.silu(g) * u), w[p + "mlp.down_proj.weight"])
         logits = x @ w[p + "mlp.gate.weight"].T
         probs = torch.softmax(logits, dim=-1)
         topv, topi = probs.topk(cfg.num_experts_per_tok, dim=-1)

@@ -1,0 +1,60 @@
+"""Tensor-parallel model runners: the single-GPU runner over this rank's shard, with the
+row-parallel outputs all-reduced and the vocab-parallel logits gathered.
+
+``TPCudaRunner``: o_proj and down_proj run as one fused GEMM+all-reduce over NVLink (or the
+NCCL baseline), the LM head computes this rank's vocabulary slice and the slices are
+gathered into a full logits row on every rank, so every rank samples the same tokens and
+the engine's host logic can run replicated on every rank. ``TorchTPRunner`` is the CPU
+(gloo) counterpart used to test the sharding end to end.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..models.decoder import CudaRunner, TorchPagedRunner
+from ..models.weights import Checkpoint
+from .comm import TPComm
+from .shard import shard_checkpoint
+
+
+class TPCudaRunner(CudaRunner):
+    def __init__(self, ck: Checkpoint, device, num_pages: int, comm: TPComm, **kw):
+        self.full_cfg = ck.config
+        self.comm = comm
+        local = shard_checkpoint(ck, comm.rank, comm.tp)
+        super().__init__(local, device, num_pages, **kw)
+        R = self.logits.shape[0]
+        self.logits_local = torch.empty(R, comm.v1 - comm.v0, dtype=torch.bfloat16, device=self.device)
+        del self.logits
+        self.logits = comm.logits_full
+
+    def _row_parallel(self, x, w, h):
+        self.comm.gemm_allreduce(x, w, h, self.ws)
+
+    def _lm_head(self, xs, B):
+        from .. import ops
+
+        if self.lm_head_q is not None:
+            loc = ops.w4a16_linear(xs, self.lm_head_q, out=self.logits_local[:B], ws=self.ws)
+        else:
+            loc = torch.matmul(xs, self.lm_head_dense.T, out=self.logits_local[:B])
+        return self.comm.gather_logits(loc, B)
+
+
+class TorchTPRunner(TorchPagedRunner):
+    """CPU fp32 oracle runner over a shard, collectives on gloo."""
+
+    def __init__(self, ck: Checkpoint, num_pages: int, comm: TPComm, max_model_len: int = 2048):
+        self.comm = comm
+        local = shard_checkpoint(ck, comm.rank, comm.tp)
+        super().__init__(local, num_pages, max_model_len)
+        self.ref.rp_hook = self._rp
+        self.ref.head_hook = self._head
+
+    def _rp(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        out = torch.zeros(x.shape[0], w.shape[0])
+        self.comm.gemm_allreduce(x, w, out, None)
+        return out
+
+    def _head(self, xs: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        return self.comm.gather_logits(xs @ w.T, xs.shape[0]).clone()
