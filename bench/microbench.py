@@ -37,18 +37,33 @@ def peaks():
         return 6650.0, 1590.0, "of fallback"
 
 
-def time_op(fn, iters=20, warmup=5):
+def time_op(fn, iters=20, warmup=5, inner=8):
+    """Device time of one call: ``inner`` back-to-back calls are captured in a CUDA graph
+    (no host launch cost between them), the graph is replayed ``iters`` times, and the
+    median replay time / inner is returned."""
     for _ in range(warmup):
         fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g):
+        for _ in range(inner):
+            fn()
+    g.replay()
     torch.cuda.synchronize()
     ts = []
     for _ in range(iters):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        fn()
+        g.replay()
         b.record()
         b.synchronize()
-        ts.append(a.elapsed_time(b))
+        ts.append(a.elapsed_time(b) / inner)
     ts.sort()
     return ts[len(ts) // 2]
 
@@ -67,7 +82,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="qwen2.5-7b")
     ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--copies", type=int, default=4)
+    ap.add_argument("--copies", type=int, default=8, help="weight copies cycled (their total exceeds L2)")
     ap.add_argument("--json", default=None)
     ap.add_argument("--ms", default="1,16,64,128,512,2048")
     args = ap.parse_args()
@@ -80,7 +95,8 @@ def main():
     rows = []
     ms = [int(x) for x in args.ms.split(",")]
     for name, (n, k) in shapes.items():
-        copies = args.copies if name != "lm_head" else 2
+        wb = n * k // 2
+        copies = max(2, min(args.copies, -(-384 * 2**20 // wb)))  # > 3x L2 of weights in the rotation
         wts = rand_int4(n, k, q.group_size, dev, copies)
         for m in ms:
             if name == "lm_head" and m > 256:
@@ -93,7 +109,7 @@ def main():
                 ops.w4a16_linear(x, wts[it[0] % copies], out=y)
                 it[0] += 1
 
-            t = time_op(fn, args.iters)
+            t = time_op(fn, args.iters, inner=copies)
             wbytes = n * k / 2 + n * (k // q.group_size) * 4
             bytes_ = wbytes + m * k * 2 + m * n * 2
             flops = 2.0 * m * n * k

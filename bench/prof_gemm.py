@@ -40,10 +40,10 @@ def main():
         t = tr.view(16, 64).cpu()
         base = int(t[t > 0].min())
         names = ["w_issue", "x_issue", "mma_xfull", "mma_afull", "dq_wfull", "dq_aempty", "dq_afull", "acc_full",
-                 "dq_lds", "dq_arrw", "dq_sts", "dq_fence", "mma_iss", "mma_cmt", "w_top", "w_wait"]
+                 "dq_lds", "dq_arrw", "dq_sts", "dq_fence", "mma_iss", "mma_cmt", "setup_done", "exit"]
         for i in range(min(64, (a.k + 63) // 64)):
             print(i, " ".join(f"{n}={(int(t[j, i]) - base) if t[j, i] > 0 else -1}" for j, n in enumerate(names)
-                               if j != 7 or i == 0))
+                               if (j not in (7, 14, 15) or i == 0) and t[j, i] > 0))
     ops.workspace(dev).check()
     print("plan", ops.gemm_plan(a.m, a.n, a.k), "ok", tuple(y.shape))
 

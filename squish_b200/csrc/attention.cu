@@ -13,6 +13,7 @@
 // Softmax runs in the log2 domain (scores pre-multiplied by scale*log2(e), exp2f).
 #include "kernels.h"
 #include "kv_format.cuh"
+#include "launch.cuh"
 
 namespace sq {
 
@@ -51,6 +52,8 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
 // M side of each MMA = the G_q query heads of this KV head (padded to 16).
 template <int D, int FK, int FV>
 __global__ void __launch_bounds__(128) decode_kernel(const AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int LD = D + 8;
   constexpr int NWARP = 4;
   extern __shared__ __align__(16) uint8_t sm[];
@@ -243,6 +246,8 @@ __global__ void __launch_bounds__(128) decode_kernel(const AttnParams p) {
 
 // grid (B, Hq), D threads: combine split partials (log2-domain LSE weights).
 __global__ void decode_merge_kernel(const AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x, hq = blockIdx.y, d = threadIdx.x;
   const int D = p.D, S = p.splits;
   const size_t base = ((size_t)b * p.Hq + hq) * S;
@@ -270,6 +275,8 @@ constexpr int PK = 32;  // kv tokens per tile
 
 template <int D, int FK, int FV>
 __global__ void __launch_bounds__(256) prefill_kernel(const AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int LD = D + 8;
   extern __shared__ __align__(16) uint8_t sm[];
   const int tile = blockIdx.x;
@@ -502,10 +509,12 @@ cudaError_t launch_decode(const AttnParams& p, cudaStream_t s) {
   auto k = decode_kernel<D, FK, FV>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  k<<<dim3(p.B, p.Hkv, p.splits), 128, smem, s>>>(p);
+  cudaError_t le = launch_k(k, dim3(p.B, p.Hkv, p.splits), dim3(128), smem, s, 1, p);
+  if (le != cudaSuccess) return le;
   e = cudaGetLastError();
   if (e != cudaSuccess || p.splits == 1) return e;
-  decode_merge_kernel<<<dim3(p.B, p.Hq), D, 0, s>>>(p);
+  le = launch_k(decode_merge_kernel, dim3(p.B, p.Hq), dim3(D), 0, s, 1, p);
+  if (le != cudaSuccess) return le;
   return cudaGetLastError();
 }
 
@@ -519,7 +528,8 @@ cudaError_t launch_prefill(const AttnParams& p, cudaStream_t s) {
   const int Gq = p.Hq / p.Hkv;
   const int hblocks = (Gq + 7) / 8;
   const int warps = Gq < 8 ? Gq : 8;
-  k<<<dim3(p.n_tiles, p.Hkv * hblocks), warps * 32, smem, s>>>(p);
+  e = launch_k(k, dim3(p.n_tiles, p.Hkv * hblocks), dim3(warps * 32), smem, s, 1, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -26,6 +26,7 @@
 
 #include "comm.h"
 #include "sm100.cuh"
+#include "launch.cuh"
 
 namespace sq {
 
@@ -50,6 +51,8 @@ __device__ bool wait_flag(const int* f, int want, int* status) {
 }
 
 __global__ void __launch_bounds__(256) tp_reduce_kernel(const TpReduceParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int tile = blockIdx.x * gridDim.y + blockIdx.y;  // same numbering as the GEMM grid
   const int par = *reinterpret_cast<volatile const int*>(p.seq) & 1;
   const int tp = p.tp;
@@ -97,6 +100,8 @@ __global__ void __launch_bounds__(256) tp_reduce_kernel(const TpReduceParams p) 
 
 // src [rows, cols] is written into every rank's dst at rows row0.., columns col0..
 __global__ void __launch_bounds__(256) tp_gather_push_kernel(const TpGatherParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int par = __ldg(p.seq) & 1;
   const int vec = p.cols / 8;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.rows * vec; i += gridDim.x * blockDim.x) {
@@ -115,6 +120,8 @@ __global__ void __launch_bounds__(256) tp_gather_push_kernel(const TpGatherParam
 }
 
 __global__ void tp_gather_wait_kernel(const TpGatherParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int par = __ldg(p.seq) & 1;
   int* flags = p.local_flags + (size_t)par * p.flag_stride;
   if ((int)threadIdx.x < p.tp) {
@@ -132,16 +139,16 @@ __global__ void tp_gather_wait_kernel(const TpGatherParams p) {
 
 cudaError_t tp_reduce_launch(const TpReduceParams& p, int grid_x, int grid_y, cudaStream_t s) {
   if (p.tp > 256) return cudaErrorInvalidValue;
-  tp_reduce_kernel<<<dim3(grid_x, grid_y), 256, 0, s>>>(p);
+  SQ_LAUNCH(tp_reduce_kernel, dim3(dim3(grid_x, grid_y)), dim3(256), 0, s, 1, p);
   return cudaGetLastError();
 }
 
 cudaError_t tp_gather_launch(const TpGatherParams& p, cudaStream_t s) {
   if (p.cols % 8 || p.ld_src % 8 || p.ld_dst % 8 || p.col0 % 8) return cudaErrorInvalidValue;
-  tp_gather_push_kernel<<<p.expect, 256, 0, s>>>(p);
+  SQ_LAUNCH(tp_gather_push_kernel, dim3(p.expect), dim3(256), 0, s, 1, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  tp_gather_wait_kernel<<<1, 32, 0, s>>>(p);
+  SQ_LAUNCH(tp_gather_wait_kernel, dim3(1), dim3(32), 0, s, 1, p);
   return cudaGetLastError();
 }
 

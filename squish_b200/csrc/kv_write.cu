@@ -8,6 +8,7 @@
 // once, already compressed, and never materialised in fp16.
 #include "kv_format.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace sq {
 
@@ -110,6 +111,8 @@ __device__ void quant_row(const float (&v)[D / 32], int fmt, int G, uint8_t* cod
 
 template <int D>
 __global__ void rope_kv_write_kernel(RopeKvParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int J = D / 32;
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -180,6 +183,8 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const __nv_bfloat16* __res
                                                       const __nv_bfloat16* __restrict__ w,
                                                       __nv_bfloat16* __restrict__ y, const int* __restrict__ row_idx,
                                                       int rows, int H, int ldx, int ldy, float eps) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[4];
   const int r = blockIdx.x;
   const int src = row_idx ? row_idx[r] : r;
@@ -235,10 +240,10 @@ cudaError_t rope_kv_write_launch(const RopeKvParams& p, int T, cudaStream_t s) {
   const int threads = 128;
   const dim3 grid(T, (p.Hq + 2 * p.Hkv + 3) / 4);
   switch (p.D) {
-    case 32: rope_kv_write_kernel<32><<<grid, threads, 0, s>>>(p); break;
-    case 64: rope_kv_write_kernel<64><<<grid, threads, 0, s>>>(p); break;
-    case 128: rope_kv_write_kernel<128><<<grid, threads, 0, s>>>(p); break;
-    case 256: rope_kv_write_kernel<256><<<grid, threads, 0, s>>>(p); break;
+    case 32: SQ_LAUNCH(rope_kv_write_kernel<32>, dim3(grid), dim3(threads), 0, s, 1, p); break;
+    case 64: SQ_LAUNCH(rope_kv_write_kernel<64>, dim3(grid), dim3(threads), 0, s, 1, p); break;
+    case 128: SQ_LAUNCH(rope_kv_write_kernel<128>, dim3(grid), dim3(threads), 0, s, 1, p); break;
+    case 256: SQ_LAUNCH(rope_kv_write_kernel<256>, dim3(grid), dim3(threads), 0, s, 1, p); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -248,10 +253,10 @@ cudaError_t rmsnorm_launch(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_
                            int rows, int H, int ldx, int ldy, float eps, cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
   const int nv = H / 8;
-  if (nv <= 128) rmsnorm_kernel<1><<<rows, 128, 0, s>>>(x, w, y, row_idx, rows, H, ldx, ldy, eps);
-  else if (nv <= 256) rmsnorm_kernel<2><<<rows, 128, 0, s>>>(x, w, y, row_idx, rows, H, ldx, ldy, eps);
-  else if (nv <= 512) rmsnorm_kernel<4><<<rows, 128, 0, s>>>(x, w, y, row_idx, rows, H, ldx, ldy, eps);
-  else if (nv <= 1024) rmsnorm_kernel<8><<<rows, 128, 0, s>>>(x, w, y, row_idx, rows, H, ldx, ldy, eps);
+  if (nv <= 128) SQ_LAUNCH(rmsnorm_kernel<1>, dim3(rows), dim3(128), 0, s, 1, x, w, y, row_idx, rows, H, ldx, ldy, eps);
+  else if (nv <= 256) SQ_LAUNCH(rmsnorm_kernel<2>, dim3(rows), dim3(128), 0, s, 1, x, w, y, row_idx, rows, H, ldx, ldy, eps);
+  else if (nv <= 512) SQ_LAUNCH(rmsnorm_kernel<4>, dim3(rows), dim3(128), 0, s, 1, x, w, y, row_idx, rows, H, ldx, ldy, eps);
+  else if (nv <= 1024) SQ_LAUNCH(rmsnorm_kernel<8>, dim3(rows), dim3(128), 0, s, 1, x, w, y, row_idx, rows, H, ldx, ldy, eps);
   else return cudaErrorInvalidValue;
   return cudaGetLastError();
 }

@@ -18,6 +18,7 @@
 #include <cstdint>
 
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace sq {
 
@@ -27,6 +28,8 @@ template <int EPL>
 __global__ void __launch_bounds__(256) moe_route_kernel(const __nv_bfloat16* __restrict__ logits, int ld, int T,
                                                         int E, int K, int renorm, int* __restrict__ topk_ids,
                                                         float* __restrict__ topk_w) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + warp;
   if (t >= T) return;
@@ -86,6 +89,8 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int* __restrict__
                                                          int max_tiles, int* __restrict__ sorted_slot,
                                                          int* __restrict__ slot_pos, int* __restrict__ tile_expert,
                                                          int* __restrict__ num_tiles, int* __restrict__ counts) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int sh[];
   int* cnt = sh;           // [E]
   int* off = sh + E;       // [E + 1]
@@ -147,6 +152,8 @@ __global__ void __launch_bounds__(128) moe_gather_kernel(const __nv_bfloat16* __
                                                          const int* __restrict__ sorted_slot,
                                                          const int* __restrict__ num_tiles, int bn, int K, int H,
                                                          __nv_bfloat16* __restrict__ xs, int ldxs) {
+  pdl_wait();
+  pdl_trigger();
   const int rows = __ldg(num_tiles) * bn;
   const int vec = H / 8;
   for (int rr = 0; rr < 4; ++rr) {
@@ -167,6 +174,8 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const __nv_bfloat16* _
                                                           const int* __restrict__ slot_pos,
                                                           const float* __restrict__ topk_w, int K, int H,
                                                           __nv_bfloat16* __restrict__ h, int ldh) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int vec = H / 8;
   for (int c = threadIdx.x; c < vec; c += blockDim.x) {
@@ -208,16 +217,16 @@ cudaError_t moe_route_launch(const __nv_bfloat16* logits, int ld, int T, int E, 
   if (T == 0) return cudaSuccess;
   if (E > 256 || K > 32 || K > E) return cudaErrorInvalidValue;
   const dim3 grid((T + 7) / 8);
-  if (E <= 64) moe_route_kernel<2><<<grid, 256, 0, s>>>(logits, ld, T, E, K, renorm, topk_ids, topk_w);
-  else if (E <= 128) moe_route_kernel<4><<<grid, 256, 0, s>>>(logits, ld, T, E, K, renorm, topk_ids, topk_w);
-  else moe_route_kernel<8><<<grid, 256, 0, s>>>(logits, ld, T, E, K, renorm, topk_ids, topk_w);
+  if (E <= 64) SQ_LAUNCH(moe_route_kernel<2>, dim3(grid), dim3(256), 0, s, 1, logits, ld, T, E, K, renorm, topk_ids, topk_w);
+  else if (E <= 128) SQ_LAUNCH(moe_route_kernel<4>, dim3(grid), dim3(256), 0, s, 1, logits, ld, T, E, K, renorm, topk_ids, topk_w);
+  else SQ_LAUNCH(moe_route_kernel<8>, dim3(grid), dim3(256), 0, s, 1, logits, ld, T, E, K, renorm, topk_ids, topk_w);
   return cudaGetLastError();
 }
 
 cudaError_t moe_align_launch(const int* ids, int TK, int E, int bn, int max_tiles, int* sorted_slot, int* slot_pos,
                              int* tile_expert, int* num_tiles, int* counts, cudaStream_t s) {
   const size_t smem = (size_t)(3 * E + 1) * sizeof(int);
-  moe_align_kernel<<<1, 1024, smem, s>>>(ids, TK, E, bn, max_tiles, sorted_slot, slot_pos, tile_expert, num_tiles,
+  SQ_LAUNCH(moe_align_kernel, dim3(1), dim3(1024), smem, s, 1, ids, TK, E, bn, max_tiles, sorted_slot, slot_pos, tile_expert, num_tiles,
                                          counts);
   return cudaGetLastError();
 }
@@ -226,7 +235,7 @@ cudaError_t moe_gather_launch(const __nv_bfloat16* x, int ldx, const int* sorted
                               int max_rows, int bn, int K, int H, __nv_bfloat16* xs, int ldxs, cudaStream_t s) {
   if (H % 8 || ldx % 8 || ldxs % 8) return cudaErrorInvalidValue;
   if (max_rows == 0) return cudaSuccess;
-  moe_gather_kernel<<<(max_rows + 3) / 4, 128, 0, s>>>(x, ldx, sorted_slot, num_tiles, bn, K, H, xs, ldxs);
+  SQ_LAUNCH(moe_gather_kernel, dim3((max_rows + 3) / 4), dim3(128), 0, s, 1, x, ldx, sorted_slot, num_tiles, bn, K, H, xs, ldxs);
   return cudaGetLastError();
 }
 
@@ -234,7 +243,7 @@ cudaError_t moe_combine_launch(const __nv_bfloat16* ys, int ldys, const int* slo
                                int K, int H, __nv_bfloat16* h, int ldh, cudaStream_t s) {
   if (H % 8 || ldys % 8 || ldh % 8) return cudaErrorInvalidValue;
   if (T == 0) return cudaSuccess;
-  moe_combine_kernel<<<T, 256, 0, s>>>(ys, ldys, slot_pos, topk_w, K, H, h, ldh);
+  SQ_LAUNCH(moe_combine_kernel, dim3(T), dim3(256), 0, s, 1, ys, ldys, slot_pos, topk_w, K, H, h, ldh);
   return cudaGetLastError();
 }
 

@@ -14,6 +14,7 @@
 //   kept tokens above tau. The draw is Gumbel-max over the kept set, which samples exactly
 //   from the renormalised distribution. Temperature <= 0 means greedy (argmax).
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace sq {
 
@@ -62,6 +63,8 @@ struct ArgMax {
 };
 
 __global__ void __launch_bounds__(kThreads) sampler_kernel(const SamplerParams p, float* __restrict__ work) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float shf[32];
   __shared__ int shi[32];
   __shared__ unsigned int hist[256];
@@ -286,7 +289,7 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const SamplerParams p
 
 cudaError_t sampler_launch(const SamplerParams& p, float* work, cudaStream_t s) {
   if (p.B == 0) return cudaSuccess;
-  sampler_kernel<<<p.B, kThreads, 0, s>>>(p, work);
+  SQ_LAUNCH(sampler_kernel, dim3(p.B), dim3(kThreads), 0, s, 1, p, work);
   return cudaGetLastError();
 }
 

@@ -71,14 +71,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that lets the hardware suspend the thread until the phase completes or
+// kSuspendNs pass, so a waiting warp takes no issue slots from the working ones.
+constexpr uint32_t kSuspendNs = 20000;
+constexpr uint32_t kMaxSuspends = 1u << 16;  // x 20 us: about a second, then report
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait. Returns false (and records `code` in *status) on timeout. The status word
-// (global memory) is polled only every 4096 spins, so a normal hand-off costs one
+// (global memory) is polled only every 256 suspended tries, so a normal hand-off costs one
 // try_wait, not an L2 round trip.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  for (uint32_t i = 1; i < kMaxSpin; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 4095u) == 0 && *reinterpret_cast<volatile int*>(status) != SQ_OK) return false;
+  for (uint32_t i = 1; i < kMaxSuspends; ++i) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if ((i & 255u) == 0 && *reinterpret_cast<volatile int*>(status) != SQ_OK) return false;
   }
   atomicCAS(status, SQ_OK, code);
   return false;
@@ -207,6 +222,27 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// D(tmem) (+)= A(tmem) x B(smem): the A operand read from tensor memory (lane = row of A,
+// each 32-bit column holds two consecutive K elements, the lower one in bits 15:0).
+__device__ __forceinline__ void mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Each thread stores 16 consecutive 32-bit columns of its own lane (its warp's 32-lane slice).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }

@@ -29,6 +29,7 @@
 #include <cstdint>
 
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace sq {
 
@@ -130,6 +131,8 @@ __device__ float2 softmax_stats(const __nv_bfloat16* row, int V, float invT, flo
 }
 
 __global__ void __launch_bounds__(kVThreads) tree_verify_kernel(const TreeVerifyParams p) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ ArgMax sha[32];
   __shared__ float shf[32];
   __shared__ int children[kMaxTreeNodes];
@@ -256,6 +259,8 @@ __global__ void __launch_bounds__(kVThreads) tree_verify_kernel(const TreeVerify
 }
 
 __global__ void kv_compact_kernel(const KvCompactParams p) {
+  pdl_wait();
+  pdl_trigger();
   // grid (layers, Hkv); pairs copied in order
   const int layer = blockIdx.x, h = blockIdx.y;
   const KvLayerPtrs L = p.layers[layer];
@@ -276,13 +281,13 @@ __global__ void kv_compact_kernel(const KvCompactParams p) {
 
 cudaError_t tree_verify_launch(const TreeVerifyParams& p, int groups, cudaStream_t s) {
   if (groups == 0) return cudaSuccess;
-  tree_verify_kernel<<<groups, kVThreads, 0, s>>>(p);
+  SQ_LAUNCH(tree_verify_kernel, dim3(groups), dim3(kVThreads), 0, s, 1, p);
   return cudaGetLastError();
 }
 
 cudaError_t kv_compact_launch(const KvCompactParams& p, int layers, cudaStream_t s) {
   if (p.n_pairs == 0 || layers == 0) return cudaSuccess;
-  kv_compact_kernel<<<dim3(layers, p.Hkv), 128, 0, s>>>(p);
+  SQ_LAUNCH(kv_compact_kernel, dim3(dim3(layers, p.Hkv)), dim3(128), 0, s, 1, p);
   return cudaGetLastError();
 }
 

@@ -28,8 +28,12 @@
 // Decode shapes (BN <= 64) run two CTAs per SM (small rings), so two independent
 // pipelines hide each other's hand-off latency. Every wait is bounded (sm100.cuh); on
 // timeout *status is set and the kernel still releases its TMEM before exiting.
+#include <cstdio>
+#include <cstdlib>
+
 #include "sm100.cuh"
 #include "w4a16_gemm.h"
+#include "launch.cuh"
 
 namespace sq {
 
@@ -48,11 +52,13 @@ struct Cfg {
   static constexpr int kDqWarps = 8;      // dequant warps 4..11; thread -> (row, half of the 64 columns)
   static constexpr int kThreads = 128 + 32 * kDqWarps;
   static constexpr int kXBytes = BN * 128;
-  static constexpr int kTmemCols = (NT * BN <= 32)    ? 32
-                                   : (NT * BN <= 64)  ? 64
-                                   : (NT * BN <= 128) ? 128
-                                   : (NT * BN <= 256) ? 256
-                                                      : 512;
+  // Single weight tile per CTA: the dequantized A operand goes to tensor memory (tcgen05.st)
+  // instead of shared memory; columns [kA0, kA0 + 32 * ring_a) hold the A ring.
+  static constexpr bool AT = (NT == 1);
+  static constexpr int kMaxRingA = 4;
+  static constexpr int kA0 = AT ? (NT * BN < 32 ? 32 : NT * BN) : 0;
+  static constexpr int kCols = AT ? kA0 + 32 * kMaxRingA : NT * BN;
+  static constexpr int kTmemCols = (kCols <= 32) ? 32 : (kCols <= 64) ? 64 : (kCols <= 128) ? 128 : (kCols <= 256) ? 256 : 512;
 };
 
 __host__ __device__ constexpr int tile_bytes(int gpk) { return W_TILE_BYTES + gpk * BM * 4; }
@@ -61,9 +67,10 @@ struct Layout {
   uint32_t x_off, w_off, w_stage, bar_off, trace_off, total;
 };
 
-__host__ __device__ inline Layout make_layout(int bn, int nt, int gpk, int rw, int rx, int ra, bool trace) {
+__host__ __device__ inline Layout make_layout(int bn, int nt, int gpk, int rw, int rx, int ra, bool trace,
+                                              bool a_in_tmem) {
   Layout L;
-  L.x_off = (uint32_t)(ra * nt * A_TILE_BYTES);
+  L.x_off = a_in_tmem ? 0u : (uint32_t)(ra * nt * A_TILE_BYTES);
   L.w_off = L.x_off + (uint32_t)(rx * bn * 128);
   L.w_stage = (uint32_t)(nt * tile_bytes(gpk));
   L.bar_off = L.w_off + (uint32_t)rw * L.w_stage;
@@ -146,6 +153,11 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
   constexpr int BN = C::BN;
   constexpr int NT = C::NT;
   const uint8_t* wbase = reinterpret_cast<const uint8_t*>(p.wq);
+  // Programmatic dependent launch: weights are static, so the plain mode streams them before
+  // waiting for the previous kernel; only the activation loads (warp 1) and the epilogue
+  // wait. Grouped and push modes read predecessor data (tile table, op counter) up front.
+  const bool early_wait = (p.tile_expert != nullptr) || (p.push_dst != nullptr);
+  if (early_wait) pdl_wait();
   if (p.tile_expert != nullptr) {  // grouped mode: whole CTA leaves before any setup
     if ((int)blockIdx.y >= __ldg(p.num_tiles)) return;
     wbase += (size_t)__ldg(p.tile_expert + blockIdx.y) * (size_t)p.expert_stride;
@@ -155,8 +167,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
 
   const int gpk = p.gpk;
   const int ring_w = p.ring_w, ring_x = p.ring_x, ring_a = p.ring_a;
-  const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a, p.trace != nullptr);
-  uint8_t* a_ring = smem;
+  const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a, p.trace != nullptr, C::AT);
+  uint8_t* a_ring = smem;  // (shared-memory A ring; with C::AT the region starts the X ring)
   uint8_t* x_ring = smem + L.x_off;
   uint8_t* w_ring = smem + L.w_off;
   uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
@@ -207,6 +219,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int tbytes = tile_bytes(gpk);
+  if (threadIdx.x == 0) trace_mark(str, 14, 0);  // setup done
+  pdl_trigger();
 
   // Warps 0-2 run converged: every lane waits, one elected lane issues (tensor-core and
   // bulk-copy instructions are issued by one thread of a converged warp).
@@ -233,6 +247,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     }
   } else if (warp == 1) {
     // ------------------------------------------------ activation producer (TMA)
+    pdl_wait();  // activations come from the previous kernel
     Ring r(ring_x);
     for (int i = 0; i < nkb; ++i) {
       if (!mbar_wait(&x_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_X)) break;
@@ -256,13 +271,20 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       tc_fence_after();
       if (elect_one()) {
         const uint32_t xa = smem_u32(x_ring + rx.s * C::kXBytes);
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const uint32_t aa = smem_u32(a_ring + (ra.s * NT + t) * A_TILE_BYTES);
+        if constexpr (C::AT) {
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            mma_bf16_ss(tmem + t * BN, sdesc_sw128(aa + k * 32), sdesc_sw128(xa + k * 32), idesc,
+            mma_bf16_ts(tmem, tmem + (uint32_t)(C::kA0 + ra.s * 32 + k * 8), sdesc_sw128(xa + k * 32), idesc,
                         (i > 0 || k > 0) ? 1u : 0u);
+        } else {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const uint32_t aa = smem_u32(a_ring + (ra.s * NT + t) * A_TILE_BYTES);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              mma_bf16_ss(tmem + t * BN, sdesc_sw128(aa + k * 32), sdesc_sw128(xa + k * 32), idesc,
+                          (i > 0 || k > 0) ? 1u : 0u);
+          }
         }
         mma_commit(&x_empty[rx.s]);
         mma_commit(&a_empty[ra.s]);
@@ -293,25 +315,44 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         const uint4 wv = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 16);
         const uint32_t* szt = reinterpret_cast<const uint32_t*>(tb + W_TILE_BYTES);
         const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        if (gpk == 1) {  // one (scale, zero) group covers the whole 64-column k-block
+          const uint32_t szw = szt[r];
+          const __nv_bfloat162 s2 = __bfloat162bfloat162(__ushort_as_bfloat16((unsigned short)(szw & 0xFFFFu)));
+          const __nv_bfloat162 z2 = __bfloat162bfloat162(__ushort_as_bfloat16((unsigned short)(szw >> 16)));
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const uint32_t szw = szt[(((c * 4 + w) * gpk) >> 3) * BM + r];
-          const __nv_bfloat16 sc = __ushort_as_bfloat16((unsigned short)(szw & 0xFFFFu));
-          const __nv_bfloat16 ze = __ushort_as_bfloat16((unsigned short)(szw >> 16));
-          o[t][w] = dq_word(ww[w], __bfloat162bfloat162(sc), __bfloat162bfloat162(ze));
+          for (int w = 0; w < 4; ++w) o[t][w] = dq_word(ww[w], s2, z2);
+        } else {
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const uint32_t szw = szt[(((c * 4 + w) * gpk) >> 3) * BM + r];
+            const __nv_bfloat16 sc = __ushort_as_bfloat16((unsigned short)(szw & 0xFFFFu));
+            const __nv_bfloat16 ze = __ushort_as_bfloat16((unsigned short)(szw >> 16));
+            o[t][w] = dq_word(ww[w], __bfloat162bfloat162(sc), __bfloat162bfloat162(ze));
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&w_empty[rw.s]);  // raw tile consumed (one arrive per warp)
       if (!mbar_wait(&a_empty[ra.s], ra.ph ^ 1u, status, SQ_ERR_TIMEOUT_A)) break;
       if (d == 0) trace_mark(str, 5, i);
+      if constexpr (C::AT) {
+        // this thread's 32 K values of row r = 16 columns of its lane in the A ring stage
+        tc_fence_after();
+        const uint32_t regs[16] = {o[0][0].x, o[0][0].y, o[0][0].z, o[0][0].w, o[0][1].x, o[0][1].y,
+                                   o[0][1].z, o[0][1].w, o[0][2].x, o[0][2].y, o[0][2].z, o[0][2].w,
+                                   o[0][3].x, o[0][3].y, o[0][3].z, o[0][3].w};
+        tmem_st16(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(C::kA0 + ra.s * 32 + c * 16), regs);
+        tmem_wait_st();
+        tc_fence_before();
+      } else {
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        uint8_t* adst = a_ring + (ra.s * NT + t) * A_TILE_BYTES + row_off;
+        for (int t = 0; t < NT; ++t) {
+          uint8_t* adst = a_ring + (ra.s * NT + t) * A_TILE_BYTES + row_off;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) *reinterpret_cast<uint4*>(adst + (((c * 4 + w) ^ sw_row) << 4)) = o[t][w];
+          for (int w = 0; w < 4; ++w) *reinterpret_cast<uint4*>(adst + (((c * 4 + w) ^ sw_row) << 4)) = o[t][w];
+        }
+        fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core (async proxy)
       }
-      fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core (async proxy)
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[ra.s]);
       if (d == 0) trace_mark(str, 6, i);
@@ -320,6 +361,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     }
   }
 
+  pdl_wait();  // (already satisfied) residual reads and output writes follow
   // ------------------------------------------------ epilogue: warps 4..7 = TMEM lane quarters
   if (warp >= 4 && warp < 8) {
     const int q = warp & 3;
@@ -408,29 +450,36 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       const int j0 = split * jb, j1 = min(BN, j0 + jb);
       const int m0 = mblk * BN;
       const uint32_t base = smem_u32(a_ring);
+      // Remote partials are read with every split's load issued before any is consumed, so
+      // the S distributed-shared-memory round trips overlap instead of chaining.
       auto ld_part = [&](int s, int idx) -> float {
         uint32_t ra, val;
         asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(base + idx * 4), "r"(s));
         asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(val) : "r"(ra) : "memory");
         return __uint_as_float(val);
       };
+      auto sum_parts = [&](int idx) -> float {
+        float v[8];
+#pragma unroll
+        for (int s = 0; s < 8; ++s) v[s] = (s < S) ? ld_part(s, idx) : 0.f;
+        float acc = 0.f;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) acc += v[s];  // split order: deterministic
+        return acc;
+      };
       if (p.epilogue == EPI_SILU_MUL) {
         for (int idx = threadIdx.x; idx < (j1 - j0) * 64; idx += blockDim.x) {
           const int j = j0 + idx / 64, r = idx % 64;
           const int m = m0 + j, nn = nblk * 64 + r;
-          float g = 0.f, u = 0.f;
-          for (int s = 0; s < S; ++s) {
-            g += ld_part(s, j * BM + r);
-            u += ld_part(s, j * BM + r + 64);
-          }
+          const float g = sum_parts(j * BM + r);
+          const float u = sum_parts(j * BM + r + 64);
           if (m < p.M && nn < (p.N >> 1)) p.y[(size_t)m * p.ldy + nn] = __float2bfloat16(silu(g) * u);
         }
       } else {
         for (int idx = threadIdx.x; idx < (j1 - j0) * BM; idx += blockDim.x) {
           const int j = j0 + idx / BM, r = idx % BM;
           const int m = m0 + j, n = nblk * BM + r;
-          float acc = 0.f;
-          for (int s = 0; s < S; ++s) acc += ld_part(s, j * BM + r);
+          float acc = sum_parts(j * BM + r);
           if (m < p.M && n < p.N) {
             acc += p.bias ? __bfloat162float(p.bias[n]) : 0.f;
             if (p.residual) acc += __bfloat162float(p.residual[(size_t)m * p.ldr + n]);
@@ -449,6 +498,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace_mark(str, 15, 0);  // epilogue done
+  __syncthreads();
   if (str != nullptr)
     for (int i = threadIdx.x; i < 16 * 64; i += blockDim.x) p.trace[i] = str[i];
   if (warp == 3) tmem_dealloc(tmem, C::kTmemCols);
@@ -459,45 +510,60 @@ cudaError_t launch_cfg(const CUtensorMap& xmap, W4A16Params p, int rw, int rx, i
   p.ring_w = rw;
   p.ring_x = rx;
   p.ring_a = ra;
-  const Layout L = make_layout(C::BN, C::NT, p.gpk, rw, rx, ra, p.trace != nullptr);
+  const Layout L = make_layout(C::BN, C::NT, p.gpk, rw, rx, ra, p.trace != nullptr, C::AT);
+  if (C::AT) {
+    // the A ring lives in TMEM; the epilogue stages through the (then idle) X + W rings
+    if (ra > C::kMaxRingA || L.bar_off < (uint32_t)(C::BN * BM * 4) || L.bar_off < 16u * BM * 4u)
+      return cudaErrorInvalidConfiguration;
+  }
   const size_t smem = (size_t)L.total + 1024;  // + alignment slack
   if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
   auto kern = w4a16_gemm_kernel<C>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
+  // all of the SM's unified L1/shared storage as shared memory, so kMinBlocks CTAs fit
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e != cudaSuccess) return e;
   dim3 grid((p.N + BM * C::NT - 1) / (BM * C::NT), (p.M + C::BN - 1) / C::BN, p.splits);
-  if (p.splits == 1) {
-    kern<<<grid, C::kThreads, smem, stream>>>(xmap, p);
-    return cudaGetLastError();
-  }
-  if (C::NT != 1 || p.splits > 8) return cudaErrorInvalidConfiguration;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(C::kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = (unsigned)p.splits;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, xmap, p);
+  if (p.splits > 1 && (C::NT != 1 || p.splits > 8)) return cudaErrorInvalidConfiguration;
+  return launch_k(kern, grid, dim3(C::kThreads), smem, stream, (unsigned)p.splits, xmap, p);
 }
 
 }  // namespace
 
-// Ring depths (stages): W = nt*(4 KiB + gpk*512 B), X = bn*128 B, A = nt*16 KiB.
-// BN <= 64 (decode): ~95-105 KiB per CTA so two CTAs share an SM.
+// Ring depths (stages): W = nt*(4 KiB + gpk*512 B), X = bn*128 B, A = nt*16 KiB (shared memory
+// only when NT = 2; single-tile configs keep the A ring in tensor memory). Decode shapes
+// (BN <= 64) and BN = 128 fit two CTAs per SM.
+// Tuning override for experiments: SQ_GEMM_RINGS="w,x,a" replaces the decode (BN <= 64)
+// ring depths; invalid or oversized settings fail the launch instead of running.
+static bool ring_override(int* w, int* x, int* a) {
+  static int v[3] = {-1, -1, -1};
+  static bool read = false;
+  if (!read) {
+    read = true;
+    if (const char* e = std::getenv("SQ_GEMM_RINGS")) {
+      if (std::sscanf(e, "%d,%d,%d", &v[0], &v[1], &v[2]) != 3 || v[0] < 2 || v[1] < 2 || v[2] < 2) v[0] = -1;
+    }
+  }
+  if (v[0] < 0) return false;
+  *w = v[0];
+  *x = v[1];
+  *a = v[2];
+  return true;
+}
+
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s) {
+  int ow, ox, oa;
+  const bool ov = ring_override(&ow, &ox, &oa);
   if (nt == 1) {
     switch (bn) {
-      case 16: return launch_cfg<Cfg<16, 1, 2>>(xmap, p, 8, 4, 3, s);
-      case 32: return launch_cfg<Cfg<32, 1, 2>>(xmap, p, 8, 4, 3, s);
-      case 64: return launch_cfg<Cfg<64, 1, 2>>(xmap, p, p.gpk >= 2 ? 6 : 8, 3, 3, s);
-      case 128: return launch_cfg<Cfg<128, 1, 1>>(xmap, p, 8, 4, 3, s);
-      case 256: return launch_cfg<Cfg<256, 1, 1>>(xmap, p, 6, 3, 2, s);
+      case 16: return ov ? launch_cfg<Cfg<16, 1, 2>>(xmap, p, ow, ox, oa, s) : launch_cfg<Cfg<16, 1, 2>>(xmap, p, 8, 8, 4, s);
+      case 32: return ov ? launch_cfg<Cfg<32, 1, 2>>(xmap, p, ow, ox, oa, s) : launch_cfg<Cfg<32, 1, 2>>(xmap, p, 8, 6, 4, s);
+      case 64:
+        if (ov) return launch_cfg<Cfg<64, 1, 2>>(xmap, p, ow, ox, oa, s);
+        return launch_cfg<Cfg<64, 1, 2>>(xmap, p, 8, 6, 4, s);
+      case 128: return launch_cfg<Cfg<128, 1, 2>>(xmap, p, 8, 4, 4, s);
+      case 256: return launch_cfg<Cfg<256, 1, 1>>(xmap, p, 6, 4, 4, s);
       default: return cudaErrorInvalidValue;
     }
   } else if (nt == 2) {

@@ -183,6 +183,11 @@ class LLMEngine:
     # ------------------------------------------------------------------ requests
     def add_request(self, prompt: list[int], params: SamplingParams | None = None, rid: str | None = None) -> str:
         params = (params or SamplingParams()).validate()
+        if not prompt:
+            raise ValueError("empty prompt")
+        lo, hi = min(prompt), max(prompt)
+        if lo < 0 or hi >= self.cfg.vocab_size:
+            raise ValueError(f"token id out of range [0, {self.cfg.vocab_size}): {lo if lo < 0 else hi}")
         rid = rid or f"req-{next(self._ids)}"
         req = Request(rid, list(map(int, prompt)), params)
         self.scheduler.add(req)

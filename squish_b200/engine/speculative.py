@@ -259,10 +259,12 @@ class DraftModelProposer:
         import torch
 
         V = target.cfg.vocab_size
-        if draft_engine.cfg.vocab_size != V:
-            raise ValueError(f"draft vocabulary {draft_engine.cfg.vocab_size} != target vocabulary {V}")
+        self.vd = draft_engine.cfg.vocab_size
+        if self.vd > V:
+            raise ValueError(f"draft vocabulary {self.vd} exceeds the target vocabulary {V}")
         dev = getattr(draft_engine.runner, "device", torch.device("cpu"))
-        self.qbuf = torch.empty(target.ecfg.max_num_seqs * sc.k, V, dtype=torch.bfloat16, device=dev)
+        # q rows over the target vocabulary; ids the draft cannot emit keep q = 0 (logit -inf)
+        self.qbuf = torch.full((target.ecfg.max_num_seqs * sc.k, V), float("-inf"), dtype=torch.bfloat16, device=dev)
 
     def _seq(self, r):
         s = self.seqs.get(r.rid)
@@ -290,11 +292,14 @@ class DraftModelProposer:
             # the draft KV is valid for the common prefix of what it computed and the target tokens
             common = 0
             old = s.tokens
-            for a, b in zip(old[:keep], r.tokens[:keep]):
+            new = [t if t < self.vd else 0 for t in r.tokens]
+            for a, b in zip(old[:keep], new[:keep]):
                 if a != b:
                     break
                 common += 1
-            s.prompt, s.output = list(r.tokens), []
+            # ids the draft's vocabulary lacks (the target's may be larger) become id 0 there
+            s.prompt = [t if t < self.vd else 0 for t in r.tokens]
+            s.output = []
             s.num_computed = common
             s.params.temperature = r.params.temperature
             seqs.append(s)
@@ -314,7 +319,7 @@ class DraftModelProposer:
             for i, e in enumerate(order):
                 si = seqs.index(e.req)
                 row = si * sc.k + j
-                self.qbuf[row].copy_(logits[i])
+                self.qbuf[row, : self.vd].copy_(logits[i, : self.vd])
                 drafts[si].append(int(toks[i]))
                 qrows[si].append(row)
                 e.req.num_computed = e.start + e.n
