@@ -44,12 +44,13 @@ constexpr int BK = 64;                     // K per stage = one 128-byte bf16 sw
 constexpr int W_TILE_BYTES = BM * BK / 2;  // 4096 nibble bytes per tile
 constexpr int A_TILE_BYTES = BM * BK * 2;  // 16384
 
-template <int BN_, int NT_, int MINB_>
+template <int BN_, int NT_, int MINB_, int DQW_ = 8>
 struct Cfg {
   static constexpr int BN = BN_;
   static constexpr int NT = NT_;          // 128-row weight tiles per CTA
   static constexpr int kMinBlocks = MINB_;
-  static constexpr int kDqWarps = 8;      // dequant warps 4..11; thread -> (row, half of the 64 columns)
+  static constexpr int kDqWarps = DQW_;   // dequant warps 4..; thread -> (row, 1/(DQW/4) of the 64 columns)
+  static constexpr int kWpt = 32 / DQW_;  // 32-bit nibble words per thread and tile (8 nibbles each)
   static constexpr int kThreads = 128 + 32 * kDqWarps;
   static constexpr int kXBytes = BN * 128;
   // Single weight tile per CTA: the dequantized A operand goes to tensor memory (tcgen05.st)
@@ -300,7 +301,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     // ------------------------------------------------ dequant warps
     const int d = threadIdx.x - 128;
     const int r = d & (BM - 1);
-    const int c = d >> 7;  // which 32-column half of the 64-column tile
+    constexpr int WPT = C::kWpt;
+    const int c = d >> 7;  // which part of the 64-column tile: words [c*WPT, c*WPT + WPT) of the row
     const int sw_row = r & 7;
     const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + sw_row * 128);
     Ring rw(ring_w), ra(ring_a);
@@ -308,23 +310,34 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       if (!mbar_wait(&w_full[rw.s], rw.ph, status, SQ_ERR_TIMEOUT_W)) break;
       if (d == 0) trace_mark(str, 4, i);
       const uint8_t* wst = w_ring + rw.s * L.w_stage;
-      uint4 o[NT][4];
+      uint4 o[NT][WPT];
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         const uint8_t* tb = wst + t * tbytes;
-        const uint4 wv = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 16);
+        // nibble words of a row: [2 halves][128 rows][4 words]
+        uint32_t ww[WPT];
+        if constexpr (WPT == 4) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 16);
+          ww[0] = wv.x;
+          ww[1] = wv.y;
+          ww[2] = wv.z;
+          ww[3] = wv.w;
+        } else {
+          const uint2 wv = *reinterpret_cast<const uint2*>(tb + ((c >> 1) * BM + r) * 16 + (c & 1) * 8);
+          ww[0] = wv.x;
+          ww[1] = wv.y;
+        }
         const uint32_t* szt = reinterpret_cast<const uint32_t*>(tb + W_TILE_BYTES);
-        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
         if (gpk == 1) {  // one (scale, zero) group covers the whole 64-column k-block
           const uint32_t szw = szt[r];
           const __nv_bfloat162 s2 = __bfloat162bfloat162(__ushort_as_bfloat16((unsigned short)(szw & 0xFFFFu)));
           const __nv_bfloat162 z2 = __bfloat162bfloat162(__ushort_as_bfloat16((unsigned short)(szw >> 16)));
 #pragma unroll
-          for (int w = 0; w < 4; ++w) o[t][w] = dq_word(ww[w], s2, z2);
+          for (int w = 0; w < WPT; ++w) o[t][w] = dq_word(ww[w], s2, z2);
         } else {
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const uint32_t szw = szt[(((c * 4 + w) * gpk) >> 3) * BM + r];
+          for (int w = 0; w < WPT; ++w) {
+            const uint32_t szw = szt[(((c * WPT + w) * gpk) >> 3) * BM + r];
             const __nv_bfloat16 sc = __ushort_as_bfloat16((unsigned short)(szw & 0xFFFFu));
             const __nv_bfloat16 ze = __ushort_as_bfloat16((unsigned short)(szw >> 16));
             o[t][w] = dq_word(ww[w], __bfloat162bfloat162(sc), __bfloat162bfloat162(ze));
@@ -336,12 +349,19 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       if (!mbar_wait(&a_empty[ra.s], ra.ph ^ 1u, status, SQ_ERR_TIMEOUT_A)) break;
       if (d == 0) trace_mark(str, 5, i);
       if constexpr (C::AT) {
-        // this thread's 32 K values of row r = 16 columns of its lane in the A ring stage
+        // this thread's 8*WPT K values of row r = 4*WPT columns of its lane in the A stage
         tc_fence_after();
-        const uint32_t regs[16] = {o[0][0].x, o[0][0].y, o[0][0].z, o[0][0].w, o[0][1].x, o[0][1].y,
-                                   o[0][1].z, o[0][1].w, o[0][2].x, o[0][2].y, o[0][2].z, o[0][2].w,
-                                   o[0][3].x, o[0][3].y, o[0][3].z, o[0][3].w};
-        tmem_st16(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(C::kA0 + ra.s * 32 + c * 16), regs);
+        const uint32_t col = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(C::kA0 + ra.s * 32 + c * WPT * 4);
+        if constexpr (WPT == 4) {
+          const uint32_t regs[16] = {o[0][0].x, o[0][0].y, o[0][0].z, o[0][0].w, o[0][1].x, o[0][1].y,
+                                     o[0][1].z, o[0][1].w, o[0][2].x, o[0][2].y, o[0][2].z, o[0][2].w,
+                                     o[0][3].x, o[0][3].y, o[0][3].z, o[0][3].w};
+          tmem_st16(col, regs);
+        } else {
+          const uint32_t regs[8] = {o[0][0].x, o[0][0].y, o[0][0].z, o[0][0].w,
+                                    o[0][1].x, o[0][1].y, o[0][1].z, o[0][1].w};
+          tmem_st8(col, regs);
+        }
         tmem_wait_st();
         tc_fence_before();
       } else {
@@ -349,7 +369,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         for (int t = 0; t < NT; ++t) {
           uint8_t* adst = a_ring + (ra.s * NT + t) * A_TILE_BYTES + row_off;
 #pragma unroll
-          for (int w = 0; w < 4; ++w) *reinterpret_cast<uint4*>(adst + (((c * 4 + w) ^ sw_row) << 4)) = o[t][w];
+          for (int w = 0; w < WPT; ++w)
+            *reinterpret_cast<uint4*>(adst + (((c * WPT + w) ^ sw_row) << 4)) = o[t][w];
         }
         fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core (async proxy)
       }
