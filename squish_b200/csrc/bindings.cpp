@@ -152,7 +152,8 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
 void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, int64_t K, int64_t group,
                 torch::Tensor y, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual,
                 int64_t epilogue, torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
-                c10::optional<torch::Tensor> trace) {
+                c10::optional<torch::Tensor> trace, int64_t wfmt) {
+  TORCH_CHECK(wfmt >= 0 && wfmt <= 3, "unknown weight format");
   CHECK_CUDA(x);
   CHECK_DT(x, torch::kBFloat16);
   CHECK_DT(y, torch::kBFloat16);
@@ -185,6 +186,7 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, 
   p.kb_per_split = (int)plan[3];
   p.gpk = group >= 64 ? 1 : (int)(64 / group);
   p.epilogue = (int)epilogue;
+  p.wfmt = (int)wfmt;
   p.trace = optr<unsigned long long>(trace);
   const CUtensorMap xmap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), bn);
   CUDA_OK(sq::w4a16_gemm_launch(xmap, p, bn, nt, cur_stream()));

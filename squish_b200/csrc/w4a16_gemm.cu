@@ -62,18 +62,21 @@ struct Cfg {
   static constexpr int kTmemCols = (kCols <= 32) ? 32 : (kCols <= 64) ? 64 : (kCols <= 128) ? 128 : (kCols <= 256) ? 256 : 512;
 };
 
-__host__ __device__ constexpr int tile_bytes(int gpk) { return W_TILE_BYTES + gpk * BM * 4; }
+__host__ __device__ constexpr int code_bytes(int wfmt) {
+  return wfmt == WF_INT8 ? 2 * W_TILE_BYTES : wfmt == WF_INT2 ? W_TILE_BYTES / 2 : W_TILE_BYTES;
+}
+__host__ __device__ constexpr int tile_bytes(int gpk, int wfmt = WF_INT4) { return code_bytes(wfmt) + gpk * BM * 4; }
 
 struct Layout {
   uint32_t x_off, w_off, w_stage, bar_off, trace_off, total;
 };
 
 __host__ __device__ inline Layout make_layout(int bn, int nt, int gpk, int rw, int rx, int ra, bool trace,
-                                              bool a_in_tmem) {
+                                              bool a_in_tmem, int wfmt) {
   Layout L;
   L.x_off = a_in_tmem ? 0u : (uint32_t)(ra * nt * A_TILE_BYTES);
   L.w_off = L.x_off + (uint32_t)(rx * bn * 128);
-  L.w_stage = (uint32_t)(nt * tile_bytes(gpk));
+  L.w_stage = (uint32_t)(nt * tile_bytes(gpk, wfmt));
   L.bar_off = L.w_off + (uint32_t)rw * L.w_stage;
   L.bar_off = (L.bar_off + 15u) & ~15u;
   L.trace_off = L.bar_off + (uint32_t)(2 * rw + 2 * rx + 2 * ra + 1) * 8u + 16u;
@@ -98,6 +101,82 @@ __device__ __forceinline__ uint4 dq_word(uint32_t w, __nv_bfloat162 s2, __nv_bfl
     o[e] = bf2_bits(v);
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// NF4: 8 level indices of one word (same interleaved order as INT4) -> 8 bf16 = level * absmax.
+// lut[(q_even) | (q_odd << 4)] holds the two levels as a bf16 pair.
+// The NormalFloat-4 levels (QLoRA, Dettmers et al. 2023), as the npy-dir __nf4 format stores them.
+__constant__ float kNf4Levels[16] = {-1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
+                                     -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f, 0.0f,
+                                     0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f,
+                                     0.33791524171829224f, 0.44070982933044434f, 0.5626170039176941f,
+                                     0.7229568362236023f, 1.0f};
+
+__device__ __forceinline__ uint4 dq_nf4(uint32_t w, __nv_bfloat162 s2, const uint32_t* lut) {
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const uint32_t t = (w >> (4 * e)) & 0x000F000Fu;
+    uint32_t pr = lut[(t & 0xFu) | ((t >> 12) & 0xF0u)];
+    __nv_bfloat162 v = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&pr), s2);
+    o[e] = bf2_bits(v);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// INT2: half h of a word of 16 codes (value 2e at bits 2e, value 2e+1 at bits 16+2e) -> 8 bf16.
+__device__ __forceinline__ uint4 dq_int2(uint32_t w, int h, __nv_bfloat162 s2, __nv_bfloat162 z2) {
+  const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.f, 128.f);
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    uint32_t t = ((w >> (2 * (4 * h + e))) & 0x00030003u) | 0x43004300u;  // bf16(128 + q)
+    __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&t);
+    v = __hfma2(__hsub2(v, k128), s2, z2);
+    o[e] = bf2_bits(v);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// INT8: 8 signed bytes (little-endian in two words) -> 8 bf16 = q * scale.
+__device__ __forceinline__ uint4 dq_int8(uint32_t a, uint32_t b, float s) {
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const uint32_t w = e < 2 ? a : b;
+    const int sh = (e & 1) * 16;
+    const float f0 = (float)((int)(w << (24 - sh)) >> 24) * s;
+    const float f1 = (float)((int)(w << (16 - sh)) >> 24) * s;
+    o[e] = bf2_bits(__floats2bfloat162_rn(f0, f1));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// The 32 K values (4 chunks of 8) of row r, part c of a tile in a non-INT4 format.
+__device__ __forceinline__ void dq_other(const uint8_t* tb, int fmt, int r, int c, int gpk, const uint32_t* lut,
+                                         uint4 (&o)[4]) {
+  const uint32_t* szt = reinterpret_cast<const uint32_t*>(tb + code_bytes(fmt));
+  uint32_t ww[8];
+  if (fmt == WF_INT8) {
+    const uint4 a = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 32);
+    const uint4 b = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 32 + 16);
+    ww[0] = a.x; ww[1] = a.y; ww[2] = a.z; ww[3] = a.w; ww[4] = b.x; ww[5] = b.y; ww[6] = b.z; ww[7] = b.w;
+  } else if (fmt == WF_INT2) {
+    const uint2 a = *reinterpret_cast<const uint2*>(tb + (c * BM + r) * 8);
+    ww[0] = a.x; ww[1] = a.y;
+  } else {
+    const uint4 a = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 16);
+    ww[0] = a.x; ww[1] = a.y; ww[2] = a.z; ww[3] = a.w;
+  }
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t szw = szt[(((c * 4 + w) * gpk) >> 3) * BM + r];
+    const __nv_bfloat16 sc = __ushort_as_bfloat16((unsigned short)(szw & 0xFFFFu));
+    const __nv_bfloat16 ze = __ushort_as_bfloat16((unsigned short)(szw >> 16));
+    if (fmt == WF_NF4) o[w] = dq_nf4(ww[w], __bfloat162bfloat162(sc), lut);
+    else if (fmt == WF_INT2) o[w] = dq_int2(ww[w >> 1], w & 1, __bfloat162bfloat162(sc), __bfloat162bfloat162(ze));
+    else o[w] = dq_int8(ww[2 * w], ww[2 * w + 1], __bfloat162float(sc));
+  }
 }
 
 __device__ __forceinline__ float silu(float g) { return g / (1.f + __expf(-g)); }
@@ -168,7 +247,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
 
   const int gpk = p.gpk;
   const int ring_w = p.ring_w, ring_x = p.ring_x, ring_a = p.ring_a;
-  const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a, p.trace != nullptr, C::AT);
+  const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a, p.trace != nullptr, C::AT, p.wfmt);
   uint8_t* a_ring = smem;  // (shared-memory A ring; with C::AT the region starts the X ring)
   uint8_t* x_ring = smem + L.x_off;
   uint8_t* w_ring = smem + L.w_off;
@@ -215,11 +294,15 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
+  __shared__ uint32_t nf4_lut[256];  // (level[q0], level[q1]) bf16 pairs, NF4 weights only
+  if (p.wfmt == WF_NF4)
+    for (int i = threadIdx.x; i < 256; i += blockDim.x)
+      nf4_lut[i] = bf2_bits(__floats2bfloat162_rn(kNf4Levels[i & 15], kNf4Levels[i >> 4]));
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int tbytes = tile_bytes(gpk);
+  const int tbytes = tile_bytes(gpk, p.wfmt);
   if (threadIdx.x == 0) trace_mark(str, 14, 0);  // setup done
   pdl_trigger();
 
@@ -314,6 +397,12 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         const uint8_t* tb = wst + t * tbytes;
+        if constexpr (WPT == 4) {
+          if (p.wfmt != WF_INT4) {
+            dq_other(tb, p.wfmt, r, c, gpk, nf4_lut, o[t]);
+            continue;
+          }
+        }
         // nibble words of a row: [2 halves][128 rows][4 words]
         uint32_t ww[WPT];
         if constexpr (WPT == 4) {
@@ -531,7 +620,8 @@ cudaError_t launch_cfg(const CUtensorMap& xmap, W4A16Params p, int rw, int rx, i
   p.ring_w = rw;
   p.ring_x = rx;
   p.ring_a = ra;
-  const Layout L = make_layout(C::BN, C::NT, p.gpk, rw, rx, ra, p.trace != nullptr, C::AT);
+  const Layout L = make_layout(C::BN, C::NT, p.gpk, rw, rx, ra, p.trace != nullptr, C::AT, p.wfmt);
+  if (p.wfmt != WF_INT4 && C::kWpt != 4) return cudaErrorInvalidConfiguration;
   if (C::AT) {
     // the A ring lives in TMEM; the epilogue stages through the (then idle) X + W rings
     if (ra > C::kMaxRingA || L.bar_off < (uint32_t)(C::BN * BM * 4) || L.bar_off < 16u * BM * 4u)

@@ -8,6 +8,13 @@
 namespace sq {
 
 enum : int { EPI_PLAIN = 0, EPI_SILU_MUL = 1 };
+// Weight code formats of a (128 rows x 64 columns) tile; the (scale, zero) words follow the codes.
+enum : int {
+  WF_INT4 = 0,  // unsigned nibbles, x = zero + q * scale                    (4 KiB of codes)
+  WF_NF4 = 1,   // NormalFloat-4 level index, x = level[q] * absmax          (4 KiB)
+  WF_INT8 = 2,  // signed bytes, x = q * scale                                (8 KiB)
+  WF_INT2 = 3,  // unsigned 2-bit codes, x = zero + q * scale                 (2 KiB)
+};
 
 struct W4A16Params {
   const uint32_t* wq;             // tile-major weight tiles [N/128][KB][1024 + gpk*128] words (nibbles, then
@@ -24,6 +31,7 @@ struct W4A16Params {
   int kb_total, kb_per_split, splits;
   int gpk;                        // (scale, zero) groups per 64-column k-block: 1, 2 or 4
   int epilogue;                   // EPI_PLAIN | EPI_SILU_MUL
+  int wfmt;                       // WF_* code format of the weight tiles
   int ring_w, ring_x, ring_a;     // set by the launcher
   unsigned long long* trace;      // optional: per-k-block role timestamps of CTA (0,0,0), 16 x 64 entries
   // Grouped (mixture-of-experts) mode, when tile_expert != nullptr: the rows of X are sorted

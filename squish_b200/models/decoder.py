@@ -110,15 +110,33 @@ class LayerWeights:
     moe: object | None = None
 
 
-def _cat_q4a(parts: list[QTensor]) -> QTensor:
-    return QTensor("q4a", (sum(p.shape[0] for p in parts), parts[0].shape[1]),
-                   packed=torch.cat([p.packed for p in parts]), scales=torch.cat([p.scales for p in parts]),
-                   offsets=torch.cat([p.offsets for p in parts]), group=parts[0].group)
+GEMM_KINDS = ("q4a", "nf4", "q8", "q2")  # stored kinds the GEMM decodes natively (others: re-encoded INT4)
+
+
+def _same_kind(parts: list[QTensor], group: int) -> list[QTensor]:
+    """Tensors fused into one GEMM must share a native kind and group; otherwise all are
+    re-encoded as INT4."""
+    k0 = parts[0].kind
+    if k0 in GEMM_KINDS and all(p.kind == k0 and p.group == parts[0].group for p in parts):
+        return parts
+    return [_as_q4a(p, group) if p.kind != "q4a" else p for p in parts]
+
+
+def _cat_rows(parts: list[QTensor]) -> QTensor:
+    def cat(name):
+        xs = [getattr(p, name) for p in parts]
+        return None if xs[0] is None else torch.cat(xs)
+
+    return QTensor(parts[0].kind, (sum(p.shape[0] for p in parts), parts[0].shape[1]), packed=cat("packed"),
+                   scales=cat("scales"), offsets=cat("offsets"), group=parts[0].group)
+
+
+_cat_q4a = _cat_rows
 
 
 def _interleave_gate_up(gate: QTensor, up: QTensor) -> QTensor:
     """Rows [g0:64, u0:64, g64:128, u64:128, ...] (F padded to a multiple of 64 with zero
-    rows), the layout the SiLU*up GEMM epilogue expects."""
+    rows, whose zero scales make them 0), the layout the SiLU*up GEMM epilogue expects."""
     f = gate.shape[0]
     fp = (f + 63) // 64 * 64
 
@@ -129,16 +147,18 @@ def _interleave_gate_up(gate: QTensor, up: QTensor) -> QTensor:
         return torch.cat([t, z])
 
     def inter(a, b):
+        if a is None:
+            return None
         a, b = pad(a), pad(b)
         return torch.stack([a.view(fp // 64, 64, -1), b.view(fp // 64, 64, -1)], 1).reshape(2 * fp, -1)
 
-    return QTensor("q4a", (2 * fp, gate.shape[1]), packed=inter(gate.packed, up.packed),
+    return QTensor(gate.kind, (2 * fp, gate.shape[1]), packed=inter(gate.packed, up.packed),
                    scales=inter(gate.scales, up.scales), offsets=inter(gate.offsets, up.offsets), group=gate.group)
 
 
 def _as_q4a(t: QTensor, group: int) -> QTensor:
-    """The tcgen05 GEMM consumes INT4 asymmetric tiles; other stored kinds (INT8, NF4, INT3,
-    INT2, AQLM, dense) are decoded once at load and re-encoded as INT4 group ``group``."""
+    """Stored kinds without a GEMM code format (INT3, AQLM, dense) are decoded once at load
+    and re-encoded as INT4 asymmetric group ``group``."""
     if t.kind == "q4a":
         return t
     from ..quant.codecs import quantize
@@ -146,9 +166,12 @@ def _as_q4a(t: QTensor, group: int) -> QTensor:
     return quantize(t.dequantize().float(), "q4a", group)
 
 
+def _native(t: QTensor, group: int) -> QTensor:
+    return t if t.kind in GEMM_KINDS else _as_q4a(t, group)
+
+
 def _to_int4(t: QTensor, device, bias: torch.Tensor | None = None, group: int = 64) -> Int4Weight:
-    t = _as_q4a(t, group)
-    return ops.prepare_int4_weight(t.packed, t.scales, t.offsets, t.shape[1], t.group, device, bias=bias)
+    return ops.kernels.prepare_weight(_native(t, group), device, bias=bias)
 
 
 def _dense(t: QTensor, device, dtype=torch.bfloat16) -> torch.Tensor:
@@ -179,7 +202,7 @@ class CudaRunner:
         for i in range(cfg.num_layers):
             p = f"model.layers.{i}."
             g = self.qcfg.group_size
-            qkv = _cat_q4a([_as_q4a(t[p + f"self_attn.{n}_proj.weight"], g) for n in "qkv"])
+            qkv = _cat_rows(_same_kind([_native(t[p + f"self_attn.{n}_proj.weight"], g) for n in "qkv"], g))
             bias = None
             if cfg.qkv_bias:
                 bias = torch.cat([t[p + f"self_attn.{n}.bias"].data.float() for n in ("q_proj", "k_proj", "v_proj")])
@@ -197,8 +220,8 @@ class CudaRunner:
                     self.moe_scratch = MoEScratch(cfg, max_num_tokens, dev)
                 lw.moe = MoELayer.from_checkpoint(ck, i, dev, self.moe_scratch)
             else:
-                lw.gate_up = _to_int4(_interleave_gate_up(_as_q4a(t[p + "mlp.gate_proj.weight"], g),
-                                                          _as_q4a(t[p + "mlp.up_proj.weight"], g)), dev)
+                gu = _same_kind([_native(t[p + "mlp.gate_proj.weight"], g), _native(t[p + "mlp.up_proj.weight"], g)], g)
+                lw.gate_up = _to_int4(_interleave_gate_up(gu[0], gu[1]), dev)
                 lw.down = _to_int4(t[p + "mlp.down_proj.weight"], dev)
             self.layers.append(lw)
             if free_checkpoint:

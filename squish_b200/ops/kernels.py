@@ -99,6 +99,7 @@ class Int4Weight:
     k: int
     group: int
     bias: torch.Tensor | None = None
+    fmt: int = 0  # WF_INT4 | WF_NF4 | WF_INT8 | WF_INT2
 
     @property
     def nbytes(self) -> int:
@@ -115,6 +116,90 @@ def prepare_int4_weight(packed: torch.Tensor, scales: torch.Tensor, offsets: tor
     wq, sz = native().repack_int4(p, s, z, int(k), int(group))
     b = None if bias is None else bias.to(dev, torch.bfloat16).contiguous()
     return Int4Weight(wq=wq, sz=sz, n=int(packed.shape[0]), k=int(k), group=int(group), bias=b)
+
+
+WF_INT4, WF_NF4, WF_INT8, WF_INT2 = 0, 1, 2, 3
+_NIB_POS = (0, 16, 4, 20, 8, 24, 12, 28)  # bit of value j in an 8-value word (pairs share a 16-bit shift)
+
+
+def _bf16_bits(x: torch.Tensor) -> torch.Tensor:
+    return x.to(torch.bfloat16).view(torch.int16).to(torch.int64) & 0xFFFF
+
+
+def repack_codes(codes: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor | None, k: int, group: int,
+                 fmt: int) -> torch.Tensor:
+    """Tile-major device layout of a quantized weight for the GEMM kernel, any WF_* format.
+
+    ``codes`` (N, K) holds one code per weight (uint8: INT4 / NF4 index 0..15, INT2 0..3,
+    INT8 two's complement). Per (128-row block, 64-column k-block) tile: the codes as
+    [2 halves][128 rows][32 values] packed into words (INT4/NF4: 8 per word in the kernel's
+    interleaved nibble order; INT2: 16 per word, value 2e at bit 2e and 2e+1 at 16+2e; INT8:
+    4 bytes little-endian), then (scale | zero << 16) bf16 pairs [groups per k-block][128].
+    Padding rows and columns get zero scales, so they dequantize to 0.
+    """
+    dev = codes.device
+    n = codes.shape[0]
+    npad = (n + 255) // 256 * 256
+    kb = (k + 63) // 64
+    kp = kb * 64
+    gpk = 1 if group >= 64 else 64 // group
+    c = torch.zeros(npad, kp, dtype=torch.int64, device=dev)
+    c[:n, :k] = codes[:, :k].to(torch.int64) & 0xFF
+    v = c.view(npad // 128, 128, kb, 2, 32).permute(0, 2, 3, 1, 4)  # [rb, kb, half, row, 32]
+    if fmt in (WF_INT4, WF_NF4):
+        pos = torch.tensor(_NIB_POS, dtype=torch.int64, device=dev)
+        words = (v.reshape(*v.shape[:4], 4, 8) << pos).sum(-1)
+    elif fmt == WF_INT2:
+        j = torch.arange(16, device=dev)
+        pos = (j % 2) * 16 + (j // 2) * 2
+        words = (v.reshape(*v.shape[:4], 2, 16) << pos).sum(-1)
+    elif fmt == WF_INT8:
+        pos = torch.arange(4, device=dev) * 8
+        words = (v.reshape(*v.shape[:4], 8, 4) << pos).sum(-1)
+    else:
+        raise ValueError(f"unknown weight format {fmt}")
+    words = words.reshape(npad // 128, kb, -1)
+    g_n = scales.shape[1]
+    cols = torch.arange(kb, device=dev)[:, None] * 64 + torch.arange(gpk, device=dev)[None, :] * (64 // gpk)
+    gi = torch.clamp(cols // group, max=g_n - 1).reshape(-1)  # [kb * gpk]
+    s = torch.zeros(npad, g_n, dtype=torch.float32, device=dev)
+    s[:n] = scales.float()
+    z = torch.zeros_like(s)
+    if zeros is not None:
+        z[:n] = zeros.float()
+    aux = _bf16_bits(s[:, gi]) | (_bf16_bits(z[:, gi]) << 16)  # [npad, kb*gpk]
+    aux = aux.view(npad // 128, 128, kb, gpk).permute(0, 2, 3, 1).reshape(npad // 128, kb, gpk * 128)
+    tile = torch.cat([words, aux], dim=-1)
+    tile = torch.where(tile >= 2**31, tile - 2**32, tile)
+    return tile.to(torch.int32).contiguous()
+
+
+def prepare_weight(t, device, bias: torch.Tensor | None = None) -> Int4Weight:
+    """A QTensor in the GEMM's device layout: INT4 asymmetric (repacked on the GPU), NF4,
+    INT8 or INT2 (repacked with tensor ops) in their own code formats."""
+    dev = torch.device(device)
+    k = int(t.shape[1])
+    b = None if bias is None else bias.to(dev, torch.bfloat16).contiguous()
+    if t.kind == "q4a":
+        w = prepare_int4_weight(t.packed, t.scales, t.offsets, k, t.group, dev)
+        w.bias = b
+        return w
+    p = t.packed.to(dev)
+    if t.kind == "nf4":
+        codes = torch.stack([p & 0xF, p >> 4], dim=-1).reshape(p.shape[0], -1)
+        wt = repack_codes(codes, t.scales.to(dev), None, k, t.group, WF_NF4)
+        fmt = WF_NF4
+    elif t.kind == "q8":
+        wt = repack_codes(p.view(torch.uint8), t.scales.to(dev), None, k, t.group, WF_INT8)
+        fmt = WF_INT8
+    elif t.kind == "q2":
+        codes = torch.stack([(p >> (2 * i)) & 3 for i in range(4)], dim=-1).reshape(p.shape[0], -1)
+        wt = repack_codes(codes, t.scales.to(dev), t.offsets.to(dev), k, t.group, WF_INT2)
+        fmt = WF_INT2
+    else:
+        raise ValueError(f"no GEMM code format for weight kind {t.kind!r}")
+    return Int4Weight(wq=wt, sz=torch.empty(0, dtype=torch.int32, device=dev), n=int(t.shape[0]), k=k,
+                      group=int(t.group), bias=b, fmt=fmt)
 
 
 def gemm_plan(m: int, n: int, k: int):
@@ -136,7 +221,8 @@ def w4a16_linear(x: torch.Tensor, w: Int4Weight, out: torch.Tensor | None = None
     if out is None:
         out = torch.empty((m, ncols), dtype=torch.bfloat16, device=x.device)
     native().w4a16_gemm(x, w.wq, w.sz, w.n, w.k, w.group, out, w.bias, residual,
-                        EPI_SILU_MUL if silu_mul else EPI_PLAIN, ws.gemm_ws, ws.gemm_counters, ws.status, trace)
+                        EPI_SILU_MUL if silu_mul else EPI_PLAIN, ws.gemm_ws, ws.gemm_counters, ws.status, trace,
+                        w.fmt)
     _count()
     return out
 

@@ -1,0 +1,69 @@
+"""The INT4 GEMM kernel's other code formats (NF4, INT8, INT2) against a plain PyTorch fp32
+reference of the same dequantized weight, the tensor-op repack against the CUDA INT4
+repack, and an engine whose linear layers are NF4 / INT8 / INT2 against the CPU oracle."""
+import dataclasses
+
+import numpy as np
+import pytest
+import torch
+
+from squish_b200 import ops
+from squish_b200.ops import kernels as K
+from squish_b200.quant.codecs import quantize
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("kind,group", [("nf4", 64), ("nf4", 32), ("q8", 64), ("q8", 32), ("q2", 64), ("q2", 128)])
+@pytest.mark.parametrize("m", [1, 37, 64, 300])
+def test_gemm_formats_match_fp32(cuda, kind, group, m):
+    g = torch.Generator().manual_seed(m + group)
+    n, k = 640, 1024
+    w = torch.randn(n, k, generator=g) * 0.05
+    t = quantize(w, kind, group)
+    dw = K.prepare_weight(t, cuda)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    y = ops.w4a16_linear(x.to(cuda), dw)
+    torch.cuda.synchronize()
+    ref = x.float() @ t.dequantize().float().T
+    err = (y.float().cpu() - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item() + 1e-2, err
+
+
+def test_tensor_op_repack_equals_cuda_int4_repack(cuda):
+    g = torch.Generator().manual_seed(5)
+    w = torch.randn(384, 704, generator=g) * 0.05
+    t = quantize(w, "q4a", 64)
+    a = K.prepare_int4_weight(t.packed, t.scales, t.offsets, 704, t.group, cuda).wq
+    p = t.packed.to(cuda)
+    codes = torch.stack([p & 0xF, p >> 4], dim=-1).reshape(p.shape[0], -1)
+    b = K.repack_codes(codes, t.scales.to(cuda), t.offsets.to(cuda), 704, t.group, K.WF_INT4)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("kind", ["nf4", "q8", "q2"])
+def test_engine_with_format_weights_matches_oracle(cuda, kind):
+    from squish_b200.engine.engine import EngineConfig, LLMEngine
+    from squish_b200.engine.sampling import SamplingParams
+    from squish_b200.models.config import get_preset
+    from squish_b200.models.reference import ReferenceModel
+    from squish_b200.models.weights import linear_names, random_checkpoint
+
+    from .test_engine_gpu import _teacher_forced_ok
+
+    cfg, q = get_preset("tiny-llama")
+    cfg = dataclasses.replace(cfg, intermediate_size=512)
+
+    def ck():
+        c = random_checkpoint(cfg, q, seed=0)
+        for name, _ in linear_names(cfg):
+            c.tensors[name] = quantize(c.tensors[name].dequantize().float(), kind, 32)
+        return c
+
+    ref = ReferenceModel(ck())
+    eng = LLMEngine.from_checkpoint(ck(), cuda, EngineConfig(max_num_seqs=2, max_model_len=256, num_pages=32))
+    prompt = np.random.default_rng(2).integers(0, cfg.vocab_size, 30).tolist()
+    out = eng.generate([prompt], SamplingParams(max_tokens=8, ignore_eos=True))[0]
+    ok, worst = _teacher_forced_ok(ref, prompt, out)
+    assert ok, (worst, out)
+    assert eng.runner.layers[0].o.fmt == {"nf4": K.WF_NF4, "q8": K.WF_INT8, "q2": K.WF_INT2}[kind]
