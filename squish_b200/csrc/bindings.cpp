@@ -152,8 +152,13 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
 void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, int64_t K, int64_t group,
                 torch::Tensor y, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual,
                 int64_t epilogue, torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
-                c10::optional<torch::Tensor> trace, int64_t wfmt) {
-  TORCH_CHECK(wfmt >= 0 && wfmt <= 3, "unknown weight format");
+                c10::optional<torch::Tensor> trace, int64_t wfmt, c10::optional<torch::Tensor> codebook) {
+  TORCH_CHECK(wfmt >= 0 && wfmt <= 5, "unknown weight format");
+  if (wfmt == sq::WF_AQLM) {
+    TORCH_CHECK(codebook.has_value() && codebook->scalar_type() == torch::kBFloat16 && codebook->is_cuda() &&
+                    codebook->is_contiguous() && codebook->numel() % (256 * 8) == 0 && codebook->numel() <= 2 * 256 * 8,
+                "AQLM needs 1 or 2 contiguous bf16 codebooks of 256 x 8 on the device");
+  }
   CHECK_CUDA(x);
   CHECK_DT(x, torch::kBFloat16);
   CHECK_DT(y, torch::kBFloat16);
@@ -187,6 +192,8 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, 
   p.gpk = group >= 64 ? 1 : (int)(64 / group);
   p.epilogue = (int)epilogue;
   p.wfmt = (int)wfmt;
+  p.codebook = optr<__nv_bfloat16>(codebook);
+  p.n_books = codebook.has_value() ? (int)(codebook->numel() / (256 * 8)) : 0;
   p.trace = optr<unsigned long long>(trace);
   const CUtensorMap xmap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), bn);
   CUDA_OK(sq::w4a16_gemm_launch(xmap, p, bn, nt, cur_stream()));

@@ -63,7 +63,10 @@ struct Cfg {
 };
 
 __host__ __device__ constexpr int code_bytes(int wfmt) {
-  return wfmt == WF_INT8 ? 2 * W_TILE_BYTES : wfmt == WF_INT2 ? W_TILE_BYTES / 2 : W_TILE_BYTES;
+  return wfmt == WF_INT8                        ? 2 * W_TILE_BYTES
+         : (wfmt == WF_INT2 || wfmt == WF_AQLM) ? W_TILE_BYTES / 2
+         : wfmt == WF_INT3                      ? 3 * W_TILE_BYTES / 4
+                                                : W_TILE_BYTES;
 }
 __host__ __device__ constexpr int tile_bytes(int gpk, int wfmt = WF_INT4) { return code_bytes(wfmt) + gpk * BM * 4; }
 
@@ -152,18 +155,57 @@ __device__ __forceinline__ uint4 dq_int8(uint32_t a, uint32_t b, float s) {
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// INT3: 32 codes u = q + 4 in three words. Pair p < 15 (values 2p, 2p+1) sits in word p / 5 at
+// bits 3*(p%5) and 16 + 3*(p%5); pair 15 is spread over bits 15 (even value) and 31 (odd
+// value) of words 0, 1, 2 (its bits 0, 1, 2).
+__device__ __forceinline__ uint32_t int3_pair(const uint32_t (&ww)[8], int p) {
+  if (p < 15) return (ww[p / 5] >> (3 * (p % 5))) & 0x00070007u;
+  return ((ww[0] >> 15) & 0x00010001u) | ((ww[1] >> 14) & 0x00020002u) | ((ww[2] >> 13) & 0x00040004u);
+}
+__device__ __forceinline__ uint4 dq_int3(const uint32_t (&ww)[8], int ch, __nv_bfloat162 s2, __nv_bfloat162 z2) {
+  const __nv_bfloat162 k132 = __floats2bfloat162_rn(132.f, 132.f);
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    uint32_t t = int3_pair(ww, ch * 4 + e) | 0x43004300u;  // bf16(128 + u)
+    __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&t);
+    v = __hfma2(__hsub2(v, k132), s2, z2);  // exact q, then q * scale + zero
+    o[e] = bf2_bits(v);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// AQLM: one 8-column group from its codebook indices (book k's index in byte k of idx).
+__device__ __forceinline__ uint4 dq_aqlm(uint32_t idx, int n_books, const uint4* books, __nv_bfloat162 s2) {
+  uint4 a = books[idx & 0xFFu];
+  if (n_books > 1) {
+    const uint4 b = books[256 + ((idx >> 8) & 0xFFu)];
+    __nv_bfloat162* pa = reinterpret_cast<__nv_bfloat162*>(&a);
+    const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) pa[e] = __hadd2(pa[e], pb[e]);
+  }
+  __nv_bfloat162* pa = reinterpret_cast<__nv_bfloat162*>(&a);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) pa[e] = __hmul2(pa[e], s2);
+  return a;
+}
+
 // The 32 K values (4 chunks of 8) of row r, part c of a tile in a non-INT4 format.
 __device__ __forceinline__ void dq_other(const uint8_t* tb, int fmt, int r, int c, int gpk, const uint32_t* lut,
-                                         uint4 (&o)[4]) {
+                                         int n_books, uint4 (&o)[4]) {
   const uint32_t* szt = reinterpret_cast<const uint32_t*>(tb + code_bytes(fmt));
   uint32_t ww[8];
   if (fmt == WF_INT8) {
     const uint4 a = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 32);
     const uint4 b = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 32 + 16);
     ww[0] = a.x; ww[1] = a.y; ww[2] = a.z; ww[3] = a.w; ww[4] = b.x; ww[5] = b.y; ww[6] = b.z; ww[7] = b.w;
-  } else if (fmt == WF_INT2) {
+  } else if (fmt == WF_INT2 || fmt == WF_AQLM) {
     const uint2 a = *reinterpret_cast<const uint2*>(tb + (c * BM + r) * 8);
     ww[0] = a.x; ww[1] = a.y;
+  } else if (fmt == WF_INT3) {
+    const uint32_t* a = reinterpret_cast<const uint32_t*>(tb + (c * BM + r) * 12);
+    ww[0] = a[0]; ww[1] = a[1]; ww[2] = a[2];
   } else {
     const uint4 a = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 16);
     ww[0] = a.x; ww[1] = a.y; ww[2] = a.z; ww[3] = a.w;
@@ -175,6 +217,10 @@ __device__ __forceinline__ void dq_other(const uint8_t* tb, int fmt, int r, int 
     const __nv_bfloat16 ze = __ushort_as_bfloat16((unsigned short)(szw >> 16));
     if (fmt == WF_NF4) o[w] = dq_nf4(ww[w], __bfloat162bfloat162(sc), lut);
     else if (fmt == WF_INT2) o[w] = dq_int2(ww[w >> 1], w & 1, __bfloat162bfloat162(sc), __bfloat162bfloat162(ze));
+    else if (fmt == WF_INT3) o[w] = dq_int3(ww, w, __bfloat162bfloat162(sc), __bfloat162bfloat162(ze));
+    else if (fmt == WF_AQLM)
+      o[w] = dq_aqlm((ww[w >> 1] >> (16 * (w & 1))) & 0xFFFFu, n_books, reinterpret_cast<const uint4*>(lut),
+                     __bfloat162bfloat162(sc));
     else o[w] = dq_int8(ww[2 * w], ww[2 * w + 1], __bfloat162float(sc));
   }
 }
@@ -294,10 +340,16 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
-  __shared__ uint32_t nf4_lut[256];  // (level[q0], level[q1]) bf16 pairs, NF4 weights only
-  if (p.wfmt == WF_NF4)
+  // format table: NF4 (level[q0], level[q1]) bf16 pairs, or the AQLM codebooks (<= 2 x 256 x 8 bf16)
+  __shared__ uint4 fmt_tab[512];
+  uint32_t* nf4_lut = reinterpret_cast<uint32_t*>(fmt_tab);
+  if (p.wfmt == WF_NF4) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x)
       nf4_lut[i] = bf2_bits(__floats2bfloat162_rn(kNf4Levels[i & 15], kNf4Levels[i >> 4]));
+  } else if (p.wfmt == WF_AQLM) {
+    for (int i = threadIdx.x; i < 256 * p.n_books; i += blockDim.x)
+      fmt_tab[i] = reinterpret_cast<const uint4*>(p.codebook)[i];
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -399,7 +451,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         const uint8_t* tb = wst + t * tbytes;
         if constexpr (WPT == 4) {
           if (p.wfmt != WF_INT4) {
-            dq_other(tb, p.wfmt, r, c, gpk, nf4_lut, o[t]);
+            dq_other(tb, p.wfmt, r, c, gpk, nf4_lut, p.n_books, o[t]);
             continue;
           }
         }

@@ -14,6 +14,9 @@ enum : int {
   WF_NF4 = 1,   // NormalFloat-4 level index, x = level[q] * absmax          (4 KiB)
   WF_INT8 = 2,  // signed bytes, x = q * scale                                (8 KiB)
   WF_INT2 = 3,  // unsigned 2-bit codes, x = zero + q * scale                 (2 KiB)
+  WF_INT3 = 4,  // 3-bit codes q + 4 (q in [-4, 3]), x = zero + q * scale      (3 KiB)
+  WF_AQLM = 5,  // per 8 columns one index into each of <= 2 codebooks of 256 x 8 values,
+                // x = scale * sum_k book_k[idx_k]                             (2 KiB)
 };
 
 struct W4A16Params {
@@ -32,6 +35,8 @@ struct W4A16Params {
   int gpk;                        // (scale, zero) groups per 64-column k-block: 1, 2 or 4
   int epilogue;                   // EPI_PLAIN | EPI_SILU_MUL
   int wfmt;                       // WF_* code format of the weight tiles
+  const __nv_bfloat16* codebook;  // WF_AQLM: [n_books][256][8] bf16
+  int n_books;
   int ring_w, ring_x, ring_a;     // set by the launcher
   unsigned long long* trace;      // optional: per-k-block role timestamps of CTA (0,0,0), 16 x 64 entries
   // Grouped (mixture-of-experts) mode, when tile_expert != nullptr: the rows of X are sorted

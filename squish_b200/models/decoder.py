@@ -110,14 +110,17 @@ class LayerWeights:
     moe: object | None = None
 
 
-GEMM_KINDS = ("q4a", "nf4", "q8", "q2")  # stored kinds the GEMM decodes natively (others: re-encoded INT4)
+# stored kinds the GEMM decodes natively (others, and INT3 with a low-rank term, are re-encoded INT4)
+GEMM_KINDS = ("q4a", "nf4", "q8", "q2", "q3", "aqlm")
 
 
 def _same_kind(parts: list[QTensor], group: int) -> list[QTensor]:
     """Tensors fused into one GEMM must share a native kind and group; otherwise all are
     re-encoded as INT4."""
     k0 = parts[0].kind
-    if k0 in GEMM_KINDS and all(p.kind == k0 and p.group == parts[0].group for p in parts):
+    # AQLM tensors carry their own codebooks, so they cannot share one fused GEMM
+    if (k0 in GEMM_KINDS and all(p.kind == k0 and p.group == parts[0].group for p in parts)
+            and not (k0 == "aqlm" and len(parts) > 1)):
         return parts
     return [_as_q4a(p, group) if p.kind != "q4a" else p for p in parts]
 
@@ -167,7 +170,7 @@ def _as_q4a(t: QTensor, group: int) -> QTensor:
 
 
 def _native(t: QTensor, group: int) -> QTensor:
-    return t if t.kind in GEMM_KINDS else _as_q4a(t, group)
+    return t if t.kind in GEMM_KINDS and not t.extra else _as_q4a(t, group)
 
 
 def _to_int4(t: QTensor, device, bias: torch.Tensor | None = None, group: int = 64) -> Int4Weight:

@@ -99,7 +99,8 @@ class Int4Weight:
     k: int
     group: int
     bias: torch.Tensor | None = None
-    fmt: int = 0  # WF_INT4 | WF_NF4 | WF_INT8 | WF_INT2
+    fmt: int = 0  # WF_INT4 | WF_NF4 | WF_INT8 | WF_INT2 | WF_INT3 | WF_AQLM
+    codebook: torch.Tensor | None = None  # WF_AQLM: [books, 256, 8] bf16
 
     @property
     def nbytes(self) -> int:
@@ -118,7 +119,7 @@ def prepare_int4_weight(packed: torch.Tensor, scales: torch.Tensor, offsets: tor
     return Int4Weight(wq=wq, sz=sz, n=int(packed.shape[0]), k=int(k), group=int(group), bias=b)
 
 
-WF_INT4, WF_NF4, WF_INT8, WF_INT2 = 0, 1, 2, 3
+WF_INT4, WF_NF4, WF_INT8, WF_INT2, WF_INT3, WF_AQLM = 0, 1, 2, 3, 4, 5
 _NIB_POS = (0, 16, 4, 20, 8, 24, 12, 28)  # bit of value j in an 8-value word (pairs share a 16-bit shift)
 
 
@@ -156,6 +157,21 @@ def repack_codes(codes: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor 
     elif fmt == WF_INT8:
         pos = torch.arange(4, device=dev) * 8
         words = (v.reshape(*v.shape[:4], 8, 4) << pos).sum(-1)
+    elif fmt == WF_INT3:
+        # pair p < 15 in word p // 5 at bits 3(p%5) / 16 + 3(p%5); pair 15 bit-sliced over bits 15 / 31
+        ws = []
+        for q in range(3):
+            acc = torch.zeros_like(v[..., 0])
+            for k in range(5):
+                pp = 5 * q + k
+                acc = acc | (v[..., 2 * pp] << (3 * k)) | (v[..., 2 * pp + 1] << (16 + 3 * k))
+            acc = acc | (((v[..., 30] >> q) & 1) << 15) | (((v[..., 31] >> q) & 1) << 31)
+            ws.append(acc)
+        words = torch.stack(ws, dim=-1)
+    elif fmt == WF_AQLM:
+        # v holds 32 index bytes per (half, row): 8 groups x 2 books ... packed 4 per word
+        pos = torch.arange(4, device=dev) * 8
+        words = (v[..., :8].reshape(*v.shape[:4], 2, 4) << pos).sum(-1)
     else:
         raise ValueError(f"unknown weight format {fmt}")
     words = words.reshape(npad // 128, kb, -1)
@@ -196,6 +212,41 @@ def prepare_weight(t, device, bias: torch.Tensor | None = None) -> Int4Weight:
         codes = torch.stack([(p >> (2 * i)) & 3 for i in range(4)], dim=-1).reshape(p.shape[0], -1)
         wt = repack_codes(codes, t.scales.to(dev), t.offsets.to(dev), k, t.group, WF_INT2)
         fmt = WF_INT2
+    elif t.kind == "q3":
+        if t.extra:
+            raise ValueError("INT3 weights with a low-rank compensator have no GEMM code format")
+        b = p.to(torch.int64).view(p.shape[0], -1, 3)
+        bits = b[..., 0] | (b[..., 1] << 8) | (b[..., 2] << 16)  # 8 codes of 3 bits
+        q = torch.stack([(bits >> (3 * j)) & 7 for j in range(8)], dim=-1).reshape(p.shape[0], -1)[:, :k]
+        u = torch.where(q >= 4, q - 8, q) + 4  # two's complement code -> q + 4 in [0, 7]
+        z = t.offsets.to(dev) if t.offsets is not None else None
+        wt = repack_codes(u, t.scales.to(dev), z, k, t.group, WF_INT3)
+        fmt = WF_INT3
+    elif t.kind == "aqlm":
+        cb = t.scales.float()
+        scale, size, gs = float(cb[0]), int(cb[1]), int(cb[2])
+        idx = t.packed.to(dev).long()  # [N, groups, books]
+        books = idx.shape[2]
+        if gs != 8 or books > 2 or size > 256:
+            raise ValueError("AQLM GEMM format needs 8-column groups, <= 2 books of <= 256 codes")
+        n_rows, groups = idx.shape[0], idx.shape[1]
+        b2 = torch.zeros(n_rows, groups, 2, dtype=torch.int64, device=dev)
+        b2[:, :, :books] = idx
+        per_kb = b2.view(n_rows, groups * 2)  # 16 index bytes per 64 columns, (group, book) order
+        # repack_codes expects one code per column: spread the 16 bytes of a k-block over the
+        # first 8 "columns" of each 32-column half
+        kb = (k + 63) // 64
+        cols = torch.zeros(n_rows, kb * 64, dtype=torch.int64, device=dev)
+        pk = torch.zeros(n_rows, kb * 16, dtype=torch.int64, device=dev)
+        pk[:, : per_kb.shape[1]] = per_kb
+        pk = pk.view(n_rows, kb, 2, 8)
+        cols.view(n_rows, kb, 2, 32)[..., :8] = pk
+        sc = torch.full((n_rows, kb), scale, dtype=torch.float32, device=dev)
+        wt = repack_codes(cols, sc, None, kb * 64, 64, WF_AQLM)
+        cbk = torch.zeros(books, 256, 8, dtype=torch.float32, device=dev)
+        cbk[:, :size] = cb[3:].to(dev).view(books, size, gs)
+        return Int4Weight(wq=wt, sz=torch.empty(0, dtype=torch.int32, device=dev), n=int(t.shape[0]), k=k, group=64,
+                          bias=b, fmt=WF_AQLM, codebook=cbk.to(torch.bfloat16).contiguous())
     else:
         raise ValueError(f"no GEMM code format for weight kind {t.kind!r}")
     return Int4Weight(wq=wt, sz=torch.empty(0, dtype=torch.int32, device=dev), n=int(t.shape[0]), k=k,
@@ -222,7 +273,7 @@ def w4a16_linear(x: torch.Tensor, w: Int4Weight, out: torch.Tensor | None = None
         out = torch.empty((m, ncols), dtype=torch.bfloat16, device=x.device)
     native().w4a16_gemm(x, w.wq, w.sz, w.n, w.k, w.group, out, w.bias, residual,
                         EPI_SILU_MUL if silu_mul else EPI_PLAIN, ws.gemm_ws, ws.gemm_counters, ws.status, trace,
-                        w.fmt)
+                        w.fmt, w.codebook)
     _count()
     return out
 

@@ -11,14 +11,14 @@ NF4 = torch.tensor([-1.0, -0.6961928009986877, -0.5250730514526367, -0.394917488
                     -0.18477343022823334, -0.09105003625154495, 0.0, 0.07958029955625534, 0.16093020141124725,
                     0.24611230194568634, 0.33791524171829224, 0.44070982933044434, 0.5626170039176941,
                     0.7229568362236023, 1.0])
-CODE_WORDS = {K.WF_INT4: 1024, K.WF_NF4: 1024, K.WF_INT8: 2048, K.WF_INT2: 512}
+CODE_WORDS = {K.WF_INT4: 1024, K.WF_NF4: 1024, K.WF_INT8: 2048, K.WF_INT2: 512, K.WF_INT3: 768, K.WF_AQLM: 512}
 
 
 def _bf16(bits):
     return (bits.to(torch.int32) << 16).view(torch.float32).to(torch.bfloat16).float()
 
 
-def emulate(wt, fmt, n, k, group):
+def emulate(wt, fmt, n, k, group, books=None):
     """What the kernel's dequant warps produce for every weight (bf16 rounding included)."""
     rb, kb, _ = wt.shape
     gpk = 1 if group >= 64 else 64 // group
@@ -33,8 +33,26 @@ def emulate(wt, fmt, n, k, group):
             sw = aux[:, :, g, :]  # [rb, kb, 128]
             s = _bf16(sw & 0xFFFF)
             z = _bf16(sw >> 16)
+            if fmt == K.WF_AQLM:  # chunk ch = one 8-column group; books[k][idx] summed, times scale
+                word = codes[:, :, c, :, ch // 2]
+                idx = (word >> (16 * (ch % 2))) & 0xFFFF
+                acc = books[0][idx & 0xFF].float()
+                if books.shape[0] > 1:
+                    acc = (acc + books[1][(idx >> 8) & 0xFF].float()).to(torch.bfloat16).float()
+                vals = (acc * s[..., None]).to(torch.bfloat16).float()  # [rb, kb, 128, 8]
+                for j in range(8):
+                    out.view(rb, 128, kb, 64)[:, :, :, c * 32 + ch * 8 + j] = vals[..., j].permute(0, 2, 1)
+                continue
             for j in range(8):
-                if fmt in (K.WF_INT4, K.WF_NF4):
+                if fmt == K.WF_INT3:
+                    p_ = ch * 4 + j // 2
+                    if p_ < 15:
+                        word = codes[:, :, c, :, p_ // 5]
+                        q = (word >> ((j % 2) * 16 + 3 * (p_ % 5))) & 7
+                    else:
+                        q = sum(((codes[:, :, c, :, b] >> (15 + 16 * (j % 2))) & 1) << b for b in range(3))
+                    q = q - 4
+                elif fmt in (K.WF_INT4, K.WF_NF4):
                     word = codes[:, :, c, :, ch]
                     q = (word >> K._NIB_POS[j]) & 0xF
                 elif fmt == K.WF_INT2:
@@ -79,3 +97,25 @@ def test_int4_codes_layout_matches_emulation():
     wt = K.repack_codes(codes, t.scales, t.offsets, 128, 64, K.WF_INT4)
     got = emulate(wt, K.WF_INT4, 256, 128, 64)
     torch.testing.assert_close(got, t.dequantize().float(), atol=3e-3, rtol=2e-2)
+
+
+def test_int3_tile_layout():
+    g = torch.Generator().manual_seed(3)
+    w = torch.randn(200, 256, generator=g) * 0.05
+    t = quantize(w, "q3", 64)
+    dw = K.prepare_weight(t, "cpu")
+    assert dw.fmt == K.WF_INT3
+    got = emulate(dw.wq, K.WF_INT3, 200, 256, 64)
+    torch.testing.assert_close(got, t.dequantize().float(), atol=2e-3, rtol=2e-2)
+
+
+def test_aqlm_tile_layout():
+    from squish_b200.quant.aqlm import aqlm_quantize
+
+    g = torch.Generator().manual_seed(4)
+    w = torch.randn(130, 192, generator=g) * 0.05
+    t = aqlm_quantize(w, n_codebooks=2, codebook_size=256, group_size=8, iters=3)
+    dw = K.prepare_weight(t, "cpu")
+    assert dw.fmt == K.WF_AQLM and dw.codebook.shape == (2, 256, 8)
+    got = emulate(dw.wq, K.WF_AQLM, 130, 192, 64, books=dw.codebook)
+    torch.testing.assert_close(got, t.dequantize().float(), atol=4e-3, rtol=3e-2)

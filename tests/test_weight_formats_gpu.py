@@ -14,7 +14,8 @@ from squish_b200.quant.codecs import quantize
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("kind,group", [("nf4", 64), ("nf4", 32), ("q8", 64), ("q8", 32), ("q2", 64), ("q2", 128)])
+@pytest.mark.parametrize("kind,group", [("nf4", 64), ("nf4", 32), ("q8", 64), ("q8", 32), ("q2", 64), ("q2", 128),
+                                        ("q3", 64), ("q3", 32), ("aqlm", 8)])
 @pytest.mark.parametrize("m", [1, 37, 64, 300])
 def test_gemm_formats_match_fp32(cuda, kind, group, m):
     g = torch.Generator().manual_seed(m + group)
@@ -41,7 +42,7 @@ def test_tensor_op_repack_equals_cuda_int4_repack(cuda):
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("kind", ["nf4", "q8", "q2"])
+@pytest.mark.parametrize("kind", ["nf4", "q8", "q2", "q3", "aqlm"])
 def test_engine_with_format_weights_matches_oracle(cuda, kind):
     from squish_b200.engine.engine import EngineConfig, LLMEngine
     from squish_b200.engine.sampling import SamplingParams
@@ -57,7 +58,13 @@ def test_engine_with_format_weights_matches_oracle(cuda, kind):
     def ck():
         c = random_checkpoint(cfg, q, seed=0)
         for name, _ in linear_names(cfg):
-            c.tensors[name] = quantize(c.tensors[name].dequantize().float(), kind, 32)
+            w = c.tensors[name].dequantize().float()
+            if kind == "aqlm":
+                from squish_b200.quant.aqlm import aqlm_quantize
+
+                c.tensors[name] = aqlm_quantize(w, iters=2)
+            else:
+                c.tensors[name] = quantize(w, kind, 32)
         return c
 
     ref = ReferenceModel(ck())
@@ -66,4 +73,5 @@ def test_engine_with_format_weights_matches_oracle(cuda, kind):
     out = eng.generate([prompt], SamplingParams(max_tokens=8, ignore_eos=True))[0]
     ok, worst = _teacher_forced_ok(ref, prompt, out)
     assert ok, (worst, out)
-    assert eng.runner.layers[0].o.fmt == {"nf4": K.WF_NF4, "q8": K.WF_INT8, "q2": K.WF_INT2}[kind]
+    assert eng.runner.layers[0].o.fmt == {"nf4": K.WF_NF4, "q8": K.WF_INT8, "q2": K.WF_INT2, "q3": K.WF_INT3,
+                                          "aqlm": K.WF_AQLM}[kind]
