@@ -45,6 +45,7 @@ class EngineConfig:
     spec: object | None = None  # speculative.SpecConfig: prompt lookup / draft model / Jacobi
     tp: int = 1                 # tensor-parallel ranks (one process per GPU, torch.distributed initialised)
     tp_mode: str = "nvlink"     # "nvlink": fused GEMM+all-reduce over peer memory; "nccl": NCCL baseline
+    peer_timeout_s: float = 10.0  # a rank whose heartbeat or liveness is older than this has failed
 
 
 @dataclass
@@ -77,6 +78,8 @@ class LLMEngine:
         self.hidden_states: dict[str, np.ndarray] = {}  # rid -> final hidden of the last prompt token
         self.proposer = None
         self.guard = None
+        self.monitor = None   # utils.fault.PeerMonitor (multi-rank engines)
+        self.injector = None  # utils.fault.FaultInjector (SQUISH_FAULT)
         self.spec_stats = {"verifies": 0, "drafted": 0, "accepted": 0, "emitted": 0}
 
     # ------------------------------------------------------------------ construction
@@ -163,6 +166,12 @@ class LLMEngine:
             runner = TorchTPRunner(ck, num_pages, comm, ecfg.max_model_len)
         eng = cls(runner, cfg, ck.quant, ecfg, num_pages)
         eng.comm = comm
+        from ..utils.fault import FaultInjector, PeerMonitor
+
+        rank = dist.get_rank()
+        eng.injector = FaultInjector(rank)
+        eng.monitor = PeerMonitor(dist.distributed_c10d._get_default_store(), rank, dist.get_world_size(),
+                                  timeout_s=ecfg.peer_timeout_s, injector=eng.injector).start_liveness()
         if dev.type == "cuda" and ecfg.cuda_graphs:
             from .cuda_graph import DecodeGraphs
 
@@ -341,6 +350,24 @@ class LLMEngine:
         sched.prefill[:0] = verify
 
     def step(self) -> list[RequestOutput]:
+        if self.monitor is None and self.injector is None:
+            return self._step()
+        n = self.stats.steps
+        try:
+            if self.injector is not None:
+                self.injector.before_step(n, on_hang=self.monitor.stop_liveness if self.monitor else None)
+            if self.monitor is not None:
+                self.monitor.check()  # fail fast, before this step's collectives
+            outs = self._step()
+        except Exception as exc:
+            if self.monitor is not None:
+                self.monitor.announce_error(f"{type(exc).__name__}: {exc}")
+            raise
+        if self.monitor is not None:
+            self.monitor.beat(n + 1)
+        return outs
+
+    def _step(self) -> list[RequestOutput]:
         sched = self.scheduler.schedule()
         self.stats.preemptions += len(sched.preempted)
         if sched.empty:

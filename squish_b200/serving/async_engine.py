@@ -70,6 +70,9 @@ class AsyncEngine:
         self._t_first: dict[str, float] = {}
         self._t_submit: dict[str, float] = {}
         self.last_error: str | None = None
+        from ..utils.fault import Watchdog
+
+        self.watchdog = Watchdog(lambda: bool(self._sinks))
 
     # ------------------------------------------------------------------ lifecycle
     def start(self) -> "AsyncEngine":
@@ -77,11 +80,13 @@ class AsyncEngine:
             self._stop.clear()
             self._thread = threading.Thread(target=self._run, name="squish-engine", daemon=True)
             self._thread.start()
+            self.watchdog.start()
         return self
 
     def stop(self, timeout: float = 5.0) -> None:
         self._stop.set()
         self._wake.set()
+        self.watchdog.stop()
         if self._thread is not None:
             self._thread.join(timeout)
 
@@ -168,6 +173,7 @@ class AsyncEngine:
                 continue
             try:
                 outs = eng.step()
+                self.watchdog.heartbeat()
             except Exception as exc:  # noqa: BLE001 - fail the in-flight requests, keep serving
                 log.exception("engine step failed")
                 self.errors_total += 1

@@ -150,7 +150,10 @@ def create_app(st: ServerState) -> FastAPI:
     async def health():
         a = st.aeng
         gov = st.governor
-        return {"status": "ok" if a.alive else "degraded", "model": st.model_name, "loaded": True,
+        wd = a.watchdog
+        ok = a.alive and not wd.poll()
+        return {"status": "ok" if ok else "degraded", "degraded_reason": None if ok else (wd.reason or "engine stopped"),
+                "model": st.model_name, "loaded": True,
                 "model_loaded": True, "load_mode": "eager", "load_error": a.last_error, "loader": "squish-b200",
                 "load_time_s": round(st.load_time_s, 2), "requests": a.requests_total, "tokens_gen": a.tokens_total,
                 "inflight": a.inflight, "avg_tps": round(a.avg_tps, 1), "avg_ttft_s": round(a.avg_ttft, 3),
