@@ -43,6 +43,8 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
     p.add_argument("--no-cuda-graphs", action="store_true")
     p.add_argument("--no-prefix-caching", "--no-block-kv-cache", dest="no_prefix_caching", action="store_true")
     p.add_argument("--chunk-align", type=int, default=0, help="grid-aligned prefill chunks (bit-exact prefix reuse)")
+    p.add_argument("--kv-host-gb", type=float, default=0.0, help="host-RAM tier for evicted prefix blocks")
+    p.add_argument("--kv-disk-dir", default=None, help="disk tier (persists prefix blocks across restarts)")
 
 
 def _ecfg(a):
@@ -51,7 +53,8 @@ def _ecfg(a):
     return EngineConfig(max_num_seqs=a.max_num_seqs, max_num_batched_tokens=a.max_num_batched_tokens,
                         max_model_len=a.max_model_len, gpu_memory_utilization=a.gpu_memory_utilization,
                         enable_prefix_caching=not a.no_prefix_caching, cuda_graphs=not a.no_cuda_graphs,
-                        chunk_align=a.chunk_align, seed=a.seed)
+                        chunk_align=a.chunk_align, seed=a.seed, kv_host_bytes=int(a.kv_host_gb * (1 << 30)),
+                        kv_disk_dir=a.kv_disk_dir)
 
 
 def _kv(a):

@@ -46,6 +46,9 @@ class EngineConfig:
     tp: int = 1                 # tensor-parallel ranks (one process per GPU, torch.distributed initialised)
     tp_mode: str = "nvlink"     # "nvlink": fused GEMM+all-reduce over peer memory; "nccl": NCCL baseline
     peer_timeout_s: float = 10.0  # a rank whose heartbeat or liveness is older than this has failed
+    kv_host_bytes: int = 0        # > 0: keep evicted prefix blocks in a host-RAM tier of this size
+    kv_disk_dir: str | None = None  # spill (and persist across restarts) evicted prefix blocks here
+    kv_disk_bytes: int = 8 << 30
 
 
 @dataclass
@@ -70,6 +73,12 @@ class LLMEngine:
         self.blocks = BlockManager(num_pages, qcfg.page_size, ecfg.enable_prefix_caching, model_key=cfg.name)
         self.scheduler = Scheduler(self.blocks, ecfg.max_num_seqs, ecfg.max_num_batched_tokens, ecfg.max_model_len,
                                    ecfg.chunk_align)
+        if ecfg.enable_prefix_caching and (ecfg.kv_host_bytes > 0 or ecfg.kv_disk_dir):
+            from ..kv.tiers import KVTierStore, PageIO, layout_of
+
+            rc = getattr(runner, "cfg", cfg)
+            self.blocks.tier = KVTierStore(PageIO(runner), layout_of(rc, qcfg), host_bytes=ecfg.kv_host_bytes,
+                                           disk_dir=ecfg.kv_disk_dir, disk_bytes=ecfg.kv_disk_bytes)
         self.requests: dict[str, Request] = {}
         self._ids = itertools.count()
         self.stats = EngineStats()
@@ -188,6 +197,11 @@ class LLMEngine:
         dev = torch.device(device)
         ck = random_checkpoint(cfg, q, seed=seed, device=dev)
         return cls.from_checkpoint(ck, dev, ecfg, **kw)
+
+    def close(self) -> None:
+        """Persist the host KV tier to disk (when a disk tier is configured)."""
+        if self.blocks.tier is not None:
+            self.blocks.tier.flush()
 
     # ------------------------------------------------------------------ requests
     def add_request(self, prompt: list[int], params: SamplingParams | None = None, rid: str | None = None) -> str:

@@ -109,6 +109,8 @@ class BlockManager:
         self.evictable: OrderedDict[int, None] = OrderedDict()
         self.hits = 0
         self.hit_tokens = 0
+        self.tier = None  # kv.tiers.KVTierStore: host / disk copies of evicted cached blocks
+        self.tier_hits = 0
 
     # ------------------------------------------------------------------ capacity
     def num_free(self) -> int:
@@ -129,6 +131,8 @@ class BlockManager:
             h = self.page_hash.pop(p, None)
             if h is not None and self.hash_to_page.get(h) == p:
                 del self.hash_to_page[h]
+                if self.tier is not None:
+                    self.tier.offload(h, p)  # keep the block's contents before the page is reused
         else:
             raise OutOfPages("KV cache is full")
         self.ref[p] = 1
@@ -150,9 +154,10 @@ class BlockManager:
         if not self.enable_prefix_caching:
             return PrefixHit([], 0)
         max_blocks = (len(tokens) - 1) // self.page_size
+        hashes = chain_hashes(tokens, self.page_size, self.model_key, max_blocks)
         pages = []
         last = None
-        for h in chain_hashes(tokens, self.page_size, self.model_key, max_blocks):
+        for h in hashes:
             p = self.hash_to_page.get(h)
             if p is None:
                 break
@@ -162,6 +167,20 @@ class BlockManager:
             if self.ref[p] == 0:
                 self.evictable.pop(p, None)
             self.ref[p] += 1
+        if self.tier is not None:
+            # continue the run from the host / disk tiers into fresh device pages
+            for h in hashes[len(pages):]:
+                if not self.tier.has(h) or not self.can_allocate(1):
+                    break
+                p = self.allocate()
+                if not self.tier.restore(h, p):
+                    self.release([p])
+                    break
+                self.hash_to_page[h] = p
+                self.page_hash[p] = h
+                pages.append(p)
+                last = h
+                self.tier_hits += 1
         if pages:
             self.hits += 1
             self.hit_tokens += len(pages) * self.page_size
