@@ -418,6 +418,29 @@ std::vector<int64_t> w4a16_gemm_push(torch::Tensor x, torch::Tensor wq, int64_t 
   return {bn, nt, plan[2], gx, gy};
 }
 
+void tp_push(torch::Tensor src, torch::Tensor push_dst, int64_t parity_stride, int64_t ld_dst,
+             torch::Tensor push_flags, int64_t flag_stride, int64_t tile_m, int64_t grid_x, int64_t grid_y, int64_t tp,
+             torch::Tensor seq) {
+  CHECK_CUDA(src);
+  CHECK_DT(src, torch::kBFloat16);
+  TORCH_CHECK(src.stride(1) == 1, "src must have unit column stride");
+  const c10::cuda::CUDAGuard g(src.device());
+  sq::TpPushParams p{};
+  p.src = ptr<__nv_bfloat16>(src);
+  p.ld_src = (int)src.stride(0);
+  p.dst = reinterpret_cast<__nv_bfloat16* const*>(push_dst.data_ptr());
+  p.parity_stride = parity_stride;
+  p.ld_dst = (int)ld_dst;
+  p.flags = reinterpret_cast<int* const*>(push_flags.data_ptr());
+  p.flag_stride = (int)flag_stride;
+  p.M = (int)src.size(0);
+  p.N = (int)src.size(1);
+  p.tile_m = (int)tile_m;
+  p.tp = (int)tp;
+  p.seq = ptr<int>(seq);
+  CUDA_OK(sq::tp_push_launch(p, (int)grid_x, (int)grid_y, cur_stream()));
+}
+
 void tp_reduce(torch::Tensor recv, int64_t recv_stride, int64_t src_stride, int64_t ld, torch::Tensor flags,
                int64_t flag_stride, int64_t flag_src_stride, int64_t expect, torch::Tensor out, bool residual,
                int64_t M, int64_t N, int64_t tile_m, int64_t tile_n, int64_t grid_x, int64_t grid_y, int64_t tp,
@@ -662,6 +685,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("w4a16_gemm_push", &w4a16_gemm_push);
   m.def("tp_reduce", &tp_reduce);
+  m.def("tp_push", &tp_push);
   m.def("tp_gather", &tp_gather);
   m.def("kv_compact", &kv_compact);
   m.def("moe_align", &moe_align);

@@ -98,6 +98,29 @@ __global__ void __launch_bounds__(256) tp_reduce_kernel(const TpReduceParams p) 
   }
 }
 
+__global__ void __launch_bounds__(256) tp_push_kernel(const TpPushParams p) {
+  pdl_wait();
+  pdl_trigger();
+  const int par = *reinterpret_cast<volatile const int*>(p.seq) & 1;
+  const int n0 = blockIdx.x * 128, m0 = blockIdx.y * p.tile_m;
+  const int n1 = min(p.N, n0 + 128), m1 = min(p.M, m0 + p.tile_m);
+  const int w = n1 - n0;
+  for (int idx = threadIdx.x; idx < (m1 - m0) * w; idx += blockDim.x) {
+    const int m = m0 + idx / w, n = n0 + idx % w;
+    const __nv_bfloat16 v = p.src[(size_t)m * p.ld_src + n];
+    for (int r = 0; r < p.tp; ++r) p.dst[r][(size_t)par * p.parity_stride + (size_t)m * p.ld_dst + n] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int tile = blockIdx.x * gridDim.y + blockIdx.y;
+    for (int r = 0; r < p.tp; ++r) {
+      int* f = p.flags[r] + (size_t)par * p.flag_stride + tile;
+      asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(f), "r"(1) : "memory");
+    }
+  }
+}
+
 // src [rows, cols] is written into every rank's dst at rows row0.., columns col0..
 __global__ void __launch_bounds__(256) tp_gather_push_kernel(const TpGatherParams p) {
   pdl_wait();
@@ -140,6 +163,12 @@ __global__ void tp_gather_wait_kernel(const TpGatherParams p) {
 cudaError_t tp_reduce_launch(const TpReduceParams& p, int grid_x, int grid_y, cudaStream_t s) {
   if (p.tp > 256) return cudaErrorInvalidValue;
   SQ_LAUNCH(tp_reduce_kernel, dim3(dim3(grid_x, grid_y)), dim3(256), 0, s, 1, p);
+  return cudaGetLastError();
+}
+
+cudaError_t tp_push_launch(const TpPushParams& p, int grid_x, int grid_y, cudaStream_t s) {
+  if (p.M == 0) return cudaSuccess;
+  SQ_LAUNCH(tp_push_kernel, dim3(grid_x, grid_y), dim3(256), 0, s, 1, p);
   return cudaGetLastError();
 }
 

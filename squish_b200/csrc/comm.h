@@ -37,6 +37,20 @@ struct TpGatherParams {
   int* status;
 };
 
+// Push a [M, N] bf16 partial into every rank's receive slot for this source, tile by tile
+// (tile_m x 128 columns, the tp_reduce numbering), bumping each tile's flag on every rank.
+struct TpPushParams {
+  const __nv_bfloat16* src;
+  int ld_src;
+  __nv_bfloat16* const* dst;  // [tp] receive slot of this source on every rank (parity 0)
+  long long parity_stride;    // elements
+  int ld_dst;
+  int* const* flags;          // [tp] this source's flag row on every rank (parity 0)
+  int flag_stride;
+  int M, N, tile_m, tp;
+  const int* seq;
+};
+cudaError_t tp_push_launch(const TpPushParams& p, int grid_x, int grid_y, cudaStream_t s);
 cudaError_t tp_reduce_launch(const TpReduceParams& p, int grid_x, int grid_y, cudaStream_t s);
 cudaError_t tp_gather_launch(const TpGatherParams& p, cudaStream_t s);
 

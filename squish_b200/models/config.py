@@ -36,6 +36,8 @@ class ModelConfig:
     num_experts_per_tok: int = 0
     moe_intermediate_size: int = 0
     norm_topk_prob: bool = True
+    expert_offset: int = 0       # expert parallelism: this rank holds experts
+    num_local_experts: int = 0   # [expert_offset, expert_offset + num_local_experts) (0 = all)
     rope_scaling: dict | None = None
     bos_token_id: int = 1
     eos_token_id: int = 2

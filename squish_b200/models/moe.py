@@ -31,10 +31,11 @@ class MoEScratch:
     def __init__(self, cfg: ModelConfig, max_tokens: int, device):
         dev = torch.device(device)
         E, K, H = cfg.num_experts, cfg.num_experts_per_tok, cfg.hidden_size
+        El = cfg.num_local_experts or E
         F = (cfg.moe_intermediate_size + 63) // 64 * 64
         T = max(max_tokens, 1)
-        bn = K_.moe_tile(T, K, E)
-        P = K_.moe_padded_rows(T, K, E, bn)
+        bn = K_.moe_tile(T, K, El)
+        P = K_.moe_padded_rows(T, K, El, bn)
         i32 = torch.int32
         self.max_tokens = T
         self.logits = torch.empty(T, E, dtype=torch.bfloat16, device=dev)
@@ -44,7 +45,8 @@ class MoEScratch:
         self.slot_pos = torch.empty(T * K, dtype=i32, device=dev)
         self.tile_expert = torch.empty(P // 16, dtype=i32, device=dev)
         self.num_tiles = torch.zeros(1, dtype=i32, device=dev)
-        self.counts = torch.zeros(E, dtype=i32, device=dev)
+        self.counts = torch.zeros(El, dtype=i32, device=dev)
+        self.part = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)  # expert-parallel partial output
         self.xs = torch.empty(P, H, dtype=torch.bfloat16, device=dev)
         self.act = torch.empty(P, F, dtype=torch.bfloat16, device=dev)
         self.ys = torch.empty(P, H, dtype=torch.bfloat16, device=dev)
@@ -65,7 +67,11 @@ class MoELayer:
         self.down = down
         self.scratch = scratch
         self.E, self.K = cfg.num_experts, cfg.num_experts_per_tok
+        self.E_local = cfg.num_local_experts or cfg.num_experts
+        self.offset = cfg.expert_offset
         self.F = cfg.moe_intermediate_size
+        # expert parallelism: callable(partial, h) adding the all-reduced partial to h
+        self.ep_reduce = None
 
     @classmethod
     def from_checkpoint(cls, ck: Checkpoint, layer: int, device, scratch: MoEScratch | None = None) -> "MoELayer":
@@ -76,7 +82,8 @@ class MoELayer:
         p = f"model.layers.{layer}.mlp."
         g = ck.quant.group_size
         gu, dn = [], []
-        for e in range(cfg.num_experts):
+        e0 = cfg.expert_offset
+        for e in range(e0, e0 + (cfg.num_local_experts or cfg.num_experts)):
             q = p + f"experts.{e}."
             w = _interleave(_as_q4a(t[q + "gate_proj.weight"], g), _as_q4a(t[q + "up_proj.weight"], g))
             gu.append(ops.prepare_int4_weight(w.packed, w.scales, w.offsets, w.shape[1], w.group, dev))
@@ -93,12 +100,14 @@ class MoELayer:
             return
         if sc is None or T > sc.max_tokens:
             sc = self.scratch = MoEScratch(self.cfg, max(T, sc.max_tokens if sc else 0), x.device)
-        E, K = self.E, self.K
+        E, K = self.E_local, self.K
         bn = K_.moe_tile(T, K, E)
         P = K_.moe_padded_rows(T, K, E, bn)
         TK = T * K
         logits = torch.mm(x, self.gate_w.t(), out=sc.logits[:T])
         K_.moe_route(logits, K, self.cfg.norm_topk_prob, sc.ids[:TK], sc.w[:TK])
+        if self.offset:
+            sc.ids[:TK].sub_(self.offset)  # global -> local expert ids; others fall outside [0, E_local)
         K_.moe_align(sc.ids[:TK], E, bn, sc.sorted_slot[:P], sc.slot_pos[:TK], sc.tile_expert[: P // bn],
                      sc.num_tiles, sc.counts)
         K_.moe_gather(x, sc.sorted_slot[:P], sc.num_tiles, bn, K, sc.xs[:P])
@@ -106,4 +115,10 @@ class MoELayer:
                                       sc.tile_expert[: P // bn], sc.num_tiles, bn, silu_mul=True, ws=ws)
         K_.w4a16_grouped_linear(act[:, : self.F], self.down, sc.ys[:P], sc.tile_expert[: P // bn], sc.num_tiles, bn,
                                 ws=ws)
-        K_.moe_combine(sc.ys[:P], sc.slot_pos[:TK], sc.w[:TK], K, h)
+        if self.ep_reduce is None:
+            K_.moe_combine(sc.ys[:P], sc.slot_pos[:TK], sc.w[:TK], K, h)
+        else:
+            part = sc.part[:T]
+            part.zero_()
+            K_.moe_combine(sc.ys[:P], sc.slot_pos[:TK], sc.w[:TK], K, part)
+            self.ep_reduce(part, h)

@@ -76,6 +76,7 @@ class ReferenceModel:
     # with an all-reduce, and the vocab-parallel LM head with a gather
     rp_hook = None
     head_hook = None
+    reduce_hook = None  # expert parallelism: all-reduce of the local experts' partial output
 
     def _rp(self, x: torch.Tensor, wt: torch.Tensor) -> torch.Tensor:
         return x @ wt.T if self.rp_hook is None else self.rp_hook(x, wt)
@@ -95,14 +96,18 @@ class ReferenceModel:
         if cfg.norm_topk_prob:
             topv = topv / topv.sum(-1, keepdim=True)
         out = torch.zeros_like(x)
+        e0 = cfg.expert_offset
+        e1 = e0 + (cfg.num_local_experts or cfg.num_experts)
         for t in range(x.shape[0]):
             for j in range(topi.shape[1]):
                 e = int(topi[t, j])
+                if not e0 <= e < e1:
+                    continue
                 q = p + f"mlp.experts.{e}."
                 g = x[t] @ w[q + "gate_proj.weight"].T
                 u = x[t] @ w[q + "up_proj.weight"].T
                 out[t] += topv[t, j] * ((torch.nn.functional.silu(g) * u) @ w[q + "down_proj.weight"].T)
-        return out
+        return out if self.reduce_hook is None else self.reduce_hook(out)
 
     @torch.no_grad()
     def forward(self, tokens: list[int], cache, start_pos: int) -> torch.Tensor:

@@ -118,6 +118,30 @@ class TPComm:
                            self.done, self.status)
         K._count(2)
 
+    def allreduce_add(self, x: torch.Tensor, h: torch.Tensor) -> None:
+        """h += all_reduce(x) over the group (x: [T, hidden] partial, e.g. local experts' output)."""
+        from ..ops import kernels as K
+
+        T = x.shape[0]
+        if self.mode != "nvlink":
+            tmp = self.tmp[:T]
+            tmp.copy_(x.to(tmp.dtype))
+            dist.all_reduce(tmp, group=self.group)
+            h.add_(tmp.to(h.dtype))
+            return
+        if T > self.max_tokens or x.shape[1] != self.hidden:
+            raise ValueError("all-reduce input exceeds the peer buffers")
+        N, tile_m = x.shape[1], 64
+        gx, gy = (N + 127) // 128, (T + tile_m - 1) // tile_m
+        if gx * gy > self.max_tiles:
+            raise ValueError("all-reduce tile grid exceeds the flag array")
+        native().tp_push(x, self.push_dst, self.recv_stride, N, self.push_flags, self.tp * self.max_tiles, tile_m,
+                         gx, gy, self.tp, self.seq)
+        native().tp_reduce(self.recv, self.recv_stride, self.src_stride, N, self.flags, self.tp * self.max_tiles,
+                           self.max_tiles, 1, h, True, T, N, tile_m, 128, gx, gy, self.tp, self.seq, self.done,
+                           self.status)
+        K._count(2)
+
     def gather_logits(self, local: torch.Tensor, B: int) -> torch.Tensor:
         """[B, v1 - v0] vocab shard on every rank -> [B, vocab] on every rank."""
         from ..ops import kernels as K

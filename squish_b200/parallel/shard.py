@@ -10,6 +10,11 @@
 Row-parallel outputs are partial sums: the runner all-reduces them (fused GEMM+all-reduce
 over NVLink, or NCCL). The local shard is a regular Checkpoint of a local ModelConfig, so
 the single-GPU runner code runs it unchanged.
+
+Mixture-of-experts layers use expert parallelism over the same ranks: attention is
+tensor-parallel as above, the router is replicated, rank r keeps experts
+[r E/tp, (r+1) E/tp), computes the MoE output of the routed slots that land on its
+experts, and the partial outputs are all-reduced like a row-parallel projection.
 """
 from __future__ import annotations
 
@@ -71,11 +76,15 @@ def kv_heads_of(rank: int, tp: int, hkv: int) -> tuple[int, int]:
 def local_config(cfg: ModelConfig, tp: int) -> ModelConfig:
     if cfg.num_heads % tp:
         raise ValueError(f"{cfg.num_heads} query heads do not split over {tp} ranks")
+    hkv = max(1, cfg.num_kv_heads // tp)
     if cfg.is_moe:
-        raise ValueError("tensor parallelism of MoE layers is not supported; use expert parallelism")
+        # attention tensor-parallel, experts split over the same ranks (expert parallelism)
+        if cfg.num_experts % tp:
+            raise ValueError(f"{cfg.num_experts} experts do not split over {tp} ranks")
+        return dataclasses.replace(cfg, name=f"{cfg.name}-tp{tp}", num_heads=cfg.num_heads // tp, num_kv_heads=hkv,
+                                   num_local_experts=cfg.num_experts // tp)
     if cfg.intermediate_size % tp:
         raise ValueError(f"FFN width {cfg.intermediate_size} does not split over {tp} ranks")
-    hkv = max(1, cfg.num_kv_heads // tp)
     return dataclasses.replace(cfg, name=f"{cfg.name}-tp{tp}", num_heads=cfg.num_heads // tp, num_kv_heads=hkv,
                                intermediate_size=cfg.intermediate_size // tp)
 
@@ -96,7 +105,7 @@ def shard_checkpoint(ck: Checkpoint, rank: int, tp: int) -> Checkpoint:
     q0, q1 = rank * hq_l * d, (rank + 1) * hq_l * d
     k0h, k1h = kv_heads_of(rank, tp, cfg.num_kv_heads)
     k0, k1 = k0h * d, k1h * d
-    f_l = cfg.intermediate_size // tp
+    f_l = cfg.intermediate_size // tp if not cfg.is_moe else 0
     f0, f1 = rank * f_l, (rank + 1) * f_l
     for i in range(cfg.num_layers):
         p = f"model.layers.{i}."
@@ -113,9 +122,17 @@ def shard_checkpoint(ck: Checkpoint, rank: int, tp: int) -> Checkpoint:
             if a + n in t:
                 out.tensors[a + n] = t[a + n]
         m = p + "mlp."
-        out.tensors[m + "gate_proj.weight"] = _rows(t[m + "gate_proj.weight"], f0, f1)
-        out.tensors[m + "up_proj.weight"] = _rows(t[m + "up_proj.weight"], f0, f1)
-        out.tensors[m + "down_proj.weight"] = _cols(t[m + "down_proj.weight"], f0, f1)
+        if cfg.is_moe:
+            e_loc = cfg.num_experts // tp
+            lc.expert_offset = rank * e_loc
+            out.tensors[m + "gate.weight"] = t[m + "gate.weight"]  # the router sees every expert
+            for e in range(rank * e_loc, (rank + 1) * e_loc):
+                for n in ("gate_proj", "up_proj", "down_proj"):
+                    out.tensors[m + f"experts.{e}.{n}.weight"] = t[m + f"experts.{e}.{n}.weight"]
+        else:
+            out.tensors[m + "gate_proj.weight"] = _rows(t[m + "gate_proj.weight"], f0, f1)
+            out.tensors[m + "up_proj.weight"] = _rows(t[m + "up_proj.weight"], f0, f1)
+            out.tensors[m + "down_proj.weight"] = _cols(t[m + "down_proj.weight"], f0, f1)
         for n in ("input_layernorm.weight", "post_attention_layernorm.weight"):
             out.tensors[p + n] = t[p + n]
     out.tensors["model.embed_tokens.weight"] = t["model.embed_tokens.weight"]

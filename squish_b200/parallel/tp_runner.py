@@ -27,6 +27,9 @@ class TPCudaRunner(CudaRunner):
         self.logits_local = torch.empty(R, comm.v1 - comm.v0, dtype=torch.bfloat16, device=self.device)
         del self.logits
         self.logits = comm.logits_full
+        for lw in self.layers:  # expert parallelism: all-reduce the local experts' partial output
+            if lw.moe is not None:
+                lw.moe.ep_reduce = lambda part, h: self.comm.allreduce_add(part, h)
 
     def _row_parallel(self, x, w, h):
         self.comm.gemm_allreduce(x, w, h, self.ws)
@@ -50,6 +53,12 @@ class TorchTPRunner(TorchPagedRunner):
         super().__init__(local, num_pages, max_model_len)
         self.ref.rp_hook = self._rp
         self.ref.head_hook = self._head
+        self.ref.reduce_hook = self._reduce
+
+    def _reduce(self, part: torch.Tensor) -> torch.Tensor:
+        out = torch.zeros_like(part)
+        self.comm.allreduce_add(part, out)
+        return out
 
     def _rp(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         out = torch.zeros(x.shape[0], w.shape[0])

@@ -17,8 +17,10 @@ from squish_b200.models.reference import ReferenceModel
 from squish_b200.models.weights import random_checkpoint
 
 
-def _cfg():
-    cfg, q = get_preset("tiny-llama")
+def _cfg(preset="tiny-llama"):
+    cfg, q = get_preset(preset)
+    if preset == "tiny-moe":
+        return dataclasses.replace(cfg, tie_embeddings=False), q
     return dataclasses.replace(cfg, tie_embeddings=False, intermediate_size=512), q
 
 
@@ -27,11 +29,11 @@ def _prompts(vocab):
     return [rng.integers(0, vocab, 23).tolist(), rng.integers(0, vocab, 40).tolist()]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, preset="tiny-llama"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        cfg, qc = _cfg()
+        cfg, qc = _cfg(preset)
         ck = random_checkpoint(cfg, qc, seed=0)
         eng = LLMEngine.from_checkpoint(ck, "cpu", EngineConfig(max_num_seqs=4, max_num_batched_tokens=64,
                                                                 max_model_len=256, num_pages=64, tp=world))
@@ -51,12 +53,12 @@ def _port():
     return p
 
 
-@pytest.mark.parametrize("world", [2])
-def test_tp_engine_matches_single_process(world):
+@pytest.mark.parametrize("world,preset", [(2, "tiny-llama"), (2, "tiny-moe")])
+def test_tp_engine_matches_single_process(world, preset):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, preset)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=600) for _ in range(world)])
@@ -65,7 +67,7 @@ def test_tp_engine_matches_single_process(world):
         assert p.exitcode == 0
     # every rank emitted the same tokens (replicated host logic)
     assert all(r[1] == res[0][1] and r[2] == res[0][2] for r in res)
-    cfg, qc = _cfg()
+    cfg, qc = _cfg(preset)
     ref = ReferenceModel(random_checkpoint(cfg, qc, seed=0))
     from .test_engine_gpu import _teacher_forced_ok
 

@@ -67,6 +67,19 @@ def _collectives_worker(rank, world, port, q):
             ref = hh.clone()
             dist.broadcast(ref, 0)
             assert torch.equal(ref, hh)
+        # generic push all-reduce (expert-parallel partial outputs)
+        for T in (3, 130):
+            part = (torch.randn(T, H, generator=torch.Generator().manual_seed(rank * 100 + T)) * 0.1)
+            base = torch.randn(T, H, generator=torch.Generator().manual_seed(T))
+            hh = base.to(torch.bfloat16).to(dev)
+            comm.allreduce_add(part.to(torch.bfloat16).to(dev), hh)
+            torch.cuda.synchronize()
+            tot = part.to(torch.bfloat16).float().to(dev)
+            dist.all_reduce(tot)
+            want = base.to(torch.bfloat16).float() + tot.cpu()
+            # bf16 output: compare against the magnitude of the result, not of the partials
+            errs.append(float((hh.float().cpu() - want).abs().max()) / float(want.abs().max()))
+        comm.check()
         # vocab gather
         from squish_b200.parallel.shard import vocab_shard
 
@@ -81,7 +94,7 @@ def _collectives_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def _engine_worker(rank, world, port, mode, q):
+def _engine_worker(rank, world, port, mode, preset, q):
     _init(rank, world, port)
     try:
         from squish_b200.engine.engine import EngineConfig, LLMEngine
@@ -89,8 +102,7 @@ def _engine_worker(rank, world, port, mode, q):
         from squish_b200.models.config import get_preset
         from squish_b200.models.weights import random_checkpoint
 
-        cfg, qc = get_preset("tiny-llama")
-        cfg = dataclasses.replace(cfg, tie_embeddings=False, intermediate_size=512)
+        cfg, qc = _preset(preset)
         ck = random_checkpoint(cfg, qc, seed=0)
         eng = LLMEngine.from_checkpoint(ck, torch.device("cuda", rank), EngineConfig(
             max_num_seqs=4, max_num_batched_tokens=128, max_model_len=256, num_pages=64, tp=world, tp_mode=mode))
@@ -119,6 +131,15 @@ def _run(target, world, *args):
     return res
 
 
+def _preset(name):
+    from squish_b200.models.config import get_preset
+
+    cfg, qc = get_preset(name)
+    if name == "tiny-moe":
+        return dataclasses.replace(cfg, tie_embeddings=False), qc
+    return dataclasses.replace(cfg, tie_embeddings=False, intermediate_size=512), qc
+
+
 needs2 = pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 
 
@@ -131,18 +152,17 @@ def test_fused_gemm_allreduce_and_gather():
 
 
 @needs2
-@pytest.mark.parametrize("mode", ["nvlink", "nccl"])
-def test_tp_engine_matches_oracle(mode):
-    from squish_b200.models.config import get_preset
+@pytest.mark.parametrize("mode,preset", [("nvlink", "tiny-llama"), ("nccl", "tiny-llama"), ("nvlink", "tiny-moe"),
+                                         ("nccl", "tiny-moe")])
+def test_tp_engine_matches_oracle(mode, preset):
     from squish_b200.models.reference import ReferenceModel
     from squish_b200.models.weights import random_checkpoint
 
     from .test_engine_gpu import _teacher_forced_ok
 
-    res = _run(_engine_worker, 2, mode)
+    res = _run(_engine_worker, 2, mode, preset)
     assert res[0][2] == res[1][2]
-    cfg, qc = get_preset("tiny-llama")
-    cfg = dataclasses.replace(cfg, tie_embeddings=False, intermediate_size=512)
+    cfg, qc = _preset(preset)
     ref = ReferenceModel(random_checkpoint(cfg, qc, seed=0))
     for p, o in zip(res[0][1], res[0][2]):
         ok, worst = _teacher_forced_ok(ref, p, o)
