@@ -85,6 +85,8 @@ def main():
     ap.add_argument("--copies", type=int, default=8, help="weight copies cycled (their total exceeds L2)")
     ap.add_argument("--json", default=None)
     ap.add_argument("--ms", default="1,16,64,128,512,2048")
+    ap.add_argument("--ops", default="qkv,o_proj,gate_up,down,lm_head", help="GEMM shapes to time")
+    ap.add_argument("--no-attn", action="store_true", help="skip the attention timings")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     cfg, q = get_preset(args.model)
@@ -95,6 +97,8 @@ def main():
     rows = []
     ms = [int(x) for x in args.ms.split(",")]
     for name, (n, k) in shapes.items():
+        if name not in args.ops.split(","):
+            continue
         wb = n * k // 2
         copies = max(2, min(args.copies, -(-384 * 2**20 // wb)))  # > 3x L2 of weights in the rotation
         wts = rand_int4(n, k, q.group_size, dev, copies)
@@ -122,6 +126,20 @@ def main():
                          "bound": "hbm" if t_bw > t_fl else "tensor", "plan": plan})
         del wts
         torch.cuda.empty_cache()
+    if not args.no_attn:
+        rows += other_ops(args, cfg, q, dev, hbm, tflops)
+    for r in rows:
+        print(json.dumps(r))
+    print(json.dumps({"peaks": {"hbm_gbs": hbm, "bf16_tflops": tflops, "basis": tag}}))
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(rows, f, indent=1)
+
+
+def other_ops(args, cfg, q, dev, hbm, tflops):
+    """Attention, RMSNorm, RoPE + KV write and sampler timings."""
+    rows = []
+    h = cfg.hidden_size
     # attention (INT4 g32 pages)
     from squish_b200.kv.paged import kv_row_bytes
 
@@ -211,12 +229,7 @@ def main():
         tp = torch.full((B,), 0.9, device=dev)
         rows.append({"op": "sampler top-p", "B": B,
                      "ms": time_op(lambda: ops.sample(lg, o, temperature=tmp, top_p=tp, seed=1), args.iters)})
-    for r in rows:
-        print(json.dumps(r))
-    print(json.dumps({"peaks": {"hbm_gbs": hbm, "bf16_tflops": tflops, "basis": tag}}))
-    if args.json:
-        with open(args.json, "w") as f:
-            json.dump(rows, f, indent=1)
+    return rows
 
 
 if __name__ == "__main__":

@@ -101,7 +101,7 @@ std::vector<torch::Tensor> repack_int4(torch::Tensor packed, torch::Tensor scale
 }
 
 // Tile choice shared by the GEMM launch and the workspace sizing in Python.
-std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
+std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t group = 64, int64_t wfmt = 0) {
   int bn, nt = 1;
   if (M <= 16) bn = 16;
   else if (M <= 32) bn = 32;
@@ -138,12 +138,24 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
     tiles = tiles_of(bn, nt);
   }
   int64_t splits = 1;
-  const int64_t slots = (bn <= 64) ? 2 * sms : sms;  // decode shapes run two CTAs per SM
-  if (tiles * 2 <= slots) {
-    // split-K over a thread-block cluster (<= 8 CTAs, portable cluster size)
-    splits = std::min<int64_t>({slots / tiles, std::max<int64_t>(1, kb / 4), 8});
+  // decode shapes run two CTAs per SM, four with the 4-dequant-warp configuration
+  const bool narrow = bn <= 64 && sq::w4a16_narrow((int)wfmt, group >= 64 ? 1 : (int)(64 / group));
+  const int64_t slots = (bn <= 64) ? (narrow ? 4 : 2) * sms : sms;
+  if (tiles * 2 < slots) {
+    // split-K over a thread-block cluster: up to 8 CTAs (portable size), 16 for the narrow
+    // configuration; at least 7 (narrow) / 4 k-blocks per split (measured on B200: qkv / o_proj
+    // of a 7B model are fastest at 8 splits, down (K = 18944) at 16)
+    const int64_t max_s = narrow ? 16 : 8, min_kps = narrow ? 7 : 4;
+    splits = std::min<int64_t>({slots / tiles, std::max<int64_t>(1, kb / min_kps), max_s});
     splits = std::max<int64_t>(splits, 1);
   }
+  static int ov_splits = -1;
+  static bool ov_s_read = false;
+  if (!ov_s_read) {  // tuning override for experiments: SQ_GEMM_SPLITS=n (1..16) for every NT=1 plan
+    ov_s_read = true;
+    if (const char* e = std::getenv("SQ_GEMM_SPLITS")) ov_splits = std::atoi(e);
+  }
+  if (ov_splits > 0 && nt == 1) splits = std::min<int64_t>({ov_splits, 16, kb});
   int64_t kps = (kb + splits - 1) / splits;
   splits = (kb + kps - 1) / kps;
   return {bn, nt, splits, kps, tiles};
@@ -170,7 +182,7 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, 
   const int64_t M = x.size(0);
   if (M == 0) return;
   const c10::cuda::CUDAGuard g(x.device());
-  auto plan = gemm_plan(M, N, K);
+  auto plan = gemm_plan(M, N, K, group, wfmt);
   const int bn = (int)plan[0], nt = (int)plan[1];
   sq::W4A16Params p{};
   p.wq = ptr<uint32_t>(wq);
@@ -386,7 +398,7 @@ std::vector<int64_t> w4a16_gemm_push(torch::Tensor x, torch::Tensor wq, int64_t 
   TORCH_CHECK(push_flags.scalar_type() == torch::kInt64 && push_flags.numel() == tp, "push_flags: [tp] pointers");
   const int64_t M = x.size(0);
   const c10::cuda::CUDAGuard g(x.device());
-  auto plan = gemm_plan(M, N, K);
+  auto plan = gemm_plan(M, N, K, group, sq::WF_INT4);
   const int bn = (int)plan[0], nt = (int)plan[1];
   sq::W4A16Params p{};
   p.wq = ptr<uint32_t>(wq);
@@ -673,7 +685,8 @@ std::vector<torch::Tensor> quantize_int4_asym_cuda(torch::Tensor x, int64_t grou
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "squish_b200 native kernels (sm_100a CUDA + C++ CPU reference)";
   m.def("repack_int4", &repack_int4);
-  m.def("gemm_plan", &gemm_plan);
+  m.def("gemm_plan", &gemm_plan, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("group") = 64,
+        py::arg("wfmt") = 0);
   m.def("w4a16_gemm", &w4a16_gemm);
   m.def("w4a16_grouped_gemm", &w4a16_grouped_gemm);
   m.def("moe_route", &moe_route);

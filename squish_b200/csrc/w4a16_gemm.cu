@@ -56,7 +56,7 @@ struct Cfg {
   // Single weight tile per CTA: the dequantized A operand goes to tensor memory (tcgen05.st)
   // instead of shared memory; columns [kA0, kA0 + 32 * ring_a) hold the A ring.
   static constexpr bool AT = (NT == 1);
-  static constexpr int kMaxRingA = 4;
+  static constexpr int kMaxRingA = MINB_ >= 3 ? 2 : 4;  // 3+ CTAs per SM share 512 TMEM columns
   static constexpr int kA0 = AT ? (NT * BN < 32 ? 32 : NT * BN) : 0;
   static constexpr int kCols = AT ? kA0 + 32 * kMaxRingA : NT * BN;
   static constexpr int kTmemCols = (kCols <= 32) ? 32 : (kCols <= 64) ? 64 : (kCols <= 128) ? 128 : (kCols <= 256) ? 256 : 512;
@@ -457,7 +457,12 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         }
         // nibble words of a row: [2 halves][128 rows][4 words]
         uint32_t ww[WPT];
-        if constexpr (WPT == 4) {
+        if constexpr (WPT == 8) {  // the whole row: both 32-column halves
+          const uint4 a = *reinterpret_cast<const uint4*>(tb + r * 16);
+          const uint4 b = *reinterpret_cast<const uint4*>(tb + (BM + r) * 16);
+          ww[0] = a.x; ww[1] = a.y; ww[2] = a.z; ww[3] = a.w;
+          ww[4] = b.x; ww[5] = b.y; ww[6] = b.z; ww[7] = b.w;
+        } else if constexpr (WPT == 4) {
           const uint4 wv = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 16);
           ww[0] = wv.x;
           ww[1] = wv.y;
@@ -493,7 +498,17 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         // this thread's 8*WPT K values of row r = 4*WPT columns of its lane in the A stage
         tc_fence_after();
         const uint32_t col = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(C::kA0 + ra.s * 32 + c * WPT * 4);
-        if constexpr (WPT == 4) {
+        if constexpr (WPT == 8) {
+          uint32_t regs[32];
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            regs[4 * w] = o[0][w].x;
+            regs[4 * w + 1] = o[0][w].y;
+            regs[4 * w + 2] = o[0][w].z;
+            regs[4 * w + 3] = o[0][w].w;
+          }
+          tmem_st32(col, regs);
+        } else if constexpr (WPT == 4) {
           const uint32_t regs[16] = {o[0][0].x, o[0][0].y, o[0][0].z, o[0][0].w, o[0][1].x, o[0][1].y,
                                      o[0][1].z, o[0][1].w, o[0][2].x, o[0][2].y, o[0][2].z, o[0][2].w,
                                      o[0][3].x, o[0][3].y, o[0][3].z, o[0][3].w};
@@ -621,12 +636,12 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         return __uint_as_float(val);
       };
       auto sum_parts = [&](int idx) -> float {
-        float v[8];
+        float v[16];
 #pragma unroll
-        for (int s = 0; s < 8; ++s) v[s] = (s < S) ? ld_part(s, idx) : 0.f;
+        for (int s = 0; s < 16; ++s) v[s] = (s < S) ? ld_part(s, idx) : 0.f;
         float acc = 0.f;
 #pragma unroll
-        for (int s = 0; s < 8; ++s) acc += v[s];  // split order: deterministic
+        for (int s = 0; s < 16; ++s) acc += v[s];  // split order: deterministic
         return acc;
       };
       if (p.epilogue == EPI_SILU_MUL) {
@@ -688,7 +703,11 @@ cudaError_t launch_cfg(const CUtensorMap& xmap, W4A16Params p, int rw, int rx, i
   e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e != cudaSuccess) return e;
   dim3 grid((p.N + BM * C::NT - 1) / (BM * C::NT), (p.M + C::BN - 1) / C::BN, p.splits);
-  if (p.splits > 1 && (C::NT != 1 || p.splits > 8)) return cudaErrorInvalidConfiguration;
+  if (p.splits > 1 && (C::NT != 1 || p.splits > 16)) return cudaErrorInvalidConfiguration;
+  if (p.splits > 8) {  // clusters of 9..16 CTAs are outside the portable size
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
   return launch_k(kern, grid, dim3(C::kThreads), smem, stream, (unsigned)p.splits, xmap, p);
 }
 
@@ -715,15 +734,30 @@ static bool ring_override(int* w, int* x, int* a) {
   return true;
 }
 
+// Decode shapes, INT4 only: 4 dequant warps (a whole 64-column row per thread) and four CTAs
+// per SM. SQ_GEMM_WIDE_DQ=1 selects the 8-warp, two-CTA configuration instead.
+bool w4a16_narrow(int wfmt, int gpk) {
+  static const bool wide = [] {
+    const char* e = std::getenv("SQ_GEMM_WIDE_DQ");
+    return e != nullptr && e[0] == '1';
+  }();
+  return !wide && wfmt == WF_INT4 && gpk == 1;
+}
+
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s) {
   int ow, ox, oa;
   const bool ov = ring_override(&ow, &ox, &oa);
   if (nt == 1) {
     switch (bn) {
-      case 16: return ov ? launch_cfg<Cfg<16, 1, 2>>(xmap, p, ow, ox, oa, s) : launch_cfg<Cfg<16, 1, 2>>(xmap, p, 8, 8, 4, s);
-      case 32: return ov ? launch_cfg<Cfg<32, 1, 2>>(xmap, p, ow, ox, oa, s) : launch_cfg<Cfg<32, 1, 2>>(xmap, p, 8, 6, 4, s);
+      case 16:
+        if (!ov && w4a16_narrow(p.wfmt, p.gpk)) return launch_cfg<Cfg<16, 1, 4, 4>>(xmap, p, 6, 6, 2, s);
+        return ov ? launch_cfg<Cfg<16, 1, 2>>(xmap, p, ow, ox, oa, s) : launch_cfg<Cfg<16, 1, 2>>(xmap, p, 8, 8, 4, s);
+      case 32:
+        if (!ov && w4a16_narrow(p.wfmt, p.gpk)) return launch_cfg<Cfg<32, 1, 4, 4>>(xmap, p, 5, 4, 2, s);
+        return ov ? launch_cfg<Cfg<32, 1, 2>>(xmap, p, ow, ox, oa, s) : launch_cfg<Cfg<32, 1, 2>>(xmap, p, 8, 6, 4, s);
       case 64:
         if (ov) return launch_cfg<Cfg<64, 1, 2>>(xmap, p, ow, ox, oa, s);
+        if (w4a16_narrow(p.wfmt, p.gpk)) return launch_cfg<Cfg<64, 1, 4, 4>>(xmap, p, 4, 3, 2, s);
         return launch_cfg<Cfg<64, 1, 2>>(xmap, p, 8, 6, 4, s);
       case 128: return launch_cfg<Cfg<128, 1, 2>>(xmap, p, 8, 4, 4, s);
       case 256: return launch_cfg<Cfg<256, 1, 1>>(xmap, p, 6, 4, 4, s);

@@ -57,6 +57,9 @@ struct W4A16Params {
   int tp;
 };
 
+// True when token tiles of <= 64 run the 4-dequant-warp configuration (four CTAs per SM):
+// INT4 codes with one (scale, zero) group per 64-column k-block.
+bool w4a16_narrow(int wfmt, int gpk);
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s);
 cudaError_t repack_int4_launch(const uint8_t* packed, const float* scales, const float* zeros, uint32_t* wt, int N,
                                int K, int group, cudaStream_t s);

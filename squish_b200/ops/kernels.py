@@ -253,8 +253,8 @@ def prepare_weight(t, device, bias: torch.Tensor | None = None) -> Int4Weight:
                       group=int(t.group), bias=b, fmt=fmt)
 
 
-def gemm_plan(m: int, n: int, k: int):
-    bn, nt, splits, kps, tiles = native().gemm_plan(m, n, k)
+def gemm_plan(m: int, n: int, k: int, group: int = 64, fmt: int = 0):
+    bn, nt, splits, kps, tiles = native().gemm_plan(m, n, k, group, fmt)
     return {"bn": bn, "nt": nt, "splits": splits, "kb_per_split": kps, "tiles": tiles}
 
 

@@ -29,6 +29,8 @@ def _rand_int4(n, k, group, seed=0):
         (16, 1024, 1024, 64),
         (33, 512, 688, 16),
         (64, 3584, 3584, 64),
+        (16, 1024, 7168, 64),  # 16-way split-K cluster (non-portable size)
+        (48, 640, 8960, 128),
         (100, 640, 1024, 128),
         (300, 1024, 896, 64),
         (1024, 2048, 512, 32),
