@@ -114,6 +114,18 @@ def main():
                 it[0] += 1
 
             t = time_op(fn, args.iters, inner=copies)
+            extra = {}
+            if m >= ops.kernels.DQ_GEMM_MIN_M and name != "lm_head":
+                # the large-M route (expand + bf16 GEMM) against its parts, the fused kernel and cuBLAS
+                saved = ops.kernels.DQ_GEMM_MIN_M
+                ops.kernels.DQ_GEMM_MIN_M = 1 << 30
+                extra["fused_ms"] = time_op(fn, args.iters, inner=copies)
+                ops.kernels.DQ_GEMM_MIN_M = saved
+                wd = ops.dequant_weight(wts[0])
+                extra["expand_ms"] = time_op(lambda: ops.dequant_weight(wts[0], out=wd), args.iters)
+                extra["bf16_gemm_ms"] = time_op(lambda: ops.bf16_linear(x, wd[:, :k], out=y), args.iters)
+                extra["cublas_ms"] = time_op(lambda: torch.mm(x, wd[:, :k].t(), out=y), args.iters)
+                del wd
             wbytes = n * k / 2 + n * (k // q.group_size) * 4
             bytes_ = wbytes + m * k * 2 + m * n * 2
             flops = 2.0 * m * n * k
@@ -123,7 +135,7 @@ def main():
             plan = ops.gemm_plan(m, n, k)
             rows.append({"op": f"w4a16 {name}", "m": m, "n": n, "k": k, "ms": t, "GB/s": bytes_ / t / 1e6,
                          "TFLOP/s": flops / t / 1e9, "roofline_ms": roof, "frac": roof / t,
-                         "bound": "hbm" if t_bw > t_fl else "tensor", "plan": plan})
+                         "bound": "hbm" if t_bw > t_fl else "tensor", "plan": plan, **extra})
         del wts
         torch.cuda.empty_cache()
     if not args.no_attn:

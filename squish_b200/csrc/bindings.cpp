@@ -15,6 +15,7 @@
 #include <cstring>
 
 #include "w4a16_gemm.h"
+#include "bf16_gemm.h"
 #include "comm.h"
 #include "cpu_ref.h"
 
@@ -209,6 +210,72 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, 
   p.trace = optr<unsigned long long>(trace);
   const CUtensorMap xmap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), bn);
   CUDA_OK(sq::w4a16_gemm_launch(xmap, p, bn, nt, cur_stream()));
+}
+
+// Expand tile-major weight codes to bf16 out[N, ld] (columns >= K hold the padding codes).
+void dequant_weight(torch::Tensor wq, int64_t N, int64_t K, int64_t group, int64_t wfmt,
+                    c10::optional<torch::Tensor> codebook, torch::Tensor out) {
+  CHECK_CUDA(wq);
+  CHECK_CUDA(out);
+  CHECK_DT(out, torch::kBFloat16);
+  TORCH_CHECK(wfmt >= 0 && wfmt <= 5, "unknown weight format");
+  const int64_t kpad = (K + 63) / 64 * 64;
+  TORCH_CHECK(out.dim() == 2 && out.size(0) >= N && out.stride(1) == 1 && out.stride(0) >= kpad &&
+                  out.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+              "out must be [>= N, >= 64 * ceil(K / 64)] bf16 with 16-byte aligned rows");
+  if (wfmt == sq::WF_AQLM) TORCH_CHECK(codebook.has_value(), "AQLM weights need their codebooks");
+  const c10::cuda::CUDAGuard g(wq.device());
+  CUDA_OK(sq::dequant_weight_launch(ptr<uint32_t>(wq), (int)wfmt, (int)N, (int)K, (int)group, (int)out.stride(0),
+                                    ptr<__nv_bfloat16>(out), optr<__nv_bfloat16>(codebook),
+                                    codebook.has_value() ? (int)(codebook->numel() / (256 * 8)) : 0, num_sms(),
+                                    cur_stream()));
+}
+
+static bool al16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+// y = x . w^T (+ bias) (+ residual), bf16 operands, persistent tcgen05 kernel. w: [N, K] with
+// unit column stride (row stride a multiple of 8 elements). With epilogue EPI_SILU_MUL the rows
+// of w are [gate 64 | up 64] blocks and y = silu(gate) * up has N / 2 columns.
+void bf16_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> bias,
+               c10::optional<torch::Tensor> residual, int64_t epilogue, torch::Tensor ws, torch::Tensor counters,
+               torch::Tensor status) {
+  CHECK_CUDA(x);
+  CHECK_CUDA(w);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(w, torch::kBFloat16);
+  CHECK_DT(y, torch::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "x [M, K], w [N, K]");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && y.stride(1) == 1, "unit column strides");
+  TORCH_CHECK(x.stride(0) % 8 == 0 && w.stride(0) % 8 == 0 && al16(x.data_ptr()) && al16(w.data_ptr()),
+              "x / w rows must be 16-byte aligned");
+  const int64_t M = x.size(0), N = w.size(0), K = x.size(1);
+  const bool silu = epilogue == sq::EPI_SILU_MUL;
+  TORCH_CHECK(y.size(0) >= M && y.size(1) >= (silu ? N / 2 : N), "y too small");
+  TORCH_CHECK(!silu || (N % 128 == 0 && !bias.has_value() && !residual.has_value()),
+              "SwiGLU epilogue: N a multiple of 128, no bias / residual");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard g(x.device());
+  sq::Bf16GemmParams p{};
+  p.bias = optr<__nv_bfloat16>(bias);
+  p.residual = optr<__nv_bfloat16>(residual);
+  p.y = ptr<__nv_bfloat16>(y);
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.ldy = (int)y.stride(0);
+  p.ldr = residual.has_value() ? (int)residual->stride(0) : 0;
+  p.epilogue = (int)epilogue;
+  p.vec = al16(p.y) && p.ldy % 8 == 0 && (!p.bias || al16(p.bias)) &&
+          (!p.residual || (al16(p.residual) && p.ldr % 8 == 0 && residual->stride(1) == 1));
+  p.status = ptr<int>(status);
+  CHECK_DT(ws, torch::kFloat32);
+  CHECK_DT(counters, torch::kInt32);
+  p.ws = ptr<float>(ws);
+  p.counters = ptr<int>(counters);
+  const CUtensorMap amap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), 128);
+  const CUtensorMap bmap = make_bf16_map(w.data_ptr(), (int)N, (int)K, (int)w.stride(0), 256);
+  CUDA_OK(sq::bf16_gemm_launch(amap, bmap, p, num_sms(), (long long)ws.numel(), (int)counters.numel(),
+                               cur_stream()));
 }
 
 // Grouped (mixture-of-experts) INT4 GEMM over expert-sorted, tile-padded rows of x.
@@ -688,6 +755,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_plan", &gemm_plan, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("group") = 64,
         py::arg("wfmt") = 0);
   m.def("w4a16_gemm", &w4a16_gemm);
+  m.def("dequant_weight", &dequant_weight);
+  m.def("bf16_gemm", &bf16_gemm);
   m.def("w4a16_grouped_gemm", &w4a16_grouped_gemm);
   m.def("moe_route", &moe_route);
   m.def("tree_verify", &tree_verify);

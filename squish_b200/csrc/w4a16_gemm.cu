@@ -832,4 +832,99 @@ cudaError_t repack_int4_launch(const uint8_t* packed, const float* scales, const
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------ weight expansion
+// Tile-major weight codes (any WF_* format) -> bf16 [N, ld] row-major, the values the fused
+// GEMM computes (one rounding of q * scale + zero). Used by the large-M path, where a
+// bf16 tensor-core GEMM over the expanded weights beats dequantizing every weight tile once
+// per token tile.
+namespace {
+// INT4: thread (row lr, word w) of a 256-thread CTA expands 8 columns (one nibble word) of
+// one row per k-block, so the 8 threads of a row store its 128 bytes contiguously.
+constexpr int kDqKbPerCta = 8;
+__global__ void __launch_bounds__(256) dequant_int4_kernel(const uint8_t* __restrict__ wq, int gpk, int kb_total,
+                                                           int N, int ld, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  const int w = threadIdx.x & 7;
+  const int row = blockIdx.y * 32 + (threadIdx.x >> 3);
+  const int rb = row >> 7, r = row & (BM - 1);
+  const int kb0 = blockIdx.x * kDqKbPerCta;
+  const int tbytes = tile_bytes(gpk, WF_INT4);
+  const uint8_t* base = wq + ((size_t)rb * kb_total) * tbytes;
+  const int woff = ((w >> 2) * BM + r) * 16 + (w & 3) * 4;
+  const int soff = W_TILE_BYTES + ((((w * gpk) >> 3) * BM + r) << 2);
+  uint32_t code[kDqKbPerCta], szw[kDqKbPerCta];
+#pragma unroll
+  for (int j = 0; j < kDqKbPerCta; ++j) {
+    const int kb = min(kb0 + j, kb_total - 1);
+    code[j] = __ldg(reinterpret_cast<const uint32_t*>(base + (size_t)kb * tbytes + woff));
+    szw[j] = __ldg(reinterpret_cast<const uint32_t*>(base + (size_t)kb * tbytes + soff));
+  }
+  pdl_wait();  // the output buffer may still be read by the previous kernel
+  if (row >= N) return;
+  __nv_bfloat16* dst = out + (size_t)row * ld + w * 8;
+#pragma unroll
+  for (int j = 0; j < kDqKbPerCta; ++j) {
+    const int kb = kb0 + j;
+    if (kb < kb_total) {
+      const __nv_bfloat16 sc = __ushort_as_bfloat16((unsigned short)(szw[j] & 0xFFFFu));
+      const __nv_bfloat16 ze = __ushort_as_bfloat16((unsigned short)(szw[j] >> 16));
+      *reinterpret_cast<uint4*>(dst + kb * 64) = dq_word(code[j], __bfloat162bfloat162(sc), __bfloat162bfloat162(ze));
+    }
+  }
+}
+
+// Other formats: thread (r, c) expands row r, columns [32c, 32c + 32) of each k-block.
+__global__ void __launch_bounds__(256) dequant_weight_kernel(const uint8_t* __restrict__ wq, int wfmt, int gpk,
+                                                             int kb_total, int kb_per_cta, int N, int ld,
+                                                             __nv_bfloat16* __restrict__ out,
+                                                             const __nv_bfloat16* codebook, int n_books) {
+  __shared__ uint4 fmt_tab[512];
+  uint32_t* lut = reinterpret_cast<uint32_t*>(fmt_tab);
+  if (wfmt == WF_NF4) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x)
+      lut[i] = bf2_bits(__floats2bfloat162_rn(kNf4Levels[i & 15], kNf4Levels[i >> 4]));
+  } else if (wfmt == WF_AQLM) {
+    for (int i = threadIdx.x; i < 256 * n_books; i += blockDim.x) fmt_tab[i] = reinterpret_cast<const uint4*>(codebook)[i];
+  }
+  __syncthreads();
+  pdl_trigger();
+  const int r = threadIdx.x & (BM - 1), c = threadIdx.x >> 7;
+  const int rb = blockIdx.y, row = rb * BM + r;
+  const int kb0 = blockIdx.x * kb_per_cta, kb1 = min(kb_total, kb0 + kb_per_cta);
+  const int tbytes = tile_bytes(gpk, wfmt);
+  pdl_wait();
+  for (int kb = kb0; kb < kb1; ++kb) {
+    const uint8_t* tb = wq + ((size_t)rb * kb_total + kb) * tbytes;
+    uint4 o[4];
+    dq_other(tb, wfmt, r, c, gpk, lut, n_books, o);
+    if (row < N) {
+      uint4* dst = reinterpret_cast<uint4*>(out + (size_t)row * ld + kb * 64 + c * 32);
+#pragma unroll
+      for (int w = 0; w < 4; ++w) dst[w] = o[w];
+    }
+  }
+}
+}  // namespace
+
+cudaError_t dequant_weight_launch(const uint32_t* wq, int wfmt, int N, int K, int group, int ld,
+                                  __nv_bfloat16* out, const __nv_bfloat16* codebook, int n_books, int num_sms,
+                                  cudaStream_t s) {
+  const int gpk = group >= 64 ? 1 : 64 / group;
+  const int kb_total = (K + 63) / 64;
+  const uint8_t* w8 = reinterpret_cast<const uint8_t*>(wq);
+  if (wfmt == WF_INT4) {
+    dim3 grid((kb_total + kDqKbPerCta - 1) / kDqKbPerCta, (N + 31) / 32);
+    SQ_LAUNCH(dequant_int4_kernel, grid, dim3(256), 0, s, 1u, w8, gpk, kb_total, N, ld, out);
+    return cudaSuccess;
+  }
+  const int rbs = (N + BM - 1) / BM;
+  // about four CTAs per SM in one wave; each CTA expands a run of k-blocks of one row block
+  const int want = max(1, (4 * num_sms + rbs - 1) / rbs);
+  const int kpc = (kb_total + min(want, kb_total) - 1) / min(want, kb_total);
+  dim3 grid((kb_total + kpc - 1) / kpc, rbs);
+  SQ_LAUNCH(dequant_weight_kernel, grid, dim3(256), 0, s, 1u, w8, wfmt, gpk, kb_total, kpc, N, ld, out, codebook,
+            n_books);
+  return cudaSuccess;
+}
+
 }  // namespace sq

@@ -61,6 +61,10 @@ struct W4A16Params {
 // INT4 codes with one (scale, zero) group per 64-column k-block.
 bool w4a16_narrow(int wfmt, int gpk);
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s);
+// Expand tile-major weight codes to bf16 [N, ld] (ld >= 64 * ceil(K / 64), a multiple of 8).
+cudaError_t dequant_weight_launch(const uint32_t* wq, int wfmt, int N, int K, int group, int ld,
+                                  __nv_bfloat16* out, const __nv_bfloat16* codebook, int n_books, int num_sms,
+                                  cudaStream_t s);
 cudaError_t repack_int4_launch(const uint8_t* packed, const float* scales, const float* zeros, uint32_t* wt, int N,
                                int K, int group, cudaStream_t s);
 

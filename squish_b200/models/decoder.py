@@ -258,6 +258,11 @@ class CudaRunner:
         self.tokens = torch.empty(B + T, dtype=torch.int32, device=dev)
         self.tokens_host = torch.empty(B + T, dtype=torch.int32, pin_memory=True)
         self.vout = torch.zeros(B, 2 + ops.kernels.MAX_TREE_NODES, dtype=torch.int32, device=dev)
+        if T >= ops.kernels.DQ_GEMM_MIN_M:
+            # bf16 expansion buffer of the large-M GEMM path, sized for the largest layer weight
+            ws = [w for lw in self.layers for w in (lw.qkv, lw.o, lw.gate_up, lw.down) if isinstance(w, ops.Int4Weight)]
+            if ws:
+                self.ws.dq_buffer(max(w.n * ((w.k + 63) // 64 * 64) for w in ws))
         self.vout_host = torch.zeros(B, 2 + ops.kernels.MAX_TREE_NODES, dtype=torch.int32, pin_memory=True)
         self._layer_ptrs = None
         self.last_verify = None

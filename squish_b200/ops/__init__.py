@@ -3,6 +3,8 @@ from .kernels import (  # noqa: F401
     KV_FORMATS,
     Int4Weight,
     Workspace,
+    bf16_linear,
+    dequant_weight,
     gemm_plan,
     paged_decode_attention,
     paged_prefill_attention,

@@ -8,6 +8,7 @@ decode split partials, the sampler's fp32 row buffer) lives in a per-device
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -34,6 +35,7 @@ class Workspace:
         self._attn_o = torch.empty(0, dtype=torch.float32, device=device)
         self._attn_lse = torch.empty(0, dtype=torch.float32, device=device)
         self._sampler = torch.empty(0, dtype=torch.float32, device=device)
+        self._dq = torch.empty(0, dtype=torch.bfloat16, device=device)  # expanded weights (large-M GEMMs)
         # set once a CUDA graph has captured these buffers: growing one then would leave the
         # graph writing to freed memory, so it becomes an error instead
         self.frozen = False
@@ -59,6 +61,14 @@ class Workspace:
             self._grow_check("sampler")
             self._sampler = torch.empty(need, dtype=torch.float32, device=self.device)
         return self._sampler
+
+    def dq_buffer(self, elems: int) -> torch.Tensor | None:
+        """bf16 scratch for one expanded weight matrix; None if it would have to grow after capture."""
+        if self._dq.numel() < elems:
+            if self.frozen:
+                return None
+            self._dq = torch.empty(elems, dtype=torch.bfloat16, device=self.device)
+        return self._dq
 
     def check(self) -> None:
         """Raise if any kernel recorded an error (a bounded wait that timed out)."""
@@ -271,9 +281,47 @@ def w4a16_linear(x: torch.Tensor, w: Int4Weight, out: torch.Tensor | None = None
     ncols = w.n // 2 if silu_mul else w.n
     if out is None:
         out = torch.empty((m, ncols), dtype=torch.bfloat16, device=x.device)
+    if m >= DQ_GEMM_MIN_M and trace is None:
+        # many token tiles: expand the weights to bf16 once, then a bf16 tensor-core GEMM
+        kpad = (w.k + 63) // 64 * 64
+        buf = ws.dq_buffer(w.n * kpad)
+        if buf is not None:
+            wd = dequant_weight(w, buf[: w.n * kpad].view(w.n, kpad))
+            return bf16_linear(x, wd[:, : w.k], out, w.bias, residual, silu_mul, ws)
     native().w4a16_gemm(x, w.wq, w.sz, w.n, w.k, w.group, out, w.bias, residual,
                         EPI_SILU_MUL if silu_mul else EPI_PLAIN, ws.gemm_ws, ws.gemm_counters, ws.status, trace,
                         w.fmt, w.codebook)
+    _count()
+    return out
+
+
+# Token count from which a quantized linear layer expands its weights to bf16 and runs the bf16
+# tensor-core GEMM instead of dequantizing inside the GEMM (measured crossover on B200).
+DQ_GEMM_MIN_M = int(os.environ.get("SQ_DQ_GEMM_MIN_M", "384"))
+
+
+def dequant_weight(w: Int4Weight, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The bf16 values of a tile-major quantized weight, [n, 64 * ceil(k / 64)] (the GEMM's exact
+    operand values; columns >= k hold padding)."""
+    kpad = (w.k + 63) // 64 * 64
+    if out is None:
+        out = torch.empty((w.n, kpad), dtype=torch.bfloat16, device=w.wq.device)
+    native().dequant_weight(w.wq, w.n, w.k, w.group, w.fmt, w.codebook, out)
+    _count()
+    return out
+
+
+def bf16_linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+                residual: torch.Tensor | None = None, silu_mul: bool = False,
+                ws: Workspace | None = None) -> torch.Tensor:
+    """y = x @ w^T (+bias) (+residual) on the persistent tcgen05 bf16 GEMM; with ``silu_mul`` the
+    rows of w are interleaved gate/up blocks of 64 and y = silu(gate) * up."""
+    ws = ws or workspace(x.device)
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty((x.shape[0], n // 2 if silu_mul else n), dtype=torch.bfloat16, device=x.device)
+    native().bf16_gemm(x, w, out, bias, residual, EPI_SILU_MUL if silu_mul else EPI_PLAIN, ws.gemm_ws,
+                       ws.gemm_counters, ws.status)
     _count()
     return out
 

@@ -48,6 +48,62 @@ def test_w4a16_gemm_matches_fp32(cuda, m, n, k, group):
     ops.workspace(cuda).check()
 
 
+@pytest.mark.parametrize("n,k,group", [(384, 512, 64), (1000, 688, 16), (256, 1024, 32), (640, 896, 128)])
+def test_dequant_weight_matches_kernel_values(cuda, n, k, group):
+    packed, scales, offsets = _rand_int4(n, k, group, seed=n + k)
+    w = ops.prepare_int4_weight(packed, scales, offsets, k, group, cuda)
+    wd = ops.dequant_weight(w)
+    torch.cuda.synchronize()
+    assert wd.shape == (n, (k + 63) // 64 * 64)
+    ref = dequant_int4_as_kernel(packed, scales, offsets, group)
+    torch.testing.assert_close(wd[:, :k].float().cpu(), ref, rtol=0, atol=1e-6 + 2e-3 * ref.abs().max().item())
+
+
+@pytest.mark.parametrize(
+    "m,n,k",
+    [(1, 256, 64), (130, 300, 200), (257, 512, 4096), (2048, 1024, 512), (700, 37888 // 8, 3584)],
+)
+def test_bf16_gemm_matches_fp32(cuda, m, n, k):
+    g = torch.Generator().manual_seed(m * 7 + n)
+    x = (torch.randn(m, k, generator=g) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16)
+    res = torch.randn(m, n, generator=g).to(torch.bfloat16)
+    y = ops.bf16_linear(x.to(cuda), w.to(cuda), bias=bias.to(cuda), residual=res.to(cuda))
+    torch.cuda.synchronize()
+    ref = x.float() @ w.float().T + bias.float() + res.float()
+    torch.testing.assert_close(y.float().cpu(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
+    ops.workspace(cuda).check()
+
+
+@pytest.mark.parametrize("m,f,k", [(333, 384, 520), (64, 256, 4096)])  # the second splits K 8 ways
+def test_bf16_gemm_silu_and_strided_weight(cuda, m, f, k):
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(m, k, generator=g) * 0.5).to(torch.bfloat16)
+    wpad = (torch.randn(2 * f, k + 56, generator=g) * 0.05).to(torch.bfloat16)  # row stride > k
+    w = wpad[:, :k]
+    y = ops.bf16_linear(x.to(cuda), wpad.to(cuda)[:, :k], silu_mul=True)
+    y2 = ops.bf16_linear(x.to(cuda), wpad.to(cuda)[:, :k], silu_mul=True)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2), "split-K reduction must be deterministic"
+    h = (x.float() @ w.float().T).view(m, f // 64, 2, 64)
+    ref = torch.nn.functional.silu(h[:, :, 0].reshape(m, f)) * h[:, :, 1].reshape(m, f)
+    torch.testing.assert_close(y.float().cpu(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
+
+
+def test_w4a16_large_m_paths_agree(cuda, monkeypatch):
+    """The expanded-weight path (m >= DQ_GEMM_MIN_M) and the fused path give the same result."""
+    n, k, group, m = 1024, 2048, 64, 512
+    packed, scales, offsets = _rand_int4(n, k, group, seed=11)
+    w = ops.prepare_int4_weight(packed, scales, offsets, k, group, cuda)
+    x = (torch.randn(m, k) * 0.5).to(torch.bfloat16).to(cuda)
+    y_dq = ops.w4a16_linear(x, w)
+    monkeypatch.setattr(ops.kernels, "DQ_GEMM_MIN_M", 1 << 30)
+    y_fused = ops.w4a16_linear(x, w)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(y_dq.float(), y_fused.float(), rtol=1e-2, atol=1e-2)
+
+
 @pytest.mark.parametrize("m", [3, 64, 257])
 def test_w4a16_bias_residual_and_determinism(cuda, m):
     n, k, group = 768, 1024, 64
@@ -65,7 +121,7 @@ def test_w4a16_bias_residual_and_determinism(cuda, m):
     torch.testing.assert_close(y1.float().cpu(), ref, rtol=2e-2, atol=3e-2)
 
 
-@pytest.mark.parametrize("m", [2, 48, 200])
+@pytest.mark.parametrize("m", [2, 48, 200, 300])
 def test_w4a16_silu_mul_epilogue(cuda, m):
     f, k, group = 640, 512, 64
     gate = torch.randn(f, k) * 0.05
