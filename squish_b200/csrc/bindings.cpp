@@ -686,7 +686,8 @@ void paged_prefill_attention(torch::Tensor q, torch::Tensor k_codes, torch::Tens
                              torch::Tensor tile_q0, torch::Tensor q_start, torch::Tensor q_len, torch::Tensor ctx_len,
                              int64_t n_tiles, torch::Tensor out, int64_t Hq, int64_t Hkv, int64_t D,
                              int64_t page_size, int64_t group, int64_t fmt_k, int64_t fmt_v, double sm_scale,
-                             c10::optional<torch::Tensor> tree_mask) {
+                             c10::optional<torch::Tensor> tree_mask, c10::optional<torch::Tensor> status,
+                             c10::optional<torch::Tensor> trace) {
   const c10::cuda::CUDAGuard g(q.device());
   auto p = attn_common(q, k_codes, k_scales, v_codes, v_scales, block_tables, out, Hq, Hkv, D, page_size, group,
                        fmt_k, fmt_v, sm_scale);
@@ -697,6 +698,26 @@ void paged_prefill_attention(torch::Tensor q, torch::Tensor k_codes, torch::Tens
   p.q_len = ptr<int>(q_len);
   p.ctx_len = ptr<int>(ctx_len);
   p.n_tiles = (int)n_tiles;
+  static const bool tc_off = [] {
+    const char* e = std::getenv("SQ_PREFILL_ATTN_LEGACY");
+    return e != nullptr && e[0] == '1';
+  }();
+  if (!tc_off && status.has_value() && sq::prefill_tc_supported(p)) {
+    const int hs = sq::prefill_tc_head_slots((int)(Hq / Hkv));
+    CUtensorMap m;
+    cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)Hq, (cuuint64_t)q.size(0)};
+    cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)q.stride(0) * 2};
+    cuuint32_t box[3] = {64, (cuuint32_t)hs, (cuuint32_t)(128 / hs)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 && q.stride(1) == 1, "q rows must be aligned");
+    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q.data_ptr(), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (q) failed (", (int)r, ")");
+    CUDA_OK(sq::paged_prefill_attn_tc_launch(m, p, ptr<int>(*status), optr<unsigned long long>(trace),
+                                             cur_stream()));
+    return;
+  }
   CUDA_OK(sq::paged_prefill_attn_launch(p, cur_stream()));
 }
 

@@ -1,5 +1,6 @@
 // kernels.h — launch interfaces of the non-GEMM CUDA kernels.
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -60,6 +61,13 @@ cudaError_t rmsnorm_launch(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_
                            int rows, int H, int ldx, int ldy, float eps, cudaStream_t s);
 cudaError_t paged_decode_attn_launch(const AttnParams& p, cudaStream_t s);
 cudaError_t paged_prefill_attn_launch(const AttnParams& p, cudaStream_t s);
+// tcgen05 prefill attention (head dim 128, 3..16 query heads per KV head, no token-tree
+// masks, quantized KV): q is read through a 3-D tensor map {D, Hq, rows} with box
+// {64, head slots, 128 / head slots} and 128-byte swizzle.
+bool prefill_tc_supported(const AttnParams& p);
+int prefill_tc_head_slots(int gq);
+cudaError_t paged_prefill_attn_tc_launch(const CUtensorMap& qmap, const AttnParams& p, int* status,
+                                         unsigned long long* trace, cudaStream_t s);
 
 struct SamplerParams {
   const __nv_bfloat16* logits;  // [B, ld]

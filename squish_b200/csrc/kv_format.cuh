@@ -127,23 +127,34 @@ struct RowPart {
   static constexpr int CHUNKS = DIMS / 8;
   static constexpr int NG = DIMS >= 32 ? DIMS / 32 : 1;
   static_assert(BYTES % 4 == 0, "row part must be a whole number of 32-bit words");
+  static constexpr int NZ = kv_asym(FMT) ? NG : 1;  // symmetric formats derive the zero from the scale
   uint32_t w[WORDS];
-  float s[NG], z[NG];
+  float s[NG], z[NZ];
 
   __device__ __forceinline__ void clear() {
 #pragma unroll
     for (int i = 0; i < WORDS; ++i) w[i] = 0u;
 #pragma unroll
-    for (int i = 0; i < NG; ++i) s[i] = z[i] = 0.f;
+    for (int i = 0; i < NG; ++i) s[i] = 0.f;
+#pragma unroll
+    for (int i = 0; i < NZ; ++i) z[i] = 0.f;
   }
 
+  // NC: read-only global loads (__ldg); false: generic loads (e.g. a shared-memory staging copy)
+  template <bool NC = true, class T>
+  static __device__ __forceinline__ T ld(const T* p) {
+    if constexpr (NC) return __ldg(p);
+    else return *p;
+  }
+
+  template <bool NC = true>
   __device__ __forceinline__ void load(const uint8_t* __restrict__ row_codes, const __half* __restrict__ row_scales,
                                        int part, int G) {
     const uint8_t* src = row_codes + part * BYTES;
     if constexpr (BYTES % 16 == 0 && (D * kv_bits(FMT) / 8) % 16 == 0) {
 #pragma unroll
       for (int i = 0; i < WORDS / 4; ++i) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + i);
+        const uint4 v = ld<NC>(reinterpret_cast<const uint4*>(src) + i);
         w[4 * i] = v.x;
         w[4 * i + 1] = v.y;
         w[4 * i + 2] = v.z;
@@ -151,19 +162,21 @@ struct RowPart {
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < WORDS; ++i) w[i] = __ldg(reinterpret_cast<const uint32_t*>(src) + i);
+      for (int i = 0; i < WORDS; ++i) w[i] = ld<NC>(reinterpret_cast<const uint32_t*>(src) + i);
     }
     if constexpr (FMT != KV_BF16) {
-      const int geff = G < DIMS ? G : DIMS;
+      // scale groups of this part: DIMS / G of them (one, shared with the neighbour part,
+      // when the group is wider than the part)
+      const int ng = DIMS >= G ? DIMS / G : 1;
 #pragma unroll
       for (int gi = 0; gi < NG; ++gi) {
-        const int g = (part * DIMS + gi * geff) / G;
+        if (gi >= ng) break;
+        const int g = (part * DIMS) / G + gi;
         if constexpr (kv_asym(FMT)) {
-          s[gi] = __half2float(__ldg(row_scales + 2 * g));
-          z[gi] = __half2float(__ldg(row_scales + 2 * g + 1));
+          s[gi] = __half2float(ld<NC>(row_scales + 2 * g));
+          z[gi] = __half2float(ld<NC>(row_scales + 2 * g + 1));
         } else {
-          s[gi] = __half2float(__ldg(row_scales + g));
-          z[gi] = (FMT == KV_INT4) ? -7.5f * s[gi] : (FMT == KV_INT2) ? -1.5f * s[gi] : 0.f;
+          s[gi] = __half2float(ld<NC>(row_scales + g));
         }
       }
     }
@@ -174,9 +187,16 @@ struct RowPart {
     if constexpr (FMT == KV_BF16) {
       return make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
     } else {
-      const int geff = G < DIMS ? G : DIMS;
-      const int gi = NG == 1 ? 0 : (c * 8) / geff;
-      const float sc = s[gi], ze = z[gi];
+      const int gi = (NG == 1 || DIMS < G) ? 0 : (c * 8) / G;
+      // select, not index: a runtime index would move s[] / z[] to local memory
+      float sc = s[0], ze = z[0];
+#pragma unroll
+      for (int i = 1; i < NG; ++i)
+        if (gi == i) {
+          sc = s[i];
+          if constexpr (kv_asym(FMT)) ze = z[i];
+        }
+      if constexpr (!kv_asym(FMT)) ze = (FMT == KV_INT4) ? -7.5f * sc : (FMT == KV_INT2) ? -1.5f * sc : 0.f;
       if constexpr (FMT == KV_INT4 || FMT == KV_V4 || FMT == KV_INT2) {
         const __nv_bfloat162 s2 = __floats2bfloat162_rn(sc, sc), z2 = __floats2bfloat162_rn(ze, ze);
         const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.f, 128.f);

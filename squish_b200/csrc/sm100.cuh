@@ -89,14 +89,19 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // Bounded wait. Returns false (and records `code` in *status) on timeout. The status word
 // (global memory) is polled only every 256 suspended tries, so a normal hand-off costs one
 // try_wait, not an L2 round trip.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
+// The slow path is out of line: kernels wait at many sites, and an inlined loop at each one
+// bloats the code the warps of a specialised kernel share through the instruction cache.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* status, int code) {
   for (uint32_t i = 1; i < kMaxSuspends; ++i) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
     if ((i & 255u) == 0 && *reinterpret_cast<volatile int*>(status) != SQ_OK) return false;
   }
   atomicCAS(status, SQ_OK, code);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, status, code);
 }
 
 // ---------------------------------------------------------------- bulk copies
@@ -136,6 +141,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
       "[%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+// 3-D tiled TMA load (no multicast); c0 innermost, same alignment rule as tma_load_2d.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
       : "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {

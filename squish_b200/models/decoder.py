@@ -352,7 +352,7 @@ class CudaRunner:
                 tm = m["tmask"][Bd:] if "tmask" in m else None
                 ops.paged_prefill_attention(q[Bd:], kc, ks, vc, vs, bt[Bd:], m["tseq"], m["tq0"], m["qs"], m["ql"],
                                             m["ctx"], st.tile_seq.shape[0], attn[Bd:], hq, hkv, d, ps, grp, self.fk,
-                                            self.fv, self.sm_scale, tree_mask=tm)
+                                            self.fv, self.sm_scale, tree_mask=tm, ws=ws)
             self._row_parallel(attn, lw.o, h)
             ops.rmsnorm(h, lw.ln2, cfg.rms_eps, out=x)
             if lw.moe is not None:

@@ -373,12 +373,14 @@ def paged_decode_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables
 
 def paged_prefill_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables, tile_seq, tile_q0, q_start,
                             q_len, ctx_len, n_tiles, out, hq, hkv, d, page_size, group, fmt_k, fmt_v, sm_scale,
-                            tree_mask=None):
+                            tree_mask=None, ws: Workspace | None = None, trace: torch.Tensor | None = None):
     """Causal attention of prefill chunks over their paged context; ``tree_mask`` (int32 per
-    query row, bit j = may attend chunk token j, 0 = causal) turns a chunk into a token tree."""
+    query row, bit j = may attend chunk token j, 0 = causal) turns a chunk into a token tree.
+    Head dim 128 with 3..16 query heads per KV head runs on the tcgen05 kernel."""
+    ws = ws or workspace(q.device)
     native().paged_prefill_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables, tile_seq, tile_q0,
                                      q_start, q_len, ctx_len, int(n_tiles), out, hq, hkv, d, page_size, group,
-                                     fmt_k, fmt_v, float(sm_scale), tree_mask)
+                                     fmt_k, fmt_v, float(sm_scale), tree_mask, ws.status, trace)
     _count()
     return out
 

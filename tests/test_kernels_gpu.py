@@ -270,13 +270,20 @@ def test_paged_decode_attention(cuda, kvfmt, hq, hkv, d, lens):
         torch.testing.assert_close(out[i].float().cpu().view(1, hq, d), ref, rtol=2e-2, atol=3e-2)
 
 
-@pytest.mark.parametrize("kvfmt,hq,hkv,d", [("int4", 28, 4, 128), ("k8v4", 16, 2, 128), ("bf16", 8, 2, 64)])
-def test_paged_prefill_attention(cuda, kvfmt, hq, hkv, d):
-    torch.manual_seed(hq + d)
+SHORT_SEQS = [(40, 40), (70, 200), (1, 1), (130, 130), (16, 48)]
+LONG_SEQS = [(300, 1100), (600, 600), (5, 900), (257, 257)]  # several 128-key tiles, partial last tiles
+
+
+# head dim 128 with 3..16 query heads per KV head runs the tcgen05 kernel (4, 8 or 16 head slots)
+@pytest.mark.parametrize("kvfmt,hq,hkv,d,seqs", [
+    ("int4", 28, 4, 128, SHORT_SEQS), ("int4", 28, 4, 128, LONG_SEQS), ("k8v4", 16, 2, 128, SHORT_SEQS),
+    ("int4", 32, 8, 128, LONG_SEQS), ("int8", 64, 4, 128, LONG_SEQS), ("int2", 12, 4, 128, SHORT_SEQS),
+    ("bf16", 8, 2, 64, SHORT_SEQS)])
+def test_paged_prefill_attention(cuda, kvfmt, hq, hkv, d, seqs):
+    torch.manual_seed(hq + d + len(seqs))
     ps, group = 16, 32 if kvfmt != "k8v4" else 64
     fk, fv = ops.KV_FORMATS[kvfmt]
     # (chunk length, total context after the chunk): fresh prompts and chunked continuations
-    seqs = [(40, 40), (70, 200), (1, 1), (130, 130), (16, 48)]
     max_pages = max((c + ps - 1) // ps for _, c in seqs)
     num_pages = sum((c + ps - 1) // ps for _, c in seqs) + 2
     kc, ks, vc, vs, kd, vd = _fill_random_cache(num_pages, hkv, ps, d, fk, fv, group, cuda, seed=3)
@@ -311,6 +318,7 @@ def test_paged_prefill_attention(cuda, kvfmt, hq, hkv, d):
         ref = attention(q[qs:qs + ql].float().view(ql, hq, d), k, v, qpos, sm_scale(d))
         # P is rounded to bf16 before the PV product (as in any bf16 flash kernel)
         torch.testing.assert_close(out[qs:qs + ql].float().cpu().view(ql, hq, d), ref, rtol=2e-2, atol=5e-2)
+    ops.workspace(cuda).check()
 
 
 def test_sampler_greedy_and_filters(cuda):
