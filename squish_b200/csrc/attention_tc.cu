@@ -378,43 +378,62 @@ __global__ void __launch_bounds__(kThreadsT, 1)
     __syncwarp();
     bool ok = mbar_wait(q_full, 0, status, SQ_ERR_TIMEOUT_X);
     const uint32_t qa = smem_u32(Qs);
-    auto issue_s = [&](int j) {
-      const int sl = j & 1;
-      ok = ok && mbar_wait(&k_full[sl], (uint32_t)(j >> 1) & 1u, status, SQ_ERR_TIMEOUT_W);
-      if (!ok) return;
-      tc_fence_after();
-      if (elect_one()) {
-        const uint32_t ka = smem_u32(Ks + sl * kTileBytes);
+    // Issue S(s) once K(s) is staged and S buffer s & 1 is free (PV(s-2) issued), and PV(j) once
+    // P(j) and V(j) are ready, whichever comes first: polling both keeps PV off the path of
+    // the K producers. Idle polls sleep briefly (this warp shares its sub-partition with a
+    // producer and two softmax warps) and are bounded.
+    int s_next = 0, pv_next = 0;
+    uint32_t idle = 0;
+    while (ok && pv_next < nt) {
+      bool prog = false;
+      if (s_next < nt && s_next <= pv_next + 1) {
+        const int sl = s_next & 1;
+        if (__shfl_sync(0xffffffffu, mbar_test(&k_full[sl], (uint32_t)(s_next >> 1) & 1u), 0)) {
+          tc_fence_after();
+          if (elect_one()) {
+            const uint32_t ka = smem_u32(Ks + sl * kTileBytes);
 #pragma unroll
-        for (int kk = 0; kk < TD / 16; ++kk)
-          mma_bf16_ss(tmem + kColS + (uint32_t)(sl * 128), sdesc_sw128(kmajor_step(qa, kk)),
-                      sdesc_sw128(kmajor_step(ka, kk)), idesc_s, kk > 0 ? 1u : 0u);
-        mma_commit(&k_empty[sl]);
-        mma_commit(&s_full[sl]);
-        tmark(tr, 4, j);
+            for (int kk = 0; kk < TD / 16; ++kk)
+              mma_bf16_ss(tmem + kColS + (uint32_t)(sl * 128), sdesc_sw128(kmajor_step(qa, kk)),
+                          sdesc_sw128(kmajor_step(ka, kk)), idesc_s, kk > 0 ? 1u : 0u);
+            mma_commit(&k_empty[sl]);
+            mma_commit(&s_full[sl]);
+            tmark(tr, 4, s_next);
+          }
+          __syncwarp();
+          ++s_next;
+          prog = true;
+        }
       }
-      __syncwarp();
-    };
-    issue_s(0);
-    if (nt > 1) issue_s(1);
-    for (int j = 0; j < nt && ok; ++j) {
-      const int sl = j & 1;
-      const uint32_t par = (uint32_t)(j >> 1) & 1u;
-      ok = mbar_wait(&p_full[sl], par, status, SQ_ERR_TIMEOUT_A) && mbar_wait(&v_full[sl], par, status, SQ_ERR_TIMEOUT_W);
-      if (!ok) break;
-      tc_fence_after();
-      if (elect_one()) {
-        const uint32_t va = smem_u32(Vs + sl * kTileBytes);
+      if (pv_next < s_next) {
+        const int j = pv_next, sl = j & 1;
+        const uint32_t par = (uint32_t)(j >> 1) & 1u;
+        if (__shfl_sync(0xffffffffu, mbar_test(&p_full[sl], par) && mbar_test(&v_full[sl], par), 0)) {
+          tc_fence_after();
+          if (elect_one()) {
+            const uint32_t va = smem_u32(Vs + sl * kTileBytes);
 #pragma unroll
-        for (int kk = 0; kk < TKEYS / 16; ++kk)
-          mma_bf16_ts(tmem + kColO, tmem + kColP + (uint32_t)(sl * 64 + kk * 8), sdesc_mn_sw128(va + kk * 2048),
-                      idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&v_empty[sl]);
-        mma_commit(&o_done[sl]);
-        tmark(tr, 7, j);
+            for (int kk = 0; kk < TKEYS / 16; ++kk)
+              mma_bf16_ts(tmem + kColO, tmem + kColP + (uint32_t)(sl * 64 + kk * 8), sdesc_mn_sw128(va + kk * 2048),
+                          idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+            mma_commit(&v_empty[sl]);
+            mma_commit(&o_done[sl]);
+            tmark(tr, 7, j);
+          }
+          __syncwarp();
+          ++pv_next;
+          prog = true;
+        }
       }
-      __syncwarp();
-      if (j + 2 < nt) issue_s(j + 2);
+      if (prog) {
+        idle = 0;
+      } else if (++idle >= (1u << 24)) {  // ~seconds without progress
+        atomicCAS(status, SQ_OK, SQ_ERR_TIMEOUT_A);
+        ok = false;
+      } else {
+        if ((idle & 255u) == 0 && *reinterpret_cast<volatile int*>(status) != SQ_OK) ok = false;
+        __nanosleep(64);
+      }
     }
   } else if (warp >= 4 && warp < 12) {
     // ------------------------------------------------ softmax + epilogue
@@ -445,26 +464,30 @@ __global__ void __launch_bounds__(kThreadsT, 1)
       const int kbase = j * TKEYS + g * 64;     // key of this group's first column
       const int lim = row_ok ? pos - kbase : -1;  // columns c <= lim are visible
       const bool diag = kbase + 63 > pos0;      // some column is in some row's future
-      // pass 1: max over this group's 64 columns
-      float mt = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t u[32];
-        tmem_ld32(sb + (uint32_t)(c * 32), u);
-        tmem_wait_ld();
-        float v[32];
+      // this group's 64 columns of S: one TMEM round trip, kept in registers
+      uint32_t u0[32], u1[32];
+      tmem_ld32(sb, u0);
+      tmem_ld32(sb + 32u, u1);
+      tmem_wait_ld();
+      float mt;
+      {
+        float m[32];
         if (diag) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = c * 32 + i <= lim ? __uint_as_float(u[i]) : -INFINITY;
+          for (int i = 0; i < 32; ++i) {
+            const float a0 = i <= lim ? __uint_as_float(u0[i]) : -INFINITY;
+            const float a1 = 32 + i <= lim ? __uint_as_float(u1[i]) : -INFINITY;
+            m[i] = fmaxf(a0, a1);
+          }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(u[i]);
+          for (int i = 0; i < 32; ++i) m[i] = fmaxf(__uint_as_float(u0[i]), __uint_as_float(u1[i]));
         }
 #pragma unroll
         for (int st = 16; st >= 1; st >>= 1)
 #pragma unroll
-          for (int i = 0; i < st; ++i) v[i] = fmaxf(v[i], v[i + st]);
-        mt = fmaxf(mt, v[0]);
+          for (int i = 0; i < st; ++i) m[i] = fmaxf(m[i], m[i + st]);
+        mt = m[0];
       }
       if (!row_ok) mt = -INFINITY;
       float* xm = row_max + (sl * 2 + g) * TR;
@@ -476,24 +499,18 @@ __global__ void __launch_bounds__(kThreadsT, 1)
       const float alpha = raise ? ex2(m_used - m_new) : 1.f;  // 0 when m_used was -inf
       m_used = m_new;
       const float base = (m_used == -INFINITY) ? 0.f : m_used;
-      // pass 2: P = 2^(s * scale - m) as bf16 pairs into TMEM
+      // P = 2^(s * scale - m) as bf16 pairs into TMEM; row sum
       const uint32_t pb = lane_base + kColP + (uint32_t)(sl * 64 + g * 32);
+      const bool masked = diag || !row_ok;
       float rs = 0.f;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t u[32];
-        tmem_ld32(sb + (uint32_t)(c * 32), u);
-        tmem_wait_ld();
+        uint32_t* uc = c == 0 ? u0 : u1;
         float e[32];
-        if (diag || !row_ok) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            e[i] = ex2(fmaf(__uint_as_float(u[i]), scale, -base));
-            if (c * 32 + i > lim) e[i] = 0.f;  // lim = -1 for rows that are not computed
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) e[i] = ex2(fmaf(__uint_as_float(u[i]), scale, -base));
+        for (int i = 0; i < 32; ++i) {
+          e[i] = ex2(fmaf(__uint_as_float(uc[i]), scale, -base));
+          if (masked && c * 32 + i > lim) e[i] = 0.f;  // lim = -1 for rows that are not computed
         }
         uint32_t pk[16];
 #pragma unroll
