@@ -1,8 +1,10 @@
 #!/usr/bin/env python
-"""Run the paged prefill attention a few times on one shape (a small, self-terminating case
-for ncu), Qwen2.5-7B heads (28 query / 4 KV heads, d 128), INT4 KV pages.
+"""Run the paged prefill (or, with --decode B, decode) attention a few times on one shape (a
+small, self-terminating case for ncu), Qwen2.5-7B heads (28 query / 4 KV heads, d 128), INT4
+KV pages.
 
     python bench/prof_attn.py --lens 2048 --iters 3
+    python bench/prof_attn.py --decode 64 --lens 1300 --iters 3
 """
 import argparse
 import math
@@ -24,9 +26,12 @@ def main():
     ap.add_argument("--kv", default="int4")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--trace", action="store_true", help="print the pipeline timeline of the heaviest CTA")
+    ap.add_argument("--decode", type=int, default=0, help="decode batch: B sequences of --lens context, 1 query each")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     lens = [int(x) for x in a.lens.split(",")]
+    if a.decode:
+        lens = lens[:1] * a.decode
     d, ps, grp = 128, 16, 32
     fk, fv = ops.KV_FORMATS[a.kv]
     cbk, nsk = kv_row_bytes(fk, d, grp)
@@ -46,6 +51,16 @@ def main():
         for s0 in range(0, n, 32):
             tseq.append(i)
             tq0.append(s0)
+    if a.decode:
+        qd = torch.randn(B, a.hq * d, device=dev, dtype=torch.bfloat16)
+        od = torch.empty_like(qd)
+        for _ in range(a.iters):
+            ops.paged_decode_attention(qd, kc, ks, vc, vs, bt, ql.to(dev), od, a.hq, a.hkv, d, ps, grp, fk, fv,
+                                       1 / math.sqrt(d), max(lens))
+        torch.cuda.synchronize()
+        ops.workspace(dev).check()
+        print("ok decode", B, "x", lens[0])
+        return
     T = int(ql.sum())
     q = torch.randn(T, a.hq * d, device=dev, dtype=torch.bfloat16)
     out = torch.empty_like(q)

@@ -48,10 +48,133 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
 }
 
 // ------------------------------------------------------------------------------- decode
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Half of one (page, head, token) row (D/2 dims) in registers, with its scale / zero per
+// 32-dim quarter converted at load, so a chunk of 8 dims dequantizes in a few bit operations
+// and two bf16x2 FMAs (4/2-bit codes) or eight fp32 FMAs (8-bit codes).
+template <int D, int FMT>
+struct FastHalf {
+  static constexpr int DL = D / 2;
+  static constexpr int kBytes = DL * kv_bits(FMT) / 8;
+  static constexpr int kWords = kBytes / 4;
+  static constexpr int NQ = DL >= 32 ? DL / 32 : 1;
+  static_assert(kBytes % 4 == 0, "half rows are whole 32-bit words");
+  uint32_t w[kWords];
+  uint32_t s2[NQ], z2[NQ];
+  float sf[NQ], zf[NQ];
+
+  __device__ __forceinline__ void clear() {
+#pragma unroll
+    for (int i = 0; i < kWords; ++i) w[i] = 0u;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      s2[q] = z2[q] = 0u;
+      sf[q] = zf[q] = 0.f;
+    }
+  }
+
+  __device__ __forceinline__ void load(const uint8_t* __restrict__ row_codes, const __half* __restrict__ row_scales,
+                                       int part, int G) {
+    const uint8_t* src = row_codes + part * kBytes;
+    if constexpr (kBytes % 16 == 0) {
+#pragma unroll
+      for (int i = 0; i < kWords / 4; ++i) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + i);
+        w[4 * i] = v.x;
+        w[4 * i + 1] = v.y;
+        w[4 * i + 2] = v.z;
+        w[4 * i + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kWords; ++i) w[i] = __ldg(reinterpret_cast<const uint32_t*>(src) + i);
+    }
+    if constexpr (FMT != KV_BF16) {
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        const int g = (part * DL + q * 32) / G;
+        float sc, ze;
+        if constexpr (kv_asym(FMT)) {
+          sc = __half2float(__ldg(row_scales + 2 * g));
+          ze = __half2float(__ldg(row_scales + 2 * g + 1));
+        } else {
+          sc = __half2float(__ldg(row_scales + g));
+          ze = FMT == KV_INT4 ? -7.5f * sc : FMT == KV_INT2 ? -1.5f * sc : 0.f;
+        }
+        sf[q] = sc;
+        zf[q] = ze;
+        s2[q] = pack_bf2(sc, sc);
+        z2[q] = pack_bf2(ze, ze);
+      }
+    }
+  }
+
+  // dims [8c, 8c + 8) of the half row -> 8 bf16
+  __device__ __forceinline__ uint4 dequant(int c) const {
+    if constexpr (FMT == KV_BF16) {
+      return make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    } else {
+      const int q = NQ == 1 ? 0 : (c >> 2);
+      uint32_t o[4];
+      if constexpr (FMT == KV_INT4 || FMT == KV_V4 || FMT == KV_INT2) {
+        const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.f, 128.f);
+        const __nv_bfloat162 s = *reinterpret_cast<const __nv_bfloat162*>(&s2[q]);
+        const __nv_bfloat162 z = *reinterpret_cast<const __nv_bfloat162*>(&z2[q]);
+        if constexpr (FMT == KV_INT2) {
+          const uint32_t word = (w[c >> 1] >> ((c & 1) * 16)) & 0xFFFFu;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint32_t t = ((word >> (4 * i)) & 0x3u) | (((word >> (4 * i + 2)) & 0x3u) << 16) | 0x43004300u;
+            const __nv_bfloat162 r = __hfma2(__hsub2(*reinterpret_cast<__nv_bfloat162*>(&t), k128), s, z);
+            o[i] = *reinterpret_cast<const uint32_t*>(&r);
+          }
+        } else {
+          // byte i of the word = dims (2i, 2i+1) as (low, high) nibble
+          const uint32_t lo = w[c] & 0x0F0F0F0Fu, hi = (w[c] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint32_t t = (__byte_perm(lo, hi, (uint32_t)(i | ((4 + i) << 8))) & 0x00FF00FFu) | 0x43004300u;
+            const __nv_bfloat162 r = __hfma2(__hsub2(*reinterpret_cast<__nv_bfloat162*>(&t), k128), s, z);
+            o[i] = *reinterpret_cast<const uint32_t*>(&r);
+          }
+        }
+      } else {  // 8-bit
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t word = w[2 * c + (i >> 1)];
+          const int sh = (i & 1) * 16;
+          float a, b;
+          if constexpr (FMT == KV_INT8) {
+            a = (float)(int8_t)((word >> sh) & 0xFF);
+            b = (float)(int8_t)((word >> (sh + 8)) & 0xFF);
+          } else {
+            a = (float)((word >> sh) & 0xFF);
+            b = (float)((word >> (sh + 8)) & 0xFF);
+          }
+          o[i] = pack_bf2(fmaf(a, sf[q], zf[q]), fmaf(b, sf[q], zf[q]));
+        }
+      }
+      return make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+
+  __device__ __forceinline__ void store(__nv_bfloat16* dst) const {
+#pragma unroll
+    for (int c = 0; c < DL / 8; ++c) *reinterpret_cast<uint4*>(dst + c * 8) = dequant(c);
+  }
+};
+
 // grid (B, Hkv, splits), 4 warps; warp w handles 16-token tiles t0+w, t0+w+4, ...
-// M side of each MMA = the G_q query heads of this KV head (padded to 16).
+// M side of each MMA = the G_q query heads of this KV head (padded to 16), read from a
+// shared-memory copy of Q by ldmatrix per tile (keeps 32 registers free for occupancy).
+// The running max is raised, and O rescaled, only when it grows by more than 2^8.
 template <int D, int FK, int FV>
-__global__ void __launch_bounds__(128) decode_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(128, (FK == KV_BF16 || kv_bits(FK) == 8) ? 3 : 4) decode_kernel(const AttnParams p) {
   pdl_wait();
   pdl_trigger();
   constexpr int LD = D + 8;
@@ -66,27 +189,23 @@ __global__ void __launch_bounds__(128) decode_kernel(const AttnParams p) {
   const int t0 = split * p.tiles_per_split;
   const int t1 = min(n_tiles, t0 + p.tiles_per_split);
   const int* bt = p.block_tables + (size_t)b * p.bt_stride;
-  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(sm) + warp * 2 * 16 * LD;
+  __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(sm);       // [16][LD]
+  __nv_bfloat16* Ks = Qs + 16 * LD + warp * 2 * 16 * LD;           // per warp [16][LD]
   __nv_bfloat16* Vs = Ks + 16 * LD;
   const float scale = p.sm_scale * kLog2e;
 
-  // Q fragments (A operand, rows = heads g and g+8).
-  uint32_t qa[D / 16][4];
+  // Q rows (query heads of this KV head; rows >= Gq zero) -> shared memory
   {
     const __nv_bfloat16* qb = p.q + (size_t)b * p.ld_q + (size_t)h * Gq * D;
-#pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      const int c0 = ks * 16 + 2 * t4;
-      auto ld2 = [&](int row, int col) -> uint32_t {
-        if (row >= Gq) return 0u;
-        return *reinterpret_cast<const uint32_t*>(qb + (size_t)row * D + col);
-      };
-      qa[ks][0] = ld2(g, c0);
-      qa[ks][1] = ld2(g + 8, c0);
-      qa[ks][2] = ld2(g, c0 + 8);
-      qa[ks][3] = ld2(g + 8, c0 + 8);
+    for (int i = threadIdx.x; i < 16 * (D / 8); i += blockDim.x) {
+      const int r = i / (D / 8), c = i % (D / 8);
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < Gq) v = *reinterpret_cast<const uint4*>(qb + (size_t)r * D + c * 8);
+      *reinterpret_cast<uint4*>(Qs + r * LD + c * 8) = v;
     }
   }
+  __syncthreads();
+  const uint32_t qbase = smem_addr(Qs);
   float o[D / 8][4];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
@@ -95,8 +214,8 @@ __global__ void __launch_bounds__(128) decode_kernel(const AttnParams p) {
   // Each lane owns half a row (token lane/2, dims [half*D/2, +D/2)) of the 16-token tile.
   // A tile never crosses a page (page_size % 16 == 0), so one page-table read per tile;
   // the next tile's raw codes are loaded into registers while this tile is computed.
-  using RK = RowPart<D, FK, 2>;
-  using RV = RowPart<D, FV, 2>;
+  using RK = FastHalf<D, FK>;
+  using RV = FastHalf<D, FV>;
   const int rr = lane >> 1, part = lane & 1;
   const int PS = p.page_size;
   constexpr int CBK = kv_code_bytes(FK, D), CBV = kv_code_bytes(FV, D);
@@ -118,8 +237,8 @@ __global__ void __launch_bounds__(128) decode_kernel(const AttnParams p) {
   fetch(t0 + warp, rk, rv);
   for (int tile = t0 + warp; tile < t1; tile += NWARP) {
     const int tok0 = tile * 16;
-    rk.store(Ks + rr * LD + part * RK::DIMS, p.group);
-    rv.store(Vs + rr * LD + part * RV::DIMS, p.group);
+    rk.store(Ks + rr * LD + part * RK::DL);
+    rv.store(Vs + rr * LD + part * RV::DL);
     fetch(tile + NWARP, rk, rv);  // in flight during this tile's math
     __syncwarp();
     float s[2][4];
@@ -128,12 +247,14 @@ __global__ void __launch_bounds__(128) decode_kernel(const AttnParams p) {
     const uint32_t kbase = smem_addr(Ks);
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(qbase + (((lane & 15) * LD) + ks * 16 + (lane >> 4) * 8) * 2, a0, a1, a2, a3);
       const int tok = (lane & 7) + ((lane >> 4) << 3);
       const int col = ks * 16 + ((lane >> 3) & 1) * 8;
       uint32_t b0, b1, b2, b3;
       ldsm_x4(kbase + (tok * LD + col) * 2, b0, b1, b2, b3);
-      mma16816(s[0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
-      mma16816(s[1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
+      mma16816(s[0], a0, a1, a2, a3, b0, b1);
+      mma16816(s[1], a0, a1, a2, a3, b2, b3);
     }
     // scale + mask + online softmax (rows g, g+8; columns = tokens)
     float mx0 = -INFINITY, mx1 = -INFINITY;
@@ -154,30 +275,33 @@ __global__ void __launch_bounds__(128) decode_kernel(const AttnParams p) {
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
     }
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float a0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - mn0);
-    const float a1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - mn1);
-    const float base0 = (mn0 == -INFINITY) ? 0.f : mn0, base1 = (mn1 == -INFINITY) ? 0.f : mn1;
-    m0 = mn0;
-    m1 = mn1;
+    // lazy max: raise only when the tile max exceeds the running one by > 2^8
+    const bool r0 = mx0 > m0 + 8.f, r1 = mx1 > m1 + 8.f;
+    const float a0 = r0 ? ex2f(m0 - mx0) : 1.f;  // 0 when m was -inf
+    const float a1 = r1 ? ex2f(m1 - mx1) : 1.f;
+    if (r0) m0 = mx0;
+    if (r1) m1 = mx1;
+    const float base0 = (m0 == -INFINITY) ? 0.f : m0, base1 = (m1 == -INFINITY) ? 0.f : m1;
     float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      s[nt][0] = exp2f(s[nt][0] - base0);
-      s[nt][1] = exp2f(s[nt][1] - base0);
-      s[nt][2] = exp2f(s[nt][2] - base1);
-      s[nt][3] = exp2f(s[nt][3] - base1);
+      s[nt][0] = ex2f(s[nt][0] - base0);
+      s[nt][1] = ex2f(s[nt][1] - base0);
+      s[nt][2] = ex2f(s[nt][2] - base1);
+      s[nt][3] = ex2f(s[nt][3] - base1);
       rs0 += s[nt][0] + s[nt][1];
       rs1 += s[nt][2] + s[nt][3];
     }
     l0 = l0 * a0 + rs0;
     l1 = l1 * a1 + rs1;
+    if (__any_sync(0xffffffffu, r0 || r1)) {
 #pragma unroll
-    for (int i = 0; i < D / 8; ++i) {
-      o[i][0] *= a0;
-      o[i][1] *= a0;
-      o[i][2] *= a1;
-      o[i][3] *= a1;
+      for (int i = 0; i < D / 8; ++i) {
+        o[i][0] *= a0;
+        o[i][1] *= a0;
+        o[i][2] *= a1;
+        o[i][3] *= a1;
+      }
     }
     const uint32_t pa0 = pack_bf2(s[0][0], s[0][1]), pa1 = pack_bf2(s[0][2], s[0][3]);
     const uint32_t pa2 = pack_bf2(s[1][0], s[1][1]), pa3 = pack_bf2(s[1][2], s[1][3]);
@@ -503,7 +627,7 @@ __global__ void __launch_bounds__(256) prefill_kernel(const AttnParams p) {
 template <int D, int FK, int FV>
 cudaError_t launch_decode(const AttnParams& p, cudaStream_t s) {
   constexpr int LD = D + 8;
-  const size_t kv_bytes = (size_t)4 * 2 * 16 * LD * 2;
+  const size_t kv_bytes = (size_t)(1 + 4 * 2) * 16 * LD * 2;  // Q tile + per-warp K / V tiles
   const size_t merge_bytes = (size_t)4 * 16 * 2 * 4 + (size_t)4 * 16 * D * 4;
   const size_t smem = kv_bytes > merge_bytes ? kv_bytes : merge_bytes;
   auto k = decode_kernel<D, FK, FV>;
