@@ -14,7 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("squish_b200", "csrc")
 
 cuda_sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-cpp_sources = [os.path.join(CSRC, "bindings.cpp"), os.path.join(CSRC, "cpu_ref.cpp")]
+cpp_sources = [os.path.join(CSRC, "bindings.cpp"), os.path.join(CSRC, "cpu_ref.cpp"), os.path.join(CSRC, "entropy.cpp")]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <string>
 
 #include "w4a16_gemm.h"
 #include "bf16_gemm.h"
@@ -27,7 +28,7 @@ namespace {
 #define CUDA_OK(expr)                                                                       \
   do {                                                                                      \
     cudaError_t _e = (expr);                                                                \
-    TORCH_CHECK(_e == cudaSuccess, "squish_b200 kernel launch failed: ", cudaGetErrorString(_e)); \
+    TORCH_CHECK(_e == cudaSuccess, std::string("squish_b200 kernel launch failed: ") + cudaGetErrorString(_e)); \
   } while (0)
 
 template <typename T>
@@ -63,7 +64,7 @@ CUtensorMap make_bf16_map(const void* base, int rows, int cols, int ld, int box_
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", (int)r, ")");
+  TORCH_CHECK(r == CUDA_SUCCESS, std::string("cuTensorMapEncodeTiled failed (") + std::to_string((int)r) + ")");
   return m;
 }
 
@@ -713,7 +714,7 @@ void paged_prefill_attention(torch::Tensor q, torch::Tensor k_codes, torch::Tens
     CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q.data_ptr(), dims, strides, box, estr,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (q) failed (", (int)r, ")");
+    TORCH_CHECK(r == CUDA_SUCCESS, std::string("cuTensorMapEncodeTiled (q) failed (") + std::to_string((int)r) + ")");
     CUDA_OK(sq::paged_prefill_attn_tc_launch(m, p, ptr<int>(*status), optr<unsigned long long>(trace),
                                              cur_stream()));
     return;

@@ -413,6 +413,8 @@ torch::Tensor dequantize_int2(torch::Tensor packed, torch::Tensor scales, torch:
 // x: [rows, D] -> codes [rows, D*bits/8] u8, scales [rows, nscale] f32 (fp16-rounded like the kernel)
 std::vector<torch::Tensor> kv_quantize(torch::Tensor x, int64_t fmt, int64_t group) {
   check_cpu_f32_2d(x, "x");
+  TORCH_CHECK(fmt >= 1 && fmt <= 5, "kv format must be int8 / int4 / int2 / k8 / v4 (1..5)");
+  TORCH_CHECK(group > 0 && x.size(1) % group == 0, "group must divide the row length");
   const int64_t R = x.size(0), D = x.size(1), NG = D / group;
   const bool asym = (fmt == 4 || fmt == 5);
   const int bits = fmt == 1 || fmt == 4 ? 8 : fmt == 2 || fmt == 5 ? 4 : 2;
@@ -467,6 +469,17 @@ std::vector<torch::Tensor> kv_quantize(torch::Tensor x, int64_t fmt, int64_t gro
 }
 
 torch::Tensor kv_dequantize(torch::Tensor codes, torch::Tensor scales, int64_t fmt, int64_t group, int64_t D) {
+  TORCH_CHECK(fmt >= 1 && fmt <= 5, "kv format must be int8 / int4 / int2 / k8 / v4 (1..5)");
+  TORCH_CHECK(group > 0 && D % group == 0, "group must divide D");
+  TORCH_CHECK(codes.dim() == 2 && scales.dim() == 2 && codes.size(0) == scales.size(0), "codes / scales: [rows, ...]");
+  TORCH_CHECK(codes.scalar_type() == torch::kUInt8 && codes.is_contiguous() && !codes.is_cuda(), "codes: uint8 CPU");
+  TORCH_CHECK(scales.scalar_type() == torch::kFloat32 && scales.is_contiguous() && !scales.is_cuda(),
+              "scales: float32 CPU");
+  {
+    const int bits = fmt == 1 || fmt == 4 ? 8 : fmt == 2 || fmt == 5 ? 4 : 2;
+    TORCH_CHECK(codes.size(1) == D * bits / 8, "codes row length does not match D and the format");
+    TORCH_CHECK(scales.size(1) >= (D / group) * ((fmt == 4 || fmt == 5) ? 2 : 1), "too few scales per row");
+  }
   const int64_t R = codes.size(0), CB = codes.size(1), NS = scales.size(1);
   const bool asym = (fmt == 4 || fmt == 5);
   const int bits = fmt == 1 || fmt == 4 ? 8 : fmt == 2 || fmt == 5 ? 4 : 2;
@@ -492,8 +505,11 @@ torch::Tensor kv_dequantize(torch::Tensor codes, torch::Tensor scales, int64_t f
 
 }  // namespace
 
+void register_entropy(pybind11::module& c);  // entropy.cpp
+
 void register_cpu(pybind11::module& m) {
   auto c = m.def_submodule("cpu", "C++ CPU reference kernels (restating squish_quant_rs)");
+  register_entropy(c);
   c.def("quantize_int8", &quantize_int8);
   c.def("dequantize_int8", &dequantize_int8);
   c.def("quantize_int4_asym", &quantize_int4_asym);

@@ -16,8 +16,8 @@ Suffix sets, in the reference loader's dispatch priority (squish/io/loader_utils
     __aqlm_idx + __aqlm_cb              AQLM additive codebooks
     __q + __s                           INT8 symmetric (per row or per group)
     __pt                                float16 passthrough
-plus __shape (the original shape) for every tensor. ``.npy.zst`` files are read when the
-``zstandard`` module is importable.
+plus __shape (the original shape) for every tensor. ``.npy.sqe`` files (rANS / Huffman coded,
+io/entropy.py) are always readable; ``.npy.zst`` files when ``zstandard`` is importable.
 
 ``squish_4bit`` (squish/quant/compressed_loader.py:1109-1240): MLX affine 4-bit, one
 safetensors file; ``weight`` uint32 words of 8 nibbles (lowest nibble = lowest column),
@@ -45,6 +45,11 @@ def safe_key(name: str) -> str:
 def _load(path: Path) -> np.ndarray:
     if path.exists():
         return np.load(str(path), mmap_mode="r")
+    sqe = Path(str(path) + ".sqe")
+    if sqe.exists():  # rANS / Huffman coded copy (io/entropy.py)
+        from .entropy import load_npy_sqe
+
+        return load_npy_sqe(sqe)
     zst = Path(str(path) + ".zst")
     if zst.exists():
         try:
@@ -61,7 +66,7 @@ def _load(path: Path) -> np.ndarray:
 
 def _exists(td: Path, key: str, suf: str) -> bool:
     p = td / f"{key}{suf}.npy"
-    return p.exists() or Path(str(p) + ".zst").exists()
+    return p.exists() or Path(str(p) + ".zst").exists() or Path(str(p) + ".sqe").exists()
 
 
 def tensor_dir(path: str | Path) -> Path:
