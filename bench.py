@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--max-batched-tokens", type=int, default=2048)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--prefill-weight-cache", type=int, default=1,
+                    help="1: keep bf16 expansions of the layer weights resident for prefill GEMMs")
     ap.add_argument("--clocks", default="1", help="sample nvidia-smi clocks during the timed region")
     return ap.parse_args()
 
@@ -190,10 +192,12 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     ecfg = EngineConfig(max_num_seqs=args.concurrency, max_num_batched_tokens=args.max_batched_tokens,
                         max_model_len=args.prompt_max + args.output_len + 16, cuda_graphs=not args.no_graphs,
-                        enable_prefix_caching=True, gpu_memory_utilization=0.85)
+                        enable_prefix_caching=True, gpu_memory_utilization=0.85,
+                        prefill_weight_cache=bool(args.prefill_weight_cache))
     t0 = time.time()
     eng = LLMEngine.from_preset(args.model, device=dev, seed=args.seed, ecfg=ecfg)  # same weights on every rank
     load_s = time.time() - t0
+    cache_gb = getattr(eng.runner, "prefill_cache_bytes", 0) / 1e9
     rng = np.random.default_rng(1000 + args.seed + rank)
     vocab = eng.cfg.vocab_size
 
@@ -271,6 +275,9 @@ def run_ours(args, world, rank, local):
             "kv": "int4 g32, 16-token pages",
             "l2": "no flush: weights (~4.4 GB) and KV exceed the 126 MB L2 every step",
             "cuda_graphs": not args.no_graphs,
+            "prefill_weight_cache_gb": round(cache_gb, 2),
+            "weights": "INT4 codes read by decode GEMMs; prefill GEMMs (>= 384 rows) read resident bf16 "
+                       "expansions of the same codes when prefill_weight_cache_gb > 0",
         },
         "ttft_ms": {"p50": pct(all_ttft, 50), "p99": pct(all_ttft, 99), "n": len(all_ttft)},
         "e2e": {"value": tot_tokens / max_wall, "unit": "tokens/s", "h2d_bytes_per_step": round(h2d),

@@ -49,6 +49,10 @@ class EngineConfig:
     kv_host_bytes: int = 0        # > 0: keep evicted prefix blocks in a host-RAM tier of this size
     kv_disk_dir: str | None = None  # spill (and persist across restarts) evicted prefix blocks here
     kv_disk_bytes: int = 8 << 30
+    # keep a bf16 expansion of every quantized layer weight resident for prefill GEMMs
+    # (>= DQ_GEMM_MIN_M tokens): ~4x the INT4 weight bytes of HBM for no per-step expansion;
+    # decode keeps reading the quantized codes
+    prefill_weight_cache: bool = True
 
 
 @dataclass
@@ -117,7 +121,8 @@ class LLMEngine:
             spec_rows = ecfg.max_num_seqs * ecfg.spec.max_nodes if ecfg.spec is not None else 0
             runner = CudaRunner(ck, dev, num_pages=1, max_num_tokens=ecfg.max_num_batched_tokens,
                                 max_num_seqs=ecfg.max_num_seqs, max_model_len=ecfg.max_model_len,
-                                free_checkpoint=True, spec_rows=spec_rows)
+                                free_checkpoint=True, spec_rows=spec_rows,
+                                prefill_weight_cache=ecfg.prefill_weight_cache)
             del runner.pools
             torch.cuda.empty_cache()
             num_pages = cls.plan_pages(ck.config, ck.quant, ecfg, dev)
@@ -160,7 +165,8 @@ class LLMEngine:
                           device=dev)
             runner = TPCudaRunner(ck, dev, 1, comm, max_num_tokens=ecfg.max_num_batched_tokens,
                                   max_num_seqs=ecfg.max_num_seqs, max_model_len=ecfg.max_model_len,
-                                  free_checkpoint=True, spec_rows=spec_rows)
+                                  free_checkpoint=True, spec_rows=spec_rows,
+                                  prefill_weight_cache=ecfg.prefill_weight_cache)
             del runner.pools
             torch.cuda.empty_cache()
             pages = torch.tensor([cls.plan_pages(runner.cfg, ck.quant, ecfg, dev)], device=dev)

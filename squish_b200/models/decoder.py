@@ -186,7 +186,7 @@ class CudaRunner:
 
     def __init__(self, ck: Checkpoint, device, num_pages: int, max_num_tokens: int = 4096, max_num_seqs: int = 256,
                  max_model_len: int = 4096, pools: KVPools | None = None, free_checkpoint: bool = False,
-                 spec_rows: int = 0):
+                 spec_rows: int = 0, prefill_weight_cache: bool = False):
         self.cfg: ModelConfig = ck.config
         self.qcfg: QuantConfig = ck.quant
         self.device = torch.device(device)
@@ -194,6 +194,7 @@ class CudaRunner:
         self.max_num_tokens = max_num_tokens
         self.max_num_seqs = max_num_seqs
         self.spec_rows = spec_rows
+        self.prefill_weight_cache = prefill_weight_cache
         self.max_model_len = max_model_len
         self.ws = ops.Workspace(dev)  # owned by this runner: its CUDA graphs capture these buffers
         self.fk, self.fv = KV_FORMATS[self.qcfg.kv_dtype]
@@ -258,10 +259,20 @@ class CudaRunner:
         self.tokens = torch.empty(B + T, dtype=torch.int32, device=dev)
         self.tokens_host = torch.empty(B + T, dtype=torch.int32, pin_memory=True)
         self.vout = torch.zeros(B, 2 + ops.kernels.MAX_TREE_NODES, dtype=torch.int32, device=dev)
+        self.prefill_cache_bytes = 0
         if T >= ops.kernels.DQ_GEMM_MIN_M:
-            # bf16 expansion buffer of the large-M GEMM path, sized for the largest layer weight
             ws = [w for lw in self.layers for w in (lw.qkv, lw.o, lw.gate_up, lw.down) if isinstance(w, ops.Int4Weight)]
-            if ws:
+            if ws and self.prefill_weight_cache and dev.type == "cuda":
+                # resident bf16 expansions: prefill GEMMs skip the per-step expansion (HBM for time).
+                # A runner whose row-parallel GEMMs run elsewhere (tensor parallel: fused with the
+                # all-reduce) caches only the column-parallel weights.
+                if type(self)._row_parallel is not CudaRunner._row_parallel:
+                    ws = [w for lw in self.layers for w in (lw.qkv, lw.gate_up) if isinstance(w, ops.Int4Weight)]
+                for w in ws:
+                    w.dense = ops.dequant_weight(w)
+                    self.prefill_cache_bytes += w.dense.numel() * 2
+            elif ws:
+                # bf16 expansion buffer of the large-M GEMM path, sized for the largest layer weight
                 self.ws.dq_buffer(max(w.n * ((w.k + 63) // 64 * 64) for w in ws))
         self.vout_host = torch.zeros(B, 2 + ops.kernels.MAX_TREE_NODES, dtype=torch.int32, pin_memory=True)
         self._layer_ptrs = None

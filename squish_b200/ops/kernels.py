@@ -111,6 +111,9 @@ class Int4Weight:
     bias: torch.Tensor | None = None
     fmt: int = 0  # WF_INT4 | WF_NF4 | WF_INT8 | WF_INT2 | WF_INT3 | WF_AQLM
     codebook: torch.Tensor | None = None  # WF_AQLM: [books, 256, 8] bf16
+    # optional resident bf16 expansion [n, 64 * ceil(k / 64)] for large-M GEMMs (the exact
+    # values the quantized GEMM computes with); None = expand per call
+    dense: torch.Tensor | None = None
 
     @property
     def nbytes(self) -> int:
@@ -283,6 +286,8 @@ def w4a16_linear(x: torch.Tensor, w: Int4Weight, out: torch.Tensor | None = None
         out = torch.empty((m, ncols), dtype=torch.bfloat16, device=x.device)
     if m >= DQ_GEMM_MIN_M and trace is None:
         # many token tiles: expand the weights to bf16 once, then a bf16 tensor-core GEMM
+        if w.dense is not None:
+            return bf16_linear(x, w.dense[:, : w.k], out, w.bias, residual, silu_mul, ws)
         kpad = (w.k + 63) // 64 * 64
         buf = ws.dq_buffer(w.n * kpad)
         if buf is not None:
