@@ -752,6 +752,41 @@ void sample(torch::Tensor logits, c10::optional<torch::Tensor> temperature, c10:
   CUDA_OK(sq::sampler_launch(p, ptr<float>(work), cur_stream()));
 }
 
+// GPU weight quantizers with the CPU library's output layouts (cpu_ref.cpp): returns
+// [codes, scales] (+ offsets for INT2). x: [rows, cols] float32 or bf16 on the GPU.
+std::vector<torch::Tensor> quantize_codec_cuda(torch::Tensor x, int64_t codec, int64_t group) {
+  CHECK_CUDA(x);
+  TORCH_CHECK(x.dim() == 2 && x.is_contiguous(), "x must be a contiguous 2-D tensor");
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 || x.scalar_type() == torch::kBFloat16, "x: float32 or bf16");
+  TORCH_CHECK(codec >= 0 && codec <= 4, "codec: 0 int8, 1 int4 sym, 2 nf4, 3 int3, 4 int2");
+  const int64_t N = x.size(0), D = x.size(1);
+  const int64_t g = (codec == 0 && group <= 0) ? D : group;
+  TORCH_CHECK(g > 0 && D % g == 0, "group must divide columns");
+  TORCH_CHECK(codec == 0 || g % (codec == 3 ? 8 : codec == 4 ? 4 : 2) == 0, "group too small for the codec's packing");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto u8 = x.options().dtype(torch::kUInt8);
+  torch::Tensor codes;
+  int64_t ld;
+  if (codec == 0) {
+    codes = torch::empty({N, D}, x.options().dtype(torch::kInt8));
+    ld = D;
+  } else if (codec == 3) {
+    ld = (D + 7) / 8 * 3;
+    codes = torch::zeros({N, ld}, u8);
+  } else {
+    ld = codec == 4 ? D / 4 : D / 2;
+    codes = torch::empty({N, ld}, u8);
+  }
+  auto scales = torch::empty({N, D / g}, x.options().dtype(torch::kFloat32));
+  auto offsets = torch::empty({codec == 4 ? N : 0, D / g}, x.options().dtype(torch::kFloat32));
+  CUDA_OK(sq::quantize_codec_launch(x.data_ptr(), x.scalar_type() == torch::kBFloat16, (int)codec,
+                                    reinterpret_cast<uint8_t*>(codes.data_ptr()), (int)ld, ptr<float>(scales),
+                                    codec == 4 ? ptr<float>(offsets) : nullptr, (int)N, (int)D, (int)g,
+                                    cur_stream()));
+  if (codec == 4) return {codes, scales, offsets};
+  return {codes, scales};
+}
+
 std::vector<torch::Tensor> quantize_int4_asym_cuda(torch::Tensor x, int64_t group, int64_t n_clip) {
   CHECK_CUDA(x);
   CHECK_CONTIG(x);
@@ -801,5 +836,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_prefill_attention", &paged_prefill_attention);
   m.def("sample", &sample);
   m.def("quantize_int4_asym", &quantize_int4_asym_cuda);
+  m.def("quantize_codec", &quantize_codec_cuda);
   sqcpu::register_cpu(m);
 }

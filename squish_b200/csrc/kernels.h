@@ -87,6 +87,9 @@ struct SamplerParams {
 };
 cudaError_t sampler_launch(const SamplerParams& p, float* work, cudaStream_t s);
 
+// codec 0 INT8 sym, 1 INT4 sym, 2 NF4, 3 INT3 (group % 8 == 0), 4 INT2 asym (offsets used)
+cudaError_t quantize_codec_launch(const void* x, bool bf16, int codec, uint8_t* codes, int code_ld, float* scales,
+                                  float* offsets, int rows, int cols, int group, cudaStream_t s);
 cudaError_t quantize_int4_asym_launch(const void* x, bool bf16, uint8_t* packed, float* scales, float* offsets,
                                       int rows, int cols, int group, int n_clip, cudaStream_t s);
 

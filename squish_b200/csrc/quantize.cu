@@ -81,7 +81,125 @@ __global__ void quantize_int4_asym_kernel(const T* __restrict__ x, uint8_t* __re
   }
 }
 
+// ------------------------------------------------------------------ other codecs
+// One thread per (row, group); the arithmetic mirrors the C++ CPU library (cpu_ref.cpp), which
+// restates squish_quant_rs: quantize_int8_grouped (lib.rs:121), quantize_int4_grouped (259),
+// NF4 (742-890), pack_int3_grouped_f32 (1125), quantize_int2_grouped_f32 (1440).
+__constant__ float kNf4Lv[16] = {-1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
+                                 -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f, 0.0f,
+                                 0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f,
+                                 0.33791524171829224f, 0.44070982933044434f, 0.5626170039176941f,
+                                 0.7229568362236023f, 1.0f};
+
+__device__ __forceinline__ float clampf_d(float v, float lo, float hi) { return fminf(fmaxf(v, lo), hi); }
+
+template <typename T>
+__device__ __forceinline__ float group_absmax(const T* src, int n) {
+  float am = 0.f;
+  for (int i = 0; i < n; ++i) am = fmaxf(am, fabsf(to_f(src[i])));
+  return am;
+}
+
+// codec: 0 INT8 sym (q int8, s = absmax/127, x * (1/s)), 1 INT4 sym (q+7 nibbles, s = absmax/7),
+// 2 NF4 (nearest level of x/absmax), 3 INT3 sym (s = absmax/3, 3-bit two's complement, 8 values
+// per 3 bytes of the row), 4 INT2 asym (s = (max-min)/3, offset min, 4 values per byte)
+template <typename T>
+__global__ void quantize_codec_kernel(const T* __restrict__ x, uint8_t* __restrict__ codes,
+                                      float* __restrict__ scales, float* __restrict__ offsets, int rows, int cols,
+                                      int group, int codec, int code_ld) {
+  const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int G = cols / group;
+  if (gid >= (long)rows * G) return;
+  const int r = (int)(gid / G), g = (int)(gid % G);
+  const T* src = x + (size_t)r * cols + (size_t)g * group;
+  uint8_t* row = codes + (size_t)r * code_ld;
+  const size_t si = (size_t)r * G + g;
+  if (codec == 4) {
+    float mn = INFINITY, mx = -INFINITY;
+    for (int i = 0; i < group; ++i) {
+      const float v = to_f(src[i]);
+      mn = fminf(mn, v);
+      mx = fmaxf(mx, v);
+    }
+    const float sc = mx == mn ? 1.f : (mx - mn) / 3.f;
+    scales[si] = sc;
+    offsets[si] = mn;
+    for (int i = 0; i < group; i += 4) {
+      uint8_t byte = 0;
+      for (int b = 0; b < 4; ++b) {
+        const uint8_t q = (uint8_t)clampf_d(roundf((to_f(src[i + b]) - mn) / sc), 0.f, 3.f);
+        byte |= (uint8_t)((q & 3) << (2 * b));
+      }
+      row[(g * group + i) / 4] = byte;
+    }
+    return;
+  }
+  const float am = group_absmax(src, group);
+  if (codec == 0) {
+    const float sc = am == 0.f ? 1.f : am / 127.f;
+    scales[si] = sc;
+    const float inv = 1.f / sc;
+    int8_t* q = reinterpret_cast<int8_t*>(row) + (size_t)g * group;
+    for (int i = 0; i < group; ++i) q[i] = (int8_t)clampf_d(roundf(to_f(src[i]) * inv), -127.f, 127.f);
+  } else if (codec == 1) {
+    const float sc = am == 0.f ? 1.f : am / 7.f;
+    scales[si] = sc;
+    for (int i = 0; i < group; i += 2) {
+      const int q0 = (int)clampf_d(roundf(to_f(src[i]) / sc), -7.f, 7.f) + 7;
+      const int q1 = (int)clampf_d(roundf(to_f(src[i + 1]) / sc), -7.f, 7.f) + 7;
+      row[(g * group + i) / 2] = (uint8_t)((q0 & 0xF) | ((q1 & 0xF) << 4));
+    }
+  } else if (codec == 2) {
+    const float sc = am == 0.f ? 1.f : am;
+    scales[si] = sc;
+    for (int i = 0; i < group; i += 2) {
+      uint8_t qq[2];
+      for (int k = 0; k < 2; ++k) {
+        const float v = to_f(src[i + k]) / sc;
+        int best = 0;
+        float bd = INFINITY;
+        for (int l = 0; l < 16; ++l) {
+          const float d = fabsf(v - kNf4Lv[l]);
+          if (d < bd) {
+            bd = d;
+            best = l;
+          }
+        }
+        qq[k] = (uint8_t)best;
+      }
+      row[(g * group + i) / 2] = (uint8_t)(qq[0] | (qq[1] << 4));
+    }
+  } else {  // codec 3: INT3; a group covers whole 8-value chunks (group % 8 == 0)
+    const float sc = am == 0.f ? 1.f : am / 3.f;
+    scales[si] = sc;
+    for (int ch = 0; ch < group / 8; ++ch) {
+      uint32_t bits = 0;
+      for (int b = 0; b < 8; ++b) {
+        const uint32_t v = (uint32_t)((int)clampf_d(roundf(to_f(src[ch * 8 + b]) / sc), -3.f, 3.f) & 7);
+        bits |= v << (3 * b);
+      }
+      const int c3 = ((g * group) / 8 + ch) * 3;
+      for (int k = 0; k < 3; ++k) row[c3 + k] = (uint8_t)((bits >> (8 * k)) & 0xFF);
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t quantize_codec_launch(const void* x, bool bf16, int codec, uint8_t* codes, int code_ld, float* scales,
+                                  float* offsets, int rows, int cols, int group, cudaStream_t s) {
+  const long total = (long)rows * (cols / group);
+  if (total == 0) return cudaSuccess;
+  const int threads = 128;
+  const unsigned blocks = (unsigned)((total + threads - 1) / threads);
+  if (bf16)
+    quantize_codec_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), codes,
+                                                                   scales, offsets, rows, cols, group, codec, code_ld);
+  else
+    quantize_codec_kernel<float><<<blocks, threads, 0, s>>>(reinterpret_cast<const float*>(x), codes, scales, offsets,
+                                                           rows, cols, group, codec, code_ld);
+  return cudaGetLastError();
+}
 
 cudaError_t quantize_int4_asym_launch(const void* x, bool bf16, uint8_t* packed, float* scales, float* offsets,
                                       int rows, int cols, int group, int n_clip, cudaStream_t s) {

@@ -40,6 +40,9 @@ def dequantize_qtensor(t: QTensor) -> torch.Tensor:
     raise ValueError(f"unknown tensor kind {k!r}")
 
 
+_GPU_CODEC = {"q8": 0, "nf4": 2, "q3": 3, "q2": 4}
+
+
 def quantize(w: torch.Tensor, kind: str, group: int, mse_clip: bool = False) -> QTensor:
     """Quantize a 2-D weight to ``kind`` (q4a | q8 | nf4 | q2 | q3 | aqlm | dense)."""
     from ..models.weights import pick_group, quantize_q4a
@@ -49,8 +52,16 @@ def quantize(w: torch.Tensor, kind: str, group: int, mse_clip: bool = False) -> 
         return quantize_q4a(w, group, mse_clip)
     if kind == "dense":
         return QTensor("dense", tuple(w.shape), data=w)
+    g = pick_group(w.shape[1], group)
+    if w.is_cuda and kind in _GPU_CODEC:
+        # the GPU quantizers (csrc/quantize.cu) produce the CPU library's layouts bit for bit
+        out = native().quantize_codec(w.detach().contiguous() if w.dtype in (torch.float32, torch.bfloat16)
+                                      else w.detach().float().contiguous(), _GPU_CODEC[kind], g)
+        out = [t.cpu() for t in out]
+        if kind == "q2":
+            return QTensor("q2", tuple(w.shape), packed=out[0], scales=out[1], offsets=out[2], group=g)
+        return QTensor(kind, tuple(w.shape), packed=out[0], scales=out[1], group=g)
     wf = w.detach().float().cpu().contiguous()
-    g = pick_group(wf.shape[1], group)
     if kind == "q8":
         q, s = C.quantize_int8(wf, g)
         return QTensor("q8", tuple(wf.shape), packed=q, scales=s, group=g)

@@ -75,3 +75,35 @@ def test_engine_with_format_weights_matches_oracle(cuda, kind):
     assert ok, (worst, out)
     assert eng.runner.layers[0].o.fmt == {"nf4": K.WF_NF4, "q8": K.WF_INT8, "q2": K.WF_INT2, "q3": K.WF_INT3,
                                           "aqlm": K.WF_AQLM}[kind]
+
+
+@pytest.mark.parametrize("codec,group", [(0, 64), (0, 0), (1, 32), (2, 64), (3, 32), (4, 64)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gpu_quantizers_match_cpu_library(codec, group, dtype):
+    """csrc/quantize.cu reproduces the CPU library's codes and scales (same float arithmetic)."""
+    from squish_b200._ext import native
+
+    C = native()
+    g = torch.Generator().manual_seed(codec * 7 + group)
+    x = (torch.randn(96, 512, generator=g) * 0.03).to(dtype)
+    xf = x.float()
+    got = [t.cpu() for t in C.quantize_codec(x.cuda(), codec, group)]
+    if codec == 0:
+        want = C.cpu.quantize_int8(xf, group)
+    elif codec == 1:
+        want = C.cpu.quantize_int4_sym(xf, group)
+    elif codec == 2:
+        want = C.cpu.quantize_nf4(xf, group)
+    elif codec == 3:
+        want = C.cpu.pack_int3(xf, group)
+    else:
+        want = C.cpu.quantize_int2(xf, group)
+    assert len(got) == len(want)
+    for a, b in zip(got, want):
+        assert a.shape == b.shape and a.dtype == b.dtype
+        if a.dtype.is_floating_point:
+            torch.testing.assert_close(a, b, rtol=1e-6, atol=0)
+        else:
+            # codes: identical except where a value sits on a rounding boundary (fused multiply-add
+            # contraction can differ between the compilers); allow a few
+            assert (a != b).float().mean().item() < 1e-3
