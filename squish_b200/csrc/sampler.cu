@@ -76,9 +76,11 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const SamplerParams p
   const bool greedy = !(temp > 0.f);
   const float inv_t = greedy ? 1.f : 1.f / temp;
 
-  // pass 0: load + mask
   const uint32_t* mask = p.allow_mask ? p.allow_mask + (size_t)row * ((V + 31) / 32) : nullptr;
-  for (int i = threadIdx.x; i < V; i += kThreads) {
+  const float rp0 = p.rep_penalty ? p.rep_penalty[row] : 1.f;
+  const bool fused_greedy = greedy && !(rp0 != 1.f && p.hist);
+  // pass 0: load + mask (greedy rows without a penalty: straight to the argmax, no fp32 copy)
+  for (int i = threadIdx.x; i < V && !fused_greedy; i += kThreads) {
     float v = __bfloat162float(lg[i]);
     if (mask && !((mask[i >> 5] >> (i & 31)) & 1u)) v = -INFINITY;
     x[i] = v;
@@ -107,12 +109,23 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const SamplerParams p
   // pass 1: temperature + max/argmax
   float mv = -INFINITY;
   int mi = 0;
-  for (int i = threadIdx.x; i < V; i += kThreads) {
-    const float v = x[i] * inv_t;
-    if (!greedy) x[i] = v;
-    if (v > mv) {
-      mv = v;
-      mi = i;
+  if (fused_greedy) {
+    for (int i = threadIdx.x; i < V; i += kThreads) {
+      float v = __bfloat162float(lg[i]);
+      if (mask && !((mask[i >> 5] >> (i & 31)) & 1u)) v = -INFINITY;
+      if (v > mv) {
+        mv = v;
+        mi = i;
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += kThreads) {
+      const float v = x[i] * inv_t;
+      if (!greedy) x[i] = v;
+      if (v > mv) {
+        mv = v;
+        mi = i;
+      }
     }
   }
   {
