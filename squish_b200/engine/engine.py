@@ -257,8 +257,17 @@ class LLMEngine:
         off = 0
         for i, e in enumerate(entries):
             r = e.req
-            pg = np.asarray(r.pages, dtype=np.int32)
-            bt[i, :len(r.pages)] = pg
+            pg = r.page_array()
+            bt[i, :len(pg)] = pg
+            if e.n == 1 and e.tree is None:  # decode: scalars, no per-entry numpy temporaries
+                ids[off] = r.token_at(e.start)
+                pos[off] = e.start
+                slots[off] = r.pages[e.start // ps] * ps + e.start % ps
+                if e.sample:
+                    rows.append(off)
+                    samp.append(r)
+                off += 1
+                continue
             if e.tree is not None:
                 tr = e.tree
                 ids[off:off + e.n] = tr.tokens
@@ -271,8 +280,7 @@ class LLMEngine:
                 vreqs.append(r)
                 off += e.n
                 continue
-            toks = r.tokens
-            ids[off:off + e.n] = toks[e.start:e.start + e.n]
+            ids[off:off + e.n] = r.token_slice(e.start, e.n)
             p = np.arange(e.start, e.start + e.n, dtype=np.int32)
             pos[off:off + e.n] = p
             slots[off:off + e.n] = pg[p // ps] * ps + p % ps

@@ -14,7 +14,7 @@ class Status(enum.Enum):
     FINISHED = 2
 
 
-@dataclass
+@dataclass(eq=False)  # identity: requests are unique, and field-wise equality is O(prompt) per compare
 class Request:
     rid: str
     prompt: list[int]
@@ -33,10 +33,35 @@ class Request:
     prefix_hit_tokens: int = 0
     preemptions: int = 0
     rng_step: int = 0
+    # cached int32 copy of `pages` for the step's block table (valid while `_bt_src is pages`
+    # and the length matches: pages only ever grow by append or are replaced by a new list)
+    _bt_src: list | None = field(default=None, repr=False)
+    _bt_arr: object = field(default=None, repr=False)
+
+    def page_array(self):
+        import numpy as np
+
+        if self._bt_src is not self.pages or len(self._bt_arr) != len(self.pages):
+            self._bt_src = self.pages
+            self._bt_arr = np.asarray(self.pages, dtype=np.int32)
+        return self._bt_arr
+
+    def token_at(self, i: int) -> int:
+        P = len(self.prompt)
+        return self.prompt[i] if i < P else self.output[i - P]
 
     @property
     def tokens(self) -> list[int]:
         return self.prompt + self.output if self.output else self.prompt
+
+    def token_slice(self, start: int, n: int) -> list[int]:
+        """tokens[start:start + n] without building the concatenated token list."""
+        P = len(self.prompt)
+        if start >= P:
+            return self.output[start - P:start - P + n]
+        if start + n <= P:
+            return self.prompt[start:start + n]
+        return self.prompt[start:] + self.output[:start + n - P]
 
     @property
     def total_len(self) -> int:

@@ -362,3 +362,11 @@ def test_sampler_distribution(cuda):
     freq = torch.bincount(out.long().cpu(), minlength=v)[:4].float() / rows
     ref2 = torch.softmax(base[:2].to(torch.bfloat16).float() / 0.7, 0)
     assert freq[2:].sum() == 0 and (freq[:2] - ref2).abs().max() < 0.03
+    # top_p: the smallest head of the sorted distribution whose mass reaches top_p, renormalised
+    full = torch.softmax(base[:4].to(torch.bfloat16).float() / 0.7, 0)
+    for tp, keep in ((0.8, 2), (0.9, 3), (0.5, 1)):
+        assert full[:keep].sum() >= tp and (keep == 1 or full[: keep - 1].sum() < tp)
+        ops.sample(logits, out, temperature=temp, top_p=torch.full((rows,), tp, device=cuda), seed=13, step=step)
+        freq = torch.bincount(out.long().cpu(), minlength=v)[:4].float() / rows
+        ref3 = full[:keep] / full[:keep].sum()
+        assert freq[keep:].sum() == 0 and (freq[:keep] - ref3).abs().max() < 0.03, (tp, freq, ref3)
