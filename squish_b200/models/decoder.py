@@ -261,13 +261,20 @@ class CudaRunner:
         self.vout = torch.zeros(B, 2 + ops.kernels.MAX_TREE_NODES, dtype=torch.int32, device=dev)
         self.prefill_cache_bytes = 0
         if T >= ops.kernels.DQ_GEMM_MIN_M:
-            ws = [w for lw in self.layers for w in (lw.qkv, lw.o, lw.gate_up, lw.down) if isinstance(w, ops.Int4Weight)]
+            allw = ws = [w for lw in self.layers for w in (lw.qkv, lw.o, lw.gate_up, lw.down)
+                         if isinstance(w, ops.Int4Weight)]
             if ws and self.prefill_weight_cache and dev.type == "cuda":
                 # resident bf16 expansions: prefill GEMMs skip the per-step expansion (HBM for time).
                 # A runner whose row-parallel GEMMs run elsewhere (tensor parallel: fused with the
                 # all-reduce) caches only the column-parallel weights.
                 if type(self)._row_parallel is not CudaRunner._row_parallel:
                     ws = [w for lw in self.layers for w in (lw.qkv, lw.gate_up) if isinstance(w, ops.Int4Weight)]
+                need = sum(w.n * ((w.k + 63) // 64 * 64) * 2 for w in ws)
+                free, _ = torch.cuda.mem_get_info(dev)
+                if need > free // 2:  # keep at least half of what is free for the KV cache
+                    self.prefill_weight_cache = False
+                    self.ws.dq_buffer(max(w.n * ((w.k + 63) // 64 * 64) for w in allw))
+                    ws = []
                 for w in ws:
                     w.dense = ops.dequant_weight(w)
                     self.prefill_cache_bytes += w.dense.numel() * 2
