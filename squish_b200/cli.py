@@ -106,13 +106,32 @@ def cmd_run(a) -> int:
 def cmd_compress(a) -> int:
     from .io.convert import compress
 
-    kind = {"int4": "q4a", "int8": "q8", "nf4": "nf4", "int3": "q3", "int2": "q2", "aqlm": "aqlm",
+    kind = {"int4": "q4a", "int8": "q8", "fp8": "fp8", "nf4": "nf4", "int3": "q3", "int2": "q2", "aqlm": "aqlm",
             "none": "dense"}[a.format]
     out = a.output or (str(Path(a.source).with_name(Path(a.source).name + "-squished")) if a.source else
                        str(ucfg.squish_home() / "models" / a.random_init))
     st = compress(a.source, out, kind=kind, group_size=a.group_size, mse_clip=a.mse, device=a.device,
-                  delete_source=a.delete_source, random_preset=a.random_init, seed=a.seed, kv_dtype=a.kv_dtype)
+                  delete_source=a.delete_source, random_preset=a.random_init, seed=a.seed, kv_dtype=a.kv_dtype,
+                  hqq=getattr(a, "hqq", False), awq=getattr(a, "awq", False),
+                  awq_scales=getattr(a, "awq_scales", None), awq_alpha=getattr(a, "awq_alpha", 0.5),
+                  awq_samples=getattr(a, "awq_samples", 16))
     print(json.dumps({"output": out, **st}))
+    return 0
+
+
+def cmd_merge_model(a) -> int:
+    from .quant.merge import merge_adapter_files
+
+    paths = []
+    for spec in a.adapters:  # "domain:path" (the domain is a label) or a bare path
+        d, _, p = spec.partition(":")
+        path = p if p and not Path(spec).exists() else spec
+        if not Path(path).expanduser().exists():
+            print(f"adapter path not found: {path}", file=sys.stderr)
+            return 2
+        paths.append(str(Path(path).expanduser()))
+    out = merge_adapter_files(paths, str(Path(a.output_path).expanduser()), a.method)
+    print(json.dumps(out))
     return 0
 
 
@@ -299,7 +318,7 @@ def build_parser() -> argparse.ArgumentParser:
     p = sub.add_parser("compress")
     p.add_argument("source", nargs="?", default=None)
     p.add_argument("-o", "--output", default=None)
-    p.add_argument("--format", default="int4", choices=["int4", "int8", "nf4", "int3", "int2", "aqlm", "none"])
+    p.add_argument("--format", default="int4", choices=["int4", "int8", "fp8", "nf4", "int3", "int2", "aqlm", "none"])
     p.add_argument("--group-size", type=int, default=64)
     p.add_argument("--mse", action="store_true", help="MSE-optimal clipping search (INT4)")
     p.add_argument("--random-init", default=None, metavar="PRESET")
@@ -307,7 +326,19 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--device", default=None)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-dtype", default="int4")
+    p.add_argument("--hqq", action="store_true", help="half-quadratic refinement of INT4 / INT2 grids")
+    p.add_argument("--awq", action="store_true", help="activation-aware scaling (calibrates on the fp32 model)")
+    p.add_argument("--awq-scales", default=None, metavar="DIR", help="apply saved AWQ scales instead")
+    p.add_argument("--awq-alpha", type=float, default=0.5)
+    p.add_argument("--awq-samples", type=int, default=16)
     p.set_defaults(fn=cmd_compress)
+
+    p = sub.add_parser("merge-model", help="merge LoRA adapters (DARE / TIES / DARE-TIES)")
+    p.add_argument("base_model", nargs="?", default=None)
+    p.add_argument("--adapters", nargs="+", required=True, metavar="DOMAIN:PATH")
+    p.add_argument("--method", default="dare-ties", choices=["dare", "ties", "dare-ties"])
+    p.add_argument("--output-path", required=True)
+    p.set_defaults(fn=cmd_merge_model)
 
     p = sub.add_parser("convert")
     p.add_argument("source")

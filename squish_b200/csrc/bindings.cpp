@@ -167,7 +167,7 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, 
                 torch::Tensor y, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual,
                 int64_t epilogue, torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
                 c10::optional<torch::Tensor> trace, int64_t wfmt, c10::optional<torch::Tensor> codebook) {
-  TORCH_CHECK(wfmt >= 0 && wfmt <= 5, "unknown weight format");
+  TORCH_CHECK(wfmt >= 0 && wfmt <= 6, "unknown weight format");
   if (wfmt == sq::WF_AQLM) {
     TORCH_CHECK(codebook.has_value() && codebook->scalar_type() == torch::kBFloat16 && codebook->is_cuda() &&
                     codebook->is_contiguous() && codebook->numel() % (256 * 8) == 0 && codebook->numel() <= 2 * 256 * 8,
@@ -219,7 +219,7 @@ void dequant_weight(torch::Tensor wq, int64_t N, int64_t K, int64_t group, int64
   CHECK_CUDA(wq);
   CHECK_CUDA(out);
   CHECK_DT(out, torch::kBFloat16);
-  TORCH_CHECK(wfmt >= 0 && wfmt <= 5, "unknown weight format");
+  TORCH_CHECK(wfmt >= 0 && wfmt <= 6, "unknown weight format");
   const int64_t kpad = (K + 63) / 64 * 64;
   TORCH_CHECK(out.dim() == 2 && out.size(0) >= N && out.stride(1) == 1 && out.stride(0) >= kpad &&
                   out.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
@@ -754,21 +754,25 @@ void sample(torch::Tensor logits, c10::optional<torch::Tensor> temperature, c10:
 
 // GPU weight quantizers with the CPU library's output layouts (cpu_ref.cpp): returns
 // [codes, scales] (+ offsets for INT2). x: [rows, cols] float32 or bf16 on the GPU.
-std::vector<torch::Tensor> quantize_codec_cuda(torch::Tensor x, int64_t codec, int64_t group) {
+std::vector<torch::Tensor> quantize_codec_cuda(torch::Tensor x, int64_t codec, int64_t group, double fixed_scale) {
   CHECK_CUDA(x);
   TORCH_CHECK(x.dim() == 2 && x.is_contiguous(), "x must be a contiguous 2-D tensor");
   TORCH_CHECK(x.scalar_type() == torch::kFloat32 || x.scalar_type() == torch::kBFloat16, "x: float32 or bf16");
-  TORCH_CHECK(codec >= 0 && codec <= 4, "codec: 0 int8, 1 int4 sym, 2 nf4, 3 int3, 4 int2");
+  TORCH_CHECK(codec >= 0 && codec <= 6, "codec: 0 int8, 1 int4 sym, 2 nf4, 3 int3, 4 int2, 5 fp8 e4m3, 6 fp8 e5m2");
   const int64_t N = x.size(0), D = x.size(1);
-  const int64_t g = (codec == 0 && group <= 0) ? D : group;
+  const int64_t g = ((codec == 0 || codec >= 5) && group <= 0) ? D : group;
   TORCH_CHECK(g > 0 && D % g == 0, "group must divide columns");
-  TORCH_CHECK(codec == 0 || g % (codec == 3 ? 8 : codec == 4 ? 4 : 2) == 0, "group too small for the codec's packing");
+  TORCH_CHECK(codec == 0 || codec >= 5 || g % (codec == 3 ? 8 : codec == 4 ? 4 : 2) == 0,
+              "group too small for the codec's packing");
   const c10::cuda::CUDAGuard guard(x.device());
   auto u8 = x.options().dtype(torch::kUInt8);
   torch::Tensor codes;
   int64_t ld;
   if (codec == 0) {
     codes = torch::empty({N, D}, x.options().dtype(torch::kInt8));
+    ld = D;
+  } else if (codec >= 5) {
+    codes = torch::empty({N, D}, u8);
     ld = D;
   } else if (codec == 3) {
     ld = (D + 7) / 8 * 3;
@@ -782,9 +786,38 @@ std::vector<torch::Tensor> quantize_codec_cuda(torch::Tensor x, int64_t codec, i
   CUDA_OK(sq::quantize_codec_launch(x.data_ptr(), x.scalar_type() == torch::kBFloat16, (int)codec,
                                     reinterpret_cast<uint8_t*>(codes.data_ptr()), (int)ld, ptr<float>(scales),
                                     codec == 4 ? ptr<float>(offsets) : nullptr, (int)N, (int)D, (int)g,
-                                    cur_stream()));
+                                    (float)fixed_scale, cur_stream()));
   if (codec == 4) return {codes, scales, offsets};
   return {codes, scales};
+}
+
+std::vector<torch::Tensor> hqq_cuda(torch::Tensor x, int64_t group, int64_t levels, double lam, int64_t iters) {
+  CHECK_CUDA(x);
+  TORCH_CHECK(x.dim() == 2 && x.is_contiguous(), "x must be a contiguous 2-D tensor");
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 || x.scalar_type() == torch::kBFloat16, "x: float32 or bf16");
+  const int64_t N = x.size(0), D = x.size(1);
+  TORCH_CHECK(group > 0 && group <= 512 && D % group == 0, "group must divide columns and be <= 512");
+  TORCH_CHECK(levels >= 2 && levels <= 256, "levels must be in [2, 256]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto codes = torch::empty({N, D}, x.options().dtype(torch::kUInt8));
+  auto scales = torch::empty({N, D / group}, x.options().dtype(torch::kFloat32));
+  auto zeros = torch::empty({N, D / group}, x.options().dtype(torch::kFloat32));
+  CUDA_OK(sq::hqq_launch(x.data_ptr(), x.scalar_type() == torch::kBFloat16,
+                         reinterpret_cast<uint8_t*>(codes.data_ptr()), ptr<float>(scales), ptr<float>(zeros), (int)N,
+                         (int)D, (int)group, (int)levels, (float)lam, (int)iters, cur_stream()));
+  return {codes, scales, zeros};
+}
+
+void channel_abs_mean_cuda(torch::Tensor x, torch::Tensor acc) {
+  CHECK_CUDA(x);
+  CHECK_CUDA(acc);
+  TORCH_CHECK(x.dim() == 2 && x.is_contiguous(), "x must be a contiguous 2-D tensor");
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 || x.scalar_type() == torch::kBFloat16, "x: float32 or bf16");
+  TORCH_CHECK(acc.scalar_type() == torch::kFloat64 && acc.numel() == x.size(1) && acc.is_contiguous(),
+              "acc: float64 with one entry per column");
+  const c10::cuda::CUDAGuard guard(x.device());
+  CUDA_OK(sq::channel_abs_mean_launch(x.data_ptr(), x.scalar_type() == torch::kBFloat16, acc.data_ptr<double>(),
+                                      (int)x.size(0), (int)x.size(1), cur_stream()));
 }
 
 std::vector<torch::Tensor> quantize_int4_asym_cuda(torch::Tensor x, int64_t group, int64_t n_clip) {
@@ -836,6 +869,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_prefill_attention", &paged_prefill_attention);
   m.def("sample", &sample);
   m.def("quantize_int4_asym", &quantize_int4_asym_cuda);
-  m.def("quantize_codec", &quantize_codec_cuda);
+  m.def("quantize_codec", &quantize_codec_cuda, py::arg("x"), py::arg("codec"), py::arg("group"),
+        py::arg("fixed_scale") = 0.0);
+  m.def("hqq", &hqq_cuda);
+  m.def("channel_abs_mean", &channel_abs_mean_cuda);
   sqcpu::register_cpu(m);
 }

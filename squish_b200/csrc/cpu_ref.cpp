@@ -11,6 +11,7 @@
 // Rust's f32::round rounds half away from zero; std::round does the same.
 #include <torch/extension.h>
 #include <ATen/Parallel.h>
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <vector>
@@ -503,6 +504,96 @@ torch::Tensor kv_dequantize(torch::Tensor codes, torch::Tensor scales, int64_t f
   return out;
 }
 
+// ---- FP8 (OCP 8-bit floating point, E4M3 "fn" and E5M2), software codec ------------------
+// The reference's experimental FP8 pair (lib.rs:960-1100) truncates the mantissa and flushes
+// subnormals; this codec rounds to nearest even, keeps subnormals and saturates to the largest
+// finite value, i.e. the conversion the sm_100a `cvt.rn.satfinite.e4m3x2/e5m2x2` instructions
+// perform, so CPU and GPU codes agree bit for bit. Scale: absmax / largest finite per group, or
+// one caller-given scale for every group (the reference's per-tensor form).
+struct Fp8Fmt {
+  int mbits, bias, maxcode;
+  float maxval;
+};
+const Fp8Fmt kE4M3{3, 7, 0x7E, 448.f}, kE5M2{2, 15, 0x7B, 57344.f};
+
+uint8_t fp8_encode(float v, const Fp8Fmt& f) {
+  const uint8_t sign = std::signbit(v) ? 0x80 : 0;
+  if (std::isnan(v)) return sign | 0x7F;
+  const float a = std::fabs(v);
+  if (a == 0.f) return sign;
+  if (std::isinf(a)) return sign | (uint8_t)f.maxcode;
+  int e2;
+  std::frexp(a, &e2);
+  const int ex = e2 - 1;          // a in [2^ex, 2^(ex+1))
+  const int emin = 1 - f.bias;    // smallest normal exponent
+  long code;
+  if (ex < emin) {
+    // subnormal: integer multiples of 2^(emin - mbits); a count of 2^mbits is the smallest normal
+    code = (long)std::nearbyint(std::ldexp(a, f.mbits - emin));
+  } else {
+    const float m = std::ldexp(a, -ex) - 1.f;  // exact, in [0, 1)
+    code = ((long)(ex + f.bias) << f.mbits) + (long)std::nearbyint(std::ldexp(m, f.mbits));  // carry rolls into the exponent
+  }
+  if (code > f.maxcode) code = f.maxcode;
+  return sign | (uint8_t)code;
+}
+
+float fp8_decode(uint8_t c, const Fp8Fmt& f) {
+  const int mag = c & 0x7F;
+  const float sg = (c & 0x80) ? -1.f : 1.f;
+  const int field = mag >> f.mbits, mant = mag & ((1 << f.mbits) - 1);
+  if (f.mbits == 3 && mag == 0x7F) return std::nanf("");
+  if (f.mbits == 2 && field == 31) return mant ? std::nanf("") : sg * INFINITY;
+  if (field == 0) return sg * std::ldexp((float)mant, 1 - f.bias - f.mbits);
+  return sg * std::ldexp(1.f + std::ldexp((float)mant, -f.mbits), field - f.bias);
+}
+
+std::vector<torch::Tensor> quantize_fp8(torch::Tensor x, int64_t fmt, int64_t group, double fixed_scale) {
+  check_cpu_f32_2d(x, "x");
+  TORCH_CHECK(fmt == 0 || fmt == 1, "fmt: 0 e4m3, 1 e5m2");
+  const Fp8Fmt& f = fmt == 0 ? kE4M3 : kE5M2;
+  const int64_t N = x.size(0), D = x.size(1), g = group <= 0 ? D : group;
+  TORCH_CHECK(D % g == 0, "group must divide columns");
+  const int64_t G = D / g;
+  auto codes = torch::empty({N, D}, torch::kUInt8);
+  auto scales = torch::empty({N, G}, torch::kFloat32);
+  const float* xp = x.data_ptr<float>();
+  uint8_t* cp = codes.data_ptr<uint8_t>();
+  float* sp = scales.data_ptr<float>();
+  prange(N * G, [&](int64_t i) {
+    const int64_t r = i / G, gi = i % G;
+    const float* src = xp + r * D + gi * g;
+    float sc = (float)fixed_scale;
+    if (!(sc > 0.f)) {
+      float am = 0.f;
+      for (int64_t j = 0; j < g; ++j) am = std::max(am, std::fabs(src[j]));
+      sc = am == 0.f ? 1.f : am / f.maxval;
+    }
+    sp[i] = sc;
+    for (int64_t j = 0; j < g; ++j) cp[r * D + gi * g + j] = fp8_encode(src[j] / sc, f);
+  });
+  return {codes, scales};
+}
+
+torch::Tensor dequantize_fp8(torch::Tensor codes, torch::Tensor scales, int64_t fmt) {
+  TORCH_CHECK(codes.scalar_type() == torch::kUInt8 && codes.dim() == 2 && codes.is_contiguous(),
+              "codes: contiguous uint8 [N, D]");
+  check_cpu_f32_2d(scales, "scales");
+  TORCH_CHECK(fmt == 0 || fmt == 1, "fmt: 0 e4m3, 1 e5m2");
+  const Fp8Fmt& f = fmt == 0 ? kE4M3 : kE5M2;
+  const int64_t N = codes.size(0), D = codes.size(1), G = scales.size(1);
+  TORCH_CHECK(scales.size(0) == N && G > 0 && D % G == 0, "scales: [N, groups] with groups dividing D");
+  const int64_t g = D / G;
+  auto out = torch::empty({N, D}, torch::kFloat32);
+  const uint8_t* cp = codes.data_ptr<uint8_t>();
+  const float* sp = scales.data_ptr<float>();
+  float* o = out.data_ptr<float>();
+  prange(N, [&](int64_t r) {
+    for (int64_t d = 0; d < D; ++d) o[r * D + d] = fp8_decode(cp[r * D + d], f) * sp[r * G + d / g];
+  });
+  return out;
+}
+
 }  // namespace
 
 void register_entropy(pybind11::module& c);  // entropy.cpp
@@ -526,6 +617,9 @@ void register_cpu(pybind11::module& m) {
   c.def("dequantize_int2", &dequantize_int2);
   c.def("kv_quantize", &kv_quantize);
   c.def("kv_dequantize", &kv_dequantize);
+  c.def("quantize_fp8", &quantize_fp8, pybind11::arg("x"), pybind11::arg("fmt"), pybind11::arg("group"),
+        pybind11::arg("fixed_scale") = 0.0);
+  c.def("dequantize_fp8", &dequantize_fp8);
 }
 
 }  // namespace sqcpu

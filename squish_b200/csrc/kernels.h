@@ -89,7 +89,13 @@ cudaError_t sampler_launch(const SamplerParams& p, float* work, cudaStream_t s);
 
 // codec 0 INT8 sym, 1 INT4 sym, 2 NF4, 3 INT3 (group % 8 == 0), 4 INT2 asym (offsets used)
 cudaError_t quantize_codec_launch(const void* x, bool bf16, int codec, uint8_t* codes, int code_ld, float* scales,
-                                  float* offsets, int rows, int cols, int group, cudaStream_t s);
+                                  float* offsets, int rows, int cols, int group, float fixed_scale, cudaStream_t s);
+// HQQ refinement (one warp per group, group <= 512): codes [rows, cols] uint8 in [0, levels-1],
+// scales / zeros [rows, cols / group]; x = zero + code * scale.
+cudaError_t hqq_launch(const void* x, bool bf16, uint8_t* codes, float* scales, float* zeros, int rows, int cols,
+                       int group, int levels, float lam, int iters, cudaStream_t s);
+// acc[c] += mean_r |x[r, c]| (AWQ calibration statistics), double accumulator.
+cudaError_t channel_abs_mean_launch(const void* x, bool bf16, double* acc, int rows, int cols, cudaStream_t s);
 cudaError_t quantize_int4_asym_launch(const void* x, bool bf16, uint8_t* packed, float* scales, float* offsets,
                                       int rows, int cols, int group, int n_clip, cudaStream_t s);
 

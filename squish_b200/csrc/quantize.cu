@@ -8,6 +8,7 @@
 // inward clip fraction beta in linspace(0, 0.1, n_clip) that minimises the
 // reconstruction MSE (squish/quant/quantizer.py:500-605).
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -106,7 +107,7 @@ __device__ __forceinline__ float group_absmax(const T* src, int n) {
 template <typename T>
 __global__ void quantize_codec_kernel(const T* __restrict__ x, uint8_t* __restrict__ codes,
                                       float* __restrict__ scales, float* __restrict__ offsets, int rows, int cols,
-                                      int group, int codec, int code_ld) {
+                                      int group, int codec, int code_ld, float fixed_scale) {
   const long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
   const int G = cols / group;
   if (gid >= (long)rows * G) return;
@@ -132,6 +133,21 @@ __global__ void quantize_codec_kernel(const T* __restrict__ x, uint8_t* __restri
       }
       row[(g * group + i) / 4] = byte;
     }
+    return;
+  }
+  if (codec == 5 || codec == 6) {
+    // FP8 (OCP E4M3 / E5M2): s = absmax / largest finite (or one scale for the whole tensor),
+    // codes = cvt.rn.satfinite(x / s)
+    const float fmax = codec == 5 ? 448.f : 57344.f;
+    float sc = fixed_scale;
+    if (!(sc > 0.f)) {
+      const float am = group_absmax(src, group);
+      sc = am == 0.f ? 1.f : am / fmax;
+    }
+    scales[si] = sc;
+    const __nv_fp8_interpretation_t kind = codec == 5 ? __NV_E4M3 : __NV_E5M2;
+    for (int i = 0; i < group; ++i)
+      row[(size_t)g * group + i] = (uint8_t)__nv_cvt_float_to_fp8(to_f(src[i]) / sc, __NV_SATFINITE, kind);
     return;
   }
   const float am = group_absmax(src, group);
@@ -187,17 +203,18 @@ __global__ void quantize_codec_kernel(const T* __restrict__ x, uint8_t* __restri
 }  // namespace
 
 cudaError_t quantize_codec_launch(const void* x, bool bf16, int codec, uint8_t* codes, int code_ld, float* scales,
-                                  float* offsets, int rows, int cols, int group, cudaStream_t s) {
+                                  float* offsets, int rows, int cols, int group, float fixed_scale, cudaStream_t s) {
   const long total = (long)rows * (cols / group);
   if (total == 0) return cudaSuccess;
   const int threads = 128;
   const unsigned blocks = (unsigned)((total + threads - 1) / threads);
   if (bf16)
-    quantize_codec_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), codes,
-                                                                   scales, offsets, rows, cols, group, codec, code_ld);
+    quantize_codec_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x), codes, scales, offsets, rows, cols, group, codec, code_ld,
+        fixed_scale);
   else
     quantize_codec_kernel<float><<<blocks, threads, 0, s>>>(reinterpret_cast<const float*>(x), codes, scales, offsets,
-                                                           rows, cols, group, codec, code_ld);
+                                                           rows, cols, group, codec, code_ld, fixed_scale);
   return cudaGetLastError();
 }
 
@@ -212,6 +229,128 @@ cudaError_t quantize_int4_asym_launch(const void* x, bool bf16, uint8_t* packed,
   else
     quantize_int4_asym_kernel<float><<<blocks, threads, 0, s>>>(reinterpret_cast<const float*>(x), packed, scales,
                                                                 offsets, rows, cols, group, n_clip);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ HQQ
+// Half-quadratic quantization (Badri & Shaji, arXiv:2309.15531), the calibration-free refinement
+// of squish/quant/hqq.py:195-222: from the min/max affine grid (scale = span / qmax, zero = min),
+// `iters` alternating steps of
+//   scale <- (sum q (w - zero) + lambda scale) / (sum q^2 + lambda)
+//   zero  <- mean(w - q scale)
+//   q     <- clamp(rint((w - zero) / max(|scale|, 1e-8)), 0, qmax)
+// One warp per (row, group); a lane holds group/32 values in registers (group <= 512).
+namespace {
+
+constexpr int kHqqPerLane = 16;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) hqq_kernel(const T* __restrict__ x, uint8_t* __restrict__ codes,
+                                                  float* __restrict__ scales, float* __restrict__ zeros, int rows,
+                                                  int cols, int group, float qmax, float lam, int iters) {
+  const long warp = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = cols / group;
+  if (warp >= (long)rows * G) return;  // uniform per warp
+  const int r = (int)(warp / G), g = (int)(warp % G);
+  const T* src = x + (size_t)r * cols + (size_t)g * group;
+  float w[kHqqPerLane], q[kHqqPerLane];
+  float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kHqqPerLane; ++j) {
+    const int i = j * 32 + lane;
+    w[j] = i < group ? to_f(src[i]) : 0.f;
+    if (i < group) {
+      mn = fminf(mn, w[j]);
+      mx = fmaxf(mx, w[j]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  float sc = fmaxf(mx - mn, 1e-6f) / qmax, z = mn;
+#pragma unroll
+  for (int j = 0; j < kHqqPerLane; ++j) q[j] = clampf_d(rintf((w[j] - z) / sc), 0.f, qmax);
+  const float inv_n = 1.f / (float)group;
+  for (int it = 0; it < iters; ++it) {
+    float c2 = 0.f, cw = 0.f;
+#pragma unroll
+    for (int j = 0; j < kHqqPerLane; ++j)
+      if (j * 32 + lane < group) {
+        c2 += q[j] * q[j];
+        cw += q[j] * (w[j] - z);
+      }
+    c2 = warp_sum(c2) + lam;
+    cw = warp_sum(cw) + lam * sc;
+    sc = cw / c2;
+    float rz = 0.f;
+#pragma unroll
+    for (int j = 0; j < kHqqPerLane; ++j)
+      if (j * 32 + lane < group) rz += w[j] - q[j] * sc;
+    z = warp_sum(rz) * inv_n;
+    const float d = fmaxf(fabsf(sc), 1e-8f);
+#pragma unroll
+    for (int j = 0; j < kHqqPerLane; ++j) q[j] = clampf_d(rintf((w[j] - z) / d), 0.f, qmax);
+  }
+  uint8_t* dst = codes + (size_t)r * cols + (size_t)g * group;
+#pragma unroll
+  for (int j = 0; j < kHqqPerLane; ++j)
+    if (j * 32 + lane < group) dst[j * 32 + lane] = (uint8_t)q[j];
+  if (lane == 0) {
+    scales[(size_t)r * G + g] = sc;
+    zeros[(size_t)r * G + g] = z;
+  }
+}
+
+// AWQ calibration statistics (squish/quant/awq.py:239-260): acc[c] += mean over rows of |x[:, c]|.
+// Blocks own 256 columns x a slab of rows; the slab's partial mean is added to acc with one
+// double atomic per column.
+template <typename T>
+__global__ void __launch_bounds__(256) channel_abs_mean_kernel(const T* __restrict__ x, double* __restrict__ acc,
+                                                               int rows, int cols, int rows_per_block) {
+  const int c = blockIdx.x * 256 + threadIdx.x;
+  if (c >= cols) return;
+  const int r0 = blockIdx.y * rows_per_block, r1 = min(rows, r0 + rows_per_block);
+  float s = 0.f;
+  for (int r = r0; r < r1; ++r) s += fabsf(to_f(x[(size_t)r * cols + c]));
+  atomicAdd(acc + c, (double)s / (double)rows);
+}
+
+}  // namespace
+
+cudaError_t hqq_launch(const void* x, bool bf16, uint8_t* codes, float* scales, float* zeros, int rows, int cols,
+                       int group, int levels, float lam, int iters, cudaStream_t s) {
+  if (group > 32 * kHqqPerLane || group <= 0 || cols % group != 0) return cudaErrorInvalidValue;
+  const long warps = (long)rows * (cols / group);
+  if (warps == 0) return cudaSuccess;
+  const unsigned blocks = (unsigned)((warps + 7) / 8);
+  const float qmax = (float)(levels - 1);
+  if (bf16)
+    hqq_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), codes, scales,
+                                                     zeros, rows, cols, group, qmax, lam, iters);
+  else
+    hqq_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), codes, scales, zeros, rows, cols,
+                                             group, qmax, lam, iters);
+  return cudaGetLastError();
+}
+
+cudaError_t channel_abs_mean_launch(const void* x, bool bf16, double* acc, int rows, int cols, cudaStream_t s) {
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  const int rpb = 64;
+  const dim3 grid((cols + 255) / 256, (rows + rpb - 1) / rpb);
+  if (bf16)
+    channel_abs_mean_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), acc, rows,
+                                                                cols, rpb);
+  else
+    channel_abs_mean_kernel<float><<<grid, 256, 0, s>>>(reinterpret_cast<const float*>(x), acc, rows, cols, rpb);
   return cudaGetLastError();
 }
 

@@ -28,6 +28,8 @@
 // Decode shapes (BN <= 64) run two CTAs per SM (small rings), so two independent
 // pipelines hide each other's hand-off latency. Every wait is bounded (sm100.cuh); on
 // timeout *status is set and the kernel still releases its TMEM before exiting.
+#include <cuda_fp8.h>
+#include <cuda_fp16.h>
 #include <cstdio>
 #include <cstdlib>
 
@@ -63,7 +65,7 @@ struct Cfg {
 };
 
 __host__ __device__ constexpr int code_bytes(int wfmt) {
-  return wfmt == WF_INT8                        ? 2 * W_TILE_BYTES
+  return (wfmt == WF_INT8 || wfmt == WF_FP8)    ? 2 * W_TILE_BYTES
          : (wfmt == WF_INT2 || wfmt == WF_AQLM) ? W_TILE_BYTES / 2
          : wfmt == WF_INT3                      ? 3 * W_TILE_BYTES / 4
                                                 : W_TILE_BYTES;
@@ -155,6 +157,20 @@ __device__ __forceinline__ uint4 dq_int8(uint32_t a, uint32_t b, float s) {
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// FP8 E4M3: 8 bytes (column order, little-endian) -> 8 bf16 values * s, two per cvt.
+__device__ __forceinline__ uint4 dq_fp8(uint32_t a, uint32_t b, float s) {
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const uint32_t w = e < 2 ? a : b;
+    const __nv_fp8x2_storage_t pr = (__nv_fp8x2_storage_t)((w >> ((e & 1) * 16)) & 0xFFFFu);
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pr, __NV_E4M3);
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+    o[e] = bf2_bits(__floats2bfloat162_rn(f.x * s, f.y * s));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // INT3: 32 codes u = q + 4 in three words. Pair p < 15 (values 2p, 2p+1) sits in word p / 5 at
 // bits 3*(p%5) and 16 + 3*(p%5); pair 15 is spread over bits 15 (even value) and 31 (odd
 // value) of words 0, 1, 2 (its bits 0, 1, 2).
@@ -196,7 +212,7 @@ __device__ __forceinline__ void dq_other(const uint8_t* tb, int fmt, int r, int 
                                          int n_books, uint4 (&o)[4]) {
   const uint32_t* szt = reinterpret_cast<const uint32_t*>(tb + code_bytes(fmt));
   uint32_t ww[8];
-  if (fmt == WF_INT8) {
+  if (fmt == WF_INT8 || fmt == WF_FP8) {
     const uint4 a = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 32);
     const uint4 b = *reinterpret_cast<const uint4*>(tb + (c * BM + r) * 32 + 16);
     ww[0] = a.x; ww[1] = a.y; ww[2] = a.z; ww[3] = a.w; ww[4] = b.x; ww[5] = b.y; ww[6] = b.z; ww[7] = b.w;
@@ -221,6 +237,7 @@ __device__ __forceinline__ void dq_other(const uint8_t* tb, int fmt, int r, int 
     else if (fmt == WF_AQLM)
       o[w] = dq_aqlm((ww[w >> 1] >> (16 * (w & 1))) & 0xFFFFu, n_books, reinterpret_cast<const uint4*>(lut),
                      __bfloat162bfloat162(sc));
+    else if (fmt == WF_FP8) o[w] = dq_fp8(ww[2 * w], ww[2 * w + 1], __bfloat162float(sc));
     else o[w] = dq_int8(ww[2 * w], ww[2 * w + 1], __bfloat162float(sc));
   }
 }

@@ -17,6 +17,7 @@ enum : int {
   WF_INT3 = 4,  // 3-bit codes q + 4 (q in [-4, 3]), x = zero + q * scale      (3 KiB)
   WF_AQLM = 5,  // per 8 columns one index into each of <= 2 codebooks of 256 x 8 values,
                 // x = scale * sum_k book_k[idx_k]                             (2 KiB)
+  WF_FP8 = 6,   // OCP FP8 E4M3 bytes, x = fp8(q) * scale                       (8 KiB)
 };
 
 struct W4A16Params {

@@ -44,9 +44,42 @@ def _write_tensor(td: Path, name: str, t: QTensor) -> int:
     return n
 
 
+def _awq_ops(cfg, q, names, ck_loader, tokenizer_dir, out: Path, dev, awq_scales: str | None, alpha: float,
+             samples: int, seq_len: int, seed: int, log) -> dict:
+    """Per-tensor AWQ operations: from a scales directory, or calibrated here on the fp32 model
+    (``ck_loader()`` builds it) and saved under ``out/awq``."""
+    from ..quant.awq import (calibration_tokens, collect_activation_scales, load_awq_scales,
+                             prepare_awq_application, save_awq_scales)
+
+    if awq_scales:
+        scales = load_awq_scales(awq_scales)
+        if not scales:
+            raise FileNotFoundError(f"no AWQ scales in {awq_scales}")
+    else:
+        tok = None
+        if tokenizer_dir is not None and ((Path(tokenizer_dir) / "tokenizer.json").exists()):
+            from ..serving.tokenizer import load_tokenizer
+
+            tok = load_tokenizer(str(tokenizer_dir), cfg.vocab_size)
+        toks = calibration_tokens(cfg.vocab_size, samples, seq_len, tokenizer=tok, seed=seed)
+        t0 = time.time()
+        scales = collect_activation_scales(ck_loader(), toks, alpha=alpha, device=dev)
+        save_awq_scales(scales, out / "awq")
+        log(f"  AWQ calibration: {len(toks)} sequences, {len(scales)} layers, {time.time() - t0:.1f}s")
+    ops = prepare_awq_application(scales, names)
+    log(f"  AWQ: scaling {sum(1 for o in ops.values() if o[0] == 'mul')} weights under "
+        f"{sum(1 for o in ops.values() if o[0] == 'div')} norms")
+    return ops
+
+
 def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size: int = 64, mse_clip: bool = False,
              device: str | None = None, delete_source: bool = False, random_preset: str | None = None,
-             seed: int = 0, kv_dtype: str = "int4", log=print) -> dict:
+             seed: int = 0, kv_dtype: str = "int4", log=print, hqq: bool = False, awq: bool = False,
+             awq_scales: str | None = None, awq_alpha: float = 0.5, awq_samples: int = 16,
+             awq_seq_len: int = 256) -> dict:
+    """``hqq``: half-quadratic refinement of INT4 / INT2 grids. ``awq`` (or ``awq_scales``, a
+    directory of saved scales): activation-aware scaling of norm-fed projections before
+    quantization; calibration needs the whole fp32 model in memory once."""
     out = Path(out_dir)
     td = out / "tensors"
     td.mkdir(parents=True, exist_ok=True)
@@ -63,11 +96,21 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
         q.group_size, q.mse_clip, q.kv_dtype = group_size, mse_clip, kv_dtype
         if "random-init" not in done:
             ck = random_checkpoint(cfg, q, seed=seed, device=dev)
+            ops = {}
+            if awq or awq_scales:
+                ops = _awq_ops(cfg, q, list(ck.tensors), lambda: ck, None, out, dev, awq_scales, awq_alpha,
+                               awq_samples, awq_seq_len, seed, log)
             for name, t in ck.tensors.items():
                 if name == "lm_head.weight" and cfg.tie_embeddings:
                     continue
-                if t.kind != "dense" and kind != "q4a":
-                    t = quantize(t.dequantize(), kind, group_size, mse_clip)
+                if name in ops:
+                    from ..quant.awq import apply_op
+
+                    w = apply_op(t.dequantize(), ops[name])
+                    t = (QTensor("dense", t.shape, data=w.cpu()) if t.kind == "dense"
+                         else quantize(w, kind, group_size, mse_clip, hqq=hqq))
+                elif t.kind != "dense" and (kind != "q4a" or hqq):
+                    t = quantize(t.dequantize(), kind, group_size, mse_clip, hqq=hqq)
                 stats["bytes"] += _write_tensor(td, name, t)
                 stats["n_quantized" if t.kind != "dense" else "n_passthrough"] += 1
                 manifest[name] = safe_key(name)
@@ -83,14 +126,39 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
         shards = sorted(p for p in src.glob("*.safetensors"))
         if not shards:
             raise FileNotFoundError(f"no *.safetensors in {src}")
+        ops = {}
+        if awq or awq_scales:
+            names = []
+            for shard in shards:
+                with safe_open(str(shard), "pt", device="cpu") as f:
+                    names += list(f.keys())
+
+            def load_dense():
+                from ..models.weights import Checkpoint
+
+                ckd = Checkpoint(cfg, q)
+                for shard in shards:
+                    with safe_open(str(shard), "pt", device="cpu") as f:
+                        for n in f.keys():
+                            ckd.tensors[n] = QTensor("dense", tuple(f.get_slice(n).get_shape()), data=f.get_tensor(n))
+                if "lm_head.weight" not in ckd.tensors and cfg.tie_embeddings:
+                    ckd.tensors["lm_head.weight"] = ckd.tensors["model.embed_tokens.weight"]
+                return ckd
+
+            ops = _awq_ops(cfg, q, names, load_dense, src, out, dev, awq_scales, awq_alpha, awq_samples,
+                           awq_seq_len, seed, log)
         for i, shard in enumerate(shards):
             if shard.name in done:
                 continue
             with safe_open(str(shard), "pt", device=str(dev) if dev.type == "cuda" else "cpu") as f:
                 for name in f.keys():
                     w = f.get_tensor(name)
+                    if name in ops:
+                        from ..quant.awq import apply_op
+
+                        w = apply_op(w, ops[name])
                     if should_quantize(name, tuple(w.shape)):
-                        t = quantize(w if dev.type == "cuda" else w.float(), kind, group_size, mse_clip)
+                        t = quantize(w if dev.type == "cuda" else w.float(), kind, group_size, mse_clip, hqq=hqq)
                         stats["n_quantized"] += 1
                     else:
                         t = QTensor("dense", tuple(w.shape), data=w.float().cpu())
@@ -115,7 +183,8 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
                                          "delete_source": delete_source}, indent=2))
     (out / "config.json").write_text(json.dumps(to_hf_config(cfg), indent=2))
     q.weight_bits = 16 if kind == "dense" else 4
-    (out / "squish_quant.json").write_text(json.dumps(dict(q.__dict__, weight_kind=kind), indent=2))
+    (out / "squish_quant.json").write_text(json.dumps(dict(q.__dict__, weight_kind=kind, hqq=hqq,
+                                                           awq=bool(awq or awq_scales)), indent=2))
     (td / ".manifest_ready").touch()
     stats["seconds"] = round(time.time() - t0, 2)
     return stats

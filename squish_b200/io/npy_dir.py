@@ -15,6 +15,7 @@ Suffix sets, in the reference loader's dispatch priority (squish/io/loader_utils
     __q2 + __s2 + __z2                  INT2 asymmetric, 4 per byte
     __aqlm_idx + __aqlm_cb              AQLM additive codebooks
     __q + __s                           INT8 symmetric (per row or per group)
+    __f8 + __sf8                        FP8 E4M3 codes + per-group scales (this package's extension)
     __pt                                float16 passthrough
 plus __shape (the original shape) for every tensor. ``.npy.sqe`` files (rANS / Huffman coded,
 io/entropy.py) are always readable; ``.npy.zst`` files when ``zstandard`` is importable.
@@ -35,7 +36,7 @@ import torch
 from ..models.weights import Checkpoint, QTensor
 
 SUFFIXES = ("__nf4", "__s_nf4", "__q4a", "__s4a", "__z4a", "__q4", "__s4", "__q3", "__s3", "__z3", "__lra",
-            "__lrb", "__q2", "__s2", "__z2", "__aqlm_idx", "__aqlm_cb", "__q", "__s", "__pt", "__shape")
+            "__lrb", "__q2", "__s2", "__z2", "__aqlm_idx", "__aqlm_cb", "__f8", "__sf8", "__q", "__s", "__pt", "__shape")
 
 
 def safe_key(name: str) -> str:
@@ -115,6 +116,9 @@ def read_tensor(td: Path, key: str) -> QTensor:
         idx, cb = arr("__aqlm_idx", np.int32), arr("__aqlm_cb", np.float32)
         t = QTensor("aqlm", shape, packed=idx, scales=cb, group=int(cb[2].item()))
         return t
+    if _exists(td, key, "__f8"):
+        q, s = arr("__f8", np.uint8), arr("__sf8", np.float32)
+        return QTensor("fp8", shape or tuple(q.shape), packed=q, scales=s, group=q.shape[1] // s.shape[1])
     if _exists(td, key, "__q"):
         q, s = arr("__q", np.int8), arr("__s", np.float32)
         if s.dim() == 1:
@@ -156,6 +160,8 @@ def tensor_files(name: str, t: QTensor) -> dict[str, np.ndarray]:
         out.update({f"{k}__nf4": np_(t.packed, np.uint8), f"{k}__s_nf4": np_(t.scales, np.float32)})
     elif t.kind == "q8":
         out.update({f"{k}__q": np_(t.packed, np.int8), f"{k}__s": np_(t.scales, np.float32)})
+    elif t.kind == "fp8":
+        out.update({f"{k}__f8": np_(t.packed, np.uint8), f"{k}__sf8": np_(t.scales, np.float32)})
     elif t.kind == "q2":
         out.update({f"{k}__q2": np_(t.packed, np.uint8), f"{k}__s2": np_(t.scales, np.float32),
                     f"{k}__z2": np_(t.offsets, np.float32)})

@@ -111,7 +111,7 @@ class LayerWeights:
 
 
 # stored kinds the GEMM decodes natively (others, and INT3 with a low-rank term, are re-encoded INT4)
-GEMM_KINDS = ("q4a", "nf4", "q8", "q2", "q3", "aqlm")
+GEMM_KINDS = ("q4a", "nf4", "q8", "fp8", "q2", "q3", "aqlm")
 
 
 def _same_kind(parts: list[QTensor], group: int) -> list[QTensor]:

@@ -52,12 +52,20 @@ def _rope(x: torch.Tensor, cs: torch.Tensor) -> torch.Tensor:
 
 
 class ReferenceModel:
-    def __init__(self, ck: Checkpoint):
+    """``device`` places the fp32 weights (CPU by default; a GPU runs calibration forwards).
+    ``tap(name, x)``, when set, sees the input of every norm-fed projection group:
+    ``model.layers.{i}.input_layernorm`` (q/k/v) and ``...post_attention_layernorm``
+    (gate/up, or the router and experts of a MoE layer), x of shape [T, hidden]."""
+
+    tap = None
+
+    def __init__(self, ck: Checkpoint, device: str | torch.device = "cpu"):
         self.cfg: ModelConfig = ck.config
         self.q: QuantConfig = ck.quant
         cfg = self.cfg
-        self.w = {k: v.dequantize().float().cpu() for k, v in ck.tensors.items()}
-        self.cos_sin = rope_table(cfg, min(cfg.max_position, 8192))
+        self.device = torch.device(device)
+        self.w = {k: v.dequantize().float().to(self.device) for k, v in ck.tensors.items()}
+        self.cos_sin = rope_table(cfg, min(cfg.max_position, 8192)).to(self.device)
         self.fk, self.fv = KV_FORMATS[self.q.kv_dtype]
 
     def _kv_roundtrip(self, x: torch.Tensor, fmt: int) -> torch.Tensor:
@@ -65,12 +73,12 @@ class ReferenceModel:
         if fmt == 0:
             return x.to(torch.bfloat16).float()
         t, h, d = x.shape
-        codes, scales = native().cpu.kv_quantize(x.reshape(t * h, d).contiguous(), fmt, self.q.kv_group)
-        return native().cpu.kv_dequantize(codes, scales, fmt, self.q.kv_group, d).reshape(t, h, d)
+        codes, scales = native().cpu.kv_quantize(x.reshape(t * h, d).cpu().contiguous(), fmt, self.q.kv_group)
+        return native().cpu.kv_dequantize(codes, scales, fmt, self.q.kv_group, d).reshape(t, h, d).to(x.device)
 
     def new_cache(self):
-        return [{"k": torch.zeros(0, self.cfg.num_kv_heads, self.cfg.head_dim),
-                 "v": torch.zeros(0, self.cfg.num_kv_heads, self.cfg.head_dim)} for _ in range(self.cfg.num_layers)]
+        z = lambda: torch.zeros(0, self.cfg.num_kv_heads, self.cfg.head_dim, device=self.device)  # noqa: E731
+        return [{"k": z(), "v": z()} for _ in range(self.cfg.num_layers)]
 
     # tensor-parallel hooks (set by the CPU tensor-parallel runner): row-parallel matmul
     # with an all-reduce, and the vocab-parallel LM head with a gather
@@ -114,13 +122,16 @@ class ReferenceModel:
         """Run ``tokens`` at positions start_pos.. (appending to ``cache``); return logits [T, V]."""
         cfg, w = self.cfg, self.w
         t = len(tokens)
-        pos = torch.arange(start_pos, start_pos + t)
+        dev = self.device
+        pos = torch.arange(start_pos, start_pos + t, device=dev)
         cs = self.cos_sin[pos]
-        h = w["model.embed_tokens.weight"][torch.tensor(tokens)]
+        h = w["model.embed_tokens.weight"][torch.tensor(tokens, device=dev)]
         d, hq, hkv = cfg.head_dim, cfg.num_heads, cfg.num_kv_heads
         for i in range(cfg.num_layers):
             p = f"model.layers.{i}."
             x = _rms(h, w[p + "input_layernorm.weight"], cfg.rms_eps)
+            if self.tap is not None:
+                self.tap(p + "input_layernorm", x)
             q = x @ w[p + "self_attn.q_proj.weight"].T
             k = x @ w[p + "self_attn.k_proj.weight"].T
             v = x @ w[p + "self_attn.v_proj.weight"].T
@@ -139,11 +150,13 @@ class ReferenceModel:
             kk = c["k"].repeat_interleave(hq // hkv, dim=1)
             vv = c["v"].repeat_interleave(hq // hkv, dim=1)
             s = torch.einsum("qhd,khd->hqk", q, kk) / math.sqrt(d)
-            kpos = torch.arange(kk.shape[0])
+            kpos = torch.arange(kk.shape[0], device=dev)
             s = s.masked_fill(kpos[None, None, :] > pos[None, :, None], float("-inf"))
             a = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vv).reshape(t, hq * d)
             h = h + a @ w[p + "self_attn.o_proj.weight"].T
             x = _rms(h, w[p + "post_attention_layernorm.weight"], cfg.rms_eps)
+            if self.tap is not None:
+                self.tap(p + "post_attention_layernorm", x)
             h = h + self._mlp(p, x)
         x = _rms(h, w["model.norm.weight"], cfg.rms_eps)
         return x @ w["lm_head.weight"].T

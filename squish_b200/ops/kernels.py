@@ -109,7 +109,7 @@ class Int4Weight:
     k: int
     group: int
     bias: torch.Tensor | None = None
-    fmt: int = 0  # WF_INT4 | WF_NF4 | WF_INT8 | WF_INT2 | WF_INT3 | WF_AQLM
+    fmt: int = 0  # WF_INT4 | WF_NF4 | WF_INT8 | WF_INT2 | WF_INT3 | WF_AQLM | WF_FP8
     codebook: torch.Tensor | None = None  # WF_AQLM: [books, 256, 8] bf16
     # optional resident bf16 expansion [n, 64 * ceil(k / 64)] for large-M GEMMs (the exact
     # values the quantized GEMM computes with); None = expand per call
@@ -132,7 +132,7 @@ def prepare_int4_weight(packed: torch.Tensor, scales: torch.Tensor, offsets: tor
     return Int4Weight(wq=wq, sz=sz, n=int(packed.shape[0]), k=int(k), group=int(group), bias=b)
 
 
-WF_INT4, WF_NF4, WF_INT8, WF_INT2, WF_INT3, WF_AQLM = 0, 1, 2, 3, 4, 5
+WF_INT4, WF_NF4, WF_INT8, WF_INT2, WF_INT3, WF_AQLM, WF_FP8 = 0, 1, 2, 3, 4, 5, 6
 _NIB_POS = (0, 16, 4, 20, 8, 24, 12, 28)  # bit of value j in an 8-value word (pairs share a 16-bit shift)
 
 
@@ -167,7 +167,7 @@ def repack_codes(codes: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor 
         j = torch.arange(16, device=dev)
         pos = (j % 2) * 16 + (j // 2) * 2
         words = (v.reshape(*v.shape[:4], 2, 16) << pos).sum(-1)
-    elif fmt == WF_INT8:
+    elif fmt in (WF_INT8, WF_FP8):
         pos = torch.arange(4, device=dev) * 8
         words = (v.reshape(*v.shape[:4], 8, 4) << pos).sum(-1)
     elif fmt == WF_INT3:
@@ -221,6 +221,9 @@ def prepare_weight(t, device, bias: torch.Tensor | None = None) -> Int4Weight:
     elif t.kind == "q8":
         wt = repack_codes(p.view(torch.uint8), t.scales.to(dev), None, k, t.group, WF_INT8)
         fmt = WF_INT8
+    elif t.kind == "fp8":
+        wt = repack_codes(p.view(torch.uint8), t.scales.to(dev), None, k, t.group, WF_FP8)
+        fmt = WF_FP8
     elif t.kind == "q2":
         codes = torch.stack([(p >> (2 * i)) & 3 for i in range(4)], dim=-1).reshape(p.shape[0], -1)
         wt = repack_codes(codes, t.scales.to(dev), t.offsets.to(dev), k, t.group, WF_INT2)

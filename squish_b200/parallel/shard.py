@@ -29,7 +29,7 @@ from ..models.weights import Checkpoint, QTensor
 def _rows(t: QTensor, r0: int, r1: int) -> QTensor:
     if t.kind == "dense":
         return QTensor("dense", (r1 - r0,) + tuple(t.shape[1:]), data=t.data[r0:r1].contiguous())
-    if t.kind not in ("q4a", "q8", "nf4", "q2", "q3"):
+    if t.kind not in ("q4a", "q8", "fp8", "nf4", "q2", "q3"):
         t = _to_q4a(t)
     return dataclasses.replace(t, shape=(r1 - r0, t.shape[1]), packed=t.packed[r0:r1].contiguous(),
                                scales=t.scales[r0:r1].contiguous(),

@@ -23,6 +23,8 @@ def dequantize_qtensor(t: QTensor) -> torch.Tensor:
         return C.dequantize_nf4(t.packed.cpu(), t.scales.cpu().float(), t.group)
     if k == "q8":
         return C.dequantize_int8(t.packed.cpu(), t.scales.cpu().float())
+    if k == "fp8":
+        return C.dequantize_fp8(t.packed.cpu().contiguous(), t.scales.cpu().float().contiguous(), 0)
     if k == "q2":
         return C.dequantize_int2(t.packed.cpu(), t.scales.cpu().float(), t.offsets.cpu().float(), t.group)
     if k == "q3":
@@ -40,14 +42,53 @@ def dequantize_qtensor(t: QTensor) -> torch.Tensor:
     raise ValueError(f"unknown tensor kind {k!r}")
 
 
-_GPU_CODEC = {"q8": 0, "nf4": 2, "q3": 3, "q2": 4}
+_GPU_CODEC = {"q8": 0, "nf4": 2, "q3": 3, "q2": 4, "fp8": 5}
+_FP8 = {"e4m3": (0, 5, 448.0), "e5m2": (1, 6, 57344.0)}
 
 
-def quantize(w: torch.Tensor, kind: str, group: int, mse_clip: bool = False) -> QTensor:
-    """Quantize a 2-D weight to ``kind`` (q4a | q8 | nf4 | q2 | q3 | aqlm | dense)."""
+def quantize_fp8(w: torch.Tensor, fmt: str = "e4m3", group: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """FP8 codes (uint8) and fp32 scales of a 2-D tensor: one scale for the whole tensor
+    (``group=0``: absmax / largest finite, the reference's quantize_fp8_e4m3_f32 /
+    quantize_fp8_e5m2_f32, squish_quant_rs/src/lib.rs:1012-1091) or one per ``group`` columns.
+    Codes round to nearest even and saturate (the hardware cvt.rn.satfinite conversion); CUDA
+    tensors are encoded by the GPU kernel, others by the C++ CPU library, bit-identically."""
+    cpu_fmt, codec, fmax = _FP8[fmt]
+    x = w.detach()
+    fixed = 0.0
+    g = group if group > 0 else x.shape[1]
+    if group <= 0:
+        am = float(x.abs().max()) if x.numel() else 0.0
+        fixed = 1.0 if am == 0.0 else am / fmax
+    if x.is_cuda:
+        x = x if x.dtype in (torch.float32, torch.bfloat16) else x.float()
+        return tuple(native().quantize_codec(x.contiguous(), codec, g, fixed))
+    return tuple(native().cpu.quantize_fp8(x.float().contiguous(), cpu_fmt, g, fixed))
+
+
+def dequantize_fp8(codes: torch.Tensor, scales: torch.Tensor, fmt: str = "e4m3") -> torch.Tensor:
+    """fp32 reconstruction of :func:`quantize_fp8` output (on the CPU)."""
+    sc = scales.float().cpu()
+    if sc.dim() < 2:
+        sc = sc.reshape(1, 1).expand(codes.shape[0], 1)
+    return native().cpu.dequantize_fp8(codes.cpu().contiguous(), sc.contiguous(), _FP8[fmt][0])
+
+
+def quantize(w: torch.Tensor, kind: str, group: int, mse_clip: bool = False, hqq: bool = False,
+             hqq_iters: int = 10) -> QTensor:
+    """Quantize a 2-D weight to ``kind`` (q4a | q8 | fp8 | nf4 | q2 | q3 | aqlm | dense).
+    ``hqq``: refine the INT4 / INT2 affine grids by half-quadratic quantization (quant/hqq.py)."""
     from ..models.weights import pick_group, quantize_q4a
 
     C = native().cpu
+    if hqq and kind in ("q4a", "q2"):
+        from .hqq import HQQConfig, HQQTensor, hqq_quantize
+
+        g = pick_group(w.shape[1], group)
+        lv = 16 if kind == "q4a" else 4
+        codes, sc, z = hqq_quantize(w.detach() if w.is_cuda else w.detach().float(), g, lv, 1.0, hqq_iters)
+        ht = HQQTensor(codes.cpu().numpy(), sc.float().cpu().numpy(), z.float().cpu().numpy(), tuple(w.shape),
+                       HQQConfig(bits=4 if kind == "q4a" else 2, group_size=g, max_iter=hqq_iters))
+        return ht.to_qtensor(kind)
     if kind == "q4a":
         return quantize_q4a(w, group, mse_clip)
     if kind == "dense":
@@ -56,7 +97,7 @@ def quantize(w: torch.Tensor, kind: str, group: int, mse_clip: bool = False) -> 
     if w.is_cuda and kind in _GPU_CODEC:
         # the GPU quantizers (csrc/quantize.cu) produce the CPU library's layouts bit for bit
         out = native().quantize_codec(w.detach().contiguous() if w.dtype in (torch.float32, torch.bfloat16)
-                                      else w.detach().float().contiguous(), _GPU_CODEC[kind], g)
+                                      else w.detach().float().contiguous(), _GPU_CODEC[kind], g, 0.0)
         out = [t.cpu() for t in out]
         if kind == "q2":
             return QTensor("q2", tuple(w.shape), packed=out[0], scales=out[1], offsets=out[2], group=g)
@@ -65,6 +106,9 @@ def quantize(w: torch.Tensor, kind: str, group: int, mse_clip: bool = False) -> 
     if kind == "q8":
         q, s = C.quantize_int8(wf, g)
         return QTensor("q8", tuple(wf.shape), packed=q, scales=s, group=g)
+    if kind == "fp8":
+        q, s = C.quantize_fp8(wf, 0, g, 0.0)
+        return QTensor("fp8", tuple(wf.shape), packed=q, scales=s, group=g)
     if kind == "nf4":
         p, s = C.quantize_nf4(wf, g)
         return QTensor("nf4", tuple(wf.shape), packed=p, scales=s, group=g)

@@ -1,0 +1,272 @@
+"""FP8 codec, HQQ, AWQ and model merging on the CPU.
+
+FP8 codes are checked against torch's own float8 casts (round to nearest even); HQQ against
+an independent float64 NumPy restatement of the half-quadratic updates; AWQ by the identity it
+must preserve (fp32 logits unchanged by scaling) and by lower quantization error on a model
+with salient activation channels; merging against the operations written out directly."""
+import dataclasses
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from squish_b200._ext import native
+from squish_b200.models.config import get_preset
+from squish_b200.models.reference import ReferenceModel
+from squish_b200.models.weights import Checkpoint, QTensor, random_checkpoint
+
+
+# ------------------------------------------------------------------------------- FP8
+@pytest.mark.parametrize("fmt,dt", [("e4m3", torch.float8_e4m3fn), ("e5m2", torch.float8_e5m2)])
+@pytest.mark.parametrize("group", [0, 64])
+def test_fp8_codes_match_torch_casts(fmt, dt, group):
+    from squish_b200.quant.codecs import dequantize_fp8, quantize_fp8
+
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(32, 256, generator=g) * torch.logspace(-7, 2, 256)[None, :]
+    codes, s = quantize_fp8(x, fmt, group)
+    gs = x.shape[1] if group == 0 else group
+    want = (x / s.repeat_interleave(gs, 1)).to(dt).view(torch.uint8)
+    assert torch.equal(codes, want)
+    back = dequantize_fp8(codes, s, fmt)
+    assert torch.equal(back, want.view(dt).float() * s.repeat_interleave(gs, 1))
+    rel = ((back - x).norm() / x.norm()).item()
+    assert rel < (0.04 if fmt == "e4m3" else 0.08)
+
+
+def test_fp8_saturates_and_keeps_subnormals():
+    C = native().cpu
+    v = torch.tensor([[0.0, -0.0, 2.0 ** -9, 3 * 2.0 ** -10, 448.0, 470.0, 1e9, -1e9]])
+    codes, _ = C.quantize_fp8(v, 0, 8, 1.0)
+    assert codes.tolist() == [[0, 128, 1, 2, 126, 126, 126, 254]]
+    codes, _ = C.quantize_fp8(torch.tensor([[57344.0, 1e9, 2.0 ** -16, 2.0 ** -17]]), 1, 4, 1.0)
+    assert codes.tolist() == [[0x7B, 0x7B, 1, 0]]
+
+
+def test_fp8_weight_kind_roundtrips_npy_dir(tmp_path):
+    from squish_b200.io.npy_dir import read_tensor, tensor_files
+    from squish_b200.quant.codecs import quantize
+
+    w = torch.randn(64, 128) * 0.05
+    t = quantize(w, "fp8", 32)
+    assert t.kind == "fp8" and t.packed.dtype == torch.uint8 and t.scales.shape == (64, 4)
+    for key, a in tensor_files("m.w", t).items():
+        np.save(str(tmp_path / f"{key}.npy"), a)
+    r = read_tensor(tmp_path, "m__w")
+    assert r.kind == "fp8" and r.group == 32
+    torch.testing.assert_close(r.dequantize(), t.dequantize())
+    assert ((t.dequantize() - w).norm() / w.norm()).item() < 0.04
+
+
+def test_fp8_repack_layout_is_int8_layout():
+    from squish_b200.ops import kernels as K
+
+    codes = torch.randint(0, 256, (128, 64), dtype=torch.uint8)
+    s = torch.rand(128, 1) + 0.5
+    assert torch.equal(K.repack_codes(codes, s, None, 64, 64, K.WF_FP8),
+                       K.repack_codes(codes, s, None, 64, 64, K.WF_INT8))
+
+
+# ------------------------------------------------------------------------------- HQQ
+def _hqq_numpy(w, group, levels, lam, iters):
+    wg = w.astype(np.float64).reshape(w.shape[0], -1, group)
+    qmax = levels - 1
+    mn, mx = wg.min(-1, keepdims=True), wg.max(-1, keepdims=True)
+    s = np.maximum(mx - mn, 1e-6) / qmax
+    z = mn
+    q = np.clip(np.round((wg - z) / s), 0, qmax)
+    for _ in range(iters):
+        s = ((q * (wg - z)).sum(-1, keepdims=True) + lam * s) / ((q ** 2).sum(-1, keepdims=True) + lam)
+        z = (wg - q * s).mean(-1, keepdims=True)
+        q = np.clip(np.round((wg - z) / np.maximum(np.abs(s), 1e-8)), 0, qmax)
+    return q.reshape(w.shape), s[..., 0], z[..., 0]
+
+
+@pytest.mark.parametrize("bits,group", [(4, 64), (2, 32), (2.5, 64), (3.5, 128)])
+def test_hqq_torch_matches_numpy_restatement(bits, group):
+    from squish_b200.quant.hqq import grid_levels, hqq_torch
+
+    w = np.random.default_rng(int(bits * 10)).normal(0, 0.02, (64, 512)).astype(np.float32)
+    lv = grid_levels(bits)
+    q, s, z = hqq_torch(torch.from_numpy(w), group, lv, 1.0, 10)
+    qn, sn, zn = _hqq_numpy(w, group, lv, 1.0, 10)
+    assert (q.numpy() != qn).mean() < 2e-3
+    np.testing.assert_allclose(s.numpy(), sn, rtol=1e-3, atol=1e-7)
+    np.testing.assert_allclose(z.numpy(), zn, rtol=1e-3, atol=1e-6)
+
+
+def test_hqq_quantizer_interface_and_q4a_form():
+    from squish_b200.quant.hqq import HQQConfig, HQQQuantizer
+
+    w = np.random.default_rng(0).normal(0, 0.02, (48, 200)).astype(np.float32)  # 200: last group padded
+    qz = HQQQuantizer(HQQConfig(bits=4, group_size=64))
+    t = qz.encode(w)
+    assert t.codes.shape == w.shape and t.scale.shape == (48, 4) and t.codes.max() <= 15
+    w_hat = qz.decode(t)
+    assert qz.relative_error(w, w_hat) < 0.12 and qz.quantisation_error_db(w, w_hat) > 18
+    # column-wise groups
+    tc = HQQQuantizer(HQQConfig(bits=3, group_size=16, axis=1)).encode(w)
+    assert tc.codes.shape == w.shape and tc.scale.shape == (200, 3)
+    # the served form decodes to the same weights
+    w2 = w[:, :192]
+    t2 = qz.encode(w2)
+    torch.testing.assert_close(t2.to_qtensor("q4a").dequantize(), torch.from_numpy(qz.decode(t2)),
+                               rtol=1e-5, atol=1e-6)
+    with pytest.raises(ValueError):
+        HQQConfig(bits=9)
+
+
+def test_hqq_refinement_beats_minmax_grid():
+    from squish_b200.quant.codecs import quantize
+
+    w = torch.from_numpy(np.random.default_rng(1).standard_t(4, (128, 512)).astype(np.float32)) * 0.02
+    e_plain = (quantize(w, "q4a", 64).dequantize() - w).norm()
+    e_hqq = (quantize(w, "q4a", 64, hqq=True).dequantize() - w).norm()
+    assert e_hqq < e_plain
+    t2 = quantize(w, "q2", 64, hqq=True)
+    assert t2.kind == "q2" and t2.packed.shape == (128, 128)
+
+
+# ------------------------------------------------------------------------------- AWQ
+def _tiny(moe=False):
+    cfg, q = get_preset("tiny-moe" if moe else "tiny-llama")
+    return cfg, q
+
+
+def _dense_ck(cfg, q, seed=0, salient=False):
+    ck = random_checkpoint(cfg, q, seed=seed)
+    out = Checkpoint(cfg, q)
+    g = torch.Generator().manual_seed(seed + 1)
+    for n, t in ck.tensors.items():
+        w = t.dequantize().float()
+        if w.dim() == 2:  # off any quantization grid
+            w = torch.randn(w.shape, generator=g) * 0.02
+        if salient and n.endswith("layernorm.weight"):
+            w = torch.ones_like(w)
+            w[torch.randperm(w.numel(), generator=g)[: w.numel() // 32]] = 12.0  # a few salient channels
+        out.tensors[n] = QTensor("dense", tuple(w.shape), data=w)
+    return out
+
+
+@pytest.mark.parametrize("moe", [False, True])
+def test_awq_scaling_preserves_fp32_model(moe):
+    from squish_b200.quant.awq import apply_awq_to_weights, calibration_tokens, collect_activation_scales
+
+    cfg, q = _tiny(moe)
+    q = dataclasses.replace(q, kv_dtype="bf16")
+    ck = _dense_ck(cfg, q)
+    toks = calibration_tokens(cfg.vocab_size, 2, 24, seed=0)
+    scales = collect_activation_scales(ck, toks, alpha=0.5, device="cpu")
+    assert len(scales) == 5 * cfg.num_layers
+    w = {n: t.data.clone() for n, t in ck.tensors.items()}
+    apply_awq_to_weights(w, scales)
+    ck2 = Checkpoint(cfg, q, {n: QTensor("dense", tuple(v.shape), data=v) for n, v in w.items()})
+    changed = [n for n in w if not torch.equal(w[n], ck.tensors[n].data)]
+    assert any("q_proj" in n for n in changed) and any("input_layernorm" in n for n in changed)
+    assert not any("o_proj" in n or "down_proj" in n for n in changed)
+    if moe:
+        assert any(n.endswith("mlp.gate.weight") for n in changed)
+    prompt = list(range(3, 19))
+    a = ReferenceModel(ck).forward(prompt, ReferenceModel(ck).new_cache(), 0)
+    m2 = ReferenceModel(ck2)
+    b = m2.forward(prompt, m2.new_cache(), 0)
+    torch.testing.assert_close(a, b, rtol=1e-3, atol=5e-4)
+
+
+def test_awq_reduces_int4_error_with_salient_channels():
+    from squish_b200.quant.awq import apply_awq_to_weights, calibration_tokens, collect_activation_scales
+    from squish_b200.quant.codecs import quantize
+
+    cfg, q = _tiny()
+    q = dataclasses.replace(q, kv_dtype="bf16")
+    ck = _dense_ck(cfg, q, seed=4, salient=True)
+    toks = calibration_tokens(cfg.vocab_size, 4, 32, seed=2)
+    scales = collect_activation_scales(ck, toks, alpha=0.5, device="cpu")
+
+    def quantized(wd):
+        return Checkpoint(cfg, q, {n: (quantize(v, "q4a", 32) if v.dim() == 2 and "embed" not in n
+                                       and "norm" not in n else QTensor("dense", tuple(v.shape), data=v))
+                                   for n, v in wd.items()})
+
+    base = {n: t.data.clone() for n, t in ck.tensors.items()}
+    scaled = apply_awq_to_weights({n: v.clone() for n, v in base.items()}, scales)
+    prompt = toks[3][:24]
+    ref = ReferenceModel(ck)
+    want = ref.forward(prompt, ref.new_cache(), 0)
+    errs = []
+    for wd in (base, scaled):
+        m = ReferenceModel(quantized(wd))
+        errs.append((m.forward(prompt, m.new_cache(), 0) - want).norm().item())
+    assert errs[1] < errs[0], errs
+
+
+def test_awq_scale_files_roundtrip(tmp_path):
+    from squish_b200.quant.awq import load_awq_scales, save_awq_scales
+
+    sc = {"model.layers.0.self_attn.q_proj": np.arange(4, dtype=np.float32) + 1}
+    save_awq_scales(sc, tmp_path)
+    assert (tmp_path / ".awq_ready").exists()
+    assert json.loads((tmp_path / "awq_index.json").read_text()) == {
+        "model.layers.0.self_attn.q_proj": "model__layers__0__self_attn__q_proj.awq.npy"}
+    got = load_awq_scales(tmp_path)
+    np.testing.assert_array_equal(got["model.layers.0.self_attn.q_proj"], sc["model.layers.0.self_attn.q_proj"])
+
+
+def test_compress_with_awq_and_hqq(tmp_path):
+    from squish_b200.io.convert import compress, load_checkpoint
+
+    st = compress(None, str(tmp_path / "m"), random_preset="tiny-llama", device="cpu", awq=True, hqq=True,
+                  awq_samples=2, awq_seq_len=16, log=lambda *_: None)
+    assert st["n_quantized"] > 0
+    assert (tmp_path / "m" / "awq" / ".awq_ready").exists()
+    meta = json.loads((tmp_path / "m" / "squish_quant.json").read_text())
+    assert meta["awq"] and meta["hqq"]
+    ck, _ = load_checkpoint(str(tmp_path / "m"), "cpu")
+    m = ReferenceModel(ck)
+    out = m.forward([1, 2, 3], m.new_cache(), 0)
+    assert torch.isfinite(out).all()
+    # the saved scales apply again from the directory
+    st2 = compress(None, str(tmp_path / "m2"), random_preset="tiny-llama", device="cpu",
+                   awq_scales=str(tmp_path / "m" / "awq"), log=lambda *_: None)
+    assert st2["n_quantized"] == st["n_quantized"]
+
+
+# ------------------------------------------------------------------------------- merging
+def test_slerp_dare_ties():
+    from squish_b200.quant.merge import dare, slerp, ties
+
+    a, b = torch.tensor([1.0, 0.0]), torch.tensor([0.0, 1.0])
+    m = slerp(a, b, 0.5)
+    torch.testing.assert_close(m, torch.tensor([2 ** -0.5, 2 ** -0.5]))
+    torch.testing.assert_close(slerp(a, 2 * a, 0.25), a * 1.25)  # parallel: plain lerp
+    base, delta = torch.zeros(20000), torch.ones(20000)
+    o = dare(base, delta, 0.25, seed=3)
+    kept = o != 0
+    assert abs(kept.float().mean().item() - 0.25) < 0.02
+    assert torch.allclose(o[kept], torch.full_like(o[kept], 4.0))
+    assert torch.equal(o, dare(base, delta, 0.25, seed=3)) and not torch.equal(o, dare(base, delta, 0.25, seed=4))
+    d = torch.tensor([[0.5, -0.1, 0.3, 0.0], [0.4, 0.2, -0.6, 0.01]])
+    out = ties(torch.zeros(4), d, trim_fraction=0.25, t=1.0)
+    # per-row threshold = the sorted |d| at index ceil(4 * 0.25) = 1: row0 0.1, row1 0.2
+    # col0: both +, mean 0.45; col1: -0.1 | +0.2 -> sign sum 0 -> no agreement; col2: +0.3, -0.6 -> 0;
+    # col3: 0.0 trimmed, 0.01 trimmed -> 0
+    torch.testing.assert_close(out, torch.tensor([0.45, 0.0, 0.0, 0.0]))
+
+
+def test_merge_model_cli(tmp_path):
+    from safetensors.torch import load_file, save_file
+
+    from squish_b200.cli import main
+
+    for i, sgn in enumerate((1.0, -1.0)):
+        d = tmp_path / f"ad{i}"
+        d.mkdir()
+        save_file({"w": sgn * torch.ones(64, 64), "b": torch.full((8,), float(i + 1))},
+                  str(d / "adapter_model.safetensors"))
+    rc = main(["merge-model", "base", "--adapters", f"a:{tmp_path / 'ad0'}", f"b:{tmp_path / 'ad1'}",
+               "--method", "ties", "--output-path", str(tmp_path / "out")])
+    assert rc == 0
+    m = load_file(str(tmp_path / "out" / "adapter_model.safetensors"))
+    torch.testing.assert_close(m["b"], torch.full((8,), 1.5))
+    assert m["w"].abs().max().item() <= 1.0

@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("kind,group", [("nf4", 64), ("nf4", 32), ("q8", 64), ("q8", 32), ("q2", 64), ("q2", 128),
-                                        ("q3", 64), ("q3", 32), ("aqlm", 8)])
+                                        ("q3", 64), ("q3", 32), ("aqlm", 8), ("fp8", 64), ("fp8", 32)])
 @pytest.mark.parametrize("m", [1, 37, 64, 300])
 def test_gemm_formats_match_fp32(cuda, kind, group, m):
     g = torch.Generator().manual_seed(m + group)
@@ -42,7 +42,7 @@ def test_tensor_op_repack_equals_cuda_int4_repack(cuda):
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("kind", ["nf4", "q8", "q2", "q3", "aqlm"])
+@pytest.mark.parametrize("kind", ["nf4", "q8", "q2", "q3", "aqlm", "fp8"])
 def test_engine_with_format_weights_matches_oracle(cuda, kind):
     from squish_b200.engine.engine import EngineConfig, LLMEngine
     from squish_b200.engine.sampling import SamplingParams
@@ -74,7 +74,7 @@ def test_engine_with_format_weights_matches_oracle(cuda, kind):
     ok, worst = _teacher_forced_ok(ref, prompt, out)
     assert ok, (worst, out)
     assert eng.runner.layers[0].o.fmt == {"nf4": K.WF_NF4, "q8": K.WF_INT8, "q2": K.WF_INT2, "q3": K.WF_INT3,
-                                          "aqlm": K.WF_AQLM}[kind]
+                                          "aqlm": K.WF_AQLM, "fp8": K.WF_FP8}[kind]
 
 
 @pytest.mark.parametrize("codec,group", [(0, 64), (0, 0), (1, 32), (2, 64), (3, 32), (4, 64)])
@@ -107,3 +107,63 @@ def test_gpu_quantizers_match_cpu_library(codec, group, dtype):
             # codes: identical except where a value sits on a rounding boundary (fused multiply-add
             # contraction can differ between the compilers); allow a few
             assert (a != b).float().mean().item() < 1e-3
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+@pytest.mark.parametrize("group", [0, 64])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gpu_fp8_codec_matches_cpu_library(fmt, group, dtype):
+    """The GPU FP8 encoder (hardware cvt.rn.satfinite) and the C++ software encoder agree bit
+    for bit, per group and per tensor."""
+    from squish_b200.quant.codecs import quantize_fp8
+
+    g = torch.Generator().manual_seed(group + len(fmt))
+    x = (torch.randn(64, 512, generator=g) * torch.logspace(-5, 1, 512)[None, :]).to(dtype)
+    cg, sg = quantize_fp8(x.cuda(), fmt, group)
+    cc, sc = quantize_fp8(x.float(), fmt, group)
+    torch.testing.assert_close(sg.cpu(), sc, rtol=1e-6, atol=0)
+    assert torch.equal(cg.cpu(), cc)
+
+
+@pytest.mark.parametrize("levels,group", [(16, 64), (4, 128), (6, 32), (256, 512)])
+def test_hqq_kernel_matches_torch(levels, group):
+    """The one-warp-per-group HQQ kernel against the torch restatement (fp32 sums in another
+    order: scales agree to 1e-4, codes except on rounding boundaries)."""
+    from squish_b200.quant.hqq import hqq_quantize, hqq_torch
+
+    g = torch.Generator().manual_seed(levels + group)
+    w = torch.randn(128, 1024, generator=g) * 0.02
+    c1, s1, z1 = hqq_quantize(w.cuda(), group, levels, 1.0, 10)
+    c2, s2, z2 = hqq_torch(w, group, levels, 1.0, 10)
+    torch.testing.assert_close(s1.cpu(), s2, rtol=1e-3, atol=1e-6)
+    torch.testing.assert_close(z1.cpu(), z2, rtol=1e-3, atol=1e-5)
+    assert (c1.cpu() != c2).float().mean().item() < 2e-3
+
+
+def test_channel_abs_mean_kernel():
+    from squish_b200._ext import native
+
+    g = torch.Generator().manual_seed(1)
+    acc = torch.zeros(896, dtype=torch.float64, device="cuda")
+    xs = [torch.randn(n, 896, generator=g) * torch.linspace(0.1, 5, 896) for n in (1, 70, 300)]
+    for x in xs:
+        native().channel_abs_mean(x.cuda(), acc)
+        native().channel_abs_mean(x.to(torch.bfloat16).cuda(), acc)
+    want = sum(x.abs().mean(0).double() + x.to(torch.bfloat16).float().abs().mean(0).double() for x in xs)
+    torch.testing.assert_close(acc.cpu(), want, rtol=1e-5, atol=1e-6)
+
+
+def test_awq_calibration_on_gpu_matches_cpu():
+    """AWQ statistics collected by the GPU forward (channel kernel) equal the CPU forward's."""
+    from squish_b200.models.config import get_preset
+    from squish_b200.models.weights import random_checkpoint
+    from squish_b200.quant.awq import calibration_tokens, collect_activation_scales
+
+    cfg, q = get_preset("tiny-llama")
+    ck = random_checkpoint(cfg, q, seed=3)
+    toks = calibration_tokens(cfg.vocab_size, 3, 40, seed=1)
+    a = collect_activation_scales(ck, toks, device="cuda")
+    b = collect_activation_scales(ck, toks, device="cpu")
+    assert a.keys() == b.keys() and len(a) == 5 * cfg.num_layers
+    for k in a:
+        np.testing.assert_allclose(a[k], b[k], rtol=1e-4, atol=1e-6)
