@@ -14,7 +14,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("squish_b200", "csrc")
 
 cuda_sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-cpp_sources = [os.path.join(CSRC, "bindings.cpp"), os.path.join(CSRC, "cpu_ref.cpp"), os.path.join(CSRC, "entropy.cpp")]
+cpp_sources = [os.path.join(CSRC, "bindings.cpp"), os.path.join(CSRC, "cpu_ref.cpp"), os.path.join(CSRC, "entropy.cpp"),
+               os.path.join(CSRC, "host_utils.cpp")]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -29,6 +30,7 @@ setup(
     name="squish_b200",
     version="0.1.0",
     packages=find_packages(include=["squish_b200", "squish_b200.*"]),
+    package_data={"squish_b200.serving": ["static/*.html"]},
     entry_points={"console_scripts": ["squish=squish_b200.cli:main"]},
     ext_modules=[
         CUDAExtension(

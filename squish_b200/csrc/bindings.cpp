@@ -839,6 +839,10 @@ std::vector<torch::Tensor> quantize_int4_asym_cuda(torch::Tensor x, int64_t grou
 
 }  // namespace
 
+namespace sqhost {
+void register_host(pybind11::module& m);  // host_utils.cpp
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "squish_b200 native kernels (sm_100a CUDA + C++ CPU reference)";
   m.def("repack_int4", &repack_int4);
@@ -874,4 +878,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("hqq", &hqq_cuda);
   m.def("channel_abs_mean", &channel_abs_mean_cuda);
   sqcpu::register_cpu(m);
+  sqhost::register_host(m);
 }

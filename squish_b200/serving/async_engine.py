@@ -48,7 +48,10 @@ class _Sink:
 
 
 class AsyncEngine:
-    def __init__(self, engine, tokenizer=None, max_pending: int = 256, model_name: str = "model"):
+    def __init__(self, engine, tokenizer=None, max_pending: int = 256, model_name: str = "model",
+                 loop_guard: bool = True):
+        from .quality_monitor import QualityMonitor
+
         self.engine = engine
         self.tokenizer = tokenizer
         self.model_name = model_name
@@ -70,6 +73,10 @@ class AsyncEngine:
         self._t_first: dict[str, float] = {}
         self._t_submit: dict[str, float] = {}
         self.last_error: str | None = None
+        self.loop_guard = loop_guard
+        self._guards: dict = {}
+        self.loops_stopped = 0
+        self.quality = QualityMonitor()
         from ..utils.fault import Watchdog
 
         self.watchdog = Watchdog(lambda: bool(self._sinks))
@@ -158,6 +165,9 @@ class AsyncEngine:
                         sink.put(GenEvent([], True, f"error: {exc}", len(prompt), 0))
             elif op == "abort":
                 eng.abort(rid)
+                self._guards.pop(rid, None)
+                self._t_submit.pop(rid, None)
+                self._t_first.pop(rid, None)
                 sink = self._sinks.pop(rid, None)
                 if sink is not None:
                     sink.put(GenEvent([], True, "abort", 0, 0))
@@ -181,6 +191,11 @@ class AsyncEngine:
                 for rid in list(self._sinks):
                     eng.abort(rid)
                     self._sinks.pop(rid).put(GenEvent([], True, "error", 0, 0))
+                    t0 = self._t_submit.pop(rid, time.perf_counter())
+                    self._t_first.pop(rid, None)
+                    self._guards.pop(rid, None)
+                    self.quality.record_request(self.model_name, time.perf_counter() - t0, None, 0, False,
+                                                type(exc).__name__)
                 continue
             now = time.perf_counter()
             for o in outs:
@@ -190,14 +205,26 @@ class AsyncEngine:
                     self._t_first[o.rid] = now
                 if sink is None:
                     continue
-                sink.put(GenEvent(o.new_tokens, o.finished, o.finish_reason, o.num_prompt_tokens,
-                                  o.num_output_tokens))
-                if o.finished:
+                finished, reason = o.finished, o.finish_reason
+                if self.loop_guard and not finished:
+                    g = self._guards.get(o.rid)
+                    if g is None:
+                        from .loop_guard import LoopGuard
+
+                        g = self._guards[o.rid] = LoopGuard()
+                    if g.feed(o.new_tokens):
+                        eng.abort(o.rid)  # verbatim loop: stop with finish reason "repetition"
+                        finished, reason = True, "repetition"
+                        self.loops_stopped += 1
+                sink.put(GenEvent(o.new_tokens, finished, reason, o.num_prompt_tokens, o.num_output_tokens))
+                if finished:
                     self._sinks.pop(o.rid, None)
+                    self._guards.pop(o.rid, None)
                     t0 = self._t_submit.pop(o.rid, now)
                     t1 = self._t_first.pop(o.rid, now)
                     dec = max(now - t1, 1e-6)
                     self.recent.append((max(o.num_output_tokens - 1, 0) / dec, t1 - t0))
+                    self.quality.record_request(self.model_name, now - t0, t1 - t0, o.num_output_tokens)
                     eng.requests.pop(o.rid, None)
 
     # ------------------------------------------------------------------ stats

@@ -100,7 +100,7 @@ def mount_ollama(app: FastAPI, st) -> None:
             if hit:
                 break
             if ev.finished:
-                reason = "length" if ev.reason == "length" else "stop"
+                reason = ev.reason if ev.reason in ("length", "repetition") else "stop"
                 break
         yield "", True, reason, n_out, t_first
 

@@ -20,7 +20,7 @@ from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
 from ..engine.sampling import SamplingParams
 from ..utils import telemetry
-from .async_engine import AsyncEngine, QueueFullError
+from .async_engine import AsyncEngine, GenEvent, QueueFullError
 from .chat_template import apply_chat_template
 from .tokenizer import IncrementalDetokenizer
 from .tool_calling import ToolCallStreamFilter, parse_tool_calls
@@ -31,8 +31,11 @@ VERSION = "0.1.0"
 
 class ServerState:
     def __init__(self, aeng: AsyncEngine, model_name: str, api_key: str | None = None, arch: str = "qwen2",
-                 governor=None, load_time_s: float = 0.0):
+                 governor=None, load_time_s: float = 0.0, response_cache: int = 256):
+        from .response_cache import ResponseCache
+
         self.aeng = aeng
+        self.cache = ResponseCache(response_cache)
         self.model_name = model_name
         self.api_key = api_key
         self.arch = arch
@@ -95,8 +98,22 @@ def _truncate_at_stop(text: str, stops: list[str]) -> tuple[str, bool]:
     return (text[:cut], True) if cut >= 0 else (text, False)
 
 
+def _finish_reason(ev_reason: str | None) -> str:
+    return ev_reason if ev_reason in ("length", "repetition") else "stop"
+
+
+def _cache_key(st: ServerState, prompt_ids, params, stops) -> str | None:
+    return st.cache.key(prompt_ids, params, repr(stops)) if st.cache.maxsize > 0 and st.cache.eligible(params) \
+        else None
+
+
 async def _run_one(st: ServerState, prompt_ids: list[int], params: SamplingParams, stops: list[str]):
-    """Collect one request; returns (text, token ids, finish_reason, prompt_tokens)."""
+    """Collect one request; returns (text, token ids, finish_reason, prompt_tokens). Greedy
+    requests seen before are answered from the response cache."""
+    key = _cache_key(st, prompt_ids, params, stops)
+    if key is not None and (hit := st.cache.get(key)) is not None:
+        text, ids, reason = hit
+        return text, list(ids), reason, len(prompt_ids)
     detok = IncrementalDetokenizer(st.tok)
     text, ids, reason, ptoks = "", [], "stop", len(prompt_ids)
     async for ev in st.aeng.stream(prompt_ids, params):
@@ -110,7 +127,23 @@ async def _run_one(st: ServerState, prompt_ids: list[int], params: SamplingParam
         if ev.finished:
             reason = "length" if ev.reason == "length" else ("stop" if ev.reason in ("stop", None) else ev.reason)
             break
+    if key is not None and reason in ("stop", "length"):
+        st.cache.put(key, (text, tuple(ids), reason))
     return text, ids, reason, ptoks
+
+
+async def _events(st: ServerState, prompt_ids, params, stops):
+    """Token events of one request, or one synthetic event replaying a cached greedy answer
+    (its text is carried in ``cached_text``)."""
+    key = _cache_key(st, prompt_ids, params, stops)
+    if key is not None and (hit := st.cache.get(key)) is not None:
+        text, ids, reason = hit
+        ev = GenEvent(list(ids), True, reason, len(prompt_ids), len(ids))
+        ev.cached_text = text
+        yield ev
+        return
+    async for ev in st.aeng.stream(prompt_ids, params):
+        yield ev
 
 
 def create_app(st: ServerState) -> FastAPI:
@@ -203,17 +236,14 @@ def create_app(st: ServerState) -> FastAPI:
         return PlainTextResponse("\n".join(lines) + "\n", media_type="text/plain; version=0.0.4")
 
     @app.get("/v1/quality")
-    async def quality():
-        a = st.aeng
-        rec = list(a.recent)
-        tps = sorted(r[0] for r in rec)
-        ttft = sorted(r[1] for r in rec)
-
-        def pct(xs, q):
-            return xs[min(len(xs) - 1, int(q * len(xs)))] if xs else None
-
-        return {"model": st.model_name, "window": len(rec), "tps_p50": pct(tps, 0.5), "tps_p95": pct(tps, 0.95),
-                "ttft_p50_s": pct(ttft, 0.5), "ttft_p95_s": pct(ttft, 0.95)}
+    async def quality(window: int = 300, model: str = ""):
+        """Rolling-window latency / throughput / TTFT percentiles and error rate per model."""
+        if window < 1 or window > 86400:
+            raise HTTPException(status_code=400, detail="window must be in [1, 86400] seconds")
+        out = st.aeng.quality.stats(window, model)
+        out["response_cache"] = {"size": st.cache.size, "hits": st.cache.hits, "misses": st.cache.misses}
+        out["loops_stopped"] = st.aeng.loops_stopped
+        return out
 
     @app.get("/v1/trace")
     async def get_trace():
@@ -341,6 +371,15 @@ def create_app(st: ServerState) -> FastAPI:
     async def root():
         return {"status": "ok", "name": "squish-b200", "version": VERSION}
 
+    @app.get("/chat")
+    async def chat_ui():
+        """Browser chat page (streams from /v1/chat/completions)."""
+        from pathlib import Path
+
+        from fastapi.responses import HTMLResponse
+
+        return HTMLResponse((Path(__file__).parent / "static" / "chat.html").read_text())
+
     @app.get("/v1/version")
     async def version():
         return {"version": VERSION}
@@ -387,10 +426,14 @@ async def _chat_stream(st, rid, created, prompt_ids, params, stops, tools, inclu
                                      "finish_reason": None}]})
     detok = IncrementalDetokenizer(st.tok)
     filt = ToolCallStreamFilter() if tools else None
-    text_all, n_out, reason = "", 0, "stop"
-    async for ev in st.aeng.stream(prompt_ids, params):
+    text_all, n_out, reason, ids = "", 0, "stop", []
+    key = _cache_key(st, prompt_ids, params, stops)
+    async for ev in _events(st, prompt_ids, params, stops):
         n_out += len(ev.token_ids)
-        delta = detok.push(ev.token_ids)
+        ids.extend(ev.token_ids)
+        delta = getattr(ev, "cached_text", None)
+        if delta is None:
+            delta = detok.push(ev.token_ids)
         text_all += delta
         hit = False
         if stops:
@@ -406,8 +449,10 @@ async def _chat_stream(st, rid, created, prompt_ids, params, stops, tools, inclu
             reason = "stop"
             break
         if ev.finished:
-            reason = "length" if ev.reason == "length" else "stop"
+            reason = _finish_reason(ev.reason)
             break
+    if key is not None and reason in ("stop", "length") and not hasattr(ev, "cached_text"):
+        st.cache.put(key, (text_all, tuple(ids), reason))
     if tools:
         _, calls = parse_tool_calls(text_all)
         if calls:
@@ -426,8 +471,10 @@ async def _completion_stream(st, rid, created, prompt_ids, params, stops):
     base = {"id": rid, "object": "text_completion", "created": created, "model": st.model_name}
     detok = IncrementalDetokenizer(st.tok)
     text_all = ""
-    async for ev in st.aeng.stream(prompt_ids, params):
-        delta = detok.push(ev.token_ids)
+    async for ev in _events(st, prompt_ids, params, stops):
+        delta = getattr(ev, "cached_text", None)
+        if delta is None:
+            delta = detok.push(ev.token_ids)
         text_all += delta
         hit = False
         if stops:
@@ -438,7 +485,7 @@ async def _completion_stream(st, rid, created, prompt_ids, params, stops):
         if hit:
             reason = "stop"
         elif ev.finished:
-            reason = "length" if ev.reason == "length" else "stop"
+            reason = _finish_reason(ev.reason)
         yield _sse({**base, "choices": [{"index": 0, "text": delta, "finish_reason": reason, "logprobs": None}]})
         if reason:
             break

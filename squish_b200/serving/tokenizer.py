@@ -90,21 +90,32 @@ def load_tokenizer(model_dir: str | None, vocab_size: int = 259, eos_token_id: i
 
 
 class IncrementalDetokenizer:
-    """Streams text for a growing token list: emits only newly completed characters."""
+    """Streams text for a growing token list: emits only newly completed characters.
+
+    Each push decodes a short window, not the whole list: the text of ids[prefix:read] (already
+    emitted) and of ids[prefix:] (with the new ids); the difference is the new text. Decoding the
+    window from a token that was already emitted keeps tokenizers that render a token
+    differently at the start of a string (SentencePiece's leading-space marker) consistent. A
+    trailing replacement character (an incomplete UTF-8 sequence) is held back until the next
+    token completes it. Cost per push is O(window), not O(generated length).
+    """
 
     def __init__(self, tokenizer):
         self.tok = tokenizer
         self.ids: list[int] = []
         self.text = ""
+        self._prefix = 0  # window start (ids before it are emitted and settled)
+        self._read = 0    # ids before it are emitted
 
     def push(self, token_ids) -> str:
         self.ids.extend(int(t) for t in token_ids)
-        full = self.tok.decode(self.ids)
-        # hold back a trailing replacement char: the next token may complete the character
-        stable = full[:-1] if full.endswith("�") else full
-        if not stable.startswith(self.text):
-            delta = stable[len(self.text):] if len(stable) > len(self.text) else ""
-        else:
-            delta = stable[len(self.text):]
-        self.text = stable if len(stable) >= len(self.text) else self.text
+        if len(self.ids) == self._read:
+            return ""
+        prev = self.tok.decode(self.ids[self._prefix:self._read]) if self._read > self._prefix else ""
+        cur = self.tok.decode(self.ids[self._prefix:])
+        if len(cur) <= len(prev) or cur.endswith("\ufffd"):
+            return ""
+        delta = cur[len(prev):] if cur.startswith(prev) else cur[len(prev):]
+        self._prefix, self._read = self._read, len(self.ids)
+        self.text += delta
         return delta

@@ -114,3 +114,86 @@ def test_memory_governor_levels():
     state["free"] = 1.0
     assert gov.evaluate() == CRITICAL and gov.critical
     assert seen == [CRITICAL]
+
+
+def test_response_cache_quality_and_chat_page(client):
+    body = {"messages": [{"role": "user", "content": "cache me"}], "max_tokens": 6, "temperature": 0,
+            "ignore_eos": True}
+    q0 = client.get("/v1/quality").json()["response_cache"]
+    a = client.post("/v1/chat/completions", json=body).json()
+    b = client.post("/v1/chat/completions", json=body).json()
+    assert a["choices"][0]["message"] == b["choices"][0]["message"]
+    assert a["usage"] == b["usage"]
+    q = client.get("/v1/quality?window=600").json()
+    assert q["response_cache"]["hits"] == q0["hits"] + 1
+    # the streamed form of the same request replays the cached answer
+    with client.stream("POST", "/v1/chat/completions", json=dict(body, stream=True)) as r:
+        chunks = [json.loads(l[6:]) for l in r.iter_lines() if l.startswith("data: {")]
+    text = "".join(c["choices"][0]["delta"].get("content", "") for c in chunks if c["choices"])
+    assert text == a["choices"][0]["message"]["content"]
+    # sampled requests are never cached
+    client.post("/v1/chat/completions", json=dict(body, temperature=0.8, seed=1))
+    assert client.get("/v1/quality").json()["response_cache"]["hits"] == q0["hits"] + 2
+    m = q["models"][0]
+    assert m["model_id"] == "tiny" and m["n_requests"] >= 1 and m["error_rate"] == 0.0
+    assert m["latency_p50_ms"] > 0 and m["ttft_p50_ms"] is not None
+    assert client.get("/v1/quality?window=0").status_code == 400
+    page = client.get("/chat")
+    assert page.status_code == 200 and "/v1/chat/completions" in page.text
+
+
+def test_loop_detector():
+    import numpy as np
+
+    from squish_b200.serving.loop_guard import LoopGuard, detect_loop
+
+    rng = np.random.default_rng(0)
+    assert not detect_loop(rng.integers(0, 30000, 400).tolist())
+    assert detect_loop(rng.integers(0, 100, 50).tolist() + [5, 6, 7] * 4)          # short unit, 4 reps
+    assert not detect_loop(rng.integers(0, 100, 50).tolist() + [5, 6, 7] * 3)      # 3 reps: not yet
+    block = rng.integers(0, 30000, 40).tolist()
+    assert detect_loop(rng.integers(0, 100, 20).tolist() + block * 2)               # a sentence twice
+    noisy = block * 3
+    noisy[70] = 1                                                                    # one drifting token
+    assert detect_loop(noisy)
+    g = LoopGuard()
+    fired = [g.feed([9, 8]) for _ in range(20)]
+    assert fired.index(True) == 7  # first check after 16 tokens
+
+
+class _LoopingEngine:
+    """Engine stand-in whose only request emits the same two tokens forever."""
+
+    def __init__(self):
+        from squish_b200.engine.request import RequestOutput
+
+        self.RO = RequestOutput
+        self.requests, self.live, self.aborted = {}, set(), []
+
+    def add_request(self, prompt, params, rid):
+        self.requests[rid] = params
+        self.live.add(rid)
+
+    def has_unfinished(self):
+        return bool(self.live)
+
+    def abort(self, rid):
+        self.aborted.append(rid)
+        self.live.discard(rid)
+
+    def step(self):
+        return [self.RO(r, [11, 12], False, None, 3, 0) for r in list(self.live)]
+
+
+def test_async_engine_stops_a_loop_with_repetition():
+    from squish_b200.engine.sampling import SamplingParams
+
+    eng = _LoopingEngine()
+    aeng = AsyncEngine(eng, ByteTokenizer(300, 2), model_name="fake").start()
+    try:
+        ev = aeng.generate([1, 2, 3], SamplingParams(max_tokens=10_000), timeout=30)
+    finally:
+        aeng.stop()
+    assert ev.reason == "repetition" and ev.finished
+    assert 16 <= len(ev.token_ids) <= 64
+    assert eng.aborted and aeng.loops_stopped == 1
