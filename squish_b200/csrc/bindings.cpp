@@ -839,6 +839,73 @@ std::vector<torch::Tensor> quantize_int4_asym_cuda(torch::Tensor x, int64_t grou
 
 }  // namespace
 
+namespace {
+
+void check_kmeans_inputs(const torch::Tensor& x, const torch::Tensor& c) {
+  CHECK_CUDA(x);
+  CHECK_CUDA(c);
+  TORCH_CHECK(x.dim() == 2 && c.dim() == 2 && x.size(1) == c.size(1), "x [n, d] and centroids [k, d]");
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && c.scalar_type() == torch::kFloat32, "float32 inputs");
+  TORCH_CHECK(x.is_contiguous() && c.is_contiguous(), "contiguous inputs");
+  const int64_t d = x.size(1);
+  TORCH_CHECK(d == 1 || d == 2 || d == 4 || d == 8 || d == 16 || d == 32 || d == 64,
+              "vector width must be 1, 2, 4, 8, 16, 32 or 64 (zero-pad others)");
+  TORCH_CHECK(c.size(0) >= 1, "at least one centroid");
+}
+
+}  // namespace
+
+std::vector<torch::Tensor> kmeans_assign_cuda(torch::Tensor x, torch::Tensor c) {
+  check_kmeans_inputs(x, c);
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto assign = torch::empty({x.size(0)}, x.options().dtype(torch::kInt32));
+  auto dist = torch::empty({x.size(0)}, x.options());
+  CUDA_OK(sq::kmeans_assign_launch(ptr<float>(x), (int)x.size(0), (int)x.size(1), ptr<float>(c), (int)c.size(0),
+                                   ptr<int>(assign), ptr<float>(dist), nullptr, cur_stream()));
+  return {assign, dist};
+}
+
+// Lloyd iterations from the given centroids (updated in place); stops early when no assignment
+// changes. Returns (assignments, iterations run).
+std::vector<torch::Tensor> kmeans_fit_cuda(torch::Tensor x, torch::Tensor c, int64_t iters) {
+  check_kmeans_inputs(x, c);
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int n = (int)x.size(0), d = (int)x.size(1), k = (int)c.size(0);
+  auto assign = torch::full({n}, -1, x.options().dtype(torch::kInt32));
+  auto sums = torch::empty({k, d}, x.options());
+  auto counts = torch::empty({k}, x.options().dtype(torch::kInt32));
+  auto changed = torch::zeros({1}, x.options().dtype(torch::kInt32));
+  auto s = cur_stream();
+  CUDA_OK(sq::kmeans_assign_launch(ptr<float>(x), n, d, ptr<float>(c), k, ptr<int>(assign), nullptr, nullptr, s));
+  int64_t it = 0;
+  for (; it < iters; ++it) {
+    CUDA_OK(sq::kmeans_update_launch(ptr<float>(x), n, d, ptr<int>(assign), ptr<float>(c), k, ptr<float>(sums),
+                                     ptr<int>(counts), s));
+    changed.zero_();
+    CUDA_OK(sq::kmeans_assign_launch(ptr<float>(x), n, d, ptr<float>(c), k, ptr<int>(assign), nullptr,
+                                     ptr<int>(changed), s));
+    if (changed.item<int>() == 0) {
+      ++it;
+      break;
+    }
+  }
+  return {assign, torch::full({1}, it, torch::kInt64)};
+}
+
+torch::Tensor pq_adc_cuda(torch::Tensor codes, torch::Tensor lut) {
+  CHECK_CUDA(codes);
+  CHECK_CUDA(lut);
+  TORCH_CHECK(codes.scalar_type() == torch::kUInt8 && codes.dim() == 2 && codes.is_contiguous(), "codes: uint8 [n, m]");
+  TORCH_CHECK(lut.scalar_type() == torch::kFloat32 && lut.dim() == 2 && lut.is_contiguous(), "lut: float32 [m, k]");
+  TORCH_CHECK(lut.size(0) == codes.size(1) && lut.size(1) <= 256, "lut [m, k <= 256] matching the codes' m");
+  TORCH_CHECK(lut.numel() <= 12288, "lut too large for shared memory (m * k <= 12288)");
+  const c10::cuda::CUDAGuard guard(codes.device());
+  auto out = torch::empty({codes.size(0)}, lut.options());
+  CUDA_OK(sq::pq_adc_launch(reinterpret_cast<const uint8_t*>(codes.data_ptr()), (int)codes.size(0),
+                            (int)codes.size(1), ptr<float>(lut), (int)lut.size(1), ptr<float>(out), cur_stream()));
+  return out;
+}
+
 namespace sqhost {
 void register_host(pybind11::module& m);  // host_utils.cpp
 }
@@ -877,6 +944,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("fixed_scale") = 0.0);
   m.def("hqq", &hqq_cuda);
   m.def("channel_abs_mean", &channel_abs_mean_cuda);
+  m.def("kmeans_assign", &kmeans_assign_cuda);
+  m.def("kmeans_fit", &kmeans_fit_cuda);
+  m.def("pq_adc", &pq_adc_cuda);
   sqcpu::register_cpu(m);
   sqhost::register_host(m);
 }

@@ -140,4 +140,11 @@ cudaError_t moe_gather_launch(const __nv_bfloat16* x, int ldx, const int* sorted
 cudaError_t moe_combine_launch(const __nv_bfloat16* ys, int ldys, const int* slot_pos, const float* topk_w, int T,
                                int K, int H, __nv_bfloat16* h, int ldh, cudaStream_t s);
 
+// k-means / product quantization (kmeans.cu); d in {1, 2, 4, 8, 16, 32, 64}
+cudaError_t kmeans_assign_launch(const float* x, int n, int d, const float* c, int k, int* assign, float* dist,
+                                 int* changed, cudaStream_t s);
+cudaError_t kmeans_update_launch(const float* x, int n, int d, const int* assign, float* c, int k, float* sums,
+                                 int* counts, cudaStream_t s);
+cudaError_t pq_adc_launch(const uint8_t* codes, int n, int m, const float* lut, int k, float* out, cudaStream_t s);
+
 }  // namespace sq

@@ -5,8 +5,8 @@ normalise the matrix by its RMS (``scale``), then for each of K codebooks fit k-
 residual groups of ``group_size`` input features, assign each group its nearest codeword
 and subtract it. Decoding: W[i, g*gs:(g+1)*gs] = scale * sum_k CB_k[idx[i, g, k]].
 
-k-means runs in PyTorch (on the GPU when the weight is on one): k-means++-style seeding by
-sampling, then Lloyd iterations with chunked nearest-centroid search.
+k-means is quant/pq.py: k-means++ seeding, then Lloyd iterations in the CUDA kernels of
+csrc/kmeans.cu when the weight is on the GPU (torch on the CPU).
 Serialised codebook: float32 [scale, codebook_size, group_size, CB_0 ..., CB_{K-1} ...].
 """
 from __future__ import annotations
@@ -16,31 +16,7 @@ import torch
 from ..models.weights import QTensor
 
 
-def _nearest(x: torch.Tensor, c: torch.Tensor, chunk: int = 65536) -> torch.Tensor:
-    out = torch.empty(x.shape[0], dtype=torch.int64, device=x.device)
-    cn = (c * c).sum(1)
-    for i in range(0, x.shape[0], chunk):
-        xb = x[i:i + chunk]
-        d = cn[None, :] - 2.0 * xb @ c.T
-        out[i:i + chunk] = d.argmin(1)
-    return out
-
-
-def kmeans(x: torch.Tensor, k: int, iters: int = 20, seed: int = 42) -> tuple[torch.Tensor, torch.Tensor]:
-    g = torch.Generator(device="cpu").manual_seed(seed)
-    n = x.shape[0]
-    k = min(k, n)
-    c = x[torch.randperm(n, generator=g)[:k].to(x.device)].clone()
-    assign = _nearest(x, c)
-    for _ in range(iters):
-        sums = torch.zeros_like(c).index_add_(0, assign, x)
-        cnt = torch.bincount(assign, minlength=k).float().clamp_min(1)[:, None]
-        c = torch.where(cnt > 0, sums / cnt, c)
-        new = _nearest(x, c)
-        if torch.equal(new, assign):
-            break
-        assign = new
-    return c, assign
+from .pq import kmeans  # noqa: E402  (GPU kernels for CUDA tensors, torch otherwise)
 
 
 def aqlm_quantize(w: torch.Tensor, n_codebooks: int = 2, codebook_size: int = 256, group_size: int = 8,

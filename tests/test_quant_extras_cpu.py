@@ -270,3 +270,37 @@ def test_merge_model_cli(tmp_path):
     m = load_file(str(tmp_path / "out" / "adapter_model.safetensors"))
     torch.testing.assert_close(m["b"], torch.full((8,), 1.5))
     assert m["w"].abs().max().item() <= 1.0
+
+
+# ------------------------------------------------------------------------------- k-means / PQ
+def test_kmeans_recovers_clusters_and_pq_adc():
+    from squish_b200.quant.pq import kmeans, pq_adc_search, pq_encode, pq_fit, pq_lut, pq_search
+
+    g = torch.Generator().manual_seed(0)
+    centers = torch.randn(8, 6, generator=g) * 5
+    lab = torch.randint(0, 8, (4000,), generator=g)
+    x = centers[lab] + 0.05 * torch.randn(4000, 6, generator=g)
+    c, a = kmeans(x, 8, iters=30, seed=1)
+    # every true cluster maps to exactly one fitted centroid
+    pairs = set(zip(lab.tolist(), a.tolist()))
+    assert len(pairs) == 8 and len({p[1] for p in pairs}) == 8
+    books = pq_fit(x, 3, 16, iters=10)
+    assert books.shape == (3, 16, 2)
+    codes = pq_encode(x, books)
+    assert codes.dtype == torch.uint8 and codes.shape == (4000, 3)
+    q = x[17]
+    lut = pq_lut(q, books)
+    approx = pq_adc_search(codes, lut)
+    recon = torch.cat([books[j][codes[:, j].long()] for j in range(3)], 1)
+    torch.testing.assert_close(approx, ((recon - q) ** 2).sum(1), rtol=1e-5, atol=1e-5)
+    _, top = pq_search(q, books, codes, topk=5)
+    assert int(lab[top[0]]) == int(lab[17])
+
+
+def test_aqlm_uses_kmeans_and_roundtrips():
+    from squish_b200.quant.aqlm import aqlm_dequantize, aqlm_quantize
+
+    w = torch.randn(64, 128) * 0.02
+    t = aqlm_quantize(w, n_codebooks=2, codebook_size=64, iters=5)
+    rel = ((aqlm_dequantize(t) - w).norm() / w.norm()).item()
+    assert rel < 0.6

@@ -167,3 +167,42 @@ def test_awq_calibration_on_gpu_matches_cpu():
     assert a.keys() == b.keys() and len(a) == 5 * cfg.num_layers
     for k in a:
         np.testing.assert_allclose(a[k], b[k], rtol=1e-4, atol=1e-6)
+
+
+@pytest.mark.parametrize("d", [3, 8, 16, 64])
+def test_kmeans_kernels_match_torch(d):
+    """csrc/kmeans.cu: assignment equals the torch nearest-centroid search; Lloyd from the same
+    seeds reaches the CPU fit's inertia; ADC equals the table sum."""
+    from squish_b200.quant import pq
+
+    g = torch.Generator().manual_seed(d)
+    x = torch.randn(20000, d, generator=g)
+    c = torch.randn(300, d, generator=g)
+    a_gpu, dist_gpu = pq.assign(x.cuda(), c.cuda())
+    a_cpu, dist_cpu = pq._sqdist_min(x.double(), c.double())
+    agree = (a_gpu.cpu() == a_cpu).float().mean().item()
+    assert agree > 0.999, agree
+    torch.testing.assert_close(dist_gpu.cpu().double(), dist_cpu, rtol=1e-4, atol=1e-4)
+    init = pq.kmeans_pp_init(x, 64, seed=3)
+    cg, ag = pq.kmeans(x.cuda(), 64, iters=15, init=init)
+    cc, ac = pq.kmeans(x, 64, iters=15, init=init)
+    inert = lambda xx, cc_, aa: ((xx - cc_[aa]) ** 2).sum().item()  # noqa: E731
+    ig, ic = inert(x, cg.cpu(), ag.cpu()), inert(x, cc, ac)
+    assert abs(ig - ic) <= 2e-3 * ic, (ig, ic)
+    codes = torch.randint(0, 256, (50000, 8), generator=g, dtype=torch.uint8)
+    lut = torch.rand(8, 256, generator=g)
+    got = pq.pq_adc_search(codes.cuda(), lut.cuda()).cpu()
+    torch.testing.assert_close(got, pq.pq_adc_search(codes, lut), rtol=1e-5, atol=1e-5)
+
+
+def test_aqlm_gpu_fit_serves_in_gemm(cuda):
+    from squish_b200.quant.aqlm import aqlm_quantize
+
+    g = torch.Generator().manual_seed(9)
+    w = torch.randn(256, 512, generator=g) * 0.02
+    t = aqlm_quantize(w.cuda(), iters=5)
+    dw = K.prepare_weight(t, cuda)
+    x = torch.randn(16, 512, generator=g).to(torch.bfloat16)
+    y = ops.w4a16_linear(x.to(cuda), dw)
+    ref = x.float() @ t.dequantize().float().T
+    assert (y.float().cpu() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item() + 1e-2
