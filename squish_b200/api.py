@@ -34,25 +34,30 @@ def default_device() -> str:
 
 def load_engine(model: str, device: str | None = None, seed: int = 0, kv_dtype: str | None = None,
                 ecfg: EngineConfig | None = None, **engine_kw) -> Loaded:
+    from .utils.startup import StartupPhase, StartupTimer
+
     t0 = time.time()
     dev = torch.device(device or default_device())
-    if model.lower() in PRESETS:
-        cfg, q = get_preset(model)
-        if kv_dtype:
-            q.kv_dtype = kv_dtype
-        ck = random_checkpoint(cfg, q, seed=seed, device=dev)
-        tok_dir = None
-    else:
-        if not Path(model).exists():
-            raise FileNotFoundError(f"{model!r} is neither a checkpoint path nor a preset "
-                                    f"({', '.join(sorted(PRESETS))})")
-        from .io.convert import load_checkpoint
+    with StartupTimer(StartupPhase.CHECKPOINT_READ, model):
+        if model.lower() in PRESETS:
+            cfg, q = get_preset(model)
+            if kv_dtype:
+                q.kv_dtype = kv_dtype
+            ck = random_checkpoint(cfg, q, seed=seed, device=dev)
+            tok_dir = None
+        else:
+            if not Path(model).exists():
+                raise FileNotFoundError(f"{model!r} is neither a checkpoint path nor a preset "
+                                        f"({', '.join(sorted(PRESETS))})")
+            from .io.convert import load_checkpoint
 
-        ck, tok_dir = load_checkpoint(model, str(dev))
-        if kv_dtype:
-            ck.quant.kv_dtype = kv_dtype
-    eng = LLMEngine.from_checkpoint(ck, dev, ecfg, **engine_kw)
-    tok = load_tokenizer(tok_dir, vocab_size=ck.config.vocab_size, eos_token_id=ck.config.eos_token_id)
+            ck, tok_dir = load_checkpoint(model, str(dev))
+            if kv_dtype:
+                ck.quant.kv_dtype = kv_dtype
+    with StartupTimer(StartupPhase.WEIGHT_UPLOAD, "engine (weights, KV pool, graphs)"):
+        eng = LLMEngine.from_checkpoint(ck, dev, ecfg, **engine_kw)
+    with StartupTimer(StartupPhase.TOKENIZER):
+        tok = load_tokenizer(tok_dir, vocab_size=ck.config.vocab_size, eos_token_id=ck.config.eos_token_id)
     return Loaded(eng, tok, ck.config.name, time.time() - t0)
 
 

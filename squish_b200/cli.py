@@ -150,35 +150,21 @@ def cmd_convert(a) -> int:
 
 
 def _local_models() -> list[dict]:
-    from .io.npy_dir import detect_format
+    import dataclasses
 
-    dirs = [ucfg.squish_home() / "models"]
+    from .serving.model_scanner import LocalModelScanner
+
     extra = ucfg.get("model.models_dir")
-    if extra:
-        dirs.append(Path(extra))
-    out = []
-    for d in dirs:
-        if not d.is_dir():
-            continue
-        for p in sorted(d.iterdir()):
-            try:
-                fmt = detect_format(p)
-            except (ValueError, OSError):
-                continue
-            size = sum(f.stat().st_size for f in p.rglob("*") if f.is_file()) if p.is_dir() else p.stat().st_size
-            out.append({"name": p.name, "path": str(p), "format": fmt, "bytes": size})
-    return out
+    sc = LocalModelScanner(extra_dirs=[Path(extra)] if extra else [])
+    return [dataclasses.asdict(m) for m in sc.find_all()]
 
 
-def _catalog() -> list[dict]:
-    from .models.config import PRESETS
+def cmd_scan(a) -> int:
+    from .serving.model_scanner import scan_before_load
 
-    rows = []
-    for name, (c, q) in sorted(PRESETS.items()):
-        rows.append({"name": name, "arch": c.arch, "layers": c.num_layers, "hidden": c.hidden_size,
-                     "params_b": round(c.num_params() / 1e9, 2) if hasattr(c, "num_params") else None,
-                     "weights": f"int{q.weight_bits} g{q.group_size}", "kv": q.kv_dtype})
-    return rows
+    r = scan_before_load(a.path)
+    print(json.dumps({"status": r.status, "scanned": r.scanned, "findings": r.findings}, indent=2))
+    return 0 if r.status == "clean" else 1
 
 
 def cmd_models(a) -> int:
@@ -348,6 +334,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.set_defaults(fn=cmd_convert)
 
     sub.add_parser("models").set_defaults(fn=cmd_models)
+    p = sub.add_parser("scan", help="static safety scan of model files (nothing is executed)")
+    p.add_argument("path")
+    p.set_defaults(fn=cmd_scan)
     sub.add_parser("catalog").set_defaults(fn=cmd_catalog)
     p = sub.add_parser("pull")
     p.add_argument("name")

@@ -196,6 +196,13 @@ def load_checkpoint(path: str, device: str | None = None):
 
     fmt = detect_format(path)
     p = Path(path)
+    if os.environ.get("SQUISH_ALLOW_UNSAFE") != "1":
+        from ..serving.model_scanner import scan_before_load
+
+        scan = scan_before_load(p)
+        if scan.status == "unsafe":
+            raise RuntimeError(f"refusing to load {p}: " + "; ".join(scan.findings[:3]) +
+                               " (set SQUISH_ALLOW_UNSAFE=1 to override)")
     if fmt == "gguf":
         from .gguf import read_gguf
 

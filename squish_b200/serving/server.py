@@ -245,6 +245,13 @@ def create_app(st: ServerState) -> FastAPI:
         out["loops_stopped"] = st.aeng.loops_stopped
         return out
 
+    @app.get("/v1/startup")
+    async def startup():
+        """Wall time of each initialisation phase of this process."""
+        from ..utils.startup import report
+
+        return report().to_dict()
+
     @app.get("/v1/trace")
     async def get_trace():
         return telemetry.tracer().to_chrome()
