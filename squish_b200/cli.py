@@ -167,6 +167,17 @@ def cmd_scan(a) -> int:
     return 0 if r.status == "clean" else 1
 
 
+def _catalog() -> list[dict]:
+    from .models.config import PRESETS
+
+    rows = []
+    for name, (c, q) in sorted(PRESETS.items()):
+        rows.append({"name": name, "arch": c.arch, "layers": c.num_layers, "hidden": c.hidden_size,
+                     "params_b": round(c.num_params() / 1e9, 2) if hasattr(c, "num_params") else None,
+                     "weights": f"int{q.weight_bits} g{q.group_size}", "kv": q.kv_dtype})
+    return rows
+
+
 def cmd_models(a) -> int:
     print(json.dumps({"local": _local_models(), "presets": [r["name"] for r in _catalog()]}, indent=2))
     return 0
