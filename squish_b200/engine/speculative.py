@@ -188,16 +188,21 @@ class PromptLookupProposer:
         self.index: dict[str, NGramIndex] = {}
 
     def propose(self, reqs) -> dict[str, DraftTree]:
+        """Drafts from the C++ n-gram index (``_C.host.NGramIndex``), fed only the tokens each
+        request gained since its last proposal."""
+        from .._ext import native
+
         trees = {}
         for r in reqs:
             idx = self.index.get(r.rid)
             if idx is None:
-                idx = self.index[r.rid] = NGramIndex(self.sc.ngram_min, self.sc.ngram_max)
-            toks = r.tokens
-            idx.update(toks)
-            chains = idx.continuations(toks, self.sc.k, self.sc.branches)
+                idx = self.index[r.rid] = native().host.NGramIndex(self.sc.ngram_min, self.sc.ngram_max)
+            have, total = len(idx), r.total_len
+            if total > have:
+                idx.extend(r.token_slice(have, total - have))
+            chains = idx.continuations(self.sc.k, self.sc.branches)
             if chains:
-                trees[r.rid] = build_tree(toks[-1], chains, self.sc.max_nodes)
+                trees[r.rid] = build_tree(r.token_at(total - 1), chains, self.sc.max_nodes)
         return trees
 
     def after_verify(self, r, accepted: int, preds=None) -> None:

@@ -150,3 +150,27 @@ def test_second_branch_acceptance_compacts_kv():
     assert got == want
     assert calls, "the second branch should have been compacted"
     assert eng.spec_stats["accepted"] > 0
+
+
+def test_cpp_ngram_index_matches_python():
+    """The C++ prompt-lookup index gives the same continuations as the Python restatement,
+    fed incrementally."""
+    import numpy as np
+
+    from squish_b200._ext import native
+    from squish_b200.engine.speculative import NGramIndex
+
+    rng = np.random.default_rng(0)
+    for trial in range(20):
+        base = rng.integers(0, 12 if trial % 2 else 400, 300).tolist()
+        toks = base + base[50:90] + rng.integers(0, 12, 30).tolist()
+        py = NGramIndex(1, 4)
+        cc = native().host.NGramIndex(1, 4)
+        pos = 0
+        for cut in sorted(rng.integers(5, len(toks), 6).tolist()) + [len(toks)]:
+            cc.extend(toks[pos:cut])
+            pos = max(pos, cut)
+            py.update(toks[:pos])
+            assert len(cc) == pos
+            for k, want in ((4, 1), (6, 3)):
+                assert cc.continuations(k, want) == py.continuations(toks[:pos], k, want)
