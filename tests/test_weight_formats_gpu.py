@@ -182,7 +182,7 @@ def test_kmeans_kernels_match_torch(d):
     a_cpu, dist_cpu = pq._sqdist_min(x.double(), c.double())
     agree = (a_gpu.cpu() == a_cpu).float().mean().item()
     assert agree > 0.999, agree
-    torch.testing.assert_close(dist_gpu.cpu().double(), dist_cpu, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(dist_gpu.cpu().double(), dist_cpu.double(), rtol=1e-4, atol=1e-4)
     init = pq.kmeans_pp_init(x, 64, seed=3)
     cg, ag = pq.kmeans(x.cuda(), 64, iters=15, init=init)
     cc, ac = pq.kmeans(x, 64, iters=15, init=init)
