@@ -77,6 +77,7 @@ class AsyncEngine:
         self._guards: dict = {}
         self.loops_stopped = 0
         self.quality = QualityMonitor()
+        self.step_ms: collections.deque = collections.deque(maxlen=4096)  # engine step wall times
         from ..utils.fault import Watchdog
 
         self.watchdog = Watchdog(lambda: bool(self._sinks))
@@ -182,7 +183,9 @@ class AsyncEngine:
                 self._wake.clear()
                 continue
             try:
+                ts = time.perf_counter()
                 outs = eng.step()
+                self.step_ms.append((time.perf_counter() - ts) * 1e3)
                 self.watchdog.heartbeat()
             except Exception as exc:  # noqa: BLE001 - fail the in-flight requests, keep serving
                 log.exception("engine step failed")

@@ -245,6 +245,29 @@ def create_app(st: ServerState) -> FastAPI:
         out["loops_stopped"] = st.aeng.loops_stopped
         return out
 
+    @app.post("/v1/route")
+    async def route(request: Request):
+        """Task category and model-family hint of a prompt (rule-based, no model call)."""
+        from .router import get_default_router
+
+        body = await _json(request)
+        prompt = body.get("prompt")
+        if prompt is None and isinstance(body.get("messages"), list):
+            prompt = " ".join(str(m.get("content", "")) for m in body["messages"] if isinstance(m, dict)
+                              and m.get("role") == "user")
+        if not isinstance(prompt, str):
+            raise HTTPException(status_code=400, detail="Provide 'prompt' or 'messages'")
+        d = get_default_router().route(prompt)
+        return {"category": d.category.value, "confidence": d.confidence, "model_hint": d.model_hint,
+                "rule": d.rule, "reasoning": d.reasoning}
+
+    @app.get("/v1/obs-report")
+    async def obs_report(threshold_ms: float = 200.0):
+        """Latency percentiles per operation and the ones above ``threshold_ms`` with hints."""
+        from .obs_report import generate_report
+
+        return generate_report(st.aeng, telemetry.tracer(), threshold_ms)
+
     @app.get("/v1/startup")
     async def startup():
         """Wall time of each initialisation phase of this process."""

@@ -197,3 +197,42 @@ def test_async_engine_stops_a_loop_with_repetition():
     assert ev.reason == "repetition" and ev.finished
     assert 16 <= len(ev.token_ids) <= 64
     assert eng.aborted and aeng.loops_stopped == 1
+
+
+def test_obs_report(client):
+    client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 3, "temperature": 0.5, "seed": 3})
+    r = client.get("/v1/obs-report?threshold_ms=0").json()
+    assert r["status"] == "degraded" and "engine.step" in r["profile"]
+    assert r["profile"]["engine.step"]["n_samples"] >= 1
+    ops = {b["op"] for b in r["bottlenecks"]}
+    assert "engine.step" in ops and all(b["hint"] for b in r["bottlenecks"] if b["op"] in ("engine.step", "ttft_ms"))
+    assert client.get("/v1/obs-report?threshold_ms=1e9").json()["status"] == "ok"
+
+
+def test_prompt_router_and_backend_router(client, monkeypatch):
+    import re
+
+    from squish_b200.serving.backend_router import BackendConfig, BackendRouter
+    from squish_b200.serving.router import PromptRouter, RouterCategory, RouterConfig, RouterRule
+
+    r = PromptRouter()
+    assert r.route("```python\nprint(1)\n```").category == RouterCategory.CODE
+    assert r.route("Solve the equation 3x + 2 = 11").category == RouterCategory.MATH
+    assert r.route("Write a poem about the sea").category == RouterCategory.CREATIVE
+    assert r.route("Who painted the Mona Lisa?").category == RouterCategory.FACTUAL
+    d = r.route("hey there, nice to meet you")
+    assert d.category == RouterCategory.CONVERSATION and d.confidence == 0.5
+    assert r.route("   ").category == RouterCategory.UNKNOWN
+    custom = PromptRouter(RouterConfig(rules=[RouterRule("sql", RouterCategory.CODE, re.compile("select .* from",
+                                                                                              re.I), 99, "sql-model")]))
+    assert custom.route("SELECT a FROM t").model_hint == "sql-model"
+    j = client.post("/v1/route", json={"messages": [{"role": "user", "content": "debug this rust function"}]}).json()
+    assert j["category"] == "code" and j["confidence"] == 1.0
+    monkeypatch.setenv("SQUISH_BACKEND", "ollama")
+    monkeypatch.delenv("SQUISH_BACKEND_URL", raising=False)
+    br = BackendRouter(BackendConfig())
+    assert br.proxy_url("v1/chat/completions") == "http://127.0.0.1:11434/v1/chat/completions"
+    monkeypatch.setenv("SQUISH_BACKEND_URL", "http://127.0.0.1:9/")
+    assert BackendRouter(BackendConfig()).health_check(timeout=0.2) is False  # nothing listens on port 9
+    with pytest.raises(ValueError):
+        BackendConfig(backend="nope")
