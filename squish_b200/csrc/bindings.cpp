@@ -906,6 +906,23 @@ torch::Tensor pq_adc_cuda(torch::Tensor codes, torch::Tensor lut) {
   return out;
 }
 
+torch::Tensor hadamard_rows_cuda(torch::Tensor x, torch::Tensor signs, int64_t block, c10::optional<torch::Tensor> out) {
+  CHECK_CUDA(x);
+  CHECK_CUDA(signs);
+  TORCH_CHECK(x.dim() == 2 && x.scalar_type() == torch::kBFloat16 && x.stride(1) == 1, "x: bf16 [M, K], unit column stride");
+  TORCH_CHECK(signs.scalar_type() == torch::kFloat32 && signs.is_contiguous() && signs.numel() == x.size(1),
+              "signs: float32 [K]");
+  TORCH_CHECK(block >= 2 && block <= 4096 && (block & (block - 1)) == 0 && x.size(1) % block == 0,
+              "block must be a power of two in [2, 4096] dividing K");
+  const c10::cuda::CUDAGuard guard(x.device());
+  torch::Tensor y = out.has_value() ? *out : torch::empty({x.size(0), x.size(1)}, x.options());
+  TORCH_CHECK(y.scalar_type() == torch::kBFloat16 && y.dim() == 2 && y.size(0) >= x.size(0) && y.size(1) == x.size(1) &&
+              y.stride(1) == 1, "out: bf16 [>= M, K]");
+  CUDA_OK(sq::hadamard_rows_launch(ptr<__nv_bfloat16>(x), (int)x.stride(0), ptr<__nv_bfloat16>(y), (int)y.stride(0),
+                                   ptr<float>(signs), (int)x.size(0), (int)x.size(1), (int)block, cur_stream()));
+  return y;
+}
+
 namespace sqhost {
 void register_host(pybind11::module& m);  // host_utils.cpp
 }
@@ -947,6 +964,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kmeans_assign", &kmeans_assign_cuda);
   m.def("kmeans_fit", &kmeans_fit_cuda);
   m.def("pq_adc", &pq_adc_cuda);
+  m.def("hadamard_rows", &hadamard_rows_cuda, py::arg("x"), py::arg("signs"), py::arg("block"),
+        py::arg("out") = py::none());
   sqcpu::register_cpu(m);
   sqhost::register_host(m);
 }

@@ -147,4 +147,8 @@ cudaError_t kmeans_update_launch(const float* x, int n, int d, const int* assign
                                  int* counts, cudaStream_t s);
 cudaError_t pq_adc_launch(const uint8_t* codes, int n, int m, const float* lut, int k, float* out, cudaStream_t s);
 
+// randomized block Walsh-Hadamard rotation of rows (hadamard.cu): y = blockdiag(H_b / sqrt(b)) (s * x)
+cudaError_t hadamard_rows_launch(const __nv_bfloat16* x, int ldx, __nv_bfloat16* y, int ldy, const float* signs,
+                                 int M, int K, int b, cudaStream_t s);
+
 }  // namespace sq

@@ -16,6 +16,7 @@ Suffix sets, in the reference loader's dispatch priority (squish/io/loader_utils
     __aqlm_idx + __aqlm_cb              AQLM additive codebooks
     __q + __s                           INT8 symmetric (per row or per group)
     __f8 + __sf8                        FP8 E4M3 codes + per-group scales (this package's extension)
+    __sqint2_idx/_scales/_zp/_meta(+_L/_R) SQINT2 (Hadamard-rotated NF2 INT2, quant/sqint2.py)
     __pt                                float16 passthrough
 plus __shape (the original shape) for every tensor. ``.npy.sqe`` files (rANS / Huffman coded,
 io/entropy.py) are always readable; ``.npy.zst`` files when ``zstandard`` is importable.
@@ -116,6 +117,10 @@ def read_tensor(td: Path, key: str) -> QTensor:
         idx, cb = arr("__aqlm_idx", np.int32), arr("__aqlm_cb", np.float32)
         t = QTensor("aqlm", shape, packed=idx, scales=cb, group=int(cb[2].item()))
         return t
+    if _exists(td, key, "__sqint2_meta"):
+        from ..quant.sqint2 import read_files
+
+        return read_files(lambda suf: _load(td / f"{key}{suf}.npy"), key, shape)
     if _exists(td, key, "__f8"):
         q, s = arr("__f8", np.uint8), arr("__sf8", np.float32)
         return QTensor("fp8", shape or tuple(q.shape), packed=q, scales=s, group=q.shape[1] // s.shape[1])
@@ -162,6 +167,10 @@ def tensor_files(name: str, t: QTensor) -> dict[str, np.ndarray]:
         out.update({f"{k}__q": np_(t.packed, np.int8), f"{k}__s": np_(t.scales, np.float32)})
     elif t.kind == "fp8":
         out.update({f"{k}__f8": np_(t.packed, np.uint8), f"{k}__sf8": np_(t.scales, np.float32)})
+    elif t.kind == "q2" and t.extra and "rot_signs" in t.extra:
+        from ..quant.sqint2 import write_files
+
+        out.update(write_files(k, t))
     elif t.kind == "q2":
         out.update({f"{k}__q2": np_(t.packed, np.uint8), f"{k}__s2": np_(t.scales, np.float32),
                     f"{k}__z2": np_(t.offsets, np.float32)})

@@ -114,13 +114,27 @@ class LayerWeights:
 GEMM_KINDS = ("q4a", "nf4", "q8", "fp8", "q2", "q3", "aqlm")
 
 
+def _rotation(t: QTensor):
+    """(signs, block) of an SQINT2 tensor stored in the rotated frame, else None."""
+    return (t.extra["rot_signs"], int(t.extra["rot_block"])) if t.extra and "rot_signs" in t.extra else None
+
+
+def _same_rotation(parts: list[QTensor]) -> bool:
+    r0 = _rotation(parts[0])
+    for p in parts[1:]:
+        r = _rotation(p)
+        if (r is None) != (r0 is None) or (r is not None and (r[1] != r0[1] or not torch.equal(r[0], r0[0]))):
+            return False
+    return True
+
+
 def _same_kind(parts: list[QTensor], group: int) -> list[QTensor]:
-    """Tensors fused into one GEMM must share a native kind and group; otherwise all are
-    re-encoded as INT4."""
+    """Tensors fused into one GEMM must share a native kind, group and input rotation; otherwise
+    all are re-encoded as INT4."""
     k0 = parts[0].kind
     # AQLM tensors carry their own codebooks, so they cannot share one fused GEMM
     if (k0 in GEMM_KINDS and all(p.kind == k0 and p.group == parts[0].group for p in parts)
-            and not (k0 == "aqlm" and len(parts) > 1)):
+            and not (k0 == "aqlm" and len(parts) > 1) and _same_rotation(parts)):
         return parts
     return [_as_q4a(p, group) if p.kind != "q4a" else p for p in parts]
 
@@ -131,7 +145,8 @@ def _cat_rows(parts: list[QTensor]) -> QTensor:
         return None if xs[0] is None else torch.cat(xs)
 
     return QTensor(parts[0].kind, (sum(p.shape[0] for p in parts), parts[0].shape[1]), packed=cat("packed"),
-                   scales=cat("scales"), offsets=cat("offsets"), group=parts[0].group)
+                   scales=cat("scales"), offsets=cat("offsets"), group=parts[0].group,
+                   extra=parts[0].extra if _rotation(parts[0]) else None)
 
 
 _cat_q4a = _cat_rows
@@ -156,7 +171,8 @@ def _interleave_gate_up(gate: QTensor, up: QTensor) -> QTensor:
         return torch.stack([a.view(fp // 64, 64, -1), b.view(fp // 64, 64, -1)], 1).reshape(2 * fp, -1)
 
     return QTensor(gate.kind, (2 * fp, gate.shape[1]), packed=inter(gate.packed, up.packed),
-                   scales=inter(gate.scales, up.scales), offsets=inter(gate.offsets, up.offsets), group=gate.group)
+                   scales=inter(gate.scales, up.scales), offsets=inter(gate.offsets, up.offsets), group=gate.group,
+                   extra=gate.extra if _rotation(gate) else None)
 
 
 def _as_q4a(t: QTensor, group: int) -> QTensor:
@@ -170,7 +186,10 @@ def _as_q4a(t: QTensor, group: int) -> QTensor:
 
 
 def _native(t: QTensor, group: int) -> QTensor:
-    return t if t.kind in GEMM_KINDS and not t.extra else _as_q4a(t, group)
+    """Kinds the GEMM decodes as stored; SQINT2 (INT2 with an input rotation) too, unless it
+    carries a low-rank residual."""
+    rot_only = t.kind == "q2" and t.extra and set(t.extra) <= {"rot_signs", "rot_block", "seed"}
+    return t if t.kind in GEMM_KINDS and (not t.extra or rot_only) else _as_q4a(t, group)
 
 
 def _to_int4(t: QTensor, device, bias: torch.Tensor | None = None, group: int = 64) -> Int4Weight:
@@ -293,6 +312,10 @@ class CudaRunner:
         self.meta_dev = torch.empty(self.meta_cap, dtype=torch.int32, device=dev)
         self.ws.reserve_attn(B, cfg.num_heads, 64, cfg.head_dim)
         self.ws.sampler_buffer(R, cfg.vocab_size)
+        rot_k = [w.k for lw in self.layers for w in (lw.qkv, lw.o, lw.gate_up, lw.down, self.lm_head_q)
+                 if w is not None and getattr(w, "rot", None) is not None]
+        if rot_k:  # SQINT2 input rotations: one scratch for the largest activation block
+            self.ws.rot_buffer(max(T, R), max(rot_k))
 
     # ------------------------------------------------------------------ metadata upload
     def upload(self, st: StepInputs) -> dict:

@@ -36,6 +36,7 @@ class Workspace:
         self._attn_lse = torch.empty(0, dtype=torch.float32, device=device)
         self._sampler = torch.empty(0, dtype=torch.float32, device=device)
         self._dq = torch.empty(0, dtype=torch.bfloat16, device=device)  # expanded weights (large-M GEMMs)
+        self._rot = torch.empty(0, dtype=torch.bfloat16, device=device)  # rotated activations (SQINT2)
         # set once a CUDA graph has captured these buffers: growing one then would leave the
         # graph writing to freed memory, so it becomes an error instead
         self.frozen = False
@@ -69,6 +70,13 @@ class Workspace:
                 return None
             self._dq = torch.empty(elems, dtype=torch.bfloat16, device=self.device)
         return self._dq
+
+    def rot_buffer(self, m: int, k: int) -> torch.Tensor:
+        """bf16 [m, k] scratch for Hadamard-rotated activations (one linear at a time)."""
+        if self._rot.numel() < m * k:
+            self._grow_check("rotation")
+            self._rot = torch.empty(m * k, dtype=torch.bfloat16, device=self.device)
+        return self._rot[: m * k].view(m, k)
 
     def check(self) -> None:
         """Raise if any kernel recorded an error (a bounded wait that timed out)."""
@@ -114,6 +122,10 @@ class Int4Weight:
     # optional resident bf16 expansion [n, 64 * ceil(k / 64)] for large-M GEMMs (the exact
     # values the quantized GEMM computes with); None = expand per call
     dense: torch.Tensor | None = None
+    # SQINT2: the weight is stored rotated (W R^T) and the input is rotated first,
+    # R x = blockdiag(H_b / sqrt(b)) (rot * x) (csrc/hadamard.cu)
+    rot: torch.Tensor | None = None  # float32 [k] signs
+    rot_block: int = 0
 
     @property
     def nbytes(self) -> int:
@@ -228,6 +240,13 @@ def prepare_weight(t, device, bias: torch.Tensor | None = None) -> Int4Weight:
         codes = torch.stack([(p >> (2 * i)) & 3 for i in range(4)], dim=-1).reshape(p.shape[0], -1)
         wt = repack_codes(codes, t.scales.to(dev), t.offsets.to(dev), k, t.group, WF_INT2)
         fmt = WF_INT2
+        if t.extra and "rot_signs" in t.extra:
+            if "sq_L" in t.extra:
+                raise ValueError("SQINT2 weights with a low-rank residual have no GEMM code format")
+            return Int4Weight(wq=wt, sz=torch.empty(0, dtype=torch.int32, device=dev), n=int(t.shape[0]), k=k,
+                              group=int(t.group), bias=b, fmt=fmt,
+                              rot=t.extra["rot_signs"].to(dev, torch.float32).contiguous(),
+                              rot_block=int(t.extra["rot_block"]))
     elif t.kind == "q3":
         if t.extra:
             raise ValueError("INT3 weights with a low-rank compensator have no GEMM code format")
@@ -284,6 +303,9 @@ def w4a16_linear(x: torch.Tensor, w: Int4Weight, out: torch.Tensor | None = None
     interleaved gate/up blocks of 64 and y = silu(gate) * up has N/2 columns."""
     ws = ws or workspace(x.device)
     m = x.shape[0]
+    if w.rot is not None:
+        x = native().hadamard_rows(x, w.rot, w.rot_block, ws.rot_buffer(m, w.k))
+        _count()
     ncols = w.n // 2 if silu_mul else w.n
     if out is None:
         out = torch.empty((m, ncols), dtype=torch.bfloat16, device=x.device)

@@ -29,12 +29,15 @@ from ..models.weights import Checkpoint, QTensor
 def _rows(t: QTensor, r0: int, r1: int) -> QTensor:
     if t.kind == "dense":
         return QTensor("dense", (r1 - r0,) + tuple(t.shape[1:]), data=t.data[r0:r1].contiguous())
-    if t.kind not in ("q4a", "q8", "fp8", "nf4", "q2", "q3"):
+    rot_only = t.kind == "q2" and t.extra and set(t.extra) <= {"rot_signs", "rot_block", "seed"}
+    if t.kind not in ("q4a", "q8", "fp8", "nf4", "q2", "q3") or (t.extra and not rot_only):
         t = _to_q4a(t)
+        rot_only = False
+    # a row slice keeps the input rotation of an SQINT2 weight (it acts on the columns)
     return dataclasses.replace(t, shape=(r1 - r0, t.shape[1]), packed=t.packed[r0:r1].contiguous(),
                                scales=t.scales[r0:r1].contiguous(),
                                offsets=None if t.offsets is None else t.offsets[r0:r1].contiguous(),
-                               extra=None)
+                               extra=t.extra if rot_only else None)
 
 
 def _to_q4a(t: QTensor) -> QTensor:

@@ -26,7 +26,12 @@ def dequantize_qtensor(t: QTensor) -> torch.Tensor:
     if k == "fp8":
         return C.dequantize_fp8(t.packed.cpu().contiguous(), t.scales.cpu().float().contiguous(), 0)
     if k == "q2":
-        return C.dequantize_int2(t.packed.cpu(), t.scales.cpu().float(), t.offsets.cpu().float(), t.group)
+        w = C.dequantize_int2(t.packed.cpu(), t.scales.cpu().float(), t.offsets.cpu().float(), t.group)
+        if t.extra and "rot_signs" in t.extra:  # SQINT2: stored in the rotated frame
+            from .sqint2 import dequantize_rotated
+
+            w = dequantize_rotated(t, w)
+        return w
     if k == "q3":
         w = C.unpack_int3(t.packed.cpu(), t.scales.cpu().float(), t.group, t.shape[-1])
         if t.offsets is not None:
@@ -75,7 +80,7 @@ def dequantize_fp8(codes: torch.Tensor, scales: torch.Tensor, fmt: str = "e4m3")
 
 def quantize(w: torch.Tensor, kind: str, group: int, mse_clip: bool = False, hqq: bool = False,
              hqq_iters: int = 10) -> QTensor:
-    """Quantize a 2-D weight to ``kind`` (q4a | q8 | fp8 | nf4 | q2 | q3 | aqlm | dense).
+    """Quantize a 2-D weight to ``kind`` (q4a | q8 | fp8 | nf4 | q2 | sqint2 | q3 | aqlm | dense).
     ``hqq``: refine the INT4 / INT2 affine grids by half-quadratic quantization (quant/hqq.py)."""
     from ..models.weights import pick_group, quantize_q4a
 
@@ -91,6 +96,10 @@ def quantize(w: torch.Tensor, kind: str, group: int, mse_clip: bool = False, hqq
         return ht.to_qtensor(kind)
     if kind == "q4a":
         return quantize_q4a(w, group, mse_clip)
+    if kind == "sqint2":
+        from .sqint2 import SQINT2Config, compress_weight
+
+        return compress_weight(w.detach(), SQINT2Config(group_size=pick_group(w.shape[1], group)))
     if kind == "dense":
         return QTensor("dense", tuple(w.shape), data=w)
     g = pick_group(w.shape[1], group)

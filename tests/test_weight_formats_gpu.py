@@ -206,3 +206,69 @@ def test_aqlm_gpu_fit_serves_in_gemm(cuda):
     y = ops.w4a16_linear(x.to(cuda), dw)
     ref = x.float() @ t.dequantize().float().T
     assert (y.float().cpu() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item() + 1e-2
+
+
+@pytest.mark.parametrize("k,b", [(3584, 512), (1024, 1024), (4096, 4096), (96, 32)])
+def test_hadamard_kernel_matches_torch(k, b):
+    from squish_b200.quant.sqint2 import fwht_blocks, rotation_signs
+
+    g = torch.Generator().manual_seed(k)
+    x = torch.randn(70, k, generator=g).to(torch.bfloat16)
+    s = rotation_signs(k, 3)
+    from squish_b200._ext import native
+
+    y = native().hadamard_rows(x.cuda(), s.cuda(), b).cpu().float()
+    ref = fwht_blocks(x.float() * s, b) / b ** 0.5
+    torch.testing.assert_close(y, ref, rtol=1e-2, atol=1e-2)
+    # strided rows into a larger output buffer
+    out = torch.zeros(80, k, dtype=torch.bfloat16, device="cuda")
+    native().hadamard_rows(x.cuda(), s.cuda(), b, out)
+    assert torch.equal(out[:70].cpu(), y.to(torch.bfloat16)) and out[70:].abs().sum().item() == 0
+
+
+@pytest.mark.parametrize("m", [1, 37, 300, 500])
+def test_sqint2_linear_matches_fp32(cuda, m):
+    """An SQINT2 weight (rotated INT2 in the tcgen05 GEMM, input rotated by the kernel) against
+    x @ W^T with W the unrotated dequantisation, in the fused-dequant (small M) and expanded
+    (large M) paths."""
+    from squish_b200.quant.sqint2 import SQINT2Config, compress_weight
+
+    g = torch.Generator().manual_seed(m)
+    n, k = 640, 1536
+    w = torch.randn(n, k, generator=g) * 0.02
+    t = compress_weight(w, SQINT2Config(group_size=64))
+    dw = K.prepare_weight(t, cuda)
+    assert dw.rot is not None and dw.rot_block == 512
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    y = ops.w4a16_linear(x.to(cuda), dw)
+    torch.cuda.synchronize()
+    ref = x.float() @ t.dequantize().float().T
+    err = (y.float().cpu() - ref).abs().max().item()
+    assert err <= 3e-2 * ref.abs().max().item() + 1e-2, err
+
+
+def test_engine_with_sqint2_weights_matches_oracle(cuda):
+    from squish_b200.engine.engine import EngineConfig, LLMEngine
+    from squish_b200.engine.sampling import SamplingParams
+    from squish_b200.models.config import get_preset
+    from squish_b200.models.reference import ReferenceModel
+    from squish_b200.models.weights import linear_names, random_checkpoint
+
+    from .test_engine_gpu import _teacher_forced_ok
+
+    cfg, q = get_preset("tiny-llama")
+    cfg = dataclasses.replace(cfg, intermediate_size=512)
+
+    def ck():
+        c = random_checkpoint(cfg, q, seed=0)
+        for name, _ in linear_names(cfg):
+            c.tensors[name] = quantize(c.tensors[name].dequantize().float(), "sqint2", 32)
+        return c
+
+    ref = ReferenceModel(ck())
+    eng = LLMEngine.from_checkpoint(ck(), cuda, EngineConfig(max_num_seqs=2, max_model_len=256, num_pages=32))
+    assert eng.runner.layers[0].qkv.rot is not None and eng.runner.layers[0].gate_up.rot is not None
+    prompt = np.random.default_rng(3).integers(0, cfg.vocab_size, 30).tolist()
+    out = eng.generate([prompt], SamplingParams(max_tokens=8, ignore_eos=True))[0]
+    ok, worst = _teacher_forced_ok(ref, prompt, out)
+    assert ok, (worst, out)
