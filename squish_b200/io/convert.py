@@ -100,17 +100,23 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
             if awq or awq_scales:
                 ops = _awq_ops(cfg, q, list(ck.tensors), lambda: ck, None, out, dev, awq_scales, awq_alpha,
                                awq_samples, awq_seq_len, seed, log)
+            router = None
+            if kind == "mixed":
+                from ..quant.mixed import MixedPrecisionRouter
+
+                router = MixedPrecisionRouter(cfg.num_layers)
             for name, t in ck.tensors.items():
                 if name == "lm_head.weight" and cfg.tie_embeddings:
                     continue
+                tkind = router.kind_for(name) if router is not None else kind
                 if name in ops:
                     from ..quant.awq import apply_op
 
                     w = apply_op(t.dequantize(), ops[name])
                     t = (QTensor("dense", t.shape, data=w.cpu()) if t.kind == "dense"
-                         else quantize(w, kind, group_size, mse_clip, hqq=hqq))
-                elif t.kind != "dense" and (kind != "q4a" or hqq):
-                    t = quantize(t.dequantize(), kind, group_size, mse_clip, hqq=hqq)
+                         else quantize(w, tkind, group_size, mse_clip, hqq=hqq))
+                elif t.kind != "dense" and (tkind != "q4a" or hqq):
+                    t = quantize(t.dequantize(), tkind, group_size, mse_clip, hqq=hqq)
                 stats["bytes"] += _write_tensor(td, name, t)
                 stats["n_quantized" if t.kind != "dense" else "n_passthrough"] += 1
                 manifest[name] = safe_key(name)
@@ -147,6 +153,11 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
 
             ops = _awq_ops(cfg, q, names, load_dense, src, out, dev, awq_scales, awq_alpha, awq_samples,
                            awq_seq_len, seed, log)
+        router = None
+        if kind == "mixed":
+            from ..quant.mixed import MixedPrecisionRouter
+
+            router = MixedPrecisionRouter(cfg.num_layers)
         for i, shard in enumerate(shards):
             if shard.name in done:
                 continue
@@ -158,7 +169,8 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
 
                         w = apply_op(w, ops[name])
                     if should_quantize(name, tuple(w.shape)):
-                        t = quantize(w if dev.type == "cuda" else w.float(), kind, group_size, mse_clip, hqq=hqq)
+                        tkind = router.kind_for(name) if router is not None else kind
+                        t = quantize(w if dev.type == "cuda" else w.float(), tkind, group_size, mse_clip, hqq=hqq)
                         stats["n_quantized"] += 1
                     else:
                         t = QTensor("dense", tuple(w.shape), data=w.float().cpu())

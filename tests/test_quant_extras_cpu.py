@@ -367,3 +367,34 @@ def test_sqint2_reads_reference_version1_files(tmp_path):
     assert r.kind == "dense"
     deq = ((NF2_VALUES[idx.numpy().astype(int)] - zp.numpy()[:, None]) * sc.numpy()[:, None]).reshape(256, 96)
     torch.testing.assert_close(r.data, torch.from_numpy(hl.T @ deq @ hr), rtol=1e-4, atol=1e-5)
+
+
+def test_mixed_precision_router_and_compress(tmp_path, monkeypatch):
+    from squish_b200.io.convert import compress, load_checkpoint
+    from squish_b200.quant.mixed import MixedPrecisionRouter
+
+    r = MixedPrecisionRouter(28)
+    assert r.boundary_layers == {0, 1, 26, 27}
+    assert r.format_for("model.layers.0.mlp.gate_proj.weight") == "int4"
+    assert r.format_for("model.layers.5.mlp.up_proj.weight") == "sqint2"
+    assert r.format_for("model.layers.5.self_attn.k_proj.weight") == "int3"
+    assert r.format_for("model.layers.5.mlp.down_proj.weight") == "int4"
+    assert r.format_for("model.norm.weight") is None and r.format_for("model.layers.5.mlp.gate_proj.bias") is None
+    assert MixedPrecisionRouter(3).boundary_layers == {0, 1, 2}
+    from squish_b200.models import config as C
+
+    cfg, q = get_preset("tiny-llama")
+    cfg = dataclasses.replace(cfg, name="tiny-llama-6l", num_layers=6)
+    monkeypatch.setitem(C.PRESETS, "tiny-llama-6l", (cfg, q))
+    compress(None, str(tmp_path / "m"), kind="mixed", random_preset="tiny-llama-6l", device="cpu", group_size=32,
+             log=lambda *_: None)
+    ck, _ = load_checkpoint(str(tmp_path / "m"), "cpu")
+    kinds = {n: t.kind for n, t in ck.tensors.items()}
+    assert {"q2", "q3", "q4a"} <= set(kinds.values())
+    rr = MixedPrecisionRouter(cfg.num_layers)
+    for n, k in kinds.items():
+        f = rr.format_for(n)
+        if f is not None and "layers" in n and n.endswith("proj.weight"):
+            assert k == {"int4": "q4a", "int3": "q3", "sqint2": "q2"}[f], (n, k)
+    m = ReferenceModel(ck)
+    assert torch.isfinite(m.forward([1, 2, 3], m.new_cache(), 0)).all()

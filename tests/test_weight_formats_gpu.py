@@ -272,3 +272,32 @@ def test_engine_with_sqint2_weights_matches_oracle(cuda):
     out = eng.generate([prompt], SamplingParams(max_tokens=8, ignore_eos=True))[0]
     ok, worst = _teacher_forced_ok(ref, prompt, out)
     assert ok, (worst, out)
+
+
+def test_engine_with_mixed_precision_checkpoint(cuda, tmp_path, monkeypatch):
+    """compress --format mixed (INT4 boundary layers, INT3 attention, SQINT2 gate/up) runs in the
+    engine with every projection in its own GEMM code format, matching the CPU oracle."""
+    from squish_b200.engine.engine import EngineConfig, LLMEngine
+    from squish_b200.engine.sampling import SamplingParams
+    from squish_b200.io.convert import compress, load_checkpoint
+    from squish_b200.models import config as C
+    from squish_b200.models.reference import ReferenceModel
+
+    from .test_engine_gpu import _teacher_forced_ok
+
+    cfg, q = C.get_preset("tiny-llama")
+    cfg = dataclasses.replace(cfg, name="tiny-llama-6l", num_layers=6, intermediate_size=512)
+    monkeypatch.setitem(C.PRESETS, "tiny-llama-6l", (cfg, q))
+    compress(None, str(tmp_path / "m"), kind="mixed", random_preset="tiny-llama-6l", device="cpu", group_size=32,
+             log=lambda *_: None)
+    ck, _ = load_checkpoint(str(tmp_path / "m"), "cpu")
+    ref = ReferenceModel(ck)
+    eng = LLMEngine.from_checkpoint(load_checkpoint(str(tmp_path / "m"), "cpu")[0], cuda,
+                                    EngineConfig(max_num_seqs=2, max_model_len=256, num_pages=32))
+    L = eng.runner.layers
+    assert L[0].qkv.fmt == K.WF_INT4 and L[2].qkv.fmt == K.WF_INT3 and L[2].gate_up.fmt == K.WF_INT2
+    assert L[2].gate_up.rot is not None and L[2].down.fmt == K.WF_INT4
+    prompt = np.random.default_rng(4).integers(0, cfg.vocab_size, 30).tolist()
+    out = eng.generate([prompt], SamplingParams(max_tokens=8, ignore_eos=True))[0]
+    ok, worst = _teacher_forced_ok(ref, prompt, out)
+    assert ok, (worst, out)
