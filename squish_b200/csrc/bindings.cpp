@@ -926,6 +926,9 @@ torch::Tensor hadamard_rows_cuda(torch::Tensor x, torch::Tensor signs, int64_t b
 namespace sqhost {
 void register_host(pybind11::module& m);  // host_utils.cpp
 }
+namespace sqgram {
+void register_grammar(pybind11::module& m);  // grammar.cpp
+}
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "squish_b200 native kernels (sm_100a CUDA + C++ CPU reference)";
@@ -968,4 +971,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out") = py::none());
   sqcpu::register_cpu(m);
   sqhost::register_host(m);
+  sqgram::register_grammar(m);
 }

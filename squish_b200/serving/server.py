@@ -10,6 +10,7 @@ batching), not serialised on one inference thread.
 from __future__ import annotations
 
 import asyncio
+import dataclasses
 import json
 import time
 import uuid
@@ -36,6 +37,7 @@ class ServerState:
 
         self.aeng = aeng
         self.cache = ResponseCache(response_cache)
+        self._grammar = None
         self.model_name = model_name
         self.api_key = api_key
         self.arch = arch
@@ -47,6 +49,25 @@ class ServerState:
     @property
     def tok(self):
         return self.aeng.tokenizer
+
+    def grammar_factory(self):
+        """JSON matcher factory (the vocabulary trie is built on first use)."""
+        if self._grammar is None:
+            from .grammar import GrammarFactory
+
+            eng = self.aeng.engine
+            self._grammar = GrammarFactory(self.tok, eng.cfg.vocab_size, self.tok.eos_token_id)
+        return self._grammar
+
+    def format_factory(self, response_format):
+        """A fresh JSON grammar per use when ``response_format`` asks for JSON (None otherwise)."""
+        from .grammar import wants_json
+
+        try:
+            want = wants_json(response_format)
+        except ValueError as exc:
+            raise HTTPException(status_code=400, detail=str(exc)) from exc
+        return None if not want else self.grammar_factory()
 
 
 def _check_auth(request: Request, st: ServerState) -> None:
@@ -329,9 +350,14 @@ def create_app(st: ServerState) -> FastAPI:
         if body.get("stream"):
             if n != 1:
                 raise HTTPException(status_code=400, detail="streaming supports n = 1")
+            gf = st.format_factory(body.get("response_format"))
+            if gf:
+                params = dataclasses.replace(params, grammar=gf.json())
             return StreamingResponse(_chat_stream(st, rid, created, prompt_ids, params, stops, tools, include_usage),
                                      media_type="text/event-stream")
-        results = await asyncio.gather(*[_run_one(st, prompt_ids, params, stops) for _ in range(n)])
+        gf = st.format_factory(body.get("response_format"))
+        per = [dataclasses.replace(params, grammar=gf.json()) if gf else params for _ in range(n)]
+        results = await asyncio.gather(*[_run_one(st, prompt_ids, p, stops) for p in per])
         choices, completion_tokens = [], 0
         for i, (text, ids, reason, _) in enumerate(results):
             msg = {"role": "assistant", "content": text}
@@ -370,9 +396,14 @@ def create_app(st: ServerState) -> FastAPI:
         if body.get("stream"):
             if len(prompts) != 1:
                 raise HTTPException(status_code=400, detail="streaming supports a single prompt")
+            gf = st.format_factory(body.get("response_format"))
+            if gf:
+                params = dataclasses.replace(params, grammar=gf.json())
             return StreamingResponse(_completion_stream(st, rid, created, prompts[0], params, stops),
                                      media_type="text/event-stream")
-        results = await asyncio.gather(*[_run_one(st, p, params, stops) for p in prompts])
+        gf = st.format_factory(body.get("response_format"))
+        results = await asyncio.gather(*[_run_one(st, p, dataclasses.replace(params, grammar=gf.json()) if gf
+                                                  else params, stops) for p in prompts])
         echo = bool(body.get("echo"))
         choices, ptoks, ctoks = [], 0, 0
         for i, ((text, ids, reason, pt), p) in enumerate(zip(results, prompts)):
