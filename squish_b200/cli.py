@@ -34,7 +34,8 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
     p.add_argument("--device", default=None)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-dtype", "--kv-bits", dest="kv_dtype", default=None,
-                   choices=["bf16", "fp16", "int8", "int4", "int2", "k8v4"])
+                   choices=["bf16", "fp16", "int8", "int4", "int2", "k8v4", "auto"],
+                   help="auto: INT8 up to 8K-token contexts, INT4 to 16K, INT2 beyond (by --max-model-len)")
     p.add_argument("--max-num-seqs", "--batch-size", dest="max_num_seqs", type=int, default=e["max_num_seqs"])
     p.add_argument("--max-num-batched-tokens", "--chunk-prefill-size", dest="max_num_batched_tokens", type=int,
                    default=e["max_num_batched_tokens"])
@@ -58,6 +59,10 @@ def _ecfg(a):
 
 
 def _kv(a):
+    if a.kv_dtype == "auto":
+        from .kv.planning import auto_kv_mode
+
+        return auto_kv_mode(a.max_model_len)
     return {"fp16": "bf16"}.get(a.kv_dtype, a.kv_dtype)
 
 

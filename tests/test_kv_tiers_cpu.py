@@ -64,3 +64,27 @@ def test_disk_tier_persists_across_engines(tmp_path):
     (d / "manifest.json").write_text(json.dumps(man))
     eng3 = _eng(kv_host_bytes=1, kv_disk_dir=str(d))
     assert not eng3.blocks.tier.disk
+
+
+def test_kv_mode_selection_and_memory_planning():
+    import pytest
+
+    from squish_b200.kv.paged import KVPools
+    from squish_b200.kv.planning import (estimate_kv_memory, estimate_max_context, recommended_kv_mode,
+                                         recommended_kv_mode_3tier)
+    from squish_b200.models.config import QuantConfig, get_preset
+
+    assert recommended_kv_mode(4096) == "int8" and recommended_kv_mode(16384) == "int2"
+    assert [recommended_kv_mode_3tier(n) for n in (8192, 8193, 16384, 16385)] == ["int8", "int4", "int4", "int2"]
+    with pytest.raises(ValueError):
+        recommended_kv_mode(10, medium_mode="int4")
+    cfg, q = get_preset("tiny-llama")
+    for mode in ("bf16", "int8", "int4", "int2", "k8v4"):
+        est = estimate_kv_memory(cfg, 1000, mode, sequences=3)
+        qq = QuantConfig(**{**q.__dict__, "kv_dtype": mode})
+        pools = KVPools(cfg, qq, est.pages, "cpu")
+        assert pools.nbytes() == est.total_bytes, mode  # the estimate is the allocation
+        n = estimate_max_context(cfg, est.total_bytes, mode, sequences=3)
+        assert n >= 1000 and estimate_kv_memory(cfg, n, mode, 3).total_bytes <= est.total_bytes
+    e8, e2 = estimate_kv_memory(cfg, 4096, "int8"), estimate_kv_memory(cfg, 4096, "int2")
+    assert e2.total_bytes < e8.total_bytes / 2.5
