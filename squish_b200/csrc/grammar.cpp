@@ -328,6 +328,391 @@ class JsonMatcher {
   bool terminated_ = false;
 };
 
+// ------------------------------------------------------------------------ schema-guided
+// A JSON schema subset compiled to a node table (by serving/grammar.py): object (listed
+// properties only, each at most once, `required` enforced before '}'), array (items), string,
+// integer, number, boolean, null, enum / const (serialized literals), and any (generic JSON).
+// The stack keeps per frame the object's node, the node of the member value being read and the
+// set of properties already used; depth is limited to 16.
+enum Kind : uint8_t { K_ANY, K_OBJECT, K_ARRAY, K_STRING, K_INTEGER, K_NUMBER, K_BOOLEAN, K_NULL, K_ENUM };
+
+struct SchemaNode {
+  uint8_t kind = K_ANY;
+  std::vector<std::string> names;  // object property names (raw key bytes)
+  std::vector<int> props;          // their nodes
+  uint64_t required = 0;
+  int items = -1;                  // array items node (-1: any)
+  std::vector<std::string> lits;   // enum literals, serialized JSON
+};
+
+class Schema {
+ public:
+  Schema(const std::vector<int64_t>& kinds, const std::vector<std::vector<std::pair<pybind11::bytes, int64_t>>>& props,
+         const std::vector<int64_t>& required, const std::vector<int64_t>& items,
+         const std::vector<std::vector<pybind11::bytes>>& lits, int64_t root)
+      : root_((int)root) {
+    const size_t n = kinds.size();
+    TORCH_CHECK(props.size() == n && required.size() == n && items.size() == n && lits.size() == n,
+                "schema tables must have one entry per node");
+    TORCH_CHECK(n >= 1 && n < 65535 && root >= 0 && (size_t)root < n, "bad schema root / size");
+    nodes_.resize(n);
+    for (size_t i = 0; i < n; ++i) {
+      SchemaNode& d = nodes_[i];
+      d.kind = (uint8_t)kinds[i];
+      TORCH_CHECK(props[i].size() <= 64, "at most 64 properties per object");
+      for (const auto& pr : props[i]) {
+        d.names.push_back(std::string(pr.first));
+        TORCH_CHECK(pr.second >= 0 && (size_t)pr.second < n, "property node out of range");
+        d.props.push_back((int)pr.second);
+      }
+      d.required = (uint64_t)required[i];
+      d.items = (int)items[i];
+      TORCH_CHECK(lits[i].size() <= 64, "at most 64 enum values");
+      for (const auto& l : lits[i]) d.lits.push_back(std::string(l));
+    }
+  }
+  const SchemaNode& node(int i) const { return nodes_[i]; }
+  int root() const { return root_; }
+
+ private:
+  std::vector<SchemaNode> nodes_;
+  int root_;
+};
+
+namespace {
+
+constexpr int kSDepth = 16;
+constexpr uint16_t kAnyNode = 0xFFFF;  // generic JSON below this point
+enum : uint8_t { L_SKEY = 32, L_ENUM = 33 };
+
+struct SState {
+  uint8_t f[kSDepth];
+  uint16_t node[kSDepth];   // schema node of the container
+  uint16_t vnode[kSDepth];  // object frames: node of the member value being read
+  uint64_t used[kSDepth];   // object frames: properties already present
+  uint64_t cand = 0;        // key / enum candidates
+  int8_t depth = 0;
+  uint8_t lex = L_STRUCT, lit = 0, lit_pos = 0, key = 0, done = 0, ws_run = 0, max_ws = 24;
+  uint8_t cpos = 0, num_int = 0;
+  uint16_t enode = 0;       // enum node being matched
+};
+
+inline const SchemaNode* sn(const Schema& sc, uint16_t id) { return id == kAnyNode ? nullptr : &sc.node(id); }
+
+inline uint16_t expected(const Schema& sc, const SState& s) {
+  if (s.depth == 0) return (uint16_t)sc.root();
+  const uint8_t f = s.f[s.depth - 1];
+  if (f <= F_OBJ_AFTER) return s.vnode[s.depth - 1];
+  const SchemaNode* n = sn(sc, s.node[s.depth - 1]);
+  return (n == nullptr || n->items < 0) ? kAnyNode : (uint16_t)n->items;
+}
+
+inline void s_value_done(SState& s) {
+  s.lex = L_STRUCT;
+  if (s.depth == 0) {
+    s.done = 1;
+    return;
+  }
+  uint8_t& f = s.f[s.depth - 1];
+  f = f == F_OBJ_VALUE ? F_OBJ_AFTER : F_ARR_AFTER;
+}
+
+inline bool s_push(SState& s, uint8_t f, uint16_t node) {
+  if (s.depth >= kSDepth) return false;
+  s.f[s.depth] = f;
+  s.node[s.depth] = node;
+  s.vnode[s.depth] = kAnyNode;
+  s.used[s.depth] = 0;
+  ++s.depth;
+  return true;
+}
+
+bool s_start_value(const Schema& sc, SState& s, uint8_t c) {
+  const uint16_t id = expected(sc, s);
+  const SchemaNode* n = sn(sc, id);
+  const uint8_t k = n == nullptr ? K_ANY : n->kind;
+  s.num_int = k == K_INTEGER;
+  switch (k) {
+    case K_OBJECT: return c == '{' && s_push(s, F_OBJ_KEY_OR_END, id);
+    case K_ARRAY: return c == '[' && s_push(s, F_ARR_VALUE_OR_END, id);
+    case K_STRING:
+      if (c != '"') return false;
+      s.lex = L_STR;
+      s.key = 0;
+      return true;
+    case K_INTEGER:
+    case K_NUMBER:
+      if (c == '-') { s.lex = L_NUM_MINUS; return true; }
+      if (c == '0') { s.lex = L_NUM_ZERO; return true; }
+      if (c >= '1' && c <= '9') { s.lex = L_NUM_INT; return true; }
+      return false;
+    case K_BOOLEAN:
+      if (c == 't') { s.lex = L_LIT; s.lit = 0; s.lit_pos = 1; return true; }
+      if (c == 'f') { s.lex = L_LIT; s.lit = 1; s.lit_pos = 1; return true; }
+      return false;
+    case K_NULL:
+      if (c != 'n') return false;
+      s.lex = L_LIT;
+      s.lit = 2;
+      s.lit_pos = 1;
+      return true;
+    case K_ENUM: {
+      uint64_t m = 0;
+      for (size_t i = 0; i < n->lits.size(); ++i)
+        if (!n->lits[i].empty() && (uint8_t)n->lits[i][0] == c) m |= 1ull << i;
+      if (!m) return false;
+      s.lex = L_ENUM;
+      s.enode = id;
+      s.cand = m;
+      s.cpos = 1;
+      return true;
+    }
+    default:  // any JSON value; containers below it are generic
+      switch (c) {
+        case '{': return s_push(s, F_OBJ_KEY_OR_END, kAnyNode);
+        case '[': return s_push(s, F_ARR_VALUE_OR_END, kAnyNode);
+        case '"': s.lex = L_STR; s.key = 0; return true;
+        case '-': s.lex = L_NUM_MINUS; return true;
+        case '0': s.lex = L_NUM_ZERO; return true;
+        case 't': s.lex = L_LIT; s.lit = 0; s.lit_pos = 1; return true;
+        case 'f': s.lex = L_LIT; s.lit = 1; s.lit_pos = 1; return true;
+        case 'n': s.lex = L_LIT; s.lit = 2; s.lit_pos = 1; return true;
+        default:
+          if (c >= '1' && c <= '9') { s.lex = L_NUM_INT; return true; }
+          return false;
+      }
+  }
+}
+
+inline bool s_obj_can_close(const Schema& sc, const SState& s) {
+  const SchemaNode* n = sn(sc, s.node[s.depth - 1]);
+  return n == nullptr || (n->required & ~s.used[s.depth - 1]) == 0;
+}
+
+inline bool s_obj_has_free_key(const Schema& sc, const SState& s) {
+  const SchemaNode* n = sn(sc, s.node[s.depth - 1]);
+  if (n == nullptr) return true;
+  const uint64_t all = n->names.size() >= 64 ? ~0ull : ((1ull << n->names.size()) - 1);
+  return (all & ~s.used[s.depth - 1]) != 0;
+}
+
+bool s_close(const Schema& sc, SState& s, uint8_t c) {
+  const bool obj = s.f[s.depth - 1] <= F_OBJ_AFTER;
+  if (obj ? c != '}' : c != ']') return false;
+  if (obj && !s_obj_can_close(sc, s)) return false;
+  --s.depth;
+  s_value_done(s);
+  return true;
+}
+
+bool s_step_struct(const Schema& sc, SState& s, uint8_t c) {
+  if (is_ws(c)) {
+    if (s.ws_run >= s.max_ws) return false;
+    ++s.ws_run;
+    return true;
+  }
+  s.ws_run = 0;
+  if (s.depth == 0) return s.done ? false : s_start_value(sc, s, c);
+  uint8_t& f = s.f[s.depth - 1];
+  switch (f) {
+    case F_OBJ_KEY_OR_END:
+      if (c == '}') return s_close(sc, s, c);
+      [[fallthrough]];
+    case F_OBJ_KEY: {
+      if (c != '"') return false;
+      const SchemaNode* n = sn(sc, s.node[s.depth - 1]);
+      if (n == nullptr) {
+        s.lex = L_STR;
+        s.key = 1;
+        return true;
+      }
+      const uint64_t all = n->names.size() >= 64 ? ~0ull : ((1ull << n->names.size()) - 1);
+      s.cand = all & ~s.used[s.depth - 1];
+      if (!s.cand) return false;
+      s.lex = L_SKEY;
+      s.cpos = 0;
+      return true;
+    }
+    case F_OBJ_COLON:
+      if (c != ':') return false;
+      f = F_OBJ_VALUE;
+      return true;
+    case F_OBJ_VALUE:
+    case F_ARR_VALUE:
+      return s_start_value(sc, s, c);
+    case F_ARR_VALUE_OR_END:
+      if (c == ']') return s_close(sc, s, c);
+      return s_start_value(sc, s, c);
+    case F_OBJ_AFTER:
+      if (c == ',') {
+        if (!s_obj_has_free_key(sc, s)) return false;
+        f = F_OBJ_KEY;
+        return true;
+      }
+      return s_close(sc, s, c);
+    case F_ARR_AFTER:
+      if (c == ',') { f = F_ARR_VALUE; return true; }
+      return s_close(sc, s, c);
+  }
+  return false;
+}
+
+inline bool s_end_number(const Schema& sc, SState& s, uint8_t c) {
+  s_value_done(s);
+  return s_step_struct(sc, s, c);
+}
+
+bool s_step(const Schema& sc, SState& s, uint8_t c) {
+  switch (s.lex) {
+    case L_STRUCT: return s_step_struct(sc, s, c);
+    case L_SKEY: {
+      const SchemaNode& n = sc.node(s.node[s.depth - 1]);
+      if (c == '"') {
+        for (size_t i = 0; i < n.names.size(); ++i)
+          if (((s.cand >> i) & 1) && n.names[i].size() == s.cpos) {
+            s.used[s.depth - 1] |= 1ull << i;
+            s.vnode[s.depth - 1] = (uint16_t)n.props[i];
+            s.f[s.depth - 1] = F_OBJ_COLON;
+            s.lex = L_STRUCT;
+            return true;
+          }
+        return false;
+      }
+      uint64_t m = 0;
+      for (size_t i = 0; i < n.names.size(); ++i)
+        if (((s.cand >> i) & 1) && s.cpos < n.names[i].size() && (uint8_t)n.names[i][s.cpos] == c) m |= 1ull << i;
+      if (!m) return false;
+      s.cand = m;
+      ++s.cpos;
+      return true;
+    }
+    case L_ENUM: {
+      const SchemaNode& n = sc.node(s.enode);
+      uint64_t m = 0;
+      bool complete = false;
+      for (size_t i = 0; i < n.lits.size(); ++i) {
+        if (!((s.cand >> i) & 1)) continue;
+        if (s.cpos < n.lits[i].size() && (uint8_t)n.lits[i][s.cpos] == c) m |= 1ull << i;
+        if (n.lits[i].size() == s.cpos) complete = true;
+      }
+      if (m) {
+        s.cand = m;
+        ++s.cpos;
+        // a quoted literal ends with its closing quote; other literals end at the next byte
+        for (size_t i = 0; i < n.lits.size(); ++i)
+          if (((m >> i) & 1) && n.lits[i].size() == s.cpos && n.lits[i].back() == '"') {
+            bool longer = false;
+            for (size_t j = 0; j < n.lits.size(); ++j) longer = longer || (((m >> j) & 1) && n.lits[j].size() > s.cpos);
+            if (!longer) s_value_done(s);
+            break;
+          }
+        return true;
+      }
+      if (!complete) return false;
+      s_value_done(s);
+      return s_step_struct(sc, s, c);
+    }
+    case L_STR:
+      if (c == '"') {
+        if (s.key) {
+          s.lex = L_STRUCT;
+          s.f[s.depth - 1] = F_OBJ_COLON;
+          s.vnode[s.depth - 1] = kAnyNode;
+        } else {
+          s_value_done(s);
+        }
+        return true;
+      }
+      if (c == '\\') { s.lex = L_ESC; return true; }
+      return c >= 0x20;
+    case L_NUM_ZERO:
+      if (s.num_int && (c == '.' || c == 'e' || c == 'E')) return false;
+      if (c == '.') { s.lex = L_NUM_DOT; return true; }
+      if (c == 'e' || c == 'E') { s.lex = L_NUM_E; return true; }
+      if (is_digit(c)) return false;
+      return s_end_number(sc, s, c);
+    case L_NUM_INT:
+      if (is_digit(c)) return true;
+      if (s.num_int && (c == '.' || c == 'e' || c == 'E')) return false;
+      if (c == '.') { s.lex = L_NUM_DOT; return true; }
+      if (c == 'e' || c == 'E') { s.lex = L_NUM_E; return true; }
+      return s_end_number(sc, s, c);
+    case L_NUM_FRAC:
+      if (is_digit(c)) return true;
+      if (c == 'e' || c == 'E') { s.lex = L_NUM_E; return true; }
+      return s_end_number(sc, s, c);
+    case L_NUM_EXP:
+      if (is_digit(c)) return true;
+      return s_end_number(sc, s, c);
+    case L_LIT:
+      if (c != (uint8_t)kLits[s.lit][s.lit_pos]) return false;
+      if (++s.lit_pos == kLitLen[s.lit]) s_value_done(s);
+      return true;
+    default: {
+      // escapes, \u digits and the number states that cannot end a value: the generic rules
+      State g;
+      g.lex = s.lex;
+      if (!step(g, c)) return false;
+      s.lex = g.lex;
+      return true;
+    }
+  }
+}
+
+inline bool s_complete(const SState& s) { return s.depth == 0 && s.done && s.lex == L_STRUCT; }
+
+}  // namespace
+
+class SchemaMatcher {
+ public:
+  SchemaMatcher(std::shared_ptr<VocabIndex> vi, std::shared_ptr<Schema> sc, int64_t max_ws)
+      : vi_(std::move(vi)), sc_(std::move(sc)) {
+    s_.max_ws = (uint8_t)std::min<int64_t>(std::max<int64_t>(max_ws, 1), 255);
+  }
+  bool advance(int64_t tok) {
+    if (tok == vi_->eos()) {
+      if (!s_complete(s_)) return false;
+      terminated_ = true;
+      return true;
+    }
+    if (tok < 0 || tok >= (int64_t)vi_->vocab() || vi_->bytes_of(tok).empty()) return false;
+    SState t = s_;
+    for (unsigned char c : vi_->bytes_of(tok))
+      if (!s_step(*sc_, t, c)) return false;
+    s_ = t;
+    return true;
+  }
+  bool is_complete() const { return s_complete(s_); }
+  bool is_terminated() const { return terminated_ || s_complete(s_); }
+  torch::Tensor allowed_mask() const {
+    const int words = (vi_->vocab() + 31) / 32;
+    auto out = torch::zeros({words}, torch::kInt32);
+    uint32_t* m = reinterpret_cast<uint32_t*>(out.data_ptr<int32_t>());
+    if (s_.lex == L_STR) {  // free string content: the plain-string tokens, then the others
+      std::memcpy(m, vi_->plain().data(), sizeof(uint32_t) * words);
+      walk(vi_->special(), 0, s_, m);
+    } else {
+      walk(vi_->full(), 0, s_, m);
+    }
+    const int e = vi_->eos();
+    if (s_complete(s_) && e >= 0 && e < vi_->vocab()) m[e >> 5] |= 1u << (e & 31);
+    return out;
+  }
+
+ private:
+  void walk(const std::vector<VocabIndex::Node>& t, int n, const SState& s, uint32_t* m) const {
+    for (int id : t[n].ends) m[id >> 5] |= 1u << (id & 31);
+    for (const auto& kc : t[n].kids) {
+      SState c = s;
+      if (s_step(*sc_, c, kc.first)) walk(t, kc.second, c, m);
+    }
+  }
+  std::shared_ptr<VocabIndex> vi_;
+  std::shared_ptr<Schema> sc_;
+  SState s_;
+  bool terminated_ = false;
+};
+
 void register_grammar(pybind11::module& m) {
   auto g = m.def_submodule("grammar", "JSON-constrained decoding: token bitmasks");
   pybind11::class_<VocabIndex, std::shared_ptr<VocabIndex>>(g, "VocabIndex")
@@ -346,6 +731,18 @@ void register_grammar(pybind11::module& m) {
       .def("allowed_mask", &JsonMatcher::allowed_mask)
       .def("is_complete", &JsonMatcher::is_complete)
       .def("is_terminated", &JsonMatcher::is_terminated);
+  pybind11::class_<Schema, std::shared_ptr<Schema>>(g, "Schema")
+      .def(pybind11::init<const std::vector<int64_t>&,
+                          const std::vector<std::vector<std::pair<pybind11::bytes, int64_t>>>&,
+                          const std::vector<int64_t>&, const std::vector<int64_t>&,
+                          const std::vector<std::vector<pybind11::bytes>>&, int64_t>());
+  pybind11::class_<SchemaMatcher>(g, "SchemaMatcher")
+      .def(pybind11::init<std::shared_ptr<VocabIndex>, std::shared_ptr<Schema>, int64_t>(), pybind11::arg("index"),
+           pybind11::arg("schema"), pybind11::arg("max_ws") = 24)
+      .def("advance", &SchemaMatcher::advance)
+      .def("allowed_mask", &SchemaMatcher::allowed_mask)
+      .def("is_complete", &SchemaMatcher::is_complete)
+      .def("is_terminated", &SchemaMatcher::is_terminated);
 }
 
 }  // namespace sqgram

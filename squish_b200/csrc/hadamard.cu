@@ -7,11 +7,15 @@
 // matrices in NumPy at load time (squish/quant/sqint2.py:384-470); here the rotation is an
 // O(b log b) butterfly per block applied to the activations, so the weights stay 2-bit.
 //
-// One CTA per (block, row): the b values (times their signs) go to shared memory in fp32,
-// log2(b) butterfly stages run with a barrier between stages, and the scaled result is stored
-// as bf16. Up to 4096-wide blocks (16 KiB of shared memory).
+// Blocks up to 1024 wide: one warp per (row, block). Lane l holds the b/32 consecutive values
+// l*b/32 .. (l+1)*b/32 - 1 in registers: the butterfly stages over the low index bits run inside
+// each lane, the stages over the high (lane) bits exchange registers with __shfl_xor_sync --
+// no shared memory, no barriers; loads and stores are 16-byte vectors covering the block.
+// Wider blocks (2048, 4096) use a shared-memory CTA per (block, row).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+
+#include <cstdint>
 
 #include "kernels.h"
 #include "launch.cuh"
@@ -45,12 +49,102 @@ __global__ void __launch_bounds__(512) hadamard_rows_kernel(const __nv_bfloat16*
   for (int i = tid; i < b; i += nt) yr[i] = __float2bfloat16(v[i] * scale);
 }
 
+template <int VPL>  // values per lane: b = 32 * VPL
+__global__ void __launch_bounds__(256) hadamard_warp_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
+                                                            __nv_bfloat16* __restrict__ y, int ldy,
+                                                            const float* __restrict__ signs, int nblk, int rows,
+                                                            float scale) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const long w = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w >= (long)rows * nblk) return;  // uniform per warp
+  const int row = (int)(w / nblk), blk = (int)(w % nblk);
+  const int col0 = blk * 32 * VPL + lane * VPL;
+  const __nv_bfloat16* xr = x + (size_t)row * ldx + col0;
+  float v[VPL];
+  if constexpr (VPL >= 8) {
+#pragma unroll
+    for (int c = 0; c < VPL / 8; ++c) {
+      const uint4 u = *reinterpret_cast<const uint4*>(xr + 8 * c);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        v[8 * c + 2 * e] = f.x;
+        v[8 * c + 2 * e + 1] = f.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < VPL; ++r) v[r] = __bfloat162float(xr[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < VPL; ++r) v[r] *= signs[col0 + r];
+#pragma unroll
+  for (int h = 1; h < VPL; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      if (i & h) continue;
+      const float a = v[i], c = v[i + h];
+      v[i] = a + c;
+      v[i + h] = a - c;
+    }
+  }
+#pragma unroll
+  for (int hl = 1; hl < 32; hl <<= 1) {
+    const bool upper = lane & hl;
+#pragma unroll
+    for (int r = 0; r < VPL; ++r) {
+      const float o = __shfl_xor_sync(0xffffffffu, v[r], hl);
+      v[r] = upper ? o - v[r] : v[r] + o;
+    }
+  }
+  __nv_bfloat16* yr = y + (size_t)row * ldy + col0;
+  if constexpr (VPL >= 8) {
+#pragma unroll
+    for (int c = 0; c < VPL / 8; ++c) {
+      uint4 u;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * c + 2 * e] * scale, v[8 * c + 2 * e + 1] * scale);
+      *reinterpret_cast<uint4*>(yr + 8 * c) = u;
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < VPL; ++r) yr[r] = __float2bfloat16(v[r] * scale);
+  }
+}
+
+template <int VPL>
+cudaError_t launch_warp(const __nv_bfloat16* x, int ldx, __nv_bfloat16* y, int ldy, const float* signs, int M, int K,
+                        cudaStream_t s) {
+  const int b = 32 * VPL, nblk = K / b;
+  const long warps = (long)M * nblk;
+  const unsigned blocks = (unsigned)((warps + 7) / 8);
+  SQ_LAUNCH(hadamard_warp_kernel<VPL>, dim3(blocks), dim3(256), 0, s, 1, x, ldx, y, ldy, signs, nblk, M,
+            1.0f / sqrtf((float)b));
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t hadamard_rows_launch(const __nv_bfloat16* x, int ldx, __nv_bfloat16* y, int ldy, const float* signs,
                                  int M, int K, int b, cudaStream_t s) {
   if (M == 0 || K == 0) return cudaSuccess;
   if (b < 2 || b > 4096 || (b & (b - 1)) != 0 || K % b != 0) return cudaErrorInvalidValue;
+  // the register path needs 16-byte aligned rows for its vector accesses (from 256-wide blocks)
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0 &&
+                      ldx % 8 == 0 && ldy % 8 == 0;
+  switch (b) {
+    case 32: return launch_warp<1>(x, ldx, y, ldy, signs, M, K, s);
+    case 64: return launch_warp<2>(x, ldx, y, ldy, signs, M, K, s);
+    case 128: return launch_warp<4>(x, ldx, y, ldy, signs, M, K, s);
+    case 256: if (vec_ok) return launch_warp<8>(x, ldx, y, ldy, signs, M, K, s); break;
+    case 512: if (vec_ok) return launch_warp<16>(x, ldx, y, ldy, signs, M, K, s); break;
+    case 1024: if (vec_ok) return launch_warp<32>(x, ldx, y, ldy, signs, M, K, s); break;
+    default: break;
+  }
   const dim3 grid(K / b, M);
   const int threads = b / 2 < 512 ? b / 2 : 512;
   SQ_LAUNCH(hadamard_rows_kernel, grid, dim3(threads), sizeof(float) * (size_t)b, s, 1, x, ldx, y, ldy, signs, b,

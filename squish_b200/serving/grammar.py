@@ -13,6 +13,8 @@ and are never allowed inside JSON (EOS is allowed once the document is complete)
 """
 from __future__ import annotations
 
+import json
+
 import numpy as np
 
 from .._ext import native
@@ -83,6 +85,81 @@ class JsonGrammar:
         return self.m.is_terminated()
 
 
+K_ANY, K_OBJECT, K_ARRAY, K_STRING, K_INTEGER, K_NUMBER, K_BOOLEAN, K_NULL, K_ENUM = range(9)
+
+
+def compile_schema(schema: dict):
+    """JSON schema -> ``_C.grammar.Schema`` node table. Supported: ``type`` object (``properties``,
+    ``required``; only listed properties may appear, each once), array (``items``), string,
+    integer, number, boolean, null; ``enum`` / ``const`` (literal values); local ``$ref``
+    (``#/$defs/..``, ``#/definitions/..``). ``anyOf`` / ``oneOf`` / type lists and an object
+    without ``properties`` accept any JSON value of the allowed shape (no constraint)."""
+    kinds, props, required, items, lits = [], [], [], [], []
+    memo: dict[int, int] = {}
+
+    def resolve(node):
+        seen = 0
+        while isinstance(node, dict) and "$ref" in node:
+            ref = node["$ref"]
+            if not ref.startswith("#/"):
+                raise ValueError(f"only local $ref is supported, got {ref!r}")
+            cur = schema
+            for part in ref[2:].split("/"):
+                cur = cur[part]
+            node = cur
+            seen += 1
+            if seen > 64:
+                raise ValueError("$ref cycle")
+        return node
+
+    def add(node) -> int:
+        node = resolve(node) if isinstance(node, dict) else {}
+        key = id(node)
+        if key in memo:
+            return memo[key]
+        i = len(kinds)
+        memo[key] = i
+        kinds.append(K_ANY)
+        props.append([])
+        required.append(0)
+        items.append(-1)
+        lits.append([])
+        if "const" in node or "enum" in node:
+            vals = [node["const"]] if "const" in node else list(node["enum"])
+            if len(vals) > 64:
+                raise ValueError("at most 64 enum values")
+            kinds[i] = K_ENUM
+            lits[i] = [json.dumps(v, separators=(",", ":"), ensure_ascii=False).encode() for v in vals]
+            return i
+        t = node.get("type")
+        if t == "object" and isinstance(node.get("properties"), dict) and node["properties"]:
+            names = list(node["properties"])
+            if len(names) > 64:
+                raise ValueError("at most 64 properties per object")
+            kinds[i] = K_OBJECT
+            req = set(node.get("required", []))
+            required[i] = sum(1 << j for j, nm in enumerate(names) if nm in req)
+            props[i] = [(nm.encode(), add(node["properties"][nm])) for nm in names]
+        elif t == "array":
+            kinds[i] = K_ARRAY
+            if isinstance(node.get("items"), dict):
+                items[i] = add(node["items"])
+        elif t in ("string", "integer", "number", "boolean", "null"):
+            kinds[i] = {"string": K_STRING, "integer": K_INTEGER, "number": K_NUMBER, "boolean": K_BOOLEAN,
+                        "null": K_NULL}[t]
+        return i
+
+    root = add(schema)
+    return native().grammar.Schema(kinds, props, required, items, lits, root)
+
+
+class SchemaGrammar(JsonGrammar):
+    """JSON constrained by a compiled schema (same interface as :class:`JsonGrammar`)."""
+
+    def __init__(self, index, schema):  # noqa: super().__init__ is replaced, not extended
+        self.m = native().grammar.SchemaMatcher(index, schema)
+
+
 class GrammarFactory:
     """Builds the vocabulary index once per tokenizer and hands out fresh matchers."""
 
@@ -92,6 +169,18 @@ class GrammarFactory:
 
     def json(self, top_object: bool = True) -> JsonGrammar:
         return JsonGrammar(self.index, top_object)
+
+    def schema(self, schema: dict) -> SchemaGrammar:
+        return SchemaGrammar(self.index, compile_schema(schema))
+
+
+def grammar_for(factory: "GrammarFactory", response_format):
+    """A fresh grammar for an OpenAI ``response_format`` (None: unconstrained)."""
+    if not wants_json(response_format):
+        return None
+    js = response_format.get("json_schema") if response_format.get("type") == "json_schema" else None
+    sch = js.get("schema") if isinstance(js, dict) else None
+    return factory.schema(sch) if isinstance(sch, dict) and sch else factory.json()
 
 
 def wants_json(response_format) -> bool | None:

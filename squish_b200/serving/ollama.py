@@ -130,8 +130,10 @@ def mount_ollama(app: FastAPI, st) -> None:
             text = apply_chat_template(msgs, st.tok, st.arch)
         prompt_ids = list(body.get("context") or []) + st.tok.encode(text)
         params, stops = _params(body, st.tok.eos_token_id)
-        if body.get("format") == "json" or isinstance(body.get("format"), dict):
+        if body.get("format") == "json":
             params.grammar = st.grammar_factory().json()
+        elif isinstance(body.get("format"), dict):  # a JSON schema
+            params.grammar = st.grammar_factory().schema(body["format"])
         stream = body.get("stream", True)
 
         async def lines():
@@ -163,8 +165,10 @@ def mount_ollama(app: FastAPI, st) -> None:
         t_start = time.perf_counter()
         prompt_ids = st.tok.encode(apply_chat_template(msgs, st.tok, st.arch, tools=tools))
         params, stops = _params(body, st.tok.eos_token_id)
-        if body.get("format") == "json" or isinstance(body.get("format"), dict):
+        if body.get("format") == "json":
             params.grammar = st.grammar_factory().json()
+        elif isinstance(body.get("format"), dict):  # a JSON schema
+            params.grammar = st.grammar_factory().schema(body["format"])
 
         async def lines():
             async for delta, done, reason, n_out, t_first in _gen(prompt_ids, params, stops, True, t_start):

@@ -60,14 +60,24 @@ class ServerState:
         return self._grammar
 
     def format_factory(self, response_format):
-        """A fresh JSON grammar per use when ``response_format`` asks for JSON (None otherwise)."""
-        from .grammar import wants_json
+        """Something whose ``json()`` gives a fresh grammar for ``response_format`` (JSON object,
+        or a JSON schema), or None when the output is unconstrained."""
+        from .grammar import grammar_for, wants_json
 
         try:
-            want = wants_json(response_format)
-        except ValueError as exc:
-            raise HTTPException(status_code=400, detail=str(exc)) from exc
-        return None if not want else self.grammar_factory()
+            if not wants_json(response_format):
+                return None
+            grammar_for(self.grammar_factory(), response_format)  # validates the schema once
+        except (ValueError, KeyError, TypeError) as exc:
+            raise HTTPException(status_code=400, detail=f"response_format: {exc}") from exc
+        fac = self.grammar_factory()
+
+        class _Per:
+            @staticmethod
+            def json():
+                return grammar_for(fac, response_format)
+
+        return _Per
 
 
 def _check_auth(request: Request, st: ServerState) -> None:

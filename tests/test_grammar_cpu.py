@@ -121,3 +121,93 @@ def test_response_format_over_http():
             assert o["response"].lstrip().startswith("{")
     finally:
         aeng.stop()
+
+
+SCHEMA = {"type": "object", "$defs": {"tag": {"enum": ["a", "bb", 3, True]}},
+          "properties": {"name": {"type": "string"}, "age": {"type": "integer"},
+                         "tags": {"type": "array", "items": {"$ref": "#/$defs/tag"}}, "ok": {"type": "boolean"},
+                         "pos": {"type": "object", "properties": {"x": {"type": "number"}}, "required": ["x"]},
+                         "any": {}},
+          "required": ["name", "age"]}
+
+
+@pytest.mark.parametrize("text,want", [
+    ('{"name": "x", "age": 3}', True),
+    ('{"age": 3, "name": "x", "tags": ["a", 3, "bb", true]}', True),
+    ('{"name":"x","age":-0,"ok":false,"pos":{"x":1.5e3},"any":[{"q":null}]}', True),
+    ('{"name": "x"}', False), ('{"name": 1, "age": 2}', False), ('{"age": 1.5, "name": "x"}', False),
+    ('{"nam": "x", "age": 1}', False), ('{"name": "x", "age": 1, "zzz": 1}', False),
+    ('{"name": "x", "age": 1, "tags": ["c"]}', False), ('{"name": "x", "name": "y", "age": 1}', False),
+    ('{"name": "x", "age": 1, "pos": {}}', False), ('{"name": "x", "age": 1, "tags": [33]}', False),
+])
+def test_schema_matcher(text, want):
+    g = GrammarFactory(ByteTokenizer(300, 2), 300, 2).schema(SCHEMA)
+    ok = _feed(g, text) and g.is_complete()
+    assert ok == want, text
+    if want:
+        assert json.loads(text)
+
+
+def test_schema_masks_agree_with_stepwise_advance():
+    from squish_b200.serving.grammar import compile_schema
+
+    rng = random.Random(2)
+    alphabet = ['{', '}', '[', ']', '"', ':', ',', ' ', 'name', 'age', '"name"', '"age": ', '": "', 'a', 'bb', '3',
+                '1', '.', '5', 'true', 'false', 'null', '"tags": [', '"a"', '"bb"', 'x', '"ok":', '"pos": {"x": ']
+    vocab = [b""] * 3 + [t.encode() for t in alphabet]
+    idx = native().grammar.VocabIndex(vocab, 2)
+    sc = compile_schema(SCHEMA)
+    for trial in range(25):
+        hist = []
+        g = native().grammar.SchemaMatcher(idx, sc)
+        for step in range(30):
+            m = g.allowed_mask().numpy().view(np.uint32)
+            allowed = {t for t in range(len(vocab)) if (m[t >> 5] >> (t & 31)) & 1}
+            for t in range(3, len(vocab)):
+                probe = native().grammar.SchemaMatcher(idx, sc)
+                for h in hist:
+                    assert probe.advance(h)
+                assert probe.advance(t) == (t in allowed)
+            choices = sorted(allowed - {2})
+            if not choices:
+                break
+            t = rng.choice(choices)
+            hist.append(t)
+            assert g.advance(t)
+
+
+def test_json_schema_over_http():
+    from fastapi.testclient import TestClient
+
+    from squish_b200.engine.engine import EngineConfig, LLMEngine
+    from squish_b200.models.config import get_preset
+    from squish_b200.models.weights import random_checkpoint
+    from squish_b200.serving.async_engine import AsyncEngine
+    from squish_b200.serving.server import ServerState, create_app
+
+    cfg, q = get_preset("tiny-llama")
+    eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), "cpu",
+                                    EngineConfig(max_num_seqs=4, max_model_len=512, num_pages=128))
+    aeng = AsyncEngine(eng, ByteTokenizer(cfg.vocab_size, cfg.eos_token_id), model_name="tiny").start()
+    schema = {"type": "object", "properties": {"v": {"enum": ["yes", "no"]}, "n": {"type": "integer"}},
+              "required": ["v", "n"]}
+    try:
+        with TestClient(create_app(ServerState(aeng, "tiny", arch="llama"))) as c:
+            done = 0
+            for seed in range(4):
+                r = c.post("/v1/chat/completions", json={
+                    "messages": [{"role": "user", "content": "answer"}], "max_tokens": 80, "temperature": 1.0,
+                    "seed": seed, "response_format": {"type": "json_schema",
+                                                      "json_schema": {"name": "a", "schema": schema}}}).json()
+                text = r["choices"][0]["message"]["content"]
+                assert text.lstrip().startswith("{")
+                if r["choices"][0]["finish_reason"] == "stop":
+                    d = json.loads(text)
+                    assert set(d) == {"v", "n"} and d["v"] in ("yes", "no") and isinstance(d["n"], int)
+                    done += 1
+            bad = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
+                                                       "response_format": {"type": "json_schema", "json_schema": {
+                                                           "schema": {"$ref": "http://x/y"}}}})
+            assert bad.status_code == 400
+    finally:
+        aeng.stop()
