@@ -76,10 +76,24 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
              device: str | None = None, delete_source: bool = False, random_preset: str | None = None,
              seed: int = 0, kv_dtype: str = "int4", log=print, hqq: bool = False, awq: bool = False,
              awq_scales: str | None = None, awq_alpha: float = 0.5, awq_samples: int = 16,
-             awq_seq_len: int = 256) -> dict:
+             awq_seq_len: int = 256, super_weights: bool = True) -> dict:
     """``hqq``: half-quadratic refinement of INT4 / INT2 grids. ``awq`` (or ``awq_scales``, a
     directory of saved scales): activation-aware scaling of norm-fed projections before
-    quantization; calibration needs the whole fp32 model in memory once."""
+    quantization; calibration needs the whole fp32 model in memory once. ``super_weights``
+    (with ``mse_clip``): rows holding a super weight skip the clip search; the coordinates found
+    are written to ``super_weights.json``."""
+    from ..quant.super_weights import SuperWeightCalibrator, protect, save_coords
+
+    sw_cal = SuperWeightCalibrator() if (super_weights and mse_clip and kind == "q4a") else None
+    sw_found = []
+
+    def q4(name, w, t):
+        """the MSE-clipped tensor with super-weight rows re-quantized unclipped"""
+        if sw_cal is None or t.kind != "q4a":
+            return t
+        hits = sw_cal.scan_tensor(name, w)
+        sw_found.extend(hits)
+        return protect(t, w, {h.row for h in hits})
     out = Path(out_dir)
     td = out / "tensors"
     td.mkdir(parents=True, exist_ok=True)
@@ -171,6 +185,7 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
                     if should_quantize(name, tuple(w.shape)):
                         tkind = router.kind_for(name) if router is not None else kind
                         t = quantize(w if dev.type == "cuda" else w.float(), tkind, group_size, mse_clip, hqq=hqq)
+                        t = q4(name, w if dev.type == "cuda" else w.float(), t)
                         stats["n_quantized"] += 1
                     else:
                         t = QTensor("dense", tuple(w.shape), data=w.float().cpu())
@@ -190,6 +205,9 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
                       "generation_config.json", "vocab.json", "merges.txt"):
             if (src / extra).exists():
                 shutil.copy2(src / extra, out / extra)
+    if sw_cal is not None:
+        save_coords(sw_found, out / "super_weights.json")
+        stats["super_weights"] = len(sw_found)
     man_path.write_text(json.dumps(manifest, indent=2))
     progress_path.write_text(json.dumps({"completed_shards": done, "total_shards": max(len(shards), 1),
                                          "delete_source": delete_source}, indent=2))

@@ -398,3 +398,43 @@ def test_mixed_precision_router_and_compress(tmp_path, monkeypatch):
             assert k == {"int4": "q4a", "int3": "q3", "sqint2": "q2"}[f], (n, k)
     m = ReferenceModel(ck)
     assert torch.isfinite(m.forward([1, 2, 3], m.new_cache(), 0)).all()
+
+
+def test_super_weight_detection_and_protection(tmp_path):
+    from safetensors.torch import save_file
+
+    from squish_b200.io.convert import compress, load_checkpoint
+    from squish_b200.quant.super_weights import SuperWeightCalibrator, calibrate_from_dir, load_coords
+
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(64, 256, generator=g) * 0.02
+    w[5, 77] = 4.0  # ~250x the row's mean |w|
+    cal = SuperWeightCalibrator()
+    hits = cal.scan_tensor("model.layers.0.mlp.down_proj.weight", w)
+    assert [(h.row, h.col) for h in hits] == [(5, 77)] and hits[0].ratio > 100
+    assert cal.scan_tensor("model.embed_tokens.weight", w) == []
+    ln = torch.ones(256)
+    ln[3] = 9.0
+    assert [h.col for h in cal.scan_tensor("model.layers.0.input_layernorm.weight", ln)] == [3]
+    # a real HF-style source dir: the compress MSE path keeps the super weight exactly
+    from squish_b200.models.config import get_preset, to_hf_config
+
+    cfg, _ = get_preset("tiny-llama")
+    src = tmp_path / "src"
+    src.mkdir()
+    (src / "config.json").write_text(json.dumps(to_hf_config(cfg)))
+    from squish_b200.models.weights import random_checkpoint
+
+    ck = random_checkpoint(cfg, get_preset("tiny-llama")[1], seed=0)
+    tensors = {n: t.dequantize().float().contiguous() for n, t in ck.tensors.items() if n != "lm_head.weight"}
+    name = "model.layers.1.mlp.down_proj.weight"
+    tensors[name] = torch.randn(tensors[name].shape, generator=g) * 0.02
+    tensors[name][10, 100] = 5.0
+    save_file(tensors, str(src / "model.safetensors"))
+    assert any(c.tensor_name == name for c in calibrate_from_dir(str(src), device="cpu"))
+    st = compress(str(src), str(tmp_path / "out"), mse_clip=True, device="cpu", group_size=32, log=lambda *_: None)
+    assert st["super_weights"] >= 1
+    coords = load_coords(tmp_path / "out" / "super_weights.json")
+    assert any(c.tensor_name == name and (c.row, c.col) == (10, 100) for c in coords)
+    out, _ = load_checkpoint(str(tmp_path / "out"), "cpu")
+    assert abs(float(out.tensors[name].dequantize()[10, 100]) - 5.0) < 1e-3
