@@ -102,3 +102,40 @@ def test_sampled_decoding_runs_in_graphs(cuda):
                                        ignore_eos=True)] * 3)
     assert all(len(o) == 16 for o in out)
     assert all(0 <= t < cfg.vocab_size for o in out for t in o)
+
+
+def test_json_grammar_on_the_cuda_engine(cuda):
+    """The grammar mask reaches the fused sampler: every sampled token is one the JSON matcher
+    allows, and finished outputs parse."""
+    import json
+
+    from squish_b200.engine.engine import EngineConfig, LLMEngine
+    from squish_b200.engine.sampling import SamplingParams
+    from squish_b200.models.config import get_preset
+    from squish_b200.models.weights import random_checkpoint
+    from squish_b200.serving.grammar import GrammarFactory
+    from squish_b200.serving.tokenizer import ByteTokenizer
+
+    cfg, q = get_preset("tiny-llama")
+    eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0), cuda,
+                                    EngineConfig(max_num_seqs=4, max_model_len=256, num_pages=64))
+    tok = ByteTokenizer(cfg.vocab_size, cfg.eos_token_id)
+    gf = GrammarFactory(tok, cfg.vocab_size, cfg.eos_token_id)
+    schema = {"type": "object", "properties": {"a": {"type": "integer"}, "b": {"enum": ["x", "y"]}},
+              "required": ["a", "b"]}
+    params = [SamplingParams(max_tokens=64, temperature=1.0, seed=s, grammar=gf.json() if s % 2 else gf.schema(schema))
+              for s in range(4)]
+    rids = [eng.add_request(tok.encode("json:"), p) for p in params]
+    outs = {r: [] for r in rids}
+    while eng.has_unfinished():
+        for o in eng.step():
+            outs[o.rid].extend(o.new_tokens)
+    for r, p in zip(rids, params):
+        ids = [t for t in outs[r] if t != cfg.eos_token_id]
+        assert all(3 <= t < 259 for t in ids), ids  # only byte tokens: specials are masked out
+        text = tok.decode(ids)
+        assert text.lstrip().startswith("{"), text
+        if eng.requests[r].finish_reason == "stop":
+            d = json.loads(text)
+            if not p.seed % 2:
+                assert set(d) == {"a", "b"} and isinstance(d["a"], int) and d["b"] in ("x", "y")
