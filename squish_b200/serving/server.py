@@ -276,6 +276,86 @@ def create_app(st: ServerState) -> FastAPI:
         out["loops_stopped"] = st.aeng.loops_stopped
         return out
 
+    # ------------------------------------------------------------------ agent
+    def agent_registry():
+        if getattr(st, "agent", None) is None:
+            from ..agent.tools import ToolRegistry, register_builtin_tools
+
+            st.agent = ToolRegistry()
+            st.mcp = {}
+            register_builtin_tools(st.agent)
+        return st.agent
+
+    @app.get("/v1/agent/tools")
+    async def agent_tools(request: Request):
+        _check_auth(request, st)
+        return {"tools": agent_registry().to_openai_schemas()}
+
+    @app.get("/v1/agent/mcp")
+    async def agent_mcp_list(request: Request):
+        _check_auth(request, st)
+        agent_registry()
+        return {"servers": [{"id": k, "command": v["command"], "tools": v["tools"]} for k, v in st.mcp.items()]}
+
+    @app.post("/v1/agent/mcp")
+    async def agent_mcp_connect(request: Request):
+        """Start an MCP server (stdio) and register its tools."""
+        from ..agent.mcp import MCPClient, MCPError, register_mcp_tools
+
+        _check_auth(request, st)
+        body = await _json(request)
+        cmd = body.get("command")
+        if not cmd:
+            raise HTTPException(status_code=400, detail="Provide 'command' (an MCP server started over stdio)")
+        reg = agent_registry()
+        sid = body.get("id") or f"mcp{len(st.mcp) + 1}"
+        try:
+            cl = MCPClient(cmd, timeout=float(body.get("timeout", 30)))
+            await asyncio.to_thread(cl.start)
+            names = await asyncio.to_thread(register_mcp_tools, cl, reg, sid)
+        except (MCPError, OSError, ValueError) as exc:
+            raise HTTPException(status_code=502, detail=f"MCP connect failed: {exc}") from exc
+        st.mcp[sid] = {"client": cl, "command": cmd, "tools": names}
+        return {"id": sid, "tools": names}
+
+    @app.delete("/v1/agent/mcp/{sid}")
+    async def agent_mcp_disconnect(sid: str, request: Request):
+        _check_auth(request, st)
+        agent_registry()
+        ent = st.mcp.pop(sid, None)
+        if ent is None:
+            raise HTTPException(status_code=404, detail=f"no MCP server {sid!r}")
+        for n in ent["tools"]:
+            st.agent.unregister(n)
+        await asyncio.to_thread(ent["client"].close)
+        return {"id": sid, "disconnected": True}
+
+    @app.post("/v1/agent/run")
+    async def agent_run(request: Request):
+        """Multi-step tool-calling loop, streamed as SSE events."""
+        from ..agent.loop import run_agent
+
+        _check_auth(request, st)
+        body = await _json(request)
+        messages = body.get("messages")
+        if not isinstance(messages, list) or not messages:
+            raise HTTPException(status_code=400, detail="'messages' must be a non-empty list")
+        max_steps = max(1, min(parse_int(body.get("max_steps"), "max_steps", 10), 50))
+        params = sampling_from_openai(dict(body, max_tokens=body.get("max_tokens", 1024)), 1024,
+                                      [st.tok.eos_token_id] if st.tok.eos_token_id is not None else [])
+
+        async def generate(msgs, tools):
+            prompt = apply_chat_template(msgs, st.tok, st.arch, tools=tools)
+            text, _, _, _ = await _run_one(st, st.tok.encode(prompt), dataclasses.replace(params), [])
+            return text
+
+        async def events():
+            async for ev in run_agent(generate, agent_registry(), messages, body.get("tools") or [], max_steps):
+                yield _sse(ev)
+            yield b"data: [DONE]\n\n"
+
+        return StreamingResponse(events(), media_type="text/event-stream")
+
     @app.post("/v1/route")
     async def route(request: Request):
         """Task category and model-family hint of a prompt (rule-based, no model call)."""
