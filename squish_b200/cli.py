@@ -46,6 +46,10 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
     p.add_argument("--chunk-align", type=int, default=0, help="grid-aligned prefill chunks (bit-exact prefix reuse)")
     p.add_argument("--kv-host-gb", type=float, default=0.0, help="host-RAM tier for evicted prefix blocks")
     p.add_argument("--kv-disk-dir", default=None, help="disk tier (persists prefix blocks across restarts)")
+    p.add_argument("--compress-prompt", action="store_true", help="extractive compression of long user messages")
+    p.add_argument("--compress-ratio", type=float, default=0.5)
+    p.add_argument("--compress-min-tokens", type=int, default=256)
+    p.add_argument("--compress-preserve-tokens", type=int, default=0)
 
 
 def _ecfg(a):
@@ -81,7 +85,10 @@ def cmd_serve(a) -> int:
     loaded = load_engine(_model(a), a.device, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a))
     aeng = AsyncEngine(loaded.engine, loaded.tokenizer, max_pending=c["max_pending"], model_name=loaded.name).start()
     key = a.api_key if a.api_key is not None else os.environ.get("SQUISH_API_KEY", c["api_key"])
-    st = ServerState(aeng, loaded.name, api_key=key or None, arch=loaded.engine.cfg.arch, load_time_s=loaded.load_s)
+    cp = ({"ratio": a.compress_ratio, "min_tokens": a.compress_min_tokens,
+           "preserve_tokens": a.compress_preserve_tokens} if getattr(a, "compress_prompt", False) else None)
+    st = ServerState(aeng, loaded.name, api_key=key or None, arch=loaded.engine.cfg.arch, load_time_s=loaded.load_s,
+                     compress_prompt=cp)
     print(f"squish: {loaded.name} loaded in {loaded.load_s:.1f}s; listening on http://{a.host or c['host']}:"
           f"{a.port or c['port']}", file=sys.stderr)
     try:

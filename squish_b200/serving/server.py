@@ -32,12 +32,15 @@ VERSION = "0.1.0"
 
 class ServerState:
     def __init__(self, aeng: AsyncEngine, model_name: str, api_key: str | None = None, arch: str = "qwen2",
-                 governor=None, load_time_s: float = 0.0, response_cache: int = 256):
+                 governor=None, load_time_s: float = 0.0, response_cache: int = 256,
+                 compress_prompt: dict | None = None):
         from .response_cache import ResponseCache
 
         self.aeng = aeng
         self.cache = ResponseCache(response_cache)
         self._grammar = None
+        # {"ratio", "min_tokens", "preserve_tokens"}: extractive compression of long user messages
+        self.compress_prompt = compress_prompt
         self.model_name = model_name
         self.api_key = api_key
         self.arch = arch
@@ -428,6 +431,12 @@ def create_app(st: ServerState) -> FastAPI:
         tools = body.get("tools") or None
         if body.get("tool_choice") == "none":
             tools = None
+        if st.compress_prompt:
+            from ..context.prompt_compressor import compress_messages
+
+            cp = st.compress_prompt
+            messages = compress_messages(messages, cp.get("ratio", 0.5), cp.get("min_tokens", 256),
+                                         cp.get("preserve_tokens", 0))
         with telemetry.span("chat_template"):
             prompt = apply_chat_template(messages, st.tok, st.arch, tools=tools)
             prompt_ids = st.tok.encode(prompt)
@@ -446,8 +455,28 @@ def create_app(st: ServerState) -> FastAPI:
             return StreamingResponse(_chat_stream(st, rid, created, prompt_ids, params, stops, tools, include_usage),
                                      media_type="text/event-stream")
         gf = st.format_factory(body.get("response_format"))
-        per = [dataclasses.replace(params, grammar=gf.json()) if gf else params for _ in range(n)]
+        sc = body.get("self_consistency")
+        if isinstance(sc, dict):  # sample k chains, answer with the majority's chain
+            n = max(2, min(parse_int(sc.get("k"), "self_consistency.k", 5), 32))
+            if params.temperature <= 0:
+                params = dataclasses.replace(params, temperature=float(sc.get("temperature", 0.7)))
+        per = [dataclasses.replace(params, grammar=gf.json() if gf else None,
+                                   seed=None if params.seed is None else params.seed + i) for i in range(n)]
         results = await asyncio.gather(*[_run_one(st, prompt_ids, p, stops) for p in per])
+        if isinstance(sc, dict):
+            from ..reasoning.self_consistency import SelfConsistencyConfig, SelfConsistencyVoter
+
+            vote = SelfConsistencyVoter(SelfConsistencyConfig(k=n, answer_pattern=sc.get("answer_pattern"))).vote(
+                [r[0] for r in results])
+            ctoks = sum(len(r[1]) for r in results)
+            text, _, reason, _ = results[vote.winner_index]
+            return {"id": rid, "object": "chat.completion", "created": created, "model": st.model_name,
+                    "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
+                                 "finish_reason": reason, "logprobs": None}],
+                    "self_consistency": {"answer": vote.answer, "votes": vote.votes, "k": n,
+                                         "agreement": vote.agreement, "distribution": vote.distribution},
+                    "usage": {"prompt_tokens": len(prompt_ids), "completion_tokens": ctoks,
+                              "total_tokens": len(prompt_ids) + ctoks}}
         choices, completion_tokens = [], 0
         for i, (text, ids, reason, _) in enumerate(results):
             msg = {"role": "assistant", "content": text}
