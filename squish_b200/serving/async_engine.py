@@ -75,6 +75,7 @@ class AsyncEngine:
         self.last_error: str | None = None
         self.loop_guard = loop_guard
         self._guards: dict = {}
+        self._unguarded: set = set()  # ignore_eos requests ask for exactly max_tokens: never cut
         self.loops_stopped = 0
         self.quality = QualityMonitor()
         self.step_ms: collections.deque = collections.deque(maxlen=4096)  # engine step wall times
@@ -115,6 +116,8 @@ class AsyncEngine:
             self._ids += 1
             rid = f"r{self._ids}"
         sink = _Sink(loop)
+        if params.ignore_eos:
+            self._unguarded.add(rid)
         self._sinks[rid] = sink
         self._t_submit[rid] = time.perf_counter()
         self._inbox.put(("add", rid, list(prompt_ids), params))
@@ -167,6 +170,7 @@ class AsyncEngine:
             elif op == "abort":
                 eng.abort(rid)
                 self._guards.pop(rid, None)
+                self._unguarded.discard(rid)
                 self._t_submit.pop(rid, None)
                 self._t_first.pop(rid, None)
                 sink = self._sinks.pop(rid, None)
@@ -209,7 +213,7 @@ class AsyncEngine:
                 if sink is None:
                     continue
                 finished, reason = o.finished, o.finish_reason
-                if self.loop_guard and not finished:
+                if self.loop_guard and not finished and o.rid not in self._unguarded:
                     g = self._guards.get(o.rid)
                     if g is None:
                         from .loop_guard import LoopGuard
@@ -223,6 +227,7 @@ class AsyncEngine:
                 if finished:
                     self._sinks.pop(o.rid, None)
                     self._guards.pop(o.rid, None)
+                    self._unguarded.discard(o.rid)
                     t0 = self._t_submit.pop(o.rid, now)
                     t1 = self._t_first.pop(o.rid, now)
                     dec = max(now - t1, 1e-6)

@@ -197,6 +197,26 @@ def test_async_engine_stops_a_loop_with_repetition():
     assert ev.reason == "repetition" and ev.finished
     assert 16 <= len(ev.token_ids) <= 64
     assert eng.aborted and aeng.loops_stopped == 1
+    # ignore_eos requests (benchmarks) run to max_tokens even when they loop
+    eng2 = _LoopingEngine()
+    aeng2 = AsyncEngine(eng2, ByteTokenizer(300, 2), model_name="fake").start()
+    try:
+        rid, sink = aeng2.submit([1, 2, 3], SamplingParams(max_tokens=100, ignore_eos=True))
+        got = []
+        import time as _t
+
+        t0 = _t.time()
+        while len(got) < 100 and _t.time() - t0 < 20:
+            try:
+                ev = sink.q.get(timeout=1)
+            except Exception:  # noqa: BLE001
+                continue
+            got += ev.token_ids
+            assert ev.reason != "repetition"
+        aeng2.abort(rid)
+    finally:
+        aeng2.stop()
+    assert len(got) >= 100 and aeng2.loops_stopped == 0
 
 
 def test_obs_report(client):
