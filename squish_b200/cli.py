@@ -127,7 +127,7 @@ def cmd_compress(a) -> int:
                   delete_source=a.delete_source, random_preset=a.random_init, seed=a.seed, kv_dtype=a.kv_dtype,
                   hqq=getattr(a, "hqq", False), awq=getattr(a, "awq", False),
                   awq_scales=getattr(a, "awq_scales", None), awq_alpha=getattr(a, "awq_alpha", 0.5),
-                  awq_samples=getattr(a, "awq_samples", 16))
+                  awq_samples=getattr(a, "awq_samples", 16), gptq=getattr(a, "gptq", False))
     print(json.dumps({"output": out, **st}))
     return 0
 
@@ -342,6 +342,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--awq-scales", default=None, metavar="DIR", help="apply saved AWQ scales instead")
     p.add_argument("--awq-alpha", type=float, default=0.5)
     p.add_argument("--awq-samples", type=int, default=16)
+    p.add_argument("--gptq", action="store_true", help="GPTQ INT4 (calibrates on the fp32 model)")
     p.set_defaults(fn=cmd_compress)
 
     p = sub.add_parser("merge-model", help="merge LoRA adapters (DARE / TIES / DARE-TIES)")

@@ -76,7 +76,7 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
              device: str | None = None, delete_source: bool = False, random_preset: str | None = None,
              seed: int = 0, kv_dtype: str = "int4", log=print, hqq: bool = False, awq: bool = False,
              awq_scales: str | None = None, awq_alpha: float = 0.5, awq_samples: int = 16,
-             awq_seq_len: int = 256, super_weights: bool = True) -> dict:
+             awq_seq_len: int = 256, super_weights: bool = True, gptq: bool = False) -> dict:
     """``hqq``: half-quadratic refinement of INT4 / INT2 grids. ``awq`` (or ``awq_scales``, a
     directory of saved scales): activation-aware scaling of norm-fed projections before
     quantization; calibration needs the whole fp32 model in memory once. ``super_weights``
@@ -84,6 +84,31 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
     are written to ``super_weights.json``."""
     from ..quant.super_weights import SuperWeightCalibrator, protect, save_coords
 
+    if gptq and (awq or awq_scales or kind != "q4a" or hqq):
+        raise ValueError("GPTQ produces INT4 (q4a) tensors and is not combined with AWQ or HQQ here")
+    hess: dict = {}
+
+    def calibrate_gptq(ck_loader, tokenizer_dir):
+        from ..quant.awq import calibration_tokens
+        from ..quant.gptq import collect_hessians
+
+        tok = None
+        if tokenizer_dir is not None and (Path(tokenizer_dir) / "tokenizer.json").exists():
+            from ..serving.tokenizer import load_tokenizer
+
+            tok = load_tokenizer(str(tokenizer_dir), cfg.vocab_size)
+        t0 = time.time()
+        hess.update(collect_hessians(ck_loader(), calibration_tokens(cfg.vocab_size, awq_samples, awq_seq_len,
+                                                                     tokenizer=tok, seed=seed), dev))
+        log(f"  GPTQ calibration: {len(hess)} projections, {time.time() - t0:.1f}s")
+
+    def gptq_or(name, w, fallback):
+        if name in hess:
+            from ..models.weights import pick_group
+            from ..quant.gptq import gptq_quantize
+
+            return gptq_quantize(w.to(dev), hess[name], pick_group(w.shape[1], group_size))
+        return fallback()
     sw_cal = SuperWeightCalibrator() if (super_weights and mse_clip and kind == "q4a") else None
     sw_found = []
 
@@ -114,6 +139,8 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
             if awq or awq_scales:
                 ops = _awq_ops(cfg, q, list(ck.tensors), lambda: ck, None, out, dev, awq_scales, awq_alpha,
                                awq_samples, awq_seq_len, seed, log)
+            if gptq:
+                calibrate_gptq(lambda: ck, None)
             router = None
             if kind == "mixed":
                 from ..quant.mixed import MixedPrecisionRouter
@@ -129,6 +156,8 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
                     w = apply_op(t.dequantize(), ops[name])
                     t = (QTensor("dense", t.shape, data=w.cpu()) if t.kind == "dense"
                          else quantize(w, tkind, group_size, mse_clip, hqq=hqq))
+                elif name in hess:
+                    t = gptq_or(name, t.dequantize(), None)
                 elif t.kind != "dense" and (tkind != "q4a" or hqq):
                     t = quantize(t.dequantize(), tkind, group_size, mse_clip, hqq=hqq)
                 stats["bytes"] += _write_tensor(td, name, t)
@@ -167,6 +196,20 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
 
             ops = _awq_ops(cfg, q, names, load_dense, src, out, dev, awq_scales, awq_alpha, awq_samples,
                            awq_seq_len, seed, log)
+        if gptq:
+            def load_dense_g():
+                from ..models.weights import Checkpoint
+
+                ckd = Checkpoint(cfg, q)
+                for shard in shards:
+                    with safe_open(str(shard), "pt", device="cpu") as f:
+                        for n in f.keys():
+                            ckd.tensors[n] = QTensor("dense", tuple(f.get_slice(n).get_shape()), data=f.get_tensor(n))
+                if "lm_head.weight" not in ckd.tensors and cfg.tie_embeddings:
+                    ckd.tensors["lm_head.weight"] = ckd.tensors["model.embed_tokens.weight"]
+                return ckd
+
+            calibrate_gptq(load_dense_g, src)
         router = None
         if kind == "mixed":
             from ..quant.mixed import MixedPrecisionRouter
@@ -184,8 +227,9 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
                         w = apply_op(w, ops[name])
                     if should_quantize(name, tuple(w.shape)):
                         tkind = router.kind_for(name) if router is not None else kind
-                        t = quantize(w if dev.type == "cuda" else w.float(), tkind, group_size, mse_clip, hqq=hqq)
-                        t = q4(name, w if dev.type == "cuda" else w.float(), t)
+                        wq = w if dev.type == "cuda" else w.float()
+                        t = gptq_or(name, wq, lambda: quantize(wq, tkind, group_size, mse_clip, hqq=hqq))
+                        t = q4(name, wq, t)
                         stats["n_quantized"] += 1
                     else:
                         t = QTensor("dense", tuple(w.shape), data=w.float().cpu())
@@ -214,7 +258,7 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
     (out / "config.json").write_text(json.dumps(to_hf_config(cfg), indent=2))
     q.weight_bits = 16 if kind == "dense" else 4
     (out / "squish_quant.json").write_text(json.dumps(dict(q.__dict__, weight_kind=kind, hqq=hqq,
-                                                           awq=bool(awq or awq_scales)), indent=2))
+                                                           awq=bool(awq or awq_scales), gptq=gptq), indent=2))
     (td / ".manifest_ready").touch()
     stats["seconds"] = round(time.time() - t0, 2)
     return stats

@@ -53,9 +53,10 @@ def _rope(x: torch.Tensor, cs: torch.Tensor) -> torch.Tensor:
 
 class ReferenceModel:
     """``device`` places the fp32 weights (CPU by default; a GPU runs calibration forwards).
-    ``tap(name, x)``, when set, sees the input of every norm-fed projection group:
-    ``model.layers.{i}.input_layernorm`` (q/k/v) and ``...post_attention_layernorm``
-    (gate/up, or the router and experts of a MoE layer), x of shape [T, hidden]."""
+    ``tap(name, x)``, when set, sees the input of every projection group, x of shape [T, width]:
+    ``model.layers.{i}.input_layernorm`` (q/k/v), ``...post_attention_layernorm`` (gate/up, or
+    the router and experts of a MoE layer), ``...self_attn.o_proj`` and ``...mlp.down_proj``
+    (dense MLP layers)."""
 
     tap = None
 
@@ -97,7 +98,10 @@ class ReferenceModel:
         if not cfg.is_moe:
             g = x @ w[p + "mlp.gate_proj.weight"].T
             u = x @ w[p + "mlp.up_proj.weight"].T
-            return self._rp((torch.nn.functional.silu(g) * u), w[p + "mlp.down_proj.weight"])
+            act = torch.nn.functional.silu(g) * u
+            if self.tap is not None:
+                self.tap(p + "mlp.down_proj", act)
+            return self._rp(act, w[p + "mlp.down_proj.weight"])
         logits = x @ w[p + "mlp.gate.weight"].T
         probs = torch.softmax(logits, dim=-1)
         topv, topi = probs.topk(cfg.num_experts_per_tok, dim=-1)
@@ -153,6 +157,8 @@ class ReferenceModel:
             kpos = torch.arange(kk.shape[0], device=dev)
             s = s.masked_fill(kpos[None, None, :] > pos[None, :, None], float("-inf"))
             a = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vv).reshape(t, hq * d)
+            if self.tap is not None:
+                self.tap(p + "self_attn.o_proj", a)
             h = h + a @ w[p + "self_attn.o_proj.weight"].T
             x = _rms(h, w[p + "post_attention_layernorm.weight"], cfg.rms_eps)
             if self.tap is not None:

@@ -54,6 +54,8 @@ class ActivationStats:
         self.count: dict[str, int] = {}
 
     def __call__(self, name: str, x: torch.Tensor) -> None:
+        if not name.endswith("layernorm"):
+            return  # AWQ scales only norm-fed projections
         x2 = x.reshape(-1, x.shape[-1]).contiguous()
         a = self.acc.get(name)
         if a is None:

@@ -438,3 +438,30 @@ def test_super_weight_detection_and_protection(tmp_path):
     assert any(c.tensor_name == name and (c.row, c.col) == (10, 100) for c in coords)
     out, _ = load_checkpoint(str(tmp_path / "out"), "cpu")
     assert abs(float(out.tensors[name].dequantize()[10, 100]) - 5.0) < 1e-3
+
+
+def test_gptq_beats_round_to_nearest_on_calibration_data(tmp_path):
+    from squish_b200.io.convert import compress, load_checkpoint
+    from squish_b200.quant.codecs import quantize
+    from squish_b200.quant.gptq import HessianStats, gptq_quantize
+
+    g = torch.Generator().manual_seed(0)
+    # correlated inputs (a few dominant directions), as real activations are
+    basis = torch.randn(8, 256, generator=g)
+    X = torch.randn(2048, 8, generator=g) @ basis + 0.1 * torch.randn(2048, 256, generator=g)
+    W = torch.randn(128, 256, generator=g) * 0.02
+    st = HessianStats()
+    st("x", X)
+    t = gptq_quantize(W, st.hessian("x"), group=64)
+    rtn = quantize(W, "q4a", 64)
+    err = lambda q: ((X @ W.T - X @ q.dequantize().T) ** 2).mean().item()  # noqa: E731
+    assert err(t) < 0.8 * err(rtn), (err(t), err(rtn))
+    st2 = compress(None, str(tmp_path / "m"), random_preset="tiny-llama", device="cpu", gptq=True, awq_samples=2,
+                   awq_seq_len=16, log=lambda *_: None)
+    assert st2["n_quantized"] > 0
+    ck, _ = load_checkpoint(str(tmp_path / "m"), "cpu")
+    m = ReferenceModel(ck)
+    assert torch.isfinite(m.forward([1, 2, 3], m.new_cache(), 0)).all()
+    with pytest.raises(ValueError):
+        compress(None, str(tmp_path / "n"), random_preset="tiny-llama", device="cpu", gptq=True, hqq=True,
+                 log=lambda *_: None)
