@@ -334,7 +334,7 @@ class JsonMatcher {
 // integer, number, boolean, null, enum / const (serialized literals), and any (generic JSON).
 // The stack keeps per frame the object's node, the node of the member value being read and the
 // set of properties already used; depth is limited to 16.
-enum Kind : uint8_t { K_ANY, K_OBJECT, K_ARRAY, K_STRING, K_INTEGER, K_NUMBER, K_BOOLEAN, K_NULL, K_ENUM };
+enum Kind : uint8_t { K_ANY, K_OBJECT, K_ARRAY, K_STRING, K_INTEGER, K_NUMBER, K_BOOLEAN, K_NULL, K_ENUM, K_UNION };
 
 struct SchemaNode {
   uint8_t kind = K_ANY;
@@ -343,6 +343,7 @@ struct SchemaNode {
   uint64_t required = 0;
   int items = -1;                  // array items node (-1: any)
   std::vector<std::string> lits;   // enum literals, serialized JSON
+  // K_UNION (type lists, anyOf / oneOf): the alternatives are the `props` nodes (names empty)
 };
 
 class Schema {
@@ -427,9 +428,60 @@ inline bool s_push(SState& s, uint8_t f, uint16_t node) {
   return true;
 }
 
-bool s_start_value(const Schema& sc, SState& s, uint8_t c) {
-  const uint16_t id = expected(sc, s);
+// can a value of node `id` start with byte c (unions: any alternative)?
+bool s_can_start(const Schema& sc, uint16_t id, uint8_t c, int depth = 0) {
   const SchemaNode* n = sn(sc, id);
+  const uint8_t k = n == nullptr ? K_ANY : n->kind;
+  switch (k) {
+    case K_OBJECT: return c == '{';
+    case K_ARRAY: return c == '[';
+    case K_STRING: return c == '"';
+    case K_INTEGER:
+    case K_NUMBER: return c == '-' || is_digit(c);
+    case K_BOOLEAN: return c == 't' || c == 'f';
+    case K_NULL: return c == 'n';
+    case K_ENUM:
+      for (const auto& l : n->lits)
+        if (!l.empty() && (uint8_t)l[0] == c) return true;
+      return false;
+    case K_UNION:
+      if (depth > 8) return false;
+      for (int a : n->props)
+        if (s_can_start(sc, (uint16_t)a, c, depth + 1)) return true;
+      return false;
+    default:
+      return c == '{' || c == '[' || c == '"' || c == '-' || is_digit(c) || c == 't' || c == 'f' || c == 'n';
+  }
+}
+
+bool s_start_as(const Schema& sc, SState& s, uint16_t id, uint8_t c, int depth = 0);
+
+bool s_start_value(const Schema& sc, SState& s, uint8_t c) { return s_start_as(sc, s, expected(sc, s), c); }
+
+// Start a value of node `id` with byte c. A union picks the one alternative that can start
+// with c; when several can (two objects, integer and number, ...), the value is read as any
+// JSON value (integer + number alone: as a number), which allows a superset of the union.
+bool s_start_as(const Schema& sc, SState& s, uint16_t id, uint8_t c, int depth) {
+  const SchemaNode* n = sn(sc, id);
+  if (n != nullptr && n->kind == K_UNION) {
+    if (depth > 8) return false;
+    int pick = -1, count = 0;
+    bool all_numeric = true;
+    for (int a : n->props)
+      if (s_can_start(sc, (uint16_t)a, c)) {
+        ++count;
+        pick = a;
+        const uint8_t ak = sc.node(a).kind;
+        all_numeric = all_numeric && (ak == K_INTEGER || ak == K_NUMBER);
+      }
+    if (count == 0) return false;
+    if (count == 1) return s_start_as(sc, s, (uint16_t)pick, c, depth + 1);
+    if (all_numeric) {
+      for (int a : n->props)
+        if (sc.node(a).kind == K_NUMBER) return s_start_as(sc, s, (uint16_t)a, c, depth + 1);
+    }
+    return s_start_as(sc, s, kAnyNode, c, depth + 1);
+  }
   const uint8_t k = n == nullptr ? K_ANY : n->kind;
   s.num_int = k == K_INTEGER;
   switch (k) {

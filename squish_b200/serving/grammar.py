@@ -85,17 +85,20 @@ class JsonGrammar:
         return self.m.is_terminated()
 
 
-K_ANY, K_OBJECT, K_ARRAY, K_STRING, K_INTEGER, K_NUMBER, K_BOOLEAN, K_NULL, K_ENUM = range(9)
+K_ANY, K_OBJECT, K_ARRAY, K_STRING, K_INTEGER, K_NUMBER, K_BOOLEAN, K_NULL, K_ENUM, K_UNION = range(10)
 
 
 def compile_schema(schema: dict):
     """JSON schema -> ``_C.grammar.Schema`` node table. Supported: ``type`` object (``properties``,
     ``required``; only listed properties may appear, each once), array (``items``), string,
     integer, number, boolean, null; ``enum`` / ``const`` (literal values); local ``$ref``
-    (``#/$defs/..``, ``#/definitions/..``). ``anyOf`` / ``oneOf`` / type lists and an object
-    without ``properties`` accept any JSON value of the allowed shape (no constraint)."""
+    (``#/$defs/..``, ``#/definitions/..``); unions -- ``anyOf`` / ``oneOf`` and type lists such
+    as ``["string", "null"]`` -- choose the alternative by the value's first byte (alternatives
+    that share it, e.g. two objects, relax to any JSON value). An object without ``properties``
+    accepts any object."""
     kinds, props, required, items, lits = [], [], [], [], []
-    memo: dict[int, int] = {}
+    memo: dict[int, int] = {}  # id(schema dict) -> node; dicts made here are kept alive in `made`
+    made: list = []
 
     def resolve(node):
         seen = 0
@@ -132,6 +135,20 @@ def compile_schema(schema: dict):
             lits[i] = [json.dumps(v, separators=(",", ":"), ensure_ascii=False).encode() for v in vals]
             return i
         t = node.get("type")
+        alts = node.get("anyOf") or node.get("oneOf")
+        if isinstance(t, list) or isinstance(alts, list):
+            if isinstance(t, list):
+                alts = [dict(node, type=x) for x in t]
+                for a in alts:
+                    a.pop("anyOf", None)
+                    a.pop("oneOf", None)
+            if len(alts) > 64:
+                raise ValueError("at most 64 union alternatives")
+            kinds[i] = K_UNION
+            made.extend(alts)
+            for a in alts:
+                props[i].append((b"", add(a)))
+            return i
         if t == "object" and isinstance(node.get("properties"), dict) and node["properties"]:
             names = list(node["properties"])
             if len(names) > 64:

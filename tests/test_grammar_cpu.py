@@ -211,3 +211,50 @@ def test_json_schema_over_http():
             assert bad.status_code == 400
     finally:
         aeng.stop()
+
+
+UNION = {"type": "object", "properties": {
+    "n": {"type": ["string", "null"]},
+    "v": {"anyOf": [{"type": "integer"}, {"type": "array", "items": {"type": "boolean"}}]},
+    "o": {"oneOf": [{"type": "object", "properties": {"a": {"type": "integer"}}, "required": ["a"]},
+                    {"type": "object", "properties": {"b": {"type": "string"}}}]},
+    "x": {"type": ["integer", "number"]}}, "required": ["n"]}
+
+
+@pytest.mark.parametrize("text,want", [
+    ('{"n": null}', True), ('{"n": "s"}', True), ('{"n": 3}', False), ('{"n": null, "v": 7}', True),
+    ('{"n": null, "v": [true, false]}', True), ('{"n": null, "v": "s"}', False), ('{"n":null,"v":[1]}', False),
+    ('{"n": null, "o": {"zz": 1}}', True),  # two object alternatives share '{': relaxed to any object
+    ('{"n": null, "x": 1.5}', True), ('{"n": null, "x": "q"}', False),
+])
+def test_schema_unions(text, want):
+    g = GrammarFactory(ByteTokenizer(300, 2), 300, 2).schema(UNION)
+    assert (_feed(g, text) and g.is_complete()) == want, text
+
+
+def test_union_masks_agree_with_stepwise_advance():
+    from squish_b200.serving.grammar import compile_schema
+
+    rng = random.Random(5)
+    alphabet = ['{', '}', '[', ']', '"', ':', ',', ' ', '"n": ', '"v": ', '"x": ', 'null', 'nul', 'l', 'true', '7',
+                '1.5', '-', '"s"', 'tr', 'ue', '"o": {', '"zz"']
+    vocab = [b""] * 3 + [t.encode() for t in alphabet]
+    idx = native().grammar.VocabIndex(vocab, 2)
+    sc = compile_schema(UNION)
+    for trial in range(20):
+        hist = []
+        g = native().grammar.SchemaMatcher(idx, sc)
+        for step in range(25):
+            m = g.allowed_mask().numpy().view(np.uint32)
+            allowed = {t for t in range(len(vocab)) if (m[t >> 5] >> (t & 31)) & 1}
+            for t in range(3, len(vocab)):
+                probe = native().grammar.SchemaMatcher(idx, sc)
+                for h in hist:
+                    assert probe.advance(h)
+                assert probe.advance(t) == (t in allowed)
+            choices = sorted(allowed - {2})
+            if not choices:
+                break
+            t = rng.choice(choices)
+            hist.append(t)
+            assert g.advance(t)
