@@ -594,6 +594,83 @@ torch::Tensor dequantize_fp8(torch::Tensor codes, torch::Tensor scales, int64_t 
   return out;
 }
 
+// ---- FP6 (1 sign + e exponent + m mantissa bits, e + m = 5), 4 values per 3 bytes ----------
+// Packing of the reference's fp6_encode_f32 / fp6_decode (lib.rs:2410-2470): the four 6-bit
+// codes a, b, c, d form the 24-bit word a<<18 | b<<12 | c<<6 | d, stored most significant byte
+// first. Values (the OCP MX FP6 convention, no infinities or NaNs): exponent field 0 holds
+// subnormals man * 2^(1 - bias - m), others (1 + man / 2^m) * 2^(field - bias), bias =
+// 2^(e-1) - 1. Encoding rounds to nearest even and saturates to the largest magnitude (the
+// reference truncates the mantissa and flushes subnormals to zero; its codes decode the same).
+struct Fp6Fmt {
+  int e, m, bias;
+  float maxval;
+};
+Fp6Fmt fp6_fmt(int64_t e, int64_t m) {
+  TORCH_CHECK(e >= 1 && m >= 0 && e + m == 5, "FP6 needs exponent + mantissa bits = 5 (exponent >= 1)");
+  const int bias = (1 << (e - 1)) - 1;
+  const float maxv = std::ldexp(1.f + (float)((1 << m) - 1) / (float)(1 << m), (1 << e) - 1 - bias);
+  return {(int)e, (int)m, bias, maxv};
+}
+uint8_t fp6_encode1(float v, const Fp6Fmt& f) {
+  const uint8_t sign = std::signbit(v) ? 0x20 : 0;
+  float a = std::fabs(v);
+  if (std::isnan(a)) return 0;  // as the reference: NaN encodes as +0
+  if (a == 0.f) return sign;
+  const long maxcode = (1L << 5) - 1;  // all exponent and mantissa bits set
+  if (std::isinf(a) || a >= f.maxval) return sign | (uint8_t)maxcode;
+  int e2;
+  std::frexp(a, &e2);
+  const int ex = e2 - 1, emin = 1 - f.bias;
+  long code;
+  if (ex < emin) {
+    code = (long)std::nearbyint(std::ldexp(a, f.m - emin));
+  } else {
+    const float mm = std::ldexp(a, -ex) - 1.f;
+    code = ((long)(ex + f.bias) << f.m) + (long)std::nearbyint(std::ldexp(mm, f.m));
+  }
+  if (code > maxcode) code = maxcode;
+  return sign | (uint8_t)code;
+}
+float fp6_decode1(uint8_t c, const Fp6Fmt& f) {
+  const float sg = (c & 0x20) ? -1.f : 1.f;
+  const int field = (c & 0x1F) >> f.m, man = c & ((1 << f.m) - 1);
+  if (field == 0) return sg * std::ldexp((float)man, 1 - f.bias - f.m);
+  return sg * std::ldexp(1.f + std::ldexp((float)man, -f.m), field - f.bias);
+}
+
+torch::Tensor fp6_encode(torch::Tensor x, int64_t exp_bits, int64_t man_bits) {
+  TORCH_CHECK(!x.is_cuda() && x.scalar_type() == torch::kFloat32 && x.is_contiguous(), "x: contiguous float32 (CPU)");
+  TORCH_CHECK(x.numel() % 4 == 0, "length must be a multiple of 4");
+  const Fp6Fmt f = fp6_fmt(exp_bits, man_bits);
+  const int64_t packs = x.numel() / 4;
+  auto out = torch::empty({packs * 3}, torch::kUInt8);
+  const float* xp = x.data_ptr<float>();
+  uint8_t* o = out.data_ptr<uint8_t>();
+  prange(packs, [&](int64_t i) {
+    const uint32_t w = ((uint32_t)fp6_encode1(xp[4 * i], f) << 18) | ((uint32_t)fp6_encode1(xp[4 * i + 1], f) << 12) |
+                       ((uint32_t)fp6_encode1(xp[4 * i + 2], f) << 6) | (uint32_t)fp6_encode1(xp[4 * i + 3], f);
+    o[3 * i] = (uint8_t)(w >> 16);
+    o[3 * i + 1] = (uint8_t)(w >> 8);
+    o[3 * i + 2] = (uint8_t)w;
+  });
+  return out;
+}
+
+torch::Tensor fp6_decode(torch::Tensor packed, int64_t n, int64_t exp_bits, int64_t man_bits) {
+  TORCH_CHECK(!packed.is_cuda() && packed.scalar_type() == torch::kUInt8 && packed.is_contiguous(),
+              "packed: contiguous uint8 (CPU)");
+  TORCH_CHECK(n % 4 == 0 && packed.numel() >= n / 4 * 3, "n must be a multiple of 4 covered by the packed bytes");
+  const Fp6Fmt f = fp6_fmt(exp_bits, man_bits);
+  auto out = torch::empty({n}, torch::kFloat32);
+  const uint8_t* p = packed.data_ptr<uint8_t>();
+  float* o = out.data_ptr<float>();
+  prange(n / 4, [&](int64_t i) {
+    const uint32_t w = ((uint32_t)p[3 * i] << 16) | ((uint32_t)p[3 * i + 1] << 8) | (uint32_t)p[3 * i + 2];
+    for (int j = 0; j < 4; ++j) o[4 * i + j] = fp6_decode1((uint8_t)((w >> (18 - 6 * j)) & 0x3F), f);
+  });
+  return out;
+}
+
 }  // namespace
 
 void register_entropy(pybind11::module& c);  // entropy.cpp
@@ -620,6 +697,8 @@ void register_cpu(pybind11::module& m) {
   c.def("quantize_fp8", &quantize_fp8, pybind11::arg("x"), pybind11::arg("fmt"), pybind11::arg("group"),
         pybind11::arg("fixed_scale") = 0.0);
   c.def("dequantize_fp8", &dequantize_fp8);
+  c.def("fp6_encode", &fp6_encode);
+  c.def("fp6_decode", &fp6_decode);
 }
 
 }  // namespace sqcpu

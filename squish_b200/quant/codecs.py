@@ -70,6 +70,42 @@ def quantize_fp8(w: torch.Tensor, fmt: str = "e4m3", group: int = 0) -> tuple[to
     return tuple(native().cpu.quantize_fp8(x.float().contiguous(), cpu_fmt, g, fixed))
 
 
+_FP6 = {"e3m2": (3, 2), "e2m3": (2, 3)}
+
+
+def fp6_encode(x: torch.Tensor, fmt: str = "e3m2") -> torch.Tensor:
+    """Pack a float tensor (numel a multiple of 4) as FP6 codes, 4 values per 3 bytes (the
+    reference's fp6_encode_f32 layout, squish_quant_rs/src/lib.rs:2410); no scaling."""
+    e, m = _FP6[fmt]
+    return native().cpu.fp6_encode(x.detach().float().cpu().reshape(-1).contiguous(), e, m)
+
+
+def fp6_decode(packed: torch.Tensor, n: int, fmt: str = "e3m2") -> torch.Tensor:
+    e, m = _FP6[fmt]
+    return native().cpu.fp6_decode(packed.cpu().contiguous(), n, e, m)
+
+
+def quantize_fp6(w: torch.Tensor, fmt: str = "e3m2", group: int = 32) -> tuple[torch.Tensor, torch.Tensor]:
+    """FP6 with one fp32 scale per ``group`` values of each row (absmax / largest FP6 value):
+    (packed bytes, scales [rows, cols / group])."""
+    e, m = _FP6[fmt]
+    fmax = (1 + ((1 << m) - 1) / (1 << m)) * 2.0 ** ((1 << e) - 1 - ((1 << (e - 1)) - 1))
+    x = w.detach().float().cpu()
+    r, c = x.shape
+    if c % group or group % 4:
+        raise ValueError("group must divide the row and be a multiple of 4")
+    g = x.reshape(r, c // group, group)
+    am = g.abs().amax(-1)
+    sc = torch.where(am > 0, am / fmax, torch.ones_like(am))
+    return fp6_encode((g / sc[..., None]).reshape(-1), fmt), sc
+
+
+def dequantize_fp6(packed: torch.Tensor, scales: torch.Tensor, shape: tuple, fmt: str = "e3m2") -> torch.Tensor:
+    r, c = shape
+    g = c // scales.shape[1]
+    return (fp6_decode(packed, r * c, fmt).reshape(r, c // g, g) * scales.float()[..., None]).reshape(r, c)
+
+
 def dequantize_fp8(codes: torch.Tensor, scales: torch.Tensor, fmt: str = "e4m3") -> torch.Tensor:
     """fp32 reconstruction of :func:`quantize_fp8` output (on the CPU)."""
     sc = scales.float().cpu()

@@ -465,3 +465,30 @@ def test_gptq_beats_round_to_nearest_on_calibration_data(tmp_path):
     with pytest.raises(ValueError):
         compress(None, str(tmp_path / "n"), random_preset="tiny-llama", device="cpu", gptq=True, hqq=True,
                  log=lambda *_: None)
+
+
+@pytest.mark.parametrize("fmt,e,m", [("e3m2", 3, 2), ("e2m3", 2, 3)])
+def test_fp6_round_to_nearest_even_and_packing(fmt, e, m):
+    from squish_b200.quant.codecs import dequantize_fp6, fp6_decode, fp6_encode, quantize_fp6
+
+    bias = (1 << (e - 1)) - 1
+    # every representable non-negative value, by code
+    vals = [(c & ((1 << m) - 1)) * 2.0 ** (1 - bias - m) if (c >> m) == 0 else
+            (1 + (c & ((1 << m) - 1)) / (1 << m)) * 2.0 ** ((c >> m) - bias) for c in range(32)]
+    grid = torch.tensor(vals)
+    assert torch.equal(fp6_decode(fp6_encode(torch.tensor(vals[:32]), fmt), 32, fmt), grid)
+    g = torch.Generator().manual_seed(e)
+    x = (torch.rand(4000, generator=g) * 2 - 1) * grid.max() * 1.2
+    y = fp6_decode(fp6_encode(x, fmt), 4000, fmt)
+    d = (x.abs()[:, None] - grid[None, :]).abs()
+    best = d.min(1).values
+    assert torch.allclose((y.abs() - x.abs()).abs(), best, atol=1e-6)  # nearest representable magnitude
+    assert torch.equal(torch.sign(y[y != 0]), torch.sign(x[y != 0]))
+    # packing: 4 codes a, b, c, d -> a<<18 | b<<12 | c<<6 | d, most significant byte first
+    p = fp6_encode(torch.tensor([vals[1], vals[2], vals[3], vals[4]]), fmt)
+    assert int.from_bytes(bytes(p.tolist()), "big") == (1 << 18) | (2 << 12) | (3 << 6) | 4
+    w = torch.randn(32, 64, generator=g) * 0.02
+    pk, sc = quantize_fp6(w, fmt, 32)
+    assert pk.numel() == 32 * 64 * 3 // 4 and sc.shape == (32, 2)
+    rel = ((dequantize_fp6(pk, sc, (32, 64), fmt) - w).norm() / w.norm()).item()
+    assert rel < (0.1 if fmt == "e3m2" else 0.06)
