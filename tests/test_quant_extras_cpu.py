@@ -492,3 +492,32 @@ def test_fp6_round_to_nearest_even_and_packing(fmt, e, m):
     assert pk.numel() == 32 * 64 * 3 // 4 and sc.shape == (32, 2)
     rel = ((dequantize_fp6(pk, sc, (32, 64), fmt) - w).norm() / w.norm()).item()
     assert rel < (0.1 if fmt == "e3m2" else 0.06)
+
+
+def test_calibration_statistics_and_wanda():
+    from squish_b200.quant.calibration import (calib_aciq, calib_absmax, calib_percentile, collect_input_norms,
+                                               wanda_importance, wanda_nm_mask, wanda_prune)
+
+    g = torch.Generator().manual_seed(0)
+    a = torch.randn(101, 6, generator=g) * torch.arange(1, 7)
+    torch.testing.assert_close(calib_absmax(a), a.abs().max(0).values)
+    torch.testing.assert_close(calib_percentile(a, 50), a.abs().sort(0).values[50])
+    torch.testing.assert_close(calib_percentile(a, 100), calib_absmax(a))
+    np_sig = np.std(a.numpy(), axis=0, ddof=1) * np.sqrt(2 * np.log(101) + 1)
+    np.testing.assert_allclose(calib_aciq(a).numpy(), np_sig, rtol=1e-5)
+    w = torch.randn(8, 10, generator=g)
+    norm = torch.rand(10, generator=g) + 0.1
+    imp = wanda_importance(w, norm)
+    torch.testing.assert_close(imp, w.abs() * norm)
+    mask = wanda_nm_mask(imp, 2, 4)  # blocks [0:4], [4:8], [8:10]
+    assert mask.dtype == torch.uint8 and mask.shape == (8, 10)
+    assert (mask[:, :4].sum(1) == 2).all() and (mask[:, 4:8].sum(1) == 2).all() and (mask[:, 8:].sum(1) == 2).all()
+    for r in range(8):
+        blk = imp[r, :4]
+        assert set(mask[r, :4].nonzero().flatten().tolist()) == set(blk.topk(2).indices.tolist())
+    pruned = wanda_prune(w, norm)
+    assert (pruned[mask == 0] == 0).all() and torch.equal(pruned[mask == 1], w[mask == 1])
+    cfg, q = get_preset("tiny-llama")
+    norms = collect_input_norms(random_checkpoint(cfg, q, seed=1), [[1, 2, 3, 4]], device="cpu")
+    assert norms["model.layers.0.input_layernorm"].shape == (cfg.hidden_size,)
+    assert norms["model.layers.0.mlp.down_proj"].shape == (cfg.intermediate_size,)
