@@ -16,6 +16,8 @@ def native():
     """Return the compiled extension module, raising a clear error if it is missing."""
     global _C
     if _C is None:
+        import torch  # noqa: F401  (loads libc10 / libtorch, which the extension links against)
+
         try:
             _C = importlib.import_module("squish_b200._C")
         except ImportError as exc:  # pragma: no cover - exercised only on unbuilt trees
