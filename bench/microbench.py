@@ -3,6 +3,15 @@
 
     python bench/microbench.py [--model qwen2.5-7b] [--json out.json]
 
+Small, self-terminating cases of one kernel each (the commands the ncu summaries in
+profiles/ run):
+
+    python bench/microbench.py case gemm --m 64 --n 37888 --k 3584 --iters 2
+    python bench/microbench.py case attn --decode 64 --lens 1300 --iters 3
+    python bench/microbench.py case attn --lens 2048 --iters 3
+    python bench/microbench.py case hadamard --m 64 --k 18944 --iters 3 [--time]
+    python bench/microbench.py case step --mode decode|prefill [--batch 64 --ctx 1000]
+
 Each op is timed with CUDA events on the launching stream after warm-up, median of
 ``--iters`` launches (inputs larger than L2 where it matters: weight streams of tens of
 MB; the INT4 weights rotate over ``--copies`` copies so every launch reads from HBM).
@@ -244,5 +253,158 @@ def other_ops(args, cfg, q, dev, hbm, tflops):
     return rows
 
 
+# ----------------------------------------------------------------------------- single-kernel cases
+def case_gemm(a):
+    dev = torch.device("cuda", 0)
+    w = torch.randn(a.n, a.k, device=dev, dtype=torch.bfloat16) * 0.02
+    p, s, o = native().quantize_int4_asym(w, a.group, 1)
+    wt = ops.prepare_int4_weight(p, s, o, a.k, a.group, dev)
+    del w, p, s, o
+    x = torch.randn(a.m, a.k, device=dev, dtype=torch.bfloat16)
+    for _ in range(a.iters):
+        y = ops.w4a16_linear(x, wt, silu_mul=a.silu)
+    torch.cuda.synchronize()
+    ops.workspace(dev).check()
+    print("plan", ops.gemm_plan(a.m, a.n, a.k), "ok", tuple(y.shape))
+
+
+def case_attn(a):
+    from squish_b200.kv.paged import kv_row_bytes
+
+    dev = torch.device("cuda", 0)
+    lens = [int(x) for x in a.lens.split(",")]
+    if a.decode:
+        lens = lens[:1] * a.decode
+    d, ps, grp = 128, 16, 32
+    fk, fv = ops.KV_FORMATS[a.kv]
+    cbk, nsk = kv_row_bytes(fk, d, grp)
+    cbv, nsv = kv_row_bytes(fv, d, grp)
+    B = len(lens)
+    pages_per = math.ceil(max(lens) / ps)
+    npg = B * pages_per + 1
+    kc = torch.randint(0, 255, (npg, a.hkv, ps, cbk), dtype=torch.uint8, device=dev)
+    vc = torch.randint(0, 255, (npg, a.hkv, ps, cbv), dtype=torch.uint8, device=dev)
+    ks = (torch.rand(npg, a.hkv, ps, max(nsk, 1), device=dev) * 0.1).half()
+    vs = (torch.rand(npg, a.hkv, ps, max(nsv, 1), device=dev) * 0.1).half()
+    bt = torch.randperm(npg - 1, device=dev)[: B * pages_per].view(B, pages_per).int()
+    ql = torch.tensor(lens, dtype=torch.int32)
+    if a.decode:
+        qd = torch.randn(B, a.hq * d, device=dev, dtype=torch.bfloat16)
+        od = torch.empty_like(qd)
+        for _ in range(a.iters):
+            ops.paged_decode_attention(qd, kc, ks, vc, vs, bt, ql.to(dev), od, a.hq, a.hkv, d, ps, grp, fk, fv,
+                                       1 / math.sqrt(d), max(lens))
+        torch.cuda.synchronize()
+        ops.workspace(dev).check()
+        print("ok decode", B, "x", lens[0])
+        return
+    qs = torch.cat([torch.zeros(1, dtype=torch.int32), ql.cumsum(0)[:-1].int()])
+    tseq, tq0 = [], []
+    for i, n in enumerate(lens):
+        for s0 in range(0, n, 32):
+            tseq.append(i)
+            tq0.append(s0)
+    T = int(ql.sum())
+    q = torch.randn(T, a.hq * d, device=dev, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    args = (torch.tensor(tseq, dtype=torch.int32, device=dev), torch.tensor(tq0, dtype=torch.int32, device=dev),
+            qs.to(dev), ql.to(dev), ql.to(dev), len(tseq))
+    for _ in range(a.iters):
+        ops.paged_prefill_attention(q, kc, ks, vc, vs, bt, *args, out, a.hq, a.hkv, d, ps, grp, fk, fv,
+                                    1 / math.sqrt(d))
+    torch.cuda.synchronize()
+    ops.workspace(dev).check()
+    print("ok", T, "tokens", len(tseq), "tiles")
+
+
+def case_hadamard(a):
+    from squish_b200.quant.sqint2 import rotation_block, rotation_signs
+
+    dev = torch.device("cuda", 0)
+    b = rotation_block(a.k)
+    s = rotation_signs(a.k, 0).to(dev)
+    n = max(1, int(256e6 // (4 * a.m * a.k)))  # several pairs: timed launches do not re-read L2
+    xs = [torch.randn(a.m, a.k, device=dev, dtype=torch.bfloat16) for _ in range(n)]
+    ys = [torch.empty_like(x) for x in xs]
+    for i in range(a.iters):
+        native().hadamard_rows(xs[i % n], s, b, ys[i % n])
+    torch.cuda.synchronize()
+    if a.time:
+        it = [0]
+
+        def fn():
+            native().hadamard_rows(xs[it[0] % n], s, b, ys[it[0] % n])
+            it[0] += 1
+
+        us = time_op(fn, 20, inner=max(8, n)) * 1e3
+        print(f"m={a.m} k={a.k} block={b}: {us:.2f} us/launch, {4 * a.m * a.k / us / 1e3:.0f} GB/s")
+    print("ok", b)
+
+
+def case_step(a):
+    import numpy as np
+
+    from squish_b200.engine.engine import EngineConfig, LLMEngine
+    from squish_b200.engine.sampling import SamplingParams
+
+    eng = LLMEngine.from_preset(a.model, device="cuda", seed=0, ecfg=EngineConfig(
+        max_num_seqs=a.batch + 1, max_num_batched_tokens=2048, max_model_len=a.ctx + 512,
+        cuda_graphs=not a.no_graphs))
+    rng = np.random.default_rng(0)
+    for _ in range(a.batch):
+        eng.add_request(rng.integers(0, eng.cfg.vocab_size, a.ctx).tolist(),
+                        SamplingParams(max_tokens=400, ignore_eos=True))
+    while any(r.in_prefill for r in eng.scheduler.running) or eng.scheduler.waiting:
+        eng.step()
+    for _ in range(3):
+        eng.step()
+    torch.cuda.synchronize()
+    if a.mode == "prefill":
+        eng.add_request(rng.integers(0, eng.cfg.vocab_size, a.ctx).tolist(), SamplingParams(max_tokens=4))
+    # ncu --profile-from-start off sees only the steps inside this window
+    torch.cuda.profiler.start()
+    for _ in range(a.steps):
+        eng.step()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print("ok", eng.stats.graph_steps, eng.stats.mixed_steps)
+
+
+def case_main(argv):
+    ap = argparse.ArgumentParser(prog="microbench.py case")
+    sub = ap.add_subparsers(dest="kind", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("--m", type=int, default=64)
+    g.add_argument("--n", type=int, default=37888)
+    g.add_argument("--k", type=int, default=3584)
+    g.add_argument("--group", type=int, default=64)
+    g.add_argument("--iters", type=int, default=5)
+    g.add_argument("--silu", action="store_true")
+    t = sub.add_parser("attn")
+    t.add_argument("--lens", default="2048", help="comma-separated prompt lengths (one chunk each)")
+    t.add_argument("--hq", type=int, default=28)
+    t.add_argument("--hkv", type=int, default=4)
+    t.add_argument("--kv", default="int4")
+    t.add_argument("--iters", type=int, default=3)
+    t.add_argument("--decode", type=int, default=0, help="decode batch: B sequences of --lens context")
+    h = sub.add_parser("hadamard")
+    h.add_argument("--m", type=int, default=64)
+    h.add_argument("--k", type=int, default=18944)
+    h.add_argument("--iters", type=int, default=3)
+    h.add_argument("--time", action="store_true")
+    st = sub.add_parser("step")
+    st.add_argument("--model", default="qwen2.5-7b")
+    st.add_argument("--batch", type=int, default=64)
+    st.add_argument("--ctx", type=int, default=1000)
+    st.add_argument("--mode", default="decode", choices=["decode", "prefill"])
+    st.add_argument("--steps", type=int, default=2)
+    st.add_argument("--no-graphs", action="store_true")
+    a = ap.parse_args(argv)
+    {"gemm": case_gemm, "attn": case_attn, "hadamard": case_hadamard, "step": case_step}[a.kind](a)
+
+
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 1 and sys.argv[1] == "case":
+        case_main(sys.argv[2:])
+    else:
+        main()

@@ -20,9 +20,15 @@
 //       int Hq, int Hkv, int D, int page_size, int group, int fmt_k, int fmt_v,
 //       float sm_scale, int splits, int tiles_per_split, void* stream);
 //
-// Returns 0 on success, SQ_NOALLOC_TOO_LARGE if B*Hq*splits*D exceeds
-// SQ_NOALLOC_MAX_PARTIAL_FLOATS (nothing is launched then), or a CUDA error code.
-// sq_noalloc_error_string() turns a return code into a message.
+// Returns 0 on success; SQ_NOALLOC_TOO_LARGE if B*Hq*splits*D exceeds
+// SQ_NOALLOC_MAX_PARTIAL_FLOATS or B*Hq*splits exceeds SQ_NOALLOC_MAX_LSE;
+// SQ_NOALLOC_BAD_ARGUMENT if the shape is one the kernel does not handle (Hkv <= 0,
+// Hq not a multiple of Hkv, more than 16 query heads per KV head, D not 32/64/128,
+// page_size not a positive multiple of 16, splits or tiles_per_split below 1, a KV
+// format pair other than bf16/int8/int4/int2 for both or k8 keys with v4 values, a KV
+// group below 32 or not dividing D, or a q/out row stride below Hq*D); otherwise a CUDA
+// error code. Nothing is launched when a check fails. sq_noalloc_error_string() turns a
+// return code into a message.
 //
 // Scratch: one static device array of SQ_NOALLOC_MAX_PARTIAL_FLOATS + SQ_NOALLOC_MAX_LSE
 // floats (4.125 MiB), present on every GPU that loads the library until the process exits.
@@ -32,7 +38,9 @@
 //
 // Set-up: the first call on each device (with that device current) looks up the array's
 // device address with cudaGetSymbolAddress and caches it; make that first call before
-// any stream capture on the device.
+// any stream capture on the device. The cached address belongs to the device's current
+// context: after cudaDeviceReset on a device the cache is stale, so a process that resets
+// a device must not call this entry point on it again.
 #pragma once
 
 #ifdef __cplusplus
@@ -42,6 +50,7 @@ extern "C" {
 #define SQ_NOALLOC_MAX_PARTIAL_FLOATS (1 << 20)
 #define SQ_NOALLOC_MAX_LSE (1 << 15)
 #define SQ_NOALLOC_TOO_LARGE (-1)
+#define SQ_NOALLOC_BAD_ARGUMENT (-2)
 
 int sq_paged_decode_attention_noalloc(const void* q, int ld_q, const void* k_codes, const void* k_scales,
                                       const void* v_codes, const void* v_scales, const int* block_tables,
