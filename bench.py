@@ -469,9 +469,15 @@ def run_reference(args, world, rank, local):
     logits_host = C * L_max * V * 4  # fp32 logits of every position, copied to the host each step
     local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
     host_need = 2 * logits_host + (8 << 30)  # the previous step's array is alive while the next is copied
-    host_avail = host_memory_available() // max(1, local_world)
+    host_avail = int(0.92 * host_memory_available()) // max(1, local_world)
     free_dev, _ = torch.cuda.mem_get_info()
-    dev_need = 16e9 + C * L_max * V * (2 * 2 + 4) + C * L_max * 18944 * 2 * 3
+    # fp16 weights, the KV the HF forward returns, and at the peak either two fp16 logit
+    # tensors (the previous step's output is alive during the forward) plus activations, or
+    # the fp16 logits plus their fp32 copy; 10 % margin
+    tokens = C * L_max
+    kv = tokens * 28 * 2 * 512 * 2
+    peak = max(2 * tokens * V * 2 + tokens * 18944 * 2 * 3, tokens * V * (2 + 4))
+    dev_need = 1.1 * (15.3e9 + kv + peak)
     why = None
     if host_need > host_avail:
         why = (f"host memory: the stock path copies {C}x{L_max}x{V} fp32 logits to the host every step "
@@ -497,7 +503,7 @@ def run_reference(args, world, rank, local):
         ``max_tokens``, as ``ignore_eos`` does in our arm."""
 
         eos_token_id = 1 << 30
-        pad_token_id = 0
+        pad_token_id = 1  # nonzero: the scheduler takes `pad_token_id or eos_token_id or 0` as its pad id
 
         def encode(self, text, add_special_tokens=True):
             return [int(t) for t in text.split()]
@@ -509,6 +515,11 @@ def run_reference(args, world, rank, local):
             return " ".join(str(int(i)) for i in ids)
 
     tok = TokenIdTokenizer()
+    # the scheduler pads every row of the batch with this id and feeds it to the embedding:
+    # it must be a token of the vocabulary (the EOS id above never is, on purpose)
+    pad = tok.pad_token_id or tok.eos_token_id or 0
+    if not 0 <= pad < V:
+        return {"impl": "reference", "unavailable": f"pad id {pad} outside the vocabulary"}
     rng = np.random.default_rng(1000 + args.seed + rank)
 
     def prompt_text(n):

@@ -94,7 +94,7 @@ def main():
     ap.add_argument("--copies", type=int, default=8, help="weight copies cycled (their total exceeds L2)")
     ap.add_argument("--json", default=None)
     ap.add_argument("--ms", default="1,16,64,128,512,2048")
-    ap.add_argument("--ops", default="qkv,o_proj,gate_up,down,lm_head", help="GEMM shapes to time")
+    ap.add_argument("--ops", default="qkv,o_proj,gate_up,down,lm_head", help="GEMM shapes to time ('none': skip)")
     ap.add_argument("--no-attn", action="store_true", help="skip the attention timings")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
@@ -106,7 +106,7 @@ def main():
     rows = []
     ms = [int(x) for x in args.ms.split(",")]
     for name, (n, k) in shapes.items():
-        if name not in args.ops.split(","):
+        if name not in args.ops.split(",") or args.ops == "none":
             continue
         wb = n * k // 2
         copies = max(2, min(args.copies, -(-384 * 2**20 // wb)))  # > 3x L2 of weights in the rotation

@@ -33,7 +33,7 @@ def default_device() -> str:
 
 
 def load_engine(model: str, device: str | None = None, seed: int = 0, kv_dtype: str | None = None,
-                ecfg: EngineConfig | None = None, **engine_kw) -> Loaded:
+                ecfg: EngineConfig | None = None, page_size: int | None = None, **engine_kw) -> Loaded:
     from .utils.startup import StartupPhase, StartupTimer
 
     t0 = time.time()
@@ -54,6 +54,10 @@ def load_engine(model: str, device: str | None = None, seed: int = 0, kv_dtype: 
             ck, tok_dir = load_checkpoint(model, str(dev))
             if kv_dtype:
                 ck.quant.kv_dtype = kv_dtype
+    if page_size:
+        if page_size % 16 or page_size <= 0:
+            raise ValueError(f"page size {page_size} is not a positive multiple of 16")
+        ck.quant.page_size = int(page_size)
     with StartupTimer(StartupPhase.WEIGHT_UPLOAD, "engine (weights, KV pool, graphs)"):
         eng = LLMEngine.from_checkpoint(ck, dev, ecfg, **engine_kw)
     with StartupTimer(StartupPhase.TOKENIZER):

@@ -50,16 +50,69 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
     p.add_argument("--compress-ratio", type=float, default=0.5)
     p.add_argument("--compress-min-tokens", type=int, default=256)
     p.add_argument("--compress-preserve-tokens", type=int, default=0)
+    p.add_argument("--page-size", type=int, default=None, help="KV page size in tokens (a multiple of 16)")
+    # speculative decoding (the reference serves with prompt lookup on: squish/server.py:5194)
+    sp = ucfg.load()["speculative"]
+    p.add_argument("--prompt-lookup", dest="prompt_lookup", action="store_true", default=bool(sp["prompt_lookup"]),
+                   help="greedy-lossless n-gram drafts from the request's own tokens (default on)")
+    p.add_argument("--no-prompt-lookup", dest="prompt_lookup", action="store_false")
+    p.add_argument("--prompt-lookup-n", type=int, default=int(sp["prompt_lookup_n"]), help="longest n-gram matched")
+    p.add_argument("--prompt-lookup-k", type=int, default=int(sp["prompt_lookup_k"]), help="draft tokens per round")
+    p.add_argument("--draft-model", default=sp["draft_model"] or None,
+                   help="draft model (checkpoint or preset of the same vocabulary) for draft/verify decoding")
+    p.add_argument("--draft-depth", type=int, default=int(sp["draft_depth"]), help="draft tokens per round")
+    p.add_argument("--jacobi", action="store_true", help="Jacobi (fixed-point) parallel decoding")
+    p.add_argument("--spec-branches", type=int, default=1, help="prompt lookup: continuations per draft tree")
+    # multi-GPU
+    p.add_argument("--tp", type=int, default=1, help="tensor-parallel GPUs (one process per GPU over NVLink)")
+    p.add_argument("--ep", type=int, default=0,
+                   help="expert-parallel GPUs for MoE models (experts split over ranks; sets --tp)")
+    p.add_argument("--dp", type=int, default=1, help="data-parallel replicas (one per GPU) behind a request router")
+    p.add_argument("--gpus", type=int, default=0, help="GPUs to use: tp x dp (dp = gpus / tp when --dp is not given)")
+    p.add_argument("--tp-mode", default="nvlink", choices=["nvlink", "nccl"],
+                   help="nvlink: fused GEMM + collectives over peer memory; nccl: NCCL collectives")
+    p.add_argument("--log-level", default="warning", choices=["debug", "info", "warning", "error", "critical"])
+    p.add_argument("--log-format", default="text", choices=["text", "json"], help="json: one JSON object per line")
+
+
+def _spec(a):
+    """SpecConfig from the flags: a draft model wins over Jacobi, which wins over prompt lookup."""
+    from .engine.speculative import SpecConfig
+
+    if getattr(a, "draft_model", None):
+        return SpecConfig(method="draft", k=a.draft_depth, draft_model=a.draft_model)
+    if getattr(a, "jacobi", False):
+        return SpecConfig(method="jacobi", k=a.draft_depth)
+    if getattr(a, "prompt_lookup", False):
+        return SpecConfig(method="prompt_lookup", k=a.prompt_lookup_k, ngram_max=a.prompt_lookup_n,
+                          branches=max(1, a.spec_branches))
+    return None
+
+
+def _parallel(a) -> tuple[int, int]:
+    """(tp, dp) from --tp / --ep / --dp / --gpus."""
+    tp = max(1, getattr(a, "tp", 1), getattr(a, "ep", 0) or 1)
+    dp = max(1, getattr(a, "dp", 1))
+    gpus = getattr(a, "gpus", 0) or 0
+    if gpus:
+        if gpus % tp:
+            raise SystemExit(f"--gpus {gpus} is not a multiple of --tp {tp}")
+        if dp == 1:
+            dp = gpus // tp
+        elif dp * tp != gpus:
+            raise SystemExit(f"--gpus {gpus} != --tp {tp} x --dp {dp}")
+    return tp, dp
 
 
 def _ecfg(a):
     from .engine.engine import EngineConfig
 
+    tp, _ = _parallel(a)
     return EngineConfig(max_num_seqs=a.max_num_seqs, max_num_batched_tokens=a.max_num_batched_tokens,
                         max_model_len=a.max_model_len, gpu_memory_utilization=a.gpu_memory_utilization,
                         enable_prefix_caching=not a.no_prefix_caching, cuda_graphs=not a.no_cuda_graphs,
                         chunk_align=a.chunk_align, seed=a.seed, kv_host_bytes=int(a.kv_host_gb * (1 << 30)),
-                        kv_disk_dir=a.kv_disk_dir)
+                        kv_disk_dir=a.kv_disk_dir, spec=_spec(a), tp=tp, tp_mode=getattr(a, "tp_mode", "nvlink"))
 
 
 def _kv(a):
@@ -74,16 +127,97 @@ def _model(a) -> str:
     return a.model or ucfg.get("model.default")
 
 
+def _logging(a) -> None:
+    from .utils.logconfig import configure_logging
+
+    configure_logging(getattr(a, "log_level", "warning"), json_format=getattr(a, "log_format", "text") == "json")
+
+
+def _relaunch_ranks(tp: int) -> int:
+    """Start the tensor-parallel ranks: this command again under torch.distributed.run, one
+    process per GPU (rank 0 serves HTTP, the others follow its steps)."""
+    import socket
+    import subprocess
+
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={tp}",
+           "--master-addr", "127.0.0.1", "--master-port", str(port), "-m", "squish_b200", *sys.argv[1:]]
+    return subprocess.call(cmd)
+
+
+def _tp_rank_setup(a, tp: int):
+    """Join the process group of a tensor-parallel server; returns (rank, device string)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    rank, local = int(os.environ["RANK"]), int(os.environ.get("LOCAL_RANK", "0"))
+    if int(os.environ.get("WORLD_SIZE", "1")) != tp:
+        raise SystemExit(f"WORLD_SIZE {os.environ.get('WORLD_SIZE')} != --tp {tp}")
+    if torch.cuda.is_available() and (a.device or "cuda").startswith("cuda"):
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        return rank, f"cuda:{local}"
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    return rank, "cpu"
+
+
+def _build_frontend(a, max_pending: int):
+    """Load the model(s) and return (front-end engine, Loaded of replica 0, follower or None).
+    One GPU: an AsyncEngine. --dp N: N replicas (cuda:0..N-1) behind a DPRouter. --tp N:
+    this process is one rank; rank 0 gets a TPAsyncEngine, the others a follower callable."""
+    from .api import load_engine
+    from .serving.async_engine import AsyncEngine
+
+    tp, dp = _parallel(a)
+    if tp > 1 and dp > 1:
+        raise SystemExit("--tp and --dp together are not supported: use one of them")
+    if tp > 1:
+        from .serving.multi import TPAsyncEngine, TPControl, follow
+
+        rank, dev = _tp_rank_setup(a, tp)
+        loaded = load_engine(_model(a), dev, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a), page_size=a.page_size)
+        ctrl = TPControl()
+        if rank != 0:
+            return None, loaded, lambda: follow(loaded.engine, ctrl)
+        aeng = TPAsyncEngine(loaded.engine, ctrl, loaded.tokenizer, max_pending=max_pending, model_name=loaded.name)
+        return aeng.start(), loaded, None
+    if dp > 1:
+        import torch
+
+        from .serving.multi import DPRouter
+
+        base = a.device or ("cuda" if torch.cuda.is_available() else "cpu")
+        reps, first = [], None
+        for i in range(dp):
+            dev = f"cuda:{i}" if base.startswith("cuda") else base
+            ld = load_engine(_model(a), dev, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a), page_size=a.page_size)
+            first = first or ld
+            reps.append(AsyncEngine(ld.engine, ld.tokenizer, max_pending=max_pending, model_name=ld.name))
+        return DPRouter(reps, max_pending=max_pending).start(), first, None
+    loaded = load_engine(_model(a), a.device, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a), page_size=a.page_size)
+    return AsyncEngine(loaded.engine, loaded.tokenizer, max_pending=max_pending, model_name=loaded.name).start(), \
+        loaded, None
+
+
 def cmd_serve(a) -> int:
     import uvicorn
 
-    from .api import load_engine
-    from .serving.async_engine import AsyncEngine
     from .serving.server import ServerState, create_app
 
+    _logging(a)
+    tp, _ = _parallel(a)
+    if tp > 1 and "RANK" not in os.environ:
+        return _relaunch_ranks(tp)
     c = ucfg.load()["server"]
-    loaded = load_engine(_model(a), a.device, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a))
-    aeng = AsyncEngine(loaded.engine, loaded.tokenizer, max_pending=c["max_pending"], model_name=loaded.name).start()
+    aeng, loaded, follower = _build_frontend(a, c["max_pending"])
+    if follower is not None:
+        follower()
+        return 0
     key = a.api_key if a.api_key is not None else os.environ.get("SQUISH_API_KEY", c["api_key"])
     cp = ({"ratio": a.compress_ratio, "min_tokens": a.compress_min_tokens,
            "preserve_tokens": a.compress_preserve_tokens} if getattr(a, "compress_prompt", False) else None)
@@ -105,7 +239,8 @@ def cmd_run(a) -> int:
     from .engine.sampling import SamplingParams
     from .serving.chat_template import apply_chat_template
 
-    llm = LLM(_model(a), a.device, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a))
+    _logging(a)
+    llm = LLM(_model(a), a.device, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a), page_size=a.page_size)
     prompt = apply_chat_template([{"role": "user", "content": " ".join(a.text)}], llm.tokenizer,
                                  arch=llm.engine.cfg.arch)
     p = SamplingParams(max_tokens=a.max_tokens, temperature=a.temperature, top_p=a.top_p,
@@ -221,7 +356,7 @@ def cmd_bench(a) -> int:
     from .api import load_engine
     from .utils.loadgen import run_load
 
-    loaded = load_engine(_model(a), a.device, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a))
+    loaded = load_engine(_model(a), a.device, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a), page_size=a.page_size)
     sync = torch.cuda.synchronize if torch.cuda.is_available() and loaded.engine.runner.__class__.__name__ == \
         "CudaRunner" else None
     rows = []

@@ -11,6 +11,8 @@
 // is the quantized KV bytes per step, not MMA rate.
 //
 // Softmax runs in the log2 domain (scores pre-multiplied by scale*log2(e), exp2f).
+#include <cstdlib>
+
 #include "kernels.h"
 #include "kv_format.cuh"
 #include "launch.cuh"
@@ -368,6 +370,374 @@ __global__ void __launch_bounds__(128, (FK == KV_BF16 || kv_bits(FK) == 8) ? 3 :
   }
 }
 
+// ----------------------------------------------------------------------------- decode, token-major MMA
+// Decode attention with the 16 keys of a tile on the MMA M side and the (<= 8) query heads of
+// one KV head on the N side, so an m16n8k16 tile wastes nothing on a GQA group of 7-8
+// heads, and with the keys multiplied in their quantized form:
+//
+//  * a key code c becomes the exact operand M0 + c by one byte permute with a constant
+//    exponent byte (bf16 128 + c for 4-bit codes, fp16 1024 + c for 8-bit codes), straight
+//    from global memory into the A fragment (no shared memory, no per-element scaling);
+//    with key value v = s * c + z per (token, group), q . k over a group is
+//    s * (q . (M0 + c)) + (z - M0 * s) * sum(q), so each group's MMA sum is scaled once per
+//    (token, head) afterwards. Every MMA k-step takes its 16 dims from one scale group.
+//    The sum(q) terms use the same rounded q values as the MMA, and the products are
+//    exact in fp32, so the M0 offset cancels to fp32 rounding;
+//  * values are dequantized once into a per-warp shared-memory tile (exact code, then one
+//    bf16 FMA with the group's scale and zero, as in the prefill kernels), dims permuted
+//    inside each 8-dim chunk to the order the byte permute produces; O^T = V^T P^T takes
+//    V^T by ldmatrix.trans and P^T from the score accumulators by movmatrix.trans;
+//  * softmax runs per head over the key axis (three shuffles), with the lazy running-max
+//    raise of the other kernels (O is rescaled only when a head's max grows by > 2^8).
+// Reference op: squish_quant_rs/src/lib.rs:3056 flash_decode_split_f32 (one split of
+// per-head softmax(q K^T / sqrt(d)) V with (out, lse) for the merge).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+__device__ __forceinline__ uint32_t movtrans(uint32_t x) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+__device__ __forceinline__ void mma16816_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// dims of the 8 positions of a value-tile chunk (the byte permute's order)
+__device__ __forceinline__ int vperm(int col) { return (col & ~7) | ((col & 3) << 1) | ((col >> 2) & 1); }
+
+template <int D, int FK, int FV, int NG>
+__global__ void __launch_bounds__(128, 4) decode_tm_kernel(const AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int NW = 4;
+  constexpr bool K8 = (FK == KV_K8);      // 8-bit keys: fp16 operands (1024 + c is exact)
+  constexpr int NS = D / 16;              // k-steps of the score MMA
+  constexpr int SPG = NS / NG;            // k-steps per key scale group
+  constexpr int KW = K8 ? D / 16 : D / 32;  // key code words a thread loads per token
+  constexpr int LDV = D + 8;
+  constexpr int CBK = kv_code_bytes(FK, D), CBV = kv_code_bytes(FV, D);
+  constexpr int NSK = NG * (kv_asym(FK) ? 2 : 1), NSV = NG * (kv_asym(FV) ? 2 : 1);
+  constexpr int G = D / NG;
+  static_assert(FV == KV_INT4 || FV == KV_V4, "4-bit values");
+  extern __shared__ __align__(16) uint8_t sm[];
+  uint16_t* Qs = reinterpret_cast<uint16_t*>(sm);                       // [8][D] operand-type bits
+  float* qsum = reinterpret_cast<float*>(sm + 8 * D * 2);               // [8][NG]
+  __nv_bfloat16* Vt = reinterpret_cast<__nv_bfloat16*>(sm + 8 * D * 2 + 8 * NG * 4);  // [NW][16][LDV]
+  const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int Gq = p.Hq / p.Hkv;
+  const int kv_len = p.seq_lens[b];
+  const int n_tiles = (kv_len + 15) / 16;
+  const int t0 = split * p.tiles_per_split;
+  const int t1 = min(n_tiles, t0 + p.tiles_per_split);
+  const int* bt = p.block_tables + (size_t)b * p.bt_stride;
+  const int PS = p.page_size;
+  const float scale = p.sm_scale * kLog2e;
+
+  // Q rows of this KV head's query heads (rows >= Gq zero), converted to the key operand type
+  {
+    const __nv_bfloat16* qb = p.q + (size_t)b * p.ld_q + (size_t)h * Gq * D;
+    for (int i = threadIdx.x; i < 8 * D / 2; i += blockDim.x) {
+      const int r = i / (D / 2), c = 2 * (i % (D / 2));
+      float2 f = make_float2(0.f, 0.f);
+      if (r < Gq) f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(qb + (size_t)r * D + c));
+      *reinterpret_cast<uint32_t*>(Qs + r * D + c) = K8 ? pack_h2(f.x, f.y) : pack_bf2(f.x, f.y);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 8 * NG) {  // per (head, group) sums of the rounded operand values
+    const int r = threadIdx.x / NG, gg = threadIdx.x % NG;
+    float acc = 0.f;
+    for (int d = gg * G; d < gg * G + G; ++d) {
+      const uint16_t u = Qs[r * D + d];
+      acc += K8 ? __half2float(__ushort_as_half(u)) : __bfloat162float(__ushort_as_bfloat16(u));
+    }
+    qsum[r * NG + gg] = acc;
+  }
+  // B fragments of Q^T for every k-step: b0 = (Q[g][pi(2t4)], Q[g][pi(2t4+1)]),
+  // b1 = (Q[g][pi(2t4+8)], Q[g][pi(2t4+9)]) in the dim order of this thread's key bytes
+  uint32_t qf[NS][2];
+#pragma unroll
+  for (int s = 0; s < NS; ++s) {
+    int d0;
+    if constexpr (K8) {
+      d0 = 4 * (t4 + 4 * s);  // word t4 + 4s: dims d0 .. d0 + 3
+      qf[s][0] = *reinterpret_cast<const uint32_t*>(Qs + g * D + d0);
+      qf[s][1] = *reinterpret_cast<const uint32_t*>(Qs + g * D + d0 + 2);
+    } else {
+      const int i = s >> 1, e = s & 1;  // word t4 + 4i, low (e = 0) or high nibbles
+      d0 = 8 * (t4 + 4 * i) + e;
+      qf[s][0] = (uint32_t)Qs[g * D + d0] | ((uint32_t)Qs[g * D + d0 + 2] << 16);
+      qf[s][1] = (uint32_t)Qs[g * D + d0 + 4] | ((uint32_t)Qs[g * D + d0 + 6] << 16);
+    }
+  }
+  __syncthreads();
+  float qs_a[NG], qs_b[NG];  // sums for this thread's two heads 2t4, 2t4 + 1
+#pragma unroll
+  for (int gg = 0; gg < NG; ++gg) {
+    qs_a[gg] = qsum[(2 * t4) * NG + gg];
+    qs_b[gg] = qsum[(2 * t4 + 1) * NG + gg];
+  }
+
+  float o[D / 16][4];
+#pragma unroll
+  for (int i = 0; i < D / 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  __nv_bfloat16* Vs = Vt + warp * 16 * LDV;
+  const uint32_t vbase = smem_addr(Vs);
+
+  // per tile: key words of tokens g and g + 8, their scales, and this lane's half value row
+  uint32_t kw[2][KW];
+  float ks[2][NG], kz[2][NG];
+  uint32_t vw[D / 16];
+  float vs_[NG > 1 ? NG / 2 : 1], vz_[NG > 1 ? NG / 2 : 1];
+  const int vr = lane >> 1, vhalf = lane & 1;
+  constexpr int NGH = NG > 1 ? NG / 2 : 1;  // value scale groups in half a row
+  auto fetch = [&](int tile) {
+    const bool live = tile < t1;
+    const int page = live ? __ldg(bt + (tile * 16) / PS) : 0;
+    const size_t row0 = ((size_t)page * p.Hkv + h) * PS + ((tile * 16) % PS);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int tok = tile * 16 + g + 8 * j;
+      const bool ok = live && tok < kv_len;
+      const size_t row = row0 + g + 8 * j;
+      const uint32_t* kc = reinterpret_cast<const uint32_t*>(p.k_codes + row * CBK);
+#pragma unroll
+      for (int i = 0; i < KW; ++i) kw[j][i] = ok ? __ldg(kc + t4 + 4 * i) : 0u;
+      const __half* sc = p.k_scales + row * NSK;
+#pragma unroll
+      for (int gg = 0; gg < NG; ++gg) {
+        float s_ = 0.f, z_ = 0.f;
+        if (ok) {
+          if constexpr (kv_asym(FK)) {
+            const __half2 sz = __ldg(reinterpret_cast<const __half2*>(sc) + gg);
+            s_ = __low2float(sz);
+            z_ = __high2float(sz);
+          } else {
+            s_ = __half2float(__ldg(sc + gg));
+            z_ = -7.5f * s_;
+          }
+        }
+        // s * (q . (M0 + c)) + (z - M0 * s) * sum(q)
+        ks[j][gg] = s_;
+        kz[j][gg] = z_ - (K8 ? 1024.f : 128.f) * s_;
+      }
+    }
+    {
+      const int tok = tile * 16 + vr;
+      const bool ok = live && tok < kv_len;
+      const size_t row = row0 + vr;
+      const uint4* vc = reinterpret_cast<const uint4*>(p.v_codes + row * CBV + vhalf * (CBV / 2));
+#pragma unroll
+      for (int i = 0; i < D / 64; ++i) {
+        const uint4 u = ok ? __ldg(vc + i) : make_uint4(0u, 0u, 0u, 0u);
+        vw[4 * i] = u.x;
+        vw[4 * i + 1] = u.y;
+        vw[4 * i + 2] = u.z;
+        vw[4 * i + 3] = u.w;
+      }
+      const __half* sc = p.v_scales + row * NSV;
+#pragma unroll
+      for (int q = 0; q < NGH; ++q) {
+        const int gg = NG > 1 ? vhalf * NGH + q : 0;
+        float s_ = 0.f, z_ = 0.f;
+        if (ok) {
+          if constexpr (kv_asym(FV)) {
+            const __half2 sz = __ldg(reinterpret_cast<const __half2*>(sc) + gg);
+            s_ = __low2float(sz);
+            z_ = __high2float(sz);
+          } else {
+            s_ = __half2float(__ldg(sc + gg));
+            z_ = -7.5f * s_;
+          }
+        }
+        vs_[q] = s_;
+        vz_[q] = z_;
+      }
+    }
+  };
+
+  fetch(t0 + warp);
+  constexpr uint32_t kMagicB = 0x43434343u, kMagicH = 0x64646464u;
+  for (int tile = t0 + warp; tile < t1; tile += NW) {
+    // ---- values of this tile -> shared memory (exact code, one FMA with scale and zero)
+    {
+      const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.f, 128.f);
+#pragma unroll
+      for (int c = 0; c < D / 16; ++c) {  // 8-dim chunks of this lane's half row
+        const int q = NG > 1 ? (c * 8) / G : 0;
+        const __nv_bfloat162 s2 = __floats2bfloat162_rn(vs_[q], vs_[q]);
+        const __nv_bfloat162 z2 = __floats2bfloat162_rn(vz_[q], vz_[q]);
+        const uint32_t L = vw[c] & 0x0F0F0F0Fu, H = (vw[c] >> 4) & 0x0F0F0F0Fu;
+        uint32_t t[4] = {prmt(L, kMagicB, 0x4140u), prmt(L, kMagicB, 0x4342u), prmt(H, kMagicB, 0x4140u),
+                         prmt(H, kMagicB, 0x4342u)};
+        uint32_t o4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 v = __hfma2(__hsub2(*reinterpret_cast<__nv_bfloat162*>(&t[e]), k128), s2, z2);
+          o4[e] = *reinterpret_cast<const uint32_t*>(&v);
+        }
+        *reinterpret_cast<uint4*>(Vs + vr * LDV + vhalf * (D / 2) + c * 8) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+      }
+    }
+    // ---- scores S^T[token][head] = K Q^T, one scale group at a time
+    float sc4[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t kcur[2][KW];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int i = 0; i < KW; ++i) kcur[j][i] = kw[j][i];
+    float kss[2][NG], kzz[2][NG];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int gg = 0; gg < NG; ++gg) {
+        kss[j][gg] = ks[j][gg];
+        kzz[j][gg] = kz[j][gg];
+      }
+    fetch(tile + NW);  // the next tile's codes are in flight during this tile's math
+    __syncwarp();
+#pragma unroll
+    for (int gg = 0; gg < NG; ++gg) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ss = 0; ss < SPG; ++ss) {
+        const int s = gg * SPG + ss;
+        uint32_t a0, a1, a2, a3;
+        if constexpr (K8) {
+          a0 = prmt(kcur[0][s], kMagicH, 0x4140u);
+          a2 = prmt(kcur[0][s], kMagicH, 0x4342u);
+          a1 = prmt(kcur[1][s], kMagicH, 0x4140u);
+          a3 = prmt(kcur[1][s], kMagicH, 0x4342u);
+          mma16816_f16(acc, a0, a1, a2, a3, qf[s][0], qf[s][1]);
+        } else {
+          const int i = s >> 1, e = s & 1;
+          const uint32_t w0 = e ? (kcur[0][i] >> 4) & 0x0F0F0F0Fu : kcur[0][i] & 0x0F0F0F0Fu;
+          const uint32_t w1 = e ? (kcur[1][i] >> 4) & 0x0F0F0F0Fu : kcur[1][i] & 0x0F0F0F0Fu;
+          a0 = prmt(w0, kMagicB, 0x4140u);
+          a2 = prmt(w0, kMagicB, 0x4342u);
+          a1 = prmt(w1, kMagicB, 0x4140u);
+          a3 = prmt(w1, kMagicB, 0x4342u);
+          mma16816(acc, a0, a1, a2, a3, qf[s][0], qf[s][1]);
+        }
+      }
+      // acc: (token g, head 2t4), (g, 2t4+1), (g+8, 2t4), (g+8, 2t4+1)
+      sc4[0] = fmaf(kss[0][gg], acc[0], fmaf(kzz[0][gg], qs_a[gg], sc4[0]));
+      sc4[1] = fmaf(kss[0][gg], acc[1], fmaf(kzz[0][gg], qs_b[gg], sc4[1]));
+      sc4[2] = fmaf(kss[1][gg], acc[2], fmaf(kzz[1][gg], qs_a[gg], sc4[2]));
+      sc4[3] = fmaf(kss[1][gg], acc[3], fmaf(kzz[1][gg], qs_b[gg], sc4[3]));
+    }
+    // ---- online softmax per head over the 16 keys (log2 domain)
+    const int tok0 = tile * 16;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int tok = tok0 + g + 8 * (e >> 1);
+      sc4[e] = (tok < kv_len) ? sc4[e] * scale : -INFINITY;
+    }
+    float mx_a = fmaxf(sc4[0], sc4[2]), mx_b = fmaxf(sc4[1], sc4[3]);
+#pragma unroll
+    for (int off = 4; off <= 16; off <<= 1) {
+      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
+      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+    }
+    const bool ra = mx_a > m_a + 8.f, rb = mx_b > m_b + 8.f;
+    if (__any_sync(0xffffffffu, ra || rb)) {
+      const float al_a = ra ? ex2f(m_a - mx_a) : 1.f, al_b = rb ? ex2f(m_b - mx_b) : 1.f;
+      if (ra) m_a = mx_a;
+      if (rb) m_b = mx_b;
+      l_a *= al_a;
+      l_b *= al_b;
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) {
+        o[i][0] *= al_a;
+        o[i][1] *= al_b;
+        o[i][2] *= al_a;
+        o[i][3] *= al_b;
+      }
+    }
+    const float base_a = (m_a == -INFINITY) ? 0.f : m_a, base_b = (m_b == -INFINITY) ? 0.f : m_b;
+    const float p0 = ex2f(sc4[0] - base_a), p1 = ex2f(sc4[1] - base_b);
+    const float p2 = ex2f(sc4[2] - base_a), p3 = ex2f(sc4[3] - base_b);
+    l_a += p0 + p2;
+    l_b += p1 + p3;
+    // P^T as the B operand: transpose the two 8x8 (token x head) blocks in registers
+    const uint32_t pb0 = movtrans(pack_bf2(p0, p1)), pb1 = movtrans(pack_bf2(p2, p3));
+    // ---- O^T[dim][head] += V^T P^T
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) {
+      const int j = lane >> 3;
+      const int tok = (lane & 7) + ((j >> 1) << 3);
+      const int col = mt * 16 + ((j & 1) << 3);
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(vbase + (tok * LDV + col) * 2, a0, a1, a2, a3);
+      mma16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+    }
+    __syncwarp();
+  }
+#pragma unroll
+  for (int off = 4; off <= 16; off <<= 1) {
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, off);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, off);
+  }
+  // cross-warp merge through shared memory: m, l [warp][8 heads], O [warp][8 heads][D]
+  __syncthreads();
+  float* mw = reinterpret_cast<float*>(sm);
+  float* lw = mw + NW * 8;
+  float* ow = lw + NW * 8;
+  if (g == 0) {
+    mw[warp * 8 + 2 * t4] = m_a;
+    mw[warp * 8 + 2 * t4 + 1] = m_b;
+    lw[warp * 8 + 2 * t4] = l_a;
+    lw[warp * 8 + 2 * t4 + 1] = l_b;
+  }
+#pragma unroll
+  for (int mt = 0; mt < D / 16; ++mt) {
+    const int d0 = vperm(mt * 16 + g), d1 = vperm(mt * 16 + g + 8);
+    ow[(warp * 8 + 2 * t4) * D + d0] = o[mt][0];
+    ow[(warp * 8 + 2 * t4 + 1) * D + d0] = o[mt][1];
+    ow[(warp * 8 + 2 * t4) * D + d1] = o[mt][2];
+    ow[(warp * 8 + 2 * t4 + 1) * D + d1] = o[mt][3];
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < Gq * D; idx += blockDim.x) {
+    const int row = idx / D, d = idx % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, mw[w * 8 + row]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float f = (mw[w * 8 + row] == -INFINITY) ? 0.f : exp2f(mw[w * 8 + row] - M);
+        L += lw[w * 8 + row] * f;
+        O += ow[(w * 8 + row) * D + d] * f;
+      }
+    }
+    const int hq = h * Gq + row;
+    if (p.splits == 1) {
+      p.out[(size_t)b * p.ld_out + (size_t)hq * D + d] = __float2bfloat16(L > 0.f ? O / L : 0.f);
+    } else {
+      const size_t base = ((size_t)b * p.Hq + hq) * p.splits + split;
+      p.o_part[base * D + d] = (L > 0.f) ? O / L : 0.f;
+      if (d == 0) p.lse_part[base] = (L > 0.f) ? M + log2f(L) : -INFINITY;
+    }
+  }
+}
+
 // grid (B, Hq), D threads: combine split partials (log2-domain LSE weights).
 __global__ void decode_merge_kernel(const AttnParams p) {
   pdl_wait();
@@ -671,10 +1041,56 @@ cudaError_t launch_prefill(const AttnParams& p, cudaStream_t s) {
 SQ_ATTN_DISPATCH(launch_decode)
 SQ_ATTN_DISPATCH(launch_prefill)
 
+template <int D, int FK, int FV, int NG>
+cudaError_t launch_decode_tm(const AttnParams& p, cudaStream_t s) {
+  constexpr int LDV = D + 8;
+  const size_t main_bytes = (size_t)8 * D * 2 + (size_t)8 * NG * 4 + (size_t)4 * 16 * LDV * 2;
+  const size_t merge_bytes = (size_t)4 * 8 * 2 * 4 + (size_t)4 * 8 * D * 4;
+  const size_t smem = main_bytes > merge_bytes ? main_bytes : merge_bytes;
+  auto k = decode_tm_kernel<D, FK, FV, NG>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaError_t le = launch_k(k, dim3(p.B, p.Hkv, p.splits), dim3(128), smem, s, 1, p);
+  if (le != cudaSuccess) return le;
+  e = cudaGetLastError();
+  if (e != cudaSuccess || p.splits == 1) return e;
+  le = launch_k(decode_merge_kernel, dim3(p.B, p.Hq), dim3(D), 0, s, 1, p);
+  if (le != cudaSuccess) return le;
+  return cudaGetLastError();
+}
+
+template <int D, int FK, int FV>
+cudaError_t launch_decode_tm_g(const AttnParams& p, cudaStream_t s) {
+  const int ng = D / p.group;
+  if (ng == 1) return launch_decode_tm<D, FK, FV, 1>(p, s);
+  if (ng == 2) return launch_decode_tm<D, FK, FV, 2>(p, s);
+  if (ng == 4) return launch_decode_tm<D, FK, FV, 4>(p, s);
+  return cudaErrorInvalidValue;
+}
+
+// The token-major decode kernel covers 4-bit values with 4-bit symmetric or 8-bit
+// asymmetric keys, up to 8 query heads per KV head, head dims 64 / 128, and 1, 2 or 4
+// scale groups per row (group >= 32); other cases run decode_kernel.
+bool decode_tm_supported(const AttnParams& p) {
+  if (p.Hkv <= 0 || p.Hq % p.Hkv != 0 || p.Hq / p.Hkv > 8) return false;
+  if (p.D != 128 && p.D != 64) return false;
+  if (p.group < 32 || p.D % p.group != 0 || p.D / p.group > 4) return false;
+  if (std::getenv("SQ_DECODE_LEGACY") != nullptr) return false;
+  return (p.fmt_k == KV_INT4 && p.fmt_v == KV_INT4) || (p.fmt_k == KV_K8 && p.fmt_v == KV_V4);
+}
+
+cudaError_t launch_decode_tm_any(const AttnParams& p, cudaStream_t s) {
+  if (p.fmt_k == KV_INT4) {
+    return p.D == 128 ? launch_decode_tm_g<128, KV_INT4, KV_INT4>(p, s) : launch_decode_tm_g<64, KV_INT4, KV_INT4>(p, s);
+  }
+  return p.D == 128 ? launch_decode_tm_g<128, KV_K8, KV_V4>(p, s) : launch_decode_tm_g<64, KV_K8, KV_V4>(p, s);
+}
+
 }  // namespace
 
 cudaError_t paged_decode_attn_launch(const AttnParams& p, cudaStream_t s) {
   if (p.B == 0) return cudaSuccess;
+  if (decode_tm_supported(p)) return launch_decode_tm_any(p, s);
   if (p.D == 128) return launch_decode_fmt<128>(p, s);
   if (p.D == 64) return launch_decode_fmt<64>(p, s);
   if (p.D == 32) return launch_decode_fmt<32>(p, s);

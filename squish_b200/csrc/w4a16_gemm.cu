@@ -761,20 +761,55 @@ bool w4a16_narrow(int wfmt, int gpk) {
   return !wide && wfmt == WF_INT4 && gpk == 1;
 }
 
+static int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+// Decode shapes stream their weights: a CTA keeps as many weight stages in flight as the
+// shared memory its SM share allows. The launch's CTAs per SM decide that share: with two or
+// fewer per SM each CTA takes half of the 228 KiB (deep rings, four TMEM A stages), otherwise
+// a quarter (the four-CTA configuration).
+template <int BN>
+cudaError_t launch_decode_narrow(const CUtensorMap& xmap, const W4A16Params& p, cudaStream_t s) {
+  const long ctas = (long)((p.N + BM - 1) / BM) * ((p.M + BN - 1) / BN) * p.splits;
+  const int per_sm = (int)((ctas + sm_count() - 1) / sm_count());
+  const bool tr = p.trace != nullptr;
+  auto fit = [&](int rx, int ra, size_t budget, int lo, int hi) {
+    for (int rw = hi; rw > lo; --rw) {
+      const Layout L = make_layout(BN, 1, p.gpk, rw, rx, ra, tr, true, p.wfmt);
+      if ((size_t)L.total + 1024 <= budget) return rw;
+    }
+    return lo;
+  };
+  if (per_sm <= 2) {
+    constexpr int rx = BN >= 32 ? 4 : 6;
+    return launch_cfg<Cfg<BN, 1, 2, 4>>(xmap, p, fit(rx, 4, 113 * 1024, 4, 24), rx, 4, s);
+  }
+  constexpr int rx = BN == 64 ? 3 : BN == 32 ? 4 : 6;
+  return launch_cfg<Cfg<BN, 1, 4, 4>>(xmap, p, fit(rx, 2, 56 * 1024, 3, 12), rx, 2, s);
+}
+
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s) {
   int ow, ox, oa;
   const bool ov = ring_override(&ow, &ox, &oa);
   if (nt == 1) {
     switch (bn) {
       case 16:
-        if (!ov && w4a16_narrow(p.wfmt, p.gpk)) return launch_cfg<Cfg<16, 1, 4, 4>>(xmap, p, 6, 6, 2, s);
+        if (!ov && w4a16_narrow(p.wfmt, p.gpk)) return launch_decode_narrow<16>(xmap, p, s);
         return ov ? launch_cfg<Cfg<16, 1, 2>>(xmap, p, ow, ox, oa, s) : launch_cfg<Cfg<16, 1, 2>>(xmap, p, 8, 8, 4, s);
       case 32:
-        if (!ov && w4a16_narrow(p.wfmt, p.gpk)) return launch_cfg<Cfg<32, 1, 4, 4>>(xmap, p, 5, 4, 2, s);
+        if (!ov && w4a16_narrow(p.wfmt, p.gpk)) return launch_decode_narrow<32>(xmap, p, s);
         return ov ? launch_cfg<Cfg<32, 1, 2>>(xmap, p, ow, ox, oa, s) : launch_cfg<Cfg<32, 1, 2>>(xmap, p, 8, 6, 4, s);
       case 64:
         if (ov) return launch_cfg<Cfg<64, 1, 2>>(xmap, p, ow, ox, oa, s);
-        if (w4a16_narrow(p.wfmt, p.gpk)) return launch_cfg<Cfg<64, 1, 4, 4>>(xmap, p, 4, 3, 2, s);
+        if (w4a16_narrow(p.wfmt, p.gpk)) return launch_decode_narrow<64>(xmap, p, s);
         return launch_cfg<Cfg<64, 1, 2>>(xmap, p, 8, 6, 4, s);
       case 128: return launch_cfg<Cfg<128, 1, 2>>(xmap, p, 8, 4, 4, s);
       case 256: return launch_cfg<Cfg<256, 1, 1>>(xmap, p, 6, 4, 4, s);

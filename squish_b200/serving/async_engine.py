@@ -152,13 +152,22 @@ class AsyncEngine:
                 return GenEvent(toks, True, ev.reason, ev.prompt_tokens, ev.completion_tokens)
 
     # ------------------------------------------------------------------ engine thread
+    def _engine_abort(self, rid: str) -> None:
+        """Abort a request from inside the engine thread (loop guard, failed step)."""
+        self.engine.abort(rid)
+
     def _drain_inbox(self) -> None:
-        eng = self.engine
+        ops = []
         while True:
             try:
-                op, rid, prompt, params = self._inbox.get_nowait()
+                ops.append(self._inbox.get_nowait())
             except queue.Empty:
-                return
+                break
+        self._apply_ops(ops)
+
+    def _apply_ops(self, ops) -> None:
+        eng = self.engine
+        for op, rid, prompt, params in ops:
             if op == "add":
                 try:
                     eng.add_request(prompt, params, rid=rid)
@@ -196,7 +205,7 @@ class AsyncEngine:
                 self.errors_total += 1
                 self.last_error = repr(exc)
                 for rid in list(self._sinks):
-                    eng.abort(rid)
+                    self._engine_abort(rid)
                     self._sinks.pop(rid).put(GenEvent([], True, "error", 0, 0))
                     t0 = self._t_submit.pop(rid, time.perf_counter())
                     self._t_first.pop(rid, None)
@@ -220,7 +229,7 @@ class AsyncEngine:
 
                         g = self._guards[o.rid] = LoopGuard()
                     if g.feed(o.new_tokens):
-                        eng.abort(o.rid)  # verbatim loop: stop with finish reason "repetition"
+                        self._engine_abort(o.rid)  # verbatim loop: stop with finish reason "repetition"
                         finished, reason = True, "repetition"
                         self.loops_stopped += 1
                 sink.put(GenEvent(o.new_tokens, finished, reason, o.num_prompt_tokens, o.num_output_tokens))

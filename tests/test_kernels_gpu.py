@@ -270,6 +270,45 @@ def test_paged_decode_attention(cuda, kvfmt, hq, hkv, d, lens):
         torch.testing.assert_close(out[i].float().cpu().view(1, hq, d), ref, rtol=2e-2, atol=3e-2)
 
 
+@pytest.mark.parametrize("kvfmt,hq,hkv,d,group", [("int4", 28, 4, 128, 128), ("int4", 28, 4, 128, 64),
+                                                  ("int4", 14, 2, 64, 32), ("int4", 8, 8, 128, 32),
+                                                  ("k8v4", 64, 8, 128, 32), ("k8v4", 32, 8, 128, 128),
+                                                  ("k8v4", 16, 4, 64, 64), ("int4", 36, 4, 128, 32)])
+@pytest.mark.parametrize("legacy", [False, True])
+def test_paged_decode_attention_token_major(cuda, monkeypatch, kvfmt, hq, hkv, d, group, legacy):
+    """The token-major decode kernel (keys multiplied as codes, scales applied after the MMA)
+    and the head-major one it replaces, on every group size / head count the first covers
+    (36 / 4 = 9 query heads per KV head falls back to the head-major kernel)."""
+    if legacy:
+        monkeypatch.setenv("SQ_DECODE_LEGACY", "1")
+    lens = [1, 15, 16, 17, 300, 2048, 777]
+    torch.manual_seed(hq * 7 + group)
+    ps = 16
+    fk, fv = ops.KV_FORMATS[kvfmt]
+    max_pages = max((l + ps - 1) // ps for l in lens)
+    num_pages = sum((l + ps - 1) // ps for l in lens) + 3
+    kc, ks, vc, vs, kd, vd = _fill_random_cache(num_pages, hkv, ps, d, fk, fv, group, cuda, seed=group + d)
+    perm = torch.randperm(num_pages)
+    bt = torch.zeros(len(lens), max_pages, dtype=torch.int32)
+    o = 0
+    for i, l in enumerate(lens):
+        n = (l + ps - 1) // ps
+        bt[i, :n] = perm[o:o + n].to(torch.int32)
+        o += n
+    q = torch.randn(len(lens), hq * d).to(torch.bfloat16)
+    out = torch.full((len(lens), hq * d), float("nan"), dtype=torch.bfloat16, device=cuda)
+    seq = torch.tensor(lens, dtype=torch.int32)
+    for splits in (None, (1, max_pages)):
+        ops.paged_decode_attention(q.to(cuda), kc, ks, vc, vs, bt.to(cuda), seq.to(cuda), out, hq, hkv, d, ps,
+                                   group, fk, fv, sm_scale(d), max_ctx=max(lens), splits=splits)
+        torch.cuda.synchronize()
+        for i, l in enumerate(lens):
+            k = _gather(kd, bt[i], l, ps).to(torch.bfloat16).float()
+            v = _gather(vd, bt[i], l, ps).to(torch.bfloat16).float()
+            ref = attention(q[i].float().view(1, hq, d), k, v, torch.tensor([l - 1]), sm_scale(d))
+            torch.testing.assert_close(out[i].float().cpu().view(1, hq, d), ref, rtol=2e-2, atol=3e-2)
+
+
 SHORT_SEQS = [(40, 40), (70, 200), (1, 1), (130, 130), (16, 48)]
 LONG_SEQS = [(300, 1100), (600, 600), (5, 900), (257, 257)]  # several 128-key tiles, partial last tiles
 
