@@ -11,6 +11,8 @@
     squish doctor            GPU, extension and interconnect checks
     squish config ...        get / set / show / reset / path of ~/.squish/config.json
     squish daemon ...        start / stop / status / ping / reload the UDS daemon
+    squish chat | info | search | rm | ps | logs | trace | quality | route | export | eval | push
+                             (cli_verbs.py)
     squish version
 
 MODEL is a checkpoint path or a preset name (random-init weights of that architecture).
@@ -127,10 +129,11 @@ def _model(a) -> str:
     return a.model or ucfg.get("model.default")
 
 
-def _logging(a) -> None:
+def _logging(a, log_file=None) -> None:
     from .utils.logconfig import configure_logging
 
-    configure_logging(getattr(a, "log_level", "warning"), json_format=getattr(a, "log_format", "text") == "json")
+    configure_logging(getattr(a, "log_level", "warning"), json_format=getattr(a, "log_format", "text") == "json",
+                      log_file=log_file)
 
 
 def _relaunch_ranks(tp: int) -> int:
@@ -209,7 +212,9 @@ def cmd_serve(a) -> int:
 
     from .serving.server import ServerState, create_app
 
-    _logging(a)
+    from .cli_verbs import log_path
+
+    _logging(a, log_file=log_path() if os.environ.get("RANK", "0") == "0" else None)
     tp, _ = _parallel(a)
     if tp > 1 and "RANK" not in os.environ:
         return _relaunch_ranks(tp)
@@ -525,6 +530,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--model", default=None)
     p.set_defaults(fn=cmd_daemon)
     sub.add_parser("version").set_defaults(fn=lambda a: print(f"squish-b200 {__version__}") or 0)
+    from .cli_verbs import add_parsers
+
+    add_parsers(sub)
     return ap
 
 

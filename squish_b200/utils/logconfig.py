@@ -33,17 +33,27 @@ class JsonLineFormatter(logging.Formatter):
         return json.dumps(out, default=str)
 
 
-def configure_logging(level: str = "warning", json_format: bool = False, stream=None) -> logging.Logger:
-    """(Re)configure the package's loggers; calling it again replaces the handler, so
-    repeated calls never duplicate lines. Unknown level names mean WARNING."""
+def configure_logging(level: str = "warning", json_format: bool = False, stream=None,
+                      log_file=None) -> logging.Logger:
+    """(Re)configure the package's loggers; calling it again replaces the handlers, so
+    repeated calls never duplicate lines. Unknown level names mean WARNING. ``log_file``
+    adds a second handler appending to that file (its directory is created)."""
     root = logging.getLogger(ROOT)
     root.setLevel(getattr(logging, str(level).upper(), logging.WARNING))
     for h in list(root.handlers):
         root.removeHandler(h)
-    h = logging.StreamHandler(stream or sys.stderr)
-    h.setFormatter(JsonLineFormatter() if json_format else
-                   logging.Formatter("%(asctime)s %(levelname)-8s %(name)s %(message)s"))
-    root.addHandler(h)
+        h.close()
+    fmt = (JsonLineFormatter() if json_format else
+           logging.Formatter("%(asctime)s %(levelname)-8s %(name)s %(message)s"))
+    handlers = [logging.StreamHandler(stream or sys.stderr)]
+    if log_file is not None:
+        import os
+
+        os.makedirs(os.path.dirname(os.path.abspath(str(log_file))), exist_ok=True)
+        handlers.append(logging.FileHandler(str(log_file), mode="a"))
+    for h in handlers:
+        h.setFormatter(fmt)
+        root.addHandler(h)
     root.propagate = False
     return root
 
