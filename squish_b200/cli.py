@@ -267,7 +267,8 @@ def cmd_compress(a) -> int:
                   delete_source=a.delete_source, random_preset=a.random_init, seed=a.seed, kv_dtype=a.kv_dtype,
                   hqq=getattr(a, "hqq", False), awq=getattr(a, "awq", False),
                   awq_scales=getattr(a, "awq_scales", None), awq_alpha=getattr(a, "awq_alpha", 0.5),
-                  awq_samples=getattr(a, "awq_samples", 16), gptq=getattr(a, "gptq", False))
+                  awq_samples=getattr(a, "awq_samples", 16), gptq=getattr(a, "gptq", False),
+                  df11=getattr(a, "df11", False))
     print(json.dumps({"output": out, **st}))
     return 0
 
@@ -483,6 +484,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--awq-alpha", type=float, default=0.5)
     p.add_argument("--awq-samples", type=int, default=16)
     p.add_argument("--gptq", action="store_true", help="GPTQ INT4 (calibrates on the fp32 model)")
+    p.add_argument("--df11", action="store_true",
+                   help="store unquantized tensors losslessly as bf16 with entropy-coded exponents (__pt_df11)")
     p.set_defaults(fn=cmd_compress)
 
     p = sub.add_parser("merge-model", help="merge LoRA adapters (DARE / TIES / DARE-TIES)")

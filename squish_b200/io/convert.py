@@ -35,9 +35,9 @@ def should_quantize(name: str, shape: tuple, patterns=PASSTHROUGH_PATTERNS) -> b
     return True
 
 
-def _write_tensor(td: Path, name: str, t: QTensor) -> int:
+def _write_tensor(td: Path, name: str, t: QTensor, df11: bool = False) -> int:
     n = 0
-    for key, a in tensor_files(name, t).items():
+    for key, a in tensor_files(name, t, df11=df11).items():
         p = td / f"{key}.npy"
         np.save(str(p), a)
         n += p.stat().st_size
@@ -76,12 +76,13 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
              device: str | None = None, delete_source: bool = False, random_preset: str | None = None,
              seed: int = 0, kv_dtype: str = "int4", log=print, hqq: bool = False, awq: bool = False,
              awq_scales: str | None = None, awq_alpha: float = 0.5, awq_samples: int = 16,
-             awq_seq_len: int = 256, super_weights: bool = True, gptq: bool = False) -> dict:
+             awq_seq_len: int = 256, super_weights: bool = True, gptq: bool = False, df11: bool = False) -> dict:
     """``hqq``: half-quadratic refinement of INT4 / INT2 grids. ``awq`` (or ``awq_scales``, a
     directory of saved scales): activation-aware scaling of norm-fed projections before
     quantization; calibration needs the whole fp32 model in memory once. ``super_weights``
     (with ``mse_clip``): rows holding a super weight skip the clip search; the coordinates found
-    are written to ``super_weights.json``."""
+    are written to ``super_weights.json``. ``df11``: passthrough (unquantized) tensors are
+    stored losslessly as DFloat11-style ``__pt_df11`` (bf16 with entropy-coded exponents)."""
     from ..quant.super_weights import SuperWeightCalibrator, protect, save_coords
 
     if gptq and (awq or awq_scales or kind != "q4a" or hqq):
@@ -160,7 +161,7 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
                     t = gptq_or(name, t.dequantize(), None)
                 elif t.kind != "dense" and (tkind != "q4a" or hqq):
                     t = quantize(t.dequantize(), tkind, group_size, mse_clip, hqq=hqq)
-                stats["bytes"] += _write_tensor(td, name, t)
+                stats["bytes"] += _write_tensor(td, name, t, df11)
                 stats["n_quantized" if t.kind != "dense" else "n_passthrough"] += 1
                 manifest[name] = safe_key(name)
             done.append("random-init")
@@ -234,7 +235,7 @@ def compress(model_dir: str | None, out_dir: str, kind: str = "q4a", group_size:
                     else:
                         t = QTensor("dense", tuple(w.shape), data=w.float().cpu())
                         stats["n_passthrough"] += 1
-                    stats["bytes"] += _write_tensor(td, name, t)
+                    stats["bytes"] += _write_tensor(td, name, t, df11)
                     manifest[name] = safe_key(name)
                     del w
             man_path.write_text(json.dumps(manifest, indent=2))

@@ -17,6 +17,9 @@ Suffix sets, in the reference loader's dispatch priority (squish/io/loader_utils
     __q + __s                           INT8 symmetric (per row or per group)
     __f8 + __sf8                        FP8 E4M3 codes + per-group scales (this package's extension)
     __sqint2_idx/_scales/_zp/_meta(+_L/_R) SQINT2 (Hadamard-rotated NF2 INT2, quant/sqint2.py)
+    __pt_df11                           lossless bf16 passthrough, DFloat11-style (io/entropy.py df11_*)
+    __vq_idx + __vq_cb (+ __vq_res, __vq_rescb, __vq_cols) + __vq_meta
+                                        VPTQ vector quantization (squish/convert.py:362-420 layout)
     __pt                                float16 passthrough
 plus __shape (the original shape) for every tensor. ``.npy.sqe`` files (rANS / Huffman coded,
 io/entropy.py) are always readable; ``.npy.zst`` files when ``zstandard`` is importable.
@@ -36,7 +39,7 @@ import torch
 
 from ..models.weights import Checkpoint, QTensor
 
-SUFFIXES = ("__nf4", "__s_nf4", "__q4a", "__s4a", "__z4a", "__q4", "__s4", "__q3", "__s3", "__z3", "__lra",
+SUFFIXES = ("__pt_df11", "__vq_idx", "__vq_cb", "__vq_res", "__vq_rescb", "__vq_cols", "__vq_meta", "__nf4", "__s_nf4", "__q4a", "__s4a", "__z4a", "__q4", "__s4", "__q3", "__s3", "__z3", "__lra",
             "__lrb", "__q2", "__s2", "__z2", "__aqlm_idx", "__aqlm_cb", "__f8", "__sf8", "__q", "__s", "__pt", "__shape")
 
 
@@ -84,10 +87,19 @@ def read_tensor(td: Path, key: str) -> QTensor:
         a = np.asarray(_load(td / f"{key}{suf}.npy"))
         return torch.from_numpy(np.array(a, dtype=dt or a.dtype, order="C", copy=True))
 
+    if _exists(td, key, "__pt_df11"):  # (the reference checks this suffix first)
+        from .entropy import df11_decode
+
+        d = torch.from_numpy(df11_decode(np.asarray(_load(td / f"{key}__pt_df11.npy")).tobytes()).copy())
+        return QTensor("dense", shape or tuple(d.shape), data=d.reshape(shape) if shape else d)
     if _exists(td, key, "__nf4") and _exists(td, key, "__s_nf4"):
         p, s = arr("__nf4", np.uint8), arr("__s_nf4", np.float32)
         return QTensor("nf4", shape or (p.shape[0], p.shape[1] * 2), packed=p, scales=s,
                        group=(p.shape[1] * 2) // s.shape[1])
+    if _exists(td, key, "__vq_idx"):
+        d = torch.from_numpy(read_vptq(lambda suf: np.asarray(_load(td / f"{key}{suf}.npy")),
+                                       lambda suf: _exists(td, key, suf)))
+        return QTensor("dense", shape or tuple(d.shape), data=d.reshape(shape) if shape else d)
     if _exists(td, key, "__q4a"):
         p, s, z = arr("__q4a", np.uint8), arr("__s4a", np.float32), arr("__z4a", np.float32)
         return QTensor("q4a", shape or (p.shape[0], p.shape[1] * 2), packed=p, scales=s, offsets=z,
@@ -135,6 +147,42 @@ def read_tensor(td: Path, key: str) -> QTensor:
     raise FileNotFoundError(f"no npy-dir files for tensor key {key!r} in {td}")
 
 
+def read_vptq(load, exists) -> np.ndarray:
+    """Dense fp32 weight of a VPTQ tensor in the reference's file layout (squish/convert.py
+    :362-420): ``__vq_meta`` = [rows, cols, group, primary entries, residual entries];
+    ``__vq_cb`` / ``__vq_rescb`` = codebook vectors (entries x group, flattened) followed by
+    three trailing scalars (entries, group, fit iterations); ``__vq_idx`` / ``__vq_res`` =
+    one codebook index per (row, group of ``group`` consecutive columns), row-major (a
+    one-element ``__vq_res`` means no residual stage); ``__vq_cols`` = per-column scales
+    (empty when absent). W[r, g*group:(g+1)*group] = cb[idx] (+ rescb[res]), times the
+    column scales. The reference's own VPTQ module is not in its release, so the decoding
+    follows this serialized layout."""
+    meta = load("__vq_meta").astype(np.int64).reshape(-1)
+    rows, cols, gs, n_cb, n_res = (int(v) for v in meta[:5])
+    if gs <= 0 or cols % gs:
+        raise ValueError(f"VPTQ group {gs} does not divide {cols} columns")
+    ng = cols // gs
+    cb = load("__vq_cb").astype(np.float32).reshape(-1)[:-3].reshape(-1, gs)
+    idx = load("__vq_idx").astype(np.int64).reshape(rows, ng)
+    if idx.min(initial=0) < 0 or idx.max(initial=0) >= cb.shape[0]:
+        raise ValueError("VPTQ index outside its codebook")
+    w = cb[idx]  # rows, ng, gs
+    if n_res > 0 and exists("__vq_res"):
+        res = load("__vq_res").astype(np.int64).reshape(-1)
+        if res.size == rows * ng:
+            rcb = load("__vq_rescb").astype(np.float32).reshape(-1)[:-3].reshape(-1, gs)
+            res = res.reshape(rows, ng)
+            if res.min(initial=0) < 0 or res.max(initial=0) >= rcb.shape[0]:
+                raise ValueError("VPTQ residual index outside its codebook")
+            w = w + rcb[res]
+    w = w.reshape(rows, cols)
+    if exists("__vq_cols"):
+        cs = load("__vq_cols").astype(np.float32).reshape(-1)
+        if cs.size == cols:
+            w = w * cs[None, :]
+    return np.ascontiguousarray(w, dtype=np.float32)
+
+
 def read_npy_dir(path: str | Path, config, quant) -> Checkpoint:
     root = Path(path)
     td = tensor_dir(root)
@@ -149,8 +197,9 @@ def read_npy_dir(path: str | Path, config, quant) -> Checkpoint:
     return ck
 
 
-def tensor_files(name: str, t: QTensor) -> dict[str, np.ndarray]:
-    """The npy-dir files of one tensor (suffix -> array)."""
+def tensor_files(name: str, t: QTensor, df11: bool = False) -> dict[str, np.ndarray]:
+    """The npy-dir files of one tensor (suffix -> array); ``df11`` stores dense tensors as
+    lossless bf16 ``__pt_df11`` instead of float16 ``__pt``."""
     k = safe_key(name)
     out = {f"{k}__shape": np.asarray(t.shape, dtype=np.int64)}
 
@@ -182,6 +231,10 @@ def tensor_files(name: str, t: QTensor) -> dict[str, np.ndarray]:
             out[f"{k}__{kk}"] = np_(v, np.float32)
     elif t.kind == "aqlm":
         out.update({f"{k}__aqlm_idx": np_(t.packed, np.uint16), f"{k}__aqlm_cb": np_(t.scales, np.float32)})
+    elif t.kind == "dense" and df11:
+        from .entropy import df11_encode
+
+        out[f"{k}__pt_df11"] = np.frombuffer(df11_encode(t.data), dtype=np.uint8).copy()
     elif t.kind == "dense":
         out[f"{k}__pt"] = np_(t.data.float(), np.float16)
     else:

@@ -264,3 +264,66 @@ def test_aqlm_codec_round_trip():
     t1 = aqlm_quantize(w, n_codebooks=1, codebook_size=16, group_size=8)
     t3 = aqlm_quantize(w, n_codebooks=3, codebook_size=16, group_size=8)
     assert (t3.dequantize() - w).norm() < (t1.dequantize() - w).norm()
+
+
+def test_df11_lossless_roundtrip_and_npy_dir(tmp_path):
+    """DFloat11-style passthrough: bf16 values come back bit for bit, ~11 bits per value for
+    normal-distributed weights; pickled blobs (the reference's writer) are refused."""
+    import pickle
+
+    import numpy as np
+    import torch
+
+    from squish_b200.io.entropy import df11_decode, df11_encode
+    from squish_b200.io.npy_dir import read_tensor
+
+    x = (torch.randn(64, 300) * 0.02).to(torch.bfloat16)
+    blob = df11_encode(x)
+    back = df11_decode(blob)
+    assert torch.equal(torch.from_numpy(back).reshape(64, 300), x.float())
+    assert len(blob) * 8 / x.numel() < 12.5
+    td = tmp_path / "tensors"
+    td.mkdir()
+    np.save(td / "w__pt_df11.npy", np.frombuffer(blob, dtype=np.uint8))
+    np.save(td / "w__shape.npy", np.array([64, 300], dtype=np.int64))
+    t = read_tensor(td, "w")
+    assert t.kind == "dense" and t.shape == (64, 300) and torch.equal(t.data.float(), x.float())
+    np.save(td / "p__pt_df11.npy", np.frombuffer(pickle.dumps([1, 2], protocol=4), dtype=np.uint8))
+    import pytest
+
+    with pytest.raises(ValueError, match="pickle"):
+        read_tensor(td, "p")
+
+
+def test_vptq_files_decode(tmp_path):
+    """The reference's VPTQ file set (squish/convert.py:362-420): codebooks with three trailing
+    scalars, per-(row, group) indices, an optional residual stage and column scales."""
+    import numpy as np
+    import torch
+
+    from squish_b200.io.npy_dir import read_tensor
+
+    rng = np.random.default_rng(0)
+    rows, cols, gs, ncb, nres = 6, 16, 4, 8, 4
+    cb = rng.standard_normal((ncb, gs)).astype(np.float32)
+    rcb = rng.standard_normal((nres, gs)).astype(np.float32) * 0.1
+    idx = rng.integers(0, ncb, (rows, cols // gs))
+    res = rng.integers(0, nres, (rows, cols // gs))
+    cs = rng.uniform(0.5, 2.0, cols).astype(np.float32)
+    td = tmp_path / "tensors"
+    td.mkdir()
+    np.save(td / "w__vq_idx.npy", idx.astype(np.int64))
+    np.save(td / "w__vq_cb.npy", np.concatenate([cb.reshape(-1), [ncb, gs, 10]]).astype(np.float32))
+    np.save(td / "w__vq_res.npy", res.astype(np.int64))
+    np.save(td / "w__vq_rescb.npy", np.concatenate([rcb.reshape(-1), [nres, gs, 10]]).astype(np.float32))
+    np.save(td / "w__vq_cols.npy", cs)
+    np.save(td / "w__vq_meta.npy", np.array([rows, cols, gs, ncb, nres], dtype=np.int64))
+    np.save(td / "w__shape.npy", np.array([rows, cols], dtype=np.int64))
+    want = (cb[idx] + rcb[res]).reshape(rows, cols) * cs[None, :]
+    t = read_tensor(td, "w")
+    assert t.kind == "dense" and torch.allclose(t.data.float(), torch.from_numpy(want))
+    # no residual stage: a one-element __vq_res
+    np.save(td / "w__vq_res.npy", np.zeros(1, dtype=np.int64))
+    np.save(td / "w__vq_cols.npy", np.array([], dtype=np.float32))
+    t = read_tensor(td, "w")
+    assert torch.allclose(t.data.float(), torch.from_numpy(cb[idx].reshape(rows, cols)))
