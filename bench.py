@@ -606,6 +606,12 @@ def run_reference(args, world, rank, local):
 
 def main():
     args = parse()
+    if args.impl == "reference":
+        # The stock path allocates the fp32 copy of every position's logits (tens of GB) right
+        # after a forward whose activations were just freed; without expandable segments the
+        # caching allocator cannot place it in the freed (fragmented) space. Allocator setting
+        # only: the reference's code runs unchanged.
+        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":

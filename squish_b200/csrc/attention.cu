@@ -414,6 +414,27 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// N consecutive fp16 values (a row's scales) in one vector load, as 32-bit words (two halves
+// each, low half first); zeros when !ok
+template <int N>
+__device__ __forceinline__ void load_halves(const __half* src, bool ok, uint32_t (&w)[(N + 1) / 2]) {
+  static_assert(N == 1 || N == 2 || N == 4 || N == 8, "scale row of 1, 2, 4 or 8 halves");
+  if constexpr (N == 8) {
+    const uint4 v = ok ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0u, 0u, 0u, 0u);
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (N == 4) {
+    const uint2 v = ok ? __ldg(reinterpret_cast<const uint2*>(src)) : make_uint2(0u, 0u);
+    w[0] = v.x; w[1] = v.y;
+  } else if constexpr (N == 2) {
+    w[0] = ok ? __ldg(reinterpret_cast<const unsigned int*>(src)) : 0u;
+  } else {
+    w[0] = ok ? (uint32_t)__half_as_ushort(__ldg(src)) : 0u;
+  }
+}
+__device__ __forceinline__ float half_at(const uint32_t* w, int i) {
+  return __half2float(__ushort_as_half((unsigned short)((w[i >> 1] >> ((i & 1) * 16)) & 0xFFFFu)));
+}
+
 // dims of the 8 positions of a value-tile chunk (the byte permute's order)
 __device__ __forceinline__ int vperm(int col) { return (col & ~7) | ((col & 3) << 1) | ((col >> 2) & 1); }
 
@@ -503,7 +524,7 @@ __global__ void __launch_bounds__(128, 4) decode_tm_kernel(const AttnParams p) {
   uint32_t kw[2][KW];
   float ks[2][NG], kz[2][NG];
   uint32_t vw[D / 16];
-  float vs_[NG > 1 ? NG / 2 : 1], vz_[NG > 1 ? NG / 2 : 1];
+  uint32_t vs2[NG > 1 ? NG / 2 : 1], vz2[NG > 1 ? NG / 2 : 1];  // bf16 pairs of scale / zero
   const int vr = lane >> 1, vhalf = lane & 1;
   constexpr int NGH = NG > 1 ? NG / 2 : 1;  // value scale groups in half a row
   auto fetch = [&](int tile) {
@@ -518,20 +539,12 @@ __global__ void __launch_bounds__(128, 4) decode_tm_kernel(const AttnParams p) {
       const uint32_t* kc = reinterpret_cast<const uint32_t*>(p.k_codes + row * CBK);
 #pragma unroll
       for (int i = 0; i < KW; ++i) kw[j][i] = ok ? __ldg(kc + t4 + 4 * i) : 0u;
-      const __half* sc = p.k_scales + row * NSK;
+      uint32_t sc[(NSK + 1) / 2];
+      load_halves<NSK>(p.k_scales + row * NSK, ok, sc);
 #pragma unroll
       for (int gg = 0; gg < NG; ++gg) {
-        float s_ = 0.f, z_ = 0.f;
-        if (ok) {
-          if constexpr (kv_asym(FK)) {
-            const __half2 sz = __ldg(reinterpret_cast<const __half2*>(sc) + gg);
-            s_ = __low2float(sz);
-            z_ = __high2float(sz);
-          } else {
-            s_ = __half2float(__ldg(sc + gg));
-            z_ = -7.5f * s_;
-          }
-        }
+        const float s_ = half_at(sc, kv_asym(FK) ? 2 * gg : gg);
+        const float z_ = kv_asym(FK) ? half_at(sc, 2 * gg + 1) : -7.5f * s_;
         // s * (q . (M0 + c)) + (z - M0 * s) * sum(q)
         ks[j][gg] = s_;
         kz[j][gg] = z_ - (K8 ? 1024.f : 128.f) * s_;
@@ -550,23 +563,15 @@ __global__ void __launch_bounds__(128, 4) decode_tm_kernel(const AttnParams p) {
         vw[4 * i + 2] = u.z;
         vw[4 * i + 3] = u.w;
       }
-      const __half* sc = p.v_scales + row * NSV;
+      uint32_t sc[(NSV + 1) / 2];
+      load_halves<NSV>(p.v_scales + row * NSV, ok, sc);
 #pragma unroll
       for (int q = 0; q < NGH; ++q) {
         const int gg = NG > 1 ? vhalf * NGH + q : 0;
-        float s_ = 0.f, z_ = 0.f;
-        if (ok) {
-          if constexpr (kv_asym(FV)) {
-            const __half2 sz = __ldg(reinterpret_cast<const __half2*>(sc) + gg);
-            s_ = __low2float(sz);
-            z_ = __high2float(sz);
-          } else {
-            s_ = __half2float(__ldg(sc + gg));
-            z_ = -7.5f * s_;
-          }
-        }
-        vs_[q] = s_;
-        vz_[q] = z_;
+        const float s_ = half_at(sc, kv_asym(FV) ? 2 * gg : gg);
+        const float z_ = kv_asym(FV) ? half_at(sc, 2 * gg + 1) : -7.5f * s_;
+        vs2[q] = pack_bf2(s_, s_);
+        vz2[q] = pack_bf2(z_, z_);
       }
     }
   };
@@ -580,8 +585,8 @@ __global__ void __launch_bounds__(128, 4) decode_tm_kernel(const AttnParams p) {
 #pragma unroll
       for (int c = 0; c < D / 16; ++c) {  // 8-dim chunks of this lane's half row
         const int q = NG > 1 ? (c * 8) / G : 0;
-        const __nv_bfloat162 s2 = __floats2bfloat162_rn(vs_[q], vs_[q]);
-        const __nv_bfloat162 z2 = __floats2bfloat162_rn(vz_[q], vz_[q]);
+        const __nv_bfloat162 s2 = *reinterpret_cast<const __nv_bfloat162*>(&vs2[q]);
+        const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&vz2[q]);
         const uint32_t L = vw[c] & 0x0F0F0F0Fu, H = (vw[c] >> 4) & 0x0F0F0F0Fu;
         uint32_t t[4] = {prmt(L, kMagicB, 0x4140u), prmt(L, kMagicB, 0x4342u), prmt(H, kMagicB, 0x4140u),
                          prmt(H, kMagicB, 0x4342u)};

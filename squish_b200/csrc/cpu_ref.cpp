@@ -412,7 +412,12 @@ torch::Tensor dequantize_int2(torch::Tensor packed, torch::Tensor scales, torch:
 
 // ---------------------------------------------------------------- KV page codecs (oracle for kv_write.cu)
 // x: [rows, D] -> codes [rows, D*bits/8] u8, scales [rows, nscale] f32 (fp16-rounded like the kernel)
-std::vector<torch::Tensor> kv_quantize(torch::Tensor x, int64_t fmt, int64_t group) {
+// fp16_scales (the paged device pools' layout): scales are rounded to fp16 before the codes
+// are chosen, so every code is the nearest under the scale that is stored. fp16_scales false:
+// float32 scales with the reference numpy codecs' arithmetic (squish/kv/kv_cache.py:78-375,
+// squish/kv/k8v4_codec.py:64-137), code for code: INT8 q = round(x / absmax * 127), stored
+// scale absmax / 127; INT4 / INT2 round(x / (absmax / L) + L); k8v4 round((x - lo) / scale).
+std::vector<torch::Tensor> kv_quantize(torch::Tensor x, int64_t fmt, int64_t group, bool fp16_scales = true) {
   check_cpu_f32_2d(x, "x");
   TORCH_CHECK(fmt >= 1 && fmt <= 5, "kv format must be int8 / int4 / int2 / k8 / v4 (1..5)");
   TORCH_CHECK(group > 0 && x.size(1) % group == 0, "group must divide the row length");
@@ -426,7 +431,7 @@ std::vector<torch::Tensor> kv_quantize(torch::Tensor x, int64_t fmt, int64_t gro
   uint8_t* cp = codes.data_ptr<uint8_t>();
   float* sp = scales.data_ptr<float>();
   const int64_t CB = D * bits / 8, NS = NG * (asym ? 2 : 1);
-  auto h16 = [](float v) { return c10::Half(v).operator float(); };
+  auto h16 = [fp16_scales](float v) { return fp16_scales ? c10::Half(v).operator float() : v; };
   prange(R, [&](int64_t r) {
     for (int64_t g = 0; g < NG; ++g) {
       const float* v = xp + r * D + g * group;
@@ -449,9 +454,11 @@ std::vector<torch::Tensor> kv_quantize(torch::Tensor x, int64_t fmt, int64_t gro
         if (s == 0.f) s = 6e-8f;
         sp[r * NS + g] = s;
       }
+      const float am_safe = std::max(am, 1e-8f);
       for (int64_t i = 0; i < group; ++i) {
         float t;
         if (asym) t = std::nearbyint((v[i] - z) / s);
+        else if (fmt == 1 && !fp16_scales) t = std::nearbyint(v[i] / am_safe * 127.f);
         else if (fmt == 1) t = std::nearbyint(v[i] / s);
         else t = std::nearbyint(v[i] / s + qmax);
         int q;
@@ -692,7 +699,8 @@ void register_cpu(pybind11::module& m) {
   c.def("unpack_int3", &unpack_int3);
   c.def("quantize_int2", &quantize_int2);
   c.def("dequantize_int2", &dequantize_int2);
-  c.def("kv_quantize", &kv_quantize);
+  c.def("kv_quantize", &kv_quantize, pybind11::arg("x"), pybind11::arg("fmt"), pybind11::arg("group"),
+        pybind11::arg("fp16_scales") = true);
   c.def("kv_dequantize", &kv_dequantize);
   c.def("quantize_fp8", &quantize_fp8, pybind11::arg("x"), pybind11::arg("fmt"), pybind11::arg("group"),
         pybind11::arg("fixed_scale") = 0.0);

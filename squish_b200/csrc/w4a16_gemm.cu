@@ -62,6 +62,8 @@ struct Cfg {
   static constexpr int kA0 = AT ? (NT * BN < 32 ? 32 : NT * BN) : 0;
   static constexpr int kCols = AT ? kA0 + 32 * kMaxRingA : NT * BN;
   static constexpr int kTmemCols = (kCols <= 32) ? 32 : (kCols <= 64) ? 64 : (kCols <= 128) ? 128 : (kCols <= 256) ? 256 : 512;
+  // pipelined dequant (two register copies of a stage) when the register budget has room
+  static constexpr bool kPipe = AT && (2 * kWpt * 4 + 48 <= 65536 / (kThreads * kMinBlocks));
 };
 
 __host__ __device__ constexpr int code_bytes(int wfmt) {
@@ -458,11 +460,11 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     const int sw_row = r & 7;
     const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + sw_row * 128);
     Ring rw(ring_w), ra(ring_a);
-    for (int i = 0; i < nkb; ++i) {
-      if (!mbar_wait(&w_full[rw.s], rw.ph, status, SQ_ERR_TIMEOUT_W)) break;
+    // Dequantize the next raw weight stage into o (waits for it, releases it); false on timeout.
+    auto dq_stage = [&](int i, uint4 (&o)[NT][WPT]) -> bool {
+      if (!mbar_wait(&w_full[rw.s], rw.ph, status, SQ_ERR_TIMEOUT_W)) return false;
       if (d == 0) trace_mark(str, 4, i);
       const uint8_t* wst = w_ring + rw.s * L.w_stage;
-      uint4 o[NT][WPT];
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         const uint8_t* tb = wst + t * tbytes;
@@ -509,49 +511,85 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&w_empty[rw.s]);  // raw tile consumed (one arrive per warp)
-      if (!mbar_wait(&a_empty[ra.s], ra.ph ^ 1u, status, SQ_ERR_TIMEOUT_A)) break;
-      if (d == 0) trace_mark(str, 5, i);
-      if constexpr (C::AT) {
-        // this thread's 8*WPT K values of row r = 4*WPT columns of its lane in the A stage
-        tc_fence_after();
-        const uint32_t col = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(C::kA0 + ra.s * 32 + c * WPT * 4);
-        if constexpr (WPT == 8) {
-          uint32_t regs[32];
+      rw.next();
+      return true;
+    };
+    // this thread's 8*WPT K values of row r = 4*WPT columns of its lane in the TMEM A stage
+    auto st_tmem = [&](const uint4 (&o)[NT][WPT]) {
+      const uint32_t col = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(C::kA0 + ra.s * 32 + c * WPT * 4);
+      if constexpr (WPT == 8) {
+        uint32_t regs[32];
 #pragma unroll
-          for (int w = 0; w < 8; ++w) {
-            regs[4 * w] = o[0][w].x;
-            regs[4 * w + 1] = o[0][w].y;
-            regs[4 * w + 2] = o[0][w].z;
-            regs[4 * w + 3] = o[0][w].w;
-          }
-          tmem_st32(col, regs);
-        } else if constexpr (WPT == 4) {
-          const uint32_t regs[16] = {o[0][0].x, o[0][0].y, o[0][0].z, o[0][0].w, o[0][1].x, o[0][1].y,
-                                     o[0][1].z, o[0][1].w, o[0][2].x, o[0][2].y, o[0][2].z, o[0][2].w,
-                                     o[0][3].x, o[0][3].y, o[0][3].z, o[0][3].w};
-          tmem_st16(col, regs);
-        } else {
-          const uint32_t regs[8] = {o[0][0].x, o[0][0].y, o[0][0].z, o[0][0].w,
-                                    o[0][1].x, o[0][1].y, o[0][1].z, o[0][1].w};
-          tmem_st8(col, regs);
+        for (int w = 0; w < 8; ++w) {
+          regs[4 * w] = o[0][w].x;
+          regs[4 * w + 1] = o[0][w].y;
+          regs[4 * w + 2] = o[0][w].z;
+          regs[4 * w + 3] = o[0][w].w;
         }
+        tmem_st32(col, regs);
+      } else if constexpr (WPT == 4) {
+        const uint32_t regs[16] = {o[0][0].x, o[0][0].y, o[0][0].z, o[0][0].w, o[0][1].x, o[0][1].y,
+                                   o[0][1].z, o[0][1].w, o[0][2].x, o[0][2].y, o[0][2].z, o[0][2].w,
+                                   o[0][3].x, o[0][3].y, o[0][3].z, o[0][3].w};
+        tmem_st16(col, regs);
+      } else {
+        const uint32_t regs[8] = {o[0][0].x, o[0][0].y, o[0][0].z, o[0][0].w,
+                                  o[0][1].x, o[0][1].y, o[0][1].z, o[0][1].w};
+        tmem_st8(col, regs);
+      }
+    };
+    if constexpr (C::AT && C::kPipe) {
+      // Software-pipelined: the tensor-memory store of stage i is in flight while stage i + 1
+      // is dequantized, so a warp's per-stage chain is max(store round trip, dequant) rather
+      // than their sum (two register copies of a stage's operand).
+      uint4 cur[NT][WPT], nxt[NT][WPT];
+      bool ok = nkb > 0 && dq_stage(0, cur);
+      for (int i = 0; ok && i < nkb; ++i) {
+        if (!mbar_wait(&a_empty[ra.s], ra.ph ^ 1u, status, SQ_ERR_TIMEOUT_A)) break;
+        if (d == 0) trace_mark(str, 5, i);
+        tc_fence_after();
+        st_tmem(cur);
+        const bool more = i + 1 < nkb;
+        if (more) ok = dq_stage(i + 1, nxt);
         tmem_wait_st();
         tc_fence_before();
-      } else {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[ra.s]);
+        if (d == 0) trace_mark(str, 6, i);
+        ra.next();
+        if (more) {
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          uint8_t* adst = a_ring + (ra.s * NT + t) * A_TILE_BYTES + row_off;
+          for (int t = 0; t < NT; ++t)
 #pragma unroll
-          for (int w = 0; w < WPT; ++w)
-            *reinterpret_cast<uint4*>(adst + (((c * WPT + w) ^ sw_row) << 4)) = o[t][w];
+            for (int w = 0; w < WPT; ++w) cur[t][w] = nxt[t][w];
         }
-        fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core (async proxy)
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&a_full[ra.s]);
-      if (d == 0) trace_mark(str, 6, i);
-      rw.next();
-      ra.next();
+    } else {
+      for (int i = 0; i < nkb; ++i) {
+        uint4 o[NT][WPT];
+        if (!dq_stage(i, o)) break;
+        if (!mbar_wait(&a_empty[ra.s], ra.ph ^ 1u, status, SQ_ERR_TIMEOUT_A)) break;
+        if (d == 0) trace_mark(str, 5, i);
+        if constexpr (C::AT) {
+          tc_fence_after();
+          st_tmem(o);
+          tmem_wait_st();
+          tc_fence_before();
+        } else {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            uint8_t* adst = a_ring + (ra.s * NT + t) * A_TILE_BYTES + row_off;
+#pragma unroll
+            for (int w = 0; w < WPT; ++w)
+              *reinterpret_cast<uint4*>(adst + (((c * WPT + w) ^ sw_row) << 4)) = o[t][w];
+          }
+          fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core (async proxy)
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[ra.s]);
+        if (d == 0) trace_mark(str, 6, i);
+        ra.next();
+      }
     }
   }
 

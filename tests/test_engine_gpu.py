@@ -59,7 +59,7 @@ def test_cuda_engine_matches_cpu_oracle(cuda, idx):
     eng.step()
     gpu_logits = eng.runner.logits[0].float().cpu()
     cos = torch.nn.functional.cosine_similarity(gpu_logits, ref_logits, dim=0)
-    assert cos > 0.99, f"cosine {cos}"
+    assert cos >= 0.999, f"cosine {cos}"
     # chunked prefill (77 tokens, 64-token budget) then greedy decode
     got = eng.generate([prompts[1]], SamplingParams(max_tokens=8, ignore_eos=True))[0]
     ok, worst = _teacher_forced_ok(ref, prompts[1], got)
