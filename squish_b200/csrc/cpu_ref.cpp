@@ -424,6 +424,7 @@ std::vector<torch::Tensor> kv_quantize(torch::Tensor x, int64_t fmt, int64_t gro
   const int64_t R = x.size(0), D = x.size(1), NG = D / group;
   const bool asym = (fmt == 4 || fmt == 5);
   const int bits = fmt == 1 || fmt == 4 ? 8 : fmt == 2 || fmt == 5 ? 4 : 2;
+  TORCH_CHECK((D * bits) % 8 == 0, "row length must fill whole bytes of codes (D * bits % 8 == 0)");
   const float qmax = fmt == 1 ? 127.f : fmt == 2 ? 7.5f : fmt == 3 ? 1.5f : fmt == 4 ? 255.f : 15.f;
   auto codes = torch::zeros({R, D * bits / 8}, torch::kUInt8);
   auto scales = torch::zeros({R, NG * (asym ? 2 : 1)}, torch::kFloat32);
@@ -485,6 +486,7 @@ torch::Tensor kv_dequantize(torch::Tensor codes, torch::Tensor scales, int64_t f
               "scales: float32 CPU");
   {
     const int bits = fmt == 1 || fmt == 4 ? 8 : fmt == 2 || fmt == 5 ? 4 : 2;
+    TORCH_CHECK(D > 0 && (D * bits) % 8 == 0, "D must fill whole bytes of codes (D * bits % 8 == 0)");
     TORCH_CHECK(codes.size(1) == D * bits / 8, "codes row length does not match D and the format");
     TORCH_CHECK(scales.size(1) >= (D / group) * ((fmt == 4 || fmt == 5) ? 2 : 1), "too few scales per row");
   }
