@@ -224,8 +224,8 @@ __global__ void __launch_bounds__(128, (FK == KV_BF16 || kv_bits(FK) == 8) ? 3 :
   const int NSK = kv_nscale(FK, D, p.group), NSV = kv_nscale(FV, D, p.group);
   auto fetch = [&](int tile, RK& a, RV& c) {
     const int tok = tile * 16 + rr;
-    if (tile < t1 && tok < kv_len) {
-      const int page = __ldg(bt + (tile * 16) / PS);
+    const int page = (tile < t1 && tok < kv_len) ? __ldg(bt + (tile * 16) / PS) : -1;
+    if (tile < t1 && tok < kv_len && kv_index_ok(page, p.num_pages, p.status)) {
       const size_t rowid = ((size_t)page * p.Hkv + h) * PS + ((tile * 16) % PS) + rr;
       a.load(p.k_codes + rowid * CBK, p.k_scales + rowid * NSK, part, p.group);
       c.load(p.v_codes + rowid * CBV, p.v_scales + rowid * NSV, part, p.group);
@@ -528,8 +528,9 @@ __global__ void __launch_bounds__(128, 4) decode_tm_kernel(const AttnParams p) {
   const int vr = lane >> 1, vhalf = lane & 1;
   constexpr int NGH = NG > 1 ? NG / 2 : 1;  // value scale groups in half a row
   auto fetch = [&](int tile) {
-    const bool live = tile < t1;
-    const int page = live ? __ldg(bt + (tile * 16) / PS) : 0;
+    int page = tile < t1 ? __ldg(bt + (tile * 16) / PS) : 0;
+    const bool live = tile < t1 && kv_index_ok(page, p.num_pages, p.status);
+    if (!live) page = 0;
     const size_t row0 = ((size_t)page * p.Hkv + h) * PS + ((tile * 16) % PS);
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
@@ -845,8 +846,8 @@ __global__ void __launch_bounds__(256) prefill_kernel(const AttnParams p) {
       if (it >= ITEMS) continue;
       const int r = it / NP, part = it % NP;
       const int tok = kt * PK + r;
-      if (tok < kv_end) {
-        const int page = __ldg(bt + tok / PS);
+      const int page = tok < kv_end ? __ldg(bt + tok / PS) : -1;
+      if (tok < kv_end && kv_index_ok(page, p.num_pages, p.status)) {
         const size_t rowid = ((size_t)page * p.Hkv + h) * PS + (tok % PS);
         rk[i].load(p.k_codes + rowid * CBK, p.k_scales + rowid * NSK, part, p.group);
         rv[i].load(p.v_codes + rowid * CBV, p.v_scales + rowid * NSV, part, p.group);

@@ -234,7 +234,10 @@ __device__ __forceinline__ void load_stages(const AttnParams& p, uint8_t* stg, u
     }
     __syncwarp();
     if (lane < np) {
-      const int page = __ldg(bt + j * ppt + lane);
+      int page = __ldg(bt + j * ppt + lane);
+      // an entry outside the pool is recorded and read as page 0 (the expected byte count of
+      // the stage barrier stays the same, so the pipeline does not stall)
+      if (!kv_index_ok(page, p.num_pages, p.status)) page = 0;
       const size_t row0 = ((size_t)page * p.Hkv + h) * PS;
       const int r0 = lane * PS;
       bulk_g2s(st + St::kKC + r0 * St::kCBK, p.k_codes + row0 * St::kCBK, (uint32_t)(PS * St::kCBK), &stg_full[slot]);

@@ -597,7 +597,7 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos
                    torch::Tensor slot_mapping, torch::Tensor k_codes, torch::Tensor k_scales, torch::Tensor v_codes,
                    torch::Tensor v_scales, int64_t Hq, int64_t Hkv, int64_t D, int64_t page_size, int64_t group,
                    int64_t fmt_k, int64_t fmt_v, c10::optional<torch::Tensor> q_norm,
-                   c10::optional<torch::Tensor> k_norm, double norm_eps) {
+                   c10::optional<torch::Tensor> k_norm, double norm_eps, c10::optional<torch::Tensor> status) {
   CHECK_CUDA(qkv);
   CHECK_DT(qkv, torch::kBFloat16);
   CHECK_DT(positions, torch::kInt32);
@@ -625,6 +625,8 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos
   p.q_norm = optr<__nv_bfloat16>(q_norm);
   p.k_norm = optr<__nv_bfloat16>(k_norm);
   p.norm_eps = (float)norm_eps;
+  p.num_pages = k_codes.dim() == 4 ? (int)k_codes.size(0) : 0;
+  p.status = optr<int>(status);
   CUDA_OK(sq::rope_kv_write_launch(p, (int)qkv.size(0), cur_stream()));
 }
 
@@ -657,6 +659,7 @@ sq::AttnParams attn_common(torch::Tensor q, torch::Tensor k_codes, torch::Tensor
   p.fmt_k = (int)fmt_k;
   p.fmt_v = (int)fmt_v;
   p.sm_scale = (float)sm_scale;
+  p.num_pages = k_codes.dim() == 4 ? (int)k_codes.size(0) : 0;  // [pages, Hkv, page_size, bytes]
   return p;
 }
 
@@ -664,10 +667,12 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_codes, torch::Tenso
                             torch::Tensor v_scales, torch::Tensor block_tables, torch::Tensor seq_lens,
                             torch::Tensor out, torch::Tensor o_part, torch::Tensor lse_part, int64_t Hq, int64_t Hkv,
                             int64_t D, int64_t page_size, int64_t group, int64_t fmt_k, int64_t fmt_v,
-                            double sm_scale, int64_t splits, int64_t tiles_per_split) {
+                            double sm_scale, int64_t splits, int64_t tiles_per_split,
+                            c10::optional<torch::Tensor> status) {
   const c10::cuda::CUDAGuard g(q.device());
   auto p = attn_common(q, k_codes, k_scales, v_codes, v_scales, block_tables, out, Hq, Hkv, D, page_size, group,
                        fmt_k, fmt_v, sm_scale);
+  p.status = optr<int>(status);
   CHECK_DT(seq_lens, torch::kInt32);
   p.seq_lens = ptr<int>(seq_lens);
   p.B = (int)seq_lens.size(0);
@@ -693,6 +698,7 @@ void paged_prefill_attention(torch::Tensor q, torch::Tensor k_codes, torch::Tens
   auto p = attn_common(q, k_codes, k_scales, v_codes, v_scales, block_tables, out, Hq, Hkv, D, page_size, group,
                        fmt_k, fmt_v, sm_scale);
   p.tree_mask = optr<int>(tree_mask);
+  p.status = optr<int>(status);
   p.tile_seq = ptr<int>(tile_seq);
   p.tile_q0 = ptr<int>(tile_q0);
   p.q_start = ptr<int>(q_start);

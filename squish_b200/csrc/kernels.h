@@ -23,6 +23,8 @@ struct RopeKvParams {
   const __nv_bfloat16* q_norm;  // [D] per-head RMSNorm weight applied before RoPE (Qwen3), or nullptr
   const __nv_bfloat16* k_norm;
   float norm_eps;
+  int num_pages;  // pages in the pools: a slot at or past num_pages * page_size is not written and
+  int* status;    // records SQ_ERR_BOUNDS here (num_pages 0 or status nullptr: unchecked)
 };
 
 struct AttnParams {
@@ -54,6 +56,10 @@ struct AttnParams {
   // optional token-tree masks (speculative verification), one per query row: bit j set =
   // the row may attend chunk token j; 0 = plain causal. A tree chunk is at most 32 tokens.
   const int* tree_mask;
+  // page-index check: a block-table entry outside [0, num_pages) is read as an empty page and
+  // records SQ_ERR_BOUNDS in *status (num_pages 0 or status nullptr: unchecked)
+  int num_pages;
+  int* status;
 };
 
 cudaError_t rope_kv_write_launch(const RopeKvParams& p, int T, cudaStream_t s);

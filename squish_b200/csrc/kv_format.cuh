@@ -33,6 +33,15 @@ __host__ __device__ constexpr float kv_qmax(int f) {
   return f == KV_INT8 ? 127.f : f == KV_INT4 ? 7.5f : f == KV_INT2 ? 1.5f : f == KV_K8 ? 255.f : 15.f;
 }
 
+// KV pool index check shared by the kernels that read or write pages: true when `idx` lies in
+// [0, limit); otherwise the first failing thread records SQ_ERR_BOUNDS (6, sm100.cuh) in
+// *status and the caller skips the access. limit <= 0 disables the check.
+__device__ __forceinline__ bool kv_index_ok(long long idx, long long limit, int* status) {
+  if (limit <= 0 || (idx >= 0 && idx < limit)) return true;
+  if (status != nullptr) atomicCAS(status, 0, 6);
+  return false;
+}
+
 struct KvLayer {
   const uint8_t* codes;
   const __half* scales;

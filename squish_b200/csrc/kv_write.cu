@@ -163,7 +163,7 @@ __global__ void rope_kv_write_kernel(RopeKvParams p) {
       __nv_bfloat16* dst = p.q_out + ((size_t)t * p.Hq + j) * D;
 #pragma unroll
       for (int jj = 0; jj < J; ++jj) dst[lane + 32 * jj] = __float2bfloat16(v[jj]);
-    } else if (slot >= 0) {
+    } else if (slot >= 0 && kv_index_ok(slot, (long long)p.num_pages * p.page_size, p.status)) {
       const bool is_k = j < p.Hq + p.Hkv;
       const int h = is_k ? j - p.Hq : j - p.Hq - p.Hkv;
       const int fmt = is_k ? p.fmt_k : p.fmt_v;

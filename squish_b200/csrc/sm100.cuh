@@ -23,7 +23,7 @@ enum : int {
   SQ_ERR_TIMEOUT_A = 3,      // dequant-buffer wait
   SQ_ERR_TIMEOUT_ACC = 4,    // accumulator-ready wait
   SQ_ERR_TIMEOUT_PEER = 5,   // cross-GPU flag wait
-  SQ_ERR_BOUNDS = 6,         // index check failed (debug builds)
+  SQ_ERR_BOUNDS = 6,         // an index (KV page, cache slot) outside its pool; the access was skipped
 };
 
 // Iteration budget for one mbarrier wait. Each try_wait already blocks for a

@@ -384,7 +384,7 @@ class CudaRunner:
             kc, ks, vc, vs = self.pools.layers[li]
             q = self.q[:T]
             ops.rope_kv_write(qkv, m["pos"], self.cos_sin, q, m["slots"], kc, ks, vc, vs, hq, hkv, d, ps, grp,
-                              self.fk, self.fv, lw.q_norm, lw.k_norm, cfg.rms_eps)
+                              self.fk, self.fv, lw.q_norm, lw.k_norm, cfg.rms_eps, ws=ws)
             attn = self.attn[:T]
             if Bd:
                 ops.paged_decode_attention(q[:Bd], kc, ks, vc, vs, bt[:Bd], m["dlens"], attn[:Bd], hq, hkv, d, ps, grp,

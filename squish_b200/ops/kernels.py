@@ -79,11 +79,13 @@ class Workspace:
         return self._rot[: m * k].view(m, k)
 
     def check(self) -> None:
-        """Raise if any kernel recorded an error (a bounded wait that timed out)."""
+        """Raise if any kernel recorded an error: a bounded wait that timed out (1-5) or an
+        index outside its pool (6: a KV page or cache slot; the access was skipped)."""
         code = int(self.status.item())
         if code != 0:
             self.status.zero_()
-            raise RuntimeError(f"squish_b200 kernel reported status {code} (bounded wait timed out)")
+            what = "index outside its pool" if code == 6 else "bounded wait timed out"
+            raise RuntimeError(f"squish_b200 kernel reported status {code} ({what})")
 
 
 _WORKSPACES: dict[int, Workspace] = {}
@@ -368,9 +370,11 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor
 
 def rope_kv_write(qkv, positions, cos_sin, q_out, slot_mapping, k_codes, k_scales, v_codes, v_scales,
                   hq: int, hkv: int, d: int, page_size: int, group: int, fmt_k: int, fmt_v: int,
-                  q_norm=None, k_norm=None, norm_eps: float = 1e-6) -> None:
+                  q_norm=None, k_norm=None, norm_eps: float = 1e-6, ws: Workspace | None = None) -> None:
+    """A slot past the pools is not written; it records SQ_ERR_BOUNDS in the workspace status."""
+    ws = ws or workspace(qkv.device)
     native().rope_kv_write(qkv, positions, cos_sin, q_out, slot_mapping, k_codes, k_scales, v_codes, v_scales,
-                           hq, hkv, d, page_size, group, fmt_k, fmt_v, q_norm, k_norm, float(norm_eps))
+                           hq, hkv, d, page_size, group, fmt_k, fmt_v, q_norm, k_norm, float(norm_eps), ws.status)
     _count()
 
 
@@ -397,7 +401,8 @@ def paged_decode_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables
     s, tps = splits or decode_splits(b, hkv, max_ctx)
     o_part, lse = ws.attn_buffers(b, hq, s, d)
     native().paged_decode_attention(q, k_codes, k_scales, v_codes, v_scales, block_tables, seq_lens, out, o_part,
-                                    lse, hq, hkv, d, page_size, group, fmt_k, fmt_v, float(sm_scale), s, tps)
+                                    lse, hq, hkv, d, page_size, group, fmt_k, fmt_v, float(sm_scale), s, tps,
+                                    ws.status)
     _count(2 if s > 1 else 1)
     return out
 

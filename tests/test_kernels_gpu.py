@@ -6,6 +6,7 @@ import torch
 
 from squish_b200 import ops
 from squish_b200._ext import native
+from squish_b200.models.config import get_preset
 
 from ._refs import apply_rope, attention, dequant_int4_as_kernel, rope_cos_sin, sm_scale
 
@@ -409,3 +410,62 @@ def test_sampler_distribution(cuda):
         freq = torch.bincount(out.long().cpu(), minlength=v)[:4].float() / rows
         ref3 = full[:keep] / full[:keep].sum()
         assert freq[keep:].sum() == 0 and (freq[:keep] - ref3).abs().max() < 0.03, (tp, freq, ref3)
+
+
+@pytest.mark.parametrize("legacy", [False, True])
+def test_out_of_pool_indices_are_skipped_and_reported(cuda, monkeypatch, legacy):
+    """A block-table entry or cache slot outside the KV pools is never dereferenced: the kernel
+    reads an empty (or the first) page instead, records SQ_ERR_BOUNDS (6) in the workspace
+    status, and the workspace check raises; sequences with valid tables are unaffected."""
+    if legacy:
+        monkeypatch.setenv("SQ_DECODE_LEGACY", "1")
+        monkeypatch.setenv("SQ_PREFILL_ATTN_LEGACY", "1")
+    ps, group, hq, hkv, d = 16, 32, 28, 4, 128
+    fk, fv = ops.KV_FORMATS["int4"]
+    lens = [40, 300]
+    num_pages = sum((l + ps - 1) // ps for l in lens) + 1
+    kc, ks, vc, vs, kd, vd = _fill_random_cache(num_pages, hkv, ps, d, fk, fv, group, cuda, seed=9)
+    bt = torch.zeros(2, 19, dtype=torch.int32)
+    bt[0, :3] = torch.tensor([0, 1, 2])
+    bt[1, :19] = torch.arange(3, 22)
+    bt[1, 5] = num_pages + 7  # outside the pool
+    ws = ops.workspace(cuda)
+    ws.status.zero_()
+    q = torch.randn(2, hq * d).to(torch.bfloat16)
+    out = torch.full((2, hq * d), float("nan"), dtype=torch.bfloat16, device=cuda)
+    ops.paged_decode_attention(q.to(cuda), kc, ks, vc, vs, bt.to(cuda), torch.tensor(lens, dtype=torch.int32,
+                               device=cuda), out, hq, hkv, d, ps, group, fk, fv, sm_scale(d), max(lens))
+    torch.cuda.synchronize()
+    assert int(ws.status.item()) == 6
+    assert bool(torch.isfinite(out.float()).all())
+    k = _gather(kd, bt[0], lens[0], ps).to(torch.bfloat16).float()
+    v = _gather(vd, bt[0], lens[0], ps).to(torch.bfloat16).float()
+    ref = attention(q[0].float().view(1, hq, d), k, v, torch.tensor([lens[0] - 1]), sm_scale(d))
+    torch.testing.assert_close(out[0].float().cpu().view(1, hq, d), ref, rtol=2e-2, atol=3e-2)
+    with pytest.raises(RuntimeError, match="status 6"):
+        ws.check()
+    # prefill chunk of the second sequence over the same bad table
+    ql = 32
+    qp = torch.randn(ql, hq * d).to(torch.bfloat16).to(cuda)
+    outp = torch.zeros(ql, hq * d, dtype=torch.bfloat16, device=cuda)
+    i32 = dict(dtype=torch.int32, device=cuda)
+    ops.paged_prefill_attention(qp, kc, ks, vc, vs, bt[1:].to(cuda), torch.zeros(1, **i32), torch.zeros(1, **i32),
+                                torch.zeros(1, **i32), torch.tensor([ql], **i32), torch.tensor([lens[1]], **i32), 1,
+                                outp, hq, hkv, d, ps, group, fk, fv, sm_scale(d))
+    torch.cuda.synchronize()
+    assert int(ws.status.item()) == 6 and bool(torch.isfinite(outp.float()).all())
+    ws.status.zero_()
+    # KV write to a slot past the pool: nothing written, status recorded
+    before = [t.clone() for t in (kc, ks, vc, vs)]
+    qkv = torch.randn(2, (hq + 2 * hkv) * d, dtype=torch.bfloat16, device=cuda)
+    from squish_b200.models.reference import rope_table
+
+    cfg, _ = get_preset("qwen2.5-7b")
+    cs = rope_table(cfg, 64).to(cuda)
+    slots = torch.tensor([num_pages * ps + 3, -1], **i32)
+    ops.rope_kv_write(qkv, torch.tensor([5, 6], **i32), cs, torch.empty(2, hq, d, dtype=torch.bfloat16, device=cuda),
+                      slots, kc, ks, vc, vs, hq, hkv, d, ps, group, fk, fv)
+    torch.cuda.synchronize()
+    assert int(ws.status.item()) == 6
+    assert all(torch.equal(a, b) for a, b in zip(before, (kc, ks, vc, vs)))
+    ws.status.zero_()
