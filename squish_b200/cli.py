@@ -71,8 +71,9 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
                    help="expert-parallel GPUs for MoE models (experts split over ranks; sets --tp)")
     p.add_argument("--dp", type=int, default=1, help="data-parallel replicas (one per GPU) behind a request router")
     p.add_argument("--gpus", type=int, default=0, help="GPUs to use: tp x dp (dp = gpus / tp when --dp is not given)")
-    p.add_argument("--tp-mode", default="nvlink", choices=["nvlink", "nccl"],
-                   help="nvlink: fused GEMM + collectives over peer memory; nccl: NCCL collectives")
+    p.add_argument("--tp-mode", default="nvlink", choices=["nvlink", "sp", "nccl"],
+                   help="nvlink: fused GEMM + all-reduce over peer memory; sp: sequence parallel (fused GEMM -> "
+                        "reduce-scatter, RMSNorm + all-gather, gather-waiting GEMM; dense models); nccl: NCCL")
     p.add_argument("--log-level", default="warning", choices=["debug", "info", "warning", "error", "critical"])
     p.add_argument("--log-format", default="text", choices=["text", "json"], help="json: one JSON object per line")
 

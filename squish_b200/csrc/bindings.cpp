@@ -166,7 +166,9 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t group = 
 void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, int64_t K, int64_t group,
                 torch::Tensor y, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual,
                 int64_t epilogue, torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
-                c10::optional<torch::Tensor> trace, int64_t wfmt, c10::optional<torch::Tensor> codebook) {
+                c10::optional<torch::Tensor> trace, int64_t wfmt, c10::optional<torch::Tensor> codebook,
+                c10::optional<torch::Tensor> ag_flags = c10::nullopt, c10::optional<torch::Tensor> ag_done = c10::nullopt,
+                int64_t ag_expect = 0, int64_t ag_tp = 0) {
   TORCH_CHECK(wfmt >= 0 && wfmt <= 6, "unknown weight format");
   if (wfmt == sq::WF_AQLM) {
     TORCH_CHECK(codebook.has_value() && codebook->scalar_type() == torch::kBFloat16 && codebook->is_cuda() &&
@@ -209,6 +211,14 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, 
   p.codebook = optr<__nv_bfloat16>(codebook);
   p.n_books = codebook.has_value() ? (int)(codebook->numel() / (256 * 8)) : 0;
   p.trace = optr<unsigned long long>(trace);
+  if (ag_flags.has_value()) {  // all-gathered X: the activation producer waits for every source
+    TORCH_CHECK(ag_done.has_value() && ag_tp > 0 && ag_tp <= 32 && ag_flags->numel() >= ag_tp,
+                "all-gather wait needs ag_done, ag_expect and 1..32 sources");
+    p.ag_flags = ptr<int>(*ag_flags);
+    p.ag_done = ptr<int>(*ag_done);
+    p.ag_expect = (int)ag_expect;
+    p.tp = (int)ag_tp;
+  }
   const CUtensorMap xmap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), bn);
   CUDA_OK(sq::w4a16_gemm_launch(xmap, p, bn, nt, cur_stream()));
 }
@@ -496,6 +506,95 @@ std::vector<int64_t> w4a16_gemm_push(torch::Tensor x, torch::Tensor wq, int64_t 
     CUDA_OK(sq::w4a16_gemm_launch(xmap, p, bn, nt, cur_stream()));
   }
   return {bn, nt, plan[2], gx, gy};
+}
+
+// Row-parallel GEMM with reduce-scatter routing: the bf16 partial of token row m goes only to
+// its owner rank (m / rows_per_rank) at push_dst[owner] + (m % rows_per_rank) * ldy, and every
+// CTA counts one arrival at push_flags[r] + parity * flag_stride on every rank. Returns
+// {total CTAs of the launch} (the owners' expected count).
+int64_t w4a16_gemm_rs(torch::Tensor x, torch::Tensor wq, int64_t N, int64_t K, int64_t group, int64_t ldy,
+                      torch::Tensor push_dst, torch::Tensor push_flags, int64_t flag_stride, torch::Tensor seq,
+                      int64_t tp, int64_t rows_per_rank, torch::Tensor ws, torch::Tensor counters,
+                      torch::Tensor status) {
+  CHECK_CUDA(x);
+  CHECK_DT(x, torch::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(1) == K, "x must be [M, K]");
+  TORCH_CHECK(push_dst.scalar_type() == torch::kInt64 && push_dst.numel() == tp, "push_dst: [tp] int64 pointers");
+  TORCH_CHECK(push_flags.scalar_type() == torch::kInt64 && push_flags.numel() == tp, "push_flags: [tp] pointers");
+  const int64_t M = x.size(0);
+  TORCH_CHECK(rows_per_rank > 0 && rows_per_rank * tp >= M, "rows_per_rank * tp must cover every row");
+  const c10::cuda::CUDAGuard g(x.device());
+  auto plan = gemm_plan(M, N, K, group, sq::WF_INT4);
+  const int bn = (int)plan[0], nt = (int)plan[1];
+  sq::W4A16Params p{};
+  p.wq = ptr<uint32_t>(wq);
+  p.sz = p.wq;
+  p.ws = ptr<float>(ws);
+  p.counters = ptr<int>(counters);
+  p.status = ptr<int>(status);
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.ldy = (int)ldy;
+  p.kb_total = (int)((K + 63) / 64);
+  p.splits = (int)plan[2];
+  p.kb_per_split = (int)plan[3];
+  p.gpk = group >= 64 ? 1 : (int)(64 / group);
+  p.epilogue = sq::EPI_PLAIN;
+  p.push_dst = reinterpret_cast<__nv_bfloat16* const*>(push_dst.data_ptr());
+  p.push_flags = reinterpret_cast<int* const*>(push_flags.data_ptr());
+  p.push_stride = 0;  // one data buffer (the owners finish reading before any peer can push again)
+  p.flag_stride = (int)flag_stride;
+  p.seq = ptr<int>(seq);
+  p.tp = (int)tp;
+  p.push_rows = (int)rows_per_rank;
+  const int64_t gx = (N + 128 * nt - 1) / (128 * nt), gy = (M + bn - 1) / bn;
+  if (M > 0) {
+    const CUtensorMap xmap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), bn);
+    CUDA_OK(sq::w4a16_gemm_launch(xmap, p, bn, nt, cur_stream()));
+  }
+  return gx * gy * plan[2];
+}
+
+void tp_rs_norm_ag(torch::Tensor recv, int64_t src_stride, int64_t ld_recv, torch::Tensor rs_flags, int64_t rs_expect,
+                   torch::Tensor h, torch::Tensor w, double eps, torch::Tensor ag_dst, int64_t ld_ag,
+                   torch::Tensor ag_flags, int64_t rank, int64_t tp, int64_t rows_per_rank, int64_t T,
+                   torch::Tensor seq, torch::Tensor done, torch::Tensor status) {
+  CHECK_CUDA(h);
+  CHECK_DT(h, torch::kBFloat16);
+  CHECK_DT(w, torch::kBFloat16);
+  TORCH_CHECK(ag_dst.scalar_type() == torch::kInt64 && ag_dst.numel() == tp, "ag_dst: [tp] int64 pointers");
+  TORCH_CHECK(ag_flags.scalar_type() == torch::kInt64 && ag_flags.numel() == tp, "ag_flags: [tp] pointers");
+  TORCH_CHECK(h.dim() == 2 && h.stride(1) == 1 && h.size(0) >= T && w.numel() == h.size(1), "h [>= T, N], w [N]");
+  const c10::cuda::CUDAGuard g(h.device());
+  sq::TpRsNormParams p{};
+  p.recv = ptr<__nv_bfloat16>(recv);
+  p.src_stride = src_stride;
+  p.ld_recv = (int)ld_recv;
+  p.rs_flags = ptr<int>(rs_flags);
+  p.rs_expect = (int)rs_expect;
+  p.h = ptr<__nv_bfloat16>(h);
+  p.ldh = (int)h.stride(0);
+  p.w = ptr<__nv_bfloat16>(w);
+  p.eps = (float)eps;
+  p.ag_dst = reinterpret_cast<__nv_bfloat16* const*>(ag_dst.data_ptr());
+  p.ld_ag = (int)ld_ag;
+  p.ag_flags = reinterpret_cast<int* const*>(ag_flags.data_ptr());
+  p.rank = (int)rank;
+  p.tp = (int)tp;
+  p.rows_per_rank = (int)rows_per_rank;
+  p.T = (int)T;
+  p.N = (int)h.size(1);
+  p.seq = ptr<int>(seq);
+  p.done = ptr<int>(done);
+  p.status = ptr<int>(status);
+  CUDA_OK(sq::tp_rs_norm_ag_launch(p, cur_stream()));
+}
+
+void tp_ag_wait(torch::Tensor ag_flags, int64_t expect, int64_t tp, torch::Tensor status) {
+  CHECK_CUDA(ag_flags);
+  const c10::cuda::CUDAGuard g(ag_flags.device());
+  CUDA_OK(sq::tp_ag_wait_launch(ptr<int>(ag_flags), (int)expect, (int)tp, ptr<int>(status), cur_stream()));
 }
 
 void tp_push(torch::Tensor src, torch::Tensor push_dst, int64_t parity_stride, int64_t ld_dst,
@@ -941,7 +1040,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("repack_int4", &repack_int4);
   m.def("gemm_plan", &gemm_plan, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("group") = 64,
         py::arg("wfmt") = 0);
-  m.def("w4a16_gemm", &w4a16_gemm);
+  m.def("w4a16_gemm", &w4a16_gemm, py::arg("x"), py::arg("wq"), py::arg("sz"), py::arg("N"), py::arg("K"),
+        py::arg("group"), py::arg("y"), py::arg("bias"), py::arg("residual"), py::arg("epilogue"), py::arg("ws"),
+        py::arg("counters"), py::arg("status"), py::arg("trace"), py::arg("wfmt"), py::arg("codebook"),
+        py::arg("ag_flags") = py::none(), py::arg("ag_done") = py::none(), py::arg("ag_expect") = 0,
+        py::arg("ag_tp") = 0);
+  m.def("w4a16_gemm_rs", &w4a16_gemm_rs);
+  m.def("tp_rs_norm_ag", &tp_rs_norm_ag);
+  m.def("tp_ag_wait", &tp_ag_wait);
   m.def("dequant_weight", &dequant_weight);
   m.def("bf16_gemm", &bf16_gemm);
   m.def("w4a16_grouped_gemm", &w4a16_grouped_gemm);

@@ -158,7 +158,108 @@ __global__ void tp_gather_wait_kernel(const TpGatherParams p) {
   }
 }
 
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 t = __bfloat1622float2(h[k]);
+    f[2 * k] = t.x;
+    f[2 * k + 1] = t.y;
+  }
+}
+
+__global__ void __launch_bounds__(32 * kRsNormRowsPerCta) tp_rs_norm_ag_kernel(const TpRsNormParams p) {
+  pdl_wait();
+  pdl_trigger();
+  const int par = *reinterpret_cast<volatile const int*>(p.seq) & 1;
+  int* flags = p.rs_flags + par * p.tp;
+  if ((int)threadIdx.x < p.tp) wait_flag(flags + threadIdx.x, p.rs_expect, p.status);
+  __syncthreads();
+  __threadfence();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lr = blockIdx.x * kRsNormRowsPerCta + warp;
+  const int own = min(p.rows_per_rank, p.T - p.rank * p.rows_per_rank);
+  if (lr < own) {
+    const int m = p.rank * p.rows_per_rank + lr;
+    __nv_bfloat16* hr = p.h + (size_t)m * p.ldh;
+    float ss = 0.f;
+    for (int c = lane * 8; c < p.N; c += 256) {  // residual + partials in source order
+      float acc[8], t[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(hr + c), acc);
+      for (int s2 = 0; s2 < p.tp; ++s2) {
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(p.recv + s2 * p.src_stride + (size_t)lr * p.ld_recv + c), t);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] += t[k];
+      }
+      uint4 o;
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        o2[k] = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
+        const float2 r2 = __bfloat1622float2(o2[k]);  // the norm sees the stored (rounded) values
+        ss += r2.x * r2.x + r2.y * r2.y;
+      }
+      *reinterpret_cast<uint4*>(hr + c) = o;
+    }
+    ss = warp_sum_f(ss);
+    const float inv = rsqrtf(ss / (float)p.N + p.eps);
+    for (int c = lane * 8; c < p.N; c += 256) {
+      float v[8], g[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(hr + c), v);  // this lane's own stores
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(p.w + c), g);
+      uint4 o;
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) o2[k] = __floats2bfloat162_rn(v[2 * k] * inv * g[2 * k], v[2 * k + 1] * inv * g[2 * k + 1]);
+      for (int r = 0; r < p.tp; ++r) *reinterpret_cast<uint4*>(p.ag_dst[r] + (size_t)m * p.ld_ag + c) = o;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int r = 0; r < p.tp; ++r)
+      asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p.ag_flags[r]), "r"(1) : "memory");
+    __threadfence();
+    if (atomicAdd(p.done, 1) == (int)gridDim.x - 1) {
+      for (int s2 = 0; s2 < p.tp; ++s2) flags[s2] = 0;
+      *p.done = 0;
+      __threadfence();
+      atomicAdd(p.seq, 1);
+    }
+  }
+}
+
+__global__ void tp_ag_wait_kernel(int* ag_flags, int expect, int tp, int* status) {
+  pdl_wait();
+  pdl_trigger();
+  if ((int)threadIdx.x < tp) wait_flag(ag_flags + threadIdx.x, expect, status);
+  __syncthreads();
+  __threadfence();
+  if ((int)threadIdx.x < tp) ag_flags[threadIdx.x] = 0;
+}
+
 }  // namespace
+
+cudaError_t tp_rs_norm_ag_launch(const TpRsNormParams& p, cudaStream_t s) {
+  if (p.tp > 32 * kRsNormRowsPerCta || p.N % 8 || p.ldh % 8 || p.ld_ag % 8 || p.ld_recv % 8)
+    return cudaErrorInvalidValue;
+  const int grid = (p.rows_per_rank + kRsNormRowsPerCta - 1) / kRsNormRowsPerCta;
+  if (grid == 0) return cudaSuccess;
+  SQ_LAUNCH(tp_rs_norm_ag_kernel, dim3(grid), dim3(32 * kRsNormRowsPerCta), 0, s, 1, p);
+  return cudaGetLastError();
+}
+
+cudaError_t tp_ag_wait_launch(int* ag_flags, int expect, int tp, int* status, cudaStream_t s) {
+  if (tp > 32) return cudaErrorInvalidValue;
+  SQ_LAUNCH(tp_ag_wait_kernel, dim3(1), dim3(32), 0, s, 1, ag_flags, expect, tp, status);
+  return cudaGetLastError();
+}
 
 cudaError_t tp_reduce_launch(const TpReduceParams& p, int grid_x, int grid_y, cudaStream_t s) {
   if (p.tp > 256) return cudaErrorInvalidValue;

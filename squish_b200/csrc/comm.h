@@ -50,6 +50,36 @@ struct TpPushParams {
   int M, N, tile_m, tp;
   const int* seq;
 };
+// Sequence-parallel collectives (reduce-scatter -> RMSNorm -> all-gather), one kernel.
+// Rank r owns token rows [r * rows_per_rank, min(T, (r + 1) * rows_per_rank)). The row-parallel
+// GEMM pushed each source's bf16 partial of the owned rows into recv (the GEMM's reduce-scatter
+// routing); this kernel waits for every source's CTAs, adds the partials in source order to the
+// residual rows of h (written back), RMS-normalises them with w and stores the normalised rows
+// into every rank's all-gather buffer (P2P stores), then counts one arrival per CTA on every
+// rank's ag counter for this source. The last CTA clears this rank's reduce-scatter counters of
+// the parity it used and advances seq (parity = seq & 1 for the next round).
+struct TpRsNormParams {
+  const __nv_bfloat16* recv;     // [tp source][rows_per_rank][ld_recv] on this rank
+  long long src_stride;          // elements per source block
+  int ld_recv;
+  int* rs_flags;                 // this rank's counters [2 parity][tp source]
+  int rs_expect;                 // CTAs of the pushing GEMM launch (the same on every rank)
+  __nv_bfloat16* h;              // residual stream [T, ldh]
+  int ldh;
+  const __nv_bfloat16* w;        // RMSNorm weight [N]
+  float eps;
+  __nv_bfloat16* const* ag_dst;  // [tp] every rank's all-gather buffer [T, ld_ag]
+  int ld_ag;
+  int* const* ag_flags;          // [tp] every rank's all-gather counter for this source
+  int rank, tp, rows_per_rank, T, N;
+  int* seq;
+  int* done;
+  int* status;
+};
+constexpr int kRsNormRowsPerCta = 8;  // one warp per row
+cudaError_t tp_rs_norm_ag_launch(const TpRsNormParams& p, cudaStream_t s);
+// Wait (one CTA, bounded) until ag_flags[s] >= expect for every source, then clear them.
+cudaError_t tp_ag_wait_launch(int* ag_flags, int expect, int tp, int* status, cudaStream_t s);
 cudaError_t tp_push_launch(const TpPushParams& p, int grid_x, int grid_y, cudaStream_t s);
 cudaError_t tp_reduce_launch(const TpReduceParams& p, int grid_x, int grid_y, cudaStream_t s);
 cudaError_t tp_gather_launch(const TpGatherParams& p, cudaStream_t s);

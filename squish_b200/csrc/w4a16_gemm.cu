@@ -62,8 +62,11 @@ struct Cfg {
   static constexpr int kA0 = AT ? (NT * BN < 32 ? 32 : NT * BN) : 0;
   static constexpr int kCols = AT ? kA0 + 32 * kMaxRingA : NT * BN;
   static constexpr int kTmemCols = (kCols <= 32) ? 32 : (kCols <= 64) ? 64 : (kCols <= 128) ? 128 : (kCols <= 256) ? 256 : 512;
-  // pipelined dequant (two register copies of a stage) when the register budget has room
-  static constexpr bool kPipe = AT && (2 * kWpt * 4 + 48 <= 65536 / (kThreads * kMinBlocks));
+  // Dequantizing stage i + 1 before stage i's tensor-memory store completes (two register
+  // copies of a stage) was measured slower on B200 (gate_up at 64 tokens: 50.7 vs 43.5 us):
+  // it delays the a_full arrival that starts MMA(i), while dequant(i + 1) already overlaps
+  // MMA(i) in the plain order. Kept selectable for experiments.
+  static constexpr bool kPipe = false;
 };
 
 __host__ __device__ constexpr int code_bytes(int wfmt) {
@@ -262,6 +265,11 @@ __device__ __forceinline__ void store_out(const W4A16Params& p, int par, int m, 
     p.y[(size_t)m * p.ldy + n] = b;
     return;
   }
+  if (p.push_rows > 0) {  // reduce-scatter: only the owner of token row m receives it
+    const int owner = m / p.push_rows;
+    p.push_dst[owner][(size_t)par * p.push_stride + (size_t)(m - owner * p.push_rows) * p.ldy + n] = b;
+    return;
+  }
   const size_t off = (size_t)par * p.push_stride + (size_t)m * p.ldy + n;
   for (int r = 0; r < p.tp; ++r) p.push_dst[r][off] = b;
 }
@@ -269,6 +277,7 @@ __device__ __forceinline__ void store_out(const W4A16Params& p, int par, int m, 
 // After this CTA's stores of an output tile: make them visible system-wide, then bump the
 // tile's arrival flag on every rank (release at system scope).
 __device__ __forceinline__ void push_signal(const W4A16Params& p, int par, int tile) {
+  if (p.push_rows > 0) tile = 0;  // reduce-scatter: one arrival counter per (parity, source)
   for (int r = 0; r < p.tp; ++r) {
     int* f = p.push_flags[r] + (size_t)par * p.flag_stride + tile;
     asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(f), "r"(1) : "memory");
@@ -403,6 +412,19 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
   } else if (warp == 1) {
     // ------------------------------------------------ activation producer (TMA)
     pdl_wait();  // activations come from the previous kernel
+    if (p.ag_flags != nullptr && lane < p.tp) {
+      // all-gathered X: every source rank's rows have landed in this rank's buffer
+      for (long long it = 0;; ++it) {
+        int v;
+        asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p.ag_flags + lane) : "memory");
+        if (v >= p.ag_expect) break;
+        if (it > (1LL << 22) || *reinterpret_cast<volatile int*>(status) != 0) {
+          atomicCAS(status, 0, SQ_ERR_TIMEOUT_PEER);
+          break;
+        }
+      }
+    }
+    __syncwarp();
     Ring r(ring_x);
     for (int i = 0; i < nkb; ++i) {
       if (!mbar_wait(&x_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_X)) break;
@@ -730,6 +752,18 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
 
   tc_fence_before();
   __syncthreads();
+  if (p.ag_flags != nullptr && threadIdx.x == 0) {
+    // every CTA's producer has passed the wait once this counter reaches the grid size; no peer
+    // can signal the next all-gather before this rank's next reduce-scatter push, which comes
+    // after this kernel
+    __threadfence();
+    const int total = (int)(gridDim.x * gridDim.y * gridDim.z);
+    if (atomicAdd(p.ag_done, 1) == total - 1) {
+      for (int s2 = 0; s2 < p.tp; ++s2) p.ag_flags[s2] = 0;
+      *p.ag_done = 0;
+      __threadfence();
+    }
+  }
   if (threadIdx.x == 0) trace_mark(str, 15, 0);  // epilogue done
   __syncthreads();
   if (str != nullptr)

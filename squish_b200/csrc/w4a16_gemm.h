@@ -56,6 +56,17 @@ struct W4A16Params {
   int flag_stride;
   const int* seq;
   int tp;
+  // Reduce-scatter routing (push_rows > 0): row m goes only to rank m / push_rows (the owner of
+  // that token), at push_dst[owner] + parity * push_stride + (m - owner * push_rows) * ldy, and
+  // every CTA adds 1 to flag index 0 of its source row on every rank (the owners wait for the
+  // launch's CTA count).
+  int push_rows;
+  // All-gather wait (ag_flags != nullptr): X was pushed into this rank's buffer by tp ranks;
+  // before its first activation load the producer waits (bounded) until ag_flags[s] >= ag_expect
+  // for every source s. The last CTA to finish clears the flags (ag_done counts finished CTAs).
+  int* ag_flags;
+  int* ag_done;
+  int ag_expect;
 };
 
 // True when token tiles of <= 64 run the 4-dequant-warp configuration (four CTAs per SM):

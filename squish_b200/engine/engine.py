@@ -44,7 +44,8 @@ class EngineConfig:
     seed: int = 0
     spec: object | None = None  # speculative.SpecConfig: prompt lookup / draft model / Jacobi
     tp: int = 1                 # tensor-parallel ranks (one process per GPU, torch.distributed initialised)
-    tp_mode: str = "nvlink"     # "nvlink": fused GEMM+all-reduce over peer memory; "nccl": NCCL baseline
+    tp_mode: str = "nvlink"     # "nvlink": fused GEMM+all-reduce over peer memory; "sp": sequence parallel
+                                # (fused GEMM->reduce-scatter, RMSNorm+all-gather); "nccl": NCCL baseline
     peer_timeout_s: float = 10.0  # a rank whose heartbeat or liveness is older than this has failed
     kv_host_bytes: int = 0        # > 0: keep evicted prefix blocks in a host-RAM tier of this size
     kv_disk_dir: str | None = None  # spill (and persist across restarts) evicted prefix blocks here

@@ -370,30 +370,15 @@ class CudaRunner:
     def forward(self, st: StepInputs, m: dict) -> torch.Tensor:
         cfg = self.cfg
         T, Bd = st.num_tokens, st.num_decode
-        Bp = st.num_prefill
         ws = self.ws
         h, x = self.h[:T], self.x[:T]
         torch.index_select(self.embed, 0, m["ids"], out=h)
-        hq, hkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
-        ps, grp = self.qcfg.page_size, self.qcfg.kv_group
+        hkv = cfg.num_kv_heads
         dsplit = ops.kernels.decode_splits(max(Bd, 1), hkv, max(st.max_decode_ctx, 1)) if Bd else (1, 1)
-        bt = m["bt"]
         for li, lw in enumerate(self.layers):
             ops.rmsnorm(h, lw.ln1, cfg.rms_eps, out=x)
             qkv = ops.w4a16_linear(x, lw.qkv, out=self.qkv[:T], ws=ws)
-            kc, ks, vc, vs = self.pools.layers[li]
-            q = self.q[:T]
-            ops.rope_kv_write(qkv, m["pos"], self.cos_sin, q, m["slots"], kc, ks, vc, vs, hq, hkv, d, ps, grp,
-                              self.fk, self.fv, lw.q_norm, lw.k_norm, cfg.rms_eps, ws=ws)
-            attn = self.attn[:T]
-            if Bd:
-                ops.paged_decode_attention(q[:Bd], kc, ks, vc, vs, bt[:Bd], m["dlens"], attn[:Bd], hq, hkv, d, ps, grp,
-                                           self.fk, self.fv, self.sm_scale, st.max_decode_ctx, ws=ws, splits=dsplit)
-            if Bp:
-                tm = m["tmask"][Bd:] if "tmask" in m else None
-                ops.paged_prefill_attention(q[Bd:], kc, ks, vc, vs, bt[Bd:], m["tseq"], m["tq0"], m["qs"], m["ql"],
-                                            m["ctx"], st.tile_seq.shape[0], attn[Bd:], hq, hkv, d, ps, grp, self.fk,
-                                            self.fv, self.sm_scale, tree_mask=tm, ws=ws)
+            attn = self._attention(li, lw, qkv, st, m, dsplit)
             self._row_parallel(attn, lw.o, h)
             ops.rmsnorm(h, lw.ln2, cfg.rms_eps, out=x)
             if lw.moe is not None:
@@ -404,6 +389,28 @@ class CudaRunner:
         B = st.logits_rows.shape[0]
         xs = ops.rmsnorm(h, self.norm, cfg.rms_eps, out=self.xs[:B], row_idx=m["rows"])
         return self._lm_head(xs, B)
+
+    def _attention(self, li: int, lw, qkv: torch.Tensor, st: StepInputs, m: dict, dsplit) -> torch.Tensor:
+        """RoPE + KV write, then decode and prefill attention of layer li over the paged cache."""
+        cfg, ws = self.cfg, self.ws
+        T, Bd, Bp = st.num_tokens, st.num_decode, st.num_prefill
+        hq, hkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        ps, grp = self.qcfg.page_size, self.qcfg.kv_group
+        bt = m["bt"]
+        kc, ks, vc, vs = self.pools.layers[li]
+        q = self.q[:T]
+        ops.rope_kv_write(qkv, m["pos"], self.cos_sin, q, m["slots"], kc, ks, vc, vs, hq, hkv, d, ps, grp,
+                          self.fk, self.fv, lw.q_norm, lw.k_norm, cfg.rms_eps, ws=ws)
+        attn = self.attn[:T]
+        if Bd:
+            ops.paged_decode_attention(q[:Bd], kc, ks, vc, vs, bt[:Bd], m["dlens"], attn[:Bd], hq, hkv, d, ps, grp,
+                                       self.fk, self.fv, self.sm_scale, st.max_decode_ctx, ws=ws, splits=dsplit)
+        if Bp:
+            tm = m["tmask"][Bd:] if "tmask" in m else None
+            ops.paged_prefill_attention(q[Bd:], kc, ks, vc, vs, bt[Bd:], m["tseq"], m["tq0"], m["qs"], m["ql"],
+                                        m["ctx"], st.tile_seq.shape[0], attn[Bd:], hq, hkv, d, ps, grp, self.fk,
+                                        self.fv, self.sm_scale, tree_mask=tm, ws=ws)
+        return attn
 
     # hooks overridden by the tensor-parallel runner
     def _row_parallel(self, x: torch.Tensor, w: Int4Weight, h: torch.Tensor) -> None:

@@ -3,7 +3,11 @@
 It runs the same architecture with the dequantized weights (offset + q * scale in
 fp32) and stores K/V through the same quantize -> dequantize codec as the device's
 paged cache (the C++ CPU restatement of csrc/kv_write.cu), so CUDA logits can be
-compared against it step by step. It has no batching and no paging: one sequence,
+compared against it step by step. With ``bf16_storage`` every tensor the device keeps in
+bf16 between kernels (normalised rows, q/k/v, attention output, SwiGLU activation,
+residual stream, logits) is rounded to bf16 at that point while all arithmetic stays fp32:
+the same op as the device, so code flips of the quantized KV cache that would come only from
+fp32-vs-bf16 inputs to the codec do not mask kernel errors. It has no batching and no paging: one sequence,
 dense per-layer caches. The reference framework has no model code of its own (the
 forward pass lives in mlx_lm / HF transformers, squish/backend.py:222-390).
 """
@@ -60,7 +64,8 @@ class ReferenceModel:
 
     tap = None
 
-    def __init__(self, ck: Checkpoint, device: str | torch.device = "cpu"):
+    def __init__(self, ck: Checkpoint, device: str | torch.device = "cpu", bf16_storage: bool = False):
+        self.bf16_storage = bf16_storage
         self.cfg: ModelConfig = ck.config
         self.q: QuantConfig = ck.quant
         cfg = self.cfg
@@ -76,6 +81,10 @@ class ReferenceModel:
         t, h, d = x.shape
         codes, scales = native().cpu.kv_quantize(x.reshape(t * h, d).cpu().contiguous(), fmt, self.q.kv_group)
         return native().cpu.kv_dequantize(codes, scales, fmt, self.q.kv_group, d).reshape(t, h, d).to(x.device)
+
+    def _st(self, x: torch.Tensor) -> torch.Tensor:
+        """A tensor the device stores in bf16 (identity in the plain fp32 mode)."""
+        return x.to(torch.bfloat16).float() if self.bf16_storage else x
 
     def new_cache(self):
         z = lambda: torch.zeros(0, self.cfg.num_kv_heads, self.cfg.head_dim, device=self.device)  # noqa: E731
@@ -98,7 +107,7 @@ class ReferenceModel:
         if not cfg.is_moe:
             g = x @ w[p + "mlp.gate_proj.weight"].T
             u = x @ w[p + "mlp.up_proj.weight"].T
-            act = torch.nn.functional.silu(g) * u
+            act = self._st(torch.nn.functional.silu(g) * u)
             if self.tap is not None:
                 self.tap(p + "mlp.down_proj", act)
             return self._rp(act, w[p + "mlp.down_proj.weight"])
@@ -133,7 +142,7 @@ class ReferenceModel:
         d, hq, hkv = cfg.head_dim, cfg.num_heads, cfg.num_kv_heads
         for i in range(cfg.num_layers):
             p = f"model.layers.{i}."
-            x = _rms(h, w[p + "input_layernorm.weight"], cfg.rms_eps)
+            x = self._st(_rms(h, w[p + "input_layernorm.weight"], cfg.rms_eps))
             if self.tap is not None:
                 self.tap(p + "input_layernorm", x)
             q = x @ w[p + "self_attn.q_proj.weight"].T
@@ -143,11 +152,11 @@ class ReferenceModel:
                 q = q + w[p + "self_attn.q_proj.bias"]
                 k = k + w[p + "self_attn.k_proj.bias"]
                 v = v + w[p + "self_attn.v_proj.bias"]
-            q, k, v = q.view(t, hq, d), k.view(t, hkv, d), v.view(t, hkv, d)
+            q, k, v = self._st(q).view(t, hq, d), self._st(k).view(t, hkv, d), self._st(v).view(t, hkv, d)
             if cfg.qk_norm:
                 q = _rms(q, w[p + "self_attn.q_norm.weight"], cfg.rms_eps)
                 k = _rms(k, w[p + "self_attn.k_norm.weight"], cfg.rms_eps)
-            q, k = _rope(q, cs), _rope(k, cs)
+            q, k = self._st(_rope(q, cs)), _rope(k, cs)
             c = cache[i]
             c["k"] = torch.cat([c["k"], self._kv_roundtrip(k, self.fk)])
             c["v"] = torch.cat([c["v"], self._kv_roundtrip(v, self.fv)])
@@ -156,16 +165,16 @@ class ReferenceModel:
             s = torch.einsum("qhd,khd->hqk", q, kk) / math.sqrt(d)
             kpos = torch.arange(kk.shape[0], device=dev)
             s = s.masked_fill(kpos[None, None, :] > pos[None, :, None], float("-inf"))
-            a = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vv).reshape(t, hq * d)
+            a = self._st(torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vv).reshape(t, hq * d))
             if self.tap is not None:
                 self.tap(p + "self_attn.o_proj", a)
-            h = h + a @ w[p + "self_attn.o_proj.weight"].T
-            x = _rms(h, w[p + "post_attention_layernorm.weight"], cfg.rms_eps)
+            h = self._st(h + a @ w[p + "self_attn.o_proj.weight"].T)
+            x = self._st(_rms(h, w[p + "post_attention_layernorm.weight"], cfg.rms_eps))
             if self.tap is not None:
                 self.tap(p + "post_attention_layernorm", x)
-            h = h + self._mlp(p, x)
-        x = _rms(h, w["model.norm.weight"], cfg.rms_eps)
-        return x @ w["lm_head.weight"].T
+            h = self._st(h + self._mlp(p, x))
+        x = self._st(_rms(h, w["model.norm.weight"], cfg.rms_eps))
+        return self._st(x @ w["lm_head.weight"].T)
 
     def greedy(self, prompt: list[int], max_new: int) -> tuple[list[int], list[torch.Tensor]]:
         cache = self.new_cache()

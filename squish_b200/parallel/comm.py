@@ -6,6 +6,13 @@ Two implementations behind one interface:
     row-parallel GEMM pushes its output tiles into every rank's receive buffer from the
     GEMM epilogue and ``tp_reduce`` sums them (csrc/comm.cu); the vocab-parallel logits are
     gathered with P2P stores. No NCCL call on the step's hot path.
+  * ``sp`` (sequence parallel): rank r owns a contiguous block of the step's token rows; the
+    row-parallel GEMMs (o_proj, down_proj) route each partial row to its owner from the GEMM
+    epilogue (reduce-scatter: (tp-1)/tp of the rows cross NVLink, not (tp-1) copies of all of
+    them), one kernel per layer half sums the partials into the owned residual rows, applies
+    the next RMSNorm and pushes the normalised rows to every rank (all-gather), and the
+    column-parallel GEMM (qkv, gate_up) waits for the gather inside its activation producer
+    while its weights already stream;
   * ``nccl``: the same math with torch.distributed all_reduce / all_gather (the baseline;
     also what CPU ranks use, over gloo).
 
@@ -35,8 +42,10 @@ class TPComm:
         self.v0, self.v1 = v0, v1
         self.per = vocab_shard(vocab, 0, self.tp)[1]  # padded shard width (ranks' shards all fit in it)
         self._ipc = []
-        if mode == "nvlink":
+        if mode in ("nvlink", "sp"):
             self._setup_peer()
+            if mode == "sp":
+                self._setup_sp()
         else:
             self.tmp = torch.empty(max_tokens, hidden, dtype=torch.bfloat16 if mode == "nccl" else torch.float32,
                                    device=self.device)
@@ -89,13 +98,96 @@ class TPComm:
         torch.cuda.synchronize(dev)
         dist.barrier(group=self.group)
 
+    # ------------------------------------------------------------------ sequence parallel
+    def _setup_sp(self):
+        """Buffers of the sequence-parallel collectives: a reduce-scatter receive area
+        [tp source][rows per rank][H], the all-gather buffer [T][H] that the next GEMM reads,
+        and counters (reduce-scatter [2 parity][tp], all-gather [tp]) -- all in IPC memory
+        that the peers store into."""
+        tp, T, H = self.tp, self.max_tokens, self.hidden
+        dev = self.device
+        R = -(-T // tp)
+        self.sp_rows_max = R
+        recv = self._alloc_shared(tp * R * H * 2)
+        xg = self._alloc_shared(T * H * 2)
+        flags = self._alloc_shared(3 * tp * 4)
+        i64 = dict(dtype=torch.int64, device=dev)
+        self.sp_push_dst = torch.tensor([p + 2 * self.rank * R * H for p in recv], **i64)
+        self.sp_push_flags = torch.tensor([p + 4 * self.rank for p in flags], **i64)
+        self.sp_ag_dst = torch.tensor(xg, **i64)
+        self.sp_ag_flag_ptrs = torch.tensor([p + 4 * (2 * tp + self.rank) for p in flags], **i64)
+        idx = dev.index
+        self.sp_recv = native().tensor_from_ptr(recv[self.rank], [tp * R * H], torch.bfloat16, idx)
+        self.xg = native().tensor_from_ptr(xg[self.rank], [T, H], torch.bfloat16, idx)
+        fl = native().tensor_from_ptr(flags[self.rank], [3 * tp], torch.int32, idx)
+        self.sp_rs_flags, self.sp_ag_flags = fl[: 2 * tp], fl[2 * tp:]
+        self.sp_seq = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.sp_done = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.sp_ag_done = torch.zeros(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
+
+    def sp_rows(self, T: int) -> int:
+        """Token rows each rank owns in a T-token step (the last rank may own fewer or none)."""
+        return -(-T // self.tp)
+
+    def ag_expect(self, T: int) -> int:
+        return -(-self.sp_rows(T) // 8)  # CTAs of each source's tp_rs_norm_ag (8 rows each)
+
+    def gemm_rs(self, x: torch.Tensor, w, ws) -> int:
+        """Row-parallel GEMM whose partial rows go to their owner ranks (reduce-scatter routing
+        in the GEMM epilogue). Returns the launch's CTA count, the owners' expected arrivals."""
+        from ..ops import kernels as K
+
+        T = x.shape[0]
+        if T > self.max_tokens or w.n != self.hidden:
+            raise ValueError("row-parallel output exceeds the sequence-parallel buffers")
+        e = native().w4a16_gemm_rs(x, w.wq, w.n, w.k, w.group, w.n, self.sp_push_dst, self.sp_push_flags, self.tp,
+                                   self.sp_seq, self.tp, self.sp_rows(T), ws.gemm_ws, ws.gemm_counters, ws.status)
+        K._count()
+        return int(e)
+
+    def rs_norm_ag(self, h: torch.Tensor, norm_w: torch.Tensor, eps: float, T: int, rs_expect: int) -> None:
+        """Owned rows: h += sum of the tp partials; then RMSNorm(h) into every rank's xg."""
+        from ..ops import kernels as K
+
+        R = self.sp_rows(T)
+        native().tp_rs_norm_ag(self.sp_recv, self.sp_rows_max * self.hidden, self.hidden, self.sp_rs_flags,
+                               int(rs_expect), h, norm_w, float(eps), self.sp_ag_dst, self.hidden,
+                               self.sp_ag_flag_ptrs, self.rank, self.tp, R, T, self.sp_seq, self.sp_done,
+                               self.status)
+        K._count()
+
+    def ag_wait(self, T: int) -> None:
+        from ..ops import kernels as K
+
+        native().tp_ag_wait(self.sp_ag_flags, self.ag_expect(T), self.tp, self.status)
+        K._count()
+
+    def gemm_ag(self, w, out: torch.Tensor, T: int, silu_mul: bool, ws) -> torch.Tensor:
+        """Column-parallel GEMM over the all-gathered rows xg[:T]: the INT4 decode kernel waits
+        for the gather inside its activation producer (the weights stream meanwhile); the
+        bf16 prefill path and rotated weights wait in a separate one-CTA kernel first."""
+        from ..ops import kernels as K
+
+        x = self.xg[:T]
+        if T >= K.DQ_GEMM_MIN_M or w.rot is not None:
+            self.ag_wait(T)
+            return K.w4a16_linear(x, w, out=out, silu_mul=silu_mul, ws=ws)
+        native().w4a16_gemm(x, w.wq, w.sz, w.n, w.k, w.group, out, w.bias, None,
+                            K.EPI_SILU_MUL if silu_mul else K.EPI_PLAIN, ws.gemm_ws, ws.gemm_counters, ws.status,
+                            None, w.fmt, w.codebook, ag_flags=self.sp_ag_flags, ag_done=self.sp_ag_done,
+                            ag_expect=self.ag_expect(T), ag_tp=self.tp)
+        K._count()
+        return out
+
     # ------------------------------------------------------------------ collectives
     def gemm_allreduce(self, x: torch.Tensor, w, h: torch.Tensor, ws) -> None:
         """h += all_reduce(x @ w^T) over the group (w: this rank's row-parallel shard)."""
         from ..ops import kernels as K
 
         T = x.shape[0]
-        if self.mode != "nvlink":
+        if self.mode not in ("nvlink", "sp"):
             tmp = self.tmp[:T]
             if self.mode == "cpu":
                 tmp.copy_(x.float() @ w.T)
@@ -123,7 +215,7 @@ class TPComm:
         from ..ops import kernels as K
 
         T = x.shape[0]
-        if self.mode != "nvlink":
+        if self.mode not in ("nvlink", "sp"):
             tmp = self.tmp[:T]
             tmp.copy_(x.to(tmp.dtype))
             dist.all_reduce(tmp, group=self.group)
@@ -146,7 +238,7 @@ class TPComm:
         """[B, v1 - v0] vocab shard on every rank -> [B, vocab] on every rank."""
         from ..ops import kernels as K
 
-        if self.mode != "nvlink":
+        if self.mode not in ("nvlink", "sp"):
             pad = torch.zeros(B, self.per, dtype=self.gath.dtype, device=self.device)
             pad[:, : local.shape[1]] = local
             g = self.gath[: self.tp * B * self.per].view(self.tp * B, self.per)
@@ -160,13 +252,13 @@ class TPComm:
         return self.logits_full[:B]
 
     def check(self) -> None:
-        if self.mode == "nvlink":
+        if self.mode in ("nvlink", "sp"):
             s = int(self.status.item())
             if s:
                 raise RuntimeError(f"tensor-parallel collective failed (status {s}: a peer did not arrive in time)")
 
     def close(self) -> None:
-        if self.mode != "nvlink":
+        if self.mode not in ("nvlink", "sp"):
             return
         torch.cuda.synchronize(self.device)
         for kind, p in reversed(self._ipc):

@@ -2,7 +2,9 @@
 row-parallel outputs all-reduced and the vocab-parallel logits gathered.
 
 ``TPCudaRunner``: o_proj and down_proj run as one fused GEMM+all-reduce over NVLink (or the
-NCCL baseline), the LM head computes this rank's vocabulary slice and the slices are
+NCCL baseline), or, in the sequence-parallel mode, as GEMM->reduce-scatter with the RMSNorm
+and all-gather fused into one kernel and the gather wait fused into the next GEMM; the LM
+head computes this rank's vocabulary slice and the slices are
 gathered into a full logits row on every rank, so every rank samples the same tokens and
 the engine's host logic can run replicated on every rank. ``TorchTPRunner`` is the CPU
 (gloo) counterpart used to test the sharding end to end.
@@ -27,9 +29,47 @@ class TPCudaRunner(CudaRunner):
         self.logits_local = torch.empty(R, comm.v1 - comm.v0, dtype=torch.bfloat16, device=self.device)
         del self.logits
         self.logits = comm.logits_full
+        if comm.mode == "sp" and any(lw.moe is not None for lw in self.layers):
+            raise ValueError("the sequence-parallel mode covers dense models; MoE models use tp_mode 'nvlink'")
         for lw in self.layers:  # expert parallelism: all-reduce the local experts' partial output
             if lw.moe is not None:
                 lw.moe.ep_reduce = lambda part, h: self.comm.allreduce_add(part, h)
+
+    def forward(self, st, m):
+        if self.comm.mode != "sp":
+            return super().forward(st, m)
+        return self._forward_sp(st, m)
+
+    def _forward_sp(self, st, m):
+        """Sequence-parallel step: the residual rows of the step are split over the ranks;
+        o_proj / down_proj reduce-scatter their partial rows to the owners from the GEMM
+        epilogue, one kernel per half layer adds them to the owned residual rows, applies the
+        next RMSNorm and all-gathers the normalised rows, and qkv / gate_up read the gathered
+        rows as soon as every rank has pushed its part."""
+        from .. import ops
+
+        cfg, comm, ws = self.cfg, self.comm, self.ws
+        T, Bd = st.num_tokens, st.num_decode
+        h = self.h[:T]
+        torch.index_select(self.embed, 0, m["ids"], out=h)
+        dsplit = ops.kernels.decode_splits(max(Bd, 1), cfg.num_kv_heads, max(st.max_decode_ctx, 1)) if Bd else (1, 1)
+        xg = comm.xg[:T]
+        ops.rmsnorm(h, self.layers[0].ln1, cfg.rms_eps, out=xg)  # every row is valid everywhere at the start
+        L = len(self.layers)
+        for li, lw in enumerate(self.layers):
+            if li == 0:
+                qkv = ops.w4a16_linear(xg, lw.qkv, out=self.qkv[:T], ws=ws)
+            else:
+                qkv = comm.gemm_ag(lw.qkv, self.qkv[:T], T, False, ws)
+            attn = self._attention(li, lw, qkv, st, m, dsplit)
+            comm.rs_norm_ag(h, lw.ln2, cfg.rms_eps, T, comm.gemm_rs(attn, lw.o, ws))
+            act = comm.gemm_ag(lw.gate_up, self.act[:T], T, True, ws)
+            nxt = self.layers[li + 1].ln1 if li + 1 < L else self.norm
+            comm.rs_norm_ag(h, nxt, cfg.rms_eps, T, comm.gemm_rs(act[:, : self.F], lw.down, ws))
+        comm.ag_wait(T)
+        B = st.logits_rows.shape[0]
+        xs = torch.index_select(xg, 0, m["rows"], out=self.xs[:B])
+        return self._lm_head(xs, B)
 
     def _row_parallel(self, x, w, h):
         self.comm.gemm_allreduce(x, w, h, self.ws)

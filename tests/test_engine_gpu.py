@@ -44,14 +44,28 @@ def _teacher_forced_ok(ref, prompt, got, tol=0.04):
     return worst <= tol, worst
 
 
+def _as_stored(ck):
+    """The checkpoint with the weight values the device computes with: INT4 group scales and
+    zeros rounded to bf16 (the device tile layout stores them as bf16 pairs). The fp32 oracle
+    then runs the same model the GPU serves, at higher precision."""
+    for t in ck.tensors.values():
+        if getattr(t, "kind", None) == "q4a":
+            t.scales = t.scales.to(torch.bfloat16).float()
+            t.offsets = t.offsets.to(torch.bfloat16).float()
+    return ck
+
+
 @pytest.mark.parametrize("idx", range(4))
 def test_cuda_engine_matches_cpu_oracle(cuda, idx):
     cfg, q = _configs()[idx]
-    ck_cpu = random_checkpoint(cfg, q, seed=0, device="cpu")
+    ck_cpu = _as_stored(random_checkpoint(cfg, q, seed=0, device="cpu"))
     ref = ReferenceModel(ck_cpu)
     prompts = [_prompt(1, 32, cfg.vocab_size), _prompt(2, 77, cfg.vocab_size)]
-    cache = ref.new_cache()
-    ref_logits = ref.forward(prompts[0], cache, 0)[-1]
+    # the logit bar is taken against the oracle with the device's bf16 storage points: with a
+    # quantized KV cache, plain fp32 inputs to the codec flip codes at rounding boundaries
+    # (the fp32 oracle moves to cosine ~0.9987 from bf16 rounding of the INT4 scales alone)
+    st = ReferenceModel(ck_cpu, bf16_storage=True)
+    ref_logits = st.forward(prompts[0], st.new_cache(), 0)[-1]
     eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
                                     EngineConfig(max_num_seqs=4, max_num_batched_tokens=64, max_model_len=512,
                                                  num_pages=128, cuda_graphs=False))

@@ -1,6 +1,7 @@
 """Tensor parallelism on 2 GPUs (skipped with fewer): the fused GEMM+all-reduce over NVLink
-peer memory and the vocab gather against fp32 references, and the tensor-parallel engine
-(fused and NCCL modes) against the CPU fp32 oracle."""
+peer memory, the sequence-parallel GEMM->reduce-scatter / RMSNorm+all-gather / gather-waiting
+GEMM and the vocab gather against fp32 references, and the tensor-parallel engine (fused,
+sequence-parallel and NCCL modes) against the CPU fp32 oracle."""
 import dataclasses
 import datetime
 import os
@@ -94,6 +95,61 @@ def _collectives_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+def _sp_worker(rank, world, port, q):
+    """Sequence-parallel collectives: GEMM -> reduce-scatter, the fused residual add + RMSNorm +
+    all-gather, and the all-gather-waiting GEMM, against fp32 references (several row counts,
+    including fewer rows than ranks and the bf16 large-M path)."""
+    _init(rank, world, port)
+    try:
+        from squish_b200 import ops
+        from squish_b200._ext import native
+        from squish_b200.parallel.comm import TPComm
+
+        dev = torch.device("cuda", rank)
+        H, V, Tmax, K, F = 1024, 4000, 512, 512, 768
+        comm = TPComm("sp", Tmax, H, 64, V, device=dev)
+        ws = ops.Workspace(dev)
+        errs = []
+        for T in (1, 7, 64, 200, 448):
+            g = torch.Generator().manual_seed(T)  # the same full tensors on every rank
+            w_o = torch.randn(H, K * world, generator=g) * 0.02
+            w_up = torch.randn(F, H, generator=g) * 0.02
+            x_full = torch.randn(T, K * world, generator=g)
+            h0 = torch.randn(T, H, generator=g)
+            lnw = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+            wl = w_o[:, rank * K:(rank + 1) * K].contiguous()
+            p, s, z = native().cpu.quantize_int4_asym(wl, 64)
+            wo = ops.prepare_int4_weight(p, s, z, K, 64, dev)
+            deq = native().cpu.dequantize_int4_asym(p, s, z, 64)
+            p2, s2, z2 = native().cpu.quantize_int4_asym(w_up, 64)
+            wup = ops.prepare_int4_weight(p2, s2, z2, H, 64, dev)
+            deq_up = native().cpu.dequantize_int4_asym(p2, s2, z2, 64)
+            x = x_full[:, rank * K:(rank + 1) * K].to(torch.bfloat16).to(dev)
+            h = h0.to(torch.bfloat16).to(dev)
+            for _ in range(3):  # repeated rounds exercise the parity / counter protocol
+                hh = h.clone()
+                e = comm.gemm_rs(x, wo, ws)
+                comm.rs_norm_ag(hh, lnw.to(dev), 1e-6, T, e)
+                y = comm.gemm_ag(wup, torch.empty(T, F, dtype=torch.bfloat16, device=dev), T, False, ws)
+            torch.cuda.synchronize()
+            comm.check()
+            part = (x.float().cpu() @ deq.T).to(dev)
+            dist.all_reduce(part)
+            hsum = (h0.to(torch.bfloat16).float() + part.cpu()).to(torch.bfloat16).float()
+            xn = (hsum * torch.rsqrt(hsum.pow(2).mean(-1, keepdim=True) + 1e-6) * lnw.float()).to(torch.bfloat16)
+            R = -(-T // world)
+            r0, r1 = rank * R, min(T, (rank + 1) * R)
+            if r1 > r0:  # owned residual rows were updated
+                errs.append(float((hh[r0:r1].float().cpu() - hsum[r0:r1]).abs().max()) / float(hsum.abs().max()))
+            errs.append(float((comm.xg[:T].float().cpu() - xn.float()).abs().max()) / float(xn.float().abs().max()))
+            want = xn.float() @ deq_up.T
+            errs.append(float((y.float().cpu() - want).abs().max()) / float(want.abs().max()))
+        comm.close()
+        q.put((rank, errs))
+    finally:
+        dist.destroy_process_group()
+
+
 def _engine_worker(rank, world, port, mode, preset, q):
     _init(rank, world, port)
     try:
@@ -152,8 +208,15 @@ def test_fused_gemm_allreduce_and_gather():
 
 
 @needs2
-@pytest.mark.parametrize("mode,preset", [("nvlink", "tiny-llama"), ("nccl", "tiny-llama"), ("nvlink", "tiny-moe"),
-                                         ("nccl", "tiny-moe")])
+def test_sequence_parallel_collectives():
+    res = _run(_sp_worker, 2)
+    for rank, errs in res:
+        assert max(errs) < 2e-2, errs
+
+
+@needs2
+@pytest.mark.parametrize("mode,preset", [("nvlink", "tiny-llama"), ("nccl", "tiny-llama"), ("sp", "tiny-llama"),
+                                         ("nvlink", "tiny-moe"), ("nccl", "tiny-moe")])
 def test_tp_engine_matches_oracle(mode, preset):
     from squish_b200.models.reference import ReferenceModel
     from squish_b200.models.weights import random_checkpoint
