@@ -53,6 +53,12 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
     p.add_argument("--compress-min-tokens", type=int, default=256)
     p.add_argument("--compress-preserve-tokens", type=int, default=0)
     p.add_argument("--page-size", type=int, default=None, help="KV page size in tokens (a multiple of 16)")
+    p.add_argument("--prompt-logit-cache", type=int, default=64,
+                   help="keep the last logits of this many recent prompts: a repeated prompt's first token "
+                        "needs no forward pass (0 = off)")
+    p.add_argument("--kv-sink-tokens", type=int, default=0, help="attention sinks kept with --kv-window-tokens")
+    p.add_argument("--kv-window-tokens", type=int, default=0,
+                   help="> 0: attend to the sink pages and the most recent N tokens only; older KV pages are freed")
     # speculative decoding (the reference serves with prompt lookup on: squish/server.py:5194)
     sp = ucfg.load()["speculative"]
     p.add_argument("--prompt-lookup", dest="prompt_lookup", action="store_true", default=bool(sp["prompt_lookup"]),
@@ -115,7 +121,9 @@ def _ecfg(a):
                         max_model_len=a.max_model_len, gpu_memory_utilization=a.gpu_memory_utilization,
                         enable_prefix_caching=not a.no_prefix_caching, cuda_graphs=not a.no_cuda_graphs,
                         chunk_align=a.chunk_align, seed=a.seed, kv_host_bytes=int(a.kv_host_gb * (1 << 30)),
-                        kv_disk_dir=a.kv_disk_dir, spec=_spec(a), tp=tp, tp_mode=getattr(a, "tp_mode", "nvlink"))
+                        kv_disk_dir=a.kv_disk_dir, spec=_spec(a), tp=tp, tp_mode=getattr(a, "tp_mode", "nvlink"),
+                        prompt_logit_cache=a.prompt_logit_cache, kv_sink_tokens=a.kv_sink_tokens,
+                        kv_window_tokens=a.kv_window_tokens)
 
 
 def _kv(a):

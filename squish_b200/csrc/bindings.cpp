@@ -696,8 +696,13 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos
                    torch::Tensor slot_mapping, torch::Tensor k_codes, torch::Tensor k_scales, torch::Tensor v_codes,
                    torch::Tensor v_scales, int64_t Hq, int64_t Hkv, int64_t D, int64_t page_size, int64_t group,
                    int64_t fmt_k, int64_t fmt_v, c10::optional<torch::Tensor> q_norm,
-                   c10::optional<torch::Tensor> k_norm, double norm_eps, c10::optional<torch::Tensor> status) {
+                   c10::optional<torch::Tensor> k_norm, double norm_eps, c10::optional<torch::Tensor> status,
+                   c10::optional<torch::Tensor> had_k, c10::optional<torch::Tensor> had_v) {
   CHECK_CUDA(qkv);
+  for (const auto* h : {&had_k, &had_v})
+    if (h->has_value())
+      TORCH_CHECK((*h)->scalar_type() == torch::kFloat32 && (*h)->numel() == D && (*h)->is_cuda(),
+                  "Hadamard signs: float32 [head_dim] on the device");
   CHECK_DT(qkv, torch::kBFloat16);
   CHECK_DT(positions, torch::kInt32);
   CHECK_DT(slot_mapping, torch::kInt32);
@@ -726,6 +731,8 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos
   p.norm_eps = (float)norm_eps;
   p.num_pages = k_codes.dim() == 4 ? (int)k_codes.size(0) : 0;
   p.status = optr<int>(status);
+  p.had_k = optr<float>(had_k);
+  p.had_v = optr<float>(had_v);
   CUDA_OK(sq::rope_kv_write_launch(p, (int)qkv.size(0), cur_stream()));
 }
 

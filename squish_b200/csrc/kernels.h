@@ -25,6 +25,12 @@ struct RopeKvParams {
   float norm_eps;
   int num_pages;  // pages in the pools: a slot at or past num_pages * page_size is not written and
   int* status;    // records SQ_ERR_BOUNDS here (num_pages 0 or status nullptr: unchecked)
+  // Hadamard-rotated KV (nullptr: off): q and k are stored as H (had_k * x) / sqrt(D), v as
+  // had_v * (H v) / sqrt(D), with H the Sylvester Hadamard matrix and had_* +-1 signs [D]. Scores
+  // are unchanged (an orthogonal map on both sides); the attention output comes out rotated and
+  // is mapped back with H (had_v * o) / sqrt(D) (hadamard_rows) before o_proj.
+  const float* had_k;
+  const float* had_v;
 };
 
 struct AttnParams {

@@ -109,6 +109,38 @@ __device__ void quant_row(const float (&v)[D / 32], int fmt, int G, uint8_t* cod
   }
 }
 
+// In-warp fast Walsh-Hadamard transform of the D values held as v[jj] = x[lane + 32 * jj],
+// scaled by 1 / sqrt(D) (orthonormal): index bits 0-4 are lane bits (butterflies through
+// shuffles), bits 5.. are register bits.
+template <int D>
+__device__ __forceinline__ void fwht_warp(float (&v)[D / 32]) {
+  constexpr int J = D / 32;
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int h = 1; h < 32; h <<= 1) {
+#pragma unroll
+    for (int jj = 0; jj < J; ++jj) {
+      const float o = __shfl_xor_sync(0xffffffffu, v[jj], h);
+      v[jj] = (lane & h) ? o - v[jj] : v[jj] + o;
+    }
+  }
+#pragma unroll
+  for (int h = 1; h < J; h <<= 1) {
+#pragma unroll
+    for (int jj = 0; jj < J; ++jj) {
+      if ((jj & h) == 0) {
+        const float a = v[jj], b = v[jj + h];
+        v[jj] = a + b;
+        v[jj + h] = a - b;
+      }
+    }
+  }
+  constexpr float kScale = D == 32 ? 0.17677669529663688f : D == 64 ? 0.125f : D == 128 ? 0.08838834764831845f
+                                                                                         : 0.0625f;
+#pragma unroll
+  for (int jj = 0; jj < J; ++jj) v[jj] *= kScale;
+}
+
 template <int D>
 __global__ void rope_kv_write_kernel(RopeKvParams p) {
   pdl_wait();
@@ -158,6 +190,15 @@ __global__ void rope_kv_write_kernel(RopeKvParams p) {
 #pragma unroll
         for (int jj = 0; jj < J; ++jj) v[jj] = r[jj];
       }
+      if (p.had_k != nullptr) {  // rotated scores basis: H (s_k * x)
+#pragma unroll
+        for (int jj = 0; jj < J; ++jj) v[jj] *= p.had_k[lane + 32 * jj];
+        fwht_warp<D>(v);
+      }
+    } else if (p.had_v != nullptr) {  // v: s_v * (H v)
+      fwht_warp<D>(v);
+#pragma unroll
+      for (int jj = 0; jj < J; ++jj) v[jj] *= p.had_v[lane + 32 * jj];
     }
     if (j < p.Hq) {
       __nv_bfloat16* dst = p.q_out + ((size_t)t * p.Hq + j) * D;

@@ -46,7 +46,7 @@ constexpr int BK = 64;                     // K per stage = one 128-byte bf16 sw
 constexpr int W_TILE_BYTES = BM * BK / 2;  // 4096 nibble bytes per tile
 constexpr int A_TILE_BYTES = BM * BK * 2;  // 16384
 
-template <int BN_, int NT_, int MINB_, int DQW_ = 8>
+template <int BN_, int NT_, int MINB_, int DQW_ = 8, bool ASMEM_ = false>
 struct Cfg {
   static constexpr int BN = BN_;
   static constexpr int NT = NT_;          // 128-row weight tiles per CTA
@@ -57,7 +57,7 @@ struct Cfg {
   static constexpr int kXBytes = BN * 128;
   // Single weight tile per CTA: the dequantized A operand goes to tensor memory (tcgen05.st)
   // instead of shared memory; columns [kA0, kA0 + 32 * ring_a) hold the A ring.
-  static constexpr bool AT = (NT == 1);
+  static constexpr bool AT = (NT == 1) && !ASMEM_;
   static constexpr int kMaxRingA = MINB_ >= 3 ? 2 : 4;  // 3+ CTAs per SM share 512 TMEM columns
   static constexpr int kA0 = AT ? (NT * BN < 32 ? 32 : NT * BN) : 0;
   static constexpr int kCols = AT ? kA0 + 32 * kMaxRingA : NT * BN;
@@ -860,6 +860,22 @@ cudaError_t launch_decode_narrow(const CUtensorMap& xmap, const W4A16Params& p, 
     }
     return lo;
   };
+  auto fit2 = [&](int rx, int ra, size_t budget, int lo, int hi) {  // A ring in shared memory
+    for (int rw = hi; rw > lo; --rw) {
+      const Layout L = make_layout(BN, 1, p.gpk, rw, rx, ra, tr, false, p.wfmt);
+      if ((size_t)L.total + 1024 <= budget) return rw;
+    }
+    return lo;
+  };
+  static const bool asmem = [] {  // experiment: the dequantized operand in shared memory
+    const char* e = std::getenv("SQ_GEMM_ASMEM");
+    return e != nullptr && e[0] == '1';
+  }();
+  if (asmem) {
+    constexpr int rx = BN >= 32 ? 4 : 6;
+    if (per_sm <= 2) return launch_cfg<Cfg<BN, 1, 2, 4, true>>(xmap, p, fit2(rx, 2, 113 * 1024, 3, 16), rx, 2, s);
+    return launch_cfg<Cfg<BN, 1, 4, 4, true>>(xmap, p, fit2(3, 1, 56 * 1024, 2, 8), 3, 1, s);
+  }
   if (per_sm <= 2) {
     constexpr int rx = BN >= 32 ? 4 : 6;
     return launch_cfg<Cfg<BN, 1, 2, 4>>(xmap, p, fit(rx, 4, 113 * 1024, 4, 24), rx, 4, s);

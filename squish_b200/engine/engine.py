@@ -12,9 +12,11 @@ prefix reuse.
 """
 from __future__ import annotations
 
+import hashlib
 import itertools
 import time
 import zlib
+from collections import OrderedDict
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -54,6 +56,15 @@ class EngineConfig:
     # (>= DQ_GEMM_MIN_M tokens): ~4x the INT4 weight bytes of HBM for no per-step expansion;
     # decode keeps reading the quantized codes
     prefill_weight_cache: bool = True
+    # > 0: keep the last-position logits of this many recently prefilled prompts; a request
+    # whose prompt repeats one of them gets its first token with no forward pass
+    prompt_logit_cache: int = 64
+    # attention window (StreamingLLM-style sinks + recent window, page granular): with
+    # kv_window_tokens > 0, a sequence keeps its first ceil(kv_sink_tokens / page_size) pages and
+    # the pages that hold any of its last kv_window_tokens positions; older pages go back to the
+    # pool and attention no longer sees them. 0 = full attention.
+    kv_sink_tokens: int = 0
+    kv_window_tokens: int = 0
 
 
 @dataclass
@@ -69,6 +80,55 @@ class EngineStats:
     graph_steps: int = 0
     mixed_steps: int = 0
     scheduled_tokens: int = 0
+    instant_first_tokens: int = 0  # first tokens sampled from the prompt-logit cache
+    evicted_pages: int = 0         # pages given back by the attention window
+
+
+class PromptLogitCache:
+    """Last-position logits of recently prefilled prompts, keyed by the prompt's token ids
+    (LRU over a preallocated [entries, vocab] buffer on the runner's device).
+
+    A request whose prompt is stored gets its first token sampled from the stored row by the
+    runner's own sampler, so TTFT is one sampling call instead of a prefill; the prompt (plus
+    that token) is then computed by the next steps exactly as for a preempted request that
+    resumes, reusing the cached prefix pages. The reference keeps a float32 last-position logit
+    per KV block and uses it only when a prompt matches whole blocks to its last token
+    (squish/kv/block_kv_cache.py:65-85); here any prompt length qualifies, since the
+    uncached tail is computed after the first token is emitted."""
+
+    def __init__(self, entries: int):
+        self.entries = entries
+        self.buf: torch.Tensor | None = None
+        self.slot: OrderedDict[bytes, int] = OrderedDict()
+        self.hits = 0
+
+    @staticmethod
+    def key(prompt: list[int]) -> bytes:
+        return hashlib.blake2b(np.asarray(prompt, dtype=np.int32).tobytes(), digest_size=16).digest()
+
+    def get(self, key: bytes) -> torch.Tensor | None:
+        s = self.slot.get(key)
+        if s is None:
+            return None
+        self.slot.move_to_end(key)
+        self.hits += 1
+        return self.buf[s]
+
+    def put(self, key: bytes, row: torch.Tensor) -> None:
+        if key in self.slot:
+            self.slot.move_to_end(key)
+            return
+        if self.buf is None or self.buf.shape[1] != row.shape[0] or self.buf.dtype != row.dtype:
+            self.buf = torch.empty(self.entries, row.shape[0], dtype=row.dtype, device=row.device)
+            self.slot.clear()
+        s = self.slot.popitem(last=False)[1] if len(self.slot) >= self.entries else len(self.slot)
+        self.buf[s].copy_(row, non_blocking=True)
+        self.slot[key] = s
+
+
+def _rng_step(r: Request) -> int:
+    """Sampler stream position of a request's next token (seeded per request id)."""
+    return (r.rng_step + (zlib.crc32(r.rid.encode()) & 0xFFFF) * 65536) & 0x7FFFFFFF
 
 
 class LLMEngine:
@@ -95,6 +155,8 @@ class LLMEngine:
         self.monitor = None   # utils.fault.PeerMonitor (multi-rank engines)
         self.injector = None  # utils.fault.FaultInjector (SQUISH_FAULT)
         self.spec_stats = {"verifies": 0, "drafted": 0, "accepted": 0, "emitted": 0}
+        self.logit_cache = PromptLogitCache(ecfg.prompt_logit_cache) if ecfg.prompt_logit_cache > 0 else None
+        self._ready: list[RequestOutput] = []  # outputs produced outside a step (cached first tokens)
 
     # ------------------------------------------------------------------ construction
     @staticmethod
@@ -222,7 +284,30 @@ class LLMEngine:
         req = Request(rid, list(map(int, prompt)), params)
         self.scheduler.add(req)
         self.requests[rid] = req
+        if self.logit_cache is not None:
+            req.prompt_key = self.logit_cache.key(req.prompt)
+            if params.grammar is None and not params.return_hidden and not params.logprobs:
+                self._instant_first_token(req)
         return rid
+
+    def _instant_first_token(self, req: Request) -> None:
+        """Sample the first token from the prompt-logit cache (no forward pass) on a hit."""
+        row = self.logit_cache.get(req.prompt_key)
+        if row is None:
+            return
+        p = req.params
+        hist = None
+        if p.repetition_penalty != 1.0:
+            hist = np.full((1, self.ecfg.hist_window), -1, dtype=np.int32)
+            t = req.prompt[-self.ecfg.hist_window:]
+            hist[0, :len(t)] = t
+        tok = self.runner.sample_row(row, p.temperature, p.top_p, p.top_k, p.min_p, p.repetition_penalty, hist,
+                                     self.ecfg.seed, _rng_step(req))
+        self.stats.instant_first_tokens += 1
+        out = self._emit(req, [tok], time.perf_counter())
+        if out.finished and req in self.scheduler.waiting:
+            self.scheduler.waiting.remove(req)
+        self._ready.append(out)
 
     def abort(self, rid: str) -> None:
         req = self.requests.get(rid)
@@ -236,7 +321,7 @@ class LLMEngine:
             self.scheduler.finish(req, "abort")
 
     def has_unfinished(self) -> bool:
-        return self.scheduler.has_work()
+        return bool(self._ready) or self.scheduler.has_work()
 
     # ------------------------------------------------------------------ step
     def build_inputs(self, sched: Schedule) -> StepInputs:
@@ -247,7 +332,7 @@ class LLMEngine:
         pos = np.empty(T, dtype=np.int32)
         slots = np.empty(T, dtype=np.int32)
         nb = len(entries)
-        maxp = max((len(e.req.pages) for e in entries), default=1)
+        maxp = max((len(e.req.page_array()) for e in entries), default=1)
         if self.graphs is not None:
             maxp = self.max_pages
         bt = np.zeros((nb, max(maxp, 1)), dtype=np.int32)
@@ -260,6 +345,8 @@ class LLMEngine:
             r = e.req
             pg = r.page_array()
             bt[i, :len(pg)] = pg
+            if r.evicted_tokens:
+                pg = r.logical_pages()
             if e.n == 1 and e.tree is None:  # decode: scalars, no per-entry numpy temporaries
                 ids[off] = r.token_at(e.start)
                 pos[off] = e.start
@@ -290,9 +377,9 @@ class LLMEngine:
                 samp.append(r)
             off += e.n
         nd = len(sched.decode)
-        dl = np.asarray([e.start + 1 for e in sched.decode], dtype=np.int32)
+        dl = np.asarray([e.start + 1 - e.req.evicted_tokens for e in sched.decode], dtype=np.int32)
         ql = np.asarray([e.n for e in sched.prefill], dtype=np.int32)
-        ctx = np.asarray([e.start + e.n for e in sched.prefill], dtype=np.int32)
+        ctx = np.asarray([e.start + e.n - e.req.evicted_tokens for e in sched.prefill], dtype=np.int32)
         qs = np.zeros(len(ql), dtype=np.int32)
         if len(ql):
             qs[1:] = np.cumsum(ql)[:-1]
@@ -305,9 +392,7 @@ class LLMEngine:
         rep = np.asarray([r.params.repetition_penalty for r in samp], dtype=np.float32)
 
         def rng_steps(reqs):
-            st_ = np.asarray([r.rng_step + (zlib.crc32(r.rid.encode()) & 0xFFFF) * 65536 for r in reqs],
-                             dtype=np.int64)
-            return (st_ & 0x7FFFFFFF).astype(np.int32)
+            return np.asarray([_rng_step(r) for r in reqs], dtype=np.int64).astype(np.int32)
 
         step = rng_steps(samp)
         hist = None
@@ -379,6 +464,12 @@ class LLMEngine:
         sched.prefill[:0] = verify
 
     def step(self) -> list[RequestOutput]:
+        if self._ready:  # first tokens sampled at submission: returned before any forward runs
+            ready, self._ready = self._ready, []
+            return ready
+        return self._step_guarded()
+
+    def _step_guarded(self) -> list[RequestOutput]:
         if self.monitor is None and self.injector is None:
             return self._step()
         n = self.stats.steps
@@ -424,6 +515,10 @@ class LLMEngine:
                 r.num_computed = e.start + e.n
                 if not e.sample:
                     self.stats.prompt_tokens += e.n
+        if self.logit_cache is not None:  # first tokens: keep the prompt's last-position logits
+            for i, r in enumerate(samp):
+                if not r.output and r.prompt_key is not None:
+                    self.logit_cache.put(r.prompt_key, self.runner.logit_row(i))
         want_hidden = [i for i, r in enumerate(samp) if r.params.return_hidden]
         if want_hidden:
             hid = self.runner.last_hidden
@@ -433,7 +528,28 @@ class LLMEngine:
             outs.append(self._emit(r, [int(t)], now))
         if st.num_verify:
             outs.extend(self._apply_verify(sched, st, now))
+        if self.ecfg.kv_window_tokens > 0:
+            for e in sched.decode + sched.prefill:
+                if e.req.status is Status.RUNNING:
+                    self._evict_window(e.req)
         return outs
+
+    def _evict_window(self, r: Request) -> None:
+        """Give back the pages between the sink pages and the recent window (page granular:
+        a page goes when its last position is older than the window)."""
+        ps = self.qcfg.page_size
+        sink = -(-self.ecfg.kv_sink_tokens // ps)
+        upto = (r.num_computed - self.ecfg.kv_window_tokens) // ps  # pages [.., upto) are out of the window
+        start = max(sink, r.evict_from)
+        if upto <= start:
+            return
+        gone = [p for p in r.pages[start:upto] if p >= 0]
+        for b in range(start, upto):
+            r.pages[b] = -1
+        self.blocks.release(gone)
+        r.evicted_tokens += len(gone) * ps
+        r.evict_from = upto
+        self.stats.evicted_pages += len(gone)
 
     def _emit(self, r: Request, new: list[int], now: float) -> RequestOutput:
         """Append tokens to a request (stopping early at a stop condition)."""

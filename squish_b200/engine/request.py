@@ -33,18 +33,34 @@ class Request:
     prefix_hit_tokens: int = 0
     preemptions: int = 0
     rng_step: int = 0
+    prompt_key: bytes | None = None  # key of the prompt in the engine's prompt-logit cache
+    # attention window (sink pages + recent window): pages given back are -1 in `pages`; the
+    # attention kernels see only the kept pages, in order, so their token count is
+    # total - evicted_tokens
+    evicted_tokens: int = 0
+    evict_from: int = 0  # first page index not yet checked for eviction
     # cached int32 copy of `pages` for the step's block table (valid while `_bt_src is pages`
     # and the length matches: pages only ever grow by append or are replaced by a new list)
     _bt_src: list | None = field(default=None, repr=False)
     _bt_arr: object = field(default=None, repr=False)
+    _bt_n: int = field(default=-1, repr=False)
+    _bt_ev: int = field(default=0, repr=False)
 
     def page_array(self):
+        """int32 array of the kept pages (the block table row the attention kernels read)."""
         import numpy as np
 
-        if self._bt_src is not self.pages or len(self._bt_arr) != len(self.pages):
-            self._bt_src = self.pages
-            self._bt_arr = np.asarray(self.pages, dtype=np.int32)
+        if self._bt_src is not self.pages or self._bt_n != len(self.pages) or self._bt_ev != self.evicted_tokens:
+            self._bt_src, self._bt_n, self._bt_ev = self.pages, len(self.pages), self.evicted_tokens
+            arr = np.asarray(self.pages, dtype=np.int32)
+            self._bt_arr = arr[arr >= 0] if self.evicted_tokens else arr
         return self._bt_arr
+
+    def logical_pages(self):
+        """int32 array of every page position (-1 where evicted): slot = pages[pos // ps]."""
+        import numpy as np
+
+        return np.asarray(self.pages, dtype=np.int32) if self.evicted_tokens else self.page_array()
 
     def token_at(self, i: int) -> int:
         P = len(self.prompt)

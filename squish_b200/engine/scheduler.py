@@ -87,6 +87,7 @@ class Scheduler:
         self.blocks.release(victim.pages)
         victim.pages = []
         victim.num_computed = 0
+        victim.evicted_tokens = victim.evict_from = 0
         victim.registered_blocks = 0
         victim.chain_hash = None
         victim.status = Status.WAITING

@@ -140,6 +140,8 @@ class BlockManager:
 
     def release(self, pages: list[int]) -> None:
         for p in pages:
+            if p < 0:  # a page the sequence already gave back (evicted from its attention window)
+                continue
             self.ref[p] -= 1
             if self.ref[p] == 0:
                 if p in self.page_hash:
@@ -197,7 +199,7 @@ class BlockManager:
             blk = np.asarray(tokens[b * ps:(b + 1) * ps], dtype=np.int32)
             h = hashlib.sha256(prev + blk.tobytes()).digest()
             p = pages[b]
-            if h not in self.hash_to_page:
+            if p >= 0 and h not in self.hash_to_page:  # (an evicted page has no content to share)
                 self.hash_to_page[h] = p
                 self.page_hash[p] = h
             prev = h

@@ -84,6 +84,7 @@ class QuantConfig:
     kv_group: int = 32
     page_size: int = 16
     mse_clip: bool = False
+    kv_hadamard: bool = False  # KV stored Hadamard-rotated (ops.kernels.kv_hadamard_signs)
 
 
 PRESETS: dict[str, tuple[ModelConfig, QuantConfig]] = {}

@@ -258,6 +258,11 @@ class CudaRunner:
         self.cos_sin = rope_table(cfg, max(max_model_len, 16) + 1).to(dev)
         self.pools = pools or KVPools(cfg, self.qcfg, num_pages, dev)
         self.sm_scale = 1.0 / math.sqrt(cfg.head_dim)
+        self.had_k = self.had_v = self.had_v_row = None
+        if getattr(self.qcfg, "kv_hadamard", False):
+            sk, sv = ops.kernels.kv_hadamard_signs(cfg.head_dim)
+            self.had_k, self.had_v = sk.to(dev), sv.to(dev)
+            self.had_v_row = sv.repeat(cfg.num_heads).to(dev)  # un-rotation of the [T, Hq * D] output
         self._alloc_buffers()
 
     # ------------------------------------------------------------------ buffers
@@ -400,7 +405,8 @@ class CudaRunner:
         kc, ks, vc, vs = self.pools.layers[li]
         q = self.q[:T]
         ops.rope_kv_write(qkv, m["pos"], self.cos_sin, q, m["slots"], kc, ks, vc, vs, hq, hkv, d, ps, grp,
-                          self.fk, self.fv, lw.q_norm, lw.k_norm, cfg.rms_eps, ws=ws)
+                          self.fk, self.fv, lw.q_norm, lw.k_norm, cfg.rms_eps, ws=ws, had_k=self.had_k,
+                          had_v=self.had_v)
         attn = self.attn[:T]
         if Bd:
             ops.paged_decode_attention(q[:Bd], kc, ks, vc, vs, bt[:Bd], m["dlens"], attn[:Bd], hq, hkv, d, ps, grp,
@@ -410,6 +416,8 @@ class CudaRunner:
             ops.paged_prefill_attention(q[Bd:], kc, ks, vc, vs, bt[Bd:], m["tseq"], m["tq0"], m["qs"], m["ql"],
                                         m["ctx"], st.tile_seq.shape[0], attn[Bd:], hq, hkv, d, ps, grp, self.fk,
                                         self.fv, self.sm_scale, tree_mask=tm, ws=ws)
+        if self.had_v_row is not None:  # values were stored rotated: o = H (s_v * o_rot) / sqrt(D)
+            native().hadamard_rows(attn, self.had_v_row, d, attn)
         return attn
 
     # hooks overridden by the tensor-parallel runner
@@ -433,6 +441,27 @@ class CudaRunner:
                        rep_penalty=m["rep"], hist=m.get("hist"), allow_mask=m.get("mask"), seed=st.seed,
                        step=m["step"], ws=self.ws)
         return out
+
+    def logit_row(self, i: int) -> torch.Tensor:
+        """The logits row the last step sampled its i-th token from."""
+        return self.logits[i]
+
+    @torch.inference_mode()
+    def sample_row(self, row: torch.Tensor, temperature: float, top_p: float, top_k: int, min_p: float,
+                   rep_penalty: float, hist: np.ndarray | None, seed: int, step: int) -> int:
+        """Sample one token from a stored logits row with the step sampler's semantics."""
+        out = self.tokens[-1:]
+        lg = row[None]
+        if temperature <= 0 and hist is None:
+            ops.sample(lg, out, ws=self.ws)
+        else:
+            dev = self.device
+            f32 = lambda v: torch.tensor([v], dtype=torch.float32, device=dev)  # noqa: E731
+            i32 = lambda v: torch.tensor([v], dtype=torch.int32, device=dev)  # noqa: E731
+            h = None if hist is None else torch.from_numpy(hist).to(dev)
+            ops.sample(lg, out, temperature=f32(temperature), top_p=f32(top_p), top_k=i32(top_k), min_p=f32(min_p),
+                       rep_penalty=f32(rep_penalty), hist=h, seed=seed, step=i32(step), ws=self.ws)
+        return int(out.item())
 
     def sample_full(self, st: StepInputs, m: dict, logits: torch.Tensor) -> torch.Tensor:
         """The sampler with every per-row parameter bound (no host-side branching: graph-safe)."""
@@ -566,7 +595,7 @@ class TorchPagedRunner:
             if cfg.qk_norm:
                 qv = _rms(qv, w[p + "self_attn.q_norm.weight"], cfg.rms_eps)
                 kv = _rms(kv, w[p + "self_attn.k_norm.weight"], cfg.rms_eps)
-            qv, kv = _rope(qv, cs), _rope(kv, cs)
+            qv, kv, vv = self.ref.rotate_kv(_rope(qv, cs), _rope(kv, cs), vv)
             kq = self.ref._kv_roundtrip(kv, self.ref.fk)
             vq = self.ref._kv_roundtrip(vv, self.ref.fv)
             valid = slots >= 0
@@ -593,7 +622,8 @@ class TorchPagedRunner:
                                 if not (tm >> j) & 1:
                                     bad[i, ctx - n + j] = True
                 s = s.masked_fill(bad[None], float("-inf"))
-                attn[r0:r0 + n] = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), V).reshape(n, hq * d)
+                o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), V)
+                attn[r0:r0 + n] = self.ref.unrotate_out(o).reshape(n, hq * d)
             h = h + self.ref._rp(attn, w[p + "self_attn.o_proj.weight"])
             x = _rms(h, w[p + "post_attention_layernorm.weight"], cfg.rms_eps)
             h = h + self.ref._mlp(p, x)
@@ -625,28 +655,40 @@ class TorchPagedRunner:
                 self.last_preds = vl.argmax(-1).numpy().astype(np.int32)
         out = np.empty(nS, dtype=np.int32)
         for i in range(nS):
-            lg = logits[i].clone()
-            if st.allow_mask is not None:
-                bits = np.unpackbits(st.allow_mask[i].view(np.uint8), bitorder="little")[: lg.shape[0]]
-                lg[torch.from_numpy(bits == 0)] = float("-inf")
-            if st.hist is not None and st.rep_penalty[i] != 1.0:
-                ids_ = [t for t in st.hist[i].tolist() if t >= 0]
-                for t in set(ids_):
-                    lg[t] = lg[t] / st.rep_penalty[i] if lg[t] > 0 else lg[t] * st.rep_penalty[i]
-            if st.temperature[i] <= 0:
-                out[i] = int(lg.argmax())
-            else:
-                g = torch.Generator().manual_seed(int(st.seed) * 1000003 + int(st.rng_step[i]))
-                pr = torch.softmax(lg / float(st.temperature[i]), -1)
-                if st.top_k[i] > 0:
-                    kth = pr.topk(int(st.top_k[i])).values[-1]
-                    pr = torch.where(pr >= kth, pr, torch.zeros_like(pr))
-                if st.top_p[i] < 1.0:
-                    sp, si = pr.sort(descending=True)
-                    cum = sp.cumsum(0)
-                    cut = int((cum < st.top_p[i]).sum()) + 1
-                    keep = torch.zeros_like(pr)
-                    keep[si[:cut]] = pr[si[:cut]]
-                    pr = keep
-                out[i] = int(torch.multinomial(pr / pr.sum(), 1, generator=g))
+            out[i] = self._sample(logits[i], None if st.allow_mask is None else st.allow_mask[i],
+                                  float(st.temperature[i]), float(st.top_p[i]), int(st.top_k[i]),
+                                  float(st.rep_penalty[i]), None if st.hist is None else st.hist[i], int(st.seed),
+                                  int(st.rng_step[i]))
         return out
+
+    @staticmethod
+    def _sample(row, mask, temperature, top_p, top_k, rep_penalty, hist, seed, step) -> int:
+        lg = row.clone()
+        if mask is not None:
+            bits = np.unpackbits(mask.view(np.uint8), bitorder="little")[: lg.shape[0]]
+            lg[torch.from_numpy(bits == 0)] = float("-inf")
+        if hist is not None and rep_penalty != 1.0:
+            for t in set(t for t in hist.tolist() if t >= 0):
+                lg[t] = lg[t] / rep_penalty if lg[t] > 0 else lg[t] * rep_penalty
+        if temperature <= 0:
+            return int(lg.argmax())
+        g = torch.Generator().manual_seed(seed * 1000003 + step)
+        pr = torch.softmax(lg / temperature, -1)
+        if top_k > 0:
+            kth = pr.topk(top_k).values[-1]
+            pr = torch.where(pr >= kth, pr, torch.zeros_like(pr))
+        if top_p < 1.0:
+            sp, si = pr.sort(descending=True)
+            cum = sp.cumsum(0)
+            cut = int((cum < top_p).sum()) + 1
+            keep = torch.zeros_like(pr)
+            keep[si[:cut]] = pr[si[:cut]]
+            pr = keep
+        return int(torch.multinomial(pr / pr.sum(), 1, generator=g))
+
+    def logit_row(self, i: int) -> torch.Tensor:
+        return self.last_logits[i]
+
+    def sample_row(self, row, temperature, top_p, top_k, min_p, rep_penalty, hist, seed, step) -> int:
+        return self._sample(row, None, temperature, top_p, top_k, rep_penalty, None if hist is None else hist[0],
+                            seed, step)

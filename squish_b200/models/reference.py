@@ -63,6 +63,9 @@ class ReferenceModel:
     (dense MLP layers)."""
 
     tap = None
+    # optional attention restriction: kv_visible(qpos [t, 1], kpos [1, n]) -> bool [t, n]
+    # (e.g. the serving engine's sink + recent-window eviction); causality is always applied
+    kv_visible = None
 
     def __init__(self, ck: Checkpoint, device: str | torch.device = "cpu", bf16_storage: bool = False):
         self.bf16_storage = bf16_storage
@@ -73,6 +76,12 @@ class ReferenceModel:
         self.w = {k: v.dequantize().float().to(self.device) for k, v in ck.tensors.items()}
         self.cos_sin = rope_table(cfg, min(cfg.max_position, 8192)).to(self.device)
         self.fk, self.fv = KV_FORMATS[self.q.kv_dtype]
+        self.had = None
+        if getattr(self.q, "kv_hadamard", False):
+            from ..ops.kernels import kv_hadamard_signs, sylvester
+
+            sk, sv = kv_hadamard_signs(cfg.head_dim)
+            self.had = (sk.to(self.device), sv.to(self.device), sylvester(cfg.head_dim).float().to(self.device))
 
     def _kv_roundtrip(self, x: torch.Tensor, fmt: int) -> torch.Tensor:
         """[T, Hkv, D] -> through the KV page codec and back."""
@@ -81,6 +90,20 @@ class ReferenceModel:
         t, h, d = x.shape
         codes, scales = native().cpu.kv_quantize(x.reshape(t * h, d).cpu().contiguous(), fmt, self.q.kv_group)
         return native().cpu.kv_dequantize(codes, scales, fmt, self.q.kv_group, d).reshape(t, h, d).to(x.device)
+
+    def rotate_kv(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+        """Hadamard-rotated KV: q, k -> H (s_k * x), v -> s_v * (H v) (identity when off)."""
+        if self.had is None:
+            return q, k, v
+        sk, sv, H = self.had
+        return (q * sk) @ H, (k * sk) @ H, (v @ H) * sv
+
+    def unrotate_out(self, a: torch.Tensor) -> torch.Tensor:
+        """Attention output over rotated values [.., D] -> H (s_v * a)."""
+        if self.had is None:
+            return a
+        sk, sv, H = self.had
+        return (a * sv) @ H
 
     def _st(self, x: torch.Tensor) -> torch.Tensor:
         """A tensor the device stores in bf16 (identity in the plain fp32 mode)."""
@@ -156,7 +179,8 @@ class ReferenceModel:
             if cfg.qk_norm:
                 q = _rms(q, w[p + "self_attn.q_norm.weight"], cfg.rms_eps)
                 k = _rms(k, w[p + "self_attn.k_norm.weight"], cfg.rms_eps)
-            q, k = self._st(_rope(q, cs)), _rope(k, cs)
+            q, k, v = self.rotate_kv(_rope(q, cs), _rope(k, cs), v)
+            q = self._st(q)
             c = cache[i]
             c["k"] = torch.cat([c["k"], self._kv_roundtrip(k, self.fk)])
             c["v"] = torch.cat([c["v"], self._kv_roundtrip(v, self.fv)])
@@ -165,7 +189,12 @@ class ReferenceModel:
             s = torch.einsum("qhd,khd->hqk", q, kk) / math.sqrt(d)
             kpos = torch.arange(kk.shape[0], device=dev)
             s = s.masked_fill(kpos[None, None, :] > pos[None, :, None], float("-inf"))
-            a = self._st(torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vv).reshape(t, hq * d))
+            if self.kv_visible is not None:
+                s = s.masked_fill(~self.kv_visible(pos[:, None], kpos[None, :])[None], float("-inf"))
+            a = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vv)
+            if self.had is not None:
+                a = self.unrotate_out(self._st(a))
+            a = self._st(a.reshape(t, hq * d))
             if self.tap is not None:
                 self.tap(p + "self_attn.o_proj", a)
             h = self._st(h + a @ w[p + "self_attn.o_proj.weight"].T)

@@ -11,6 +11,7 @@ import math
 import os
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from .._ext import native
@@ -370,12 +371,34 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor
 
 def rope_kv_write(qkv, positions, cos_sin, q_out, slot_mapping, k_codes, k_scales, v_codes, v_scales,
                   hq: int, hkv: int, d: int, page_size: int, group: int, fmt_k: int, fmt_v: int,
-                  q_norm=None, k_norm=None, norm_eps: float = 1e-6, ws: Workspace | None = None) -> None:
-    """A slot past the pools is not written; it records SQ_ERR_BOUNDS in the workspace status."""
+                  q_norm=None, k_norm=None, norm_eps: float = 1e-6, ws: Workspace | None = None,
+                  had_k=None, had_v=None) -> None:
+    """A slot past the pools is not written; it records SQ_ERR_BOUNDS in the workspace status.
+    With ``had_k`` / ``had_v`` (+-1 signs [d], :func:`kv_hadamard_signs`) q and k are written as
+    H (s_k * x) / sqrt(d) and v as s_v * (H v) / sqrt(d)."""
     ws = ws or workspace(qkv.device)
     native().rope_kv_write(qkv, positions, cos_sin, q_out, slot_mapping, k_codes, k_scales, v_codes, v_scales,
-                           hq, hkv, d, page_size, group, fmt_k, fmt_v, q_norm, k_norm, float(norm_eps), ws.status)
+                           hq, hkv, d, page_size, group, fmt_k, fmt_v, q_norm, k_norm, float(norm_eps), ws.status,
+                           had_k, had_v)
     _count()
+
+
+def kv_hadamard_signs(d: int, seed: int = 0x4B56) -> tuple[torch.Tensor, torch.Tensor]:
+    """The +-1 sign vectors (s_k, s_v), float32 [d], of the Hadamard-rotated KV cache: a fixed
+    function of (d, seed), so every rank, the oracle and a restarted server agree. Randomized
+    Hadamard rotation of K and V before quantization, as the reference's HadamardKVCache
+    (squish/kv/kv_cache.py:2769-2860), with separate signs for K and V."""
+    g = np.random.default_rng(seed + d)
+    s = np.where(g.random((2, d)) < 0.5, -1.0, 1.0).astype(np.float32)
+    return torch.from_numpy(s[0].copy()), torch.from_numpy(s[1].copy())
+
+
+def sylvester(d: int) -> torch.Tensor:
+    """Sylvester-ordered Hadamard matrix H_d / sqrt(d) (symmetric, orthonormal), float64."""
+    h = torch.ones(1, 1, dtype=torch.float64)
+    while h.shape[0] < d:
+        h = torch.cat([torch.cat([h, h], 1), torch.cat([h, -h], 1)], 0)
+    return h / math.sqrt(d)
 
 
 MAX_DECODE_SPLITS = 64

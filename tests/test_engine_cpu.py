@@ -74,3 +74,102 @@ def test_sampling_params_and_stop(tiny):
     assert stop == first[: first.index(tok) + 1]
     with pytest.raises(ValueError):
         SamplingParams(top_p=0.0).validate()
+
+
+def test_repeat_prompt_first_token_without_forward(tiny):
+    """A repeated prompt gets its first token from the prompt-logit cache (no step runs for
+    it), and the rest of the output is the same as the first time (greedy and sampled)."""
+    p = _prompt(31, 37)
+    eng = LLMEngine.from_checkpoint(tiny, "cpu", EngineConfig(max_num_seqs=4, max_num_batched_tokens=64,
+                                                              max_model_len=256, num_pages=64))
+    for params in (SamplingParams(max_tokens=8, ignore_eos=True),
+                   SamplingParams(max_tokens=8, ignore_eos=True, temperature=0.8, top_k=50, repetition_penalty=1.2)):
+        rid1 = eng.add_request(p, params)
+        while eng.has_unfinished():
+            eng.step()
+        first = eng.requests[rid1].output
+        n0, steps0 = eng.stats.instant_first_tokens, eng.stats.steps
+        rid2 = eng.add_request(p, params, rid=rid1 + "-again")
+        assert eng.stats.instant_first_tokens == n0 + 1
+        r2 = eng.requests[rid2]
+        assert len(r2.output) == 1 and r2.first_token_time is not None  # before any step
+        outs = eng.step()
+        assert outs[0].rid == rid2 and outs[0].new_tokens == r2.output[:1]
+        while eng.has_unfinished():
+            eng.step()
+        if params.temperature == 0:
+            assert r2.output == first
+        assert len(r2.output) == 8 and eng.stats.steps > steps0
+    # a one-token request finishes at add time, and the engine reports it on the next step
+    rid3 = eng.add_request(p, SamplingParams(max_tokens=1, ignore_eos=True))
+    r3 = eng.requests[rid3]
+    assert r3.finish_reason == "length" and eng.has_unfinished()
+    assert [o.rid for o in eng.step()] == [rid3] and not eng.has_unfinished()
+
+
+def window_rule(sink_tokens, window, ps=16):
+    """Keys the engine's page-granular sink + window eviction leaves visible to query q: after the
+    step that made num_computed = q, pages [ceil(sink / ps), (q - window) // ps) are gone."""
+    sink = -(-sink_tokens // ps)
+
+    def visible(q, k):
+        page = k // ps
+        return (page < sink) | (page >= torch.div(q - window, ps, rounding_mode="floor"))
+    return visible
+
+
+def test_sink_and_window_eviction_matches_windowed_oracle(tiny):
+    p = _prompt(33, 40)
+    eng = LLMEngine.from_checkpoint(tiny, "cpu", EngineConfig(max_num_seqs=2, max_num_batched_tokens=64,
+                                                              max_model_len=256, num_pages=64, kv_sink_tokens=4,
+                                                              kv_window_tokens=32))
+    got = eng.generate([p], SamplingParams(max_tokens=70, ignore_eos=True))[0]
+    # the last step computes position 108 (109 tokens): pages [1, (109 - 32) // 16 = 4) were given
+    # back; page 0 holds the sinks
+    assert eng.stats.evicted_pages == 3
+    ref = ReferenceModel(tiny)
+    ref.kv_visible = window_rule(4, 32)
+    assert got == ref.greedy(p, 70)[0]
+    # logits of the last step: equal to the windowed oracle's, and not to full attention's
+    seq = p + got[:-1]
+    win = ref.forward(seq, ref.new_cache(), 0)[-1]
+    full_ref = ReferenceModel(tiny)
+    full = full_ref.forward(seq, full_ref.new_cache(), 0)[-1]
+    last = eng.runner.last_logits[0]
+    assert torch.allclose(last, win, atol=1e-4, rtol=1e-4)
+    assert (last - full).abs().max() > 100 * (last - win).abs().max()
+
+
+def test_hadamard_rotated_kv_keeps_the_model_and_cuts_kv_error(tiny):
+    """Rotating q/k/v by a randomized Hadamard transform before the KV codec leaves the model
+    unchanged up to quantization (scores and outputs are rotation invariant) and, for INT4 KV
+    with outlier channels, lowers the cache's reconstruction error."""
+    import dataclasses
+
+    from squish_b200.ops.kernels import sylvester
+
+    d = tiny.config.head_dim
+    H = sylvester(d).float()
+    assert torch.allclose(H @ H, torch.eye(d), atol=1e-6)
+    ck_rot = dataclasses.replace(tiny, quant=dataclasses.replace(tiny.quant, kv_dtype="bf16", kv_hadamard=True))
+    ck_bf = dataclasses.replace(tiny, quant=dataclasses.replace(tiny.quant, kv_dtype="bf16"))
+    p = _prompt(34, 30)
+    a, b = ReferenceModel(ck_rot), ReferenceModel(ck_bf)
+    la, lb = a.forward(p, a.new_cache(), 0), b.forward(p, b.new_cache(), 0)
+    assert torch.nn.functional.cosine_similarity(la[-1], lb[-1], dim=0) > 0.9999
+    # INT4 reconstruction error on keys with outlier channels, with and without rotation
+    g = torch.Generator().manual_seed(0)
+    k = torch.randn(256, 1, d, generator=g)
+    k[..., 3] *= 20.0
+    k[..., d - 7] *= 12.0
+    m_rot = ReferenceModel(dataclasses.replace(tiny, quant=dataclasses.replace(tiny.quant, kv_hadamard=True)))
+    m_plain = ReferenceModel(tiny)
+    _, kr, _ = m_rot.rotate_kv(k, k, k)
+    err_rot = (m_rot._kv_roundtrip(kr, m_rot.fk) - kr).pow(2).mean()
+    err_plain = (m_plain._kv_roundtrip(k, m_plain.fk) - k).pow(2).mean()
+    assert err_rot < 0.5 * err_plain
+    # the engine on the CPU runner with rotated INT4 KV matches the rotated oracle exactly
+    ck4 = dataclasses.replace(tiny, quant=dataclasses.replace(tiny.quant, kv_hadamard=True))
+    eng = LLMEngine.from_checkpoint(ck4, "cpu", EngineConfig(max_num_seqs=2, max_num_batched_tokens=64,
+                                                             max_model_len=256, num_pages=32))
+    assert eng.generate([p], SamplingParams(max_tokens=10, ignore_eos=True))[0] == ReferenceModel(ck4).greedy(p, 10)[0]

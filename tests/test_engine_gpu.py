@@ -25,7 +25,9 @@ def _configs():
     qwen3 = ModelConfig("tiny-qwen3", "qwen3", 1000, 512, 2, 8, 2, 128, 768, 1e-6, 1e6, qk_norm=True,
                         max_position=4096)
     return [(tiny, tq), (qwen2, QuantConfig(4, 64, True, "int4", 32, 16)),
-            (qwen3, QuantConfig(4, 64, True, "k8v4", 64, 16)), (tiny, dataclasses.replace(tq, kv_dtype="bf16"))]
+            (qwen3, QuantConfig(4, 64, True, "k8v4", 64, 16)), (tiny, dataclasses.replace(tq, kv_dtype="bf16")),
+            (tiny, dataclasses.replace(tq, kv_hadamard=True)),  # Hadamard-rotated KV, D = 32 and 128
+            (qwen3, QuantConfig(4, 64, True, "int4", 32, 16, kv_hadamard=True))]
 
 
 def _teacher_forced_ok(ref, prompt, got, tol=0.04):
@@ -55,7 +57,7 @@ def _as_stored(ck):
     return ck
 
 
-@pytest.mark.parametrize("idx", range(4))
+@pytest.mark.parametrize("idx", range(6))
 def test_cuda_engine_matches_cpu_oracle(cuda, idx):
     cfg, q = _configs()[idx]
     ck_cpu = _as_stored(random_checkpoint(cfg, q, seed=0, device="cpu"))
@@ -105,6 +107,52 @@ def test_graphs_match_eager(cuda):
         if graphs:
             assert eng.graphs.graphs, "decode steps should have run through CUDA graphs"
     assert outs[0] == outs[1]
+
+
+def test_repeat_prompt_first_token_from_logit_cache(cuda):
+    """A repeated prompt's first token is sampled from the stored bf16 logits row by the CUDA
+    sampler before any forward; it equals the first run's, and sampled runs stay valid."""
+    cfg, q = get_preset("tiny-llama")
+    eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
+                                    EngineConfig(max_num_seqs=4, max_model_len=256, num_pages=64))
+    p = _prompt(41, 45, cfg.vocab_size)
+    first = eng.generate([p], SamplingParams(max_tokens=12, ignore_eos=True))[0]
+    steps = eng.stats.steps
+    rid = eng.add_request(p, SamplingParams(max_tokens=12, ignore_eos=True))
+    assert eng.stats.instant_first_tokens == 1 and eng.stats.steps == steps
+    assert eng.step()[0].new_tokens == first[:1]
+    while eng.has_unfinished():
+        eng.step()
+    # the rest is computed by prefill over the uncached tail instead of decode steps: the same
+    # model through a different kernel, so only the cached first token must match exactly
+    got = eng.requests[rid].output
+    assert got[0] == first[0] and len(got) == 12
+    ok, worst = _teacher_forced_ok(ReferenceModel(random_checkpoint(cfg, q, seed=0, device="cpu")), p, got)
+    assert ok, (worst, got)
+    sp = SamplingParams(max_tokens=6, temperature=0.9, top_p=0.9, top_k=40, repetition_penalty=1.1, ignore_eos=True)
+    out = eng.generate([p], sp)[0]
+    assert eng.stats.instant_first_tokens == 2 and len(out) == 6 and all(0 <= t < cfg.vocab_size for t in out)
+    eng.runner.ws.check()
+
+
+def test_sink_window_eviction_on_the_cuda_engine(cuda):
+    """Sink + recent-window eviction through the CUDA kernels (decode graphs included): the
+    kept pages are compacted into the block table; every token is the windowed oracle's choice
+    (teacher forced), and the pages went back to the pool."""
+    from tests.test_engine_cpu import window_rule
+
+    cfg, q = get_preset("tiny-llama")
+    eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
+                                    EngineConfig(max_num_seqs=4, max_model_len=512, num_pages=64, kv_sink_tokens=4,
+                                                 kv_window_tokens=48))
+    p = _prompt(42, 50, cfg.vocab_size)
+    got = eng.generate([p], SamplingParams(max_tokens=120, ignore_eos=True))[0]
+    assert eng.stats.evicted_pages == (169 - 48) // 16 - 1 and eng.stats.graph_steps > 0
+    ref = ReferenceModel(_as_stored(random_checkpoint(cfg, q, seed=0, device="cpu")), bf16_storage=True)
+    ref.kv_visible = window_rule(4, 48)
+    ok, worst = _teacher_forced_ok(ref, p, got)
+    assert ok, (worst, got)
+    eng.runner.ws.check()
 
 
 def test_sampled_decoding_runs_in_graphs(cuda):

@@ -49,6 +49,9 @@ def test_flags_build_the_engine_config():
         _parallel(_args("--gpus", "6", "--tp", "4"))
     e = _ecfg(_args("--tp", "2", "--tp-mode", "nccl"))
     assert (e.tp, e.tp_mode) == (2, "nccl")
+    e = _ecfg(_args("--kv-sink-tokens", "4", "--kv-window-tokens", "256", "--prompt-logit-cache", "0"))
+    assert (e.kv_sink_tokens, e.kv_window_tokens, e.prompt_logit_cache) == (4, 256, 0)
+    assert _ecfg(_args()).prompt_logit_cache > 0
 
 
 def _client(*extra):
