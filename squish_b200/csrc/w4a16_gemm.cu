@@ -345,6 +345,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
   const int kb0 = split * p.kb_per_split;
   const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
   const int nkb = max(0, kb1 - kb0);
+  const int krot = (p.krot != 0 && nkb > 0) ? (int)((nblk * 7u + mblk * 3u) % (unsigned)nkb) : 0;
   int* status = p.status;
 
   if (threadIdx.x == 0) {
@@ -397,7 +398,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       if (elect_one()) {
         uint8_t* dst = w_ring + r.s * L.w_stage;
         mbar_expect_tx(&w_full[r.s], L.w_stage);
-        const int kb = kb0 + i;
+        const int kb = kb0 + (i + krot) % nkb;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
           const size_t tile = ((size_t)nblk * NT + t) * p.kb_total + kb;
@@ -430,7 +431,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       if (!mbar_wait(&x_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_X)) break;
       if (elect_one()) {
         mbar_expect_tx(&x_full[r.s], C::kXBytes);
-        tma_load_2d(x_ring + r.s * C::kXBytes, &xmap, (kb0 + i) * BK, mblk * BN, &x_full[r.s]);
+        tma_load_2d(x_ring + r.s * C::kXBytes, &xmap, (kb0 + (i + krot) % nkb) * BK, mblk * BN, &x_full[r.s]);
         trace_mark(str, 1, i);
       }
       __syncwarp();
@@ -871,20 +872,30 @@ cudaError_t launch_decode_narrow(const CUtensorMap& xmap, const W4A16Params& p, 
     const char* e = std::getenv("SQ_GEMM_ASMEM");
     return e != nullptr && e[0] == '1';
   }();
+  static const int rx_env = [] {  // experiment: activation ring depth of the two-CTA configuration
+    const char* e = std::getenv("SQ_GEMM_RX");
+    return e != nullptr ? std::atoi(e) : 0;
+  }();
   if (asmem) {
     constexpr int rx = BN >= 32 ? 4 : 6;
     if (per_sm <= 2) return launch_cfg<Cfg<BN, 1, 2, 4, true>>(xmap, p, fit2(rx, 2, 113 * 1024, 3, 16), rx, 2, s);
     return launch_cfg<Cfg<BN, 1, 4, 4, true>>(xmap, p, fit2(3, 1, 56 * 1024, 2, 8), 3, 1, s);
   }
   if (per_sm <= 2) {
-    constexpr int rx = BN >= 32 ? 4 : 6;
+    const int rx = rx_env >= 2 && rx_env <= 12 ? rx_env : BN >= 32 ? 4 : 6;
     return launch_cfg<Cfg<BN, 1, 2, 4>>(xmap, p, fit(rx, 4, 113 * 1024, 4, 24), rx, 4, s);
   }
   constexpr int rx = BN == 64 ? 3 : BN == 32 ? 4 : 6;
   return launch_cfg<Cfg<BN, 1, 4, 4>>(xmap, p, fit(rx, 2, 56 * 1024, 3, 12), rx, 2, s);
 }
 
-cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s) {
+cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p0, int bn, int nt, cudaStream_t s) {
+  static const int krot_env = [] {  // experiment: SQ_GEMM_KROT=1 rotates every CTA's k-block order
+    const char* e = std::getenv("SQ_GEMM_KROT");
+    return e != nullptr ? std::atoi(e) : 0;
+  }();
+  W4A16Params p = p0;
+  if (krot_env) p.krot = 1;
   int ow, ox, oa;
   const bool ov = ring_override(&ow, &ox, &oa);
   if (nt == 1) {

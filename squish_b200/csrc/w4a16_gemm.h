@@ -67,6 +67,9 @@ struct W4A16Params {
   int* ag_flags;
   int* ag_done;
   int ag_expect;
+  // k-block order rotation (krot != 0): CTA (x, y) starts its k loop at a CTA-dependent block and
+  // wraps, so the CTAs of one launch do not all read the same activation tile at the same time
+  int krot;
 };
 
 // True when token tiles of <= 64 run the 4-dequant-warp configuration (four CTAs per SM):

@@ -66,6 +66,9 @@ class ReferenceModel:
     # optional attention restriction: kv_visible(qpos [t, 1], kpos [1, n]) -> bool [t, n]
     # (e.g. the serving engine's sink + recent-window eviction); causality is always applied
     kv_visible = None
+    # optional KV override: kv_source(layer, start_pos, t) -> (K, V) [t, Hkv, D] fp32 to append
+    # instead of this model's own codec output (e.g. the device's cache pages, read back), or None
+    kv_source = None
 
     def __init__(self, ck: Checkpoint, device: str | torch.device = "cpu", bf16_storage: bool = False):
         self.bf16_storage = bf16_storage
@@ -182,8 +185,10 @@ class ReferenceModel:
             q, k, v = self.rotate_kv(_rope(q, cs), _rope(k, cs), v)
             q = self._st(q)
             c = cache[i]
-            c["k"] = torch.cat([c["k"], self._kv_roundtrip(k, self.fk)])
-            c["v"] = torch.cat([c["v"], self._kv_roundtrip(v, self.fv)])
+            src = None if self.kv_source is None else self.kv_source(i, start_pos, t)
+            kq, vq = src if src is not None else (self._kv_roundtrip(k, self.fk), self._kv_roundtrip(v, self.fv))
+            c["k"] = torch.cat([c["k"], kq.to(dev)])
+            c["v"] = torch.cat([c["v"], vq.to(dev)])
             kk = c["k"].repeat_interleave(hq // hkv, dim=1)
             vv = c["v"].repeat_interleave(hq // hkv, dim=1)
             s = torch.einsum("qhd,khd->hqk", q, kk) / math.sqrt(d)
