@@ -58,8 +58,9 @@ struct Cfg {
   // Single weight tile per CTA: the dequantized A operand goes to tensor memory (tcgen05.st)
   // instead of shared memory; columns [kA0, kA0 + 32 * ring_a) hold the A ring.
   static constexpr bool AT = (NT == 1) && !ASMEM_;
-  static constexpr int kMaxRingA = MINB_ >= 3 ? 2 : 4;  // 3+ CTAs per SM share 512 TMEM columns
   static constexpr int kA0 = AT ? (NT * BN < 32 ? 32 : NT * BN) : 0;
+  // CTAs per SM share 512 TMEM columns: 3+ -> 2 A stages, 2 -> 4, one CTA -> what is left (<= 12)
+  static constexpr int kMaxRingA = MINB_ >= 3 ? 2 : MINB_ == 2 ? 4 : ((512 - kA0) / 32 < 12 ? (512 - kA0) / 32 : 12);
   static constexpr int kCols = AT ? kA0 + 32 * kMaxRingA : NT * BN;
   static constexpr int kTmemCols = (kCols <= 32) ? 32 : (kCols <= 64) ? 64 : (kCols <= 128) ? 128 : (kCols <= 256) ? 256 : 512;
   // Dequantizing stage i + 1 before stage i's tensor-memory store completes (two register
@@ -876,6 +877,14 @@ cudaError_t launch_decode_narrow(const CUtensorMap& xmap, const W4A16Params& p, 
     const char* e = std::getenv("SQ_GEMM_RX");
     return e != nullptr ? std::atoi(e) : 0;
   }();
+  static const int one_ra = [] {  // experiment: one CTA per SM, 8 dequant warps, this many A stages
+    const char* e = std::getenv("SQ_GEMM_ONE");
+    return e != nullptr ? std::atoi(e) : 0;
+  }();
+  if (one_ra >= 2 && one_ra <= Cfg<BN, 1, 1, 8>::kMaxRingA) {
+    const int rx = rx_env >= 2 && rx_env <= 16 ? rx_env : 8;
+    return launch_cfg<Cfg<BN, 1, 1, 8>>(xmap, p, fit(rx, one_ra, 226 * 1024, 4, 40), rx, one_ra, s);
+  }
   if (asmem) {
     constexpr int rx = BN >= 32 ? 4 : 6;
     if (per_sm <= 2) return launch_cfg<Cfg<BN, 1, 2, 4, true>>(xmap, p, fit2(rx, 2, 113 * 1024, 3, 16), rx, 2, s);
