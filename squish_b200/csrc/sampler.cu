@@ -9,11 +9,10 @@
 // with its token bitmask (squish/grammar/grammar_engine.py:220-254).
 //
 // Instead of sorting the vocabulary, every filter becomes a logit threshold:
-//   min-p: tau_m = max + log(min_p);  top-k: tau_k = k-th largest logit;  top-p: the last logit
-//   of the shortest sorted head whose mass reaches top_p. Both are exact radix selections on
-//   the order-preserving bit pattern (8 passes of 4 bits, weighted by 1 or by exp(x - max)).
-//   The draw is Gumbel-max over the kept set, which samples exactly from the renormalised
-//   distribution. Temperature <= 0 means greedy (argmax).
+//   min-p: tau_m = max + log(min_p);  top-k: tau_k = k-th largest logit (4-pass radix
+//   select on the order-preserving bit pattern); top-p: bisection on tau for the mass of
+//   kept tokens above tau. The draw is Gumbel-max over the kept set, which samples exactly
+//   from the renormalised distribution. Temperature <= 0 means greedy (argmax).
 #include "kernels.h"
 #include "launch.cuh"
 
@@ -58,83 +57,6 @@ __device__ T block_reduce(T v, Op op, T* sh) {
   return sh[0];
 }
 
-__device__ __forceinline__ float ord2f(uint32_t k) {
-  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
-}
-
-struct RadixSmem {
-  float part[32][16];  // per-warp bin sums
-  float tot[16];
-  float above;
-  uint32_t prefix;
-};
-
-// Largest order key T such that the weight of the elements with key >= T (among keys >= lo) is
-// at least `target`; weight 1 per element (counting: the k-th largest) or exp(x - xmax) (mass).
-// Radix descent 4 bits per pass from the top: each thread sums its elements into 16 bin
-// registers (no shared-memory atomics, so no contention when the logits crowd a few bins), the
-// block adds the bins, and the bin where the running weight from the top reaches the target
-// extends the prefix. If the candidates weigh less than the target, every one is kept (T = the
-// smallest key present).
-template <bool kMass>
-__device__ uint32_t radix_select(const float* __restrict__ x, int V, uint32_t lo, float target, float xmax,
-                                 RadixSmem& rs) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (threadIdx.x == 0) {
-    rs.prefix = 0u;
-    rs.above = 0.f;
-  }
-  __syncthreads();
-  uint32_t prefix = 0u, pmask = 0u;
-  for (int shift = 28; shift >= 0; shift -= 4) {
-    float acc[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-#pragma unroll 4
-    for (int i = threadIdx.x; i < V; i += kThreads) {
-      const float v = x[i];
-      const uint32_t key = f2ord(v);
-      if (key >= lo && (key & pmask) == prefix) {
-        const uint32_t b = (key >> shift) & 15u;
-        const float w = kMass ? __expf(v - xmax) : 1.f;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] += (b == (uint32_t)j) ? w : 0.f;
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) rs.part[warp][j] = acc[j];
-    }
-    __syncthreads();
-    if (threadIdx.x < 16) {
-      float t = 0.f;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += rs.part[w][threadIdx.x];
-      rs.tot[threadIdx.x] = t;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float above = rs.above;
-      int b = 15;
-      for (; b > 0; --b) {
-        if (above + rs.tot[b] >= target) break;
-        above += rs.tot[b];
-      }
-      rs.above = above;
-      rs.prefix = prefix | ((uint32_t)b << shift);
-    }
-    __syncthreads();
-    prefix = rs.prefix;
-    pmask |= 15u << shift;
-    __syncthreads();  // rs is rewritten by the next pass
-  }
-  return prefix;
-}
-
 struct ArgMax {
   float v;
   int i;
@@ -145,7 +67,7 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const SamplerParams p
   pdl_trigger();
   __shared__ float shf[32];
   __shared__ int shi[32];
-  __shared__ RadixSmem rs;
+  __shared__ unsigned int hist[256];
   const int row = blockIdx.x;
   const int V = p.V;
   float* x = work + (size_t)row * V;
@@ -262,11 +184,57 @@ __global__ void __launch_bounds__(kThreads) sampler_kernel(const SamplerParams p
   const float min_p = p.min_p ? p.min_p[row] : 0.f;
   if (min_p > 0.f) tau = fmaxf(tau, xmax + __logf(min_p));
   const int top_k = p.top_k ? p.top_k[row] : 0;
-  if (top_k > 0 && top_k < V) tau = fmaxf(tau, ord2f(radix_select<false>(x, V, f2ord(tau), (float)top_k, xmax, rs)));
+  if (top_k > 0 && top_k < V) {
+    // radix select the k-th largest ordered key, 8 bits per pass from the top
+    uint32_t prefix = 0, pmask = 0;
+    int k = top_k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = threadIdx.x; i < 256; i += kThreads) hist[i] = 0;
+      __syncthreads();
+      for (int i = threadIdx.x; i < V; i += kThreads) {
+        const uint32_t key = f2ord(x[i]);
+        if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 0xFF], 1u);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        int acc = 0, bin = 255;
+        for (; bin > 0; --bin) {
+          if (acc + (int)hist[bin] >= k) break;
+          acc += hist[bin];
+        }
+        shi[0] = bin;
+        shi[1] = k - acc;
+      }
+      __syncthreads();
+      prefix |= (uint32_t)shi[0] << shift;
+      pmask |= 0xFFu << shift;
+      k = shi[1];
+      __syncthreads();
+    }
+    const uint32_t u = (prefix & 0x80000000u) ? (prefix & 0x7FFFFFFFu) : ~prefix;
+    tau = fmaxf(tau, __uint_as_float(u));
+  }
   const float top_p = p.top_p ? p.top_p[row] : 1.f;
-  // the smallest head of the sorted kept logits whose mass (normalised over the full softmax)
-  // reaches top_p: its last key is the threshold
-  if (top_p < 1.f) tau = fmaxf(tau, ord2f(radix_select<true>(x, V, f2ord(tau), top_p * z, xmax, rs)));
+  if (top_p < 1.f) {
+    // largest t with sum_{x_i >= max(t, tau)} p_i >= top_p  (p normalised over the full softmax)
+    float lo = (tau == -INFINITY) ? xmax - 40.f : tau, hi = xmax;
+    auto mass = [&](float t) {
+      float m = 0.f;
+      for (int i = threadIdx.x; i < V; i += kThreads) {
+        const float v = x[i];
+        if (v >= t) m += __expf(v - xmax);
+      }
+      return block_reduce(m, [](float a, float b) { return a + b; }, shf) / z;
+    };
+    if (mass(lo) >= top_p) {
+      for (int it = 0; it < 24; ++it) {
+        const float mid = 0.5f * (lo + hi);
+        if (mass(mid) >= top_p) lo = mid;
+        else hi = mid;
+      }
+      tau = fmaxf(tau, lo);
+    }
+  }
   // Gumbel-max draw over the kept set
   const uint64_t step = p.step ? (uint64_t)p.step[row] : 0ull;
   float best = -INFINITY;

@@ -786,7 +786,7 @@ cudaError_t launch_cfg(const CUtensorMap& xmap, W4A16Params p, int rw, int rx, i
       return cudaErrorInvalidConfiguration;
   }
   const size_t smem = (size_t)L.total + 1024;  // + alignment slack
-  if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
+  if (smem + 512 * sizeof(uint4) > 227 * 1024) return cudaErrorInvalidConfiguration;  // + static fmt_tab
   auto kern = w4a16_gemm_kernel<C>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -883,7 +883,7 @@ cudaError_t launch_decode_narrow(const CUtensorMap& xmap, const W4A16Params& p, 
   }();
   if (one_ra >= 2 && one_ra <= Cfg<BN, 1, 1, 8>::kMaxRingA) {
     const int rx = rx_env >= 2 && rx_env <= 16 ? rx_env : 8;
-    return launch_cfg<Cfg<BN, 1, 1, 8>>(xmap, p, fit(rx, one_ra, 226 * 1024, 4, 40), rx, one_ra, s);
+    return launch_cfg<Cfg<BN, 1, 1, 8>>(xmap, p, fit(rx, one_ra, 216 * 1024, 4, 40), rx, one_ra, s);
   }
   if (asmem) {
     constexpr int rx = BN >= 32 ? 4 : 6;
