@@ -793,6 +793,42 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_codes, torch::Tenso
   CUDA_OK(sq::paged_decode_attn_launch(p, cur_stream()));
 }
 
+// Attention mass per KV page (H2O-style scores), accumulated into mass[num_pages] (float32).
+void page_mass(torch::Tensor q, torch::Tensor k_codes, torch::Tensor k_scales, torch::Tensor block_tables,
+               torch::Tensor seq_lens, torch::Tensor mass, int64_t Hq, int64_t Hkv, int64_t D, int64_t page_size,
+               int64_t group, int64_t fmt_k, double sm_scale, c10::optional<torch::Tensor> status) {
+  CHECK_CUDA(q);
+  CHECK_DT(q, torch::kBFloat16);
+  CHECK_DT(block_tables, torch::kInt32);
+  CHECK_DT(seq_lens, torch::kInt32);
+  CHECK_DT(mass, torch::kFloat32);
+  TORCH_CHECK(q.dim() == 2 && q.stride(1) == 1, "q: [B, Hq * D] with unit column stride");
+  TORCH_CHECK(k_codes.dim() == 4 && mass.numel() >= k_codes.size(0), "mass: one float per page");
+  TORCH_CHECK(block_tables.dim() == 2 && block_tables.stride(1) == 1 && block_tables.size(0) >= seq_lens.size(0),
+              "block_tables: [>= B, pages]");
+  const c10::cuda::CUDAGuard g(q.device());
+  sq::PageMassParams p{};
+  p.q = ptr<__nv_bfloat16>(q);
+  p.ld_q = (int)q.stride(0);
+  p.k_codes = ptr<uint8_t>(k_codes);
+  p.k_scales = reinterpret_cast<const __half*>(k_scales.data_ptr());
+  p.block_tables = ptr<int>(block_tables);
+  p.bt_stride = (int)block_tables.stride(0);
+  p.seq_lens = ptr<int>(seq_lens);
+  p.mass = ptr<float>(mass);
+  p.B = (int)seq_lens.size(0);
+  p.Hq = (int)Hq;
+  p.Hkv = (int)Hkv;
+  p.D = (int)D;
+  p.page_size = (int)page_size;
+  p.group = (int)group;
+  p.fmt_k = (int)fmt_k;
+  p.num_pages = (int)k_codes.size(0);
+  p.sm_scale = (float)sm_scale;
+  p.status = optr<int>(status);
+  CUDA_OK(sq::page_mass_launch(p, cur_stream()));
+}
+
 void paged_prefill_attention(torch::Tensor q, torch::Tensor k_codes, torch::Tensor k_scales, torch::Tensor v_codes,
                              torch::Tensor v_scales, torch::Tensor block_tables, torch::Tensor tile_seq,
                              torch::Tensor tile_q0, torch::Tensor q_start, torch::Tensor q_len, torch::Tensor ctx_len,
@@ -1075,6 +1111,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine);
   m.def("rmsnorm", &rmsnorm);
   m.def("rope_kv_write", &rope_kv_write);
+  m.def("page_mass", &page_mass);
   m.def("paged_decode_attention", &paged_decode_attention);
   m.def("paged_prefill_attention", &paged_prefill_attention);
   m.def("sample", &sample);

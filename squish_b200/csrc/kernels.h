@@ -33,6 +33,24 @@ struct RopeKvParams {
   const float* had_v;
 };
 
+// Attention mass per KV page (kv_score.cu): for every decode row b, the softmax probabilities of
+// its query heads over the row's keys (block table row b, seq_lens[b] keys) summed per page and
+// added to mass[page].
+struct PageMassParams {
+  const __nv_bfloat16* q;  // [B, ld_q] (Hq * D per row)
+  int ld_q;
+  const uint8_t* k_codes;
+  const __half* k_scales;
+  const int* block_tables;  // [B, bt_stride]
+  int bt_stride;
+  const int* seq_lens;      // [B]
+  float* mass;              // [num_pages], accumulated
+  int B, Hq, Hkv, D, page_size, group, fmt_k, num_pages;
+  float sm_scale;
+  int* status;
+};
+cudaError_t page_mass_launch(const PageMassParams& p, cudaStream_t s);
+
 struct AttnParams {
   const __nv_bfloat16* q;  // [rows, ld_q] (Hq*D per row)
   int ld_q;

@@ -65,6 +65,12 @@ class EngineConfig:
     # pool and attention no longer sees them. 0 = full attention.
     kv_sink_tokens: int = 0
     kv_window_tokens: int = 0
+    # heavy-hitter (H2O-style) eviction: keep at most kv_h2o_budget tokens per sequence; when
+    # over, the pages outside the sinks and the recent window with the least accumulated
+    # attention mass go back to the pool. The mass is measured on the device every
+    # kv_h2o_interval decode steps (those steps run outside CUDA graphs). 0 = off.
+    kv_h2o_budget: int = 0
+    kv_h2o_interval: int = 4
 
 
 @dataclass
@@ -176,6 +182,8 @@ class LLMEngine:
         ecfg = ecfg or EngineConfig(**kw)
         dev = torch.device(device)
         if ecfg.tp > 1:
+            if ecfg.kv_h2o_budget > 0:
+                raise ValueError("heavy-hitter KV eviction runs on one GPU per engine (use --dp for more GPUs)")
             return cls._from_checkpoint_tp(ck, dev, ecfg)
         if dev.type == "cuda":
             from ..models.decoder import CudaRunner
@@ -495,13 +503,16 @@ class LLMEngine:
         if self.proposer is not None and sched.decode:
             self._attach_drafts(sched)
         st, samp = self.build_inputs(sched)
+        score = self._h2o_score_step(sched)
+        self.runner.score_step = score
         if (self.graphs is not None and not sched.prefill and st.allow_mask is None and st.num_verify == 0
-                and self.graphs.can_run(st)):
+                and not score and self.graphs.can_run(st)):
             toks = self.graphs.run(st)
             self.stats.graph_steps += 1
         else:
             toks = self.runner.execute(st)
             self.stats.mixed_steps += 1 if sched.prefill else 0
+        self.runner.score_step = False
         self.stats.scheduled_tokens += st.num_tokens
         self.stats.steps += 1
         self.stats.h2d_bytes += st.h2d_bytes()
@@ -528,11 +539,67 @@ class LLMEngine:
             outs.append(self._emit(r, [int(t)], now))
         if st.num_verify:
             outs.extend(self._apply_verify(sched, st, now))
-        if self.ecfg.kv_window_tokens > 0:
+        if score:
+            self._h2o_collect(sched)
+        if self.ecfg.kv_h2o_budget > 0:
+            for e in sched.decode:
+                if e.req.status is Status.RUNNING:
+                    self._evict_h2o(e.req)
+        elif self.ecfg.kv_window_tokens > 0:
             for e in sched.decode + sched.prefill:
                 if e.req.status is Status.RUNNING:
                     self._evict_window(e.req)
         return outs
+
+    # ------------------------------------------------------------------ heavy-hitter eviction
+    def _h2o_score_step(self, sched: Schedule) -> bool:
+        b = self.ecfg.kv_h2o_budget
+        if b <= 0 or not sched.decode or self.stats.steps % max(1, self.ecfg.kv_h2o_interval):
+            return False
+        # refresh while some decoding sequence is near its budget
+        return any(e.req.num_computed - e.req.evicted_tokens > b // 2 for e in sched.decode)
+
+    def _h2o_collect(self, sched: Schedule) -> None:
+        """Add this step's attention mass per page (all layers and heads) to each decoding
+        sequence's per-page totals."""
+        mass = self.runner.page_mass_buf
+        reqs = [e.req for e in sched.decode if e.tree is None]
+        if not reqs:
+            return
+        idx = [np.flatnonzero(np.asarray(r.pages) >= 0) for r in reqs]
+        phys = np.concatenate([np.asarray(r.pages, dtype=np.int64)[i] for r, i in zip(reqs, idx)])
+        vals = mass[torch.from_numpy(phys).to(mass.device)].float().cpu().numpy()
+        off = 0
+        for r, i in zip(reqs, idx):
+            if r.h2o_mass is None or len(r.h2o_mass) < len(r.pages):
+                grown = np.zeros(max(len(r.pages), 16) * 2, dtype=np.float64)
+                if r.h2o_mass is not None:
+                    grown[:len(r.h2o_mass)] = r.h2o_mass
+                r.h2o_mass = grown
+            r.h2o_mass[i] += vals[off:off + len(i)]
+            off += len(i)
+            r.h2o_scored = len(r.pages)
+
+    def _evict_h2o(self, r: Request) -> None:
+        """Over budget: give back the scored pages outside the sinks and the recent window with
+        the least accumulated attention mass (only full pages scored at least once)."""
+        ps, ec = self.qcfg.page_size, self.ecfg
+        over = r.num_computed - r.evicted_tokens - ec.kv_h2o_budget
+        if over <= 0 or r.h2o_mass is None:
+            return
+        sink = -(-ec.kv_sink_tokens // ps)
+        recent = (r.num_computed - max(ec.kv_window_tokens, ps)) // ps  # pages [recent, ..) are protected
+        cand = [b for b in range(sink, min(recent, r.h2o_scored)) if r.pages[b] >= 0]
+        if not cand:
+            return
+        cand.sort(key=lambda b: (r.h2o_mass[b], b))
+        gone = cand[:-(-over // ps)]
+        self.blocks.release([r.pages[b] for b in gone])
+        for b in gone:
+            r.pages[b] = -1
+            r.evicted_at[b] = r.num_computed
+        r.evicted_tokens += len(gone) * ps
+        self.stats.evicted_pages += len(gone)
 
     def _evict_window(self, r: Request) -> None:
         """Give back the pages between the sink pages and the recent window (page granular:

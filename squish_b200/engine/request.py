@@ -39,6 +39,11 @@ class Request:
     # total - evicted_tokens
     evicted_tokens: int = 0
     evict_from: int = 0  # first page index not yet checked for eviction
+    # heavy-hitter eviction: accumulated attention mass per logical page, pages scored so far,
+    # and when each evicted page went (num_computed at the time)
+    h2o_mass: object = field(default=None, repr=False)
+    h2o_scored: int = 0
+    evicted_at: dict = field(default_factory=dict, repr=False)
     # cached int32 copy of `pages` for the step's block table (valid while `_bt_src is pages`
     # and the length matches: pages only ever grow by append or are replaced by a new list)
     _bt_src: list | None = field(default=None, repr=False)

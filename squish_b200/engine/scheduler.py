@@ -87,7 +87,9 @@ class Scheduler:
         self.blocks.release(victim.pages)
         victim.pages = []
         victim.num_computed = 0
-        victim.evicted_tokens = victim.evict_from = 0
+        victim.evicted_tokens = victim.evict_from = victim.h2o_scored = 0
+        victim.h2o_mass = None
+        victim.evicted_at = {}
         victim.registered_blocks = 0
         victim.chain_hash = None
         victim.status = Status.WAITING

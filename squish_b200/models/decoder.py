@@ -258,6 +258,9 @@ class CudaRunner:
         self.cos_sin = rope_table(cfg, max(max_model_len, 16) + 1).to(dev)
         self.pools = pools or KVPools(cfg, self.qcfg, num_pages, dev)
         self.sm_scale = 1.0 / math.sqrt(cfg.head_dim)
+        # attention mass per KV page, refreshed on the steps the engine marks (H2O-style eviction)
+        self.score_step = False
+        self.page_mass_buf = torch.zeros(self.pools.num_pages, dtype=torch.float32, device=dev)
         self.had_k = self.had_v = self.had_v_row = None
         if getattr(self.qcfg, "kv_hadamard", False):
             sk, sv = ops.kernels.kv_hadamard_signs(cfg.head_dim)
@@ -411,6 +414,9 @@ class CudaRunner:
         if Bd:
             ops.paged_decode_attention(q[:Bd], kc, ks, vc, vs, bt[:Bd], m["dlens"], attn[:Bd], hq, hkv, d, ps, grp,
                                        self.fk, self.fv, self.sm_scale, st.max_decode_ctx, ws=ws, splits=dsplit)
+            if self.score_step:
+                ops.kernels.page_mass(q[:Bd].view(Bd, hq * d), kc, ks, bt[:Bd], m["dlens"], self.page_mass_buf, hq,
+                                      hkv, d, ps, grp, self.fk, self.sm_scale, ws=ws)
         if Bp:
             tm = m["tmask"][Bd:] if "tmask" in m else None
             ops.paged_prefill_attention(q[Bd:], kc, ks, vc, vs, bt[Bd:], m["tseq"], m["tq0"], m["qs"], m["ql"],
@@ -497,6 +503,8 @@ class CudaRunner:
     @torch.inference_mode()
     def execute(self, st: StepInputs) -> np.ndarray:
         self.timer_start()
+        if self.score_step:
+            self.page_mass_buf.zero_()
         m = self.upload(st)
         logits = self.forward(st, m)
         nS = st.num_sample_rows
@@ -555,6 +563,8 @@ class TorchPagedRunner:
         self.last_logits = None
         self.logits = None
         self.last_verify = self.last_preds = None
+        self.score_step = False
+        self.page_mass_buf = torch.zeros(num_pages)
 
     def kv_compact(self, src: list[int], dst: list[int]) -> None:
         for a, b in zip(src, dst):
@@ -567,6 +577,8 @@ class TorchPagedRunner:
 
         cfg, w = self.cfg, self.ref.w
         T = st.num_tokens
+        if self.score_step:
+            self.page_mass_buf.zero_()
         ids = torch.from_numpy(st.input_ids.astype(np.int64))
         pos = torch.from_numpy(st.positions.astype(np.int64))
         slots = torch.from_numpy(st.slot_mapping.astype(np.int64))
@@ -622,7 +634,11 @@ class TorchPagedRunner:
                                 if not (tm >> j) & 1:
                                     bad[i, ctx - n + j] = True
                 s = s.masked_fill(bad[None], float("-inf"))
-                o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), V)
+                pr = torch.softmax(s, -1)
+                if self.score_step and bt_row < Bd:  # attention mass per page (H2O-style scores)
+                    per_key = pr.sum((0, 1))
+                    self.page_mass_buf.index_add_(0, pages.repeat_interleave(self.ps)[:ctx], per_key)
+                o = torch.einsum("hqk,khd->qhd", pr, V)
                 attn[r0:r0 + n] = self.ref.unrotate_out(o).reshape(n, hq * d)
             h = h + self.ref._rp(attn, w[p + "self_attn.o_proj.weight"])
             x = _rms(h, w[p + "post_attention_layernorm.weight"], cfg.rms_eps)

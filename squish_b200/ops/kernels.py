@@ -401,6 +401,16 @@ def sylvester(d: int) -> torch.Tensor:
     return h / math.sqrt(d)
 
 
+def page_mass(q, k_codes, k_scales, block_tables, seq_lens, mass, hq: int, hkv: int, d: int, page_size: int,
+              group: int, fmt_k: int, sm_scale: float, ws: Workspace | None = None) -> None:
+    """mass[page] += the softmax attention probability of decode row b's query heads on the
+    keys of that page (summed over heads), for every row of ``seq_lens`` (kv_score.cu)."""
+    ws = ws or workspace(q.device)
+    native().page_mass(q, k_codes, k_scales, block_tables, seq_lens, mass, hq, hkv, d, page_size, group, fmt_k,
+                       float(sm_scale), ws.status)
+    _count()
+
+
 MAX_DECODE_SPLITS = 64
 
 

@@ -173,3 +173,41 @@ def test_hadamard_rotated_kv_keeps_the_model_and_cuts_kv_error(tiny):
     eng = LLMEngine.from_checkpoint(ck4, "cpu", EngineConfig(max_num_seqs=2, max_num_batched_tokens=64,
                                                              max_model_len=256, num_pages=32))
     assert eng.generate([p], SamplingParams(max_tokens=10, ignore_eos=True))[0] == ReferenceModel(ck4).greedy(p, 10)[0]
+
+
+def eviction_log_rule(r, ps=16):
+    """Keys visible to query position q given a request's eviction record: page b is gone for
+    every query at or after the num_computed at which it was evicted."""
+    gone = torch.full(((len(r.prompt) + len(r.output)) // ps + 2,), 1 << 30, dtype=torch.int64)
+    for b, at in r.evicted_at.items():
+        gone[b] = at
+
+    def visible(q, k):
+        return q < gone[torch.div(k, ps, rounding_mode="floor")]
+    return visible
+
+
+def test_heavy_hitter_eviction_keeps_budget_and_matches_oracle(tiny):
+    """H2O-style eviction: the engine scores pages by accumulated attention mass, keeps the
+    sequence within its token budget (sinks and the recent window always kept), and every
+    token equals the oracle's with exactly the pages the engine dropped hidden from the
+    queries that came after each drop."""
+    p = _prompt(35, 40)
+    eng = LLMEngine.from_checkpoint(tiny, "cpu", EngineConfig(max_num_seqs=2, max_num_batched_tokens=64,
+                                                              max_model_len=256, num_pages=64, kv_sink_tokens=16,
+                                                              kv_window_tokens=32, kv_h2o_budget=80,
+                                                              kv_h2o_interval=2))
+    rid = eng.add_request(p, SamplingParams(max_tokens=90, ignore_eos=True))
+    kept_max = 0
+    while eng.has_unfinished():
+        eng.step()
+        r = eng.requests[rid]
+        if r.status.name == "RUNNING":
+            kept_max = max(kept_max, r.num_computed - r.evicted_tokens)
+    r = eng.requests[rid]
+    assert eng.stats.evicted_pages >= 3 and kept_max <= 80 + 16
+    assert 0 not in r.evicted_at  # the sink page stays
+    assert all(b < (at - 32) // 16 for b, at in r.evicted_at.items())  # never inside the window
+    ref = ReferenceModel(tiny)
+    ref.kv_visible = eviction_log_rule(r)
+    assert r.output == ref.greedy(p, 90)[0]

@@ -197,6 +197,29 @@ def test_sink_window_eviction_on_the_cuda_engine(cuda):
     eng.runner.ws.check()
 
 
+def test_heavy_hitter_eviction_on_the_cuda_engine(cuda):
+    """H2O-style eviction with the device's page-mass kernel: the sequence stays within its
+    budget, and every token is the oracle's choice (teacher forced) with the pages the engine
+    dropped hidden from the queries after each drop."""
+    from tests.test_engine_cpu import eviction_log_rule
+
+    cfg, q = get_preset("tiny-llama")
+    eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
+                                    EngineConfig(max_num_seqs=4, max_model_len=512, num_pages=64, kv_sink_tokens=16,
+                                                 kv_window_tokens=48, kv_h2o_budget=112, kv_h2o_interval=3))
+    p = _prompt(43, 60, cfg.vocab_size)
+    rid = eng.add_request(p, SamplingParams(max_tokens=150, ignore_eos=True))
+    while eng.has_unfinished():
+        eng.step()
+    r = eng.requests[rid]
+    assert eng.stats.evicted_pages >= 4 and 0 not in r.evicted_at and eng.stats.graph_steps > 0
+    ref = ReferenceModel(_as_stored(random_checkpoint(cfg, q, seed=0, device="cpu")), bf16_storage=True)
+    ref.kv_visible = eviction_log_rule(r)
+    ok, worst = _teacher_forced_ok(ref, p, r.output)
+    assert ok, (worst, r.output)
+    eng.runner.ws.check()
+
+
 def test_sampled_decoding_runs_in_graphs(cuda):
     cfg, q = get_preset("tiny-llama")
     eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,

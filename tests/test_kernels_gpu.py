@@ -469,3 +469,55 @@ def test_out_of_pool_indices_are_skipped_and_reported(cuda, monkeypatch, legacy)
     assert int(ws.status.item()) == 6
     assert all(torch.equal(a, b) for a, b in zip(before, (kc, ks, vc, vs)))
     ws.status.zero_()
+
+
+@pytest.mark.parametrize("kv,d,hq,hkv", [("int4", 128, 28, 4), ("k8v4", 64, 8, 2), ("bf16", 32, 8, 2)])
+def test_page_attention_mass(cuda, kv, d, hq, hkv):
+    """Attention mass per KV page (H2O scores): for each decode row, the softmax probabilities
+    of all query heads over the row's keys, summed per page, accumulated into mass[page];
+    against fp32 on the CPU from the same pages decoded by the CPU codec."""
+    from squish_b200.kv.paged import kv_row_bytes
+
+    ps, group = 16, 32
+    fk, _ = ops.KV_FORMATS[kv]
+    cb, ns = kv_row_bytes(fk, d, group)
+    lens = [37, 300, 16, 129]
+    B = len(lens)
+    npg = sum(-(-n // ps) for n in lens) + 3
+    g = torch.Generator().manual_seed(5)
+    if fk == 0:
+        kc = torch.randn(npg, hkv, ps, d, generator=g).to(torch.bfloat16).view(torch.uint8).reshape(npg, hkv, ps, cb)
+        ks = torch.zeros(npg, hkv, ps, 1, dtype=torch.float16)
+    else:
+        kc = torch.randint(0, 256, (npg, hkv, ps, cb), generator=g, dtype=torch.uint8)
+        ks = (torch.rand(npg, hkv, ps, max(ns, 1), generator=g) * 0.2 + 0.05).half()
+    perm = torch.randperm(npg, generator=g)
+    maxp = max(-(-n // ps) for n in lens)
+    bt = torch.zeros(B, maxp, dtype=torch.int32)
+    o = 0
+    for b, n in enumerate(lens):
+        k = -(-n // ps)
+        bt[b, :k] = perm[o:o + k].int()
+        o += k
+    q = (torch.randn(B, hq * d, generator=g) * 2).to(torch.bfloat16)
+    mass = torch.zeros(npg, device=cuda)
+    ops.kernels.page_mass(q.to(cuda), kc.to(cuda), ks.to(cuda), bt.to(cuda), torch.tensor(lens, dtype=torch.int32,
+                          device=cuda), mass, hq, hkv, d, ps, group, fk, 1 / math.sqrt(d))
+    torch.cuda.synchronize()
+    ops.workspace(cuda).check()
+    if fk == 0:
+        K = kc.view(torch.bfloat16).float().reshape(npg, hkv, ps, d)
+    else:
+        K = C.cpu.kv_dequantize(kc.reshape(-1, cb).contiguous(), ks.reshape(-1, ks.shape[-1]).float().contiguous(),
+                                fk, group, d).reshape(npg, hkv, ps, d)
+    want = torch.zeros(npg, dtype=torch.float64)
+    for b, n in enumerate(lens):
+        pos = torch.arange(n)
+        pages = bt[b, pos // ps].long()
+        Kb = K[pages, :, pos % ps].double()                       # [n, hkv, d]
+        Kb = Kb.repeat_interleave(hq // hkv, dim=1)               # [n, hq, d]
+        s = torch.einsum("hd,nhd->hn", q[b].double().view(hq, d), Kb) / math.sqrt(d)
+        want.index_add_(0, pages, torch.softmax(s, -1).sum(0))
+    got = mass.double().cpu()
+    assert torch.allclose(got, want, rtol=2e-2, atol=2e-3), (got - want).abs().max()
+    assert abs(float(got.sum()) - hq * B) < 1e-2 * hq * B  # each head's probabilities sum to 1
