@@ -174,49 +174,68 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   }
 }
 
-__global__ void __launch_bounds__(32 * kRsNormRowsPerCta) tp_rs_norm_ag_kernel(const TpRsNormParams p) {
+// One CTA per owned row (grid = rows_per_rank on every rank, so every source signals the same
+// count); the row lives in registers, kRsNormMaxChunks chunks of 8 columns per thread.
+__global__ void __launch_bounds__(1024) tp_rs_norm_ag_kernel(const TpRsNormParams p) {
   pdl_wait();
   pdl_trigger();
+  __shared__ float red[32];
   const int par = *reinterpret_cast<volatile const int*>(p.seq) & 1;
   int* flags = p.rs_flags + par * p.tp;
   if ((int)threadIdx.x < p.tp) wait_flag(flags + threadIdx.x, p.rs_expect, p.status);
   __syncthreads();
   __threadfence();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int lr = blockIdx.x * kRsNormRowsPerCta + warp;
+  const int lr = blockIdx.x;
   const int own = min(p.rows_per_rank, p.T - p.rank * p.rows_per_rank);
-  if (lr < own) {
+  if (lr < own) {  // (uniform over the CTA)
     const int m = p.rank * p.rows_per_rank + lr;
     __nv_bfloat16* hr = p.h + (size_t)m * p.ldh;
+    float v[kRsNormMaxChunks][8];
     float ss = 0.f;
-    for (int c = lane * 8; c < p.N; c += 256) {  // residual + partials in source order
-      float acc[8], t[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(hr + c), acc);
+#pragma unroll
+    for (int k = 0; k < kRsNormMaxChunks; ++k) {
+      const int c = (threadIdx.x + k * blockDim.x) * 8;
+      if (c >= p.N) break;
+      float t[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(hr + c), v[k]);  // residual + partials in source order
       for (int s2 = 0; s2 < p.tp; ++s2) {
         bf16x8_to_f32(*reinterpret_cast<const uint4*>(p.recv + s2 * p.src_stride + (size_t)lr * p.ld_recv + c), t);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc[k] += t[k];
+        for (int e = 0; e < 8; ++e) v[k][e] += t[e];
       }
       uint4 o;
       __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        o2[k] = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
-        const float2 r2 = __bfloat1622float2(o2[k]);  // the norm sees the stored (rounded) values
+      for (int e = 0; e < 4; ++e) {
+        o2[e] = __floats2bfloat162_rn(v[k][2 * e], v[k][2 * e + 1]);
+        const float2 r2 = __bfloat1622float2(o2[e]);  // the norm sees the stored (rounded) values
+        v[k][2 * e] = r2.x;
+        v[k][2 * e + 1] = r2.y;
         ss += r2.x * r2.x + r2.y * r2.y;
       }
       *reinterpret_cast<uint4*>(hr + c) = o;
     }
     ss = warp_sum_f(ss);
-    const float inv = rsqrtf(ss / (float)p.N + p.eps);
-    for (int c = lane * 8; c < p.N; c += 256) {
-      float v[8], g[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(hr + c), v);  // this lane's own stores
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = (int)threadIdx.x < (int)(blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+      t = warp_sum_f(t);
+      if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = rsqrtf(red[0] / (float)p.N + p.eps);
+#pragma unroll
+    for (int k = 0; k < kRsNormMaxChunks; ++k) {
+      const int c = (threadIdx.x + k * blockDim.x) * 8;
+      if (c >= p.N) break;
+      float g[8];
       bf16x8_to_f32(*reinterpret_cast<const uint4*>(p.w + c), g);
       uint4 o;
       __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) o2[k] = __floats2bfloat162_rn(v[2 * k] * inv * g[2 * k], v[2 * k + 1] * inv * g[2 * k + 1]);
+      for (int e = 0; e < 4; ++e)
+        o2[e] = __floats2bfloat162_rn(v[k][2 * e] * inv * g[2 * e], v[k][2 * e + 1] * inv * g[2 * e + 1]);
       for (int r = 0; r < p.tp; ++r) *reinterpret_cast<uint4*>(p.ag_dst[r] + (size_t)m * p.ld_ag + c) = o;
     }
   }
@@ -247,11 +266,12 @@ __global__ void tp_ag_wait_kernel(int* ag_flags, int expect, int tp, int* status
 }  // namespace
 
 cudaError_t tp_rs_norm_ag_launch(const TpRsNormParams& p, cudaStream_t s) {
-  if (p.tp > 32 * kRsNormRowsPerCta || p.N % 8 || p.ldh % 8 || p.ld_ag % 8 || p.ld_recv % 8)
+  if (p.tp > 32 || p.N % 8 || p.ldh % 8 || p.ld_ag % 8 || p.ld_recv % 8 || p.N > 8 * 1024 * kRsNormMaxChunks)
     return cudaErrorInvalidValue;
-  const int grid = (p.rows_per_rank + kRsNormRowsPerCta - 1) / kRsNormRowsPerCta;
+  const int grid = p.rows_per_rank;  // one CTA per owned row
   if (grid == 0) return cudaSuccess;
-  SQ_LAUNCH(tp_rs_norm_ag_kernel, dim3(grid), dim3(32 * kRsNormRowsPerCta), 0, s, 1, p);
+  const int threads = min(1024, (p.N / 8 + 31) / 32 * 32);  // one 8-column chunk per thread up to N = 8192
+  SQ_LAUNCH(tp_rs_norm_ag_kernel, dim3(grid), dim3(threads), 0, s, 1, p);
   return cudaGetLastError();
 }
 

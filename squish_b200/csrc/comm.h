@@ -53,10 +53,11 @@ struct TpPushParams {
 // Sequence-parallel collectives (reduce-scatter -> RMSNorm -> all-gather), one kernel.
 // Rank r owns token rows [r * rows_per_rank, min(T, (r + 1) * rows_per_rank)). The row-parallel
 // GEMM pushed each source's bf16 partial of the owned rows into recv (the GEMM's reduce-scatter
-// routing); this kernel waits for every source's CTAs, adds the partials in source order to the
-// residual rows of h (written back), RMS-normalises them with w and stores the normalised rows
-// into every rank's all-gather buffer (P2P stores), then counts one arrival per CTA on every
-// rank's ag counter for this source. The last CTA clears this rank's reduce-scatter counters of
+// routing); this kernel (one CTA per owned row, rows_per_rank CTAs on every rank) waits for
+// every source's CTAs, adds the partials in source order to the residual rows of h (written
+// back), RMS-normalises them with w and stores the normalised rows into every rank's all-gather
+// buffer (P2P stores), then counts one arrival per CTA on every rank's ag counter for this
+// source. The last CTA clears this rank's reduce-scatter counters of
 // the parity it used and advances seq (parity = seq & 1 for the next round).
 struct TpRsNormParams {
   const __nv_bfloat16* recv;     // [tp source][rows_per_rank][ld_recv] on this rank
@@ -76,7 +77,7 @@ struct TpRsNormParams {
   int* done;
   int* status;
 };
-constexpr int kRsNormRowsPerCta = 8;  // one warp per row
+constexpr int kRsNormMaxChunks = 4;  // one CTA per row: <= 4 chunks of 8 columns per thread (N <= 32768)
 cudaError_t tp_rs_norm_ag_launch(const TpRsNormParams& p, cudaStream_t s);
 // Wait (one CTA, bounded) until ag_flags[s] >= expect for every source, then clear them.
 cudaError_t tp_ag_wait_launch(int* ag_flags, int expect, int tp, int* status, cudaStream_t s);

@@ -132,7 +132,7 @@ class TPComm:
         return -(-T // self.tp)
 
     def ag_expect(self, T: int) -> int:
-        return -(-self.sp_rows(T) // 8)  # CTAs of each source's tp_rs_norm_ag (8 rows each)
+        return self.sp_rows(T)  # CTAs of each source's tp_rs_norm_ag (one per owned row)
 
     def gemm_rs(self, x: torch.Tensor, w, ws) -> int:
         """Row-parallel GEMM whose partial rows go to their owner ranks (reduce-scatter routing
