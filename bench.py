@@ -341,6 +341,7 @@ def run_ours(args, world, rank, local):
     steps0 = eng.stats.steps
     launches0 = LAUNCHES[0]
     g0, mx0, sched0 = eng.stats.graph_steps, eng.stats.mixed_steps, eng.stats.scheduled_tokens
+    host0, wait0 = dict(eng.stats.host_s), runner.sync_wait_s
     clocks = ClockSampler(local, args.clocks != "0")
     barrier(world)
     clocks.start()
@@ -360,8 +361,11 @@ def run_ours(args, world, rank, local):
     h2d = (eng.stats.h2d_bytes - h2d0) / max(1, eng.stats.steps - steps0)
     d2h = (eng.stats.d2h_bytes - d2h0) / max(1, eng.stats.steps - steps0)
     sched_tok = (eng.stats.scheduled_tokens - sched0) / args.steps
+    host = {k: round((v - host0[k]) * 1000 / args.steps, 3) for k, v in eng.stats.host_s.items()}
+    host["device_wait"] = round((runner.sync_wait_s - wait0) * 1000 / args.steps, 3)
     detail = {"graph_decode": eng.stats.graph_steps - g0, "with_prefill": eng.stats.mixed_steps - mx0,
-              "tokens_per_step": sched_tok, "prefill_tokens_per_step": sched_tok - tokens / args.steps}
+              "tokens_per_step": sched_tok, "prefill_tokens_per_step": sched_tok - tokens / args.steps,
+              "host_ms_per_step": host, "wall_ms_per_step": round(wall * 1000 / args.steps, 3)}
     tot_tokens, tot_launch = reduce([tokens, launches], "sum", world)
     max_dev_ms, max_wall = reduce([dev_ms, wall], "max", world)
     all_ttft = gather_list(ttfts, world)

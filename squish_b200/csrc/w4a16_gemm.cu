@@ -450,7 +450,9 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       tc_fence_after();
       if (elect_one()) {
         const uint32_t xa = smem_u32(x_ring + rx.s * C::kXBytes);
-        if constexpr (C::AT) {
+        if (p.dbg & 2) {
+          // (timing experiment: no MMA)
+        } else if constexpr (C::AT) {
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             mma_bf16_ts(tmem, tmem + (uint32_t)(C::kA0 + ra.s * 32 + k * 8), sdesc_sw128(xa + k * 32), idesc,
@@ -517,7 +519,10 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
           ww[1] = wv.y;
         }
         const uint32_t* szt = reinterpret_cast<const uint32_t*>(tb + W_TILE_BYTES);
-        if (gpk == 1) {  // one (scale, zero) group covers the whole 64-column k-block
+        if (p.dbg & 1) {
+#pragma unroll
+          for (int w = 0; w < WPT; ++w) o[t][w] = make_uint4(ww[w], ww[w] ^ 1u, ww[w] ^ 2u, ww[w] ^ 3u);
+        } else if (gpk == 1) {  // one (scale, zero) group covers the whole 64-column k-block
           const uint32_t szw = szt[r];
           const __nv_bfloat162 s2 = __bfloat162bfloat162(__ushort_as_bfloat16((unsigned short)(szw & 0xFFFFu)));
           const __nv_bfloat162 z2 = __bfloat162bfloat162(__ushort_as_bfloat16((unsigned short)(szw >> 16)));
@@ -903,8 +908,13 @@ cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p0, in
     const char* e = std::getenv("SQ_GEMM_KROT");
     return e != nullptr ? std::atoi(e) : 0;
   }();
+  static const int dbg_env = [] {  // experiment: SQ_GEMM_DBG bit 0 = no dequant arithmetic, bit 1 = no MMA
+    const char* e = std::getenv("SQ_GEMM_DBG");
+    return e != nullptr ? std::atoi(e) : 0;
+  }();
   W4A16Params p = p0;
   if (krot_env) p.krot = 1;
+  p.dbg = dbg_env;
   int ow, ox, oa;
   const bool ov = ring_override(&ow, &ox, &oa);
   if (nt == 1) {

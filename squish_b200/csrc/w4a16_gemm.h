@@ -70,6 +70,9 @@ struct W4A16Params {
   // k-block order rotation (krot != 0): CTA (x, y) starts its k loop at a CTA-dependent block and
   // wraps, so the CTAs of one launch do not all read the same activation tile at the same time
   int krot;
+  // timing experiments only (results are wrong when set): bit 0 skips the dequant arithmetic
+  // (raw code words go to the operand), bit 1 skips the MMAs (the ring slots are still retired)
+  int dbg;
 };
 
 // True when token tiles of <= 64 run the 4-dequant-warp configuration (four CTAs per SM):

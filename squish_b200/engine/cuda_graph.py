@@ -112,5 +112,5 @@ class DecodeGraphs:
         toks = out["tokens"]
         r.tokens_host[:bucket].copy_(toks, non_blocking=True)
         r.timer_stop()
-        torch.cuda.current_stream(r.device).synchronize()
+        r.sync()
         return r.tokens_host[:B].numpy().copy()

@@ -86,6 +86,9 @@ class EngineStats:
     graph_steps: int = 0
     mixed_steps: int = 0
     scheduled_tokens: int = 0
+    # host seconds per phase of step(): schedule, build (step inputs), run (launches + the wait
+    # for the device, the wait alone in runner.sync_wait_s), post (tokens, stops, blocks)
+    host_s: dict = field(default_factory=lambda: {"schedule": 0.0, "build": 0.0, "run": 0.0, "post": 0.0})
     instant_first_tokens: int = 0  # first tokens sampled from the prompt-logit cache
     evicted_pages: int = 0         # pages given back by the attention window
 
@@ -496,13 +499,17 @@ class LLMEngine:
         return outs
 
     def _step(self) -> list[RequestOutput]:
+        hs = self.stats.host_s
+        t0 = time.perf_counter()
         sched = self.scheduler.schedule()
         self.stats.preemptions += len(sched.preempted)
         if sched.empty:
             return []
         if self.proposer is not None and sched.decode:
             self._attach_drafts(sched)
+        t1 = time.perf_counter()
         st, samp = self.build_inputs(sched)
+        t2 = time.perf_counter()
         score = self._h2o_score_step(sched)
         self.runner.score_step = score
         if (self.graphs is not None and not sched.prefill and st.allow_mask is None and st.num_verify == 0
@@ -513,6 +520,10 @@ class LLMEngine:
             toks = self.runner.execute(st)
             self.stats.mixed_steps += 1 if sched.prefill else 0
         self.runner.score_step = False
+        t3 = time.perf_counter()
+        hs["schedule"] += t1 - t0
+        hs["build"] += t2 - t1
+        hs["run"] += t3 - t2
         self.stats.scheduled_tokens += st.num_tokens
         self.stats.steps += 1
         self.stats.h2d_bytes += st.h2d_bytes()
@@ -541,6 +552,7 @@ class LLMEngine:
             outs.extend(self._apply_verify(sched, st, now))
         if score:
             self._h2o_collect(sched)
+        hs["post"] += time.perf_counter() - t3
         if self.ecfg.kv_h2o_budget > 0:
             for e in sched.decode:
                 if e.req.status is Status.RUNNING:

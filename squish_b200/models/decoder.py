@@ -16,6 +16,7 @@ the oracle of the engine path in CPU tests.
 from __future__ import annotations
 
 import math
+import time
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -479,6 +480,12 @@ class CudaRunner:
     # ------------------------------------------------------------------ device-side step timing
     timing = False
     _events: list = []
+    sync_wait_s = 0.0  # host time spent waiting for the device at the end of steps
+
+    def sync(self) -> None:
+        t = time.perf_counter()
+        torch.cuda.current_stream(self.device).synchronize()
+        self.sync_wait_s += time.perf_counter() - t
 
     def timer_start(self) -> None:
         if self.timing:
@@ -523,7 +530,7 @@ class CudaRunner:
                 ops.sample(vl, preds, ws=self.ws)
                 self.tokens_host[B:B + nv].copy_(preds, non_blocking=True)
         self.timer_stop()
-        torch.cuda.current_stream(self.device).synchronize()
+        self.sync()
         self.last_logits = logits if st.all_logits else None
         self.last_hidden = self.xs[:B]
         if G:
