@@ -2,7 +2,7 @@
 """Per-op timing of one tensor-parallel half layer in each collective mode (torchrun, one
 process per GPU):
 
-    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 bench/tp_ops.py [--hidden 8192] [--m 16,64]
+    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 bench/tp_ops.py [--hidden 8192] [--rows 16,64]
 
 A half layer is: row-parallel GEMM (o_proj shard: [M, hidden / tp] x [hidden, hidden / tp]^T)
 -> the collective -> RMSNorm -> column-parallel GEMM (qkv shard, hidden -> qkv_out / tp).
@@ -60,7 +60,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--hidden", type=int, default=8192)
     ap.add_argument("--qkv", type=int, default=10240, help="full qkv output width")
-    ap.add_argument("--m", default="16,64")
+    ap.add_argument("--rows", default="16,64", help="token rows M")
     ap.add_argument("--modes", default="nccl,nvlink,sp")
     ap.add_argument("--iters", type=int, default=200)
     a = ap.parse_args()
@@ -70,7 +70,7 @@ def main():
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     H = a.hidden
-    ms = [int(x) for x in a.m.split(",")]
+    ms = [int(x) for x in a.rows.split(",")]
     w_o = weight(H, H // world, 1 + rank, dev)
     w_qkv = weight(a.qkv // world, H, 100 + rank, dev)
     lnw = torch.ones(H, dtype=torch.bfloat16, device=dev)
