@@ -68,6 +68,36 @@ CUtensorMap make_bf16_map(const void* base, int rows, int cols, int ld, int box_
   return m;
 }
 
+// Activation map of the INT4 GEMM. With xg > 1 k-blocks per load (K a multiple of 64): a 3-D
+// view {64 columns, rows, k-block} (k-block stride 128 B) whose box {64, box_rows, xg} lands as
+// xg consecutive [box_rows x 128 B] swizzled tiles, the layout of xg single-k-block loads.
+CUtensorMap make_x_map(const torch::Tensor& x, int rows, int cols, int box_rows, int xg) {
+  const int ld = (int)x.stride(0);
+  if (xg <= 1 || cols % 64 != 0) return make_bf16_map(x.data_ptr(), rows, cols, ld, box_rows);
+  CUtensorMap m;
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(cols / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)xg};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, x.data_ptr(), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, std::string("cuTensorMapEncodeTiled (3-D) failed (") + std::to_string((int)r) + ")");
+  return m;
+}
+
+// k-blocks per activation load of the INT4 GEMM (SQ_GEMM_XG overrides; 1 when K is not a
+// multiple of 64)
+int gemm_xg(int64_t K, const sq::W4A16Params& p, int bn) {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("SQ_GEMM_XG");
+    v = e != nullptr ? std::max(1, std::min(4, std::atoi(e))) : 1;
+  }
+  if (K % 64 != 0 || p.tile_expert != nullptr || !sq::w4a16_decode_grouping(bn, p.wfmt, p.gpk)) return 1;
+  return std::max(1, std::min(v, p.kb_per_split));
+}
+
 int num_sms() {
   static int n = 0;
   if (!n) {
@@ -219,7 +249,8 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, 
     p.ag_expect = (int)ag_expect;
     p.tp = (int)ag_tp;
   }
-  const CUtensorMap xmap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), bn);
+  p.xg = gemm_xg(K, p, bn);
+  const CUtensorMap xmap = make_x_map(x, (int)M, (int)K, bn, p.xg);
   CUDA_OK(sq::w4a16_gemm_launch(xmap, p, bn, nt, cur_stream()));
 }
 
@@ -327,7 +358,8 @@ void w4a16_grouped_gemm(torch::Tensor x, torch::Tensor wq, int64_t N, int64_t K,
   p.num_tiles = ptr<int>(num_tiles);
   p.expert_stride = (long long)wq.stride(0) * wq.element_size();
   TORCH_CHECK(p.expert_stride % 16 == 0, "expert stride must be 16-byte aligned");
-  const CUtensorMap xmap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), (int)bn);
+  p.xg = gemm_xg(K, p, (int)bn);
+  const CUtensorMap xmap = make_x_map(x, (int)M, (int)K, (int)bn, p.xg);
   CUDA_OK(sq::w4a16_gemm_launch(xmap, p, (int)bn, 1, cur_stream()));
 }
 
@@ -502,7 +534,8 @@ std::vector<int64_t> w4a16_gemm_push(torch::Tensor x, torch::Tensor wq, int64_t 
   p.tp = (int)tp;
   const int64_t gx = (N + 128 * nt - 1) / (128 * nt), gy = (M + bn - 1) / bn;
   if (M > 0) {
-    const CUtensorMap xmap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), bn);
+    p.xg = gemm_xg(K, p, bn);
+    const CUtensorMap xmap = make_x_map(x, (int)M, (int)K, bn, p.xg);
     CUDA_OK(sq::w4a16_gemm_launch(xmap, p, bn, nt, cur_stream()));
   }
   return {bn, nt, plan[2], gx, gy};
@@ -550,7 +583,8 @@ int64_t w4a16_gemm_rs(torch::Tensor x, torch::Tensor wq, int64_t N, int64_t K, i
   p.push_rows = (int)rows_per_rank;
   const int64_t gx = (N + 128 * nt - 1) / (128 * nt), gy = (M + bn - 1) / bn;
   if (M > 0) {
-    const CUtensorMap xmap = make_bf16_map(x.data_ptr(), (int)M, (int)K, (int)x.stride(0), bn);
+    p.xg = gemm_xg(K, p, bn);
+    const CUtensorMap xmap = make_x_map(x, (int)M, (int)K, bn, p.xg);
     CUDA_OK(sq::w4a16_gemm_launch(xmap, p, bn, nt, cur_stream()));
   }
   return gx * gy * plan[2];

@@ -68,6 +68,10 @@ struct Cfg {
   // it delays the a_full arrival that starts MMA(i), while dequant(i + 1) already overlaps
   // MMA(i) in the plain order. Kept selectable for experiments.
   static constexpr bool kPipe = false;
+  // static shared table for NF4 levels / AQLM codebooks: only the 8-dequant-warp configurations
+  // decode those formats (the 4-warp decode configurations are INT4 only), so the others keep
+  // their 8 KiB for the rings: several CTAs per SM must fit 228 KiB including it
+  static constexpr int kFmtTab = DQW_ == 4 ? 1 : 512;
 };
 
 __host__ __device__ constexpr int code_bytes(int wfmt) {
@@ -82,12 +86,14 @@ struct Layout {
   uint32_t x_off, w_off, w_stage, bar_off, trace_off, total;
 };
 
+// rw / rx count ring stages of wg weight k-blocks / xg activation k-blocks (one bulk copy / one
+// TMA load each).
 __host__ __device__ inline Layout make_layout(int bn, int nt, int gpk, int rw, int rx, int ra, bool trace,
-                                              bool a_in_tmem, int wfmt) {
+                                              bool a_in_tmem, int wfmt, int wg = 1, int xg = 1) {
   Layout L;
   L.x_off = a_in_tmem ? 0u : (uint32_t)(ra * nt * A_TILE_BYTES);
-  L.w_off = L.x_off + (uint32_t)(rx * bn * 128);
-  L.w_stage = (uint32_t)(nt * tile_bytes(gpk, wfmt));
+  L.w_off = L.x_off + (uint32_t)(rx * xg * bn * 128);
+  L.w_stage = (uint32_t)(nt * wg * tile_bytes(gpk, wfmt));
   L.bar_off = L.w_off + (uint32_t)rw * L.w_stage;
   L.bar_off = (L.bar_off + 15u) & ~15u;
   L.trace_off = L.bar_off + (uint32_t)(2 * rw + 2 * rx + 2 * ra + 1) * 8u + 16u;
@@ -322,7 +328,11 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
 
   const int gpk = p.gpk;
   const int ring_w = p.ring_w, ring_x = p.ring_x, ring_a = p.ring_a;
-  const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a, p.trace != nullptr, C::AT, p.wfmt);
+  // k-blocks per weight bulk copy / per activation TMA load
+  const int wg = p.wg > 1 ? p.wg : 1;
+  const int xg = p.xg > 1 ? p.xg : 1;
+  const uint32_t xstage = (uint32_t)(xg * C::kXBytes);
+  const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a, p.trace != nullptr, C::AT, p.wfmt, wg, xg);
   uint8_t* a_ring = smem;  // (shared-memory A ring; with C::AT the region starts the X ring)
   uint8_t* x_ring = smem + L.x_off;
   uint8_t* w_ring = smem + L.w_off;
@@ -346,7 +356,6 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
   const int kb0 = split * p.kb_per_split;
   const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
   const int nkb = max(0, kb1 - kb0);
-  const int krot = (p.krot != 0 && nkb > 0) ? (int)((nblk * 7u + mblk * 3u) % (unsigned)nkb) : 0;
   int* status = p.status;
 
   if (threadIdx.x == 0) {
@@ -371,14 +380,16 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     tmem_relinquish();
   }
   // format table: NF4 (level[q0], level[q1]) bf16 pairs, or the AQLM codebooks (<= 2 x 256 x 8 bf16)
-  __shared__ uint4 fmt_tab[512];
+  __shared__ uint4 fmt_tab[C::kFmtTab];
   uint32_t* nf4_lut = reinterpret_cast<uint32_t*>(fmt_tab);
-  if (p.wfmt == WF_NF4) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x)
-      nf4_lut[i] = bf2_bits(__floats2bfloat162_rn(kNf4Levels[i & 15], kNf4Levels[i >> 4]));
-  } else if (p.wfmt == WF_AQLM) {
-    for (int i = threadIdx.x; i < 256 * p.n_books; i += blockDim.x)
-      fmt_tab[i] = reinterpret_cast<const uint4*>(p.codebook)[i];
+  if constexpr (C::kFmtTab >= 512) {
+    if (p.wfmt == WF_NF4) {
+      for (int i = threadIdx.x; i < 256; i += blockDim.x)
+        nf4_lut[i] = bf2_bits(__floats2bfloat162_rn(kNf4Levels[i & 15], kNf4Levels[i >> 4]));
+    } else if (p.wfmt == WF_AQLM) {
+      for (int i = threadIdx.x; i < 256 * p.n_books; i += blockDim.x)
+        fmt_tab[i] = reinterpret_cast<const uint4*>(p.codebook)[i];
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -394,16 +405,17 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     // ------------------------------------------------ weight producer: one bulk copy per tile
     const uint64_t pol = policy_evict_first();
     Ring r(ring_w);
-    for (int i = 0; i < nkb; ++i) {
+    for (int i = 0; i < nkb; i += wg) {
       if (!mbar_wait(&w_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_W)) break;
       if (elect_one()) {
+        // wg consecutive k-blocks of a 128-row block are contiguous (tile-major layout): one copy
+        const int cnt = min(wg, nkb - i);
         uint8_t* dst = w_ring + r.s * L.w_stage;
-        mbar_expect_tx(&w_full[r.s], L.w_stage);
-        const int kb = kb0 + (i + krot) % nkb;
+        mbar_expect_tx(&w_full[r.s], (uint32_t)(NT * cnt * tbytes));
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-          const size_t tile = ((size_t)nblk * NT + t) * p.kb_total + kb;
-          bulk_g2s_hint(dst + t * tbytes, wbase + tile * tbytes, (uint32_t)tbytes,
+          const size_t tile = ((size_t)nblk * NT + t) * p.kb_total + kb0 + i;
+          bulk_g2s_hint(dst + (size_t)t * wg * tbytes, wbase + tile * tbytes, (uint32_t)(cnt * tbytes),
                         &w_full[r.s], pol);
         }
         trace_mark(str, 0, i);
@@ -428,11 +440,14 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     }
     __syncwarp();
     Ring r(ring_x);
-    for (int i = 0; i < nkb; ++i) {
+    for (int i = 0; i < nkb; i += xg) {
       if (!mbar_wait(&x_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_X)) break;
       if (elect_one()) {
-        mbar_expect_tx(&x_full[r.s], C::kXBytes);
-        tma_load_2d(x_ring + r.s * C::kXBytes, &xmap, (kb0 + (i + krot) % nkb) * BK, mblk * BN, &x_full[r.s]);
+        mbar_expect_tx(&x_full[r.s], xstage);  // (a 3-D box always transfers all xg k-blocks)
+        if (xg > 1)  // 3-D map {64 columns, rows, k-block}: xg consecutive k-blocks in one load
+          tma_load_3d(x_ring + r.s * xstage, &xmap, 0, mblk * BN, kb0 + i, &x_full[r.s]);
+        else
+          tma_load_2d(x_ring + r.s * xstage, &xmap, (kb0 + i) * BK, mblk * BN, &x_full[r.s]);
         trace_mark(str, 1, i);
       }
       __syncwarp();
@@ -443,13 +458,14 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
     Ring rx(ring_x), ra(ring_a);
     for (int i = 0; i < nkb; ++i) {
-      if (!mbar_wait(&x_full[rx.s], rx.ph, status, SQ_ERR_TIMEOUT_X)) break;
+      const int xsub = i % xg;
+      if (xsub == 0 && !mbar_wait(&x_full[rx.s], rx.ph, status, SQ_ERR_TIMEOUT_X)) break;
       if (lane == 0) trace_mark(str, 2, i);
       if (!mbar_wait(&a_full[ra.s], ra.ph, status, SQ_ERR_TIMEOUT_A)) break;
       if (lane == 0) trace_mark(str, 3, i);
       tc_fence_after();
       if (elect_one()) {
-        const uint32_t xa = smem_u32(x_ring + rx.s * C::kXBytes);
+        const uint32_t xa = smem_u32(x_ring + rx.s * xstage + xsub * C::kXBytes);
         if (p.dbg & 2) {
           // (timing experiment: no MMA)
         } else if constexpr (C::AT) {
@@ -467,12 +483,13 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
                           (i > 0 || k > 0) ? 1u : 0u);
           }
         }
-        mma_commit(&x_empty[rx.s]);
+        const bool xlast = xsub == xg - 1 || i == nkb - 1;
+        if (xlast) mma_commit(&x_empty[rx.s]);
         mma_commit(&a_empty[ra.s]);
         trace_mark(str, 12, i);
       }
       __syncwarp();
-      rx.next();
+      if (xsub == xg - 1 || i == nkb - 1) rx.next();
       ra.next();
     }
     if (elect_one()) mma_commit(acc_full);
@@ -488,12 +505,13 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     Ring rw(ring_w), ra(ring_a);
     // Dequantize the next raw weight stage into o (waits for it, releases it); false on timeout.
     auto dq_stage = [&](int i, uint4 (&o)[NT][WPT]) -> bool {
-      if (!mbar_wait(&w_full[rw.s], rw.ph, status, SQ_ERR_TIMEOUT_W)) return false;
+      const int wsub = i % wg;
+      if (wsub == 0 && !mbar_wait(&w_full[rw.s], rw.ph, status, SQ_ERR_TIMEOUT_W)) return false;
       if (d == 0) trace_mark(str, 4, i);
       const uint8_t* wst = w_ring + rw.s * L.w_stage;
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
-        const uint8_t* tb = wst + t * tbytes;
+        const uint8_t* tb = wst + (size_t)(t * wg + wsub) * tbytes;
         if constexpr (WPT == 4) {
           if (p.wfmt != WF_INT4) {
             dq_other(tb, p.wfmt, r, c, gpk, nf4_lut, p.n_books, o[t]);
@@ -538,9 +556,11 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
           }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&w_empty[rw.s]);  // raw tile consumed (one arrive per warp)
-      rw.next();
+      if (wsub == wg - 1 || i == nkb - 1) {  // the copy's last tile consumed: release the slot
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&w_empty[rw.s]);  // (one arrive per warp)
+        rw.next();
+      }
       return true;
     };
     // this thread's 8*WPT K values of row r = 4*WPT columns of its lane in the TMEM A stage
@@ -783,21 +803,32 @@ cudaError_t launch_cfg(const CUtensorMap& xmap, W4A16Params p, int rw, int rx, i
   p.ring_w = rw;
   p.ring_x = rx;
   p.ring_a = ra;
-  const Layout L = make_layout(C::BN, C::NT, p.gpk, rw, rx, ra, p.trace != nullptr, C::AT, p.wfmt);
+  const Layout L = make_layout(C::BN, C::NT, p.gpk, rw, rx, ra, p.trace != nullptr, C::AT, p.wfmt,
+                               p.wg > 1 ? p.wg : 1, p.xg > 1 ? p.xg : 1);
   if (p.wfmt != WF_INT4 && C::kWpt != 4) return cudaErrorInvalidConfiguration;
+  if (p.xg > 1 && (C::NT != 1 || C::BN > 64)) return cudaErrorInvalidConfiguration;
   if (C::AT) {
     // the A ring lives in TMEM; the epilogue stages through the (then idle) X + W rings
     if (ra > C::kMaxRingA || L.bar_off < (uint32_t)(C::BN * BM * 4) || L.bar_off < 16u * BM * 4u)
       return cudaErrorInvalidConfiguration;
   }
   const size_t smem = (size_t)L.total + 1024;  // + alignment slack
-  if (smem + 512 * sizeof(uint4) > 227 * 1024) return cudaErrorInvalidConfiguration;  // + static fmt_tab
+  if (smem + C::kFmtTab * sizeof(uint4) > 227 * 1024) return cudaErrorInvalidConfiguration;  // + static fmt_tab
   auto kern = w4a16_gemm_kernel<C>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   // all of the SM's unified L1/shared storage as shared memory, so kMinBlocks CTAs fit
   e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e != cudaSuccess) return e;
+  static bool occ_checked = false;  // once per configuration: report a layout that loses CTAs per SM
+  if (!occ_checked) {
+    occ_checked = true;
+    int blocks = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, C::kThreads, smem) == cudaSuccess &&
+        blocks < C::kMinBlocks)
+      std::fprintf(stderr, "w4a16_gemm: BN=%d NT=%d runs %d CTA(s) per SM, not %d (%zu B shared)\n", C::BN, C::NT,
+                   blocks, C::kMinBlocks, smem);
+  }
   dim3 grid((p.N + BM * C::NT - 1) / (BM * C::NT), (p.M + C::BN - 1) / C::BN, p.splits);
   if (p.splits > 1 && (C::NT != 1 || p.splits > 16)) return cudaErrorInvalidConfiguration;
   if (p.splits > 8) {  // clusters of 9..16 CTAs are outside the portable size
@@ -832,6 +863,11 @@ static bool ring_override(int* w, int* x, int* a) {
 
 // Decode shapes, INT4 only: 4 dequant warps (a whole 64-column row per thread) and four CTAs
 // per SM. SQ_GEMM_WIDE_DQ=1 selects the 8-warp, two-CTA configuration instead.
+bool w4a16_decode_grouping(int bn, int wfmt, int gpk) {
+  int ow, ox, oa;
+  return bn <= 64 && w4a16_narrow(wfmt, gpk) && !ring_override(&ow, &ox, &oa);
+}
+
 bool w4a16_narrow(int wfmt, int gpk) {
   static const bool wide = [] {
     const char* e = std::getenv("SQ_GEMM_WIDE_DQ");
@@ -856,65 +892,44 @@ static int sm_count() {
 // fewer per SM each CTA takes half of the 228 KiB (deep rings, four TMEM A stages), otherwise
 // a quarter (the four-CTA configuration).
 template <int BN>
-cudaError_t launch_decode_narrow(const CUtensorMap& xmap, const W4A16Params& p, cudaStream_t s) {
+cudaError_t launch_decode_narrow(const CUtensorMap& xmap, W4A16Params p, cudaStream_t s) {
   const long ctas = (long)((p.N + BM - 1) / BM) * ((p.M + BN - 1) / BN) * p.splits;
   const int per_sm = (int)((ctas + sm_count() - 1) / sm_count());
   const bool tr = p.trace != nullptr;
-  auto fit = [&](int rx, int ra, size_t budget, int lo, int hi) {
+  const int xg = p.xg > 1 ? p.xg : 1;
+  auto fit = [&](int rx, int ra, int wg, size_t budget, int lo, int hi) {
     for (int rw = hi; rw > lo; --rw) {
-      const Layout L = make_layout(BN, 1, p.gpk, rw, rx, ra, tr, true, p.wfmt);
+      const Layout L = make_layout(BN, 1, p.gpk, rw, rx, ra, tr, true, p.wfmt, wg, xg);
       if ((size_t)L.total + 1024 <= budget) return rw;
     }
     return lo;
   };
-  auto fit2 = [&](int rx, int ra, size_t budget, int lo, int hi) {  // A ring in shared memory
-    for (int rw = hi; rw > lo; --rw) {
-      const Layout L = make_layout(BN, 1, p.gpk, rw, rx, ra, tr, false, p.wfmt);
-      if ((size_t)L.total + 1024 <= budget) return rw;
-    }
-    return lo;
-  };
-  static const bool asmem = [] {  // experiment: the dequantized operand in shared memory
-    const char* e = std::getenv("SQ_GEMM_ASMEM");
-    return e != nullptr && e[0] == '1';
+  // shared-memory budgets per CTA: the SM's 228 KiB over the resident CTAs, less the 1 KiB the
+  // hardware keeps per CTA (the budget covers the dynamic part + 1 KiB of alignment slack).
+  // Ring depths count loads: a weight stage holds wg k-blocks, an activation stage xg.
+  static const int wg_env = [] {  // k-blocks per weight copy (SQ_GEMM_WG overrides)
+    const char* e = std::getenv("SQ_GEMM_WG");
+    return e != nullptr ? std::max(1, std::min(8, std::atoi(e))) : 1;
   }();
-  static const int rx_env = [] {  // experiment: activation ring depth of the two-CTA configuration
-    const char* e = std::getenv("SQ_GEMM_RX");
-    return e != nullptr ? std::atoi(e) : 0;
-  }();
-  static const int one_ra = [] {  // experiment: one CTA per SM, 8 dequant warps, this many A stages
-    const char* e = std::getenv("SQ_GEMM_ONE");
-    return e != nullptr ? std::atoi(e) : 0;
-  }();
-  if (one_ra >= 2 && one_ra <= Cfg<BN, 1, 1, 8>::kMaxRingA) {
-    const int rx = rx_env >= 2 && rx_env <= 16 ? rx_env : 8;
-    return launch_cfg<Cfg<BN, 1, 1, 8>>(xmap, p, fit(rx, one_ra, 216 * 1024, 4, 40), rx, one_ra, s);
-  }
-  if (asmem) {
-    constexpr int rx = BN >= 32 ? 4 : 6;
-    if (per_sm <= 2) return launch_cfg<Cfg<BN, 1, 2, 4, true>>(xmap, p, fit2(rx, 2, 113 * 1024, 3, 16), rx, 2, s);
-    return launch_cfg<Cfg<BN, 1, 4, 4, true>>(xmap, p, fit2(3, 1, 56 * 1024, 2, 8), 3, 1, s);
-  }
+  p.wg = wg_env;
   if (per_sm <= 2) {
-    const int rx = rx_env >= 2 && rx_env <= 12 ? rx_env : BN >= 32 ? 4 : 6;
-    return launch_cfg<Cfg<BN, 1, 2, 4>>(xmap, p, fit(rx, 4, 113 * 1024, 4, 24), rx, 4, s);
+    const int rx = std::max(2, (BN >= 32 ? 4 : 6) / xg);
+    return launch_cfg<Cfg<BN, 1, 2, 4>>(xmap, p, fit(rx, 4, p.wg, 112 * 1024, std::max(2, 4 / p.wg), 24 / p.wg + 1),
+                                        rx, 4, s);
   }
-  constexpr int rx = BN == 64 ? 3 : BN == 32 ? 4 : 6;
-  return launch_cfg<Cfg<BN, 1, 4, 4>>(xmap, p, fit(rx, 2, 56 * 1024, 3, 12), rx, 2, s);
+  p.wg = std::min(p.wg > 1 ? p.wg : 1, 2);  // a quarter of the SM: two-k-block copies at most
+  const int rx = std::max(2, (BN == 64 ? 3 : BN == 32 ? 4 : 6) / xg);
+  return launch_cfg<Cfg<BN, 1, 4, 4>>(xmap, p, fit(rx, 2, p.wg, 55 * 1024, 2, 12 / p.wg + 1), rx, 2, s);
 }
 
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p0, int bn, int nt, cudaStream_t s) {
-  static const int krot_env = [] {  // experiment: SQ_GEMM_KROT=1 rotates every CTA's k-block order
-    const char* e = std::getenv("SQ_GEMM_KROT");
-    return e != nullptr ? std::atoi(e) : 0;
-  }();
   static const int dbg_env = [] {  // experiment: SQ_GEMM_DBG bit 0 = no dequant arithmetic, bit 1 = no MMA
     const char* e = std::getenv("SQ_GEMM_DBG");
     return e != nullptr ? std::atoi(e) : 0;
   }();
   W4A16Params p = p0;
-  if (krot_env) p.krot = 1;
   p.dbg = dbg_env;
+  p.wg = 1;  // (the decode configuration groups weight copies)
   int ow, ox, oa;
   const bool ov = ring_override(&ow, &ox, &oa);
   if (nt == 1) {

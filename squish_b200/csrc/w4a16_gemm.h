@@ -67,17 +67,20 @@ struct W4A16Params {
   int* ag_flags;
   int* ag_done;
   int ag_expect;
-  // k-block order rotation (krot != 0): CTA (x, y) starts its k loop at a CTA-dependent block and
-  // wraps, so the CTAs of one launch do not all read the same activation tile at the same time
-  int krot;
   // timing experiments only (results are wrong when set): bit 0 skips the dequant arithmetic
   // (raw code words go to the operand), bit 1 skips the MMAs (the ring slots are still retired)
   int dbg;
+  // k-blocks per weight bulk copy (wg, set by the launcher) and per activation TMA load (xg: the
+  // caller's x map is then the 3-D {64, rows, k-block} view with box depth xg); 0 or 1 = one
+  int wg, xg;
 };
 
 // True when token tiles of <= 64 run the 4-dequant-warp configuration (four CTAs per SM):
 // INT4 codes with one (scale, zero) group per 64-column k-block.
 bool w4a16_narrow(int wfmt, int gpk);
+// True when a launch with token tile bn runs the decode configuration, which takes an activation
+// map of xg > 1 k-blocks per load (W4A16Params::xg).
+bool w4a16_decode_grouping(int bn, int wfmt, int gpk);
 cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p, int bn, int nt, cudaStream_t s);
 // Expand tile-major weight codes to bf16 [N, ld] (ld >= 64 * ceil(K / 64), a multiple of 8).
 cudaError_t dequant_weight_launch(const uint32_t* wq, int wfmt, int N, int K, int group, int ld,

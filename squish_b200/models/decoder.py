@@ -261,7 +261,7 @@ class CudaRunner:
         self.sm_scale = 1.0 / math.sqrt(cfg.head_dim)
         # attention mass per KV page, refreshed on the steps the engine marks (H2O-style eviction)
         self.score_step = False
-        self.page_mass_buf = torch.zeros(self.pools.num_pages, dtype=torch.float32, device=dev)
+        self.page_mass_buf = torch.zeros(0, dtype=torch.float32, device=dev)  # sized at the first scoring step
         self.had_k = self.had_v = self.had_v_row = None
         if getattr(self.qcfg, "kv_hadamard", False):
             sk, sv = ops.kernels.kv_hadamard_signs(cfg.head_dim)
@@ -511,6 +511,9 @@ class CudaRunner:
     def execute(self, st: StepInputs) -> np.ndarray:
         self.timer_start()
         if self.score_step:
+            n = self.pools.layers[0][0].shape[0]
+            if self.page_mass_buf.numel() != n:  # (the page pool is sized after the weights load)
+                self.page_mass_buf = torch.zeros(n, dtype=torch.float32, device=self.device)
             self.page_mass_buf.zero_()
         m = self.upload(st)
         logits = self.forward(st, m)

@@ -499,7 +499,7 @@ def test_page_attention_mass(cuda, kv, d, hq, hkv):
         k = -(-n // ps)
         bt[b, :k] = perm[o:o + k].int()
         o += k
-    q = (torch.randn(B, hq * d, generator=g) * 2).to(torch.bfloat16)
+    q = (torch.randn(B, hq * d, generator=g) * 0.5).to(torch.bfloat16)
     mass = torch.zeros(npg, device=cuda)
     ops.kernels.page_mass(q.to(cuda), kc.to(cuda), ks.to(cuda), bt.to(cuda), torch.tensor(lens, dtype=torch.int32,
                           device=cuda), mass, hq, hkv, d, ps, group, fk, 1 / math.sqrt(d))
@@ -508,8 +508,9 @@ def test_page_attention_mass(cuda, kv, d, hq, hkv):
     if fk == 0:
         K = kc.view(torch.bfloat16).float().reshape(npg, hkv, ps, d)
     else:
+        # (the kernel, like the attention kernels, computes with the bf16 dequantized keys)
         K = C.cpu.kv_dequantize(kc.reshape(-1, cb).contiguous(), ks.reshape(-1, ks.shape[-1]).float().contiguous(),
-                                fk, group, d).reshape(npg, hkv, ps, d)
+                                fk, group, d).reshape(npg, hkv, ps, d).to(torch.bfloat16).float()
     want = torch.zeros(npg, dtype=torch.float64)
     for b, n in enumerate(lens):
         pos = torch.arange(n)
