@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--output-len", type=int, default=256)
     ap.add_argument("--max-batched-tokens", type=int, default=2048)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--host-profile", action="store_true",
+                    help="profile the host side of the timed steps (cProfile, top functions on stderr)")
     ap.add_argument("--ref-budget-s", type=float, default=150.0,
                     help="reference arm: time budget of the timed window (at least 3 steps)")
     ap.add_argument("--no-graphs", action="store_true")
@@ -331,6 +333,7 @@ def run_ours(args, world, rank, local):
     for _ in range(args.warmup):
         top_up()
         eng.step()
+    eng.warmup_graphs()  # every decode graph of the steady state captured before timing
     # timed region
     runner = eng.runner
     runner.timing = True
@@ -345,12 +348,24 @@ def run_ours(args, world, rank, local):
     clocks = ClockSampler(local, args.clocks != "0")
     barrier(world)
     clocks.start()
+    prof = None
+    if args.host_profile:
+        import cProfile
+
+        prof = cProfile.Profile()
     w0 = time.perf_counter()
+    if prof is not None:
+        prof.enable()
     for _ in range(args.steps):
         top_up()
         eng.step()
     torch.cuda.synchronize()
     wall = time.perf_counter() - w0
+    if prof is not None:
+        import pstats
+
+        prof.disable()
+        pstats.Stats(prof, stream=sys.stderr).sort_stats("tottime").print_stats(30)
     barrier(world)
     clk = clocks.stop()
     dev_ms = runner.device_time_ms()

@@ -208,10 +208,12 @@ def _build_frontend(a, max_pending: int):
         for i in range(dp):
             dev = f"cuda:{i}" if base.startswith("cuda") else base
             ld = load_engine(_model(a), dev, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a), page_size=a.page_size)
+            ld.engine.warmup_graphs()  # decode graphs captured before the first request
             first = first or ld
             reps.append(AsyncEngine(ld.engine, ld.tokenizer, max_pending=max_pending, model_name=ld.name))
         return DPRouter(reps, max_pending=max_pending).start(), first, None
     loaded = load_engine(_model(a), a.device, seed=a.seed, kv_dtype=_kv(a), ecfg=_ecfg(a), page_size=a.page_size)
+    loaded.engine.warmup_graphs()
     return AsyncEngine(loaded.engine, loaded.tokenizer, max_pending=max_pending, model_name=loaded.name).start(), \
         loaded, None
 

@@ -92,7 +92,7 @@ int gemm_xg(int64_t K, const sq::W4A16Params& p, int bn) {
   static int v = -1;
   if (v < 0) {
     const char* e = std::getenv("SQ_GEMM_XG");
-    v = e != nullptr ? std::max(1, std::min(4, std::atoi(e))) : 1;
+    v = e != nullptr ? std::max(1, std::min(4, std::atoi(e))) : 2;
   }
   if (K % 64 != 0 || p.tile_expert != nullptr || !sq::w4a16_decode_grouping(bn, p.wfmt, p.gpk)) return 1;
   return std::max(1, std::min(v, p.kb_per_split));

@@ -95,6 +95,28 @@ class DecodeGraphs:
         return g, {"tokens": toks, "launches": n_kernels}
 
     @torch.inference_mode()
+    def prewarm(self, batch: int, max_len: int) -> int:
+        """Capture the graphs of ``batch`` decoding sequences for every context bucket up to
+        ``max_len`` ahead of time (inert rows), so no capture, with its garbage collection, runs
+        inside a serving step. Returns the number of graphs captured."""
+        bucket = next((b for b in BATCH_BUCKETS if b >= min(batch, self.max_batch)), None)
+        if bucket is None or not self.enabled:
+            return 0
+        e, f = np.zeros(0, dtype=np.int32), np.zeros(0, dtype=np.float32)
+        st0 = StepInputs(e, e, e, 0, e, e, e, e, e, e, np.zeros((0, 1), dtype=np.int32), e, f, f, e, f, f, e, None,
+                         self.eng.ecfg.seed, 1)
+        n = 0
+        ctxb = 256
+        while True:
+            if (bucket, ctxb) not in self.graphs:
+                self.graphs[(bucket, ctxb)] = self._capture(self._pad(st0, bucket, ctxb))
+                n += 1
+            if ctxb >= max_len:
+                break
+            ctxb *= 2
+        return n
+
+    @torch.inference_mode()
     def run(self, st: StepInputs) -> np.ndarray:
         B = st.num_decode
         bucket = next(b for b in BATCH_BUCKETS if b >= B)

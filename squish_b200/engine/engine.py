@@ -331,6 +331,20 @@ class LLMEngine:
         else:
             self.scheduler.finish(req, "abort")
 
+    def warmup_graphs(self, batch: int | None = None) -> int:
+        """Capture the decode CUDA graphs a steady state of ``batch`` sequences (default
+        max_num_seqs) replays, for every context bucket up to max_model_len, then freeze the
+        objects alive so far out of the cyclic garbage collector's scans. Call after loading,
+        before serving; returns the number of graphs captured."""
+        import gc
+
+        n = 0
+        if self.graphs is not None:
+            n = self.graphs.prewarm(batch or self.ecfg.max_num_seqs, self.ecfg.max_model_len)
+        gc.collect()
+        gc.freeze()
+        return n
+
     def has_unfinished(self) -> bool:
         return bool(self._ready) or self.scheduler.has_work()
 

@@ -220,6 +220,22 @@ def test_heavy_hitter_eviction_on_the_cuda_engine(cuda):
     eng.runner.ws.check()
 
 
+def test_prewarmed_graphs_replay_without_capture(cuda):
+    """warmup_graphs() captures the steady-state decode graphs up front: a run afterwards
+    captures nothing new and matches an engine without graphs."""
+    cfg, q = get_preset("tiny-llama")
+    prompts = [_prompt(60 + i, 30 + 7 * i, cfg.vocab_size) for i in range(4)]
+    ecfg = EngineConfig(max_num_seqs=4, max_model_len=512, num_pages=128)
+    eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda, ecfg)
+    assert eng.warmup_graphs() == 2  # context buckets 256 and 512 at batch bucket 4
+    n = len(eng.graphs.graphs)
+    got = eng.generate(prompts, SamplingParams(max_tokens=20, ignore_eos=True))
+    assert len(eng.graphs.graphs) == n and eng.stats.graph_steps > 0
+    ref = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
+                                    dataclasses.replace(ecfg, cuda_graphs=False))
+    assert got == ref.generate(prompts, SamplingParams(max_tokens=20, ignore_eos=True))
+
+
 def test_sampled_decoding_runs_in_graphs(cuda):
     cfg, q = get_preset("tiny-llama")
     eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
