@@ -63,11 +63,6 @@ struct Cfg {
   static constexpr int kMaxRingA = MINB_ >= 3 ? 2 : MINB_ == 2 ? 4 : ((512 - kA0) / 32 < 12 ? (512 - kA0) / 32 : 12);
   static constexpr int kCols = AT ? kA0 + 32 * kMaxRingA : NT * BN;
   static constexpr int kTmemCols = (kCols <= 32) ? 32 : (kCols <= 64) ? 64 : (kCols <= 128) ? 128 : (kCols <= 256) ? 256 : 512;
-  // Dequantizing stage i + 1 before stage i's tensor-memory store completes (two register
-  // copies of a stage) was measured slower on B200 (gate_up at 64 tokens: 50.7 vs 43.5 us):
-  // it delays the a_full arrival that starts MMA(i), while dequant(i + 1) already overlaps
-  // MMA(i) in the plain order. Kept selectable for experiments.
-  static constexpr bool kPipe = false;
   // static shared table for NF4 levels / AQLM codebooks: only the 8-dequant-warp configurations
   // decode those formats (the 4-warp decode configurations are INT4 only), so the others keep
   // their 8 KiB for the rings: several CTAs per SM must fit 228 KiB including it
@@ -331,6 +326,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
   // k-blocks per weight bulk copy / per activation TMA load
   const int wg = p.wg > 1 ? p.wg : 1;
   const int xg = p.xg > 1 ? p.xg : 1;
+  const int ag = (C::AT && p.ag > 1) ? p.ag : 1;  // k-blocks per tensor-memory A stage (one hand-off)
   const uint32_t xstage = (uint32_t)(xg * C::kXBytes);
   const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a, p.trace != nullptr, C::AT, p.wfmt, wg, xg);
   uint8_t* a_ring = smem;  // (shared-memory A ring; with C::AT the region starts the X ring)
@@ -461,7 +457,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       const int xsub = i % xg;
       if (xsub == 0 && !mbar_wait(&x_full[rx.s], rx.ph, status, SQ_ERR_TIMEOUT_X)) break;
       if (lane == 0) trace_mark(str, 2, i);
-      if (!mbar_wait(&a_full[ra.s], ra.ph, status, SQ_ERR_TIMEOUT_A)) break;
+      const int asub = i % ag;
+      if (asub == 0 && !mbar_wait(&a_full[ra.s], ra.ph, status, SQ_ERR_TIMEOUT_A)) break;
       if (lane == 0) trace_mark(str, 3, i);
       tc_fence_after();
       if (elect_one()) {
@@ -471,8 +468,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         } else if constexpr (C::AT) {
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            mma_bf16_ts(tmem, tmem + (uint32_t)(C::kA0 + ra.s * 32 + k * 8), sdesc_sw128(xa + k * 32), idesc,
-                        (i > 0 || k > 0) ? 1u : 0u);
+            mma_bf16_ts(tmem, tmem + (uint32_t)(C::kA0 + (ra.s * ag + asub) * 32 + k * 8), sdesc_sw128(xa + k * 32),
+                        idesc, (i > 0 || k > 0) ? 1u : 0u);
         } else {
 #pragma unroll
           for (int t = 0; t < NT; ++t) {
@@ -483,14 +480,13 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
                           (i > 0 || k > 0) ? 1u : 0u);
           }
         }
-        const bool xlast = xsub == xg - 1 || i == nkb - 1;
-        if (xlast) mma_commit(&x_empty[rx.s]);
-        mma_commit(&a_empty[ra.s]);
+        if (xsub == xg - 1 || i == nkb - 1) mma_commit(&x_empty[rx.s]);
+        if (asub == ag - 1 || i == nkb - 1) mma_commit(&a_empty[ra.s]);
         trace_mark(str, 12, i);
       }
       __syncwarp();
       if (xsub == xg - 1 || i == nkb - 1) rx.next();
-      ra.next();
+      if (asub == ag - 1 || i == nkb - 1) ra.next();
     }
     if (elect_one()) mma_commit(acc_full);
     __syncwarp();
@@ -564,8 +560,9 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       return true;
     };
     // this thread's 8*WPT K values of row r = 4*WPT columns of its lane in the TMEM A stage
-    auto st_tmem = [&](const uint4 (&o)[NT][WPT]) {
-      const uint32_t col = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(C::kA0 + ra.s * 32 + c * WPT * 4);
+    auto st_tmem = [&](const uint4 (&o)[NT][WPT], int asub) {
+      const uint32_t col =
+          tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(C::kA0 + (ra.s * ag + asub) * 32 + c * WPT * 4);
       if constexpr (WPT == 8) {
         uint32_t regs[32];
 #pragma unroll
@@ -587,43 +584,21 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         tmem_st8(col, regs);
       }
     };
-    if constexpr (C::AT && C::kPipe) {
-      // Software-pipelined: the tensor-memory store of stage i is in flight while stage i + 1
-      // is dequantized, so a warp's per-stage chain is max(store round trip, dequant) rather
-      // than their sum (two register copies of a stage's operand).
-      uint4 cur[NT][WPT], nxt[NT][WPT];
-      bool ok = nkb > 0 && dq_stage(0, cur);
-      for (int i = 0; ok && i < nkb; ++i) {
-        if (!mbar_wait(&a_empty[ra.s], ra.ph ^ 1u, status, SQ_ERR_TIMEOUT_A)) break;
-        if (d == 0) trace_mark(str, 5, i);
-        tc_fence_after();
-        st_tmem(cur);
-        const bool more = i + 1 < nkb;
-        if (more) ok = dq_stage(i + 1, nxt);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[ra.s]);
-        if (d == 0) trace_mark(str, 6, i);
-        ra.next();
-        if (more) {
-#pragma unroll
-          for (int t = 0; t < NT; ++t)
-#pragma unroll
-            for (int w = 0; w < WPT; ++w) cur[t][w] = nxt[t][w];
-        }
-      }
-    } else {
+    {
       for (int i = 0; i < nkb; ++i) {
         uint4 o[NT][WPT];
         if (!dq_stage(i, o)) break;
-        if (!mbar_wait(&a_empty[ra.s], ra.ph ^ 1u, status, SQ_ERR_TIMEOUT_A)) break;
+        const int asub = i % ag;
+        const bool alast = asub == ag - 1 || i == nkb - 1;
+        if (asub == 0 && !mbar_wait(&a_empty[ra.s], ra.ph ^ 1u, status, SQ_ERR_TIMEOUT_A)) break;
         if (d == 0) trace_mark(str, 5, i);
         if constexpr (C::AT) {
-          tc_fence_after();
-          st_tmem(o);
-          tmem_wait_st();
-          tc_fence_before();
+          if (asub == 0) tc_fence_after();
+          st_tmem(o, asub);
+          if (alast) {  // the stage's stores land before the MMA warp is told
+            tmem_wait_st();
+            tc_fence_before();
+          }
         } else {
 #pragma unroll
           for (int t = 0; t < NT; ++t) {
@@ -634,10 +609,12 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
           }
           fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core (async proxy)
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[ra.s]);
+        if (alast) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[ra.s]);
+          ra.next();
+        }
         if (d == 0) trace_mark(str, 6, i);
-        ra.next();
       }
     }
   }
@@ -809,7 +786,8 @@ cudaError_t launch_cfg(const CUtensorMap& xmap, W4A16Params p, int rw, int rx, i
   if (p.xg > 1 && (C::NT != 1 || C::BN > 64)) return cudaErrorInvalidConfiguration;
   if (C::AT) {
     // the A ring lives in TMEM; the epilogue stages through the (then idle) X + W rings
-    if (ra > C::kMaxRingA || L.bar_off < (uint32_t)(C::BN * BM * 4) || L.bar_off < 16u * BM * 4u)
+    if (ra * (p.ag > 1 ? p.ag : 1) > C::kMaxRingA || L.bar_off < (uint32_t)(C::BN * BM * 4) ||
+        L.bar_off < 16u * BM * 4u)
       return cudaErrorInvalidConfiguration;
   }
   const size_t smem = (size_t)L.total + 1024;  // + alignment slack
@@ -909,12 +887,19 @@ cudaError_t launch_decode_narrow(const CUtensorMap& xmap, W4A16Params p, cudaStr
     const char* e = std::getenv("SQ_GEMM_RX");
     return e != nullptr ? std::atoi(e) : 0;
   }();
+  static const int ag_env = [] {  // k-blocks per A stage hand-off (SQ_GEMM_AG overrides)
+    const char* e = std::getenv("SQ_GEMM_AG");
+    return e != nullptr ? std::max(1, std::min(4, std::atoi(e))) : 1;
+  }();
   p.wg = wg_env;
   if (per_sm <= 2) {
+    p.ag = ag_env;
+    const int ra = std::max(1, 4 / p.ag);
     const int rx = rx_env >= 2 && rx_env <= 16 ? rx_env : std::max(2, (BN >= 32 ? 4 : 6) / xg);
-    return launch_cfg<Cfg<BN, 1, 2, 4>>(xmap, p, fit(rx, 4, p.wg, 112 * 1024, std::max(2, 4 / p.wg), 24 / p.wg + 1),
-                                        rx, 4, s);
+    return launch_cfg<Cfg<BN, 1, 2, 4>>(xmap, p, fit(rx, ra, p.wg, 112 * 1024, std::max(2, 4 / p.wg), 24 / p.wg + 1),
+                                        rx, ra, s);
   }
+  p.ag = 1;
   p.wg = std::min(p.wg > 1 ? p.wg : 1, 2);  // a quarter of the SM: two-k-block copies at most
   const int rx = std::max(2, (BN == 64 ? 3 : BN == 32 ? 4 : 6) / xg);
   return launch_cfg<Cfg<BN, 1, 4, 4>>(xmap, p, fit(rx, 2, p.wg, 55 * 1024, 2, 12 / p.wg + 1), rx, 2, s);
@@ -927,7 +912,8 @@ cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p0, in
   }();
   W4A16Params p = p0;
   p.dbg = dbg_env;
-  p.wg = 1;  // (the decode configuration groups weight copies)
+  p.wg = 1;  // (the decode configuration groups weight copies and A stages)
+  p.ag = 1;
   int ow, ox, oa;
   const bool ov = ring_override(&ow, &ox, &oa);
   if (nt == 1) {

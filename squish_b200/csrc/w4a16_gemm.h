@@ -73,6 +73,8 @@ struct W4A16Params {
   // k-blocks per weight bulk copy (wg, set by the launcher) and per activation TMA load (xg: the
   // caller's x map is then the 3-D {64, rows, k-block} view with box depth xg); 0 or 1 = one
   int wg, xg;
+  // k-blocks per tensor-memory A stage (one dequant -> MMA hand-off), set by the launcher
+  int ag;
 };
 
 // True when token tiles of <= 64 run the 4-dequant-warp configuration (four CTAs per SM):
