@@ -590,6 +590,38 @@ int64_t w4a16_gemm_rs(torch::Tensor x, torch::Tensor wq, int64_t N, int64_t K, i
   return gx * gy * plan[2];
 }
 
+// One-shot all-reduce: out (+)= sum over ranks of src, through double-buffered peer slots.
+void tp_oneshot(torch::Tensor src, torch::Tensor part_ptrs, int64_t par_stride, torch::Tensor flag_ptrs,
+                torch::Tensor out, bool residual_in_out, int64_t rank, int64_t tp, torch::Tensor seq, torch::Tensor done,
+                torch::Tensor status) {
+  CHECK_CUDA(src);
+  CHECK_DT(src, torch::kBFloat16);
+  CHECK_DT(out, torch::kBFloat16);
+  TORCH_CHECK(src.dim() == 2 && out.dim() == 2 && src.size(0) == out.size(0) && src.size(1) == out.size(1) &&
+                  src.stride(1) == 1 && out.stride(1) == 1,
+              "src / out: [M, N] with unit column stride");
+  TORCH_CHECK(part_ptrs.numel() == tp && flag_ptrs.numel() == tp && part_ptrs.is_cuda() && flag_ptrs.is_cuda(),
+              "one device pointer per rank");
+  const c10::cuda::CUDAGuard g(src.device());
+  sq::TpOneshotParams p{};
+  p.src = ptr<__nv_bfloat16>(src);
+  p.ld_src = (int)src.stride(0);
+  p.part = reinterpret_cast<__nv_bfloat16* const*>(part_ptrs.data_ptr());
+  p.par_stride = par_stride;
+  p.flags = reinterpret_cast<int* const*>(flag_ptrs.data_ptr());
+  p.out = ptr<__nv_bfloat16>(out);
+  p.ld_out = (int)out.stride(0);
+  p.residual_in_out = residual_in_out ? 1 : 0;
+  p.M = (int)src.size(0);
+  p.N = (int)src.size(1);
+  p.rank = (int)rank;
+  p.tp = (int)tp;
+  p.seq = ptr<int>(seq);
+  p.done = ptr<int>(done);
+  p.status = ptr<int>(status);
+  CUDA_OK(sq::tp_oneshot_launch(p, cur_stream()));
+}
+
 void tp_rs_norm_ag(torch::Tensor recv, int64_t src_stride, int64_t ld_recv, torch::Tensor rs_flags, int64_t rs_expect,
                    torch::Tensor h, torch::Tensor w, double eps, torch::Tensor ag_dst, int64_t ld_ag,
                    torch::Tensor ag_flags, int64_t rank, int64_t tp, int64_t rows_per_rank, int64_t T,
@@ -1124,6 +1156,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ag_tp") = 0);
   m.def("w4a16_gemm_rs", &w4a16_gemm_rs);
   m.def("tp_rs_norm_ag", &tp_rs_norm_ag);
+  m.def("tp_oneshot", &tp_oneshot);
   m.def("tp_ag_wait", &tp_ag_wait);
   m.def("dequant_weight", &dequant_weight);
   m.def("bf16_gemm", &bf16_gemm);

@@ -22,6 +22,7 @@
 // which a peer issues only after it finished reading the previous gather's output.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <cstdint>
 
 #include "comm.h"
@@ -254,6 +255,65 @@ __global__ void __launch_bounds__(1024) tp_rs_norm_ag_kernel(const TpRsNormParam
   }
 }
 
+// chunk of CTA b: 8-element vectors [b * per, (b + 1) * per) of the row-major [M, N] output
+__global__ void __launch_bounds__(kOneshotThreads) tp_oneshot_kernel(const TpOneshotParams p) {
+  pdl_wait();  // the partial (previous kernel) is complete
+  pdl_trigger();
+  const int s = *reinterpret_cast<volatile const int*>(p.seq);
+  const int par = s & 1, val = s + 1;
+  const int vecs_row = p.N / 8;
+  const long long total = (long long)p.M * vecs_row;
+  const long long per = (total + gridDim.x - 1) / gridDim.x;
+  const long long v0 = blockIdx.x * per, v1 = min(total, v0 + per);
+  __nv_bfloat16* mine = p.part[p.rank] + (size_t)par * p.par_stride;
+  for (long long v = v0 + threadIdx.x; v < v1; v += blockDim.x) {  // own chunk into the peer-visible slot
+    const int m = (int)(v / vecs_row), n = (int)(v % vecs_row) * 8;
+    *reinterpret_cast<uint4*>(mine + (size_t)m * p.N + n) =
+        *reinterpret_cast<const uint4*>(p.src + (size_t)m * p.ld_src + n);
+  }
+  __threadfence_system();
+  __syncthreads();
+  const int b = blockIdx.x;
+  if ((int)threadIdx.x < p.tp) {  // publish chunk b on every rank, then wait for every peer's
+    int* f = p.flags[threadIdx.x] + b * p.tp + p.rank;
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(f), "r"(val) : "memory");
+    wait_flag(p.flags[p.rank] + b * p.tp + threadIdx.x, val, p.status);
+  }
+  __syncthreads();
+  for (long long v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+    const int m = (int)(v / vecs_row), n = (int)(v % vecs_row) * 8;
+    float acc[8], t[8];
+    __nv_bfloat16* o = p.out + (size_t)m * p.ld_out + n;
+    if (p.residual_in_out) {
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(o), acc);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    }
+    for (int r = 0; r < p.tp; ++r) {  // rank order: the same sum on every rank
+      // (peer memory: load through L2 only)
+      bf16x8_to_f32(__ldcg(reinterpret_cast<const uint4*>(p.part[r] + (size_t)par * p.par_stride + (size_t)m * p.N + n)),
+                    t);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += t[e];
+    }
+    uint4 w;
+    __nv_bfloat162* w2 = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) w2[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+    *reinterpret_cast<uint4*>(o) = w;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(p.done, 1) == (int)gridDim.x - 1) {
+      *p.done = 0;
+      __threadfence();
+      atomicAdd(p.seq, 1);
+    }
+  }
+}
+
 __global__ void tp_ag_wait_kernel(int* ag_flags, int expect, int tp, int* status) {
   pdl_wait();
   pdl_trigger();
@@ -272,6 +332,17 @@ cudaError_t tp_rs_norm_ag_launch(const TpRsNormParams& p, cudaStream_t s) {
   if (grid == 0) return cudaSuccess;
   const int threads = min(1024, (p.N / 8 + 31) / 32 * 32);  // one 8-column chunk per thread up to N = 8192
   SQ_LAUNCH(tp_rs_norm_ag_kernel, dim3(grid), dim3(threads), 0, s, 1, p);
+  return cudaGetLastError();
+}
+
+cudaError_t tp_oneshot_launch(const TpOneshotParams& p, cudaStream_t s) {
+  if (p.M == 0) return cudaSuccess;
+  if (p.tp > 32 || p.N % 8 || p.ld_src % 8 || p.ld_out % 8 || p.par_stride < (long long)p.M * p.N)
+    return cudaErrorInvalidValue;
+  const long long vecs = (long long)p.M * (p.N / 8);
+  // ~4 vectors per thread; every rank computes the same grid (same M, N)
+  const int grid = (int)std::min<long long>(kOneshotMaxCtas, (vecs + 4 * kOneshotThreads - 1) / (4 * kOneshotThreads));
+  SQ_LAUNCH(tp_oneshot_kernel, dim3(grid), dim3(kOneshotThreads), 0, s, 1, p);
   return cudaGetLastError();
 }
 

@@ -81,6 +81,28 @@ constexpr int kRsNormMaxChunks = 4;  // one CTA per row: <= 4 chunks of 8 column
 cudaError_t tp_rs_norm_ag_launch(const TpRsNormParams& p, cudaStream_t s);
 // Wait (one CTA, bounded) until ag_flags[s] >= expect for every source, then clear them.
 cudaError_t tp_ag_wait_launch(int* ag_flags, int expect, int tp, int* status, cudaStream_t s);
+// One-shot all-reduce over peer memory, for small row-parallel outputs (decode): CTA b copies
+// chunk b of this rank's partial `src` [M, ld_src] into its own double-buffered peer-visible
+// slot part[rank][parity], publishes chunk b (flag value seq + 1 in every rank's slot
+// [b][rank]), waits (bounded) for chunk b of every peer, then out[chunk b] = residual + the tp
+// partials summed in rank order (bit-identical on every rank). The last CTA advances seq.
+struct TpOneshotParams {
+  const __nv_bfloat16* src;
+  int ld_src;
+  __nv_bfloat16* const* part;  // [tp] every rank's slot base (parity 0); parity 1 at + par_stride
+  long long par_stride;        // elements
+  int* const* flags;           // [tp] every rank's flag array [kOneshotMaxCtas][tp]
+  __nv_bfloat16* out;
+  int ld_out;
+  int residual_in_out;         // out += sum (out holds the residual) instead of out = sum
+  int M, N, rank, tp;
+  int* seq;
+  int* done;
+  int* status;
+};
+constexpr int kOneshotMaxCtas = 148;
+constexpr int kOneshotThreads = 256;
+cudaError_t tp_oneshot_launch(const TpOneshotParams& p, cudaStream_t s);
 cudaError_t tp_push_launch(const TpPushParams& p, int grid_x, int grid_y, cudaStream_t s);
 cudaError_t tp_reduce_launch(const TpReduceParams& p, int grid_x, int grid_y, cudaStream_t s);
 cudaError_t tp_gather_launch(const TpGatherParams& p, cudaStream_t s);

@@ -2,10 +2,13 @@
 
 Two implementations behind one interface:
 
-  * ``nvlink`` (default on GPUs): buffers shared by CUDA IPC across the group; the
-    row-parallel GEMM pushes its output tiles into every rank's receive buffer from the
-    GEMM epilogue and ``tp_reduce`` sums them (csrc/comm.cu); the vocab-parallel logits are
-    gathered with P2P stores. No NCCL call on the step's hot path.
+  * ``nvlink`` (default on GPUs): buffers shared by CUDA IPC across the group. Decode-sized
+    row-parallel outputs (<= 256 tokens) run the GEMM into a local scratch and then one
+    one-shot all-reduce kernel (``tp_oneshot``: each CTA publishes its chunk in a
+    double-buffered peer-visible slot, waits for the peers' chunk, sums in rank order);
+    larger ones push output tiles into every rank's receive buffer from the GEMM epilogue and
+    ``tp_reduce`` sums them (csrc/comm.cu). The vocab-parallel logits are gathered with P2P
+    stores. No NCCL call on the step's hot path.
   * ``sp`` (sequence parallel): rank r owns a contiguous block of the step's token rows; the
     row-parallel GEMMs (o_proj, down_proj) route each partial row to its owner from the GEMM
     epilogue (reduce-scatter: (tp-1)/tp of the rows cross NVLink, not (tp-1) copies of all of
@@ -21,11 +24,20 @@ logic is replicated SPMD on every rank), which both protocols rely on.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
 from .._ext import native
 from .shard import vocab_shard
+
+
+ONESHOT_MAX_CTAS = 148  # csrc/comm.h kOneshotMaxCtas
+# Row-parallel outputs of at most this many tokens take the one-shot all-reduce (GEMM into a
+# local scratch, then one kernel that publishes, waits and sums); larger ones the fused
+# push-from-the-epilogue path
+ONESHOT_MAX_TOKENS = int(os.environ.get("SQ_TP_ONESHOT_MAX_TOKENS", "256"))
 
 
 class TPComm:
@@ -95,6 +107,14 @@ class TPComm:
         self.seq = torch.zeros(1, dtype=torch.int32, device=dev)
         self.done = torch.zeros(1, dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        # one-shot all-reduce: double-buffered partial slots and per-chunk arrival flags
+        os_part = self._alloc_shared(2 * T * H * 2)
+        os_flags = self._alloc_shared(ONESHOT_MAX_CTAS * tp * 4)
+        self.os_part_ptrs = torch.tensor(os_part, **i64)
+        self.os_flag_ptrs = torch.tensor(os_flags, **i64)
+        self.os_tmp = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        self.os_seq = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.os_done = torch.zeros(1, dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)
         dist.barrier(group=self.group)
 
@@ -199,6 +219,12 @@ class TPComm:
         N = w.n
         if T > self.max_tokens or N != self.hidden:
             raise ValueError("row-parallel output exceeds the peer buffers")
+        if T <= ONESHOT_MAX_TOKENS:
+            part = K.w4a16_linear(x, w, out=self.os_tmp[:T], ws=ws)
+            native().tp_oneshot(part, self.os_part_ptrs, self.max_tokens * self.hidden, self.os_flag_ptrs, h, True,
+                                self.rank, self.tp, self.os_seq, self.os_done, self.status)
+            K._count()
+            return
         bn, nt, _, _, _ = native().gemm_plan(T, N, w.k)
         if ((N + 128 * nt - 1) // (128 * nt)) * ((T + bn - 1) // bn) > self.max_tiles:
             raise ValueError("GEMM tile grid exceeds the flag array")
