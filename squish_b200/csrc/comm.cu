@@ -271,7 +271,8 @@ __global__ void __launch_bounds__(kOneshotThreads) tp_oneshot_kernel(const TpOne
     *reinterpret_cast<uint4*>(mine + (size_t)m * p.N + n) =
         *reinterpret_cast<const uint4*>(p.src + (size_t)m * p.ld_src + n);
   }
-  __threadfence_system();
+  // The CTA barrier orders every thread's chunk stores before the publishing threads'
+  // system-scope release stores (release is cumulative), so no per-thread system fence.
   __syncthreads();
   const int b = blockIdx.x;
   if ((int)threadIdx.x < p.tp) {  // publish chunk b on every rank, then wait for every peer's

@@ -620,6 +620,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         if (alast) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&a_full[ra.s]);
+          if (lane == 0 && warp < 8) trace_mark(str, 4 + warp, i);  // trace slots 8-11: each warp's hand-off
           ra.next();
         }
         if (d == 0) trace_mark(str, 6, i);
