@@ -341,8 +341,9 @@ cudaError_t tp_oneshot_launch(const TpOneshotParams& p, cudaStream_t s) {
   if (p.tp > 32 || p.N % 8 || p.ld_src % 8 || p.ld_out % 8 || p.par_stride < (long long)p.M * p.N)
     return cudaErrorInvalidValue;
   const long long vecs = (long long)p.M * (p.N / 8);
-  // ~4 vectors per thread; every rank computes the same grid (same M, N)
-  const int grid = (int)std::min<long long>(kOneshotMaxCtas, (vecs + 4 * kOneshotThreads - 1) / (4 * kOneshotThreads));
+  // one 8-element vector per thread up to kOneshotMaxCtas CTAs (latency bound: spread the
+  // chunks); every rank computes the same grid (same M, N)
+  const int grid = (int)std::min<long long>(kOneshotMaxCtas, (vecs + kOneshotThreads - 1) / kOneshotThreads);
   SQ_LAUNCH(tp_oneshot_kernel, dim3(grid), dim3(kOneshotThreads), 0, s, 1, p);
   return cudaGetLastError();
 }

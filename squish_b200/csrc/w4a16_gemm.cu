@@ -457,7 +457,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       __syncwarp();
       r.next();
     }
-  } else if (warp == 2) {
+  } else if (warp == ((p.dbg & 8) ? 3 : 2)) {
     // ------------------------------------------------ MMA issuer
     constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
     Ring rx(ring_x), ra(ring_a);
