@@ -89,6 +89,10 @@ class EngineStats:
     # host seconds per phase of step(): schedule, build (step inputs), run (launches + the wait
     # for the device, the wait alone in runner.sync_wait_s), post (tokens, stops, blocks)
     host_s: dict = field(default_factory=lambda: {"schedule": 0.0, "build": 0.0, "run": 0.0, "post": 0.0})
+    # step wall-time histogram (seconds; cumulative counts per upper bound, Prometheus style)
+    step_buckets: tuple = (0.002, 0.005, 0.01, 0.02, 0.05, 0.1, 0.25, 1.0, float("inf"))
+    step_counts: list = field(default_factory=lambda: [0] * 9)
+    step_time_sum: float = 0.0
     instant_first_tokens: int = 0  # first tokens sampled from the prompt-logit cache
     evicted_pages: int = 0         # pages given back by the attention window
 
@@ -566,7 +570,13 @@ class LLMEngine:
             outs.extend(self._apply_verify(sched, st, now))
         if score:
             self._h2o_collect(sched)
-        hs["post"] += time.perf_counter() - t3
+        t4 = time.perf_counter()
+        hs["post"] += t4 - t3
+        dt = t4 - t0
+        self.stats.step_time_sum += dt
+        for i, b in enumerate(self.stats.step_buckets):
+            if dt <= b:
+                self.stats.step_counts[i] += 1
         if self.ecfg.kv_h2o_budget > 0:
             for e in sched.decode:
                 if e.req.status is Status.RUNNING:

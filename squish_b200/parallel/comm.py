@@ -50,11 +50,13 @@ class TPComm:
         self.device = device or (torch.device("cuda", torch.cuda.current_device()) if mode != "cpu"
                                  else torch.device("cpu"))
         self.max_tokens, self.hidden, self.max_rows, self.vocab = max_tokens, hidden, max_rows, vocab
+        self.link_bytes = 0  # host-side tally of collective payload bytes received by this rank
         v0, v1 = vocab_shard(vocab, self.rank, self.tp)
         self.v0, self.v1 = v0, v1
         self.per = vocab_shard(vocab, 0, self.tp)[1]  # padded shard width (ranks' shards all fit in it)
         self._ipc = []
         if mode in ("nvlink", "sp"):
+            self._check_peer_access()
             self._setup_peer()
             if mode == "sp":
                 self._setup_sp()
@@ -65,6 +67,19 @@ class TPComm:
             self.gath = torch.empty(self.tp * max_rows * self.per, dtype=self.tmp.dtype, device=self.device)
 
     # ------------------------------------------------------------------ NVLink peer memory
+    def _check_peer_access(self) -> None:
+        """Every rank must reach every peer's memory directly (NVLink / NVSwitch peer access);
+        all ranks agree before any IPC buffer is opened."""
+        n = torch.cuda.device_count()
+        me = self.device.index
+        ok = all(torch.cuda.can_device_access_peer(me, j) for j in range(n) if j != me) if n > 1 else True
+        flag = torch.tensor([0 if ok else 1], dtype=torch.int32, device=self.device)
+        dist.all_reduce(flag, group=self.group)
+        if int(flag.item()):
+            raise RuntimeError(f"tp_mode '{self.mode}' needs peer access between every pair of GPUs "
+                               "(NVLink / NVSwitch); use tp_mode 'nccl'")
+
+
     def _alloc_shared(self, nbytes: int) -> list[int]:
         """One IPC buffer per rank; returns every rank's device pointer (own first opened)."""
         ptr, handle = native().ipc_alloc(int(nbytes))
@@ -172,6 +187,7 @@ class TPComm:
         from ..ops import kernels as K
 
         R = self.sp_rows(T)
+        self.link_bytes += 2 * (self.tp - 1) * R * self.hidden * 2  # reduce-scatter in + all-gather in
         native().tp_rs_norm_ag(self.sp_recv, self.sp_rows_max * self.hidden, self.hidden, self.sp_rs_flags,
                                int(rs_expect), h, norm_w, float(eps), self.sp_ag_dst, self.hidden,
                                self.sp_ag_flag_ptrs, self.rank, self.tp, R, T, self.sp_seq, self.sp_done,
@@ -207,6 +223,7 @@ class TPComm:
         from ..ops import kernels as K
 
         T = x.shape[0]
+        self.link_bytes += (self.tp - 1) * T * h.shape[1] * 2  # peers' partials received by this rank
         if self.mode not in ("nvlink", "sp"):
             tmp = self.tmp[:T]
             if self.mode == "cpu":

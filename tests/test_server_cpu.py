@@ -32,6 +32,7 @@ def test_models_health_metrics(client):
     assert h["status"] == "ok" and h["model_loaded"]
     m = client.get("/v1/metrics").text
     assert "squish_requests_total" in m and "squish_paged_kv_free_blocks" in m
+    assert 'squish_step_seconds_bucket{gpu="cpu",le="+Inf"}' in m and "squish_step_seconds_sum" in m
     assert client.get("/readyz").json()["status"] == "ready"
 
 
