@@ -266,6 +266,12 @@ class TPComm:
             return
         if T > self.max_tokens or x.shape[1] != self.hidden:
             raise ValueError("all-reduce input exceeds the peer buffers")
+        self.link_bytes += (self.tp - 1) * T * self.hidden * 2
+        if T <= ONESHOT_MAX_TOKENS and x.dtype == torch.bfloat16 and x.stride(1) == 1:
+            native().tp_oneshot(x, self.os_part_ptrs, self.max_tokens * self.hidden, self.os_flag_ptrs, h, True,
+                                self.rank, self.tp, self.os_seq, self.os_done, self.status)
+            K._count()
+            return
         N, tile_m = x.shape[1], 64
         gx, gy = (N + 127) // 128, (T + tile_m - 1) // tile_m
         if gx * gy > self.max_tiles:
