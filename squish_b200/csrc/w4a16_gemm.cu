@@ -296,6 +296,18 @@ __device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, int* s
   if (fast && mbar_test(bar, parity)) return true;
   return mbar_wait(bar, parity, status, code);
 }
+// Wait of a role warp (producers, MMA issue) sharing its SM sub-partition with a dequant warp:
+// poll the non-blocking test and sleep between polls (bounded, then the ordinary bounded wait),
+// so the waiting warp takes almost no issue slots from the dequant warp.
+__device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, int* status, int code, bool nap) {
+  if (nap) {
+    for (int i = 0; i < (1 << 20); ++i) {
+      if (mbar_test(bar, parity)) return true;
+      __nanosleep(64);
+    }
+  }
+  return mbar_wait(bar, parity, status, code);
+}
 
 struct Ring {
   int s = 0;
@@ -335,6 +347,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
   const int xg = p.xg > 1 ? p.xg : 1;
   const int ag = (C::AT && p.ag > 1) ? p.ag : 1;  // k-blocks per tensor-memory A stage (one hand-off)
   const bool tw = (p.dbg & 4) != 0;  // test_wait before try_wait
+  const bool nap = (p.dbg & 16) != 0;  // role warps poll and sleep
   const uint32_t xstage = (uint32_t)(xg * C::kXBytes);
   const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a, p.trace != nullptr, C::AT, p.wfmt, wg, xg);
   uint8_t* a_ring = smem;  // (shared-memory A ring; with C::AT the region starts the X ring)
@@ -410,7 +423,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     const uint64_t pol = policy_evict_first();
     Ring r(ring_w);
     for (int i = 0; i < nkb; i += wg) {
-      if (!gemm_wait(&w_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_W, tw)) break;
+      if (!role_wait(&w_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_W, nap)) break;
       if (elect_one()) {
         // wg consecutive k-blocks of a 128-row block are contiguous (tile-major layout): one copy
         const int cnt = min(wg, nkb - i);
@@ -445,7 +458,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     __syncwarp();
     Ring r(ring_x);
     for (int i = 0; i < nkb; i += xg) {
-      if (!gemm_wait(&x_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_X, tw)) break;
+      if (!role_wait(&x_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_X, nap)) break;
       if (elect_one()) {
         mbar_expect_tx(&x_full[r.s], xstage);  // (a 3-D box always transfers all xg k-blocks)
         if (xg > 1)  // 3-D map {64 columns, rows, k-block}: xg consecutive k-blocks in one load
@@ -463,10 +476,10 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     Ring rx(ring_x), ra(ring_a);
     for (int i = 0; i < nkb; ++i) {
       const int xsub = i % xg;
-      if (xsub == 0 && !gemm_wait(&x_full[rx.s], rx.ph, status, SQ_ERR_TIMEOUT_X, tw)) break;
+      if (xsub == 0 && !role_wait(&x_full[rx.s], rx.ph, status, SQ_ERR_TIMEOUT_X, nap)) break;
       if (lane == 0) trace_mark(str, 2, i);
       const int asub = i % ag;
-      if (asub == 0 && !gemm_wait(&a_full[ra.s], ra.ph, status, SQ_ERR_TIMEOUT_A, tw)) break;
+      if (asub == 0 && !role_wait(&a_full[ra.s], ra.ph, status, SQ_ERR_TIMEOUT_A, nap)) break;
       if (lane == 0) trace_mark(str, 3, i);
       tc_fence_after();
       if (elect_one()) {

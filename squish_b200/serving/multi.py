@@ -72,6 +72,12 @@ class _AggStats:
 
     def __getattr__(self, name):
         vals = [getattr(e.stats, name) for e in self.engines]
+        if name == "step_counts":  # histogram bins: element-wise
+            return [sum(c) for c in zip(*vals)]
+        if isinstance(vals[0], tuple):  # bin bounds: the same on every replica
+            return vals[0]
+        if isinstance(vals[0], dict):
+            return {k: sum(v[k] for v in vals) for k in vals[0]}
         if isinstance(vals[0], list):
             return [v for part in vals for v in part]
         return sum(vals)

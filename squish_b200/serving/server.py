@@ -262,7 +262,8 @@ def create_app(st: ServerState) -> FastAPI:
         m("squish_engine_steps_total", "counter", "Engine iterations", stats.steps)
         m("squish_preemptions_total", "counter", "Requests preempted for KV capacity", stats.preemptions)
         m("squish_errors_total", "counter", "Engine step failures", a.errors_total)
-        gpu = getattr(getattr(eng.runner, "device", None), "index", None)
+        runner = getattr(eng, "runner", None)  # (a data-parallel router view has none)
+        gpu = getattr(getattr(runner, "device", None), "index", None)
         lab = f'gpu="{gpu if gpu is not None else "cpu"}"'
         lines.extend(["# HELP squish_step_seconds Engine step wall time", "# TYPE squish_step_seconds histogram"])
         for b, c in zip(stats.step_buckets, stats.step_counts):
@@ -270,7 +271,7 @@ def create_app(st: ServerState) -> FastAPI:
             lines.append(f'squish_step_seconds_bucket{{{lab},le="{le}"}} {c}')
         lines.append(f"squish_step_seconds_sum{{{lab}}} {stats.step_time_sum:.6f}")
         lines.append(f"squish_step_seconds_count{{{lab}}} {stats.step_counts[-1]}")
-        comm = getattr(eng.runner, "comm", None)
+        comm = getattr(runner, "comm", None)
         if comm is not None:
             m("squish_tp_link_bytes_total", "counter", "Tensor-parallel collective payload bytes received by this rank",
               comm.link_bytes)
