@@ -290,25 +290,6 @@ __device__ __forceinline__ void cluster_sync() {
 }
 
 // ring position: stage index and phase parity, advanced without division
-// Bounded wait, testing the phase once with the non-blocking test_wait first when `fast` (a
-// phase completed long ago then costs one test instead of a potentially suspending try_wait).
-__device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, int* status, int code, bool fast) {
-  if (fast && mbar_test(bar, parity)) return true;
-  return mbar_wait(bar, parity, status, code);
-}
-// Wait of a role warp (producers, MMA issue) sharing its SM sub-partition with a dequant warp:
-// poll the non-blocking test and sleep between polls (bounded, then the ordinary bounded wait),
-// so the waiting warp takes almost no issue slots from the dequant warp.
-__device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, int* status, int code, bool nap) {
-  if (nap) {
-    for (int i = 0; i < (1 << 20); ++i) {
-      if (mbar_test(bar, parity)) return true;
-      __nanosleep(64);
-    }
-  }
-  return mbar_wait(bar, parity, status, code);
-}
-
 struct Ring {
   int s = 0;
   uint32_t ph = 0;
@@ -346,8 +327,6 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
   const int wg = p.wg > 1 ? p.wg : 1;
   const int xg = p.xg > 1 ? p.xg : 1;
   const int ag = (C::AT && p.ag > 1) ? p.ag : 1;  // k-blocks per tensor-memory A stage (one hand-off)
-  const bool tw = (p.dbg & 4) != 0;  // test_wait before try_wait
-  const bool nap = (p.dbg & 16) != 0;  // role warps poll and sleep
   const uint32_t xstage = (uint32_t)(xg * C::kXBytes);
   const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a, p.trace != nullptr, C::AT, p.wfmt, wg, xg);
   uint8_t* a_ring = smem;  // (shared-memory A ring; with C::AT the region starts the X ring)
@@ -423,7 +402,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     const uint64_t pol = policy_evict_first();
     Ring r(ring_w);
     for (int i = 0; i < nkb; i += wg) {
-      if (!role_wait(&w_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_W, nap)) break;
+      if (!mbar_wait(&w_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_W)) break;
       if (elect_one()) {
         // wg consecutive k-blocks of a 128-row block are contiguous (tile-major layout): one copy
         const int cnt = min(wg, nkb - i);
@@ -458,7 +437,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     __syncwarp();
     Ring r(ring_x);
     for (int i = 0; i < nkb; i += xg) {
-      if (!role_wait(&x_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_X, nap)) break;
+      if (!mbar_wait(&x_empty[r.s], r.ph ^ 1u, status, SQ_ERR_TIMEOUT_X)) break;
       if (elect_one()) {
         mbar_expect_tx(&x_full[r.s], xstage);  // (a 3-D box always transfers all xg k-blocks)
         if (xg > 1)  // 3-D map {64 columns, rows, k-block}: xg consecutive k-blocks in one load
@@ -470,16 +449,16 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       __syncwarp();
       r.next();
     }
-  } else if (warp == ((p.dbg & 8) ? 3 : 2)) {
+  } else if (warp == 2) {
     // ------------------------------------------------ MMA issuer
     constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
     Ring rx(ring_x), ra(ring_a);
     for (int i = 0; i < nkb; ++i) {
       const int xsub = i % xg;
-      if (xsub == 0 && !role_wait(&x_full[rx.s], rx.ph, status, SQ_ERR_TIMEOUT_X, nap)) break;
+      if (xsub == 0 && !mbar_wait(&x_full[rx.s], rx.ph, status, SQ_ERR_TIMEOUT_X)) break;
       if (lane == 0) trace_mark(str, 2, i);
       const int asub = i % ag;
-      if (asub == 0 && !role_wait(&a_full[ra.s], ra.ph, status, SQ_ERR_TIMEOUT_A, nap)) break;
+      if (asub == 0 && !mbar_wait(&a_full[ra.s], ra.ph, status, SQ_ERR_TIMEOUT_A)) break;
       if (lane == 0) trace_mark(str, 3, i);
       tc_fence_after();
       if (elect_one()) {
@@ -523,7 +502,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
     // Dequantize the next raw weight stage into o (waits for it, releases it); false on timeout.
     auto dq_stage = [&](int i, uint4 (&o)[NT][WPT]) -> bool {
       const int wsub = i % wg;
-      if (wsub == 0 && !gemm_wait(&w_full[rw.s], rw.ph, status, SQ_ERR_TIMEOUT_W, tw)) return false;
+      if (wsub == 0 && !mbar_wait(&w_full[rw.s], rw.ph, status, SQ_ERR_TIMEOUT_W)) return false;
       if (d == 0) trace_mark(str, 4, i);
       const uint8_t* wst = w_ring + rw.s * L.w_stage;
 #pragma unroll
@@ -611,7 +590,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         if (!dq_stage(i, o)) break;
         const int asub = i % ag;
         const bool alast = asub == ag - 1 || i == nkb - 1;
-        if (asub == 0 && !gemm_wait(&a_empty[ra.s], ra.ph ^ 1u, status, SQ_ERR_TIMEOUT_A, tw)) break;
+        if (asub == 0 && !mbar_wait(&a_empty[ra.s], ra.ph ^ 1u, status, SQ_ERR_TIMEOUT_A)) break;
         if (d == 0) trace_mark(str, 5, i);
         if constexpr (C::AT) {
           if (asub == 0) tc_fence_after();
