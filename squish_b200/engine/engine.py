@@ -71,6 +71,10 @@ class EngineConfig:
     # kv_h2o_interval decode steps (those steps run outside CUDA graphs). 0 = off.
     kv_h2o_budget: int = 0
     kv_h2o_interval: int = 4
+    # > 1: the decoder layers split over this many GPUs of this process (cuda:i .. cuda:i+pp-1,
+    # from the engine's device), hidden states passed device to device; steps run eagerly
+    pp: int = 1
+    pp_devices: tuple | None = None  # explicit stage devices (default: consecutive GPUs)
 
 
 @dataclass
@@ -192,6 +196,8 @@ class LLMEngine:
             if ecfg.kv_h2o_budget > 0:
                 raise ValueError("heavy-hitter KV eviction runs on one GPU per engine (use --dp for more GPUs)")
             return cls._from_checkpoint_tp(ck, dev, ecfg)
+        if dev.type == "cuda" and ecfg.pp > 1:
+            return cls._from_checkpoint_layer_split(ck, dev, ecfg)
         if dev.type == "cuda":
             from ..models.decoder import CudaRunner
 
@@ -221,6 +227,40 @@ class LLMEngine:
             eng.proposer = make_proposer(ecfg.spec, eng)
             eng.guard = _Guard(ecfg.spec.miss_limit, ecfg.spec.cooldown) if ecfg.spec.adaptive else None
         return eng
+
+    @classmethod
+    def _from_checkpoint_layer_split(cls, ck: Checkpoint, dev: torch.device, ecfg: EngineConfig) -> "LLMEngine":
+        """Layer-split engine: the layers over ecfg.pp GPUs of this process (the pool of every
+        stage has the same page count; each stage holds only its layers' pages)."""
+        import dataclasses
+
+        from ..kv.paged import KVPools
+        from ..models.decoder import LayerSplitRunner
+
+        if ecfg.spec is not None or ecfg.kv_h2o_budget > 0 or ecfg.kv_host_bytes > 0 or ecfg.kv_disk_dir:
+            raise ValueError("the layer split serves plain decoding (no speculation, H2O eviction or KV tiers)")
+        base = dev.index or 0
+        devs = ([torch.device(d) for d in ecfg.pp_devices] if ecfg.pp_devices else
+                [torch.device("cuda", base + i) for i in range(ecfg.pp)])
+        runner = LayerSplitRunner(ck, devs, 1, max_num_tokens=ecfg.max_num_batched_tokens,
+                                  max_num_seqs=ecfg.max_num_seqs, max_model_len=ecfg.max_model_len,
+                                  prefill_weight_cache=ecfg.prefill_weight_cache)
+        for st_ in runner.stages:
+            del st_.pools
+        torch.cuda.empty_cache()
+        if ecfg.num_pages:
+            num_pages = ecfg.num_pages
+        else:  # the tightest stage decides (its layers' bytes per page against its free memory)
+            num_pages = None
+            for st_, d in zip(runner.stages, devs):
+                free, total = torch.cuda.mem_get_info(d)
+                per = bytes_per_page(st_.cfg, ck.quant)
+                n = int((free - (1.0 - ecfg.gpu_memory_utilization) * total) // per)
+                num_pages = n if num_pages is None else min(num_pages, n)
+            num_pages = max(16, num_pages)
+        for st_, d in zip(runner.stages, devs):
+            st_.pools = KVPools(st_.cfg, ck.quant, num_pages, d)
+        return cls(runner, ck.config, ck.quant, dataclasses.replace(ecfg, cuda_graphs=False), num_pages)
 
     @classmethod
     def _from_checkpoint_tp(cls, ck: Checkpoint, dev: torch.device, ecfg: EngineConfig) -> "LLMEngine":

@@ -376,12 +376,26 @@ class CudaRunner:
         return d
 
     # ------------------------------------------------------------------ forward
+    # layer split: a callable(st, T) that runs the earlier stages and leaves the hidden state of
+    # the step's T tokens in self.h[:T] (set by LayerSplitRunner), instead of the embedding
+    upstream = None
+
     def forward(self, st: StepInputs, m: dict) -> torch.Tensor:
+        self.run_layers(st, m)
+        B = st.logits_rows.shape[0]
+        xs = ops.rmsnorm(self.h[:st.num_tokens], self.norm, self.cfg.rms_eps, out=self.xs[:B], row_idx=m["rows"])
+        return self._lm_head(xs, B)
+
+    def run_layers(self, st: StepInputs, m: dict) -> None:
+        """Embedding (or the upstream stages) and this runner's decoder layers, in place on self.h."""
         cfg = self.cfg
         T, Bd = st.num_tokens, st.num_decode
         ws = self.ws
         h, x = self.h[:T], self.x[:T]
-        torch.index_select(self.embed, 0, m["ids"], out=h)
+        if self.upstream is not None:
+            self.upstream(st, T)
+        else:
+            torch.index_select(self.embed, 0, m["ids"], out=h)
         hkv = cfg.num_kv_heads
         dsplit = ops.kernels.decode_splits(max(Bd, 1), hkv, max(st.max_decode_ctx, 1)) if Bd else (1, 1)
         for li, lw in enumerate(self.layers):
@@ -395,9 +409,6 @@ class CudaRunner:
             else:
                 act = ops.w4a16_linear(x, lw.gate_up, out=self.act[:T], silu_mul=True, ws=ws)
                 self._row_parallel(act[:, : self.F], lw.down, h)
-        B = st.logits_rows.shape[0]
-        xs = ops.rmsnorm(h, self.norm, cfg.rms_eps, out=self.xs[:B], row_idx=m["rows"])
-        return self._lm_head(xs, B)
 
     def _attention(self, li: int, lw, qkv: torch.Tensor, st: StepInputs, m: dict, dsplit) -> torch.Tensor:
         """RoPE + KV write, then decode and prefill attention of layer li over the paged cache."""
@@ -556,6 +567,81 @@ class CudaRunner:
 
 
 # ----------------------------------------------------------------------------- CPU oracle of the step
+def layer_slice(ck: Checkpoint, a: int, b: int) -> Checkpoint:
+    """The checkpoint of decoder layers [a, b) (renumbered from 0) plus the embedding, final norm
+    and LM head (tensors shared, not copied)."""
+    import dataclasses
+
+    pre = "model.layers."
+    tensors = {}
+    for k, v in ck.tensors.items():
+        if not k.startswith(pre):
+            tensors[k] = v
+            continue
+        i, rest = k[len(pre):].split(".", 1)
+        if a <= int(i) < b:
+            tensors[f"{pre}{int(i) - a}.{rest}"] = v
+    return Checkpoint(dataclasses.replace(ck.config, num_layers=b - a), ck.quant, tensors)
+
+
+class LayerSplitRunner:
+    """The decoder layers split in contiguous ranges over several GPUs of one process, the
+    reference's only multi-device mode (HF ``device_map="auto"``, squish/backend.py:295): stage
+    i holds layers [b_i, b_i+1) and their KV pages on its device, the hidden state of the
+    step's tokens moves to the next device once per stage, and the last stage applies the final
+    norm, the LM head and the sampler. Every stage keeps its own copy of the embedding and
+    head tensors (only the first / last use them). The engine talks to the last stage; steps
+    run eagerly (no CUDA graphs)."""
+
+    def __init__(self, ck: Checkpoint, devices: list, num_pages: int, **kw):
+        L, S = ck.config.num_layers, len(devices)
+        if S < 2 or S > L:
+            raise ValueError(f"layer split needs 2..{L} stages, got {S}")
+        bounds = [round(i * L / S) for i in range(S + 1)]
+        self.bounds = bounds
+        self.stages = [CudaRunner(layer_slice(ck, bounds[i], bounds[i + 1]), d, num_pages, **kw)
+                       for i, d in enumerate(devices)]
+        self.cfg = ck.config
+        for k in range(1, S):
+            self.stages[k].upstream = self._feeder(k)
+
+    def _feeder(self, k: int):
+        def run(st: StepInputs, T: int) -> None:
+            prev, cur = self.stages[k - 1], self.stages[k]
+            prev.run_layers(st, prev.upload(st))
+            # (a cross-device copy is ordered after the source device's current stream)
+            cur.h[:T].copy_(prev.h[:T], non_blocking=True)
+        return run
+
+    @property
+    def last(self) -> CudaRunner:
+        return self.stages[-1]
+
+    _own = ("stages", "bounds", "cfg")
+
+    def __getattr__(self, name):  # the engine-facing surface is the last stage's
+        if name in LayerSplitRunner._own:
+            raise AttributeError(name)
+        return getattr(self.stages[-1], name)
+
+    def __setattr__(self, name, value):
+        if name in LayerSplitRunner._own:
+            object.__setattr__(self, name, value)
+        else:
+            setattr(self.stages[-1], name, value)
+
+    @property
+    def pools_all(self) -> list:
+        return [s.pools for s in self.stages]
+
+    def execute(self, st: StepInputs) -> np.ndarray:
+        return self.last.execute(st)
+
+    def kv_compact(self, src, dst) -> None:
+        for s in self.stages:
+            s.kv_compact(src, dst)
+
+
 class TorchPagedRunner:
     """The same step semantics as CudaRunner in plain PyTorch on the CPU (fp32)."""
 

@@ -211,3 +211,15 @@ def test_heavy_hitter_eviction_keeps_budget_and_matches_oracle(tiny):
     ref = ReferenceModel(tiny)
     ref.kv_visible = eviction_log_rule(r)
     assert r.output == ref.greedy(p, 90)[0]
+
+
+def test_layer_slice_renumbers_layers_and_shares_tensors(tiny):
+    from squish_b200.models.decoder import layer_slice
+
+    part = layer_slice(tiny, 1, 3)
+    assert part.config.num_layers == 2 and part.quant is tiny.quant
+    assert "model.layers.0.self_attn.q_proj.weight" in part.tensors and "model.layers.2.mlp.up_proj.weight" not in part
+    assert part.tensors["model.layers.1.mlp.down_proj.weight"] is tiny.tensors["model.layers.2.mlp.down_proj.weight"]
+    assert part.tensors["model.embed_tokens.weight"] is tiny.tensors["model.embed_tokens.weight"]
+    n_layer = sum(k.startswith("model.layers.") for k in tiny.tensors) // tiny.config.num_layers
+    assert sum(k.startswith("model.layers.") for k in part.tensors) == 2 * n_layer

@@ -236,6 +236,23 @@ def test_prewarmed_graphs_replay_without_capture(cuda):
     assert got == ref.generate(prompts, SamplingParams(max_tokens=20, ignore_eos=True))
 
 
+def test_layer_split_engine_matches_single_gpu(cuda):
+    """Layers split in two stages (both on this GPU when only one is present: the same code
+    path as two GPUs, the hand-off becomes a same-device copy): the same tokens as the
+    one-stage engine, greedy, with chunked prefill."""
+    cfg, q = get_preset("tiny-llama")
+    prompts = [_prompt(70 + i, 25 + 30 * i, cfg.vocab_size) for i in range(3)]
+    ecfg = EngineConfig(max_num_seqs=4, max_num_batched_tokens=64, max_model_len=512, num_pages=64, cuda_graphs=False)
+    one = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda, ecfg)
+    want = one.generate(prompts, SamplingParams(max_tokens=16, ignore_eos=True))
+    devs = ("cuda:0", "cuda:1") if torch.cuda.device_count() > 1 else ("cuda:0", "cuda:0")
+    split = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
+                                      dataclasses.replace(ecfg, pp=2, pp_devices=devs))
+    assert len(split.runner.stages) == 2 and split.runner.bounds == [0, 2, 4]
+    assert split.generate(prompts, SamplingParams(max_tokens=16, ignore_eos=True)) == want
+    split.runner.ws.check()
+
+
 def test_sampled_decoding_runs_in_graphs(cuda):
     cfg, q = get_preset("tiny-llama")
     eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,

@@ -52,6 +52,7 @@ def test_flags_build_the_engine_config():
     e = _ecfg(_args("--kv-sink-tokens", "4", "--kv-window-tokens", "256", "--prompt-logit-cache", "0"))
     assert (e.kv_sink_tokens, e.kv_window_tokens, e.prompt_logit_cache) == (4, 256, 0)
     assert _ecfg(_args()).prompt_logit_cache > 0
+    assert _ecfg(_args("--pp", "2")).pp == 2
 
 
 def _client(*extra):
