@@ -647,9 +647,12 @@ def run_reference(args, world, rank, local):
     wait_tokens(C * warm)
     per_step, = reduce([(time.perf_counter() - t_start) / max(warm, 1)], "max", world)
     steps = min(args.steps, max(3, int(args.ref_budget_s / max(per_step, 1e-3))))
+    clocks = ClockSampler(local, args.clocks != "0")
+    clocks.start()
     w0 = time.perf_counter()
     wait_tokens(C * (warm + steps))
     wall = time.perf_counter() - w0
+    clk = clocks.stop()
     failed = [f for f in fins if f not in ("length", "stop")]
     bad, = reduce([1.0 if failed else 0.0], "max", world)
     if bad:
@@ -684,6 +687,7 @@ def run_reference(args, world, rank, local):
                       f"--ref-budget-s {args.ref_budget_s:.0f}",
             "host_allocator": "glibc: one arena, no mmap, no trim (freed logit pages reused)" if malloc_tuned
             else "default",
+            "clocks": clk,
             "impl": "reference"}
 
 
