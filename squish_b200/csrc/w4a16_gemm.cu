@@ -60,7 +60,9 @@ struct Cfg {
   static constexpr bool AT = (NT == 1) && !ASMEM_;
   static constexpr int kA0 = AT ? (NT * BN < 32 ? 32 : NT * BN) : 0;
   // CTAs per SM share 512 TMEM columns: 3+ -> 2 A stages, 2 -> 4, one CTA -> what is left (<= 12)
-  static constexpr int kMaxRingA = MINB_ >= 3 ? 2 : MINB_ == 2 ? 4 : ((512 - kA0) / 32 < 12 ? (512 - kA0) / 32 : 12);
+  // (two CTAs: the A stages fill the 256 columns each CTA allocates anyway, 6 for 64 tokens)
+  static constexpr int kMaxRingA = MINB_ >= 3 ? 2 : MINB_ == 2 ? ((256 - kA0) / 32 > 4 ? (256 - kA0) / 32 : 4)
+                                                     : ((512 - kA0) / 32 < 12 ? (512 - kA0) / 32 : 12);
   static constexpr int kCols = AT ? kA0 + 32 * kMaxRingA : NT * BN;
   static constexpr int kTmemCols = (kCols <= 32) ? 32 : (kCols <= 64) ? 64 : (kCols <= 128) ? 128 : (kCols <= 256) ? 256 : 512;
   // static shared table for NF4 levels / AQLM codebooks: only the 8-dequant-warp configurations
@@ -895,7 +897,11 @@ cudaError_t launch_decode_narrow(const CUtensorMap& xmap, W4A16Params p, cudaStr
   p.wg = wg_env;
   if (per_sm <= 2) {
     p.ag = ag_env;
-    const int ra = std::max(1, 4 / p.ag);
+    static const int ra_env = [] {  // A k-blocks in flight (SQ_GEMM_RA overrides; <= the TMEM room)
+      const char* e = std::getenv("SQ_GEMM_RA");
+      return e != nullptr ? std::atoi(e) : 4;
+    }();
+    const int ra = std::max(1, std::min(ra_env, Cfg<BN, 1, 2, 4>::kMaxRingA) / p.ag);
     const int rx = rx_env >= 2 && rx_env <= 16 ? rx_env : std::max(2, (BN >= 32 ? 4 : 6) / xg);
     return launch_cfg<Cfg<BN, 1, 2, 4>>(xmap, p, fit(rx, ra, p.wg, 112 * 1024, std::max(2, 4 / p.wg), 24 / p.wg + 1),
                                         rx, ra, s);
