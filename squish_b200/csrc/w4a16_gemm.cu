@@ -329,8 +329,6 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
   const int wg = p.wg > 1 ? p.wg : 1;
   const int xg = p.xg > 1 ? p.xg : 1;
   const int ag = (C::AT && p.ag > 1) ? p.ag : 1;  // k-blocks per tensor-memory A stage (one hand-off)
-  // the dequant warp that completes an A stage issues its MMAs (no separate MMA warp)
-  const bool inline_mma = C::AT && p.inline_mma != 0 && ring_a <= 16;
   const uint32_t xstage = (uint32_t)(xg * C::kXBytes);
   const Layout L = make_layout(BN, NT, gpk, ring_w, ring_x, ring_a, p.trace != nullptr, C::AT, p.wfmt, wg, xg);
   uint8_t* a_ring = smem;  // (shared-memory A ring; with C::AT the region starts the X ring)
@@ -381,17 +379,6 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
   }
   // format table: NF4 (level[q0], level[q1]) bf16 pairs, or the AQLM codebooks (<= 2 x 256 x 8 bf16)
   __shared__ uint4 fmt_tab[C::kFmtTab];
-  // inline MMA issue (p.inline_mma, A in TMEM): per A-ring slot arrival counts of the dequant
-  // warps, the next A stage to issue, the activation ring position of the issuers
-  __shared__ int il_cnt[16];
-  __shared__ volatile int il_next;
-  __shared__ int il_xs, il_xph;
-  if (threadIdx.x < 16) il_cnt[threadIdx.x] = 0;
-  if (threadIdx.x == 0) {
-    il_next = 0;
-    il_xs = 0;
-    il_xph = 0;
-  }
   uint32_t* nf4_lut = reinterpret_cast<uint32_t*>(fmt_tab);
   if constexpr (C::kFmtTab >= 512) {
     if (p.wfmt == WF_NF4) {
@@ -464,7 +451,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
       __syncwarp();
       r.next();
     }
-  } else if (warp == 2 && !inline_mma) {
+  } else if (warp == 2) {
     // ------------------------------------------------ MMA issuer
     constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
     Ring rx(ring_x), ra(ring_a);
@@ -599,55 +586,6 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
         tmem_st8(col, regs);
       }
     };
-    // Inline issue of A stage starting at k-block g0 (slot s, phase ph): by the warp whose
-    // arrival completed the stage, in stage order (bounded wait for the previous issuer).
-    auto issue_stage = [&](int g0, int s, uint32_t ph) -> bool {
-      const int g = g0 / ag;
-      for (long long it = 0; il_next != g; ++it) {
-        if (it > (1LL << 24) || *reinterpret_cast<volatile int*>(status) != 0) {
-          atomicCAS(status, 0, SQ_ERR_TIMEOUT_A);
-          return false;
-        }
-      }
-      if (lane == 0) il_cnt[s] = 0;  // (every arrival of this stage is in; the slot's next use follows a_empty)
-      if (!mbar_wait(&a_full[s], ph, status, SQ_ERR_TIMEOUT_A)) return false;  // (complete: the sync point)
-      tc_fence_after();
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
-      int xs = il_xs;
-      uint32_t xph = (uint32_t)il_xph;
-      const int g1 = min(nkb, g0 + ag);
-      for (int j = g0; j < g1; ++j) {
-        const int xsub = j % xg;
-        if (xsub == 0 && !mbar_wait(&x_full[xs], xph, status, SQ_ERR_TIMEOUT_X)) return false;
-        tc_fence_after();
-        if (elect_one()) {
-          const uint32_t xa = smem_u32(x_ring + xs * xstage + xsub * C::kXBytes);
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_bf16_ts(tmem, tmem + (uint32_t)(C::kA0 + (s * ag + (j - g0)) * 32 + k * 8), sdesc_sw128(xa + k * 32),
-                        idesc, (j > 0 || k > 0) ? 1u : 0u);
-          if (xsub == xg - 1 || j == nkb - 1) mma_commit(&x_empty[xs]);
-          if (j == g1 - 1) mma_commit(&a_empty[s]);
-          if (j == nkb - 1) mma_commit(acc_full);
-          trace_mark(str, 12, j);
-        }
-        __syncwarp();
-        if (xsub == xg - 1 || j == nkb - 1) {
-          if (++xs == ring_x) {
-            xs = 0;
-            xph ^= 1u;
-          }
-        }
-      }
-      if (lane == 0) {
-        il_xs = xs;
-        il_xph = (int)xph;
-        __threadfence_block();
-        il_next = g + 1;
-      }
-      __syncwarp();
-      return true;
-    };
     {
       for (int i = 0; i < nkb; ++i) {
         uint4 o[NT][WPT];
@@ -677,14 +615,6 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
           __syncwarp();
           if (lane == 0) mbar_arrive(&a_full[ra.s]);
           if (lane == 0 && warp < 8) trace_mark(str, 4 + warp, i);  // trace slots 8-11: each warp's hand-off
-          if constexpr (C::AT) {
-            if (inline_mma) {
-              int prev = 0;
-              if (lane == 0) prev = atomicAdd(&il_cnt[ra.s], 1);
-              prev = __shfl_sync(0xffffffffu, prev, 0);
-              if (prev == C::kDqWarps - 1 && !issue_stage(i - asub, ra.s, ra.ph)) break;
-            }
-          }
           ra.next();
         }
         if (d == 0) trace_mark(str, 6, i);
@@ -960,11 +890,6 @@ cudaError_t launch_decode_narrow(const CUtensorMap& xmap, W4A16Params p, cudaStr
     const char* e = std::getenv("SQ_GEMM_RX");
     return e != nullptr ? std::atoi(e) : 0;
   }();
-  static const int inline_env = [] {  // experiment: dequant warps issue the MMAs (SQ_GEMM_INLINE=1)
-    const char* e = std::getenv("SQ_GEMM_INLINE");
-    return e != nullptr && e[0] == '1' ? 1 : 0;
-  }();
-  p.inline_mma = inline_env;
   static const int ag_env = [] {  // k-blocks per A stage hand-off (SQ_GEMM_AG overrides)
     const char* e = std::getenv("SQ_GEMM_AG");
     return e != nullptr ? std::max(1, std::min(4, std::atoi(e))) : 2;  // (measured 47.2 -> 45.8 us gate_up)
@@ -996,7 +921,6 @@ cudaError_t w4a16_gemm_launch(const CUtensorMap& xmap, const W4A16Params& p0, in
   p.dbg = dbg_env;
   p.wg = 1;  // (the decode configuration groups weight copies and A stages)
   p.ag = 1;
-  p.inline_mma = 0;
   int ow, ox, oa;
   const bool ov = ring_override(&ow, &ox, &oa);
   if (nt == 1) {

@@ -75,8 +75,6 @@ struct W4A16Params {
   int wg, xg;
   // k-blocks per tensor-memory A stage (one dequant -> MMA hand-off), set by the launcher
   int ag;
-  // the dequant warp whose arrival completes an A stage issues its MMAs (no MMA warp)
-  int inline_mma;
 };
 
 // True when token tiles of <= 64 run the 4-dequant-warp configuration (four CTAs per SM):
