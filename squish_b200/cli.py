@@ -73,6 +73,8 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
     p.add_argument("--spec-branches", type=int, default=1, help="prompt lookup: continuations per draft tree")
     # multi-GPU
     p.add_argument("--tp", type=int, default=1, help="tensor-parallel GPUs (one process per GPU over NVLink)")
+    p.add_argument("--offload-layers", type=int, default=0,
+                   help="keep the last N layers' weights in host memory, streamed to the GPU each step")
     p.add_argument("--pp", type=int, default=1,
                    help="split the layers over this many GPUs of one process (layer-split fallback)")
     p.add_argument("--ep", type=int, default=0,
@@ -125,7 +127,7 @@ def _ecfg(a):
                         chunk_align=a.chunk_align, seed=a.seed, kv_host_bytes=int(a.kv_host_gb * (1 << 30)),
                         kv_disk_dir=a.kv_disk_dir, spec=_spec(a), tp=tp, tp_mode=getattr(a, "tp_mode", "nvlink"),
                         prompt_logit_cache=a.prompt_logit_cache, kv_sink_tokens=a.kv_sink_tokens,
-                        kv_window_tokens=a.kv_window_tokens, pp=a.pp)
+                        kv_window_tokens=a.kv_window_tokens, pp=a.pp, offload_layers=a.offload_layers)
 
 
 def _kv(a):

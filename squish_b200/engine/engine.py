@@ -74,6 +74,9 @@ class EngineConfig:
     # > 1: the decoder layers split over this many GPUs of this process (cuda:i .. cuda:i+pp-1,
     # from the engine's device), hidden states passed device to device; steps run eagerly
     pp: int = 1
+    # > 0: the quantized weights of the last N decoder layers stay in pinned host memory and
+    # stream to the GPU one layer ahead of use (models larger than HBM); steps run eagerly
+    offload_layers: int = 0
     pp_devices: tuple | None = None  # explicit stage devices (default: consecutive GPUs)
 
 
@@ -206,7 +209,12 @@ class LLMEngine:
             runner = CudaRunner(ck, dev, num_pages=1, max_num_tokens=ecfg.max_num_batched_tokens,
                                 max_num_seqs=ecfg.max_num_seqs, max_model_len=ecfg.max_model_len,
                                 free_checkpoint=True, spec_rows=spec_rows,
-                                prefill_weight_cache=ecfg.prefill_weight_cache)
+                                prefill_weight_cache=ecfg.prefill_weight_cache and not ecfg.offload_layers,
+                                offload_layers=ecfg.offload_layers)
+            if ecfg.offload_layers:
+                import dataclasses
+
+                ecfg = dataclasses.replace(ecfg, cuda_graphs=False)  # (side-stream copies each step)
             del runner.pools
             torch.cuda.empty_cache()
             num_pages = cls.plan_pages(ck.config, ck.quant, ecfg, dev)

@@ -206,7 +206,7 @@ class CudaRunner:
 
     def __init__(self, ck: Checkpoint, device, num_pages: int, max_num_tokens: int = 4096, max_num_seqs: int = 256,
                  max_model_len: int = 4096, pools: KVPools | None = None, free_checkpoint: bool = False,
-                 spec_rows: int = 0, prefill_weight_cache: bool = False):
+                 spec_rows: int = 0, prefill_weight_cache: bool = False, offload_layers: int = 0):
         self.cfg: ModelConfig = ck.config
         self.qcfg: QuantConfig = ck.quant
         self.device = torch.device(device)
@@ -267,7 +267,62 @@ class CudaRunner:
             sk, sv = ops.kernels.kv_hadamard_signs(cfg.head_dim)
             self.had_k, self.had_v = sk.to(dev), sv.to(dev)
             self.had_v_row = sv.repeat(cfg.num_heads).to(dev)  # un-rotation of the [T, Hq * D] output
+        self.offload = None
+        if offload_layers > 0:
+            self._offload_setup(offload_layers)
         self._alloc_buffers()
+
+    # ------------------------------------------------------------------ weight offload
+    _OFF_NAMES = ("qkv", "o", "gate_up", "down")
+
+    def _offload_setup(self, n: int) -> None:
+        """Keep the quantized weights of the last ``n`` layers in pinned host memory and stream
+        each one into one of two device staging sets just ahead of its use (a copy stream,
+        events both ways), so a model larger than HBM runs with only two layers' weights
+        resident for those layers. The reference pages layers between tiers with numpy copies
+        (squish/io/split_loader.py, squish/io/model_shard_loader.py)."""
+        import dataclasses
+
+        if any(lw.moe is not None for lw in self.layers):
+            raise ValueError("weight offload covers dense decoder layers")
+        L = len(self.layers)
+        n = min(n, L)
+        first = L - n
+        host, staged = {}, [{}, {}]
+        for li in range(first, L):
+            lw = self.layers[li]
+            host[li] = {}
+            for name in self._OFF_NAMES:
+                w = getattr(lw, name)
+                if w.dense is not None or w.rot is not None:
+                    raise ValueError("offloaded layers stream their quantized codes only")
+                host[li][name] = w.wq.to("cpu").pin_memory()
+                for b in range(min(2, n)):
+                    if name not in staged[b]:
+                        staged[b][name] = torch.empty_like(w.wq)
+        for k, li in enumerate(range(first, L)):
+            lw = self.layers[li]
+            for name in self._OFF_NAMES:
+                setattr(lw, name, dataclasses.replace(getattr(lw, name), wq=staged[k % 2][name]))
+        torch.cuda.empty_cache()
+        self.offload = {"first": first, "host": host, "staged": staged, "stream": torch.cuda.Stream(self.device),
+                        "copied": [torch.cuda.Event(), torch.cuda.Event()],
+                        "done": [torch.cuda.Event(), torch.cuda.Event()]}
+
+    def _offload_fetch(self, li: int) -> None:
+        """Queue the copy of offloaded layer li into its staging set, after the layer that last
+        used that set has finished."""
+        o = self.offload
+        b = (li - o["first"]) % 2
+        cs = o["stream"]
+        if li - o["first"] >= 2:
+            cs.wait_event(o["done"][b])
+        else:
+            cs.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(cs):
+            for name in self._OFF_NAMES:
+                o["staged"][b][name].copy_(o["host"][li][name], non_blocking=True)
+            o["copied"][b].record(cs)
 
     # ------------------------------------------------------------------ buffers
     def _alloc_buffers(self):
@@ -398,7 +453,15 @@ class CudaRunner:
             torch.index_select(self.embed, 0, m["ids"], out=h)
         hkv = cfg.num_kv_heads
         dsplit = ops.kernels.decode_splits(max(Bd, 1), hkv, max(st.max_decode_ctx, 1)) if Bd else (1, 1)
+        o = self.offload
+        if o is not None:
+            self._offload_fetch(o["first"])
         for li, lw in enumerate(self.layers):
+            if o is not None and li >= o["first"]:
+                b = (li - o["first"]) % 2
+                if li + 1 < len(self.layers):
+                    self._offload_fetch(li + 1)  # the next layer streams in while this one computes
+                torch.cuda.current_stream(self.device).wait_event(o["copied"][b])
             ops.rmsnorm(h, lw.ln1, cfg.rms_eps, out=x)
             qkv = ops.w4a16_linear(x, lw.qkv, out=self.qkv[:T], ws=ws)
             attn = self._attention(li, lw, qkv, st, m, dsplit)
@@ -409,6 +472,8 @@ class CudaRunner:
             else:
                 act = ops.w4a16_linear(x, lw.gate_up, out=self.act[:T], silu_mul=True, ws=ws)
                 self._row_parallel(act[:, : self.F], lw.down, h)
+            if o is not None and li >= o["first"]:
+                o["done"][(li - o["first"]) % 2].record(torch.cuda.current_stream(self.device))
 
     def _attention(self, li: int, lw, qkv: torch.Tensor, st: StepInputs, m: dict, dsplit) -> torch.Tensor:
         """RoPE + KV write, then decode and prefill attention of layer li over the paged cache."""

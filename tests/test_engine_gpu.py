@@ -253,6 +253,25 @@ def test_layer_split_engine_matches_single_gpu(cuda):
     split.runner.ws.check()
 
 
+def test_weight_offload_matches_resident_weights(cuda):
+    """The last layers' weights streamed from pinned host memory each step (two device staging
+    sets, copy stream + events): the same tokens as resident weights, and the staged layers
+    hold no resident copy."""
+    cfg, q = get_preset("tiny-llama")
+    prompts = [_prompt(80 + i, 20 + 25 * i, cfg.vocab_size) for i in range(3)]
+    ecfg = EngineConfig(max_num_seqs=4, max_num_batched_tokens=64, max_model_len=512, num_pages=64, cuda_graphs=False)
+    want = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda, ecfg).generate(
+        prompts, SamplingParams(max_tokens=16, ignore_eos=True))
+    for n in (1, 3):
+        eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,
+                                        dataclasses.replace(ecfg, offload_layers=n))
+        o = eng.runner.offload
+        assert o["first"] == cfg.num_layers - n and len(o["host"]) == n
+        assert all(t.is_pinned() for hl in o["host"].values() for t in hl.values())
+        assert eng.generate(prompts, SamplingParams(max_tokens=16, ignore_eos=True)) == want
+        eng.runner.ws.check()
+
+
 def test_sampled_decoding_runs_in_graphs(cuda):
     cfg, q = get_preset("tiny-llama")
     eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), cuda,

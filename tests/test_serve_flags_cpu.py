@@ -53,6 +53,7 @@ def test_flags_build_the_engine_config():
     assert (e.kv_sink_tokens, e.kv_window_tokens, e.prompt_logit_cache) == (4, 256, 0)
     assert _ecfg(_args()).prompt_logit_cache > 0
     assert _ecfg(_args("--pp", "2")).pp == 2
+    assert _ecfg(_args("--offload-layers", "3")).offload_layers == 3
 
 
 def _client(*extra):
