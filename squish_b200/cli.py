@@ -388,6 +388,47 @@ def cmd_bench(a) -> int:
     return 0
 
 
+def nvlink_topology(nvml=None) -> list[dict] | None:
+    """Per GPU: NVLink links up and the NVML P2P status toward every other GPU (read-only NVML
+    queries; None when NVML is unavailable). ``nvml`` is the pynvml module (a stand-in in tests)."""
+    if nvml is None:
+        try:
+            import pynvml as nvml
+        except ImportError:
+            return None
+    try:
+        nvml.nvmlInit()
+    except Exception:  # noqa: BLE001 - no driver: nothing to report
+        return None
+    try:
+        n = nvml.nvmlDeviceGetCount()
+        hs = [nvml.nvmlDeviceGetHandleByIndex(i) for i in range(n)]
+        out = []
+        for i, h in enumerate(hs):
+            links = 0
+            for ln in range(getattr(nvml, "NVML_NVLINK_MAX_LINKS", 18)):
+                try:
+                    links += int(nvml.nvmlDeviceGetNvLinkState(h, ln) == getattr(nvml, "NVML_FEATURE_ENABLED", 1))
+                except Exception:  # noqa: BLE001 - link index past this GPU's links
+                    break
+            p2p = {}
+            for j, hj in enumerate(hs):
+                if j == i:
+                    continue
+                try:
+                    st = nvml.nvmlDeviceGetP2PStatus(h, hj, getattr(nvml, "NVML_P2P_CAPS_INDEX_NVLINK", 3))
+                    p2p[j] = st == getattr(nvml, "NVML_P2P_STATUS_OK", 0)
+                except Exception:  # noqa: BLE001
+                    p2p[j] = None
+            out.append({"index": i, "nvlinks_up": links, "nvlink_p2p": p2p})
+        return out
+    finally:
+        try:
+            nvml.nvmlShutdown()
+        except Exception:  # noqa: BLE001
+            pass
+
+
 def doctor_report() -> dict:
     import torch
 
@@ -410,6 +451,7 @@ def doctor_report() -> dict:
         rep["gpus"] = gpus
         if n > 1:
             rep["peer_access"] = all(torch.cuda.can_device_access_peer(0, j) for j in range(1, n))
+        rep["nvlink"] = nvlink_topology()
         try:
             rep["nccl"] = ".".join(map(str, torch.cuda.nccl.version()))
         except (AttributeError, RuntimeError):

@@ -141,3 +141,33 @@ def test_llm_api_and_loadgen_cpu():
     assert [len(o["token_ids"]) for o in outs] == [3, 3] and outs[0]["finish_reason"] == "length"
     r = run_load(llm.engine, num_requests=5, concurrency=2, prompt_min=4, prompt_max=12, max_tokens=3)
     assert r["requests"] == 5 and r["output_tokens"] == 15 and r["ttft_ms_p50"] > 0
+
+
+def test_nvlink_topology_from_nvml_queries():
+    """The doctor's NVLink report from (read-only) NVML queries, against a stand-in NVML of two
+    GPUs with 18 links up and NVLink P2P between them."""
+    class FakeNVML:
+        NVML_NVLINK_MAX_LINKS = 18
+        NVML_FEATURE_ENABLED = 1
+        NVML_P2P_CAPS_INDEX_NVLINK = 3
+        NVML_P2P_STATUS_OK = 0
+        calls = []
+
+        def nvmlInit(self): self.calls.append("init")
+        def nvmlShutdown(self): self.calls.append("shutdown")
+        def nvmlDeviceGetCount(self): return 2
+        def nvmlDeviceGetHandleByIndex(self, i): return f"h{i}"
+        def nvmlDeviceGetNvLinkState(self, h, ln): return 1
+        def nvmlDeviceGetP2PStatus(self, a, b, idx):
+            assert idx == 3
+            return 0
+
+    f = FakeNVML()
+    topo = cli.nvlink_topology(f)
+    assert topo == [{"index": 0, "nvlinks_up": 18, "nvlink_p2p": {1: True}},
+                    {"index": 1, "nvlinks_up": 18, "nvlink_p2p": {0: True}}]
+    assert f.calls == ["init", "shutdown"]
+    # no driver: nothing to report
+    class NoDriver(FakeNVML):
+        def nvmlInit(self): raise RuntimeError("NVML Shared Library Not Found")
+    assert cli.nvlink_topology(NoDriver()) is None
