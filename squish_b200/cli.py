@@ -70,6 +70,10 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
                    help="draft model (checkpoint or preset of the same vocabulary) for draft/verify decoding")
     p.add_argument("--draft-depth", type=int, default=int(sp["draft_depth"]), help="draft tokens per round")
     p.add_argument("--jacobi", action="store_true", help="Jacobi (fixed-point) parallel decoding")
+    p.add_argument("--medusa-heads", default=None,
+                   help="Medusa head file or directory (medusa_head.{i}.* tensors): tree drafts from extra heads "
+                        "on the final hidden state")
+    p.add_argument("--medusa-top-k", type=int, default=4, help="Medusa: candidates per head")
     p.add_argument("--spec-branches", type=int, default=1, help="prompt lookup: continuations per draft tree")
     # multi-GPU
     p.add_argument("--tp", type=int, default=1, help="tensor-parallel GPUs (one process per GPU over NVLink)")
@@ -83,17 +87,22 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
     p.add_argument("--gpus", type=int, default=0, help="GPUs to use: tp x dp (dp = gpus / tp when --dp is not given)")
     p.add_argument("--tp-mode", default="nvlink", choices=["nvlink", "sp", "nccl"],
                    help="nvlink: fused GEMM + all-reduce over peer memory; sp: sequence parallel (fused GEMM -> "
-                        "reduce-scatter, RMSNorm + all-gather, gather-waiting GEMM; dense models); nccl: NCCL")
+                        "reduce-scatter, RMSNorm + all-gather, gather-waiting GEMM; MoE layers use the expert "
+                        "all-to-all over peer memory); nccl: NCCL")
     p.add_argument("--log-level", default="warning", choices=["debug", "info", "warning", "error", "critical"])
     p.add_argument("--log-format", default="text", choices=["text", "json"], help="json: one JSON object per line")
 
 
 def _spec(a):
-    """SpecConfig from the flags: a draft model wins over Jacobi, which wins over prompt lookup."""
+    """SpecConfig from the flags: a draft model wins over Medusa heads, then Jacobi, then prompt
+    lookup."""
     from .engine.speculative import SpecConfig
 
     if getattr(a, "draft_model", None):
         return SpecConfig(method="draft", k=a.draft_depth, draft_model=a.draft_model)
+    if getattr(a, "medusa_heads", None):
+        return SpecConfig(method="medusa", k=a.draft_depth, medusa_heads=a.medusa_heads,
+                          medusa_top_k=getattr(a, "medusa_top_k", 4))
     if getattr(a, "jacobi", False):
         return SpecConfig(method="jacobi", k=a.draft_depth)
     if getattr(a, "prompt_lookup", False):

@@ -376,7 +376,8 @@ void moe_route(torch::Tensor logits, int64_t K, bool renorm, torch::Tensor topk_
 }
 
 void moe_align(torch::Tensor ids, int64_t E, int64_t bn, torch::Tensor sorted_slot, torch::Tensor slot_pos,
-               torch::Tensor tile_expert, torch::Tensor num_tiles, c10::optional<torch::Tensor> counts) {
+               torch::Tensor tile_expert, torch::Tensor num_tiles, c10::optional<torch::Tensor> counts,
+               c10::optional<torch::Tensor> wait_flags, int64_t wait_expect, c10::optional<torch::Tensor> status) {
   CHECK_CUDA(ids);
   CHECK_DT(ids, torch::kInt32);
   CHECK_CONTIG(ids);
@@ -384,9 +385,12 @@ void moe_align(torch::Tensor ids, int64_t E, int64_t bn, torch::Tensor sorted_sl
   TORCH_CHECK(sorted_slot.numel() >= TK + E * (bn - 1), "sorted_slot too small for the padded layout");
   TORCH_CHECK(tile_expert.numel() * bn >= sorted_slot.numel(), "tile_expert too small");
   const c10::cuda::CUDAGuard g(ids.device());
+  TORCH_CHECK(!wait_flags || (status && wait_flags->is_cuda() && wait_flags->scalar_type() == torch::kInt32),
+              "wait_flags needs an int32 device tensor and a status word");
   CUDA_OK(sq::moe_align_launch(ptr<int>(ids), (int)TK, (int)E, (int)bn, (int)tile_expert.numel(),
                                ptr<int>(sorted_slot), ptr<int>(slot_pos), ptr<int>(tile_expert), ptr<int>(num_tiles),
-                               optr<int>(counts), cur_stream()));
+                               optr<int>(counts), cur_stream(), optr<int>(wait_flags),
+                               wait_flags ? (int)wait_flags->numel() : 0, (int)wait_expect, optr<int>(status)));
 }
 
 void moe_gather(torch::Tensor x, torch::Tensor sorted_slot, torch::Tensor num_tiles, int64_t bn, int64_t K,
@@ -625,7 +629,7 @@ void tp_oneshot(torch::Tensor src, torch::Tensor part_ptrs, int64_t par_stride, 
 void tp_rs_norm_ag(torch::Tensor recv, int64_t src_stride, int64_t ld_recv, torch::Tensor rs_flags, int64_t rs_expect,
                    torch::Tensor h, torch::Tensor w, double eps, torch::Tensor ag_dst, int64_t ld_ag,
                    torch::Tensor ag_flags, int64_t rank, int64_t tp, int64_t rows_per_rank, int64_t T,
-                   torch::Tensor seq, torch::Tensor done, torch::Tensor status) {
+                   torch::Tensor seq, torch::Tensor done, torch::Tensor status, bool local_only) {
   CHECK_CUDA(h);
   CHECK_DT(h, torch::kBFloat16);
   CHECK_DT(w, torch::kBFloat16);
@@ -654,7 +658,82 @@ void tp_rs_norm_ag(torch::Tensor recv, int64_t src_stride, int64_t ld_recv, torc
   p.seq = ptr<int>(seq);
   p.done = ptr<int>(done);
   p.status = ptr<int>(status);
+  p.local_only = local_only ? 1 : 0;
   CUDA_OK(sq::tp_rs_norm_ag_launch(p, cur_stream()));
+}
+
+// Expert-parallel dispatch of this rank's owned rows (see ep_a2a.cu). Pointer arrays are
+// [tp] int64 device tensors of every rank's buffers.
+void ep_dispatch(torch::Tensor x, c10::optional<torch::Tensor> logits, bool renorm, torch::Tensor ids,
+                 torch::Tensor w, int64_t own, int64_t R, int64_t K, int64_t E_local, int64_t rank, int64_t tp,
+                 torch::Tensor recv_x, torch::Tensor recv_ids, torch::Tensor recv_w, torch::Tensor flags) {
+  CHECK_CUDA(x);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(ids, torch::kInt32);
+  CHECK_DT(w, torch::kFloat32);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(0) >= own, "x: [>= own, H]");
+  TORCH_CHECK(ids.is_contiguous() && w.is_contiguous() && ids.numel() >= own * K && w.numel() >= own * K,
+              "ids / w: contiguous [own, K]");
+  TORCH_CHECK(own <= R, "own rows exceed the slots per source");
+  for (const auto* t : {&recv_x, &recv_ids, &recv_w, &flags})
+    TORCH_CHECK(t->scalar_type() == torch::kInt64 && t->numel() == tp && t->is_cuda(), "pointer arrays: [tp] int64");
+  const c10::cuda::CUDAGuard g(x.device());
+  sq::EpDispatchParams p{};
+  p.x = ptr<__nv_bfloat16>(x);
+  p.ldx = (int)x.stride(0);
+  p.ids = ptr<int>(ids);
+  p.w = ptr<float>(w);
+  if (logits) {  // route in the dispatch kernel
+    CHECK_DT((*logits), torch::kBFloat16);
+    TORCH_CHECK(logits->dim() == 2 && logits->stride(1) == 1 && logits->size(0) >= own, "logits: [>= own, E]");
+    p.logits = ptr<__nv_bfloat16>(*logits);
+    p.ld_logits = (int)logits->stride(0);
+    p.E = (int)logits->size(1);
+    p.renorm = renorm ? 1 : 0;
+  }
+  p.recv_x = reinterpret_cast<__nv_bfloat16* const*>(recv_x.data_ptr());
+  p.recv_ids = reinterpret_cast<int* const*>(recv_ids.data_ptr());
+  p.recv_w = reinterpret_cast<float* const*>(recv_w.data_ptr());
+  p.flags = reinterpret_cast<int* const*>(flags.data_ptr());
+  p.own = (int)own;
+  p.R = (int)R;
+  p.H = (int)x.size(1);
+  p.K = (int)K;
+  p.E_local = (int)E_local;
+  p.rank = (int)rank;
+  p.tp = (int)tp;
+  CUDA_OK(sq::ep_dispatch_launch(p, cur_stream()));
+}
+
+void ep_combine(torch::Tensor ys, torch::Tensor slot_pos, torch::Tensor w, int64_t R, int64_t K, int64_t tp,
+                int64_t T, torch::Tensor dst, int64_t ld_dst, torch::Tensor flags, int64_t flag_stride,
+                torch::Tensor seq) {
+  CHECK_CUDA(ys);
+  CHECK_DT(ys, torch::kBFloat16);
+  CHECK_DT(slot_pos, torch::kInt32);
+  CHECK_DT(w, torch::kFloat32);
+  TORCH_CHECK(ys.dim() == 2 && ys.stride(1) == 1, "ys: [P, H]");
+  TORCH_CHECK(slot_pos.numel() >= tp * R * K && w.numel() >= tp * R * K, "slot_pos / w: [tp R K]");
+  TORCH_CHECK(dst.scalar_type() == torch::kInt64 && dst.numel() == tp && flags.scalar_type() == torch::kInt64 &&
+                  flags.numel() == tp,
+              "dst / flags: [tp] int64 pointers");
+  const c10::cuda::CUDAGuard g(ys.device());
+  sq::EpCombineParams p{};
+  p.ys = ptr<__nv_bfloat16>(ys);
+  p.ldys = (int)ys.stride(0);
+  p.slot_pos = ptr<int>(slot_pos);
+  p.w = ptr<float>(w);
+  p.dst = reinterpret_cast<__nv_bfloat16* const*>(dst.data_ptr());
+  p.ld_dst = (int)ld_dst;
+  p.flags = reinterpret_cast<int* const*>(flags.data_ptr());
+  p.flag_stride = (int)flag_stride;
+  p.seq = ptr<int>(seq);
+  p.R = (int)R;
+  p.H = (int)ys.size(1);
+  p.K = (int)K;
+  p.tp = (int)tp;
+  p.T = (int)T;
+  CUDA_OK(sq::ep_combine_launch(p, cur_stream()));
 }
 
 void tp_ag_wait(torch::Tensor ag_flags, int64_t expect, int64_t tp, torch::Tensor status) {
@@ -1156,6 +1235,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ag_tp") = 0);
   m.def("w4a16_gemm_rs", &w4a16_gemm_rs);
   m.def("tp_rs_norm_ag", &tp_rs_norm_ag);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_combine", &ep_combine);
   m.def("tp_oneshot", &tp_oneshot);
   m.def("tp_ag_wait", &tp_ag_wait);
   m.def("dequant_weight", &dequant_weight);
@@ -1173,7 +1254,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_push", &tp_push);
   m.def("tp_gather", &tp_gather);
   m.def("kv_compact", &kv_compact);
-  m.def("moe_align", &moe_align);
+  m.def("moe_align", &moe_align, py::arg("ids"), py::arg("E"), py::arg("bn"), py::arg("sorted_slot"),
+        py::arg("slot_pos"), py::arg("tile_expert"), py::arg("num_tiles"), py::arg("counts") = py::none(),
+        py::arg("wait_flags") = py::none(), py::arg("wait_expect") = 0, py::arg("status") = py::none());
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
   m.def("rmsnorm", &rmsnorm);

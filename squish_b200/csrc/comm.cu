@@ -237,14 +237,18 @@ __global__ void __launch_bounds__(1024) tp_rs_norm_ag_kernel(const TpRsNormParam
 #pragma unroll
       for (int e = 0; e < 4; ++e)
         o2[e] = __floats2bfloat162_rn(v[k][2 * e] * inv * g[2 * e], v[k][2 * e + 1] * inv * g[2 * e + 1]);
-      for (int r = 0; r < p.tp; ++r) *reinterpret_cast<uint4*>(p.ag_dst[r] + (size_t)m * p.ld_ag + c) = o;
+      if (p.local_only)
+        *reinterpret_cast<uint4*>(p.ag_dst[p.rank] + (size_t)m * p.ld_ag + c) = o;
+      else
+        for (int r = 0; r < p.tp; ++r) *reinterpret_cast<uint4*>(p.ag_dst[r] + (size_t)m * p.ld_ag + c) = o;
     }
   }
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int r = 0; r < p.tp; ++r)
-      asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p.ag_flags[r]), "r"(1) : "memory");
+    if (!p.local_only)
+      for (int r = 0; r < p.tp; ++r)
+        asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p.ag_flags[r]), "r"(1) : "memory");
     __threadfence();
     if (atomicAdd(p.done, 1) == (int)gridDim.x - 1) {
       for (int s2 = 0; s2 < p.tp; ++s2) flags[s2] = 0;

@@ -76,6 +76,10 @@ struct TpRsNormParams {
   int* seq;
   int* done;
   int* status;
+  // local_only != 0: the normalised rows go to this rank's buffer only (ag_dst[rank]) and no
+  // all-gather arrival is counted (the input of an expert-parallel dispatch, which sends each
+  // row only to the ranks that hold its experts)
+  int local_only;
 };
 constexpr int kRsNormMaxChunks = 4;  // one CTA per row: <= 4 chunks of 8 columns per thread (N <= 32768)
 cudaError_t tp_rs_norm_ag_launch(const TpRsNormParams& p, cudaStream_t s);
@@ -103,6 +107,50 @@ struct TpOneshotParams {
 constexpr int kOneshotMaxCtas = 148;
 constexpr int kOneshotThreads = 256;
 cudaError_t tp_oneshot_launch(const TpOneshotParams& p, cudaStream_t s);
+// Expert-parallel all-to-all over peer memory (sequence-parallel layout: rank r owns token rows
+// [r R, r R + own)). Every receiver holds, per source rank s, R row slots of x, and R x K slots
+// of (local expert id or -1, routing weight).
+//
+// Dispatch: one CTA per owned row slot t (R CTAs on every rank). The row's K routed experts
+// name the ranks that hold them (expert e lives on rank e / E_local); the row is stored once
+// into each such rank's x slot [rank][t], and every rank gets the K (id, weight) pairs of the
+// row with the ids that are not its own set to -1 (rows past `own` send -1 everywhere). Then one
+// arrival per CTA on every rank's dispatch counter for this source (receivers wait for R).
+// With router logits given, warp 0 of each CTA first routes its row (softmax, top-K, renorm:
+// the MoE routing kernel's warp routine) and writes ids / w; otherwise ids / w are read.
+struct EpDispatchParams {
+  const __nv_bfloat16* x;        // [own, ldx] this rank's normalised rows
+  int ldx;
+  const __nv_bfloat16* logits;   // [own, ld_logits] router logits, or nullptr
+  int ld_logits, E, renorm;
+  int* ids;                      // [own, K] global expert ids (router output / input)
+  float* w;                      // [own, K] routing weights
+  __nv_bfloat16* const* recv_x;  // [tp] every rank's x slots base [tp src][R][H]
+  int* const* recv_ids;          // [tp] every rank's id slots [tp src][R][K]
+  float* const* recv_w;          // [tp] every rank's weight slots [tp src][R][K]
+  int* const* flags;             // [tp] every rank's dispatch counter for this source
+  int own, R, H, K, E_local, rank, tp;
+};
+// Combine: one CTA per received row slot (s, t) (tp x R CTAs): the weighted sum of the local
+// experts' outputs for the row's slots (K in order, zeros when none of its experts is here)
+// goes to the row owner's reduce-scatter receive block for this source, dst[s] + t * ld_dst,
+// and one arrival on the owner's reduce-scatter counter [parity][this source] (the owner
+// waits for R arrivals per source in tp_rs_norm_ag, which adds the tp partial rows to the
+// residual, normalises and all-gathers as after a row-parallel GEMM).
+struct EpCombineParams {
+  const __nv_bfloat16* ys;       // [P, ldys] local experts' outputs in sorted slot order
+  int ldys;
+  const int* slot_pos;           // [tp R K] position of each received slot in ys (-1: not here)
+  const float* w;                // [tp R K] received routing weights
+  __nv_bfloat16* const* dst;     // [tp] owner's receive block for this source
+  int ld_dst;
+  int* const* flags;             // [tp] owner's counter row for this source (parity 0)
+  int flag_stride;               // elements between parities
+  const int* seq;                // parity = seq & 1
+  int R, H, K, tp, T;
+};
+cudaError_t ep_dispatch_launch(const EpDispatchParams& p, cudaStream_t s);
+cudaError_t ep_combine_launch(const EpCombineParams& p, cudaStream_t s);
 cudaError_t tp_push_launch(const TpPushParams& p, int grid_x, int grid_y, cudaStream_t s);
 cudaError_t tp_reduce_launch(const TpReduceParams& p, int grid_x, int grid_y, cudaStream_t s);
 cudaError_t tp_gather_launch(const TpGatherParams& p, cudaStream_t s);

@@ -163,8 +163,11 @@ cudaError_t kv_compact_launch(const KvCompactParams& p, int layers, cudaStream_t
 
 cudaError_t moe_route_launch(const __nv_bfloat16* logits, int ld, int T, int E, int K, bool renorm, int* topk_ids,
                              float* topk_w, cudaStream_t s);
+// wait_flags != nullptr: first wait (bounded, then clear) until wait_flags[s] >= wait_expect for
+// s < wait_n -- the expert-parallel receiver's dispatch arrivals -- recording a timeout in status
 cudaError_t moe_align_launch(const int* ids, int TK, int E, int bn, int max_tiles, int* sorted_slot, int* slot_pos,
-                             int* tile_expert, int* num_tiles, int* counts, cudaStream_t s);
+                             int* tile_expert, int* num_tiles, int* counts, cudaStream_t s,
+                             int* wait_flags = nullptr, int wait_n = 0, int wait_expect = 0, int* status = nullptr);
 cudaError_t moe_gather_launch(const __nv_bfloat16* x, int ldx, const int* sorted_slot, const int* num_tiles,
                               int max_rows, int bn, int K, int H, __nv_bfloat16* xs, int ldxs, cudaStream_t s);
 cudaError_t moe_combine_launch(const __nv_bfloat16* ys, int ldys, const int* slot_pos, const float* topk_w, int T,

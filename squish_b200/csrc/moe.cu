@@ -19,6 +19,8 @@
 
 #include "kernels.h"
 #include "launch.cuh"
+#include "moe_route.cuh"
+#include "sm100.cuh"
 
 namespace sq {
 
@@ -33,64 +35,39 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const __nv_bfloat16* __r
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + warp;
   if (t >= T) return;
-  float v[EPL];
-  float m = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    const int e = lane + 32 * i;
-    v[i] = e < E ? __bfloat162float(logits[(size_t)t * ld + e]) : -INFINITY;
-    m = fmaxf(m, v[i]);
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    v[i] = (lane + 32 * i) < E ? __expf(v[i] - m) : -1.f;
-    s += v[i] > 0.f ? v[i] : 0.f;
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  const float inv = 1.f / s;
-  float picked = 0.f;
-  for (int k = 0; k < K; ++k) {
-    float bv = -2.f;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < EPL; ++i)
-      if (v[i] > bv) {  // strict: the lower index wins ties within a lane
-        bv = v[i];
-        bi = lane + 32 * i;
+  route_row_warp<EPL>(logits + (size_t)t * ld, E, K, renorm, lane, topk_ids + (size_t)t * K, topk_w + (size_t)t * K);
+}
+
+// Bounded wait (one thread per source) until every source's dispatch counter reached `expect`,
+// then clear it: the expert-parallel receiver's arrival check, fused into the align kernel.
+__device__ __forceinline__ void wait_dispatch(int* flags, int n, int expect, int* status) {
+  if ((int)threadIdx.x < n) {
+    int* f = flags + threadIdx.x;
+    bool ok = false;
+    for (long long i = 0; i < (1LL << 22); ++i) {
+      int v;
+      asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if (v >= expect) {
+        ok = true;
+        break;
       }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
+      if ((i & 4095) == 4095 && *reinterpret_cast<volatile int*>(status) != 0) break;
     }
-#pragma unroll
-    for (int i = 0; i < EPL; ++i)
-      if (lane + 32 * i == bi) v[i] = -1.f;
-    const float pr = bv * inv;
-    picked += pr;
-    if (lane == 0) {
-      topk_ids[(size_t)t * K + k] = bi;
-      topk_w[(size_t)t * K + k] = pr;
-    }
+    if (!ok) atomicCAS(status, 0, SQ_ERR_TIMEOUT_PEER);
+    *f = 0;
   }
-  __syncwarp();
-  if (renorm && lane < K) topk_w[(size_t)t * K + lane] /= picked;
+  __syncthreads();
+  __threadfence();
 }
 
 __global__ void __launch_bounds__(1024) moe_align_kernel(const int* __restrict__ ids, int TK, int E, int bn,
                                                          int max_tiles, int* __restrict__ sorted_slot,
                                                          int* __restrict__ slot_pos, int* __restrict__ tile_expert,
-                                                         int* __restrict__ num_tiles, int* __restrict__ counts) {
+                                                         int* __restrict__ num_tiles, int* __restrict__ counts,
+                                                         int* wait_flags, int wait_n, int wait_expect, int* status) {
   pdl_wait();
   pdl_trigger();
+  if (wait_flags != nullptr) wait_dispatch(wait_flags, wait_n, wait_expect, status);
   extern __shared__ int sh[];
   int* cnt = sh;           // [E]
   int* off = sh + E;       // [E + 1]
@@ -224,10 +201,12 @@ cudaError_t moe_route_launch(const __nv_bfloat16* logits, int ld, int T, int E, 
 }
 
 cudaError_t moe_align_launch(const int* ids, int TK, int E, int bn, int max_tiles, int* sorted_slot, int* slot_pos,
-                             int* tile_expert, int* num_tiles, int* counts, cudaStream_t s) {
+                             int* tile_expert, int* num_tiles, int* counts, cudaStream_t s, int* wait_flags,
+                             int wait_n, int wait_expect, int* status) {
+  if (wait_flags != nullptr && (wait_n > 32 || status == nullptr)) return cudaErrorInvalidValue;
   const size_t smem = (size_t)(3 * E + 1) * sizeof(int);
   SQ_LAUNCH(moe_align_kernel, dim3(1), dim3(1024), smem, s, 1, ids, TK, E, bn, max_tiles, sorted_slot, slot_pos, tile_expert, num_tiles,
-                                         counts);
+                                         counts, wait_flags, wait_n, wait_expect, status);
   return cudaGetLastError();
 }
 

@@ -135,4 +135,5 @@ class DecodeGraphs:
         r.tokens_host[:bucket].copy_(toks, non_blocking=True)
         r.timer_stop()
         r.sync()
+        r.last_hidden = r.xs[:B]  # final-norm rows of the replayed step (static buffer)
         return r.tokens_host[:B].numpy().copy()

@@ -614,8 +614,11 @@ class LLMEngine:
                 self.hidden_states[samp[i].rid] = hid[i].float().cpu().numpy()
         for r, t in zip(samp, toks.tolist()):
             outs.append(self._emit(r, [int(t)], now))
+        self._hid_rows = [(r, i) for i, r in enumerate(samp)]
         if st.num_verify:
             outs.extend(self._apply_verify(sched, st, now))
+        if getattr(self.proposer, "wants_hidden", False):
+            self._observe_hidden()
         if score:
             self._h2o_collect(sched)
         t4 = time.perf_counter()
@@ -768,12 +771,24 @@ class LLMEngine:
                 self.guard.record(r.rid, nacc)
             p_ = None if preds is None else preds[vrow:vrow + tr.size]
             self.proposer.after_verify(r, nacc, p_)
+            # the final token came from the last accepted node's row (after the sampled rows)
+            self._hid_rows.append((r, st.num_sample_rows + vrow + (path[-1] if path else 0)))
             vrow += tr.size
             g += 1
             outs.append(self._emit(r, toks, now))
         if src:
             self.runner.kv_compact(src, dst)
         return outs
+
+    def _observe_hidden(self) -> None:
+        """Hand the hidden-state proposer (Medusa heads) the final-norm rows that produced each
+        live request's newest token."""
+        live = [(r, i) for r, i in self._hid_rows if r.finish_time is None]
+        if not live:
+            return
+        hid = self.runner.last_hidden
+        idx = torch.tensor([i for _, i in live], dtype=torch.long, device=hid.device)
+        self.proposer.observe([r for r, _ in live], hid.index_select(0, idx))
 
     def _publish_blocks(self, r: Request) -> None:
         full = r.num_computed // self.qcfg.page_size

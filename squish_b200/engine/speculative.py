@@ -18,7 +18,10 @@ Proposers (the reference's speculative/ package):
     vocabulary proposes k tokens per round from its own paged KV cache, batched over all
     requests; its softmax rows are the q of the rejection test;
   * Jacobi (experimental/jacobi_decode.py:184-330) — the previous verification's own
-    predictions past the accepted point are the next guess (fixed-point iteration).
+    predictions past the accepted point are the next guess (fixed-point iteration);
+  * Medusa heads (speculative/speculative.py:1821-2050) — extra heads on the final hidden
+    state propose the tokens after the next one; the best rank paths of their top-k lists
+    form the tree (engine/medusa.py).
 """
 from __future__ import annotations
 
@@ -32,7 +35,7 @@ TREE_META_INTS = 2 + 3 * MAX_TREE_NODES
 
 @dataclass
 class SpecConfig:
-    method: str = "prompt_lookup"   # "prompt_lookup" | "draft" | "jacobi"
+    method: str = "prompt_lookup"   # "prompt_lookup" | "draft" | "jacobi" | "medusa"
     k: int = 4                      # draft depth (tokens per branch)
     branches: int = 1               # prompt lookup: distinct continuations per tree
     max_nodes: int = 16             # tree size cap (<= 32)
@@ -43,6 +46,11 @@ class SpecConfig:
     miss_limit: int = 4
     cooldown: int = 8
     force_accept: int | None = None  # benchmark knob: accept exactly this many drafts (0..k)
+    # Medusa heads (method "medusa"): a head file / directory, or "random:<num_heads>" (tests,
+    # benchmarks); candidates per head; paths kept from the Cartesian product
+    medusa_heads: str | None = None
+    medusa_top_k: int = 4
+    medusa_paths: int = 16
 
 
 @dataclass
@@ -347,11 +355,72 @@ class DraftModelProposer:
             s.pages = []
 
 
+class MedusaProposer:
+    """Drafts from Medusa heads (engine/medusa.py) over the final hidden state of the row that
+    produced each request's newest token: the engine calls ``observe`` after every step with
+    those rows; ``propose`` turns a request's per-head top-k lists into a tree of the best rank
+    paths rooted at the pending token."""
+    deterministic = True
+    wants_hidden = True
+
+    def __init__(self, sc: SpecConfig, heads):
+        self.sc = sc
+        self.heads = heads
+        self.cands: dict[str, np.ndarray] = {}
+
+    def observe(self, reqs, hidden) -> None:
+        if not reqs:
+            return
+        tops = self.heads.topk(hidden, self.sc.medusa_top_k)
+        for r, t in zip(reqs, tops):
+            self.cands[r.rid] = t
+
+    def propose(self, reqs) -> dict[str, DraftTree]:
+        from .medusa import rank_paths
+
+        trees = {}
+        n, k = self.heads.num_heads, self.sc.medusa_top_k
+        depth = min(n, self.sc.k)
+        paths = rank_paths(depth, k, self.sc.medusa_paths)
+        for r in reqs:
+            c = self.cands.pop(r.rid, None)
+            if c is None:
+                continue
+            chains = [[int(c[h, rk]) for h, rk in enumerate(p)] for p in paths]
+            trees[r.rid] = build_tree(r.token_at(r.total_len - 1), chains, self.sc.max_nodes)
+        return trees
+
+    def after_verify(self, r, accepted: int, preds=None) -> None:
+        pass
+
+    def forget(self, rid: str) -> None:
+        self.cands.pop(rid, None)
+
+
+def load_medusa_heads(sc: SpecConfig, target):
+    """The proposer's heads on the target's device: a file / directory, or random heads."""
+    from .medusa import MedusaHeads
+
+    cfg = target.cfg
+    dev = getattr(target.runner, "device", "cpu")
+    spec = sc.medusa_heads or "random:3"
+    if spec.startswith("random"):
+        n = int(spec.split(":", 1)[1]) if ":" in spec else 3
+        return MedusaHeads.random(cfg.hidden_size, cfg.vocab_size, num_heads=n, device=dev)
+    heads = MedusaHeads.load(spec, device=dev)
+    if heads.hidden != cfg.hidden_size or heads.vocab != cfg.vocab_size:
+        raise ValueError(f"Medusa heads are {heads.hidden} -> {heads.vocab}; the model is "
+                         f"{cfg.hidden_size} -> {cfg.vocab_size}")
+    return heads
+
+
 def make_proposer(sc: SpecConfig, target):
     if sc.method == "prompt_lookup":
         return PromptLookupProposer(sc)
     if sc.method == "jacobi":
         return JacobiProposer(sc)
+    if sc.method == "medusa":
+        return MedusaProposer(sc, load_medusa_heads(sc, target))
     if sc.method == "draft":
         if not sc.draft_model:
             raise ValueError("speculative method 'draft' needs draft_model")

@@ -122,3 +122,30 @@ class MoELayer:
             part.zero_()
             K_.moe_combine(sc.ys[:P], sc.slot_pos[:TK], sc.w[:TK], K, part)
             self.ep_reduce(part, h)
+
+    def forward_a2a(self, comm, x_own: torch.Tensor, T: int, ws=None) -> int:
+        """Expert-parallel step with the all-to-all over peer memory (sequence-parallel layout,
+        csrc/ep_a2a.cu): route this rank's owned rows x_own [own, H], dispatch each row to the
+        ranks holding its experts, run the local experts over the tp x R received row slots and
+        send the weighted sums back to the row owners' reduce-scatter blocks. Returns the
+        arrivals per source that the owners' tp_rs_norm_ag waits for."""
+        sc = self.scratch
+        R = comm.sp_rows(T)
+        Tr = comm.tp * R
+        if sc is None or Tr > sc.max_tokens:
+            sc = self.scratch = MoEScratch(self.cfg, max(Tr, sc.max_tokens if sc else 0), x_own.device)
+        E, K = self.E_local, self.K
+        own = x_own.shape[0]
+        logits = torch.mm(x_own, self.gate_w.t(), out=sc.logits[:own]) if own else None
+        comm.ep_dispatch(x_own, logits, self.cfg.norm_topk_prob, sc.ids, sc.w, T)  # routes, then sends
+        bn = K_.moe_tile(Tr, K, E)
+        P = K_.moe_padded_rows(Tr, K, E, bn)
+        TK = Tr * K
+        comm.ep_align(T, bn, sc.sorted_slot[:P], sc.slot_pos[:TK], sc.tile_expert[: P // bn], sc.num_tiles,
+                      sc.counts)
+        K_.moe_gather(comm.ep_x[:Tr], sc.sorted_slot[:P], sc.num_tiles, bn, K, sc.xs[:P])
+        act = K_.w4a16_grouped_linear(sc.xs[:P], self.gate_up, sc.act[:P, : self.gate_up.n // 2],
+                                      sc.tile_expert[: P // bn], sc.num_tiles, bn, silu_mul=True, ws=ws)
+        K_.w4a16_grouped_linear(act[:, : self.F], self.down, sc.ys[:P], sc.tile_expert[: P // bn], sc.num_tiles, bn,
+                                ws=ws)
+        return comm.ep_combine(sc.ys[:P], sc.slot_pos[:TK], T)

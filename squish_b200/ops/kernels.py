@@ -486,8 +486,13 @@ def moe_route(logits: torch.Tensor, top_k: int, renorm: bool, ids: torch.Tensor,
 
 
 def moe_align(ids: torch.Tensor, experts: int, bn: int, sorted_slot: torch.Tensor, slot_pos: torch.Tensor,
-              tile_expert: torch.Tensor, num_tiles: torch.Tensor, counts: torch.Tensor | None = None) -> None:
-    native().moe_align(ids, experts, bn, sorted_slot, slot_pos, tile_expert, num_tiles, counts)
+              tile_expert: torch.Tensor, num_tiles: torch.Tensor, counts: torch.Tensor | None = None,
+              wait_flags: torch.Tensor | None = None, wait_expect: int = 0, status: torch.Tensor | None = None) -> None:
+    """Expert-sorted, tile-padded slot layout of the routed ids (one CTA). With ``wait_flags`` the
+    kernel first waits (bounded) until every entry reached ``wait_expect`` and clears them (the
+    expert-parallel receiver's dispatch arrivals; a timeout is recorded in ``status``)."""
+    native().moe_align(ids, experts, bn, sorted_slot, slot_pos, tile_expert, num_tiles, counts, wait_flags,
+                       int(wait_expect), status)
     _count()
 
 

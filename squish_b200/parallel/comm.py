@@ -15,7 +15,10 @@ Two implementations behind one interface:
     them), one kernel per layer half sums the partials into the owned residual rows, applies
     the next RMSNorm and pushes the normalised rows to every rank (all-gather), and the
     column-parallel GEMM (qkv, gate_up) waits for the gather inside its activation producer
-    while its weights already stream;
+    while its weights already stream; MoE layers replace the FFN's all-gather / reduce-scatter
+    with the expert-parallel all-to-all (``setup_ep`` / ``ep_dispatch`` / ``ep_combine``,
+    csrc/ep_a2a.cu): each owned row goes only to the ranks holding its routed experts and the
+    weighted expert sums come back through the reduce-scatter blocks;
   * ``nccl``: the same math with torch.distributed all_reduce / all_gather (the baseline;
     also what CPU ranks use, over gloo).
 
@@ -162,6 +165,79 @@ class TPComm:
         torch.cuda.synchronize(dev)
         dist.barrier(group=self.group)
 
+    # ------------------------------------------------------------------ expert-parallel all-to-all
+    def setup_ep(self, top_k: int, experts_local: int) -> None:
+        """Receive slots of the expert-parallel all-to-all (sequence-parallel mode; csrc/ep_a2a.cu):
+        per source rank, R rows of x and R x K (local expert id | -1, routing weight) pairs, and one
+        dispatch counter per source -- IPC memory that the sources store into. The combine goes
+        back through the reduce-scatter buffers above."""
+        if self.mode != "sp":
+            raise ValueError("the expert-parallel all-to-all runs in the sequence-parallel mode")
+        if getattr(self, "ep_k", None) == top_k and self.ep_experts == experts_local:
+            return
+        tp, R, H, K = self.tp, self.sp_rows_max, self.hidden, top_k
+        x = self._alloc_shared(tp * R * H * 2)
+        ids = self._alloc_shared(tp * R * K * 4)
+        w = self._alloc_shared(tp * R * K * 4)
+        fl = self._alloc_shared(tp * 4)
+        i64 = dict(dtype=torch.int64, device=self.device)
+        idx = self.device.index
+        self.ep_k, self.ep_experts = K, experts_local
+        self.ep_x_ptrs = torch.tensor(x, **i64)
+        self.ep_ids_ptrs = torch.tensor(ids, **i64)
+        self.ep_w_ptrs = torch.tensor(w, **i64)
+        self.ep_flag_ptrs = torch.tensor([p + 4 * self.rank for p in fl], **i64)
+        self.ep_x = native().tensor_from_ptr(x[self.rank], [tp * R, H], torch.bfloat16, idx)
+        self.ep_ids = native().tensor_from_ptr(ids[self.rank], [tp * R * K], torch.int32, idx)
+        self.ep_w = native().tensor_from_ptr(w[self.rank], [tp * R * K], torch.float32, idx)
+        self.ep_flags = native().tensor_from_ptr(fl[self.rank], [tp], torch.int32, idx)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+
+    def ep_own(self, T: int) -> tuple[int, int]:
+        """(first owned row, owned rows) of this rank in a T-token step."""
+        R = self.sp_rows(T)
+        r0 = self.rank * R
+        return r0, max(0, min(R, T - r0))
+
+    def ep_dispatch(self, x_own: torch.Tensor, logits: torch.Tensor | None, renorm: bool, ids: torch.Tensor,
+                    w: torch.Tensor, T: int) -> None:
+        """Route each owned row (x_own [own, H]; router logits [own, E], or None when ids / w
+        already hold the [own, K] global expert ids and weights) and send it to the ranks
+        holding its experts. The receivers' arrival wait runs in ``ep_align``."""
+        from ..ops import kernels as K_
+
+        R = self.sp_rows(T)
+        own = x_own.shape[0]
+        if T > self.max_tokens:
+            raise ValueError("expert-parallel step exceeds the sequence-parallel buffers")
+        native().ep_dispatch(x_own, logits, bool(renorm), ids, w, own, R, self.ep_k, self.ep_experts, self.rank,
+                             self.tp, self.ep_x_ptrs, self.ep_ids_ptrs, self.ep_w_ptrs, self.ep_flag_ptrs)
+        K_._count()
+
+    def ep_align(self, T: int, bn: int, sorted_slot, slot_pos, tile_expert, num_tiles, counts) -> None:
+        """Wait (bounded) for every source's R dispatched row slots of this step, then lay the
+        received slots out expert-sorted for the grouped GEMMs (one kernel)."""
+        from ..ops import kernels as K_
+
+        R = self.sp_rows(T)
+        TK = self.tp * R * self.ep_k
+        K_.moe_align(self.ep_ids[:TK], self.ep_experts, bn, sorted_slot, slot_pos, tile_expert, num_tiles, counts,
+                     wait_flags=self.ep_flags, wait_expect=R, status=self.status)
+
+    def ep_combine(self, ys: torch.Tensor, slot_pos: torch.Tensor, T: int) -> int:
+        """Weighted expert outputs of the received rows back to their owners' reduce-scatter
+        blocks; returns the arrivals each owner expects per source (for rs_norm_ag)."""
+        from ..ops import kernels as K_
+
+        R = self.sp_rows(T)
+        # link bytes: dispatch (at most every owned row to every peer) + combine rows
+        self.link_bytes += 2 * (self.tp - 1) * R * self.hidden * 2
+        native().ep_combine(ys, slot_pos, self.ep_w, R, self.ep_k, self.tp, T, self.sp_push_dst, self.hidden,
+                            self.sp_push_flags, self.tp, self.sp_seq)
+        K_._count()
+        return R
+
     def sp_rows(self, T: int) -> int:
         """Token rows each rank owns in a T-token step (the last rank may own fewer or none)."""
         return -(-T // self.tp)
@@ -182,16 +258,18 @@ class TPComm:
         K._count()
         return int(e)
 
-    def rs_norm_ag(self, h: torch.Tensor, norm_w: torch.Tensor, eps: float, T: int, rs_expect: int) -> None:
-        """Owned rows: h += sum of the tp partials; then RMSNorm(h) into every rank's xg."""
+    def rs_norm_ag(self, h: torch.Tensor, norm_w: torch.Tensor, eps: float, T: int, rs_expect: int,
+                   local_only: bool = False) -> None:
+        """Owned rows: h += sum of the tp partials; then RMSNorm(h) into every rank's xg (only
+        this rank's xg with local_only: the input of an expert-parallel dispatch)."""
         from ..ops import kernels as K
 
         R = self.sp_rows(T)
-        self.link_bytes += 2 * (self.tp - 1) * R * self.hidden * 2  # reduce-scatter in + all-gather in
+        self.link_bytes += (1 if local_only else 2) * (self.tp - 1) * R * self.hidden * 2  # RS in (+ AG in)
         native().tp_rs_norm_ag(self.sp_recv, self.sp_rows_max * self.hidden, self.hidden, self.sp_rs_flags,
                                int(rs_expect), h, norm_w, float(eps), self.sp_ag_dst, self.hidden,
                                self.sp_ag_flag_ptrs, self.rank, self.tp, R, T, self.sp_seq, self.sp_done,
-                               self.status)
+                               self.status, bool(local_only))
         K._count()
 
     def ag_wait(self, T: int) -> None:

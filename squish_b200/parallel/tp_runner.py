@@ -3,7 +3,9 @@ row-parallel outputs all-reduced and the vocab-parallel logits gathered.
 
 ``TPCudaRunner``: o_proj and down_proj run as one fused GEMM+all-reduce over NVLink (or the
 NCCL baseline), or, in the sequence-parallel mode, as GEMM->reduce-scatter with the RMSNorm
-and all-gather fused into one kernel and the gather wait fused into the next GEMM; the LM
+and all-gather fused into one kernel and the gather wait fused into the next GEMM (MoE layers:
+the owned rows go to the ranks holding their experts and the expert sums come back through the
+reduce-scatter blocks, an all-to-all over peer memory instead of an all-reduce); the LM
 head computes this rank's vocabulary slice and the slices are
 gathered into a full logits row on every rank, so every rank samples the same tokens and
 the engine's host logic can run replicated on every rank. ``TorchTPRunner`` is the CPU
@@ -29,11 +31,18 @@ class TPCudaRunner(CudaRunner):
         self.logits_local = torch.empty(R, comm.v1 - comm.v0, dtype=torch.bfloat16, device=self.device)
         del self.logits
         self.logits = comm.logits_full
-        if comm.mode == "sp" and any(lw.moe is not None for lw in self.layers):
-            raise ValueError("the sequence-parallel mode covers dense models; MoE models use tp_mode 'nvlink'")
-        for lw in self.layers:  # expert parallelism: all-reduce the local experts' partial output
-            if lw.moe is not None:
-                lw.moe.ep_reduce = lambda part, h: self.comm.allreduce_add(part, h)
+        moe = [lw.moe for lw in self.layers if lw.moe is not None]
+        if moe and comm.mode == "sp":
+            # expert parallelism with the all-to-all: the MoE scratch covers every source's slots
+            from ..models.moe import MoEScratch
+
+            comm.setup_ep(self.cfg.num_experts_per_tok, self.cfg.num_local_experts or self.cfg.num_experts)
+            self.moe_scratch = MoEScratch(self.cfg, comm.tp * comm.sp_rows_max, self.device)
+            for mo in moe:
+                mo.scratch = self.moe_scratch
+        else:
+            for mo in moe:  # expert parallelism: all-reduce the local experts' partial output
+                mo.ep_reduce = lambda part, h: self.comm.allreduce_add(part, h)
 
     def forward(self, st, m):
         if self.comm.mode != "sp":
@@ -62,10 +71,17 @@ class TPCudaRunner(CudaRunner):
             else:
                 qkv = comm.gemm_ag(lw.qkv, self.qkv[:T], T, False, ws)
             attn = self._attention(li, lw, qkv, st, m, dsplit)
-            comm.rs_norm_ag(h, lw.ln2, cfg.rms_eps, T, comm.gemm_rs(attn, lw.o, ws))
-            act = comm.gemm_ag(lw.gate_up, self.act[:T], T, True, ws)
+            e = comm.gemm_rs(attn, lw.o, ws)
+            if lw.moe is not None:  # owned rows normalised locally, then the expert all-to-all
+                comm.rs_norm_ag(h, lw.ln2, cfg.rms_eps, T, e, local_only=True)
+                r0, own = comm.ep_own(T)
+                e = lw.moe.forward_a2a(comm, xg[r0:r0 + own], T, ws)
+            else:
+                comm.rs_norm_ag(h, lw.ln2, cfg.rms_eps, T, e)
+                act = comm.gemm_ag(lw.gate_up, self.act[:T], T, True, ws)
+                e = comm.gemm_rs(act[:, : self.F], lw.down, ws)
             nxt = self.layers[li + 1].ln1 if li + 1 < L else self.norm
-            comm.rs_norm_ag(h, nxt, cfg.rms_eps, T, comm.gemm_rs(act[:, : self.F], lw.down, ws))
+            comm.rs_norm_ag(h, nxt, cfg.rms_eps, T, e)
         comm.ag_wait(T)
         B = st.logits_rows.shape[0]
         xs = torch.index_select(xg, 0, m["rows"], out=self.xs[:B])

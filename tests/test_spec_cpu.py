@@ -1,6 +1,7 @@
 """Speculative decoding on the CPU oracle: draft trees, n-gram lookup, the verifier's host
 restatement (greedy exactness and the lossless sampling property), and the engine paths
-(prompt lookup with branching trees, Jacobi, draft model) against plain greedy decoding.
+(prompt lookup with branching trees, Jacobi, draft model, Medusa heads) against plain greedy
+decoding.
 
 Mirrors the reference's greedy-identity contract (tests/test_prompt_lookup_batched.py):
 speculation must not change greedy output.
@@ -96,7 +97,8 @@ def _prompts():
 
 
 @pytest.mark.parametrize("spec", [SpecConfig("prompt_lookup", k=4, branches=3, max_nodes=12),
-                                  SpecConfig("jacobi", k=3), SpecConfig("draft", k=3, draft_model="tiny-llama")])
+                                  SpecConfig("jacobi", k=3), SpecConfig("draft", k=3, draft_model="tiny-llama"),
+                                  SpecConfig("medusa", k=3, medusa_heads="random:3", medusa_top_k=2)])
 def test_speculative_greedy_matches_plain_greedy(spec):
     sp = SamplingParams(max_tokens=24, ignore_eos=True)
     want = _engine().generate(_prompts(), sp)
@@ -174,3 +176,59 @@ def test_cpp_ngram_index_matches_python():
             assert len(cc) == pos
             for k, want in ((4, 1), (6, 3)):
                 assert cc.continuations(k, want) == py.continuations(toks[:pos], k, want)
+
+
+def test_medusa_heads_roundtrip_and_rank_paths(tmp_path):
+    from safetensors.torch import save_file
+
+    from squish_b200.engine.medusa import MedusaHeads, rank_paths
+
+    heads = MedusaHeads.random(64, 300, num_heads=3, num_layers=1, seed=1)
+    sd = heads.state_dict()
+    assert sorted(sd) == sorted([f"medusa_head.{i}.0.linear.{n}" for i in range(3) for n in ("weight", "bias")] +
+                                [f"medusa_head.{i}.1.weight" for i in range(3)])
+    save_file(sd, str(tmp_path / "medusa_lm_head.safetensors"))
+    back = MedusaHeads.load(tmp_path)
+    h = torch.randn(5, 64)
+    for a, b in zip(heads.logits(h), back.logits(h)):
+        torch.testing.assert_close(a, b)
+    # the reference's plain linear head (no residual block, a bias)
+    lin = {"medusa_head.0.0.weight": torch.randn(300, 64), "medusa_head.0.0.bias": torch.randn(300)}
+    one = MedusaHeads.from_state_dict(lin)
+    want = h @ lin["medusa_head.0.0.weight"].T + lin["medusa_head.0.0.bias"]
+    torch.testing.assert_close(one.logits(h)[0], want)
+    assert one.topk(h, 3).shape == (5, 1, 3)
+    assert np.array_equal(one.topk(h, 3)[:, 0], want.topk(3, -1).indices.numpy())
+    p = rank_paths(3, 2, 5)
+    assert p[0] == (0, 0, 0) and sorted(p[1:4]) == [(0, 0, 1), (0, 1, 0), (1, 0, 0)] and sum(p[4]) == 2
+
+
+def test_medusa_sees_the_rows_that_produced_each_token():
+    """The Medusa proposer gets, after every step, the final-norm hidden row whose logits gave
+    each request's newest token (decode rows and the last accepted node of a verified tree);
+    with oracle candidates (the true continuation at rank 1) drafts are accepted and greedy
+    output is unchanged."""
+    prompt = _prompts()[1]
+    sp = SamplingParams(max_tokens=16, ignore_eos=True)
+    want = _engine().generate([prompt], sp)[0]
+    eng = _engine(SpecConfig("medusa", k=3, medusa_heads="random:3", medusa_top_k=2, medusa_paths=8,
+                             max_nodes=16, adaptive=False))
+    prop = eng.proposer
+    lm = eng.runner.ref.w["lm_head.weight"].float()
+    seen = []
+
+    def observe(reqs, hidden):
+        for r, h in zip(reqs, hidden):
+            seen.append(int((h.float() @ lm.T).argmax()) == r.output[-1])
+            done = len(r.output)
+            true = (want[done:done + 3] + [0, 0, 0])[:3]
+            cand = np.zeros((3, 2), dtype=np.int32)
+            cand[:, 0] = [(t + 1) % 32000 for t in true]
+            cand[:, 1] = true
+            prop.cands[r.rid] = cand
+
+    prop.observe = observe
+    got = eng.generate([prompt], sp)[0]
+    assert got == want
+    assert seen and all(seen), seen
+    assert eng.spec_stats["accepted"] > 0

@@ -131,7 +131,8 @@ def test_kv_compact_moves_rows(cuda):
 
 
 @pytest.mark.parametrize("spec", [SpecConfig("prompt_lookup", k=4, branches=3, max_nodes=12),
-                                  SpecConfig("jacobi", k=3), SpecConfig("draft", k=3, draft_model="tiny-llama")])
+                                  SpecConfig("jacobi", k=3), SpecConfig("draft", k=3, draft_model="tiny-llama"),
+                                  SpecConfig("medusa", k=3, medusa_heads="random:3", medusa_top_k=2)])
 def test_speculative_engine_matches_oracle(cuda, spec):
     cfg, q = get_preset("tiny-llama")
     rng = np.random.default_rng(3)
@@ -151,3 +152,27 @@ def test_speculative_engine_matches_oracle(cuda, spec):
     # sampled speculation runs too (temperature only)
     o2 = eng.generate(prompts[:1], SamplingParams(max_tokens=16, temperature=0.8, ignore_eos=True))[0]
     assert len(o2) == 16
+
+
+def test_medusa_heads_int4_projection_matches_fp32(cuda):
+    """On the GPU the heads' vocabulary projections are INT4 weights run by the W4A16 GEMM:
+    logits against the fp32 heads with the dequantized projection."""
+    from squish_b200._ext import native
+    from squish_b200.engine.medusa import MedusaHeads
+
+    cpu = MedusaHeads.random(256, 1000, num_heads=2, num_layers=1, seed=4)
+    dev = MedusaHeads.from_state_dict(cpu.state_dict(), device=cuda)
+    assert dev.quantized
+    h = torch.randn(7, 256)
+    got = dev.logits(h.to(cuda))
+    for i, g in enumerate(got):
+        sd = cpu.state_dict()
+        u = sd[f"medusa_head.{i}.1.weight"]
+        p, s, z = native().cpu.quantize_int4_asym(u, 64)
+        uq = native().cpu.dequantize_int4_asym(p, s, z, 64)
+        w, b = sd[f"medusa_head.{i}.0.linear.weight"], sd[f"medusa_head.{i}.0.linear.bias"]
+        r = h.to(torch.bfloat16).float()
+        r = r + torch.nn.functional.silu(r @ w.T + b)
+        want = r @ uq.T
+        err = (g.cpu() - want).abs().max().item()
+        assert err <= 0.03 * want.abs().max().item(), err

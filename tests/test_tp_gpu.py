@@ -1,7 +1,8 @@
 """Tensor parallelism on 2 GPUs (skipped with fewer): the fused GEMM+all-reduce over NVLink
 peer memory, the sequence-parallel GEMM->reduce-scatter / RMSNorm+all-gather / gather-waiting
-GEMM and the vocab gather against fp32 references, and the tensor-parallel engine (fused,
-sequence-parallel and NCCL modes) against the CPU fp32 oracle."""
+GEMM, the expert-parallel all-to-all and the vocab gather against fp32 references, and the
+tensor-parallel engine (fused, sequence-parallel and NCCL modes; dense and MoE) against the
+CPU fp32 oracle."""
 import dataclasses
 import datetime
 import os
@@ -150,6 +151,80 @@ def _sp_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+def _ep_worker(rank, world, port, q):
+    """Expert-parallel all-to-all (dispatch of the owned rows to the experts' ranks, local
+    grouped INT4 experts, combine back through the reduce-scatter blocks, residual + RMSNorm)
+    against an fp32 reference of the same experts with the GPU's own routing decisions."""
+    _init(rank, world, port)
+    try:
+        from squish_b200 import ops
+        from squish_b200.models.config import get_preset
+        from squish_b200.models.moe import MoELayer, MoEScratch
+        from squish_b200.models.weights import random_checkpoint
+        from squish_b200.parallel.comm import TPComm
+        from squish_b200.parallel.shard import shard_checkpoint
+
+        dev = torch.device("cuda", rank)
+        cfg, qc = get_preset("tiny-moe")
+        ck = random_checkpoint(cfg, qc, seed=3, device="cpu")
+        local = shard_checkpoint(ck, rank, world)
+        lc = local.config
+        H, Tmax, kk = cfg.hidden_size, 512, cfg.num_experts_per_tok
+        comm = TPComm("sp", Tmax, H, 64, cfg.vocab_size, device=dev)
+        comm.setup_ep(kk, lc.num_local_experts)
+        layer = MoELayer.from_checkpoint(local, 0, dev, MoEScratch(lc, world * comm.sp_rows_max, dev))
+        ws = ops.Workspace(dev)
+        pre = "model.layers.0.mlp.experts."
+        experts = {}
+
+        def expert(e):
+            if e not in experts:
+                experts[e] = [ck[f"{pre}{e}.{n}.weight"].dequantize() for n in ("gate_proj", "up_proj", "down_proj")]
+            return experts[e]
+
+        wg = ck["model.layers.0.mlp.gate.weight"].data.to(torch.bfloat16).float()
+        errs, route_ok = [], True
+        for T in (1, 3, 64, 300):
+            g = torch.Generator().manual_seed(T)  # the same rows on every rank
+            x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+            h0 = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16)
+            lnw = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+            r0, own = comm.ep_own(T)
+            h = h0.to(dev)
+            for _ in range(3):  # repeated rounds exercise the counters and the buffer reuse
+                hh = h.clone()
+                comm.xg[r0:r0 + own].copy_(x[r0:r0 + own].to(dev))
+                e = layer.forward_a2a(comm, comm.xg[r0:r0 + own], T, ws)
+                comm.rs_norm_ag(hh, lnw.to(dev), 1e-6, T, e)
+                comm.ag_wait(T)
+            torch.cuda.synchronize()
+            comm.check()
+            if own == 0:
+                continue
+            ti = layer.scratch.ids[: own * kk].view(own, kk).cpu()
+            tv = layer.scratch.w[: own * kk].view(own, kk).cpu()
+            xf = x[r0:r0 + own].float()
+            p = torch.softmax((xf @ wg.T).to(torch.bfloat16).float(), -1)
+            route_ok &= bool((torch.gather(p, 1, ti.long()) >= p.topk(kk, -1).values[:, -1:] - 2e-2).all())
+            out = h0[r0:r0 + own].float().clone()
+            for t in range(own):
+                for j in range(kk):
+                    gw, uw, dw = expert(int(ti[t, j]))
+                    a = (torch.nn.functional.silu(xf[t] @ gw.T) * (xf[t] @ uw.T)).to(torch.bfloat16).float()
+                    out[t] += tv[t, j] * (a @ dw.T)
+            got = hh[r0:r0 + own].float().cpu()
+            scale = (out - h0[r0:r0 + own].float()).abs().max().item()
+            errs.append(((got - out).abs().max().item() - 2e-3) / max(scale, 1e-6))
+            # the owned rows of the gathered buffer hold RMSNorm of the stored residual rows
+            xn = (got * torch.rsqrt(got.pow(2).mean(-1, keepdim=True) + 1e-6) * lnw.float()).to(torch.bfloat16)
+            errs.append(float((comm.xg[r0:r0 + own].float().cpu() - xn.float()).abs().max())
+                        / float(xn.float().abs().max()))
+        comm.close()
+        q.put((rank, errs, route_ok))
+    finally:
+        dist.destroy_process_group()
+
+
 def _engine_worker(rank, world, port, mode, preset, q):
     _init(rank, world, port)
     try:
@@ -215,8 +290,16 @@ def test_sequence_parallel_collectives():
 
 
 @needs2
+def test_expert_parallel_all_to_all():
+    res = _run(_ep_worker, 2)
+    for rank, errs, route_ok in res:
+        assert route_ok
+        assert max(errs) < 2e-2, errs
+
+
+@needs2
 @pytest.mark.parametrize("mode,preset", [("nvlink", "tiny-llama"), ("nccl", "tiny-llama"), ("sp", "tiny-llama"),
-                                         ("nvlink", "tiny-moe"), ("nccl", "tiny-moe")])
+                                         ("nvlink", "tiny-moe"), ("nccl", "tiny-moe"), ("sp", "tiny-moe")])
 def test_tp_engine_matches_oracle(mode, preset):
     from squish_b200.models.reference import ReferenceModel
     from squish_b200.models.weights import random_checkpoint
