@@ -283,7 +283,7 @@ def cmd_compress(a) -> int:
     from .io.convert import compress
 
     kind = {"int4": "q4a", "int8": "q8", "fp8": "fp8", "nf4": "nf4", "int3": "q3", "int2": "q2", "sqint2": "sqint2",
-            "mixed": "mixed", "aqlm": "aqlm",
+            "mixed": "mixed", "aqlm": "aqlm", "any4": "any4", "quarot": "quarot",
             "none": "dense"}[a.format]
     out = a.output or (str(Path(a.source).with_name(Path(a.source).name + "-squished")) if a.source else
                        str(ucfg.squish_home() / "models" / a.random_init))
@@ -535,8 +535,11 @@ def build_parser() -> argparse.ArgumentParser:
     p = sub.add_parser("compress")
     p.add_argument("source", nargs="?", default=None)
     p.add_argument("-o", "--output", default=None)
-    p.add_argument("--format", default="int4", choices=["int4", "int8", "fp8", "nf4", "int3", "int2", "sqint2", "mixed", "aqlm", "none"],
-                   help="mixed: INT4 boundary layers, INT3 attention, SQINT2 gate/up, INT4 elsewhere")
+    p.add_argument("--format", default="int4",
+                   choices=["int4", "int8", "fp8", "nf4", "any4", "quarot", "int3", "int2", "sqint2", "mixed", "aqlm",
+                            "none"],
+                   help="mixed: INT4 boundary layers, INT3 attention, SQINT2 gate/up, INT4 elsewhere; any4: NF4 codes "
+                        "with a learned 16-level table per tensor; quarot: INT4 of the block-Hadamard rotated weight")
     p.add_argument("--group-size", type=int, default=64)
     p.add_argument("--mse", action="store_true", help="MSE-optimal clipping search (INT4)")
     p.add_argument("--random-init", default=None, metavar="PRESET")

@@ -193,6 +193,14 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t group = 
   return {bn, nt, splits, kps, tiles};
 }
 
+// NF4-format weights may carry a learned 16-level table (any4) in place of the NormalFloat levels
+static void check_level_table(int64_t wfmt, const c10::optional<torch::Tensor>& codebook) {
+  if (wfmt == sq::WF_NF4 && codebook.has_value())
+    TORCH_CHECK(codebook->scalar_type() == torch::kBFloat16 && codebook->is_cuda() && codebook->is_contiguous() &&
+                    codebook->numel() == 16,
+                "a 4-bit level table is 16 contiguous bf16 values on the device");
+}
+
 void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, int64_t K, int64_t group,
                 torch::Tensor y, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> residual,
                 int64_t epilogue, torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
@@ -205,6 +213,7 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, int64_t N, 
                     codebook->is_contiguous() && codebook->numel() % (256 * 8) == 0 && codebook->numel() <= 2 * 256 * 8,
                 "AQLM needs 1 or 2 contiguous bf16 codebooks of 256 x 8 on the device");
   }
+  check_level_table(wfmt, codebook);
   CHECK_CUDA(x);
   CHECK_DT(x, torch::kBFloat16);
   CHECK_DT(y, torch::kBFloat16);
@@ -266,6 +275,7 @@ void dequant_weight(torch::Tensor wq, int64_t N, int64_t K, int64_t group, int64
                   out.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
               "out must be [>= N, >= 64 * ceil(K / 64)] bf16 with 16-byte aligned rows");
   if (wfmt == sq::WF_AQLM) TORCH_CHECK(codebook.has_value(), "AQLM weights need their codebooks");
+  check_level_table(wfmt, codebook);
   const c10::cuda::CUDAGuard g(wq.device());
   CUDA_OK(sq::dequant_weight_launch(ptr<uint32_t>(wq), (int)wfmt, (int)N, (int)K, (int)group, (int)out.stride(0),
                                     ptr<__nv_bfloat16>(out), optr<__nv_bfloat16>(codebook),

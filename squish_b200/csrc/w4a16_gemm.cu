@@ -381,9 +381,11 @@ __global__ void __launch_bounds__(C::kThreads, C::kMinBlocks)
   __shared__ uint4 fmt_tab[C::kFmtTab];
   uint32_t* nf4_lut = reinterpret_cast<uint32_t*>(fmt_tab);
   if constexpr (C::kFmtTab >= 512) {
-    if (p.wfmt == WF_NF4) {
+    if (p.wfmt == WF_NF4) {  // NormalFloat-4 levels, or a learned 16-level table (any4) in codebook
       for (int i = threadIdx.x; i < 256; i += blockDim.x)
-        nf4_lut[i] = bf2_bits(__floats2bfloat162_rn(kNf4Levels[i & 15], kNf4Levels[i >> 4]));
+        nf4_lut[i] = bf2_bits(p.codebook != nullptr
+                                  ? __halves2bfloat162(p.codebook[i & 15], p.codebook[i >> 4])
+                                  : __floats2bfloat162_rn(kNf4Levels[i & 15], kNf4Levels[i >> 4]));
     } else if (p.wfmt == WF_AQLM) {
       for (int i = threadIdx.x; i < 256 * p.n_books; i += blockDim.x)
         fmt_tab[i] = reinterpret_cast<const uint4*>(p.codebook)[i];
@@ -1058,7 +1060,8 @@ __global__ void __launch_bounds__(256) dequant_weight_kernel(const uint8_t* __re
   uint32_t* lut = reinterpret_cast<uint32_t*>(fmt_tab);
   if (wfmt == WF_NF4) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x)
-      lut[i] = bf2_bits(__floats2bfloat162_rn(kNf4Levels[i & 15], kNf4Levels[i >> 4]));
+      lut[i] = bf2_bits(codebook != nullptr ? __halves2bfloat162(codebook[i & 15], codebook[i >> 4])
+                                            : __floats2bfloat162_rn(kNf4Levels[i & 15], kNf4Levels[i >> 4]));
   } else if (wfmt == WF_AQLM) {
     for (int i = threadIdx.x; i < 256 * n_books; i += blockDim.x) fmt_tab[i] = reinterpret_cast<const uint4*>(codebook)[i];
   }

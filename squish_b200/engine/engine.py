@@ -787,7 +787,10 @@ class LLMEngine:
         if not live:
             return
         hid = self.runner.last_hidden
-        idx = torch.tensor([i for _, i in live], dtype=torch.long, device=hid.device)
+        rows = [i for _, i in live]
+        if max(rows) >= hid.shape[0]:  # checked on the host: a bad row must not reach a device gather
+            raise RuntimeError(f"hidden row {max(rows)} outside the step's {hid.shape[0]} logits rows")
+        idx = torch.tensor(rows, dtype=torch.long, device=hid.device)
         self.proposer.observe([r for r, _ in live], hid.index_select(0, idx))
 
     def _publish_blocks(self, r: Request) -> None:

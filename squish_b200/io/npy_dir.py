@@ -16,6 +16,9 @@ Suffix sets, in the reference loader's dispatch priority (squish/io/loader_utils
     __aqlm_idx + __aqlm_cb              AQLM additive codebooks
     __q + __s                           INT8 symmetric (per row or per group)
     __f8 + __sf8                        FP8 E4M3 codes + per-group scales (this package's extension)
+    __nf4 + __s_nf4 + __lv_nf4          any4: NF4 codes with a learned 16-level table (extension)
+    __q4a + ... + __rot_signs (+ __rot_meta) QuaRot: INT4 asymmetric codes of W R^T, R the block
+                                        Hadamard over these input signs (extension)
     __sqint2_idx/_scales/_zp/_meta(+_L/_R) SQINT2 (Hadamard-rotated NF2 INT2, quant/sqint2.py)
     __pt_df11                           lossless bf16 passthrough, DFloat11-style (io/entropy.py df11_*)
     __vq_idx + __vq_cb (+ __vq_res, __vq_rescb, __vq_cols) + __vq_meta
@@ -39,7 +42,8 @@ import torch
 
 from ..models.weights import Checkpoint, QTensor
 
-SUFFIXES = ("__pt_df11", "__vq_idx", "__vq_cb", "__vq_res", "__vq_rescb", "__vq_cols", "__vq_meta", "__nf4", "__s_nf4", "__q4a", "__s4a", "__z4a", "__q4", "__s4", "__q3", "__s3", "__z3", "__lra",
+SUFFIXES = ("__pt_df11", "__vq_idx", "__vq_cb", "__vq_res", "__vq_rescb", "__vq_cols", "__vq_meta", "__lv_nf4", "__nf4",
+            "__s_nf4", "__rot_signs", "__rot_meta", "__q4a", "__s4a", "__z4a", "__q4", "__s4", "__q3", "__s3", "__z3", "__lra",
             "__lrb", "__q2", "__s2", "__z2", "__aqlm_idx", "__aqlm_cb", "__f8", "__sf8", "__q", "__s", "__pt", "__shape")
 
 
@@ -94,16 +98,23 @@ def read_tensor(td: Path, key: str) -> QTensor:
         return QTensor("dense", shape or tuple(d.shape), data=d.reshape(shape) if shape else d)
     if _exists(td, key, "__nf4") and _exists(td, key, "__s_nf4"):
         p, s = arr("__nf4", np.uint8), arr("__s_nf4", np.float32)
-        return QTensor("nf4", shape or (p.shape[0], p.shape[1] * 2), packed=p, scales=s,
-                       group=(p.shape[1] * 2) // s.shape[1])
+        t = QTensor("nf4", shape or (p.shape[0], p.shape[1] * 2), packed=p, scales=s,
+                    group=(p.shape[1] * 2) // s.shape[1])
+        if _exists(td, key, "__lv_nf4"):
+            t.extra = {"levels": arr("__lv_nf4", np.float32)}
+        return t
     if _exists(td, key, "__vq_idx"):
         d = torch.from_numpy(read_vptq(lambda suf: np.asarray(_load(td / f"{key}{suf}.npy")),
                                        lambda suf: _exists(td, key, suf)))
         return QTensor("dense", shape or tuple(d.shape), data=d.reshape(shape) if shape else d)
     if _exists(td, key, "__q4a"):
         p, s, z = arr("__q4a", np.uint8), arr("__s4a", np.float32), arr("__z4a", np.float32)
-        return QTensor("q4a", shape or (p.shape[0], p.shape[1] * 2), packed=p, scales=s, offsets=z,
-                       group=(p.shape[1] * 2) // s.shape[1])
+        t = QTensor("q4a", shape or (p.shape[0], p.shape[1] * 2), packed=p, scales=s, offsets=z,
+                    group=(p.shape[1] * 2) // s.shape[1])
+        if _exists(td, key, "__rot_signs"):
+            meta = arr("__rot_meta", np.int64)
+            t.extra = {"rot_signs": arr("__rot_signs", np.float32), "rot_block": int(meta[0]), "seed": int(meta[1])}
+        return t
     if _exists(td, key, "__q4"):
         p, s = arr("__q4", np.uint8), arr("__s4", np.float32)
         if s.dim() == 1:
@@ -210,8 +221,14 @@ def tensor_files(name: str, t: QTensor, df11: bool = False) -> dict[str, np.ndar
     if t.kind == "q4a":
         out.update({f"{k}__q4a": np_(t.packed, np.uint8), f"{k}__s4a": np_(t.scales, np.float32),
                     f"{k}__z4a": np_(t.offsets, np.float32)})
+        if t.extra and "rot_signs" in t.extra:
+            out[f"{k}__rot_signs"] = np_(t.extra["rot_signs"], np.float32)
+            out[f"{k}__rot_meta"] = np.asarray([int(t.extra["rot_block"]), int(t.extra.get("seed", 0))],
+                                               dtype=np.int64)
     elif t.kind == "nf4":
         out.update({f"{k}__nf4": np_(t.packed, np.uint8), f"{k}__s_nf4": np_(t.scales, np.float32)})
+        if t.extra and "levels" in t.extra:
+            out[f"{k}__lv_nf4"] = np_(t.extra["levels"], np.float32)
     elif t.kind == "q8":
         out.update({f"{k}__q": np_(t.packed, np.int8), f"{k}__s": np_(t.scales, np.float32)})
     elif t.kind == "fp8":

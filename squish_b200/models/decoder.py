@@ -129,13 +129,24 @@ def _same_rotation(parts: list[QTensor]) -> bool:
     return True
 
 
+def _levels(t: QTensor):
+    return (t.extra or {}).get("levels")
+
+
+def _same_levels(parts: list[QTensor]) -> bool:
+    l0 = _levels(parts[0])
+    return all((_levels(p) is None) == (l0 is None) and (l0 is None or torch.equal(_levels(p), l0))
+               for p in parts[1:])
+
+
 def _same_kind(parts: list[QTensor], group: int) -> list[QTensor]:
     """Tensors fused into one GEMM must share a native kind, group and input rotation; otherwise
     all are re-encoded as INT4."""
     k0 = parts[0].kind
-    # AQLM tensors carry their own codebooks, so they cannot share one fused GEMM
+    # AQLM tensors carry their own codebooks, so they cannot share one fused GEMM; any4 tensors
+    # (NF4 codes with a learned level table) only when their tables agree
     if (k0 in GEMM_KINDS and all(p.kind == k0 and p.group == parts[0].group for p in parts)
-            and not (k0 == "aqlm" and len(parts) > 1) and _same_rotation(parts)):
+            and not (k0 == "aqlm" and len(parts) > 1) and _same_rotation(parts) and _same_levels(parts)):
         return parts
     return [_as_q4a(p, group) if p.kind != "q4a" else p for p in parts]
 
@@ -147,7 +158,7 @@ def _cat_rows(parts: list[QTensor]) -> QTensor:
 
     return QTensor(parts[0].kind, (sum(p.shape[0] for p in parts), parts[0].shape[1]), packed=cat("packed"),
                    scales=cat("scales"), offsets=cat("offsets"), group=parts[0].group,
-                   extra=parts[0].extra if _rotation(parts[0]) else None)
+                   extra=parts[0].extra if (_rotation(parts[0]) or _levels(parts[0]) is not None) else None)
 
 
 _cat_q4a = _cat_rows
@@ -186,11 +197,20 @@ def _as_q4a(t: QTensor, group: int) -> QTensor:
     return quantize(t.dequantize().float(), "q4a", group)
 
 
+def gemm_extra_ok(t: QTensor) -> bool:
+    """Extras the GEMM handles as stored: an input rotation (SQINT2 INT2, QuaRot INT4 / INT2),
+    an any4 level table on NF4 codes."""
+    if not t.extra:
+        return True
+    if t.kind in ("q2", "q4a"):
+        return set(t.extra) <= {"rot_signs", "rot_block", "seed"}
+    return t.kind == "nf4" and set(t.extra) <= {"levels"}
+
+
 def _native(t: QTensor, group: int) -> QTensor:
-    """Kinds the GEMM decodes as stored; SQINT2 (INT2 with an input rotation) too, unless it
-    carries a low-rank residual."""
-    rot_only = t.kind == "q2" and t.extra and set(t.extra) <= {"rot_signs", "rot_block", "seed"}
-    return t if t.kind in GEMM_KINDS and (not t.extra or rot_only) else _as_q4a(t, group)
+    """Kinds the GEMM decodes as stored (with the extras of ``gemm_extra_ok``); others, and
+    SQINT2 with a low-rank residual, are re-encoded as INT4."""
+    return t if t.kind in GEMM_KINDS and gemm_extra_ok(t) else _as_q4a(t, group)
 
 
 def _to_int4(t: QTensor, device, bias: torch.Tensor | None = None, group: int = 64) -> Int4Weight:
@@ -611,7 +631,7 @@ class CudaRunner:
         self.timer_stop()
         self.sync()
         self.last_logits = logits if st.all_logits else None
-        self.last_hidden = self.xs[:B]
+        self.last_hidden = self.xs[:logits.shape[0]]  # every logits row: sampled, then verified nodes
         if G:
             self.last_verify = self.vout_host[:G].numpy().copy()
             nv = logits.shape[0] - nS

@@ -48,7 +48,12 @@ class QTensor:
         q[:, 1::2] = ((p >> 4) & 0xF).float()
         s = self.scales.float().repeat_interleave(self.group, dim=1)[:, : q.shape[1]]
         o = self.offsets.float().repeat_interleave(self.group, dim=1)[:, : q.shape[1]]
-        return o + q * s
+        w = o + q * s
+        if self.extra and "rot_signs" in self.extra:  # QuaRot: stored in the rotated frame (W R^T)
+            from ..quant.sqint2 import unrotate
+
+            w = unrotate(w, self.extra["rot_signs"], int(self.extra["rot_block"]))
+        return w
 
 
 @dataclass

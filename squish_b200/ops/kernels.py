@@ -121,7 +121,7 @@ class Int4Weight:
     group: int
     bias: torch.Tensor | None = None
     fmt: int = 0  # WF_INT4 | WF_NF4 | WF_INT8 | WF_INT2 | WF_INT3 | WF_AQLM | WF_FP8
-    codebook: torch.Tensor | None = None  # WF_AQLM: [books, 256, 8] bf16
+    codebook: torch.Tensor | None = None  # WF_AQLM: [books, 256, 8] bf16; WF_NF4 (any4): [16] bf16 levels
     # optional resident bf16 expansion [n, 64 * ceil(k / 64)] for large-M GEMMs (the exact
     # values the quantized GEMM computes with); None = expand per call
     dense: torch.Tensor | None = None
@@ -227,11 +227,19 @@ def prepare_weight(t, device, bias: torch.Tensor | None = None) -> Int4Weight:
     if t.kind == "q4a":
         w = prepare_int4_weight(t.packed, t.scales, t.offsets, k, t.group, dev)
         w.bias = b
+        if t.extra and "rot_signs" in t.extra:  # QuaRot: stored rotated, the input is rotated first
+            w.rot = t.extra["rot_signs"].to(dev, torch.float32).contiguous()
+            w.rot_block = int(t.extra["rot_block"])
         return w
     p = t.packed.to(dev)
     if t.kind == "nf4":
         codes = torch.stack([p & 0xF, p >> 4], dim=-1).reshape(p.shape[0], -1)
         wt = repack_codes(codes, t.scales.to(dev), None, k, t.group, WF_NF4)
+        lv = (t.extra or {}).get("levels")
+        if lv is not None:  # any4: a learned 16-level table in place of the NormalFloat levels
+            return Int4Weight(wq=wt, sz=torch.empty(0, dtype=torch.int32, device=dev), n=int(t.shape[0]), k=k,
+                              group=int(t.group), bias=b, fmt=WF_NF4,
+                              codebook=lv.to(dev, torch.float32).to(torch.bfloat16).contiguous())
         fmt = WF_NF4
     elif t.kind == "q8":
         wt = repack_codes(p.view(torch.uint8), t.scales.to(dev), None, k, t.group, WF_INT8)

@@ -29,11 +29,14 @@ from ..models.weights import Checkpoint, QTensor
 def _rows(t: QTensor, r0: int, r1: int) -> QTensor:
     if t.kind == "dense":
         return QTensor("dense", (r1 - r0,) + tuple(t.shape[1:]), data=t.data[r0:r1].contiguous())
-    rot_only = t.kind == "q2" and t.extra and set(t.extra) <= {"rot_signs", "rot_block", "seed"}
+    from ..models.decoder import gemm_extra_ok
+
+    rot_only = bool(t.extra) and gemm_extra_ok(t)
     if t.kind not in ("q4a", "q8", "fp8", "nf4", "q2", "q3") or (t.extra and not rot_only):
         t = _to_q4a(t)
         rot_only = False
-    # a row slice keeps the input rotation of an SQINT2 weight (it acts on the columns)
+    # a row slice keeps the input rotation of an SQINT2 weight (it acts on the columns) and the
+    # level table of an any4 weight
     return dataclasses.replace(t, shape=(r1 - r0, t.shape[1]), packed=t.packed[r0:r1].contiguous(),
                                scales=t.scales[r0:r1].contiguous(),
                                offsets=None if t.offsets is None else t.offsets[r0:r1].contiguous(),
@@ -49,7 +52,7 @@ def _to_q4a(t: QTensor) -> QTensor:
 def _cols(t: QTensor, c0: int, c1: int) -> QTensor:
     if t.kind == "dense":
         return QTensor("dense", (t.shape[0], c1 - c0), data=t.data[:, c0:c1].contiguous())
-    if t.kind != "q4a":
+    if t.kind != "q4a" or t.extra:  # (an input rotation does not survive a column slice)
         t = _to_q4a(t)
     g = t.group
     if c0 % g or c1 % g or c0 % 2:

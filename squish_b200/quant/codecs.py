@@ -18,8 +18,20 @@ def dequantize_qtensor(t: QTensor) -> torch.Tensor:
     C = native().cpu
     k = t.kind
     if k == "q4a":
-        return C.dequantize_int4_asym(t.packed.cpu(), t.scales.cpu().float(), t.offsets.cpu().float(), t.group)
+        w = C.dequantize_int4_asym(t.packed.cpu(), t.scales.cpu().float(), t.offsets.cpu().float(), t.group)
+        if t.extra and "rot_signs" in t.extra:  # QuaRot: stored in the rotated frame
+            from .sqint2 import unrotate
+
+            w = unrotate(w, t.extra["rot_signs"], int(t.extra["rot_block"]))
+        return w
     if k == "nf4":
+        lv = (t.extra or {}).get("levels")
+        if lv is not None:  # any4: codes index a learned 16-level table
+            p = t.packed.cpu()
+            codes = torch.stack([p & 0xF, p >> 4], dim=-1).reshape(p.shape[0], -1).long()
+            # the GEMM multiplies bf16 levels by bf16 scales: match its table precision
+            levels = lv.float().cpu().to(torch.bfloat16).float()
+            return levels[codes] * t.scales.cpu().float().repeat_interleave(t.group, dim=1)[:, : codes.shape[1]]
         return C.dequantize_nf4(t.packed.cpu(), t.scales.cpu().float(), t.group)
     if k == "q8":
         return C.dequantize_int8(t.packed.cpu(), t.scales.cpu().float())
@@ -116,7 +128,8 @@ def dequantize_fp8(codes: torch.Tensor, scales: torch.Tensor, fmt: str = "e4m3")
 
 def quantize(w: torch.Tensor, kind: str, group: int, mse_clip: bool = False, hqq: bool = False,
              hqq_iters: int = 10) -> QTensor:
-    """Quantize a 2-D weight to ``kind`` (q4a | q8 | fp8 | nf4 | q2 | sqint2 | q3 | aqlm | dense).
+    """Quantize a 2-D weight to ``kind`` (q4a | q8 | fp8 | nf4 | any4 | quarot | q2 | sqint2 | q3 | aqlm |
+    dense).
     ``hqq``: refine the INT4 / INT2 affine grids by half-quadratic quantization (quant/hqq.py)."""
     from ..models.weights import pick_group, quantize_q4a
 
@@ -157,6 +170,15 @@ def quantize(w: torch.Tensor, kind: str, group: int, mse_clip: bool = False, hqq
     if kind == "nf4":
         p, s = C.quantize_nf4(wf, g)
         return QTensor("nf4", tuple(wf.shape), packed=p, scales=s, group=g)
+    if kind == "any4":
+        from .research import quantize_any4
+
+        return quantize_any4(wf, g)
+    if kind == "quarot":
+        from .research import quarot_quantize
+        from .sqint2 import rotation_block
+
+        return quarot_quantize(wf, g, bits=4, block=rotation_block(wf.shape[1]))
     if kind == "q2":
         p, s, z = C.quantize_int2(wf, g)
         return QTensor("q2", tuple(wf.shape), packed=p, scales=s, offsets=z, group=g)

@@ -1,4 +1,5 @@
-"""The INT4 GEMM kernel's other code formats (NF4, INT8, INT2) against a plain PyTorch fp32
+"""The INT4 GEMM kernel's other code formats (NF4, any4 learned 4-bit tables, QuaRot rotated
+INT4, INT8, INT2) against a plain PyTorch fp32
 reference of the same dequantized weight, the tensor-op repack against the CUDA INT4
 repack, and an engine whose linear layers are NF4 / INT8 / INT2 against the CPU oracle."""
 import dataclasses
@@ -15,8 +16,9 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("kind,group", [("nf4", 64), ("nf4", 32), ("q8", 64), ("q8", 32), ("q2", 64), ("q2", 128),
-                                        ("q3", 64), ("q3", 32), ("aqlm", 8), ("fp8", 64), ("fp8", 32)])
-@pytest.mark.parametrize("m", [1, 37, 64, 300])
+                                        ("q3", 64), ("q3", 32), ("aqlm", 8), ("fp8", 64), ("fp8", 32),
+                                        ("any4", 64), ("any4", 32)])
+@pytest.mark.parametrize("m", [1, 37, 64, 300, 512])
 def test_gemm_formats_match_fp32(cuda, kind, group, m):
     g = torch.Generator().manual_seed(m + group)
     n, k = 640, 1024
@@ -42,7 +44,27 @@ def test_tensor_op_repack_equals_cuda_int4_repack(cuda):
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("kind", ["nf4", "q8", "q2", "q3", "aqlm", "fp8"])
+@pytest.mark.parametrize("m", [1, 64, 512])
+def test_quarot_rotated_int4_gemm_matches_fp32(cuda, m):
+    """QuaRot INT4 weights (stored as W R^T): the runner rotates the input with the same
+    block Hadamard and the GEMM computes (W R^T)(R x) = W x."""
+    from squish_b200.quant.research import quarot_quantize
+
+    g = torch.Generator().manual_seed(m)
+    w = torch.randn(640, 1024, generator=g) * 0.05
+    w[:, 7] *= 30
+    t = quarot_quantize(w, 64, bits=4, block=128, seed=3)
+    dw = K.prepare_weight(t, cuda)
+    assert dw.rot is not None and dw.rot_block == 128
+    x = torch.randn(m, 1024, generator=g).to(torch.bfloat16)
+    y = ops.w4a16_linear(x.to(cuda), dw)
+    torch.cuda.synchronize()
+    ref = x.float() @ t.dequantize().float().T
+    err = (y.float().cpu() - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item() + 1e-2, err
+
+
+@pytest.mark.parametrize("kind", ["nf4", "q8", "q2", "q3", "aqlm", "fp8", "any4"])
 def test_engine_with_format_weights_matches_oracle(cuda, kind):
     from squish_b200.engine.engine import EngineConfig, LLMEngine
     from squish_b200.engine.sampling import SamplingParams
