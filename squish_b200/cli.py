@@ -59,6 +59,11 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
     p.add_argument("--kv-sink-tokens", type=int, default=0, help="attention sinks kept with --kv-window-tokens")
     p.add_argument("--kv-window-tokens", type=int, default=0,
                    help="> 0: attend to the sink pages and the most recent N tokens only; older KV pages are freed")
+    p.add_argument("--kv-h2o-budget", type=int, default=0,
+                   help="> 0: heavy-hitter eviction keeps at most N tokens per sequence (least-attended pages go)")
+    p.add_argument("--kv-h2o-interval", type=int, default=4, help="decode steps between attention-mass refreshes")
+    p.add_argument("--kv-h2o-decay", type=float, default=1.0,
+                   help="score decay per refresh (1 = accumulated H2O scores; < 1 favours recent queries)")
     # speculative decoding (the reference serves with prompt lookup on: squish/server.py:5194)
     sp = ucfg.load()["speculative"]
     p.add_argument("--prompt-lookup", dest="prompt_lookup", action="store_true", default=bool(sp["prompt_lookup"]),
@@ -136,7 +141,9 @@ def _ecfg(a):
                         chunk_align=a.chunk_align, seed=a.seed, kv_host_bytes=int(a.kv_host_gb * (1 << 30)),
                         kv_disk_dir=a.kv_disk_dir, spec=_spec(a), tp=tp, tp_mode=getattr(a, "tp_mode", "nvlink"),
                         prompt_logit_cache=a.prompt_logit_cache, kv_sink_tokens=a.kv_sink_tokens,
-                        kv_window_tokens=a.kv_window_tokens, pp=a.pp, offload_layers=a.offload_layers)
+                        kv_window_tokens=a.kv_window_tokens, pp=a.pp, offload_layers=a.offload_layers,
+                        kv_h2o_budget=getattr(a, "kv_h2o_budget", 0), kv_h2o_interval=getattr(a, "kv_h2o_interval", 4),
+                        kv_h2o_decay=getattr(a, "kv_h2o_decay", 1.0))
 
 
 def _kv(a):

@@ -71,6 +71,10 @@ class EngineConfig:
     # kv_h2o_interval decode steps (those steps run outside CUDA graphs). 0 = off.
     kv_h2o_budget: int = 0
     kv_h2o_interval: int = 4
+    # score memory: each refresh multiplies a sequence's page scores by this before adding the
+    # new mass (1.0 = H2O's accumulated attention; < 1 weights recent queries, the observation
+    # window of GreenKV / SnapKV-style scoring with an effective window of 1 / (1 - decay) refreshes)
+    kv_h2o_decay: float = 1.0
     # > 1: the decoder layers split over this many GPUs of this process (cuda:i .. cuda:i+pp-1,
     # from the engine's device), hidden states passed device to device; steps run eagerly
     pp: int = 1
@@ -663,6 +667,8 @@ class LLMEngine:
                 if r.h2o_mass is not None:
                     grown[:len(r.h2o_mass)] = r.h2o_mass
                 r.h2o_mass = grown
+            if self.ecfg.kv_h2o_decay != 1.0:
+                r.h2o_mass *= self.ecfg.kv_h2o_decay
             r.h2o_mass[i] += vals[off:off + len(i)]
             off += len(i)
             r.h2o_scored = len(r.pages)

@@ -187,16 +187,17 @@ def eviction_log_rule(r, ps=16):
     return visible
 
 
-def test_heavy_hitter_eviction_keeps_budget_and_matches_oracle(tiny):
-    """H2O-style eviction: the engine scores pages by accumulated attention mass, keeps the
-    sequence within its token budget (sinks and the recent window always kept), and every
-    token equals the oracle's with exactly the pages the engine dropped hidden from the
-    queries that came after each drop."""
+@pytest.mark.parametrize("decay", [1.0, 0.5])
+def test_heavy_hitter_eviction_keeps_budget_and_matches_oracle(tiny, decay):
+    """H2O-style eviction: the engine scores pages by accumulated (decay 1) or recency-weighted
+    (decay < 1) attention mass, keeps the sequence within its token budget (sinks and the
+    recent window always kept), and every token equals the oracle's with exactly the pages the
+    engine dropped hidden from the queries that came after each drop."""
     p = _prompt(35, 40)
     eng = LLMEngine.from_checkpoint(tiny, "cpu", EngineConfig(max_num_seqs=2, max_num_batched_tokens=64,
                                                               max_model_len=256, num_pages=64, kv_sink_tokens=16,
                                                               kv_window_tokens=32, kv_h2o_budget=80,
-                                                              kv_h2o_interval=2))
+                                                              kv_h2o_interval=2, kv_h2o_decay=decay))
     rid = eng.add_request(p, SamplingParams(max_tokens=90, ignore_eos=True))
     kept_max = 0
     while eng.has_unfinished():

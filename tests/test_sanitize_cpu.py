@@ -1,7 +1,8 @@
 """The host C++ libraries under AddressSanitizer + UndefinedBehaviorSanitizer with randomized and
 malformed inputs: entropy decoders fed arbitrary bytes and truncated streams, the JSON /
-JSON-schema matchers fed random token sequences and random schemas, the CPU codecs fed odd
-shapes and extreme values, the n-gram index and loop detector fed random token streams. Any
+JSON-schema matchers fed random token sequences and random schemas, the CPU codecs and the
+research codec / KV score kernels fed odd shapes, extreme values and bad arguments, the n-gram
+index and loop detector fed random token streams. Any
 sanitizer report (out-of-bounds access, use after free, signed overflow, misaligned load ...)
 ends the child process with a non-zero status and fails the test."""
 import pytest
@@ -98,6 +99,26 @@ for shape in [(1, 2), (3, 64), (5, 96), (2, 4096)]:
             C.fp6_decode(C.fp6_encode(w.reshape(-1)[:n4].contiguous(), 3, 2), n4, 3, 2)
         except Exception:
             pass
+# ---- research codecs and KV scores: odd shapes, degenerate values, bad arguments
+for shape in [(1, 2), (3, 64), (4, 96)]:
+    for scale in (0.0, 1.0, 3e4):
+        w = torch.randn(*shape) * scale
+        for call in (lambda: C.any4_quantize(w, 2, 3, 1), lambda: C.any4_quantize(w, 5, 3, 1),
+                     lambda: C.quarot_group_quant(w, 7, 7.0, True), lambda: C.quarot_group_quant(w, 3, 1.0, False),
+                     lambda: C.bit_distiller_quant(w, 8, 5), lambda: C.gguf_mixed_quant(w, 3, 64),
+                     lambda: C.flute_lut_encode(w, torch.randn(shape[1], 4), 1),
+                     lambda: C.flute_lut_decode(torch.full(shape, 9, dtype=torch.uint8), torch.randn(shape[1], 4), 1),
+                     lambda: C.qmoe_compress(w, 3, 4), lambda: C.any4_lloyd(w.reshape(-1), torch.randn(16), 5, 2),
+                     lambda: C.adaround_step(w, w, w, w, 0.1, 2.0, 0.01, 1.1, -0.1),
+                     lambda: C.batched_cosine_similarity(w, w), lambda: C.gru_step(w.reshape(-1)[:3], w.reshape(-1)[:3],
+                                                                                  w.reshape(-1)[:1]),
+                     lambda: C.cluster_kv_score(torch.randint(0, 5, (shape[1],)), w[0], 4),
+                     lambda: C.green_kv_score(w[None], w[None]), lambda: C.cake_entropy(w[None], w[None], 1.0),
+                     lambda: C.magic_pig_attention(w[None], w[None], w[None], 3, 5, 0)):
+            try:
+                call()
+            except Exception:
+                pass
 # ---- serving helpers: loop detector and n-gram index on random streams
 for _ in range(100):
     t = rng.integers(0, 20, rng.integers(0, 400)).tolist()

@@ -54,6 +54,8 @@ def test_flags_build_the_engine_config():
     assert _ecfg(_args()).prompt_logit_cache > 0
     assert _ecfg(_args("--pp", "2")).pp == 2
     assert _ecfg(_args("--offload-layers", "3")).offload_layers == 3
+    e = _ecfg(_args("--kv-h2o-budget", "512", "--kv-h2o-interval", "8", "--kv-h2o-decay", "0.9"))
+    assert (e.kv_h2o_budget, e.kv_h2o_interval, e.kv_h2o_decay) == (512, 8, 0.9)
 
 
 def _client(*extra):

@@ -95,8 +95,11 @@ def test_engine_with_format_weights_matches_oracle(cuda, kind):
     out = eng.generate([prompt], SamplingParams(max_tokens=8, ignore_eos=True))[0]
     ok, worst = _teacher_forced_ok(ref, prompt, out)
     assert ok, (worst, out)
-    assert eng.runner.layers[0].o.fmt == {"nf4": K.WF_NF4, "q8": K.WF_INT8, "q2": K.WF_INT2, "q3": K.WF_INT3,
-                                          "aqlm": K.WF_AQLM, "fp8": K.WF_FP8}[kind]
+    o = eng.runner.layers[0].o
+    assert o.fmt == {"nf4": K.WF_NF4, "q8": K.WF_INT8, "q2": K.WF_INT2, "q3": K.WF_INT3, "aqlm": K.WF_AQLM,
+                     "fp8": K.WF_FP8, "any4": K.WF_NF4}[kind]
+    if kind == "any4":  # served by the NF4 path with the tensor's learned table
+        assert o.codebook is not None and o.codebook.numel() == 16
 
 
 @pytest.mark.parametrize("codec,group", [(0, 64), (0, 0), (1, 32), (2, 64), (3, 32), (4, 64)])
