@@ -16,7 +16,8 @@ CSRC = os.path.join("squish_b200", "csrc")
 cuda_sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
 cpp_sources = [os.path.join(CSRC, "bindings.cpp"), os.path.join(CSRC, "cpu_ref.cpp"), os.path.join(CSRC, "entropy.cpp"),
                os.path.join(CSRC, "host_utils.cpp"), os.path.join(CSRC, "grammar.cpp"),
-               os.path.join(CSRC, "quant_research.cpp"), os.path.join(CSRC, "kv_research.cpp")]
+               os.path.join(CSRC, "quant_research.cpp"), os.path.join(CSRC, "kv_research.cpp"),
+               os.path.join(CSRC, "recurrent.cpp")]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

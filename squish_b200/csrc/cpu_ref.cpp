@@ -685,12 +685,14 @@ torch::Tensor fp6_decode(torch::Tensor packed, int64_t n, int64_t exp_bits, int6
 void register_entropy(pybind11::module& c);   // entropy.cpp
 void register_research(pybind11::module& c);  // quant_research.cpp
 void register_kv_research(pybind11::module& c);  // kv_research.cpp
+void register_recurrent(pybind11::module& c);    // recurrent.cpp
 
 void register_cpu(pybind11::module& m) {
   auto c = m.def_submodule("cpu", "C++ CPU reference kernels (restating squish_quant_rs)");
   register_entropy(c);
   register_research(c);
   register_kv_research(c);
+  register_recurrent(c);
   c.def("quantize_int8", &quantize_int8);
   c.def("dequantize_int8", &dequantize_int8);
   c.def("quantize_int4_asym", &quantize_int4_asym);

@@ -22,7 +22,7 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 CSRC = os.path.join(ROOT, "squish_b200", "csrc")
 BUILD = os.path.join(ROOT, "build", "asan")
 SOURCES = ["host_module.cpp", "cpu_ref.cpp", "entropy.cpp", "host_utils.cpp", "grammar.cpp", "quant_research.cpp",
-           "kv_research.cpp"]
+           "kv_research.cpp", "recurrent.cpp"]
 FLAGS = ["-O1", "-g", "-std=c++17", "-fsanitize=address,undefined", "-fno-omit-frame-pointer",
          "-fno-sanitize-recover=undefined", "-fno-sanitize=vptr"]
 

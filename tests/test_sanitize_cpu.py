@@ -114,7 +114,11 @@ for shape in [(1, 2), (3, 64), (4, 96)]:
                                                                                   w.reshape(-1)[:1]),
                      lambda: C.cluster_kv_score(torch.randint(0, 5, (shape[1],)), w[0], 4),
                      lambda: C.green_kv_score(w[None], w[None]), lambda: C.cake_entropy(w[None], w[None], 1.0),
-                     lambda: C.magic_pig_attention(w[None], w[None], w[None], 3, 5, 0)):
+                     lambda: C.magic_pig_attention(w[None], w[None], w[None], 3, 5, 0),
+                     lambda: C.mamba2_scan(w[0], w.T, w.T, w[0], w[0, :1].repeat(shape[0])),
+                     lambda: C.hawk_scan(w, w, w[0], w[0]), lambda: C.delta_net_scan(w[None], w[None], w[None], w[:1]),
+                     lambda: C.ternary_gemv(torch.randint(-2, 3, shape, dtype=torch.int8), w[0], 1.0),
+                     lambda: C.sparse_act_gemv(w, w[0], 0.5)):
             try:
                 call()
             except Exception:
