@@ -145,10 +145,49 @@ def _same_kind(parts: list[QTensor], group: int) -> list[QTensor]:
     k0 = parts[0].kind
     # AQLM tensors carry their own codebooks, so they cannot share one fused GEMM; any4 tensors
     # (NF4 codes with a learned level table) only when their tables agree
-    if (k0 in GEMM_KINDS and all(p.kind == k0 and p.group == parts[0].group for p in parts)
+    if (k0 in GEMM_KINDS and all(p.kind == k0 and p.group == parts[0].group and gemm_extra_ok(p) for p in parts)
             and not (k0 == "aqlm" and len(parts) > 1) and _same_rotation(parts) and _same_levels(parts)):
         return parts
-    return [_as_q4a(p, group) if p.kind != "q4a" else p for p in parts]
+    return [_as_q4a(p, group) for p in parts]
+
+
+_LOWRANK_KEYS = (("lra", "lrb"), ("sq_L", "sq_R"))
+
+
+def _lowrank(t: QTensor):
+    """(keys, A [N, r], B [r, K]) of a low-rank residual W += A B, or None."""
+    ex = t.extra or {}
+    for ka, kb in _LOWRANK_KEYS:
+        if ka in ex and ex[ka] is not None:
+            return (ka, kb), ex[ka].float(), ex[kb].float()
+    return None
+
+
+def _merged_extra(parts: list[QTensor], rows) -> dict | None:
+    """Extras of a fused weight: the shared rotation / level table, and the parts' low-rank
+    residuals as one block-diagonal factor pair (``rows(As)`` arranges the A row blocks the way
+    the fused weight arranges the parts' rows)."""
+    p0 = parts[0]
+    ex = {}
+    if _rotation(p0):
+        ex.update({k: p0.extra[k] for k in ("rot_signs", "rot_block", "seed") if k in p0.extra})
+    if _levels(p0) is not None:
+        ex["levels"] = _levels(p0)
+    lrs = [_lowrank(p) for p in parts]
+    if any(lr is not None for lr in lrs):
+        keys = next(lr[0] for lr in lrs if lr is not None)
+        ranks = [0 if lr is None else lr[1].shape[1] for lr in lrs]
+        R = sum(ranks)
+        As, Bs, c = [], [], 0
+        for p, lr, r in zip(parts, lrs, ranks):
+            a = torch.zeros(p.shape[0], R)
+            if lr is not None:
+                a[:, c:c + r] = lr[1]
+                Bs.append(lr[2])
+            As.append(a)
+            c += r
+        ex[keys[0]], ex[keys[1]] = rows(As), torch.cat(Bs)
+    return ex or None
 
 
 def _cat_rows(parts: list[QTensor]) -> QTensor:
@@ -158,7 +197,7 @@ def _cat_rows(parts: list[QTensor]) -> QTensor:
 
     return QTensor(parts[0].kind, (sum(p.shape[0] for p in parts), parts[0].shape[1]), packed=cat("packed"),
                    scales=cat("scales"), offsets=cat("offsets"), group=parts[0].group,
-                   extra=parts[0].extra if (_rotation(parts[0]) or _levels(parts[0]) is not None) else None)
+                   extra=_merged_extra(parts, torch.cat))
 
 
 _cat_q4a = _cat_rows
@@ -184,13 +223,13 @@ def _interleave_gate_up(gate: QTensor, up: QTensor) -> QTensor:
 
     return QTensor(gate.kind, (2 * fp, gate.shape[1]), packed=inter(gate.packed, up.packed),
                    scales=inter(gate.scales, up.scales), offsets=inter(gate.offsets, up.offsets), group=gate.group,
-                   extra=gate.extra if _rotation(gate) else None)
+                   extra=_merged_extra([gate, up], lambda As: inter(As[0], As[1])))
 
 
 def _as_q4a(t: QTensor, group: int) -> QTensor:
     """Stored kinds without a GEMM code format (INT3, AQLM, dense) are decoded once at load
     and re-encoded as INT4 asymmetric group ``group``."""
-    if t.kind == "q4a":
+    if t.kind == "q4a" and not t.extra:
         return t
     from ..quant.codecs import quantize
 
@@ -198,18 +237,25 @@ def _as_q4a(t: QTensor, group: int) -> QTensor:
 
 
 def gemm_extra_ok(t: QTensor) -> bool:
-    """Extras the GEMM handles as stored: an input rotation (SQINT2 INT2, QuaRot INT4 / INT2),
-    an any4 level table on NF4 codes."""
+    """Extras the GEMM path handles as stored: an input rotation (SQINT2 INT2, QuaRot INT4),
+    an any4 level table on NF4 codes, a low-rank residual (SQINT2 residual, MiLo INT3
+    compensator: two skinny GEMMs after the quantized one)."""
     if not t.extra:
         return True
-    if t.kind in ("q2", "q4a"):
-        return set(t.extra) <= {"rot_signs", "rot_block", "seed"}
-    return t.kind == "nf4" and set(t.extra) <= {"levels"}
+    keys = set(t.extra)
+    if t.kind == "q2":
+        return keys <= {"rot_signs", "rot_block", "seed", "sq_L", "sq_R"} and (
+            "rot_signs" in keys or not keys & {"sq_L", "sq_R"})
+    if t.kind == "q4a":
+        return keys <= {"rot_signs", "rot_block", "seed"}
+    if t.kind == "q3":
+        return keys <= {"lra", "lrb"}
+    return t.kind == "nf4" and keys <= {"levels"}
 
 
 def _native(t: QTensor, group: int) -> QTensor:
-    """Kinds the GEMM decodes as stored (with the extras of ``gemm_extra_ok``); others, and
-    SQINT2 with a low-rank residual, are re-encoded as INT4."""
+    """Kinds the GEMM decodes as stored (with the extras of ``gemm_extra_ok``); others are
+    re-encoded as INT4."""
     return t if t.kind in GEMM_KINDS and gemm_extra_ok(t) else _as_q4a(t, group)
 
 

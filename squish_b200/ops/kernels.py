@@ -129,6 +129,10 @@ class Int4Weight:
     # R x = blockdiag(H_b / sqrt(b)) (rot * x) (csrc/hadamard.cu)
     rot: torch.Tensor | None = None  # float32 [k] signs
     rot_block: int = 0
+    # low-rank residual W += A B (MiLo INT3 compensator; SQINT2 residual in the rotated frame):
+    # y += (x B^T) A^T after the GEMM, on the (rotated) input, before any SiLU*up epilogue
+    lr_a: torch.Tensor | None = None  # [n, r] (rows in the weight's row order)
+    lr_b: torch.Tensor | None = None  # [r, k]
 
     @property
     def nbytes(self) -> int:
@@ -218,6 +222,17 @@ def repack_codes(codes: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor 
     return tile.to(torch.int32).contiguous()
 
 
+def _lowrank_factors(t, dev):
+    """(A [n, r], B [r, k]) bf16 on the device of a MiLo (``lra``/``lrb``) or SQINT2 residual
+    (``sq_L``/``sq_R``) weight, else (None, None)."""
+    ex = t.extra or {}
+    for a, b in (("lra", "lrb"), ("sq_L", "sq_R")):
+        if a in ex and ex[a] is not None and ex[a].numel():
+            return (ex[a].to(dev, torch.float32).to(torch.bfloat16).contiguous(),
+                    ex[b].to(dev, torch.float32).to(torch.bfloat16).contiguous())
+    return None, None
+
+
 def prepare_weight(t, device, bias: torch.Tensor | None = None) -> Int4Weight:
     """A QTensor in the GEMM's device layout: INT4 asymmetric (repacked on the GPU), NF4,
     INT8 or INT2 (repacked with tensor ops) in their own code formats."""
@@ -252,22 +267,21 @@ def prepare_weight(t, device, bias: torch.Tensor | None = None) -> Int4Weight:
         wt = repack_codes(codes, t.scales.to(dev), t.offsets.to(dev), k, t.group, WF_INT2)
         fmt = WF_INT2
         if t.extra and "rot_signs" in t.extra:
-            if "sq_L" in t.extra:
-                raise ValueError("SQINT2 weights with a low-rank residual have no GEMM code format")
+            lr = _lowrank_factors(t, dev)
             return Int4Weight(wq=wt, sz=torch.empty(0, dtype=torch.int32, device=dev), n=int(t.shape[0]), k=k,
                               group=int(t.group), bias=b, fmt=fmt,
                               rot=t.extra["rot_signs"].to(dev, torch.float32).contiguous(),
-                              rot_block=int(t.extra["rot_block"]))
+                              rot_block=int(t.extra["rot_block"]), lr_a=lr[0], lr_b=lr[1])
     elif t.kind == "q3":
-        if t.extra:
-            raise ValueError("INT3 weights with a low-rank compensator have no GEMM code format")
-        b = p.to(torch.int64).view(p.shape[0], -1, 3)
-        bits = b[..., 0] | (b[..., 1] << 8) | (b[..., 2] << 16)  # 8 codes of 3 bits
+        lr = _lowrank_factors(t, dev)
+        bb = p.to(torch.int64).view(p.shape[0], -1, 3)
+        bits = bb[..., 0] | (bb[..., 1] << 8) | (bb[..., 2] << 16)  # 8 codes of 3 bits
         q = torch.stack([(bits >> (3 * j)) & 7 for j in range(8)], dim=-1).reshape(p.shape[0], -1)[:, :k]
         u = torch.where(q >= 4, q - 8, q) + 4  # two's complement code -> q + 4 in [0, 7]
         z = t.offsets.to(dev) if t.offsets is not None else None
         wt = repack_codes(u, t.scales.to(dev), z, k, t.group, WF_INT3)
-        fmt = WF_INT3
+        return Int4Weight(wq=wt, sz=torch.empty(0, dtype=torch.int32, device=dev), n=int(t.shape[0]), k=k,
+                          group=int(t.group), bias=b, fmt=WF_INT3, lr_a=lr[0], lr_b=lr[1])
     elif t.kind == "aqlm":
         cb = t.scales.float()
         scale, size, gs = float(cb[0]), int(cb[1]), int(cb[2])
@@ -317,6 +331,37 @@ def w4a16_linear(x: torch.Tensor, w: Int4Weight, out: torch.Tensor | None = None
     if w.rot is not None:
         x = native().hadamard_rows(x, w.rot, w.rot_block, ws.rot_buffer(m, w.k))
         _count()
+    if w.lr_a is not None:
+        return _lowrank_linear(x, w, out, residual, silu_mul, ws, trace)
+    return _linear_core(x, w, out, residual, silu_mul, ws, trace)
+
+
+def _lowrank_term(x: torch.Tensor, w: Int4Weight) -> torch.Tensor:
+    """(x B^T) A^T in fp32 (two skinny library GEMMs, rank r)."""
+    return (x.float() @ w.lr_b.float().T) @ w.lr_a.float().T
+
+
+def _lowrank_linear(x, w, out, residual, silu_mul, ws, trace):
+    """A quantized GEMM plus its low-rank residual. With the SiLU*up epilogue the correction
+    must precede the activation: plain GEMM into [m, n], add, then SiLU(gate) * up."""
+    m = x.shape[0]
+    if not silu_mul:
+        y = _linear_core(x, w, out, residual, False, ws, trace)
+        y.add_(_lowrank_term(x, w).to(y.dtype))
+        return y
+    if residual is not None:
+        raise ValueError("a residual cannot follow the SiLU*up epilogue")
+    full = _linear_core(x, w, None, None, False, ws, trace).float() + _lowrank_term(x, w)
+    g, u = full.view(m, w.n // 128, 2, 64).unbind(2)
+    act = (torch.nn.functional.silu(g) * u).reshape(m, w.n // 2).to(torch.bfloat16)
+    if out is None:
+        return act
+    out.copy_(act)
+    return out
+
+
+def _linear_core(x, w, out, residual, silu_mul, ws, trace):
+    m = x.shape[0]
     ncols = w.n // 2 if silu_mul else w.n
     if out is None:
         out = torch.empty((m, ncols), dtype=torch.bfloat16, device=x.device)

@@ -285,7 +285,7 @@ class TPComm:
         from ..ops import kernels as K
 
         x = self.xg[:T]
-        if T >= K.DQ_GEMM_MIN_M or w.rot is not None:
+        if T >= K.DQ_GEMM_MIN_M or w.rot is not None or w.lr_a is not None:
             self.ag_wait(T)
             return K.w4a16_linear(x, w, out=out, silu_mul=silu_mul, ws=ws)
         native().w4a16_gemm(x, w.wq, w.sz, w.n, w.k, w.group, out, w.bias, None,

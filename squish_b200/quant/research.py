@@ -187,3 +187,17 @@ class OnlineLogistic:
         self.w = C().sgd_weight_update(self.w, x, err, self.lr)
         return yh
 
+
+
+# ----------------------------------------------------------------------------- MiLo
+def milo_int3(w: torch.Tensor, group: int, rank: int) -> QTensor:
+    """INT3 weight with a MiLo-style low-rank compensator: the rank-``rank`` truncated SVD of
+    the INT3 quantization residual, W ~ deq(Q) + A B (npy-dir ``__lra`` / ``__lrb``; the runner
+    adds (x B^T) A^T after the INT3 GEMM)."""
+    from .codecs import quantize
+
+    wf = w.detach().float().cpu()
+    t = quantize(wf, "q3", group)
+    U, S, Vh = torch.linalg.svd(wf - t.dequantize().float(), full_matrices=False)
+    t.extra = {"lra": (U[:, :rank] * S[:rank]).contiguous(), "lrb": Vh[:rank].contiguous()}
+    return t

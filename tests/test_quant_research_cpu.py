@@ -222,3 +222,43 @@ def test_any4_and_quarot_survive_npy_dir_and_compress(tmp_path):
         c2, _ = convert.load_checkpoint(str(out))
         t = c2["model.layers.0.self_attn.q_proj.weight"]
         assert t.kind == kind and key in t.extra
+
+
+def test_lowrank_residual_weights_fuse_exactly():
+    """MiLo INT3 compensators and SQINT2 residuals survive the fused qkv (row concatenation) and
+    gate/up (64-row interleave) layouts as block-diagonal factor pairs: the fused weight
+    dequantizes to the fused dequantized parts."""
+    from squish_b200.models.decoder import _cat_rows, _interleave_gate_up, _same_kind, gemm_extra_ok
+    from squish_b200.quant.sqint2 import SQINT2Config, compress_weight
+
+    g = torch.Generator().manual_seed(11)
+    a = R.milo_int3(torch.randn(96, 128, generator=g) * 0.05, 32, 4)
+    b = R.milo_int3(torch.randn(64, 128, generator=g) * 0.05, 32, 2)
+    c = R.quantize_any4(torch.randn(64, 128, generator=g), 32)  # (a different kind)
+    assert gemm_extra_ok(a) and _same_kind([a, b], 32) == [a, b]
+    assert all(t.kind == "q4a" for t in _same_kind([a, c], 32))
+    fused = _cat_rows([a, b])
+    torch.testing.assert_close(fused.dequantize(), torch.cat([a.dequantize(), b.dequantize()]), rtol=0, atol=1e-5)
+    gu = _interleave_gate_up(a, R.milo_int3(torch.randn(96, 128, generator=g) * 0.05, 32, 3))
+    ga, ua = a.dequantize(), gu.dequantize()
+    torch.testing.assert_close(ua[0:64], ga[0:64], rtol=0, atol=1e-5)  # first 64 gate rows lead
+    torch.testing.assert_close(ua[128:160], ga[64:96], rtol=0, atol=1e-5)
+    # SQINT2 with a rank-4 residual in the rotated frame
+    s1 = compress_weight(torch.randn(64, 128, generator=g) * 0.05, SQINT2Config(group_size=32, residual_rank=4))
+    s2 = compress_weight(torch.randn(32, 128, generator=g) * 0.05, SQINT2Config(group_size=32, residual_rank=4))
+    assert "sq_L" in s1.extra and gemm_extra_ok(s1)
+    if _same_kind([s1, s2], 32) == [s1, s2]:  # same rotation (same seed and block)
+        f2 = _cat_rows([s1, s2])
+        torch.testing.assert_close(f2.dequantize(), torch.cat([s1.dequantize(), s2.dequantize()]), rtol=0,
+                                   atol=1e-4)
+
+
+def test_milo_compensator_reduces_error():
+    g = torch.Generator().manual_seed(12)
+    w = torch.randn(128, 256, generator=g) * 0.05
+    w += torch.randn(128, 4, generator=g) @ torch.randn(4, 256, generator=g) * 0.05  # a low-rank component
+    from squish_b200.quant.codecs import quantize
+
+    plain = (quantize(w, "q3", 32).dequantize() - w).pow(2).mean().item()
+    comp = (R.milo_int3(w, 32, 8).dequantize() - w).pow(2).mean().item()
+    assert comp < 0.8 * plain, (comp, plain)

@@ -64,7 +64,38 @@ def test_quarot_rotated_int4_gemm_matches_fp32(cuda, m):
     assert err <= 2e-2 * ref.abs().max().item() + 1e-2, err
 
 
-@pytest.mark.parametrize("kind", ["nf4", "q8", "q2", "q3", "aqlm", "fp8", "any4"])
+@pytest.mark.parametrize("m", [1, 64, 512])
+def test_lowrank_residual_gemms_match_fp32(cuda, m):
+    """Quantized GEMM + low-rank residual: a MiLo INT3 weight (plain and as an interleaved
+    gate/up pair under the SiLU*up epilogue) and an SQINT2 weight with a rotated-frame residual."""
+    from squish_b200.models.decoder import _interleave_gate_up
+    from squish_b200.quant.research import milo_int3
+    from squish_b200.quant.sqint2 import SQINT2Config, compress_weight
+
+    g = torch.Generator().manual_seed(m)
+    x = torch.randn(m, 512, generator=g).to(torch.bfloat16)
+    xf = x.float()
+
+    def check(y, ref):
+        err = (y.float().cpu() - ref).abs().max().item()
+        assert err <= 2e-2 * ref.abs().max().item() + 1e-2, err
+
+    t = milo_int3(torch.randn(384, 512, generator=g) * 0.05, 32, 8)
+    dw = K.prepare_weight(t, cuda)
+    assert dw.lr_a is not None and dw.lr_a.shape == (384, 8)
+    check(ops.w4a16_linear(x.to(cuda), dw), xf @ t.dequantize().T)
+    gate = milo_int3(torch.randn(192, 512, generator=g) * 0.05, 32, 4)
+    up = milo_int3(torch.randn(192, 512, generator=g) * 0.05, 32, 4)
+    gu = K.prepare_weight(_interleave_gate_up(gate, up), cuda)
+    want = torch.nn.functional.silu(xf @ gate.dequantize().T) * (xf @ up.dequantize().T)
+    check(ops.w4a16_linear(x.to(cuda), gu, silu_mul=True), want)
+    s2 = compress_weight(torch.randn(256, 512, generator=g) * 0.05, SQINT2Config(group_size=32, residual_rank=4))
+    ds = K.prepare_weight(s2, cuda)
+    assert ds.rot is not None and ds.lr_a is not None
+    check(ops.w4a16_linear(x.to(cuda), ds), xf @ s2.dequantize().T)
+
+
+@pytest.mark.parametrize("kind", ["nf4", "q8", "q2", "q3", "aqlm", "fp8", "any4", "milo"])
 def test_engine_with_format_weights_matches_oracle(cuda, kind):
     from squish_b200.engine.engine import EngineConfig, LLMEngine
     from squish_b200.engine.sampling import SamplingParams
@@ -85,6 +116,10 @@ def test_engine_with_format_weights_matches_oracle(cuda, kind):
                 from squish_b200.quant.aqlm import aqlm_quantize
 
                 c.tensors[name] = aqlm_quantize(w, iters=2)
+            elif kind == "milo":  # INT3 + low-rank compensator
+                from squish_b200.quant.research import milo_int3
+
+                c.tensors[name] = milo_int3(w, 32, 4)
             else:
                 c.tensors[name] = quantize(w, kind, 32)
         return c
@@ -97,9 +132,12 @@ def test_engine_with_format_weights_matches_oracle(cuda, kind):
     assert ok, (worst, out)
     o = eng.runner.layers[0].o
     assert o.fmt == {"nf4": K.WF_NF4, "q8": K.WF_INT8, "q2": K.WF_INT2, "q3": K.WF_INT3, "aqlm": K.WF_AQLM,
-                     "fp8": K.WF_FP8, "any4": K.WF_NF4}[kind]
+                     "fp8": K.WF_FP8, "any4": K.WF_NF4, "milo": K.WF_INT3}[kind]
     if kind == "any4":  # served by the NF4 path with the tensor's learned table
         assert o.codebook is not None and o.codebook.numel() == 16
+    if kind == "milo":  # the compensator runs after the INT3 GEMM (fused qkv / gate_up too)
+        assert o.lr_a is not None and eng.runner.layers[0].qkv.lr_a is not None
+        assert eng.runner.layers[0].gate_up.lr_a is not None
 
 
 @pytest.mark.parametrize("codec,group", [(0, 64), (0, 0), (1, 32), (2, 64), (3, 32), (4, 64)])
