@@ -5,7 +5,8 @@
 // The reference ships these as Rust functions of squish_quant_rs (no Python caller besides its
 // tests): any4 Lloyd calibration (src/lib.rs:4470), QuaRot group quantization (2870-2932),
 // AdaRound steps (3421), FLUTE LUT encode / decode (3764-3827), QMoE block codebooks (4696),
-// BitDistiller group quantization (4969), GGUF-style blocks with super-block scales (5137), the
+// BitDistiller group quantization and refinement (4969, 5039), GGUF-style blocks with
+// super-block scales (5137), PQ cache sub-codebooks (5223), the
 // ReDrafter GRU step and batched cosine similarity (1977-2013), logistic / SGD predictor steps
 // (2765-2786). Each function here states its math; where this file departs from a reference
 // kernel (unsigned codes at 8 bits, the published AdaRound regulariser, nearest-level
@@ -257,13 +258,13 @@ torch::Tensor flute_lut_decode(torch::Tensor codes, torch::Tensor codebook, int6
   return out;
 }
 
-// ---------------------------------------------------------------------------------- QMoE
-// Block codebook of an expert's weights: k-means (squared L2) over [N, block] rows, started at
-// k evenly spaced blocks; empty centroids keep their position. Returns (codebook [k, block],
-// assignments int32 [N]).
-std::tuple<torch::Tensor, torch::Tensor> qmoe_compress(torch::Tensor blocks, int64_t k, int64_t n_iter) {
-  auto x = f32c(blocks);
-  TORCH_CHECK(x.dim() == 2 && k >= 1, "blocks [N, block], k >= 1");
+// ---------------------------------------------------------------------------------- QMoE / PQ
+// k-means (squared L2) over [N, D] rows. Start: k evenly spaced rows (seed < 0) or k rows drawn
+// with a seeded splitmix64 (seed >= 0, PQ sub-codebooks); empty centroids keep their position.
+// Returns (centroids [k, D], assignments int32 [N]).
+std::tuple<torch::Tensor, torch::Tensor> kmeans_rows(torch::Tensor rows, int64_t k, int64_t n_iter, int64_t seed) {
+  auto x = f32c(rows);
+  TORCH_CHECK(x.dim() == 2 && k >= 1, "rows [N, D], k >= 1");
   const int64_t N = x.size(0), D = x.size(1);
   auto cb = torch::zeros({k, D}, torch::kFloat32);
   auto asg = torch::zeros({N}, torch::kInt32);
@@ -271,8 +272,9 @@ std::tuple<torch::Tensor, torch::Tensor> qmoe_compress(torch::Tensor blocks, int
   const float* xp = x.data_ptr<float>();
   float* cp = cb.data_ptr<float>();
   int32_t* ap = asg.data_ptr<int32_t>();
+  uint64_t rng = (uint64_t)seed * 0x2545F4914F6CDD1Dull + 7;
   for (int64_t c = 0; c < k; ++c) {
-    const int64_t src = std::min(N - 1, c * N / k);
+    const int64_t src = seed < 0 ? std::min(N - 1, c * N / k) : (int64_t)(splitmix64(rng) % (uint64_t)N);
     std::copy(xp + src * D, xp + src * D + D, cp + c * D);
   }
   std::vector<double> sum(k * D);
@@ -310,6 +312,17 @@ std::tuple<torch::Tensor, torch::Tensor> qmoe_compress(torch::Tensor blocks, int
   return {cb, asg};
 }
 
+// QMoE: block codebook of an expert's weights (evenly spaced start).
+std::tuple<torch::Tensor, torch::Tensor> qmoe_compress(torch::Tensor blocks, int64_t k, int64_t n_iter) {
+  return kmeans_rows(blocks, k, n_iter, -1);
+}
+
+// PQ cache: the centroids of one sub-space's sub-vectors [N, sub_dim] (seeded start).
+torch::Tensor pq_cache_fit(torch::Tensor sub_vecs, int64_t k, int64_t n_iter, int64_t seed) {
+  TORCH_CHECK(seed >= 0, "seed >= 0");
+  return std::get<0>(kmeans_rows(sub_vecs, k, n_iter, seed));
+}
+
 // ---------------------------------------------------------------------------------- BitDistiller / GGUF
 // Per-row groups of `group` columns, min/max asymmetric: scale = (max - min) / (2^bits - 1),
 // code = round((w - min) / scale) in [0, 2^bits - 1] (unsigned, so 8-bit codes fit), zero =
@@ -340,6 +353,59 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> bit_distiller_quant(torc
         cp[r * C + c] = (uint8_t)std::min(L, std::max(0.f, std::nearbyint((xp[r * C + c] - mn) / range * L)));
     }
   return {codes, scales, zeros};
+}
+
+// BitDistiller-style teacher-guided grid refinement: per row group, the importance of each
+// weight is p = softmax(teacher / temperature) over the group (the teacher's soft targets);
+// among n_grid grids shrinking [min, max] about its midpoint by factors 1 .. 1/2, keep the one
+// with the least p-weighted squared reconstruction error. Returns (scales [R, G], zeros [R, G])
+// for codes round(w / scale + zero) in [0, 2^bits - 1]. (The reference's refinement is a
+// different heuristic over the same inputs.)
+std::tuple<torch::Tensor, torch::Tensor> bit_distiller_refine(torch::Tensor w, torch::Tensor teacher, int64_t bits,
+                                                              int64_t group, int64_t n_grid, double temperature) {
+  auto x = f32c(w), t = f32c(teacher);
+  TORCH_CHECK(x.dim() == 2 && t.sizes() == x.sizes() && bits >= 2 && bits <= 8 && group > 0 && n_grid >= 1 &&
+                  temperature > 0,
+              "w / teacher [R, C], 2 <= bits <= 8, group > 0, n_grid >= 1, temperature > 0");
+  const int64_t R = x.size(0), C = x.size(1), G = (C + group - 1) / group;
+  const float L = (float)((1 << bits) - 1);
+  auto scales = torch::empty({R, G}, torch::kFloat32), zeros = torch::empty({R, G}, torch::kFloat32);
+  float *sp = scales.data_ptr<float>(), *zp = zeros.data_ptr<float>();
+  const float *xp = x.data_ptr<float>(), *tp = t.data_ptr<float>();
+  std::vector<float> p(group);
+  for (int64_t r = 0; r < R; ++r)
+    for (int64_t g = 0; g < G; ++g) {
+      const int64_t c0 = g * group, c1 = std::min(C, c0 + group), n = c1 - c0;
+      float mn = INFINITY, mx = -INFINITY, tm = -INFINITY;
+      for (int64_t c = c0; c < c1; ++c) {
+        mn = std::min(mn, xp[r * C + c]);
+        mx = std::max(mx, xp[r * C + c]);
+        tm = std::max(tm, tp[r * C + c]);
+      }
+      double z = 0;
+      for (int64_t i = 0; i < n; ++i) z += (p[i] = std::exp((tp[r * C + c0 + i] - tm) / (float)temperature));
+      const float mid = 0.5f * (mn + mx), half = 0.5f * (mx - mn);
+      float best_e = INFINITY, best_s = 1.f, best_z = 0.f;
+      for (int64_t k = 0; k < n_grid; ++k) {
+        const float f = n_grid > 1 ? 1.f - 0.5f * (float)k / (float)(n_grid - 1) : 1.f;
+        const float lo = mid - half * f, s = std::max(2.f * half * f, 1e-8f) / L, zz = -lo / s;
+        double e = 0;
+        for (int64_t i = 0; i < n; ++i) {
+          const float v = xp[r * C + c0 + i];
+          const float q = std::min(L, std::max(0.f, std::nearbyint(v / s + zz)));
+          const float d = (q - zz) * s - v;
+          e += p[i] / z * d * d;
+        }
+        if (e < best_e) {
+          best_e = (float)e;
+          best_s = s;
+          best_z = zz;
+        }
+      }
+      sp[r * G + g] = best_s;
+      zp[r * G + g] = best_z;
+    }
+  return {scales, zeros};
 }
 
 // GGUF-style blocks: the same per-block min / scale codes, plus one super-block scale per 8
@@ -444,6 +510,11 @@ void register_research(pybind11::module& c) {
   c.def("flute_lut_encode", &flute_lut_encode);
   c.def("flute_lut_decode", &flute_lut_decode);
   c.def("qmoe_compress", &qmoe_compress);
+  c.def("pq_cache_fit", &pq_cache_fit, pybind11::arg("sub_vecs"), pybind11::arg("k"), pybind11::arg("n_iter") = 20,
+        pybind11::arg("seed") = 0);
+  c.def("bit_distiller_refine", &bit_distiller_refine, pybind11::arg("w"), pybind11::arg("teacher"),
+        pybind11::arg("bits"), pybind11::arg("group"), pybind11::arg("n_grid") = 16,
+        pybind11::arg("temperature") = 1.0);
   c.def("bit_distiller_quant", &bit_distiller_quant);
   c.def("gguf_mixed_quant", &gguf_mixed_quant);
   c.def("gru_step", &gru_step);

@@ -262,3 +262,31 @@ def test_milo_compensator_reduces_error():
     plain = (quantize(w, "q3", 32).dequantize() - w).pow(2).mean().item()
     comp = (R.milo_int3(w, 32, 8).dequantize() - w).pow(2).mean().item()
     assert comp < 0.8 * plain, (comp, plain)
+
+
+def test_pq_cache_fit_is_a_lloyd_fixed_point():
+    g = torch.Generator().manual_seed(13)
+    x = torch.cat([torch.randn(100, 4, generator=g) + 5 * i for i in range(4)])
+    cb = R.C().pq_cache_fit(x, 4, 50, 3)
+    a = torch.cdist(x, cb).argmin(1)
+    for j in range(4):
+        if (a == j).any():
+            torch.testing.assert_close(cb[j], x[a == j].mean(0), rtol=1e-4, atol=1e-4)
+
+
+def test_bit_distiller_refine_lowers_teacher_weighted_error():
+    g = torch.Generator().manual_seed(14)
+    w = torch.randn(16, 128, generator=g)
+    w[:, ::17] *= 6  # outliers stretch the min / max grid
+    teacher = torch.randn(16, 128, generator=g)
+    s, z = R.C().bit_distiller_refine(w, teacher, 4, 64, 16, 0.5)
+    q0, s0, z0 = R.bit_distiller_quant(w, 4, 64)
+
+    def err(scale, zero):
+        sc = scale.repeat_interleave(64, 1)
+        ze = zero.repeat_interleave(64, 1)
+        q = torch.clamp(torch.round(w / sc + ze), 0, 15)
+        p = torch.softmax(teacher.view(16, 2, 64) / 0.5, -1).view(16, 128)
+        return (p * ((q - ze) * sc - w) ** 2).sum().item()
+
+    assert err(s, z) <= err(s0, z0) + 1e-6
