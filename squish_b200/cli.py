@@ -64,6 +64,8 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
     p.add_argument("--kv-h2o-interval", type=int, default=4, help="decode steps between attention-mass refreshes")
     p.add_argument("--kv-h2o-decay", type=float, default=1.0,
                    help="score decay per refresh (1 = accumulated H2O scores; < 1 favours recent queries)")
+    p.add_argument("--kv-budget-adaptive", action="store_true",
+                   help="share the page pool among running sequences: heavy-hitter budgets shrink under pressure")
     # speculative decoding (the reference serves with prompt lookup on: squish/server.py:5194)
     sp = ucfg.load()["speculative"]
     p.add_argument("--prompt-lookup", dest="prompt_lookup", action="store_true", default=bool(sp["prompt_lookup"]),
@@ -143,7 +145,8 @@ def _ecfg(a):
                         prompt_logit_cache=a.prompt_logit_cache, kv_sink_tokens=a.kv_sink_tokens,
                         kv_window_tokens=a.kv_window_tokens, pp=a.pp, offload_layers=a.offload_layers,
                         kv_h2o_budget=getattr(a, "kv_h2o_budget", 0), kv_h2o_interval=getattr(a, "kv_h2o_interval", 4),
-                        kv_h2o_decay=getattr(a, "kv_h2o_decay", 1.0))
+                        kv_h2o_decay=getattr(a, "kv_h2o_decay", 1.0),
+                        kv_budget_adaptive=getattr(a, "kv_budget_adaptive", False))
 
 
 def _kv(a):

@@ -75,6 +75,10 @@ class EngineConfig:
     # new mass (1.0 = H2O's accumulated attention; < 1 weights recent queries, the observation
     # window of GreenKV / SnapKV-style scoring with an effective window of 1 / (1 - decay) refreshes)
     kv_h2o_decay: float = 1.0
+    # heavy-hitter budgets arbitrated against the page pool (kv/budget.py): every running
+    # sequence asks for kv_h2o_budget tokens; when their sum exceeds the pool, each gets a
+    # proportional share (never less than its protected sinks + window + one page)
+    kv_budget_adaptive: bool = False
     # > 1: the decoder layers split over this many GPUs of this process (cuda:i .. cuda:i+pp-1,
     # from the engine's device), hidden states passed device to device; steps run eagerly
     pp: int = 1
@@ -170,6 +174,11 @@ class LLMEngine:
                                            disk_dir=ecfg.kv_disk_dir, disk_bytes=ecfg.kv_disk_bytes)
         self.requests: dict[str, Request] = {}
         self._ids = itertools.count()
+        self.kv_broker = None
+        if ecfg.kv_h2o_budget > 0 and ecfg.kv_budget_adaptive:
+            from ..kv.budget import KVBudgetBroker
+
+            self.kv_broker = KVBudgetBroker(num_pages * qcfg.page_size)
         self.stats = EngineStats()
         self.max_pages = (ecfg.max_model_len + qcfg.page_size - 1) // qcfg.page_size
         self.graphs = None
@@ -633,6 +642,8 @@ class LLMEngine:
             if dt <= b:
                 self.stats.step_counts[i] += 1
         if self.ecfg.kv_h2o_budget > 0:
+            if self.kv_broker is not None:
+                self._sync_budgets()
             for e in sched.decode:
                 if e.req.status is Status.RUNNING:
                     self._evict_h2o(e.req)
@@ -644,11 +655,10 @@ class LLMEngine:
 
     # ------------------------------------------------------------------ heavy-hitter eviction
     def _h2o_score_step(self, sched: Schedule) -> bool:
-        b = self.ecfg.kv_h2o_budget
-        if b <= 0 or not sched.decode or self.stats.steps % max(1, self.ecfg.kv_h2o_interval):
+        if self.ecfg.kv_h2o_budget <= 0 or not sched.decode or self.stats.steps % max(1, self.ecfg.kv_h2o_interval):
             return False
         # refresh while some decoding sequence is near its budget
-        return any(e.req.num_computed - e.req.evicted_tokens > b // 2 for e in sched.decode)
+        return any(e.req.num_computed - e.req.evicted_tokens > self.h2o_budget(e.req) // 2 for e in sched.decode)
 
     def _h2o_collect(self, sched: Schedule) -> None:
         """Add this step's attention mass per page (all layers and heads) to each decoding
@@ -673,11 +683,29 @@ class LLMEngine:
             off += len(i)
             r.h2o_scored = len(r.pages)
 
+    def _sync_budgets(self) -> None:
+        """One broker registration per running sequence (kv_h2o_budget tokens each)."""
+        br = self.kv_broker
+        live = {f"h2o:{r.rid}" for r in self.scheduler.running}
+        for name in [n for n in br.names() if n not in live]:
+            br.unregister(name)
+        for name in sorted(live - set(br.names())):
+            br.register(name, self.ecfg.kv_h2o_budget)
+
+    def h2o_budget(self, r: Request) -> int:
+        """Tokens sequence ``r`` may keep: kv_h2o_budget, or its arbitrated share."""
+        ec = self.ecfg
+        name = f"h2o:{r.rid}"
+        if self.kv_broker is None or name not in self.kv_broker.names():
+            return ec.kv_h2o_budget
+        floor = ec.kv_sink_tokens + max(ec.kv_window_tokens, self.qcfg.page_size) + self.qcfg.page_size
+        return max(floor, self.kv_broker.allocated(name))
+
     def _evict_h2o(self, r: Request) -> None:
         """Over budget: give back the scored pages outside the sinks and the recent window with
         the least accumulated attention mass (only full pages scored at least once)."""
         ps, ec = self.qcfg.page_size, self.ecfg
-        over = r.num_computed - r.evicted_tokens - ec.kv_h2o_budget
+        over = r.num_computed - r.evicted_tokens - self.h2o_budget(r)
         if over <= 0 or r.h2o_mass is None:
             return
         sink = -(-ec.kv_sink_tokens // ps)

@@ -224,3 +224,47 @@ def test_layer_slice_renumbers_layers_and_shares_tensors(tiny):
     assert part.tensors["model.embed_tokens.weight"] is tiny.tensors["model.embed_tokens.weight"]
     n_layer = sum(k.startswith("model.layers.") for k in tiny.tensors) // tiny.config.num_layers
     assert sum(k.startswith("model.layers.") for k in part.tensors) == 2 * n_layer
+
+
+def test_kv_budget_broker_shares():
+    from squish_b200.kv.budget import KVBudgetBroker
+
+    b = KVBudgetBroker(0)
+    assert b.register("a", 500) == 500 and b.register("b", 300) == 300  # unconstrained
+    b.set_total(1000)
+    assert (b.allocated("a"), b.allocated("b")) == (500, 300)  # fits
+    b.register("c", 400)
+    al = b.snapshot()["allocated"]
+    assert sum(al.values()) == 1000 and al["a"] > al["c"] > al["b"]  # proportional
+    assert abs(al["a"] - 1000 * 500 / 1200) <= 1
+    b.set_total(2)
+    assert all(v >= 1 for v in b.snapshot()["allocated"].values())
+    b.unregister("c")
+    b.set_total(0)
+    assert b.snapshot()["allocated"] == {"a": 500, "b": 300}
+
+
+def test_adaptive_heavy_hitter_budgets_share_the_pool(tiny):
+    """With budgets arbitrated against a small page pool, two long sequences each keep a
+    proportional share (below kv_h2o_budget), and each output still equals the oracle's under
+    its own eviction record."""
+    prompts = [_prompt(40, 30), _prompt(41, 30)]
+    eng = LLMEngine.from_checkpoint(tiny, "cpu", EngineConfig(max_num_seqs=2, max_num_batched_tokens=64,
+                                                              max_model_len=256, num_pages=14, kv_sink_tokens=16,
+                                                              kv_window_tokens=32, kv_h2o_budget=160,
+                                                              kv_h2o_interval=1, kv_budget_adaptive=True))
+    rids = [eng.add_request(p, SamplingParams(max_tokens=120, ignore_eos=True)) for p in prompts]
+    shares = set()
+    while eng.has_unfinished():
+        eng.step()
+        for rid in rids:
+            r = eng.requests[rid]
+            if r.status.name == "RUNNING":
+                shares.add(eng.h2o_budget(r))
+    assert min(shares) < 160  # the pool (14 pages = 224 tokens) cannot hold two 160-token budgets
+    assert eng.stats.evicted_pages > 0
+    ref = ReferenceModel(tiny)
+    for p, rid in zip(prompts, rids):
+        r = eng.requests[rid]
+        ref.kv_visible = eviction_log_rule(r)
+        assert r.output == ref.greedy(p, 120)[0]

@@ -56,6 +56,7 @@ def test_flags_build_the_engine_config():
     assert _ecfg(_args("--offload-layers", "3")).offload_layers == 3
     e = _ecfg(_args("--kv-h2o-budget", "512", "--kv-h2o-interval", "8", "--kv-h2o-decay", "0.9"))
     assert (e.kv_h2o_budget, e.kv_h2o_interval, e.kv_h2o_decay) == (512, 8, 0.9)
+    assert _ecfg(_args("--kv-budget-adaptive")).kv_budget_adaptive
 
 
 def _client(*extra):
