@@ -154,9 +154,27 @@ class PromptLogitCache:
         self.slot[key] = s
 
 
+def _sampling_row(r: Request) -> tuple:
+    """(temperature, top_p, min_p, repetition_penalty, top_k) of a request, built once (the
+    sampling parameters of a request do not change)."""
+    row = r._samp_row
+    if row is None:
+        p = r.params
+        row = r._samp_row = (p.temperature, p.top_p, p.min_p, p.repetition_penalty, float(p.top_k))
+    return row
+
+
+def _rng_base(r: Request) -> int:
+    """Per-request sampler stream offset (a hash of the request id, computed once)."""
+    b = r._rng_base
+    if b is None:
+        b = r._rng_base = (zlib.crc32(r.rid.encode()) & 0xFFFF) * 65536
+    return b
+
+
 def _rng_step(r: Request) -> int:
     """Sampler stream position of a request's next token (seeded per request id)."""
-    return (r.rng_step + (zlib.crc32(r.rid.encode()) & 0xFFFF) * 65536) & 0x7FFFFFFF
+    return (r.rng_step + _rng_base(r)) & 0x7FFFFFFF
 
 
 class LLMEngine:
@@ -422,9 +440,10 @@ class LLMEngine:
         pos = np.empty(T, dtype=np.int32)
         slots = np.empty(T, dtype=np.int32)
         nb = len(entries)
-        maxp = max((len(e.req.page_array()) for e in entries), default=1)
         if self.graphs is not None:
             maxp = self.max_pages
+        else:
+            maxp = max((len(e.req.page_array()) for e in entries), default=1)
         bt = np.zeros((nb, max(maxp, 1)), dtype=np.int32)
         rows, samp = [], []
         trees = [e for e in entries if e.tree is not None]
@@ -475,11 +494,10 @@ class LLMEngine:
             qs[1:] = np.cumsum(ql)[:-1]
         tseq, tq0 = prefill_tiles(ql)
         B = len(samp)
-        temp = np.asarray([r.params.temperature for r in samp], dtype=np.float32)
-        topp = np.asarray([r.params.top_p for r in samp], dtype=np.float32)
-        topk = np.asarray([r.params.top_k for r in samp], dtype=np.int32)
-        minp = np.asarray([r.params.min_p for r in samp], dtype=np.float32)
-        rep = np.asarray([r.params.repetition_penalty for r in samp], dtype=np.float32)
+        # one pass over the sampled requests: (temperature, top_p, min_p, penalty) and top_k
+        pf = np.array([_sampling_row(r) for r in samp], dtype=np.float32).reshape(B, 5)
+        temp, topp, minp, rep = pf[:, 0].copy(), pf[:, 1].copy(), pf[:, 2].copy(), pf[:, 3].copy()
+        topk = pf[:, 4].astype(np.int32)
 
         def rng_steps(reqs):
             return np.asarray([_rng_step(r) for r in reqs], dtype=np.int64).astype(np.int32)

@@ -50,6 +50,9 @@ class Request:
     _bt_arr: object = field(default=None, repr=False)
     _bt_n: int = field(default=-1, repr=False)
     _bt_ev: int = field(default=0, repr=False)
+    # per-request constants of the step inputs, computed on first use
+    _rng_base: int | None = field(default=None, repr=False)
+    _samp_row: tuple | None = field(default=None, repr=False)
 
     def page_array(self):
         """int32 array of the kept pages (the block table row the attention kernels read)."""
