@@ -335,7 +335,7 @@ class LLMEngine:
 
             comm = TPComm("cpu", ecfg.max_num_batched_tokens, cfg.hidden_size, rows, cfg.vocab_size)
             num_pages = cls.plan_pages(cfg, ck.quant, ecfg, dev)
-            runner = TorchTPRunner(ck, num_pages, comm, ecfg.max_model_len)
+            runner = TorchTPRunner(ck, num_pages, comm, ecfg.max_model_len, ep_a2a=ecfg.tp_mode == "sp")
         eng = cls(runner, cfg, ck.quant, ecfg, num_pages)
         eng.comm = comm
         from ..utils.fault import FaultInjector, PeerMonitor

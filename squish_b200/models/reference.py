@@ -121,6 +121,7 @@ class ReferenceModel:
     rp_hook = None
     head_hook = None
     reduce_hook = None  # expert parallelism: all-reduce of the local experts' partial output
+    moe_hook = None     # expert parallelism with an all-to-all: callable(prefix, x) -> MoE(x)
 
     def _rp(self, x: torch.Tensor, wt: torch.Tensor) -> torch.Tensor:
         return x @ wt.T if self.rp_hook is None else self.rp_hook(x, wt)
@@ -137,6 +138,8 @@ class ReferenceModel:
             if self.tap is not None:
                 self.tap(p + "mlp.down_proj", act)
             return self._rp(act, w[p + "mlp.down_proj.weight"])
+        if self.moe_hook is not None:
+            return self.moe_hook(p, x)
         logits = x @ w[p + "mlp.gate.weight"].T
         probs = torch.softmax(logits, dim=-1)
         topv, topi = probs.topk(cfg.num_experts_per_tok, dim=-1)
@@ -150,11 +153,25 @@ class ReferenceModel:
                 e = int(topi[t, j])
                 if not e0 <= e < e1:
                     continue
-                q = p + f"mlp.experts.{e}."
-                g = x[t] @ w[q + "gate_proj.weight"].T
-                u = x[t] @ w[q + "up_proj.weight"].T
-                out[t] += topv[t, j] * ((torch.nn.functional.silu(g) * u) @ w[q + "down_proj.weight"].T)
+                out[t] += topv[t, j] * self.expert(p, e, x[t])
         return out if self.reduce_hook is None else self.reduce_hook(out)
+
+    def route(self, p: str, x: torch.Tensor):
+        """(weights, global expert ids) [T, K] of the router of MoE layer ``p``."""
+        cfg = self.cfg
+        probs = torch.softmax(x @ self.w[p + "mlp.gate.weight"].T, dim=-1)
+        topv, topi = probs.topk(cfg.num_experts_per_tok, dim=-1)
+        if cfg.norm_topk_prob:
+            topv = topv / topv.sum(-1, keepdim=True)
+        return topv, topi
+
+    def expert(self, p: str, e: int, xr: torch.Tensor) -> torch.Tensor:
+        """Expert ``e`` (global id) of MoE layer ``p`` on one row."""
+        w = self.w
+        q = p + f"mlp.experts.{e}."
+        g = xr @ w[q + "gate_proj.weight"].T
+        u = xr @ w[q + "up_proj.weight"].T
+        return (torch.nn.functional.silu(g) * u) @ w[q + "down_proj.weight"].T
 
     @torch.no_grad()
     def forward(self, tokens: list[int], cache, start_pos: int) -> torch.Tensor:

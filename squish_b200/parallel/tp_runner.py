@@ -101,15 +101,68 @@ class TPCudaRunner(CudaRunner):
 
 
 class TorchTPRunner(TorchPagedRunner):
-    """CPU fp32 oracle runner over a shard, collectives on gloo."""
+    """CPU fp32 oracle runner over a shard, collectives on gloo. With ``ep_a2a`` MoE layers
+    use the expert all-to-all layout of the sequence-parallel GPU mode (csrc/ep_a2a.cu): rank r
+    owns rows [r R, r R + own) of the step, routes them, sends each row to the ranks holding its
+    experts as (row slot [src][t], local expert id or -1, weight), the receivers run their
+    experts over the received slots and return the weighted sums to the row owners, which add
+    them up in source order -- here with all_to_all_single, then an all-gather of the owned
+    rows (the CPU runner keeps every row on every rank)."""
 
-    def __init__(self, ck: Checkpoint, num_pages: int, comm: TPComm, max_model_len: int = 2048):
+    def __init__(self, ck: Checkpoint, num_pages: int, comm: TPComm, max_model_len: int = 2048,
+                 ep_a2a: bool = False):
         self.comm = comm
         local = shard_checkpoint(ck, comm.rank, comm.tp)
         super().__init__(local, num_pages, max_model_len)
         self.ref.rp_hook = self._rp
         self.ref.head_hook = self._head
         self.ref.reduce_hook = self._reduce
+        if ep_a2a and local.config.is_moe:
+            self.ref.moe_hook = self._moe_a2a
+
+    def _moe_a2a(self, p: str, x: torch.Tensor) -> torch.Tensor:
+        import torch.distributed as dist
+
+        ref, comm = self.ref, self.comm
+        tp, rank = comm.tp, comm.rank
+        cfg = ref.cfg
+        T, H = x.shape
+        K, El, e0 = cfg.num_experts_per_tok, cfg.num_local_experts, cfg.expert_offset
+        R = -(-T // tp)
+        r0 = rank * R
+        own = max(0, min(R, T - r0))
+        # dispatch: row slot t of this source in every destination that holds one of its experts
+        send_x = torch.zeros(tp, R, H)
+        send_id = torch.full((tp, R, K), -1, dtype=torch.int64)
+        send_w = torch.zeros(tp, R, K)
+        if own:
+            topv, topi = ref.route(p, x[r0:r0 + own])
+            for t in range(own):
+                for k in range(K):
+                    e = int(topi[t, k])
+                    d = e // El
+                    send_x[d, t] = x[r0 + t]
+                    send_id[d, t, k] = e - d * El
+                    send_w[d, t, k] = topv[t, k]
+        recv_x, recv_id, recv_w = torch.empty_like(send_x), torch.empty_like(send_id), torch.empty_like(send_w)
+        g = comm.group
+        dist.all_to_all_single(recv_x, send_x, group=g)
+        dist.all_to_all_single(recv_id, send_id, group=g)
+        dist.all_to_all_single(recv_w, send_w, group=g)
+        # local experts over the received slots, weighted sums per slot (k in order)
+        ys = torch.zeros(tp, R, H)
+        for s_ in range(tp):
+            for t in range(R):
+                for k in range(K):
+                    lid = int(recv_id[s_, t, k])
+                    if lid >= 0:
+                        ys[s_, t] += recv_w[s_, t, k] * ref.expert(p, e0 + lid, recv_x[s_, t])
+        back = torch.empty_like(ys)
+        dist.all_to_all_single(back, ys, group=g)  # [source rank][my row slot]
+        mine = back.sum(0)  # source order
+        full = torch.empty(tp * R, H)
+        dist.all_gather_into_tensor(full, mine.contiguous(), group=g)
+        return full[:T]
 
     def _reduce(self, part: torch.Tensor) -> torch.Tensor:
         out = torch.zeros_like(part)

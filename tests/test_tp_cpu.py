@@ -29,14 +29,15 @@ def _prompts(vocab):
     return [rng.integers(0, vocab, 23).tolist(), rng.integers(0, vocab, 40).tolist()]
 
 
-def _worker(rank, world, port, q, preset="tiny-llama"):
+def _worker(rank, world, port, q, preset="tiny-llama", mode="nvlink"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         cfg, qc = _cfg(preset)
         ck = random_checkpoint(cfg, qc, seed=0)
         eng = LLMEngine.from_checkpoint(ck, "cpu", EngineConfig(max_num_seqs=4, max_num_batched_tokens=64,
-                                                                max_model_len=256, num_pages=64, tp=world))
+                                                                max_model_len=256, num_pages=64, tp=world,
+                                                                tp_mode=mode))
         outs = eng.generate(_prompts(cfg.vocab_size), SamplingParams(max_tokens=10, ignore_eos=True))
         sampled = eng.generate(_prompts(cfg.vocab_size)[:1], SamplingParams(max_tokens=6, temperature=0.9,
                                                                             ignore_eos=True))
@@ -53,12 +54,15 @@ def _port():
     return p
 
 
-@pytest.mark.parametrize("world,preset", [(2, "tiny-llama"), (2, "tiny-moe")])
-def test_tp_engine_matches_single_process(world, preset):
+@pytest.mark.parametrize("world,preset,mode", [(2, "tiny-llama", "nvlink"), (2, "tiny-moe", "nvlink"),
+                                               (2, "tiny-moe", "sp")])
+def test_tp_engine_matches_single_process(world, preset, mode):
+    """mode "sp" with a MoE model: the expert all-to-all layout (routing of owned rows, slots
+    with local ids or -1, weighted sums returned to the owners) on gloo ranks."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, preset)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, preset, mode)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=600) for _ in range(world)])
