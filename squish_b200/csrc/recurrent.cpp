@@ -3,7 +3,7 @@
 // DeltaNet delta-rule scan, a ternary-weight GEMV and an activation-sparse GEMV.
 //
 // The reference ships these as Rust functions of squish_quant_rs with no model that uses them
-// (src/lib.rs:3331 mamba2_ssm_scan, 3525 hawk_rglr_scan, 3889 delta_net_scan, 3646
+// (src/lib.rs:3331 mamba2_ssm_scan, 3378 mamba2_ssm_decode, 3525 hawk_rglr_scan, 3889 delta_net_scan, 3646
 // ternary_gemv, 3158 sparse_act_gemv); they are kept here as library kernels with the same
 // math, stated per function.
 #include <torch/extension.h>
@@ -44,6 +44,24 @@ std::tuple<torch::Tensor, torch::Tensor> mamba2_scan(torch::Tensor a, torch::Ten
     yp[t] = (float)acc;
   }
   return {y, h};
+}
+
+// One Mamba-2 decode step (the scan at T = 1): h' = exp(a) h + B x, y = C . h'.
+// a, x scalars; B / C / h [N] -> (y, h').
+std::tuple<double, torch::Tensor> mamba2_step(double a, torch::Tensor b, torch::Tensor c, double x, torch::Tensor h) {
+  auto B = f32(b).view({-1}), Cv = f32(c).view({-1});
+  auto hn = f32(h).view({-1}).clone();
+  const int64_t N = hn.numel();
+  TORCH_CHECK(B.numel() == N && Cv.numel() == N, "B, C and h: [N]");
+  float* hp = hn.data_ptr<float>();
+  const float *bp = B.data_ptr<float>(), *cp = Cv.data_ptr<float>();
+  const float da = std::exp((float)a);
+  double y = 0;
+  for (int64_t n = 0; n < N; ++n) {
+    hp[n] = da * hp[n] + bp[n] * (float)x;
+    y += (double)cp[n] * hp[n];
+  }
+  return {y, hn};
 }
 
 // Hawk real-gated linear recurrence, elementwise over the state:
@@ -155,6 +173,7 @@ torch::Tensor sparse_act_gemv(torch::Tensor w, torch::Tensor x, double threshold
 
 void register_recurrent(pybind11::module& c) {
   c.def("mamba2_scan", &mamba2_scan);
+  c.def("mamba2_step", &mamba2_step);
   c.def("hawk_scan", &hawk_scan);
   c.def("delta_net_scan", &delta_net_scan);
   c.def("ternary_gemv", &ternary_gemv, pybind11::arg("w"), pybind11::arg("x"), pybind11::arg("scale") = 1.0);

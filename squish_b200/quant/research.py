@@ -201,3 +201,23 @@ def milo_int3(w: torch.Tensor, group: int, rank: int) -> QTensor:
     U, S, Vh = torch.linalg.svd(wf - t.dequantize().float(), full_matrices=False)
     t.extra = {"lra": (U[:, :rank] * S[:rank]).contiguous(), "lrb": Vh[:rank].contiguous()}
     return t
+
+
+# ----------------------------------------------------------------------------- randomized SVD
+def randomized_svd(a: torch.Tensor, rank: int, oversample: int = 8, n_iter: int = 2, seed: int = 0):
+    """Rank-``rank`` truncated SVD by random projection (Halko, Martinsson and Tropp 2011):
+    Y = A G (G Gaussian, rank + oversample columns), ``n_iter`` power iterations with QR
+    re-orthonormalisation, Q = qr(Y), then the exact SVD of the small Q^T A. Returns (U, S, Vh)
+    with U [m, rank], S [rank], Vh [rank, n]; runs on the tensor's device."""
+    af = a.float()
+    m, n = af.shape
+    k = min(rank + oversample, m, n)
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    omega = torch.randn(n, k, generator=g).to(af.device)
+    q, _ = torch.linalg.qr(af @ omega)
+    for _ in range(n_iter):
+        q, _ = torch.linalg.qr(af.T @ q)
+        q, _ = torch.linalg.qr(af @ q)
+    ub, s, vh = torch.linalg.svd(q.T @ af, full_matrices=False)
+    return (q @ ub)[:, :rank], s[:rank], vh[:rank]
+

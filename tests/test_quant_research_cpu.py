@@ -290,3 +290,11 @@ def test_bit_distiller_refine_lowers_teacher_weighted_error():
         return (p * ((q - ze) * sc - w) ** 2).sum().item()
 
     assert err(s, z) <= err(s0, z0) + 1e-6
+
+
+def test_randomized_svd_matches_exact_on_low_rank_plus_noise():
+    g = torch.Generator().manual_seed(15)
+    a = torch.randn(200, 6, generator=g) @ torch.randn(6, 150, generator=g) + 1e-3 * torch.randn(200, 150, generator=g)
+    U, S, Vh = R.randomized_svd(a, 6, seed=1)
+    torch.testing.assert_close(S, torch.linalg.svdvals(a)[:6], rtol=1e-3, atol=1e-3)
+    assert ((U * S) @ Vh - a).abs().max().item() < 0.02

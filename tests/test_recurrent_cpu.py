@@ -63,3 +63,12 @@ def test_ternary_and_sparse_gemv():
     wf = torch.randn(20, 64, generator=g)
     xs = x * (x.abs() > 0.8)
     torch.testing.assert_close(C().sparse_act_gemv(wf, x, 0.8), wf @ xs, rtol=1e-5, atol=1e-5)
+
+
+def test_mamba2_step_is_one_scan_step():
+    g = torch.Generator().manual_seed(4)
+    B, Cm, h = (torch.randn(8, generator=g) for _ in range(3))
+    y, h1 = C().mamba2_step(-0.3, B, Cm, 0.7, h)
+    ys, hs = C().mamba2_scan(torch.tensor([-0.3]), B[None], Cm[None], torch.tensor([0.7]), h)
+    assert abs(y - float(ys[0])) < 1e-5
+    torch.testing.assert_close(h1, hs)
