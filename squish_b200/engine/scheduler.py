@@ -114,7 +114,7 @@ class Scheduler:
         preempted: list[Request] = []
         # 1. decodes (oldest first); preempt from the back on page exhaustion
         for req in list(self.running):
-            if req.status is not Status.RUNNING or req not in self.running:
+            if req.status is not Status.RUNNING:  # (preempted this step: status WAITING, off the list)
                 continue
             pending = req.total_len - req.num_computed
             if pending != 1:
