@@ -81,6 +81,9 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
                    help="Medusa head file or directory (medusa_head.{i}.* tensors): tree drafts from extra heads "
                         "on the final hidden state")
     p.add_argument("--medusa-top-k", type=int, default=4, help="Medusa: candidates per head")
+    p.add_argument("--eagle-head", default=None,
+                   help="EAGLE draft head file or directory (fc / layers.0.* tensors): drafts from a one-layer "
+                        "model over the target's features")
     p.add_argument("--spec-branches", type=int, default=1, help="prompt lookup: continuations per draft tree")
     # multi-GPU
     p.add_argument("--tp", type=int, default=1, help="tensor-parallel GPUs (one process per GPU over NVLink)")
@@ -101,12 +104,14 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
 
 
 def _spec(a):
-    """SpecConfig from the flags: a draft model wins over Medusa heads, then Jacobi, then prompt
-    lookup."""
+    """SpecConfig from the flags: a draft model wins over an EAGLE head, then Medusa heads, then
+    Jacobi, then prompt lookup."""
     from .engine.speculative import SpecConfig
 
     if getattr(a, "draft_model", None):
         return SpecConfig(method="draft", k=a.draft_depth, draft_model=a.draft_model)
+    if getattr(a, "eagle_head", None):
+        return SpecConfig(method="eagle", k=a.draft_depth, eagle_head=a.eagle_head)
     if getattr(a, "medusa_heads", None):
         return SpecConfig(method="medusa", k=a.draft_depth, medusa_heads=a.medusa_heads,
                           medusa_top_k=getattr(a, "medusa_top_k", 4))

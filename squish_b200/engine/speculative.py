@@ -21,7 +21,9 @@ Proposers (the reference's speculative/ package):
     predictions past the accepted point are the next guess (fixed-point iteration);
   * Medusa heads (speculative/speculative.py:1821-2050) — extra heads on the final hidden
     state propose the tokens after the next one; the best rank paths of their top-k lists
-    form the tree (engine/medusa.py).
+    form the tree (engine/medusa.py);
+  * EAGLE draft head (speculative/speculative.py:416-580) — a one-layer draft model over the
+    target's features and token embeddings proposes a greedy chain (engine/eagle.py).
 """
 from __future__ import annotations
 
@@ -35,7 +37,7 @@ TREE_META_INTS = 2 + 3 * MAX_TREE_NODES
 
 @dataclass
 class SpecConfig:
-    method: str = "prompt_lookup"   # "prompt_lookup" | "draft" | "jacobi" | "medusa"
+    method: str = "prompt_lookup"   # "prompt_lookup" | "draft" | "jacobi" | "medusa" | "eagle"
     k: int = 4                      # draft depth (tokens per branch)
     branches: int = 1               # prompt lookup: distinct continuations per tree
     max_nodes: int = 16             # tree size cap (<= 32)
@@ -51,6 +53,8 @@ class SpecConfig:
     medusa_heads: str | None = None
     medusa_top_k: int = 4
     medusa_paths: int = 16
+    # EAGLE draft head (method "eagle"): a head file / directory, or "random" (tests, benchmarks)
+    eagle_head: str | None = None
 
 
 @dataclass
@@ -397,6 +401,67 @@ class MedusaProposer:
         self.cands.pop(rid, None)
 
 
+class EagleProposer:
+    """Drafts from an EAGLE head (engine/eagle.py): ``observe`` commits each live request's
+    (feature, newest token) pair to its head history and keeps the resulting position;
+    ``propose`` drafts k greedy tokens from it for all requests in one batch per draft step."""
+    deterministic = True
+    wants_hidden = True
+
+    def __init__(self, sc: SpecConfig, head):
+        self.sc = sc
+        self.head = head
+        self.states: dict[str, dict] = {}
+        self.start: dict[str, tuple] = {}
+
+    def observe(self, reqs, hidden) -> None:
+        if not reqs:
+            return
+        states = [self.states.setdefault(r.rid, self.head.new_state()) for r in reqs]
+        toks = [r.token_at(r.total_len - 1) for r in reqs]
+        h, logits = self.head.step(states, hidden, toks, commit=True)
+        for i, r in enumerate(reqs):
+            self.start[r.rid] = (h[i], logits[i])
+
+    def propose(self, reqs) -> dict[str, DraftTree]:
+        import torch
+
+        reqs = [r for r in reqs if r.rid in self.start]
+        if not reqs:
+            return {}
+        starts = [self.start.pop(r.rid) for r in reqs]
+        h = torch.stack([s[0] for s in starts])
+        logits = torch.stack([s[1] for s in starts])
+        drafts = self.head.draft([self.states[r.rid] for r in reqs], h, logits, self.sc.k)
+        return {r.rid: build_tree(r.token_at(r.total_len - 1), [d], self.sc.max_nodes) for r, d in zip(reqs, drafts)}
+
+    def after_verify(self, r, accepted: int, preds=None) -> None:
+        pass
+
+    def forget(self, rid: str) -> None:
+        self.states.pop(rid, None)
+        self.start.pop(rid, None)
+
+
+def load_eagle_head(sc: SpecConfig, target):
+    """The EAGLE head on the target's device, tied to the target's embedding, final norm and
+    LM head (dequantized to fp32 once)."""
+    from .eagle import EagleHead
+
+    cfg = target.cfg
+    dev = getattr(target.runner, "device", "cpu")
+    ck = getattr(target, "checkpoint_tensors", None)
+    if ck is None:
+        raise ValueError("the EAGLE head needs the target checkpoint's embedding, final norm and LM head")
+    emb = ck["model.embed_tokens.weight"].dequantize()
+    lm = ck["lm_head.weight"].dequantize() if "lm_head.weight" in ck else emb
+    norm = ck["model.norm.weight"].dequantize()
+    spec = sc.eagle_head or "random"
+    if spec == "random":
+        return EagleHead.random(cfg, emb, lm, norm, device=dev)
+    return EagleHead.load(spec, cfg, emb, lm, norm, device=dev)
+
+
 def load_medusa_heads(sc: SpecConfig, target):
     """The proposer's heads on the target's device: a file / directory, or random heads."""
     from .medusa import MedusaHeads
@@ -421,6 +486,8 @@ def make_proposer(sc: SpecConfig, target):
         return JacobiProposer(sc)
     if sc.method == "medusa":
         return MedusaProposer(sc, load_medusa_heads(sc, target))
+    if sc.method == "eagle":
+        return EagleProposer(sc, load_eagle_head(sc, target))
     if sc.method == "draft":
         if not sc.draft_model:
             raise ValueError("speculative method 'draft' needs draft_model")

@@ -37,6 +37,10 @@ def _args(*extra):
 def test_flags_build_the_engine_config():
     assert _spec(_args()).method == "prompt_lookup"  # on by default, as in the reference
     assert _spec(_args("--no-prompt-lookup")) is None
+    sc = _spec(_args("--medusa-heads", "heads.safetensors", "--medusa-top-k", "3"))
+    assert (sc.method, sc.medusa_heads, sc.medusa_top_k) == ("medusa", "heads.safetensors", 3)
+    sc = _spec(_args("--eagle-head", "eagle_dir", "--medusa-heads", "x"))
+    assert (sc.method, sc.eagle_head) == ("eagle", "eagle_dir")
     s = _spec(_args("--prompt-lookup-n", "4", "--prompt-lookup-k", "6"))
     assert (s.ngram_max, s.k) == (4, 6)
     assert _spec(_args("--jacobi", "--draft-depth", "3")).method == "jacobi"

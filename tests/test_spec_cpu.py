@@ -98,7 +98,8 @@ def _prompts():
 
 @pytest.mark.parametrize("spec", [SpecConfig("prompt_lookup", k=4, branches=3, max_nodes=12),
                                   SpecConfig("jacobi", k=3), SpecConfig("draft", k=3, draft_model="tiny-llama"),
-                                  SpecConfig("medusa", k=3, medusa_heads="random:3", medusa_top_k=2)])
+                                  SpecConfig("medusa", k=3, medusa_heads="random:3", medusa_top_k=2),
+                                  SpecConfig("eagle", k=3, eagle_head="random")])
 def test_speculative_greedy_matches_plain_greedy(spec):
     sp = SamplingParams(max_tokens=24, ignore_eos=True)
     want = _engine().generate(_prompts(), sp)
@@ -232,3 +233,49 @@ def test_medusa_sees_the_rows_that_produced_each_token():
     assert got == want
     assert seen and all(seen), seen
     assert eng.spec_stats["accepted"] > 0
+
+
+def test_eagle_head_batched_step_matches_a_full_causal_pass(tmp_path):
+    """The head's incremental, batched steps equal one causal pass of its decoder layer over the
+    same (feature, token) sequence, and the published tensor names round-trip."""
+    import math
+
+    from safetensors.torch import save_file
+
+    from squish_b200.engine.eagle import EagleHead
+    from squish_b200.models.reference import _rms, _rope, rope_table
+
+    cfg, _ = get_preset("tiny-llama")
+    g = torch.Generator().manual_seed(0)
+    emb = torch.randn(cfg.vocab_size, cfg.hidden_size, generator=g)
+    lm = torch.randn(cfg.vocab_size, cfg.hidden_size, generator=g) * 0.05
+    head = EagleHead.random(cfg, emb, lm, torch.ones(cfg.hidden_size), seed=3)
+    T = 6
+    feats = torch.randn(2, T, cfg.hidden_size, generator=g)
+    toks = torch.randint(0, cfg.vocab_size, (2, T), generator=g)
+    states = [head.new_state(), head.new_state()]
+    got = [head.step(states, feats[:, t], toks[:, t].tolist(), commit=True)[0] for t in range(T)]
+    got = torch.stack(got, 1)  # [2, T, H]
+    t_, d, hq, hkv = head.t, cfg.head_dim, cfg.num_heads, cfg.num_kv_heads
+    for b in range(2):
+        z = torch.cat([feats[b], emb[toks[b]]], 1) @ t_["fc.weight"].T + t_["fc.bias"]
+        cs = rope_table(cfg, T)
+        q = _rope((z @ t_["layers.0.self_attn.q_proj.weight"].T).view(T, hq, d), cs)
+        k = _rope((z @ t_["layers.0.self_attn.k_proj.weight"].T).view(T, hkv, d), cs).repeat_interleave(hq // hkv, 1)
+        v = (z @ t_["layers.0.self_attn.v_proj.weight"].T).view(T, hkv, d).repeat_interleave(hq // hkv, 1)
+        s = torch.einsum("qhd,khd->hqk", q, k) / math.sqrt(d)
+        s = s.masked_fill(torch.ones(T, T).triu(1).bool(), float("-inf"))
+        o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).reshape(T, -1)
+        h = z + o @ t_["layers.0.self_attn.o_proj.weight"].T
+        m = _rms(h, t_["layers.0.post_attention_layernorm.weight"], cfg.rms_eps)
+        h = h + (torch.nn.functional.silu(m @ t_["layers.0.mlp.gate_proj.weight"].T)
+                 * (m @ t_["layers.0.mlp.up_proj.weight"].T)) @ t_["layers.0.mlp.down_proj.weight"].T
+        torch.testing.assert_close(got[b], h, rtol=1e-4, atol=1e-4)
+    # drafting leaves the committed history as it was
+    n0 = states[0]["k"].shape[0]
+    h0, lg = head.step(states, feats[:, 0], [1, 2], commit=True)
+    head.draft(states, h0, lg, 4)
+    assert states[0]["k"].shape[0] == n0 + 1
+    save_file({"model." + k: v for k, v in head.state_dict().items()}, str(tmp_path / "eagle.safetensors"))
+    back = EagleHead.load(tmp_path, cfg, emb, lm, torch.ones(cfg.hidden_size))
+    assert all(torch.equal(back.t[k], v) for k, v in head.t.items())
