@@ -81,6 +81,8 @@ def _engine_args(p: argparse.ArgumentParser) -> None:
                    help="Medusa head file or directory (medusa_head.{i}.* tensors): tree drafts from extra heads "
                         "on the final hidden state")
     p.add_argument("--medusa-top-k", type=int, default=4, help="Medusa: candidates per head")
+    p.add_argument("--redrafter-head", default=None,
+                   help="recurrent drafter file or directory (gru.* / proj.* tensors): GRU drafts from the target's features")
     p.add_argument("--eagle-head", default=None,
                    help="EAGLE draft head file or directory (fc / layers.0.* tensors): drafts from a one-layer "
                         "model over the target's features")
@@ -110,6 +112,8 @@ def _spec(a):
 
     if getattr(a, "draft_model", None):
         return SpecConfig(method="draft", k=a.draft_depth, draft_model=a.draft_model)
+    if getattr(a, "redrafter_head", None):
+        return SpecConfig(method="redrafter", k=a.draft_depth, redrafter_head=a.redrafter_head)
     if getattr(a, "eagle_head", None):
         return SpecConfig(method="eagle", k=a.draft_depth, eagle_head=a.eagle_head)
     if getattr(a, "medusa_heads", None):

@@ -229,14 +229,14 @@ class LLMEngine:
         # an EAGLE head ties the target's embedding, final norm and LM head (kept before the
         # CUDA runner frees the host copy of the checkpoint)
         keep = None
-        if ecfg.spec is not None and ecfg.spec.method == "eagle":
+        if ecfg.spec is not None and ecfg.spec.method in ("eagle", "redrafter"):
             keep = {k: ck.tensors[k] for k in ("model.embed_tokens.weight", "model.norm.weight", "lm_head.weight")
                     if k in ck.tensors}
         if ecfg.tp > 1:
             if ecfg.kv_h2o_budget > 0:
                 raise ValueError("heavy-hitter KV eviction runs on one GPU per engine (use --dp for more GPUs)")
             if keep is not None:
-                raise ValueError("the EAGLE head runs on one GPU per engine (use --dp for more GPUs)")
+                raise ValueError("feature-based drafters run on one GPU per engine (use --dp for more GPUs)")
             return cls._from_checkpoint_tp(ck, dev, ecfg)
         if dev.type == "cuda" and ecfg.pp > 1:
             return cls._from_checkpoint_layer_split(ck, dev, ecfg)

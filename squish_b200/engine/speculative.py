@@ -37,7 +37,7 @@ TREE_META_INTS = 2 + 3 * MAX_TREE_NODES
 
 @dataclass
 class SpecConfig:
-    method: str = "prompt_lookup"   # "prompt_lookup" | "draft" | "jacobi" | "medusa" | "eagle"
+    method: str = "prompt_lookup"   # prompt_lookup | draft | jacobi | medusa | eagle | redrafter
     k: int = 4                      # draft depth (tokens per branch)
     branches: int = 1               # prompt lookup: distinct continuations per tree
     max_nodes: int = 16             # tree size cap (<= 32)
@@ -53,8 +53,10 @@ class SpecConfig:
     medusa_heads: str | None = None
     medusa_top_k: int = 4
     medusa_paths: int = 16
-    # EAGLE draft head (method "eagle"): a head file / directory, or "random" (tests, benchmarks)
+    # EAGLE draft head (method "eagle") / recurrent drafter (method "redrafter"): a head file or
+    # directory, or "random" (tests, benchmarks)
     eagle_head: str | None = None
+    redrafter_head: str | None = None
 
 
 @dataclass
@@ -443,6 +445,59 @@ class EagleProposer:
         self.start.pop(rid, None)
 
 
+class ReDrafterProposer:
+    """Drafts from a recurrent drafter (engine/redrafter.py): the feature that produced each
+    request's newest token starts the GRU; greedy chains batched over requests."""
+    deterministic = True
+    wants_hidden = True
+
+    def __init__(self, sc: SpecConfig, head):
+        self.sc = sc
+        self.head = head
+        self.feat: dict[str, object] = {}
+
+    def observe(self, reqs, hidden) -> None:
+        for r, f in zip(reqs, hidden):
+            self.feat[r.rid] = f
+
+    def propose(self, reqs) -> dict[str, DraftTree]:
+        import torch
+
+        reqs = [r for r in reqs if r.rid in self.feat]
+        if not reqs:
+            return {}
+        feats = torch.stack([self.feat.pop(r.rid) for r in reqs])
+        toks = [r.token_at(r.total_len - 1) for r in reqs]
+        drafts = self.head.draft(feats, toks, self.sc.k)
+        return {r.rid: build_tree(t, [d], self.sc.max_nodes) for r, t, d in zip(reqs, toks, drafts)}
+
+    def after_verify(self, r, accepted: int, preds=None) -> None:
+        pass
+
+    def forget(self, rid: str) -> None:
+        self.feat.pop(rid, None)
+
+
+def _tied_tensors(target):
+    ck = getattr(target, "checkpoint_tensors", None)
+    if ck is None:
+        raise ValueError("a feature-based drafter needs the target checkpoint's embedding, final norm and LM head")
+    emb = ck["model.embed_tokens.weight"].dequantize()
+    lm = ck["lm_head.weight"].dequantize() if "lm_head.weight" in ck else emb
+    return emb, lm, ck["model.norm.weight"].dequantize()
+
+
+def load_redrafter_head(sc: SpecConfig, target):
+    from .redrafter import ReDrafterHead
+
+    emb, lm, norm = _tied_tensors(target)
+    dev = getattr(target.runner, "device", "cpu")
+    spec = sc.redrafter_head or "random"
+    if spec == "random":
+        return ReDrafterHead.random(target.cfg, emb, lm, norm, device=dev)
+    return ReDrafterHead.load(spec, target.cfg, emb, lm, norm, device=dev)
+
+
 def load_eagle_head(sc: SpecConfig, target):
     """The EAGLE head on the target's device, tied to the target's embedding, final norm and
     LM head (dequantized to fp32 once)."""
@@ -488,6 +543,8 @@ def make_proposer(sc: SpecConfig, target):
         return MedusaProposer(sc, load_medusa_heads(sc, target))
     if sc.method == "eagle":
         return EagleProposer(sc, load_eagle_head(sc, target))
+    if sc.method == "redrafter":
+        return ReDrafterProposer(sc, load_redrafter_head(sc, target))
     if sc.method == "draft":
         if not sc.draft_model:
             raise ValueError("speculative method 'draft' needs draft_model")

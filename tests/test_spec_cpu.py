@@ -99,7 +99,8 @@ def _prompts():
 @pytest.mark.parametrize("spec", [SpecConfig("prompt_lookup", k=4, branches=3, max_nodes=12),
                                   SpecConfig("jacobi", k=3), SpecConfig("draft", k=3, draft_model="tiny-llama"),
                                   SpecConfig("medusa", k=3, medusa_heads="random:3", medusa_top_k=2),
-                                  SpecConfig("eagle", k=3, eagle_head="random")])
+                                  SpecConfig("eagle", k=3, eagle_head="random"),
+                                  SpecConfig("redrafter", k=3, redrafter_head="random")])
 def test_speculative_greedy_matches_plain_greedy(spec):
     sp = SamplingParams(max_tokens=24, ignore_eos=True)
     want = _engine().generate(_prompts(), sp)
@@ -279,3 +280,25 @@ def test_eagle_head_batched_step_matches_a_full_causal_pass(tmp_path):
     save_file({"model." + k: v for k, v in head.state_dict().items()}, str(tmp_path / "eagle.safetensors"))
     back = EagleHead.load(tmp_path, cfg, emb, lm, torch.ones(cfg.hidden_size))
     assert all(torch.equal(back.t[k], v) for k, v in head.t.items())
+
+
+def test_redrafter_gru_matches_torch_cell():
+    """The drafter's GRU cell (C++ kernel on the CPU path) equals torch's GRUCell with the same
+    weights, and the greedy chain follows its own argmax."""
+    from squish_b200.engine.redrafter import ReDrafterHead
+
+    cfg, _ = get_preset("tiny-llama")
+    g = torch.Generator().manual_seed(1)
+    H = cfg.hidden_size
+    emb = torch.randn(cfg.vocab_size, H, generator=g)
+    head = ReDrafterHead.random(cfg, emb, torch.randn(cfg.vocab_size, H, generator=g) * 0.05, torch.ones(H), seed=2)
+    cell = torch.nn.GRUCell(H, H)
+    with torch.no_grad():
+        cell.weight_ih.copy_(head.t["gru.weight_ih"])
+        cell.weight_hh.copy_(head.t["gru.weight_hh"])
+        cell.bias_ih.copy_(head.t["gru.bias_ih"])
+        cell.bias_hh.copy_(head.t["gru.bias_hh"])
+        e, s = torch.randn(3, H, generator=g), torch.randn(3, H, generator=g)
+        torch.testing.assert_close(head.gru(e, s), cell(e, s), rtol=1e-4, atol=1e-5)
+    d = head.draft(torch.randn(2, H, generator=g), [5, 9], 4)
+    assert [len(x) for x in d] == [4, 4]
