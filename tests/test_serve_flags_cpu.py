@@ -41,6 +41,8 @@ def test_flags_build_the_engine_config():
     assert (sc.method, sc.medusa_heads, sc.medusa_top_k) == ("medusa", "heads.safetensors", 3)
     sc = _spec(_args("--eagle-head", "eagle_dir", "--medusa-heads", "x"))
     assert (sc.method, sc.eagle_head) == ("eagle", "eagle_dir")
+    sc = _spec(_args("--redrafter-head", "rd.safetensors", "--eagle-head", "e"))
+    assert (sc.method, sc.redrafter_head) == ("redrafter", "rd.safetensors")
     s = _spec(_args("--prompt-lookup-n", "4", "--prompt-lookup-k", "6"))
     assert (s.ngram_max, s.k) == (4, 6)
     assert _spec(_args("--jacobi", "--draft-depth", "3")).method == "jacobi"
