@@ -381,21 +381,45 @@ def cmd_models(a) -> int:
 
 
 def cmd_catalog(a) -> int:
-    print(json.dumps(_catalog(), indent=2))
+    import dataclasses
+
+    from . import catalog
+
+    es = catalog.search(a.search) if getattr(a, "search", None) else catalog.list_catalog(getattr(a, "tag", None))
+    print(json.dumps({"catalog": [dataclasses.asdict(e) for e in es], "presets": _catalog()}, indent=2))
     return 0
 
 
 def cmd_pull(a) -> int:
+    """Materialize a catalog model: from a local checkpoint directory (``--from``: compressed
+    to INT4), else as random weights of its architecture preset (no network access here)."""
+    from . import catalog
     from .models.config import PRESETS
 
-    if a.name.lower() not in PRESETS:
-        print(f"squish pull: no network access here; {a.name!r} is not a built-in preset "
-              f"({', '.join(sorted(PRESETS))}). Download the HF checkpoint elsewhere and run "
-              f"'squish compress <dir>'.", file=sys.stderr)
+    e = catalog.resolve(a.name)
+    src = getattr(a, "source_dir", None)
+    if e is None and not src and a.name.lower() in PRESETS:  # a preset name outside the catalog
+        a.source, a.random_init, a.output = None, a.name.lower(), None
+        a.format, a.mse, a.delete_source, a.kv_dtype = "int4", False, False, "int4"
+        a.group_size = PRESETS[a.name.lower()][1].group_size
+        return cmd_compress(a)
+    if e is None and not src:
+        near = [x.id for x in catalog.suggest(a.name)]
+        print(f"squish pull: {a.name!r} is not in the catalog" + (f"; did you mean {', '.join(near)}?" if near else ""),
+              file=sys.stderr)
         return 2
-    a.source, a.random_init, a.output = None, a.name.lower(), None
+    preset = e.preset if e is not None else None
+    if src:
+        a.source, a.random_init = src, None
+    elif preset in PRESETS:
+        a.source, a.random_init = None, preset
+    else:
+        print(f"squish pull: no network access here; download {e.hf_repo} elsewhere and run "
+              f"'squish pull {a.name} --from <dir>'", file=sys.stderr)
+        return 2
+    a.output = None if not src else str(ucfg.squish_home() / "models" / (e.id.replace(":", "-") if e else Path(src).name))
     a.format, a.mse, a.delete_source, a.kv_dtype = "int4", False, False, "int4"
-    a.group_size = PRESETS[a.name.lower()][1].group_size
+    a.group_size = PRESETS[preset][1].group_size if preset in PRESETS else 64
     return cmd_compress(a)
 
 
@@ -594,9 +618,13 @@ def build_parser() -> argparse.ArgumentParser:
     p = sub.add_parser("scan", help="static safety scan of model files (nothing is executed)")
     p.add_argument("path")
     p.set_defaults(fn=cmd_scan)
-    sub.add_parser("catalog").set_defaults(fn=cmd_catalog)
-    p = sub.add_parser("pull")
+    p = sub.add_parser("catalog", help="known models (built in + ~/.squish/catalog.json) and presets")
+    p.add_argument("--search", default=None)
+    p.add_argument("--tag", default=None)
+    p.set_defaults(fn=cmd_catalog)
+    p = sub.add_parser("pull", help="materialize a catalog model (local --from dir, or random weights of its preset)")
     p.add_argument("name")
+    p.add_argument("--from", dest="source_dir", default=None, help="local HF checkpoint directory to compress")
     p.add_argument("--device", default=None)
     p.add_argument("--seed", type=int, default=0)
     p.set_defaults(fn=cmd_pull)

@@ -197,9 +197,13 @@ def _local_models() -> list[dict]:
 def cmd_search(a) -> int:
     from .models.config import PRESETS
 
+    from . import catalog
+
     q = a.query.lower()
-    hits = [{"name": n, "source": "preset", "arch": c.arch, "params_b": round(c.num_params() / 1e9, 2)}
-            for n, (c, _) in sorted(PRESETS.items()) if q in n or q in c.arch]
+    hits = [{"name": e.id, "source": "catalog", "repo": e.hf_repo, "params": e.params, "preset": e.preset}
+            for e in catalog.search(a.query)]
+    hits += [{"name": n, "source": "preset", "arch": c.arch, "params_b": round(c.num_params() / 1e9, 2)}
+             for n, (c, _) in sorted(PRESETS.items()) if q in n or q in c.arch]
     for m in _local_models():
         if q in json.dumps(m).lower():
             hits.append({"name": m.get("name"), "source": "local", "path": m.get("path")})

@@ -125,6 +125,18 @@ _register(ModelConfig("qwen3-30b-a3b", "qwen3_moe", 151936, 2048, 48, 32, 4, 128
           QuantConfig(4, 64, True, "int4", 32, 16))
 
 
+# Qwen3-8B shape: dense, q/k norms, INT4 g64 weights, INT4 KV.
+_register(ModelConfig("qwen3-8b", "qwen3", 151936, 4096, 36, 32, 8, 128, 12288, 1e-6, 1e6, qk_norm=True,
+                      max_position=40960, bos_token_id=151643, eos_token_id=151645),
+          QuantConfig(4, 64, True, "int4", 32, 16))
+# Llama-3.1-8B shape: Llama-3 RoPE frequency scaling, INT4 g64 weights, INT4 KV.
+_register(ModelConfig("llama-3.1-8b", "llama", 128256, 4096, 32, 32, 8, 128, 14336, 1e-5, 5e5, max_position=131072,
+                      rope_scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                    "high_freq_factor": 4.0, "original_max_position_embeddings": 8192},
+                      bos_token_id=128000, eos_token_id=128009),
+          QuantConfig(4, 64, True, "int4", 32, 16))
+
+
 def get_preset(name: str) -> tuple[ModelConfig, QuantConfig]:
     key = name.lower()
     if key not in PRESETS:

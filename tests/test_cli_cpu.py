@@ -40,8 +40,10 @@ def test_cli_config_catalog_version(home, capsys):
     assert cli.main(["config", "get", "model.default"]) == 0
     assert capsys.readouterr().out.strip().splitlines()[-1] == '"tiny-llama"'
     assert cli.main(["catalog"]) == 0
-    names = [r["name"] for r in json.loads(capsys.readouterr().out)]
+    d = json.loads(capsys.readouterr().out)
+    names = [r["name"] for r in d["presets"]]
     assert "qwen2.5-7b" in names and "llama-3-70b" in names
+    assert "qwen2.5:7b" in [e["id"] for e in d["catalog"]]
     assert cli.main(["version"]) == 0
 
 
