@@ -375,6 +375,31 @@ class LLMEngine:
         if self.blocks.tier is not None:
             self.blocks.tier.flush()
 
+    def save_session(self, tokens: list[int]) -> int:
+        """Copy the cached KV blocks of a conversation (its prompt + output tokens, full blocks
+        only) into the host / disk tiers now, rather than when their pages are reused, and write
+        the host tier to disk: a later request with the same prefix (this process or a restarted
+        one on the same disk directory) restores them instead of recomputing. Returns the blocks
+        saved. The reference keeps per-session KV files (squish/kv/kv_cache.py:3263-3560,
+        ``SessionKVCache`` / ``DiskKVCache``); here sessions are the chained-hash blocks."""
+        from ..kv.paged import chain_hashes
+
+        tier = self.blocks.tier
+        if tier is None:
+            raise ValueError("saving a session needs a KV tier (kv_host_bytes or kv_disk_dir)")
+        n = 0
+        for h in chain_hashes(tokens, self.qcfg.page_size, self.blocks.model_key):
+            p = self.blocks.hash_to_page.get(h)
+            if p is None:
+                if tier.has(h):
+                    continue
+                break  # the chain is broken here: later blocks cannot be matched anyway
+            if not tier.has(h):
+                tier.offload(h, p)
+                n += 1
+        tier.flush()
+        return n
+
     # ------------------------------------------------------------------ requests
     def add_request(self, prompt: list[int], params: SamplingParams | None = None, rid: str | None = None) -> str:
         params = (params or SamplingParams()).validate()

@@ -88,3 +88,23 @@ def test_kv_mode_selection_and_memory_planning():
         assert n >= 1000 and estimate_kv_memory(cfg, n, mode, 3).total_bytes <= est.total_bytes
     e8, e2 = estimate_kv_memory(cfg, 4096, "int8"), estimate_kv_memory(cfg, 4096, "int2")
     assert e2.total_bytes < e8.total_bytes / 2.5
+
+
+def test_saved_session_restores_in_a_new_engine(tmp_path):
+    """A conversation saved explicitly (no eviction needed) is restored from disk by a restarted
+    engine: its blocks come back instead of being recomputed, and the continuation equals a
+    fresh computation."""
+    rng = np.random.default_rng(2)
+    d = tmp_path / "kv"
+    eng = _eng(kv_host_bytes=1 << 20, kv_disk_dir=str(d))
+    prompt = rng.integers(0, 32000, 70).tolist()
+    out = eng.generate([prompt], SP)[0]
+    convo = prompt + out  # 76 tokens: 4 full blocks
+    assert eng.save_session(convo) == 4
+    assert eng.save_session(convo) == 0  # already saved
+    assert len(list(d.glob("*.npz"))) >= 4
+    eng2 = _eng(kv_host_bytes=1 << 20, kv_disk_dir=str(d))
+    follow = convo + [7, 8, 9]
+    got = eng2.generate([follow], SP)[0]
+    assert eng2.blocks.tier.stats["restored_disk"] >= 4
+    assert got == _eng().generate([follow], SP)[0]
