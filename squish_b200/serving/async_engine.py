@@ -128,6 +128,17 @@ class AsyncEngine:
         self._inbox.put(("abort", rid, None, None))
         self._wake.set()
 
+    def call(self, fn, timeout: float = 30.0):
+        """Run ``fn(engine)`` on the engine thread between steps (the engine is not thread
+        safe) and return its result; its exception is raised here."""
+        box: queue.Queue = queue.Queue(maxsize=1)
+        self._inbox.put(("call", None, fn, box))
+        self._wake.set()
+        ok, val = box.get(timeout=timeout)
+        if not ok:
+            raise val
+        return val
+
     async def stream(self, prompt_ids: list[int], params: SamplingParams):
         """Async generator of GenEvent for one request."""
         rid, sink = self.submit(prompt_ids, params, asyncio.get_running_loop())
@@ -168,6 +179,12 @@ class AsyncEngine:
     def _apply_ops(self, ops) -> None:
         eng = self.engine
         for op, rid, prompt, params in ops:
+            if op == "call":  # (prompt = the function, params = the reply box)
+                try:
+                    params.put((True, prompt(eng)))
+                except Exception as exc:  # noqa: BLE001 - handed back to the caller
+                    params.put((False, exc))
+                continue
             if op == "add":
                 try:
                     eng.add_request(prompt, params, rid=rid)

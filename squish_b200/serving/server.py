@@ -424,6 +424,29 @@ def create_app(st: ServerState) -> FastAPI:
         ids = st.tok.encode(text)
         return {"token_ids": ids, "token_count": len(ids), "model": st.model_name}
 
+    @app.post("/v1/sessions/save")
+    async def save_session(request: Request):
+        """Keep a conversation's KV cache: the chat (``messages``, with the assistant's reply as
+        the last message) or ``text`` is tokenized as the model saw it, and its cached blocks are
+        copied to the host / disk KV tiers now, so a follow-up turn, also after a restart on the
+        same disk directory, starts from them."""
+        _check_auth(request, st)
+        body = await _json(request)
+        if "messages" in body:
+            # (the template's trailing assistant prompt only touches the last, partial block)
+            text = apply_chat_template(body["messages"], st.tok, st.arch)
+        elif "text" in body:
+            text = body["text"]
+        else:
+            raise HTTPException(status_code=400, detail="Provide 'text' or 'messages' in request body")
+        ids = st.tok.encode(text)
+        loop = asyncio.get_running_loop()
+        try:
+            n = await loop.run_in_executor(None, lambda: st.aeng.call(lambda eng: eng.save_session(ids)))
+        except ValueError as exc:
+            raise HTTPException(status_code=400, detail=str(exc)) from exc
+        return {"blocks_saved": n, "token_count": len(ids), "model": st.model_name}
+
     @app.post("/v1/detokenize")
     async def detokenize(request: Request):
         _check_auth(request, st)

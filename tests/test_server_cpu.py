@@ -257,3 +257,25 @@ def test_prompt_router_and_backend_router(client, monkeypatch):
     assert BackendRouter(BackendConfig()).health_check(timeout=0.2) is False  # nothing listens on port 9
     with pytest.raises(ValueError):
         BackendConfig(backend="nope")
+
+
+def test_session_save_route(tmp_path):
+    """POST /v1/sessions/save runs on the engine thread: without a KV tier it is refused, with a
+    disk tier the conversation's full blocks land on disk."""
+    from squish_b200.serving.async_engine import AsyncEngine
+    from squish_b200.serving.server import ServerState, create_app
+
+    cfg, q = get_preset("tiny-llama")
+    for tier, want in ((False, 400), (True, 200)):
+        kw = {"kv_disk_dir": str(tmp_path / "kv"), "kv_host_bytes": 1 << 20} if tier else {}
+        eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), "cpu",
+                                        EngineConfig(max_num_seqs=4, max_model_len=512, num_pages=64, **kw))
+        aeng = AsyncEngine(eng, ByteTokenizer(cfg.vocab_size, cfg.eos_token_id), model_name="tiny").start()
+        with TestClient(create_app(ServerState(aeng, "tiny", api_key=None, arch="llama"))) as c:
+            text = "a conversation long enough to fill a few sixteen-token KV pages " * 2
+            c.post("/v1/completions", json={"prompt": text, "max_tokens": 2, "temperature": 0})
+            r = c.post("/v1/sessions/save", json={"text": text})
+            assert r.status_code == want, r.text
+            if tier:
+                assert r.json()["blocks_saved"] >= 4 and list((tmp_path / "kv").glob("*.npz"))
+        aeng.stop()
