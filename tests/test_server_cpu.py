@@ -279,3 +279,20 @@ def test_session_save_route(tmp_path):
             if tier:
                 assert r.json()["blocks_saved"] >= 4 and list((tmp_path / "kv").glob("*.npz"))
         aeng.stop()
+
+
+def test_engine_thread_call_returns_and_raises():
+    """AsyncEngine.call runs a function on the engine thread between steps and hands back its
+    result or its exception."""
+    cfg, q = get_preset("tiny-llama")
+    eng = LLMEngine.from_checkpoint(random_checkpoint(cfg, q, seed=0, device="cpu"), "cpu",
+                                    EngineConfig(max_num_seqs=2, max_model_len=256, num_pages=32))
+    aeng = AsyncEngine(eng, ByteTokenizer(cfg.vocab_size, cfg.eos_token_id), model_name="tiny").start()
+    try:
+        import threading
+
+        assert aeng.call(lambda e: (e is eng, threading.current_thread() is not threading.main_thread())) == (True, True)
+        with pytest.raises(ValueError, match="KV tier"):
+            aeng.call(lambda e: e.save_session(list(range(64))))
+    finally:
+        aeng.stop()
